@@ -1,0 +1,50 @@
+# SPDX-License-Identifier: Apache-2.0
+# Builds libvccl.so (sm_100a) plus the native tools and tests into
+# vkccl_b200/_native/.  `make -j` from the repository root.
+
+CUDA_HOME ?= /usr/local/cuda
+NVCC      ?= $(CUDA_HOME)/bin/nvcc
+ARCH      ?= -gencode arch=compute_100a,code=sm_100a
+OUT       := vkccl_b200/_native
+OBJ       := $(OUT)/obj
+BIN       := $(OUT)/bin
+CUTLASS_INC ?= $(shell python3 -c "import os,site;print(os.path.join(site.getsitepackages()[0],'flashinfer','data','cutlass','include'))" 2>/dev/null)
+
+NVFLAGS := $(ARCH) -O3 -lineinfo -std=c++17 -Xcompiler -fPIC -Xcompiler -Wall \
+           -Iinclude -Icsrc -I$(CUDA_HOME)/include --expt-relaxed-constexpr \
+           -diag-suppress 177,550,20281
+LDFLAGS := -cudart static -lpthread -ldl -lrt
+
+LIB_CC  := $(wildcard csrc/common/*.cc csrc/control/*.cc csrc/runtime/*.cc)
+LIB_CU  := $(wildcard csrc/runtime/*.cu csrc/fused/*.cu)
+LIB_OBJ := $(patsubst csrc/%,$(OBJ)/%.o,$(LIB_CC) $(LIB_CU))
+HDRS    := $(wildcard include/*.h csrc/*/*.h csrc/*/*.cuh)
+
+TOOLS   := $(BIN)/vccl-bench $(BIN)/vccl-info $(BIN)/vccl-devbuf-demo
+TESTS   := $(BIN)/test_bootstrap $(BIN)/test_collectives $(BIN)/test_control
+
+all: $(OUT)/libvccl.so $(TOOLS) $(TESTS)
+
+$(OBJ)/%.cc.o: csrc/%.cc $(HDRS)
+	@mkdir -p $(dir $@)
+	$(NVCC) $(NVFLAGS) -x cu -c $< -o $@
+
+$(OBJ)/%.cu.o: csrc/%.cu $(HDRS)
+	@mkdir -p $(dir $@)
+	$(NVCC) $(NVFLAGS) -I$(CUTLASS_INC) -c $< -o $@
+
+$(OUT)/libvccl.so: $(LIB_OBJ)
+	$(NVCC) $(ARCH) -shared -o $@ $^ $(LDFLAGS)
+
+$(BIN)/%: csrc/tools/%.cc $(OUT)/libvccl.so include/vccl.h
+	@mkdir -p $(BIN)
+	$(NVCC) $(NVFLAGS) -x cu $< -o $@ -L$(OUT) -lvccl -Xlinker -rpath,'$$ORIGIN/..' $(LDFLAGS)
+
+$(BIN)/test_%: csrc/tests/test_%.cc $(OUT)/libvccl.so $(HDRS)
+	@mkdir -p $(BIN)
+	$(NVCC) $(NVFLAGS) -x cu $< -o $@ -L$(OUT) -lvccl -Xlinker -rpath,'$$ORIGIN/..' $(LDFLAGS)
+
+clean:
+	rm -rf $(OUT)/obj $(OUT)/bin $(OUT)/libvccl.so
+
+.PHONY: all clean

@@ -1,0 +1,29 @@
+// SPDX-License-Identifier: Apache-2.0
+// Host helpers shared by the GEMM-based fused kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+
+namespace vccl {
+namespace gemm {
+
+// K-major bf16 tensor map for rows x K with a (64 x boxRows) box, 128B swizzle.
+bool makeMapKMajor(CUtensorMap* map, const void* base, int rows, int K, int boxRows);
+int smCount();
+int pickBN(int M, int N);
+int* errorFlag();
+
+template <typename Epi, typename Hooks>
+cudaError_t launchGemm(const void* A, const void* B, int M, int N, int K, const Epi& epi, const Hooks& hooks,
+                       cudaStream_t st, int bnOverride, int gridCap);
+
+inline long envLongGemm(const char* name) {
+  const char* v = std::getenv(name);
+  return v ? std::strtol(v, nullptr, 10) : 0;
+}
+
+}  // namespace gemm
+}  // namespace vccl

@@ -1,0 +1,66 @@
+// SPDX-License-Identifier: Apache-2.0
+// Kernel argument structures shared by host launchers and device code.
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "kernels/device_common.cuh"
+
+namespace vccl {
+namespace dev {
+
+enum Where : uint32_t {
+  kWhereStart = 1,
+  kWhereLL = 2,
+  kWherePush = 3,
+  kWhereReduce = 4,
+  kWhereNvls = 5,
+  kWhereGather = 6,
+  kWhereP2pSend = 7,
+  kWhereP2pRecv = 8,
+  kWhereFused = 9,
+};
+
+struct CollArgs {
+  const char* send;
+  char* recv;
+  size_t count;   // AR/Reduce/Bcast: elements; AG: sendcount; RS: recvcount
+  int root;       // Reduce/Bcast root; -1 for all-reduce
+  int premul;     // scale own contribution by `scalar`
+  int avg;        // post-scale by 1/nranks
+  double scalar;
+};
+
+constexpr int kMaxP2pOps = 160;
+constexpr int kMaxP2pWork = 160;
+enum P2pKind : int { kP2pSend = 0, kP2pRecv = 1, kP2pCopy = 2 };
+
+struct P2pOpDesc {
+  char* dst;        // recv buffer (recv/copy)
+  const char* src;  // send buffer (send/copy)
+  size_t bytes;
+  int peer;
+  int kind;
+};
+struct P2pWork {
+  int16_t peer;
+  int8_t kind;
+  int8_t ch;
+};
+struct P2pPlan {
+  int nops;
+  int nwork;
+  P2pOpDesc ops[kMaxP2pOps];
+  P2pWork work[kMaxP2pWork];
+};
+
+__host__ __device__ __forceinline__ int p2pChannels(size_t bytes) {
+  size_t ch = bytes / (1u << 20);
+  if (ch < 1) ch = 1;
+  if (ch > static_cast<size_t>(kMaxChannels)) ch = kMaxChannels;
+  return static_cast<int>(ch);
+}
+
+}  // namespace dev
+}  // namespace vccl

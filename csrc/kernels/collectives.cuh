@@ -1,0 +1,418 @@
+// SPDX-License-Identifier: Apache-2.0
+// Reduction collectives over symmetric NVLink-mapped workspaces.
+//
+// These replace the reference's host-side ring / recursive-doubling / chain
+// algorithms over TCP (reference: src/core/collectives.cc:102-620) with
+// single-kernel algorithms that fit a uniform NVSwitch fabric:
+//
+//   allReduceLL       one NVLink hop: every rank stores its (pre-scaled)
+//                     payload into every peer's LL region as 16-byte lines
+//                     {data, flag, data, flag}; readers spin on the flags.
+//                     No barriers.  Small messages.
+//   allReduceTwoShot  push reduce-scatter into the owners' staging slots,
+//                     local reduction, then every rank pulls the reduced
+//                     chunks (also used for Reduce, where only the root
+//                     pulls).  Any dtype/op.
+//   allReduceNvls     copy into the multicast-bound staging region, then
+//                     multimem.ld_reduce + multimem.st of the owned chunk
+//                     (the NVSwitch reduces and broadcasts), copy out.
+//   reduceScatterPush push chunk q to rank q's slot, reduce locally.
+//
+// Every barrier-based kernel begins with a barrier: once block b has met
+// every peer in this launch, each peer has finished all earlier launches on
+// this communicator, so staging memory may be overwritten.  Rounds inside a
+// launch alternate staging halves or are separated by the data-ready
+// barrier of the next round.
+#pragma once
+
+#include "kernels/coll_abi.cuh"
+#include "kernels/device_common.cuh"
+#include "kernels/dtypes.cuh"
+#include "kernels/movers.cuh"
+
+namespace vccl {
+namespace dev {
+
+__device__ __forceinline__ void blockRange(size_t total, int parts, int idx, size_t align, size_t* lo,
+                                           size_t* hi) {
+  size_t per = (total + parts - 1) / parts;
+  per = (per + align - 1) / align * align;
+  size_t a = per * static_cast<size_t>(idx);
+  *lo = a < total ? a : total;
+  size_t b = *lo + per;
+  *hi = b < total ? b : total;
+}
+
+// ---------------------------------------------------------------------------
+// LL one-shot all-reduce.  Grid is always kLLBlocks so every block's epoch
+// advances once per launch (epochs are equal across blocks and ranks).
+// send/recv must be 8-byte aligned and count*sizeof(T) <= kLLMaxBytes.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t readWord(const char* base, size_t w, size_t bytes) {
+  const size_t off = w * 8;
+  if (off + 8 <= bytes) return *reinterpret_cast<const uint64_t*>(base + off);
+  uint64_t v = 0;
+  for (size_t i = 0; off + i < bytes; i++)
+    v |= static_cast<uint64_t>(static_cast<unsigned char>(base[off + i])) << (8 * i);
+  return v;
+}
+__device__ __forceinline__ void writeWord(char* base, size_t w, size_t bytes, uint64_t v) {
+  const size_t off = w * 8;
+  if (off + 8 <= bytes) {
+    *reinterpret_cast<uint64_t*>(base + off) = v;
+    return;
+  }
+  for (size_t i = 0; off + i < bytes; i++) base[off + i] = static_cast<char>((v >> (8 * i)) & 0xff);
+}
+
+template <typename T>
+struct WordPack {
+  static constexpr int N = 8 / sizeof(T);
+  using Acc = typename Elem<T>::Acc;
+  Acc v[N];
+  __device__ __forceinline__ void load(uint64_t raw) {
+    union { uint64_t u; T e[N]; } c;
+    c.u = raw;
+#pragma unroll
+    for (int i = 0; i < N; i++) v[i] = Elem<T>::toAcc(c.e[i]);
+  }
+  __device__ __forceinline__ uint64_t pack() const {
+    union { uint64_t u; T e[N]; } c;
+#pragma unroll
+    for (int i = 0; i < N; i++) c.e[i] = Elem<T>::fromAcc(v[i]);
+    return c.u;
+  }
+  template <int K>
+  __device__ __forceinline__ void fold(uint64_t raw) {
+    union { uint64_t u; T e[N]; } c;
+    c.u = raw;
+#pragma unroll
+    for (int i = 0; i < N; i++) v[i] = combine<T, K>(v[i], Elem<T>::toAcc(c.e[i]));
+  }
+  __device__ __forceinline__ void scale(double s) {
+#pragma unroll
+    for (int i = 0; i < N; i++) v[i] = scaleAcc<T>(v[i], s);
+  }
+};
+
+__device__ __forceinline__ void stVolatile16(char* p, const uint4& v) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ldVolatile16(const char* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ char* llSlot(const DevComm& c, int owner, uint32_t parity, int src) {
+  return c.ctrl[owner] + kLLOff + (static_cast<size_t>(parity) * kMaxRanks + src) * kLLSlotBytes;
+}
+
+// Wait for a complete LL line of epoch e; false on timeout/abort.
+__device__ __forceinline__ bool llWait(const DevComm& c, const char* p, uint32_t e, uint64_t* out) {
+  uint4 v = ldVolatile16(p);
+  if (v.y != e || v.w != e) {
+    const uint64_t start = globalTimerNs();
+    for (uint32_t spin = 1;; ++spin) {
+      v = ldVolatile16(p);
+      if (v.y == e && v.w == e) break;
+      if ((spin & 1023u) == 0u && shouldGiveUp(c, start, kWhereLL, 0)) return false;
+    }
+  }
+  *out = static_cast<uint64_t>(v.x) | (static_cast<uint64_t>(v.z) << 32);
+  return true;
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(512) allReduceLL(DevComm c, CollArgs a) {
+  __shared__ uint32_t sE;
+  const int blk = blockIdx.x;
+  if (threadIdx.x == 0) {
+    uint32_t* ep = ctrlAt<uint32_t>(c, c.rank, kLLEpochOff) + blk;
+    sE = *ep + 1u;
+    *ep = sE;
+  }
+  __syncthreads();
+  const uint32_t e = sE;
+  const uint32_t par = e & 1u;
+  const size_t bytes = a.count * sizeof(T);
+  const size_t words = (bytes + 7) / 8;
+  size_t w0, w1;
+  blockRange(words, gridDim.x, blk, 1, &w0, &w1);
+  const int n = c.nranks, me = c.rank;
+
+  for (size_t w = w0 + threadIdx.x; w < w1; w += blockDim.x) {
+    uint64_t word = readWord(a.send, w, bytes);
+    if (a.premul) {
+      WordPack<T> p;
+      p.load(word);
+      p.scale(a.scalar);
+      word = p.pack();
+    }
+    const uint4 line = make_uint4(static_cast<uint32_t>(word), e, static_cast<uint32_t>(word >> 32), e);
+    for (int k = 1; k < n; k++) {
+      int p = me + k;
+      if (p >= n) p -= n;
+      stVolatile16(llSlot(c, p, par, me) + w * 16, line);
+    }
+  }
+  for (size_t w = w0 + threadIdx.x; w < w1; w += blockDim.x) {
+    WordPack<T> acc;
+    acc.load(readWord(a.send, w, bytes));
+    if (a.premul) acc.scale(a.scalar);
+    bool ok = true;
+    for (int k = 1; k < n && ok; k++) {
+      int p = me + k;
+      if (p >= n) p -= n;
+      uint64_t v;
+      ok = llWait(c, llSlot(c, me, par, p) + w * 16, e, &v);
+      if (ok) acc.template fold<K>(v);
+    }
+    if (!ok) break;
+    if (a.avg) acc.scale(1.0 / n);
+    writeWord(a.recv, w, bytes, acc.pack());
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Two-shot all-reduce / reduce.  Staging: n input slots + 1 result slot of
+// slotElems elements each.  root < 0: all-reduce; else only root gathers.
+// ---------------------------------------------------------------------------
+template <typename T, int K, bool VEC>
+__global__ void __launch_bounds__(512) allReduceTwoShot(DevComm c, CollArgs a, size_t slotElems) {
+  const int blk = blockIdx.x, G = gridDim.x, n = c.nranks, me = c.rank;
+  constexpr size_t PK = VEC ? 16 / sizeof(T) : 1;
+  const size_t esz = sizeof(T);
+  const size_t slotBytes = slotElems * esz;
+  if (!blockBarrier(c, blk, kWhereStart)) return;
+  const size_t roundElems = slotElems * n;
+  for (size_t base = 0; base < a.count; base += roundElems) {
+    const size_t m = (a.count - base) < roundElems ? (a.count - base) : roundElems;
+    size_t ce = (m + n - 1) / n;
+    ce = (ce + PK - 1) / PK * PK;
+    size_t s0, s1;
+    blockRange(ce, G, blk, PK, &s0, &s1);
+    // 1. push my contribution to chunk q into rank q's slot `me`
+    for (int k = 1; k < n; k++) {
+      const int q = (me + k) % n;
+      const size_t lo = q * ce + s0;
+      const size_t hiRaw = q * ce + s1;
+      const size_t hi = hiRaw < m ? hiRaw : m;
+      if (lo < hi)
+        copyScaled<T, VEC>(c.data[q] + me * slotBytes + s0 * esz, a.send + (base + lo) * esz, hi - lo, a.premul,
+                           a.scalar);
+    }
+    if (!blockBarrier(c, blk, kWherePush)) return;
+    // 2. reduce my chunk
+    {
+      const size_t lo = me * ce + s0;
+      const size_t hiRaw = me * ce + s1;
+      const size_t hi = hiRaw < m ? hiRaw : m;
+      if (lo < hi) {
+        char* resultSlot = c.data[me] + n * slotBytes + s0 * esz;
+        char* out = nullptr;
+        char* out2 = nullptr;
+        if (a.root < 0) {
+          out = a.recv + (base + lo) * esz;
+          out2 = resultSlot;
+        } else if (a.root == me) {
+          out = a.recv + (base + lo) * esz;
+        } else {
+          out2 = resultSlot;
+        }
+        const char* slots = c.data[me] + s0 * esz;
+        reduceInto<T, K, VEC>(
+            n, me, out, out2, a.send + (base + lo) * esz, [&](int p) { return slots + p * slotBytes; }, hi - lo,
+            a.premul, a.scalar, a.avg);
+      }
+    }
+    if (!blockBarrier(c, blk, kWhereReduce)) return;
+    // 3. gather the reduced chunks
+    if (a.root < 0 || a.root == me) {
+      for (int k = 1; k < n; k++) {
+        const int q = (me + k) % n;
+        const size_t lo = q * ce + s0;
+        const size_t hiRaw = q * ce + s1;
+        const size_t hi = hiRaw < m ? hiRaw : m;
+        if (lo < hi)
+          copyScaled<T, VEC>(a.recv + (base + lo) * esz, c.data[q] + n * slotBytes + s0 * esz, hi - lo, false,
+                             1.0);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// NVLS all-reduce (f32 / bf16 / f16; sum, and min/max for 16-bit floats).
+// ---------------------------------------------------------------------------
+template <typename T, int K>
+struct Multimem;
+
+#define VCCL_MM(T, TNAME, OPNAME, KV)                                                                     \
+  template <>                                                                                             \
+  struct Multimem<T, KV> {                                                                                \
+    __device__ __forceinline__ static uint4 ldReduce(const char* p) {                                     \
+      uint4 v;                                                                                            \
+      asm volatile("multimem.ld_reduce.relaxed.sys.global." OPNAME ".v4." TNAME " {%0,%1,%2,%3}, [%4];" \
+                   : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)                                           \
+                   : "l"(p)                                                                               \
+                   : "memory");                                                                           \
+      return v;                                                                                           \
+    }                                                                                                     \
+  };
+VCCL_MM(float, "f32", "add", kSum)
+VCCL_MM(__nv_bfloat16, "bf16x2", "add.acc::f32", kSum)
+VCCL_MM(__half, "f16x2", "add.acc::f32", kSum)
+VCCL_MM(__nv_bfloat16, "bf16x2", "min", kMin)
+VCCL_MM(__half, "f16x2", "min", kMin)
+VCCL_MM(__nv_bfloat16, "bf16x2", "max", kMax)
+VCCL_MM(__half, "f16x2", "max", kMax)
+#undef VCCL_MM
+
+template <typename T, int K>
+struct HasMultimem {
+  static constexpr bool value = false;
+};
+template <> struct HasMultimem<float, kSum> { static constexpr bool value = true; };
+template <> struct HasMultimem<__nv_bfloat16, kSum> { static constexpr bool value = true; };
+template <> struct HasMultimem<__half, kSum> { static constexpr bool value = true; };
+template <> struct HasMultimem<__nv_bfloat16, kMin> { static constexpr bool value = true; };
+template <> struct HasMultimem<__half, kMin> { static constexpr bool value = true; };
+template <> struct HasMultimem<__nv_bfloat16, kMax> { static constexpr bool value = true; };
+template <> struct HasMultimem<__half, kMax> { static constexpr bool value = true; };
+
+__device__ __forceinline__ void multimemStore16(char* p, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Copy `elems` elements with optional scaling; any alignment on the user side.
+template <typename T>
+__device__ __forceinline__ void copyInScaled(char* dst, const char* src, size_t elems, bool doScale, double s) {
+  if (!doScale) {
+    copyAny(dst, src, elems * sizeof(T));
+  } else if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15u) == 0) {
+    copyScaled<T, true>(dst, src, elems, true, s);
+  } else {
+    copyScaled<T, false>(dst, src, elems, true, s);
+  }
+}
+
+// Reduce [lo, hi) of the multicast region through the switch and store the
+// result back to every rank's copy (16-byte units, several in flight).
+template <typename T, int K>
+__device__ __forceinline__ void nvlsReduceRange(char* mc, size_t lo, size_t hi, bool avg, int n) {
+  constexpr int U = 4;
+  const size_t nthr = blockDim.x;
+  const size_t units = (hi - lo + 15) / 16;
+  size_t i = threadIdx.x;
+  for (; i + (U - 1) * nthr < units; i += U * nthr) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) v[u] = Multimem<T, K>::ldReduce(mc + lo + (i + u * nthr) * 16);
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      if (avg) {
+        Pack<T> p;
+        p.load(v[u]);
+        p.scale(1.0 / n);
+        v[u] = p.pack();
+      }
+      multimemStore16(mc + lo + (i + u * nthr) * 16, v[u]);
+    }
+  }
+  for (; i < units; i += nthr) {
+    uint4 v = Multimem<T, K>::ldReduce(mc + lo + i * 16);
+    if (avg) {
+      Pack<T> p;
+      p.load(v);
+      p.scale(1.0 / n);
+      v = p.pack();
+    }
+    multimemStore16(mc + lo + i * 16, v);
+  }
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(512) allReduceNvls(DevComm c, CollArgs a, size_t roundBytes) {
+  const int blk = blockIdx.x, G = gridDim.x, n = c.nranks, me = c.rank;
+  const size_t esz = sizeof(T);
+  const size_t total = a.count * esz;
+  if (!blockBarrier(c, blk, kWhereStart)) return;
+  char* local = c.data[me];
+  for (size_t off = 0; off < total; off += roundBytes) {
+    const size_t m = (total - off) < roundBytes ? (total - off) : roundBytes;
+    size_t cb = (m + n - 1) / n;
+    cb = (cb + 15) / 16 * 16;
+    size_t s0, s1;
+    blockRange(cb, G, blk, 16, &s0, &s1);
+    // 1. copy in: my sub-slice of every chunk
+    for (int q = 0; q < n; q++) {
+      const size_t lo = q * cb + s0;
+      const size_t hiRaw = q * cb + s1;
+      const size_t hi = hiRaw < m ? hiRaw : m;
+      if (lo < hi) copyInScaled<T>(local + lo, a.send + off + lo, (hi - lo) / esz, a.premul, a.scalar);
+    }
+    if (!blockBarrier(c, blk, kWhereNvls)) return;
+    // 2. reduce my chunk through the switch and broadcast the result
+    if constexpr (HasMultimem<T, K>::value) {
+      const size_t lo = me * cb + s0;
+      const size_t hiRaw = me * cb + s1;
+      const size_t hi = hiRaw < m ? hiRaw : m;
+      if (lo < hi) nvlsReduceRange<T, K>(c.mcData, lo, hi, a.avg != 0, n);
+    }
+    fenceProxyAlias();
+    if (!blockBarrier(c, blk, kWhereNvls)) return;
+    // 3. copy out
+    for (int q = 0; q < n; q++) {
+      const size_t lo = q * cb + s0;
+      const size_t hiRaw = q * cb + s1;
+      const size_t hi = hiRaw < m ? hiRaw : m;
+      if (lo < hi) copyAny(a.recv + off + lo, local + lo, hi - lo);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Reduce-scatter: push chunk q to rank q's slot, reduce locally.
+// ---------------------------------------------------------------------------
+template <typename T, int K, bool VEC>
+__global__ void __launch_bounds__(512) reduceScatterPush(DevComm c, CollArgs a, size_t slotElems) {
+  const int blk = blockIdx.x, G = gridDim.x, n = c.nranks, me = c.rank;
+  constexpr size_t PK = VEC ? 16 / sizeof(T) : 1;
+  const size_t esz = sizeof(T);
+  const size_t slotBytes = slotElems * esz;
+  const size_t half = (c.dataBytes / 2) / 16 * 16;
+  if (!blockBarrier(c, blk, kWhereStart)) return;
+  const size_t rc = a.count;
+  int k = 0;
+  for (size_t base = 0; base < rc; base += slotElems, k++) {
+    const size_t m = (rc - base) < slotElems ? (rc - base) : slotElems;
+    size_t s0, s1;
+    blockRange(m, G, blk, PK, &s0, &s1);
+    const size_t hoff = (k & 1) * half;
+    if (s0 < s1) {
+      for (int s = 1; s < n; s++) {
+        const int q = (me + s) % n;
+        copyScaled<T, VEC>(c.data[q] + hoff + me * slotBytes + s0 * esz, a.send + (q * rc + base + s0) * esz,
+                           s1 - s0, a.premul, a.scalar);
+      }
+    }
+    if (!blockBarrier(c, blk, kWherePush)) return;
+    if (s0 < s1) {
+      const char* slots = c.data[me] + hoff + s0 * esz;
+      reduceInto<T, K, VEC>(
+          n, me, a.recv + (base + s0) * esz, nullptr, a.send + (me * rc + base + s0) * esz,
+          [&](int p) { return slots + p * slotBytes; }, s1 - s0, a.premul, a.scalar, a.avg);
+    }
+  }
+}
+
+}  // namespace dev
+}  // namespace vccl

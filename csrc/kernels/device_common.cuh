@@ -1,0 +1,207 @@
+// SPDX-License-Identifier: Apache-2.0
+// Device-side building blocks shared by every collective kernel.
+//
+// Each rank owns two symmetric allocations that every peer maps:
+//   ctrl: barrier flags, epochs, point-to-point counters, the LL region and
+//         the point-to-point slot rings;
+//   data: the staging region used by the barrier-based algorithms; when the
+//         node supports NVLS it is also bound to a multicast object, and
+//         `mcData` is its multicast address.
+// All cross-GPU waits are bounded by %globaltimer.  A wait that runs out (or
+// sees the host-mapped abort word) records an error in the host-mapped status
+// words and makes its block return; it never traps.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vccl {
+namespace dev {
+
+constexpr int kMaxRanks = 8;     // one NVSwitch domain of an HGX B200 board
+constexpr int kMaxBlocks = 128;  // largest grid of a barrier-based kernel
+constexpr int kLLBlocks = 16;    // fixed grid of the LL kernels
+constexpr int kMaxChannels = 8;  // point-to-point channels per peer
+constexpr int kP2pSlots = 4;     // ring depth of one channel
+
+// ---- ctrl allocation layout (byte offsets) ---------------------------------
+constexpr size_t kBarFlagsOff = 0;                                    // u32[kMaxBlocks][kMaxRanks], written by peers
+constexpr size_t kBarEpochOff = kBarFlagsOff + kMaxBlocks * kMaxRanks * 4;  // u32[kMaxBlocks], local
+constexpr size_t kLLEpochOff = kBarEpochOff + kMaxBlocks * 4;         // u32[kLLBlocks], local
+constexpr size_t kP2pHeadOff = 8192;                                  // u64[kMaxRanks][kMaxChannels], written by senders
+constexpr size_t kP2pTailOff = kP2pHeadOff + kMaxRanks * kMaxChannels * 8;  // written by receivers
+constexpr size_t kP2pSentOff = kP2pTailOff + kMaxRanks * kMaxChannels * 8;  // local
+constexpr size_t kP2pRecvdOff = kP2pSentOff + kMaxRanks * kMaxChannels * 8; // local
+constexpr size_t kFusedEpochOff = 16384;                              // u32[kMaxBlocks], local (fused kernels)
+constexpr size_t kFusedFlagsOff = 20480;                              // u32[kMaxBlocks][kMaxRanks], written by peers
+constexpr size_t kMoeCountsOff = 32768;                               // u32[2][kMaxRanks][64], written by peers
+constexpr size_t kCtrlHeader = 1 << 20;
+
+constexpr size_t kLLMaxBytes = 256 << 10;               // largest LL payload per rank
+constexpr size_t kLLSlotBytes = 2 * kLLMaxBytes;        // LL lines carry 8 payload bytes per 16
+constexpr size_t kLLOff = kCtrlHeader;                  // [parity][src rank][slot]
+constexpr size_t kLLBytes = 2 * kMaxRanks * kLLSlotBytes;
+
+constexpr size_t kP2pSlotBytes = 512 << 10;
+constexpr size_t kP2pOff = kLLOff + kLLBytes;           // [src rank][channel][slot]
+constexpr size_t kP2pBytes = size_t(kMaxRanks) * kMaxChannels * kP2pSlots * kP2pSlotBytes;
+constexpr size_t kCtrlBytes = kP2pOff + kP2pBytes;
+
+// Status words (host-mapped): [0] error code, [1] where, [2] rank, [3] detail.
+enum : uint32_t { kOk = 0, kErrTimeout = 1, kErrAborted = 2, kErrBadArg = 3 };
+
+struct DevComm {
+  int rank;
+  int nranks;
+  char* ctrl[kMaxRanks];  // every rank's ctrl allocation, mapped here
+  char* data[kMaxRanks];  // every rank's data allocation, mapped here
+  char* mcData;           // multicast address of the data allocations, or null
+  size_t dataBytes;
+  uint32_t* status;              // host-mapped, written by kernels
+  const uint32_t* abortWord;     // host-mapped, written by vcclCommAbort
+  uint64_t timeoutNs;
+};
+
+__device__ __forceinline__ uint64_t globalTimerNs() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t ldAcquireSys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t ldAcquireSys64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void stRelaxedSys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void stReleaseSys64(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void fenceSys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void fenceProxyAlias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+
+// Record the first failure.  Status lives in host-mapped memory: plain
+// volatile stores, first writer wins.
+__device__ __forceinline__ void recordFailure(const DevComm& c, uint32_t code, uint32_t where,
+                                              uint32_t detail) {
+  volatile uint32_t* s = c.status;
+  if (atomicCAS(c.status, 0u, code) == 0u) {
+    s[1] = where;
+    s[2] = static_cast<uint32_t>(c.rank);
+    s[3] = detail;
+  }
+  __threadfence_system();
+}
+
+__device__ __forceinline__ bool shouldGiveUp(const DevComm& c, uint64_t start, uint32_t where,
+                                             uint32_t detail) {
+  if (*reinterpret_cast<const volatile uint32_t*>(c.abortWord) != 0u) {
+    recordFailure(c, kErrAborted, where, detail);
+    return true;
+  }
+  if (globalTimerNs() - start > c.timeoutNs) {
+    recordFailure(c, kErrTimeout, where, detail);
+    return true;
+  }
+  return false;
+}
+
+// Spin until *flag - target >= 0 (wrapping compare).  False on timeout/abort.
+__device__ __forceinline__ bool waitAtLeast(const DevComm& c, const uint32_t* flag, uint32_t target,
+                                            uint32_t where, uint32_t detail) {
+  if (static_cast<int32_t>(ldAcquireSys(flag) - target) >= 0) return true;
+  const uint64_t start = globalTimerNs();
+  for (uint32_t spin = 1;; ++spin) {
+    if (static_cast<int32_t>(ldAcquireSys(flag) - target) >= 0) return true;
+    if ((spin & 255u) == 0u && shouldGiveUp(c, start, where, detail)) return false;
+  }
+}
+__device__ __forceinline__ bool waitAtLeast64(const DevComm& c, const uint64_t* flag,
+                                              uint64_t target, uint32_t where, uint32_t detail) {
+  if (ldAcquireSys64(flag) >= target) return true;
+  const uint64_t start = globalTimerNs();
+  for (uint32_t spin = 1;; ++spin) {
+    if (ldAcquireSys64(flag) >= target) return true;
+    if ((spin & 255u) == 0u && shouldGiveUp(c, start, where, detail)) return false;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ T* ctrlAt(const DevComm& c, int rank, size_t off) {
+  return reinterpret_cast<T*>(c.ctrl[rank] + off);
+}
+
+// All threads of the block call this.  Block `blk` of this rank meets block
+// `blk` of every other rank.  Writes made by the block before the call are
+// visible to the peers' blocks after it.  Returns false if the block must
+// abandon the kernel (timeout or abort recorded).
+__device__ __forceinline__ bool blockBarrier(const DevComm& c, int blk, uint32_t where,
+                                             size_t epochOff = kBarEpochOff,
+                                             size_t flagsOff = kBarFlagsOff) {
+  __shared__ uint32_t sEpoch;
+  __shared__ int sFailed;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t* ep = ctrlAt<uint32_t>(c, c.rank, epochOff) + blk;
+    sEpoch = *ep + 1u;
+    *ep = sEpoch;
+    sFailed = 0;
+  }
+  __syncthreads();
+  const int t = threadIdx.x;
+  if (t < c.nranks) {
+    const uint32_t e = sEpoch;
+    fenceSys();
+    stRelaxedSys(ctrlAt<uint32_t>(c, t, flagsOff) + blk * kMaxRanks + c.rank, e);
+    const uint32_t* mine = ctrlAt<uint32_t>(c, c.rank, flagsOff) + blk * kMaxRanks + t;
+    if (!waitAtLeast(c, mine, e, where, static_cast<uint32_t>(t))) sFailed = 1;
+  }
+  __syncthreads();
+  return sFailed == 0;
+}
+
+// ---- 16-byte vector memory helpers -----------------------------------------
+__device__ __forceinline__ uint4 ldCG(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 ldNC(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ void stG(void* p, const uint4& v) {
+  *reinterpret_cast<uint4*>(p) = v;
+}
+
+// Grid-stride byte copy with the widest access the alignment allows.
+__device__ __forceinline__ void copyBytes(char* dst, const char* src, size_t n, size_t tid,
+                                          size_t nthr) {
+  if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15u) == 0) {
+    const size_t nv = n / 16;
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    for (size_t i = tid; i < nv; i += nthr) d[i] = ldCG(s + i);
+    for (size_t i = nv * 16 + tid; i < n; i += nthr) dst[i] = src[i];
+  } else if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 3u) == 0) {
+    const size_t nw = n / 4;
+    const uint32_t* s = reinterpret_cast<const uint32_t*>(src);
+    uint32_t* d = reinterpret_cast<uint32_t*>(dst);
+    for (size_t i = tid; i < nw; i += nthr) d[i] = s[i];
+    for (size_t i = nw * 4 + tid; i < n; i += nthr) dst[i] = src[i];
+  } else {
+    for (size_t i = tid; i < n; i += nthr) dst[i] = src[i];
+  }
+}
+
+}  // namespace dev
+}  // namespace vccl

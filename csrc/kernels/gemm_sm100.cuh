@@ -1,0 +1,326 @@
+// SPDX-License-Identifier: Apache-2.0
+// Persistent bf16 GEMM on 5th-generation tensor cores (sm_100a).
+//
+//   C[M, N] = A[M, K] * B[N, K]^T      (A, B K-major; fp32 accumulation)
+//
+// One CTA per SM loops over output tiles.  Warp roles:
+//   warp 0     TMA producer: loads A and B k-blocks (128B swizzle) into a
+//              STAGES-deep shared-memory ring, signalling `full` mbarriers.
+//   warp 1     MMA issuer: one elected thread issues tcgen05.mma (M=128,
+//              N=BN, K=16) into a TMEM accumulator, releasing ring slots
+//              with tcgen05.commit -> `empty`.  Owns the TMEM allocation.
+//   warps 2-5  epilogue: tcgen05.ld the accumulator (warp w reads TMEM
+//              lanes 32*(w%4)..+31 = tile rows), apply the Epilogue policy,
+//              hand the accumulator back.  Two accumulators alternate so
+//              the epilogue of tile i overlaps the MMAs of tile i+1.
+// Epilogue policies are how the fused kernels (SiLU*mul, reduce-scatter
+// pushes to peer GPUs) reuse this mainloop.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "kernels/sm100.cuh"
+
+namespace vccl {
+namespace gemm {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // one 128-byte swizzle atom of bf16
+constexpr int kThreads = 192;
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOff = STAGES * kStageBytes;
+  static constexpr int kBytes = kBarOff + 256 + 1024;  // + barriers + alignment slack
+};
+
+struct TileInfo {
+  int tm, tn;  // tile coordinates
+  int row0, col0;
+};
+
+struct GemmShape {
+  int M, N, K;
+  int tilesM, tilesN;
+};
+
+// Tile order: consecutive CTAs share the B (weight) tile.
+__device__ __forceinline__ TileInfo tileAt(const GemmShape& s, int t, int BN) {
+  TileInfo ti;
+  ti.tn = t / s.tilesM;
+  ti.tm = t % s.tilesM;
+  ti.row0 = ti.tm * kBM;
+  ti.col0 = ti.tn * BN;
+  return ti;
+}
+
+__device__ __forceinline__ uint32_t packBf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Plain store of the accumulator to C (row-major, ldc elements).
+struct EpiStore {
+  __nv_bfloat16* C;
+  int ldc;
+  template <int BN>
+  __device__ __forceinline__ void operator()(uint32_t tmemAcc, const TileInfo& ti, const GemmShape& s,
+                                             int laneRow) const {
+    const int row = ti.row0 + laneRow;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      uint32_t r[16];
+      sm100::tmemLoad16(tmemAcc + c, r);
+      sm100::tmemLoadWait();
+      const int col = ti.col0 + c;
+      if (row < s.M && col < s.N) {
+        uint4 o0, o1;
+        o0.x = packBf16(__uint_as_float(r[0]), __uint_as_float(r[1]));
+        o0.y = packBf16(__uint_as_float(r[2]), __uint_as_float(r[3]));
+        o0.z = packBf16(__uint_as_float(r[4]), __uint_as_float(r[5]));
+        o0.w = packBf16(__uint_as_float(r[6]), __uint_as_float(r[7]));
+        o1.x = packBf16(__uint_as_float(r[8]), __uint_as_float(r[9]));
+        o1.y = packBf16(__uint_as_float(r[10]), __uint_as_float(r[11]));
+        o1.z = packBf16(__uint_as_float(r[12]), __uint_as_float(r[13]));
+        o1.w = packBf16(__uint_as_float(r[14]), __uint_as_float(r[15]));
+        uint4* dst = reinterpret_cast<uint4*>(C + static_cast<size_t>(row) * ldc + col);
+        dst[0] = o0;
+        dst[1] = o1;
+      }
+    }
+  }
+};
+
+// Gate/up epilogue.  B holds the gate and up projections interleaved in
+// groups of 16 rows (g0..15, u0..15, g16..31, u16..31, ...), so every
+// 32-column slice of the accumulator is (16 gate, 16 up) of the same output
+// columns for any tile width.  Writes silu(gate) * up; C has N/2 columns.
+struct EpiSiluMul {
+  __nv_bfloat16* C;
+  int ldc;
+  template <int BN>
+  __device__ __forceinline__ void operator()(uint32_t tmemAcc, const TileInfo& ti, const GemmShape& s,
+                                             int laneRow) const {
+    const int row = ti.row0 + laneRow;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t g[16], u[16];
+      sm100::tmemLoad16(tmemAcc + c, g);
+      sm100::tmemLoad16(tmemAcc + c + 16, u);
+      sm100::tmemLoadWait();
+      const int col = (ti.col0 + c) / 2;
+      if (row < s.M && col < s.N / 2) {
+        float o[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const float x = __uint_as_float(g[i]);
+          o[i] = x / (1.0f + __expf(-x)) * __uint_as_float(u[i]);
+        }
+        uint4 o0, o1;
+        o0.x = packBf16(o[0], o[1]);
+        o0.y = packBf16(o[2], o[3]);
+        o0.z = packBf16(o[4], o[5]);
+        o0.w = packBf16(o[6], o[7]);
+        o1.x = packBf16(o[8], o[9]);
+        o1.y = packBf16(o[10], o[11]);
+        o1.z = packBf16(o[12], o[13]);
+        o1.w = packBf16(o[14], o[15]);
+        uint4* dst = reinterpret_cast<uint4*>(C + static_cast<size_t>(row) * ldc + col);
+        dst[0] = o0;
+        dst[1] = o1;
+      }
+    }
+  }
+};
+
+// Hooks a fused kernel may provide around the tile loop (no-ops here).
+struct NoHooks {
+  // Called by every epilogue thread before the first tile.  Return false to
+  // abandon the kernel.
+  __device__ __forceinline__ bool beforeTiles(volatile int*) const { return true; }
+  // Called by every epilogue thread after its last tile (all its stores done).
+  __device__ __forceinline__ void afterTiles(volatile int*) const {}
+};
+
+template <int BN, int STAGES, typename Epi, typename Hooks = NoHooks>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemmKernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, GemmShape s,
+               Epi epi, Hooks hooks, int* errorFlag) {
+  using L = Smem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smemRaw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smemRaw) + 1023) & ~uintptr_t(1023));
+  uint64_t* fullBar = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* emptyBar = fullBar + STAGES;
+  uint64_t* accFull = emptyBar + STAGES;
+  uint64_t* accEmpty = accFull + 2;
+  uint64_t* drainBar = accEmpty + 2;
+  uint32_t* tmemSlot = reinterpret_cast<uint32_t*>(drainBar + 1);
+  volatile int* abortFlag = reinterpret_cast<volatile int*>(tmemSlot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  constexpr uint32_t kTmemCols = 2 * BN;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; i++) {
+      sm100::mbarInit(&fullBar[i], 1);
+      sm100::mbarInit(&emptyBar[i], 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      sm100::mbarInit(&accFull[i], 1);
+      sm100::mbarInit(&accEmpty[i], 4);
+    }
+    sm100::mbarInit(drainBar, 1);
+    *abortFlag = 0;
+    sm100::fenceBarrierInit();
+  }
+  if (warp == 1) {
+    sm100::tmemAlloc(tmemSlot, kTmemCols);
+    sm100::tmemRelinquish();
+  }
+  sm100::tcFenceBefore();
+  __syncthreads();
+  sm100::tcFenceAfter();
+  const uint32_t tmemBase = *tmemSlot;
+  const int numTiles = s.tilesM * s.tilesN;
+  const int numK = (s.K + kBK - 1) / kBK;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (sm100::electOne()) {
+      sm100::tmaPrefetchDesc(&mapA);
+      sm100::tmaPrefetchDesc(&mapB);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < numTiles && ok; t += gridDim.x) {
+        const TileInfo ti = tileAt(s, t, BN);
+        for (int kb = 0; kb < numK; kb++) {
+          if (!sm100::mbarWait(&emptyBar[stage], phase ^ 1u, abortFlag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a = smem + stage * L::kStageBytes;
+          uint8_t* b = a + L::kABytes;
+          sm100::mbarArriveExpectTx(&fullBar[stage], L::kStageBytes);
+          sm100::tmaLoad2d(a, &mapA, &fullBar[stage], kb * kBK, ti.row0);
+          sm100::tmaLoad2d(b, &mapB, &fullBar[stage], kb * kBK, ti.col0);
+          issued++;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let the copies already issued land before the CTA can exit.
+        const int n = issued < static_cast<uint32_t>(STAGES) ? static_cast<int>(issued) : STAGES;
+        int s2 = stage;
+        uint32_t p2 = phase;
+        for (int i = 0; i < n; i++) {
+          if (--s2 < 0) {
+            s2 = STAGES - 1;
+            p2 ^= 1u;
+          }
+          volatile int never = 0;
+          sm100::mbarWait(&fullBar[s2], p2, &never, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (sm100::electOne()) {
+      constexpr uint32_t idesc = sm100::idescBf16F32(kBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t accPhase = 0;
+      bool ok = true;
+      bool anyIssued = false;
+      for (int t = blockIdx.x; t < numTiles && ok; t += gridDim.x) {
+        if (!sm100::mbarWait(&accEmpty[acc], accPhase ^ 1u, abortFlag)) {
+          ok = false;
+          break;
+        }
+        sm100::tcFenceAfter();
+        const uint32_t tmemAcc = tmemBase + acc * BN;
+        for (int kb = 0; kb < numK; kb++) {
+          if (!sm100::mbarWait(&fullBar[stage], phase, abortFlag)) {
+            ok = false;
+            break;
+          }
+          sm100::tcFenceAfter();
+          const uint32_t aAddr = sm100::smemAddr(smem + stage * L::kStageBytes);
+          const uint32_t bAddr = aAddr + L::kABytes;
+          const uint64_t ad = sm100::smemDescSw128(aAddr);
+          const uint64_t bd = sm100::smemDescSw128(bAddr);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; k++) {
+            // +32 bytes per K=16 step inside the swizzle atom (descriptor units of 16 B).
+            sm100::mmaBf16(tmemAcc, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          anyIssued = true;
+          sm100::mmaCommit(&emptyBar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        sm100::mmaCommit(&accFull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          accPhase ^= 1u;
+        }
+      }
+      if (!ok && anyIssued) {
+        // Drain every MMA in flight before TMEM is released.
+        sm100::mmaCommit(drainBar);
+        volatile int never = 0;
+        sm100::mbarWait(drainBar, 0, &never, 200000000ull);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;             // TMEM lane quarter this warp may access
+    const int laneRow = quarter * 32 + lane;  // tile row of this thread
+    int acc = 0;
+    uint32_t accPhase = 0;
+    bool ok = hooks.beforeTiles(abortFlag);
+    if (!ok) *abortFlag = 1;
+    for (int t = blockIdx.x; t < numTiles && ok; t += gridDim.x) {
+      if (!sm100::mbarWait(&accFull[acc], accPhase, abortFlag)) {
+        ok = false;
+        break;
+      }
+      sm100::tcFenceAfter();
+      const TileInfo ti = tileAt(s, t, BN);
+      const uint32_t tmemAcc = tmemBase + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      epi.template operator()<BN>(tmemAcc, ti, s, laneRow);
+      sm100::tcFenceBefore();
+      __syncwarp();
+      if (lane == 0) sm100::mbarArrive(&accEmpty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        accPhase ^= 1u;
+      }
+    }
+    if (ok) hooks.afterTiles(abortFlag);
+  }
+
+  __syncthreads();
+  if (*abortFlag && threadIdx.x == 0 && errorFlag) atomicExch(errorFlag, 1);
+  if (warp == 1) {
+    sm100::tcFenceAfter();
+    sm100::tmemDealloc(tmemBase, kTmemCols);
+  }
+}
+
+}  // namespace gemm
+}  // namespace vccl

@@ -1,0 +1,106 @@
+// SPDX-License-Identifier: Apache-2.0
+// Communicator state.
+//
+// Mirrors the reference communicator's responsibilities (reference:
+// src/core/comm.h:19-169): rank/size, bootstrap, registrations, PreMulSum op
+// table, first-error latch with abort, last-error text.  The transport and
+// its MR cache are replaced by DeviceState: the symmetric NVLink workspaces,
+// the optional NVLS multicast mapping, a private stream and the host-mapped
+// status/abort words that kernels report through.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "control/bootstrap.h"
+#include "kernels/device_common.cuh"
+#include "vccl.h"
+
+namespace vccl {
+
+// One cuMem allocation per rank, exported to and mapped by every rank.
+struct SymmetricBuffer {
+  size_t bytes = 0;
+  size_t align = 0;
+  CUmemGenericAllocationHandle localHandle = 0;
+  std::vector<CUmemGenericAllocationHandle> handles;  // per rank (imported for peers)
+  std::vector<CUdeviceptr> va;                         // per rank mapping in this process
+  // NVLS
+  CUmemGenericAllocationHandle mcHandle = 0;
+  CUdeviceptr mcVa = 0;
+  bool mcBound = false;
+};
+
+struct DeviceState {
+  int device = -1;
+  CUdevice cuDevice = 0;
+  int smCount = 0;
+  cudaStream_t stream = nullptr;   // internal stream (blocking helpers)
+  SymmetricBuffer ctrl;
+  SymmetricBuffer data;
+  bool nvls = false;
+  uint32_t* hostStatus = nullptr;  // pinned + mapped
+  uint32_t* devStatus = nullptr;
+  uint32_t* hostAbort = nullptr;
+  uint32_t* devAbort = nullptr;
+  dev::DevComm dc{};
+  int nblocks = 32;                // grid of barrier-based kernels
+  size_t llMaxBytes = 0;           // LL all-reduce threshold
+};
+
+struct CustomOp {
+  double scalar = 1.0;
+  bool live = false;
+};
+
+struct Registration {
+  void* base = nullptr;
+  size_t bytes = 0;
+  bool hostPinned = false;                    // we cudaHostRegister'ed it
+  void* mapped = nullptr;                     // dmabuf host mapping we own
+  size_t mappedBytes = 0;
+  CUmemGenericAllocationHandle imported = 0;  // VMM import we own
+  CUdeviceptr importedVa = 0;
+  size_t importedBytes = 0;
+  cudaExternalMemory_t extMem = nullptr;      // external-memory import we own
+};
+
+vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<DeviceState>* out);
+void deviceStateDestroy(DeviceState* ds, Bootstrap* bs, bool peersAlive);
+
+}  // namespace vccl
+
+struct vcclComm {
+  int rank = -1;
+  int nranks = 0;
+  bool blocking = true;
+  std::unique_ptr<vccl::Bootstrap> bootstrap;
+  std::unique_ptr<vccl::DeviceState> dev;
+
+  std::atomic<vcclResult_t> asyncError{vcclSuccess};
+  std::atomic<bool> aborted{false};
+  std::mutex errMu;
+  std::string lastError;
+
+  std::vector<vccl::CustomOp> customOps;
+  std::mutex opsMu;
+
+  std::mutex regMu;
+  std::vector<vccl::Registration*> regs;
+
+  int device() const { return dev ? dev->device : -1; }
+
+  // First error wins; fatal codes latch the communicator dead so later calls
+  // fail fast with vcclInvalidUsage (reference: src/core/comm.h:150-168).
+  void noteError(vcclResult_t r);
+  // Pull a kernel-reported failure from the host-mapped status words.
+  vcclResult_t pollDeviceStatus();
+  bool premulScalar(vcclRedOp_t op, double* scalar);
+};

@@ -1,0 +1,327 @@
+// SPDX-License-Identifier: Apache-2.0
+// Device data plane set-up: symmetric workspaces and NVLS multicast.
+//
+// Replaces the reference's transport creation (reference:
+// src/transport/tcp.cc:26-92, src/transport/verbs.cc:256-304): instead of
+// sockets or RDMA queue pairs, every rank allocates exportable device memory
+// with the CUDA VMM API, hands the POSIX fd to every peer over the bootstrap's
+// Unix sockets, and maps every peer's allocation into its own address space.
+// Kernels then load and store peer memory directly over NVLink.
+#include <unistd.h>
+
+#include <cstring>
+
+#include "common/env.h"
+#include "common/log.h"
+#include "runtime/comm.h"
+#include "runtime/cudrv.h"
+
+namespace vccl {
+namespace {
+
+#define CU_TRY(call)                                                          \
+  do {                                                                        \
+    CUresult cu_r_ = (call);                                                  \
+    if (cu_r_ != CUDA_SUCCESS) {                                              \
+      VERR("%s failed: %s", #call, cuErrorText(cu_r_));                       \
+      return vcclSystemError;                                                 \
+    }                                                                         \
+  } while (0)
+
+#define CUDART_TRY(call)                                                      \
+  do {                                                                        \
+    cudaError_t rt_e_ = (call);                                               \
+    if (rt_e_ != cudaSuccess) {                                               \
+      VERR("%s failed: %s", #call, cudaGetErrorString(rt_e_));                \
+      return vcclSystemError;                                                 \
+    }                                                                         \
+  } while (0)
+
+size_t roundUp(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+CUmemAllocationProp exportableProp(int device) {
+  CUmemAllocationProp prop;
+  memset(&prop, 0, sizeof(prop));
+  prop.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+  prop.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+  prop.location.id = device;
+  prop.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+  return prop;
+}
+
+vcclResult_t mapForDevice(const DriverApi* d, CUmemGenericAllocationHandle h, size_t bytes,
+                          size_t align, int device, CUdeviceptr* va) {
+  CU_TRY(d->memAddressReserve(va, bytes, align, 0, 0));
+  CUresult r = d->memMap(*va, bytes, 0, h, 0);
+  if (r != CUDA_SUCCESS) {
+    d->memAddressFree(*va, bytes);
+    *va = 0;
+    VERR("cuMemMap failed: %s", cuErrorText(r));
+    return vcclSystemError;
+  }
+  CUmemAccessDesc acc;
+  memset(&acc, 0, sizeof(acc));
+  acc.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+  acc.location.id = device;
+  acc.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
+  r = d->memSetAccess(*va, bytes, &acc, 1);
+  if (r != CUDA_SUCCESS) {
+    d->memUnmap(*va, bytes);
+    d->memAddressFree(*va, bytes);
+    *va = 0;
+    VERR("cuMemSetAccess failed: %s", cuErrorText(r));
+    return vcclSystemError;
+  }
+  return vcclSuccess;
+}
+
+// Allocate `bytes` (already rounded) on this device, export, exchange, map
+// every rank's allocation.
+vcclResult_t symmetricAlloc(Bootstrap* bs, DeviceState* ds, size_t bytes, size_t align,
+                            SymmetricBuffer* b) {
+  const DriverApi* d = driverApi();
+  const int n = bs->nranks(), me = bs->rank();
+  CUmemAllocationProp prop = exportableProp(ds->device);
+  b->bytes = bytes;
+  b->align = align;
+  CU_TRY(d->memCreate(&b->localHandle, bytes, &prop, 0));
+  int fd = -1;
+  CU_TRY(d->memExport(&fd, b->localHandle, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0));
+  std::vector<std::vector<int>> fds;
+  vcclResult_t res = bs->exchangeFds({fd}, &fds);
+  closeFd(fd);
+  VTRY(res);
+  b->handles.assign(n, 0);
+  b->va.assign(n, 0);
+  for (int p = 0; p < n; p++) {
+    if (p == me) {
+      b->handles[p] = b->localHandle;
+    } else if (res == vcclSuccess) {
+      CUresult r = d->memImport(&b->handles[p],
+                                reinterpret_cast<void*>(static_cast<uintptr_t>(fds[p][0])),
+                                CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR);
+      if (r != CUDA_SUCCESS) {
+        VERR("cuMemImportFromShareableHandle (rank %d) failed: %s", p, cuErrorText(r));
+        res = vcclSystemError;
+      }
+    }
+    for (int f : fds[p]) closeFd(f);
+  }
+  VTRY(res);
+  for (int p = 0; p < n; p++) VTRY(mapForDevice(d, b->handles[p], bytes, align, ds->device, &b->va[p]));
+  return vcclSuccess;
+}
+
+void symmetricFree(const DriverApi* d, int me, SymmetricBuffer* b) {
+  for (size_t p = 0; p < b->va.size(); p++) {
+    if (b->va[p]) {
+      d->memUnmap(b->va[p], b->bytes);
+      d->memAddressFree(b->va[p], b->bytes);
+    }
+    if (b->handles.size() > p && b->handles[p] && static_cast<int>(p) != me) d->memRelease(b->handles[p]);
+  }
+  if (b->localHandle) d->memRelease(b->localHandle);
+  b->va.clear();
+  b->handles.clear();
+  b->localHandle = 0;
+}
+
+// Every rank reports success of a step; all ranks learn whether everyone
+// succeeded (so that optional features are enabled or skipped together).
+bool everyone(Bootstrap* bs, bool mine) {
+  std::vector<uint8_t> v(bs->nranks(), 0);
+  v[bs->rank()] = mine ? 1 : 0;
+  if (bs->allGather(v.data(), 1) != vcclSuccess) return false;
+  for (uint8_t x : v)
+    if (!x) return false;
+  return true;
+}
+
+void multicastTeardown(const DriverApi* d, DeviceState* ds) {
+  SymmetricBuffer& b = ds->data;
+  if (b.mcVa) {
+    d->memUnmap(b.mcVa, b.bytes);
+    d->memAddressFree(b.mcVa, b.bytes);
+    b.mcVa = 0;
+  }
+  if (b.mcBound) {
+    d->mcUnbind(b.mcHandle, ds->cuDevice, 0, b.bytes);
+    b.mcBound = false;
+  }
+  if (b.mcHandle) {
+    d->memRelease(b.mcHandle);
+    b.mcHandle = 0;
+  }
+}
+
+vcclResult_t multicastSetup(Bootstrap* bs, DeviceState* ds) {
+  const DriverApi* d = driverApi();
+  SymmetricBuffer& b = ds->data;
+  const int n = bs->nranks(), me = bs->rank();
+  CUmulticastObjectProp mp;
+  memset(&mp, 0, sizeof(mp));
+  mp.numDevices = static_cast<unsigned int>(n);
+  mp.size = b.bytes;
+  mp.handleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+  bool ok = true;
+  int fd = -1;
+  if (me == 0) {
+    ok = d->mcCreate(&b.mcHandle, &mp) == CUDA_SUCCESS &&
+         d->memExport(&fd, b.mcHandle, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0) == CUDA_SUCCESS;
+  }
+  if (!everyone(bs, ok)) {
+    closeFd(fd);
+    multicastTeardown(d, ds);
+    return vcclInternalError;
+  }
+  std::vector<int> fds;
+  if (me == 0) fds.push_back(fd);
+  VTRY(bs->broadcastFds(0, &fds, 1));
+  if (me == 0) {
+    closeFd(fd);
+  } else {
+    ok = fds.size() == 1 &&
+         d->memImport(&b.mcHandle, reinterpret_cast<void*>(static_cast<uintptr_t>(fds[0])),
+                      CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR) == CUDA_SUCCESS;
+    for (int f : fds) closeFd(f);
+  }
+  ok = ok && d->mcAddDevice(b.mcHandle, ds->cuDevice) == CUDA_SUCCESS;
+  // Every device must be added before any memory is bound.
+  if (!everyone(bs, ok)) {
+    multicastTeardown(d, ds);
+    return vcclInternalError;
+  }
+  CUresult br = d->mcBindMem(b.mcHandle, 0, b.localHandle, 0, b.bytes, 0);
+  ok = br == CUDA_SUCCESS;
+  if (!ok) VWARN("cuMulticastBindMem failed: %s", cuErrorText(br));
+  b.mcBound = ok;
+  if (!everyone(bs, ok)) {
+    multicastTeardown(d, ds);
+    return vcclInternalError;
+  }
+  ok = mapForDevice(d, b.mcHandle, b.bytes, b.align, ds->device, &b.mcVa) == vcclSuccess;
+  if (!everyone(bs, ok)) {
+    multicastTeardown(d, ds);
+    return vcclInternalError;
+  }
+  return vcclSuccess;
+}
+
+}  // namespace
+
+vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<DeviceState>* out) {
+  const DriverApi* d = driverApi();
+  if (d == nullptr) return vcclSystemError;
+  auto ds = std::make_unique<DeviceState>();
+  ds->device = device;
+  CUDART_TRY(cudaSetDevice(device));
+  CUDART_TRY(cudaFree(nullptr));
+  CU_TRY(d->deviceGet(&ds->cuDevice, device));
+  CUDART_TRY(cudaDeviceGetAttribute(&ds->smCount, cudaDevAttrMultiProcessorCount, device));
+  CUDART_TRY(cudaStreamCreateWithFlags(&ds->stream, cudaStreamNonBlocking));
+  CUDART_TRY(cudaHostAlloc(reinterpret_cast<void**>(&ds->hostStatus), 64,
+                           cudaHostAllocMapped | cudaHostAllocPortable));
+  CUDART_TRY(cudaHostAlloc(reinterpret_cast<void**>(&ds->hostAbort), 64,
+                           cudaHostAllocMapped | cudaHostAllocPortable));
+  memset(ds->hostStatus, 0, 64);
+  memset(ds->hostAbort, 0, 64);
+  CUDART_TRY(cudaHostGetDevicePointer(reinterpret_cast<void**>(&ds->devStatus), ds->hostStatus, 0));
+  CUDART_TRY(cudaHostGetDevicePointer(reinterpret_cast<void**>(&ds->devAbort), ds->hostAbort, 0));
+
+  const int n = bs->nranks(), me = bs->rank();
+  ds->nblocks = static_cast<int>(envLong("VCCL_NBLOCKS", 64));
+  if (ds->nblocks < 1) ds->nblocks = 1;
+  if (ds->nblocks > dev::kMaxBlocks) ds->nblocks = dev::kMaxBlocks;
+  ds->llMaxBytes = envBytes("VCCL_LL_MAX", 64u << 10);
+  if (ds->llMaxBytes > dev::kLLMaxBytes) ds->llMaxBytes = dev::kLLMaxBytes;
+
+  if (n > 1) {
+    if (n > dev::kMaxRanks) {
+      VERR("device communicators support at most %d ranks (one NVSwitch domain)", dev::kMaxRanks);
+      return vcclInvalidUsage;
+    }
+    // Granularities: every rank computes the same values on identical GPUs;
+    // the allgather below double-checks the resulting sizes.
+    CUmemAllocationProp prop = exportableProp(device);
+    size_t gran = 0;
+    CU_TRY(d->memGranularity(&gran, &prop, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED));
+    size_t dataAlign = gran;
+    const bool tryNvls = envLong("VCCL_NVLS_ENABLE", 1) != 0 && d->mcCreate != nullptr;
+    int mcCap = 0;
+    if (tryNvls) d->deviceGetAttribute(&mcCap, CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED, ds->cuDevice);
+    size_t dataBytes = envBytes("VCCL_BUFFSIZE", 256u << 20);
+    if (dataBytes < (4u << 20)) dataBytes = 4u << 20;
+    if (mcCap) {
+      CUmulticastObjectProp mp;
+      memset(&mp, 0, sizeof(mp));
+      mp.numDevices = static_cast<unsigned int>(n);
+      mp.size = dataBytes;
+      mp.handleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+      size_t mg = 0;
+      if (d->mcGranularity(&mg, &mp, CU_MULTICAST_GRANULARITY_RECOMMENDED) == CUDA_SUCCESS && mg > 0)
+        dataAlign = std::max(dataAlign, mg);
+      else
+        mcCap = 0;
+    }
+    dataBytes = roundUp(dataBytes, dataAlign);
+    const size_t ctrlBytes = roundUp(dev::kCtrlBytes, gran);
+    struct Sizes { uint64_t ctrl, data; } mine{ctrlBytes, dataBytes};
+    std::vector<Sizes> all(n);
+    all[me] = mine;
+    VTRY(bs->allGather(all.data(), sizeof(Sizes)));
+    for (const Sizes& s : all) {
+      if (s.ctrl != mine.ctrl || s.data != mine.data) {
+        VERR("ranks disagree on workspace sizes (check VCCL_BUFFSIZE on every rank)");
+        return vcclInvalidUsage;
+      }
+    }
+    VTRY(symmetricAlloc(bs, ds.get(), ctrlBytes, gran, &ds->ctrl));
+    VTRY(symmetricAlloc(bs, ds.get(), dataBytes, dataAlign, &ds->data));
+    CUDART_TRY(cudaMemset(reinterpret_cast<void*>(ds->ctrl.va[me]), 0, dev::kCtrlHeader));
+    CUDART_TRY(cudaMemset(reinterpret_cast<void*>(ds->ctrl.va[me] + dev::kLLOff), 0xff, dev::kLLBytes));
+    CUDART_TRY(cudaDeviceSynchronize());
+    VTRY(bs->barrier());
+    if (everyone(bs, mcCap != 0)) ds->nvls = multicastSetup(bs, ds.get()) == vcclSuccess;
+    VINFO("rank %d/%d on device %d: workspace ctrl %zu MiB, data %zu MiB, NVLS %s", me, n, device,
+          ctrlBytes >> 20, dataBytes >> 20, ds->nvls ? "on" : "off");
+  }
+
+  dev::DevComm& dc = ds->dc;
+  memset(&dc, 0, sizeof(dc));
+  dc.rank = me;
+  dc.nranks = n;
+  for (int p = 0; p < n && n > 1; p++) {
+    dc.ctrl[p] = reinterpret_cast<char*>(ds->ctrl.va[p]);
+    dc.data[p] = reinterpret_cast<char*>(ds->data.va[p]);
+  }
+  dc.mcData = ds->nvls ? reinterpret_cast<char*>(ds->data.mcVa) : nullptr;
+  dc.dataBytes = ds->data.bytes;
+  dc.status = ds->devStatus;
+  dc.abortWord = ds->devAbort;
+  dc.timeoutNs = deviceTimeoutNs();
+  *out = std::move(ds);
+  return vcclSuccess;
+}
+
+void deviceStateDestroy(DeviceState* ds, Bootstrap* bs, bool peersAlive) {
+  if (ds == nullptr) return;
+  const DriverApi* d = driverApi();
+  cudaSetDevice(ds->device);
+  if (ds->stream) cudaStreamSynchronize(ds->stream);
+  cudaDeviceSynchronize();
+  cudaGetLastError();
+  // Peers may still be reading our memory until they are done too.
+  if (peersAlive && bs && bs->nranks() > 1) bs->barrier();
+  if (d) {
+    multicastTeardown(d, ds);
+    symmetricFree(d, bs ? bs->rank() : 0, &ds->data);
+    symmetricFree(d, bs ? bs->rank() : 0, &ds->ctrl);
+  }
+  if (ds->hostStatus) cudaFreeHost(ds->hostStatus);
+  if (ds->hostAbort) cudaFreeHost(ds->hostAbort);
+  if (ds->stream) cudaStreamDestroy(ds->stream);
+  ds->hostStatus = ds->hostAbort = nullptr;
+  ds->stream = nullptr;
+}
+
+}  // namespace vccl

@@ -1,0 +1,40 @@
+// SPDX-License-Identifier: Apache-2.0
+// Host-side kernel launchers (one translation unit per kernel family so the
+// template instantiations compile in parallel).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "kernels/coll_abi.cuh"
+#include "kernels/dtypes.cuh"
+#include "vccl.h"
+
+namespace vccl {
+
+enum class ArAlgo : int { LL = 0, TwoShot = 1, Nvls = 2 };
+
+struct LaunchCtx {
+  dev::DevComm dc;
+  cudaStream_t stream;
+  int nblocks;     // max grid of barrier kernels
+  bool nvls;
+};
+
+// redKind: dev::kSum/kProd/kMax/kMin.  Returns cudaErrorInvalidValue for an
+// unsupported combination (the caller picks another algorithm).
+cudaError_t launchAllReduce(const LaunchCtx& lc, ArAlgo algo, vcclDataType_t dt, int redKind,
+                            const dev::CollArgs& a);
+cudaError_t launchReduceScatter(const LaunchCtx& lc, vcclDataType_t dt, int redKind,
+                                const dev::CollArgs& a);
+cudaError_t launchAllGather(const LaunchCtx& lc, const void* send, void* recv, size_t bytes);
+cudaError_t launchBroadcast(const LaunchCtx& lc, const void* send, void* recv, size_t bytes, int root,
+                            bool useNvls);
+cudaError_t launchP2p(const LaunchCtx& lc, const dev::P2pPlan& plan);
+// Single-rank helpers: dst = src * scale (float types) or plain copy.
+cudaError_t launchScaleCopy(cudaStream_t s, vcclDataType_t dt, void* dst, const void* src, size_t count,
+                            double scale);
+
+bool nvlsSupports(vcclDataType_t dt, int redKind);
+int gridFor(size_t bytes, int maxBlocks);
+
+}  // namespace vccl

@@ -1,0 +1,81 @@
+// SPDX-License-Identifier: Apache-2.0
+// All-reduce / reduce launchers (LL, two-shot, NVLS).
+#include "kernels/collectives.cuh"
+#include "runtime/dispatch.cuh"
+#include "runtime/launch.h"
+
+namespace vccl {
+
+constexpr int kThreads = 512;
+
+int gridFor(size_t bytes, int maxBlocks) {
+  // ~32 KiB per block: each block keeps 8 x 16 B loads per thread in flight
+  // (64 KiB at 512 threads), so this fills the NVLink pipe with enough
+  // blocks while small messages do not pay for idle ones.
+  size_t g = (bytes + (32u << 10) - 1) / (32u << 10);
+  if (g < 1) g = 1;
+  if (g > static_cast<size_t>(maxBlocks)) g = maxBlocks;
+  return static_cast<int>(g);
+}
+
+bool nvlsSupports(vcclDataType_t dt, int k) {
+  if (k == dev::kSum) return dt == vcclFloat32 || dt == vcclBfloat16 || dt == vcclFloat16;
+  if (k == dev::kMin || k == dev::kMax) return dt == vcclBfloat16 || dt == vcclFloat16;
+  return false;
+}
+
+cudaError_t launchAllReduce(const LaunchCtx& lc, ArAlgo algo, vcclDataType_t dt, int redKind,
+                            const dev::CollArgs& a) {
+  const size_t esz = vcclTypeSize(dt);
+  const size_t bytes = a.count * esz;
+  const int n = lc.dc.nranks;
+  if (algo == ArAlgo::LL) {
+    if (bytes > dev::kLLMaxBytes ||
+        ((reinterpret_cast<uintptr_t>(a.send) | reinterpret_cast<uintptr_t>(a.recv)) & 7u) != 0 || a.root >= 0)
+      return cudaErrorInvalidValue;
+    VCCL_DISPATCH_TYPE(dt, VCCL_DISPATCH_OP(redKind, {
+      dev::allReduceLL<T, K><<<dev::kLLBlocks, kThreads, 0, lc.stream>>>(lc.dc, a);
+    }))
+    return cudaGetLastError();
+  }
+  if (algo == ArAlgo::Nvls) {
+    if (!lc.nvls || !nvlsSupports(dt, redKind) || a.root >= 0) return cudaErrorInvalidValue;
+    const size_t roundBytes = (lc.dc.dataBytes - 16 * dev::kMaxRanks) / 16 * 16;
+    const int g = gridFor(bytes / n, lc.nblocks);
+    switch (dt) {
+      case vcclFloat32:
+        dev::allReduceNvls<float, dev::kSum><<<g, kThreads, 0, lc.stream>>>(lc.dc, a, roundBytes);
+        break;
+      case vcclBfloat16:
+        VCCL_DISPATCH_OP(redKind, {
+          if constexpr (dev::HasMultimem<__nv_bfloat16, K>::value)
+            dev::allReduceNvls<__nv_bfloat16, K><<<g, kThreads, 0, lc.stream>>>(lc.dc, a, roundBytes);
+        })
+        break;
+      case vcclFloat16:
+        VCCL_DISPATCH_OP(redKind, {
+          if constexpr (dev::HasMultimem<__half, K>::value)
+            dev::allReduceNvls<__half, K><<<g, kThreads, 0, lc.stream>>>(lc.dc, a, roundBytes);
+        })
+        break;
+      default:
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+  }
+  // Two-shot (all-reduce, or reduce when a.root >= 0).
+  const bool vec = ((reinterpret_cast<uintptr_t>(a.send) | reinterpret_cast<uintptr_t>(a.recv)) & 15u) == 0;
+  const size_t pk = 16 / esz;
+  size_t slotElems = lc.dc.dataBytes / (n + 1) / esz;
+  slotElems = slotElems / pk * pk;
+  const int g = gridFor(bytes / n, lc.nblocks);
+  VCCL_DISPATCH_TYPE(dt, VCCL_DISPATCH_OP(redKind, {
+    if (vec)
+      dev::allReduceTwoShot<T, K, true><<<g, kThreads, 0, lc.stream>>>(lc.dc, a, slotElems);
+    else
+      dev::allReduceTwoShot<T, K, false><<<g, kThreads, 0, lc.stream>>>(lc.dc, a, slotElems);
+  }))
+  return cudaGetLastError();
+}
+
+}  // namespace vccl

@@ -1,0 +1,67 @@
+// SPDX-License-Identifier: Apache-2.0
+// vccl-info: survey of the GPUs, their NVLink peer access and NVLS
+// (multicast) support, marking what the library will use.
+//
+// Replaces the reference's RDMA device / GID survey (reference:
+// tools/vccl_info.cc:66-114) with the B200 data plane's equivalents: which
+// devices exist, which pairs can map each other's memory over NVLink, and
+// whether NVSwitch multicast objects (NVLS) can be created.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+
+int main() {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    std::printf("no CUDA devices visible\n");
+    return 0;
+  }
+  using GetAttr = CUresult (*)(int*, CUdevice_attribute, CUdevice);
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q{};
+  cudaGetDriverEntryPointByVersion("cuDeviceGetAttribute", &fn, 2000, cudaEnableDefault, &q);
+  GetAttr getAttr = reinterpret_cast<GetAttr>(fn);
+  int drv = 0, rt = 0;
+  cudaDriverGetVersion(&drv);
+  cudaRuntimeGetVersion(&rt);
+  std::printf("CUDA driver %d, runtime %d, %d device(s)\n", drv, rt, n);
+  for (int d = 0; d < n; d++) {
+    cudaDeviceProp p;
+    cudaGetDeviceProperties(&p, d);
+    int mc = 0, vmm = 0, fd = 0;
+    if (getAttr) {
+      getAttr(&mc, CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED, d);
+      getAttr(&vmm, CU_DEVICE_ATTRIBUTE_VIRTUAL_MEMORY_MANAGEMENT_SUPPORTED, d);
+      getAttr(&fd, CU_DEVICE_ATTRIBUTE_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR_SUPPORTED, d);
+    }
+    std::printf("  [%d] %s sm_%d%d  %d SMs  %.1f GiB  bus %02x:%02x  VMM=%d posix-fd=%d multicast(NVLS)=%d\n", d,
+                p.name, p.major, p.minor, p.multiProcessorCount, p.totalGlobalMem / 1073741824.0, p.pciBusID,
+                p.pciDeviceID, vmm, fd, mc);
+  }
+  std::printf("peer access matrix (P = NVLink/P2P capable, A = native atomics):\n      ");
+  for (int b = 0; b < n; b++) std::printf("%4d", b);
+  std::printf("\n");
+  bool allPeer = true;
+  for (int a = 0; a < n; a++) {
+    std::printf("  %2d: ", a);
+    for (int b = 0; b < n; b++) {
+      if (a == b) {
+        std::printf("   -");
+        continue;
+      }
+      int can = 0, atom = 0;
+      cudaDeviceCanAccessPeer(&can, a, b);
+      cudaDeviceGetP2PAttribute(&atom, cudaDevP2PAttrNativeAtomicSupported, a, b);
+      allPeer &= can != 0;
+      std::printf("  %c%c", can ? 'P' : '.', atom ? 'A' : ' ');
+    }
+    std::printf("\n");
+  }
+  const char* nvlsEnv = std::getenv("VCCL_NVLS_ENABLE");
+  const bool nvlsOff = nvlsEnv && std::atoi(nvlsEnv) == 0;
+  std::printf("vccl will use: %s peer-to-peer workspaces%s\n", allPeer ? "NVLink" : "(NOT all pairs P2P!)",
+              nvlsOff ? ", NVLS disabled by VCCL_NVLS_ENABLE=0" : ", NVLS multicast when every rank supports it");
+  return 0;
+}

@@ -1,0 +1,67 @@
+/* SPDX-License-Identifier: Apache-2.0
+ *
+ * vccl-b200 fused tensor-parallel operations (additions; no counterpart in
+ * the reference C API).
+ *
+ * All calls are stream-ordered, take device pointers, and use bf16 row-major
+ * tensors unless stated.  Weights follow torch.nn.Linear: W[out, in].
+ */
+#ifndef VCCL_TP_H_
+#define VCCL_TP_H_
+
+#include "vccl.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* C[M,N] = A[M,K] * W[N,K]^T on tcgen05 tensor cores (K % 8 == 0,
+ * N % 16 == 0, 16-byte aligned pointers). */
+vcclResult_t vcclGemmBf16(const void* A, const void* W, void* C, int M, int N, int K, vcclStream_t stream);
+
+/* H[M,N/2] = silu(A W_g^T) * (A W_u^T), with W[N,K] holding gate and up rows
+ * interleaved in groups of 16 (vcclInterleaveGateUp layout). */
+vcclResult_t vcclGemmSiluMul(const void* A, const void* W, void* H, int M, int N, int K, vcclStream_t stream);
+
+/* out = RMSNorm(residual + AllReduce(partial)) * weight, and residual is
+ * updated in place to residual + AllReduce(partial).  Shapes [rows, hidden]. */
+vcclResult_t vcclAllReduceAddRMSNorm(const void* partial, void* residual, const void* weight, void* out,
+                                     size_t rows, size_t hidden, float eps, vcclDataType_t datatype,
+                                     vcclComm_t comm, vcclStream_t stream);
+
+/* Row-parallel GEMM fused with reduce-scatter over the communicator:
+ * every rank computes P = A[M,K] W[N,K]^T, rows of P are owned by rank
+ * (row / (M / nranks)); out[M/nranks, N] = sum over ranks of the owned rows.
+ * Tiles are pushed to their owner over NVLink from the GEMM epilogue. */
+vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void* out, int M, int N, int K,
+                                   vcclComm_t comm, vcclStream_t stream);
+
+/* All-gather fused into a column-parallel GEMM: X_shard[M/nranks, K] per
+ * rank, out = AllGather(X)[M,K] W[N,K]^T.  With siluMul != 0 the epilogue
+ * applies silu(gate)*up (W interleaved as for vcclGemmSiluMul; out has N/2
+ * columns).  Remote shards are pulled into local memory by copy warps while
+ * the tensor cores work on the shards already present. */
+vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, void* out, int M, int N, int K, int siluMul,
+                               vcclComm_t comm, vcclStream_t stream);
+
+/* Expert-parallel MoE dispatch with fp8 e4m3 1x128 block quantisation.
+ * x[T,H] bf16, topkIds[T,topk] int32 (global expert ids), topkW[T,topk] f32,
+ * experts split evenly over ranks.  recvX receives the bf16 (dequantised)
+ * rows this rank's experts must process, in (source rank, token, k) order;
+ * recvMeta[i] = {source rank, source token, k, local expert}; *recvCount is
+ * written on the device.  capacity bounds rows per rank. */
+vcclResult_t vcclMoeDispatchFp8(const void* x, const int* topkIds, const float* topkW, void* recvX, int* recvMeta,
+                                float* recvW, int* recvCount, int T, int H, int topk, int numExperts, int capacity,
+                                vcclComm_t comm, vcclStream_t stream);
+
+/* Inverse of dispatch: expertOut[rows,H] (bf16) travels back to the source
+ * ranks and out[T,H] = sum_k topkW[t,k] * expertOut(t,k). */
+vcclResult_t vcclMoeCombine(const void* expertOut, const int* recvMeta, const float* recvW, const int* recvCount,
+                            void* out, int T, int H, int topk, int capacity, vcclComm_t comm,
+                            vcclStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VCCL_TP_H_ */

@@ -1,0 +1,73 @@
+# SPDX-License-Identifier: Apache-2.0
+"""tcgen05 GEMM numerics vs a plain fp32 PyTorch reference."""
+
+import pytest
+import torch
+
+from conftest import gpu_count
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [
+    (128, 256, 64),
+    (1, 3584, 4096),      # decode, gate/up shard
+    (32, 4096, 1792),     # decode, down shard
+    (300, 528, 200),      # ragged M and K
+    (512, 3584, 4096),
+    (2048, 4096, 1792),
+]
+
+
+def _ref(a, w):
+    return (a.float() @ w.float().T)
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_gemm_bf16(m, n, k):
+    if gpu_count() == 0:
+        pytest.skip("no GPU")
+    from vkccl_b200.ops.gemm import gemm_bf16
+
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.02).bfloat16()
+    out = gemm_bf16(a, w)
+    torch.cuda.synchronize()
+    ref = _ref(a, w)
+    err = (out.float() - ref).abs().max().item()
+    scale = ref.abs().max().item() + 1e-6
+    assert err <= 1e-2 * scale + 1e-3, f"max err {err} (scale {scale})"
+
+
+@pytest.mark.parametrize("bn", [256, 128, 64, 32])
+def test_gemm_all_tile_widths(bn, monkeypatch):
+    if gpu_count() == 0:
+        pytest.skip("no GPU")
+    monkeypatch.setenv("VCCL_GEMM_BN", str(bn))
+    from vkccl_b200.ops.gemm import gemm_bf16
+
+    a = torch.randn(384, 1024, device="cuda").bfloat16()
+    w = (torch.randn(768, 1024, device="cuda") * 0.02).bfloat16()
+    out = gemm_bf16(a, w)
+    ref = _ref(a, w)
+    torch.cuda.synchronize()
+    assert (out.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item() + 1e-3
+
+
+@pytest.mark.parametrize("m", [1, 32, 512])
+def test_gemm_silu_mul(m):
+    if gpu_count() == 0:
+        pytest.skip("no GPU")
+    from vkccl_b200.ops.gemm import gemm_silu_mul, interleave_gate_up
+
+    k, inter = 4096, 1792
+    a = torch.randn(m, k, device="cuda").bfloat16()
+    wg = (torch.randn(inter, k, device="cuda") * 0.02).bfloat16()
+    wu = (torch.randn(inter, k, device="cuda") * 0.02).bfloat16()
+    out = gemm_silu_mul(a, interleave_gate_up(wg, wu))
+    torch.cuda.synchronize()
+    g = a.float() @ wg.float().T
+    u = a.float() @ wu.float().T
+    ref = torch.nn.functional.silu(g) * u
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 2e-2 * ref.abs().max().item() + 1e-3, err

@@ -1,0 +1,162 @@
+# SPDX-License-Identifier: Apache-2.0
+"""Collective bandwidth sweep: vccl-b200 next to NCCL on the same GPUs.
+
+Launch one process per GPU:
+
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 -m vkccl_b200.bench.collectives \
+        --ops allreduce,allgather,reducescatter,broadcast --dtypes bf16,f32 -b 8 -e 1G
+
+Every number is device time from CUDA events on the launching stream,
+averaged over --iters launches captured in one CUDA graph (so host launch
+overhead is excluded for both libraries), reported as the maximum over
+ranks.  busbw factors follow the reference bench (reference:
+bench/vccl_bench.cc:147-152): 2(n-1)/n all-reduce, (n-1)/n all-gather and
+reduce-scatter, 1 broadcast.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+from vkccl_b200 import comm as vc
+from vkccl_b200.torch_comm import vccl_dtype
+
+DT = {"bf16": torch.bfloat16, "f32": torch.float32, "f16": torch.float16}
+
+
+def parse_size(s: str) -> int:
+    mult = {"K": 1 << 10, "M": 1 << 20, "G": 1 << 30}
+    if s[-1].upper() in mult:
+        return int(float(s[:-1]) * mult[s[-1].upper()])
+    return int(s)
+
+
+def bus_factor(op: str, n: int) -> float:
+    if op == "allreduce":
+        return 2.0 * (n - 1) / n
+    if op in ("allgather", "reducescatter"):
+        return (n - 1) / n
+    return 1.0
+
+
+def make_call(lib: str, op: str, comm, send, recv, n):
+    dt = vccl_dtype(send)
+    if lib == "nccl":
+        if op == "allreduce":
+            return lambda: dist.all_reduce(recv)
+        if op == "allgather":
+            return lambda: dist.all_gather_into_tensor(recv, send)
+        if op == "reducescatter":
+            return lambda: dist.reduce_scatter_tensor(recv, send)
+        return lambda: dist.broadcast(recv, 0)
+    if op == "allreduce":
+        return lambda: comm.all_reduce(send, recv, count=send.numel(), dtype=dt)
+    if op == "allgather":
+        return lambda: comm.all_gather(send, recv, sendcount=send.numel(), dtype=dt)
+    if op == "reducescatter":
+        return lambda: comm.reduce_scatter(send, recv, recvcount=recv.numel(), dtype=dt)
+    return lambda: comm.broadcast(recv, 0, count=recv.numel(), dtype=dt)
+
+
+def time_graph(fn, iters: int, warmup: int) -> float:
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    del g
+    return ms * 1000.0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ops", default="allreduce,allgather,reducescatter,broadcast")
+    ap.add_argument("--dtypes", default="bf16")
+    ap.add_argument("-b", default="8")
+    ap.add_argument("-e", default="256M")
+    ap.add_argument("-f", type=float, default=4.0)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--libs", default="vccl,nccl")
+    ap.add_argument("--out", default="")
+    a = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    uid = vc.get_unique_id() if rank == 0 else None
+    raw = torch.zeros(vc.UNIQUE_ID_BYTES, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        raw.copy_(torch.frombuffer(bytearray(uid.to_bytes()), dtype=torch.uint8))
+    dist.broadcast(raw, 0)
+    comm = vc.Communicator(world, vc.UniqueId.from_bytes(bytes(raw.cpu().numpy())), rank, cuda_device=local)
+    rows = []
+    lo, hi = parse_size(a.b), parse_size(a.e)
+    for op in a.ops.split(","):
+        for dname in a.dtypes.split(","):
+            dt = DT[dname]
+            es = torch.tensor([], dtype=dt).element_size()
+            size = lo
+            while size <= hi:
+                count = max(1, size // es)
+                if op in ("allgather", "reducescatter"):
+                    per = max(1, count // world)
+                    count = per * world
+                if op == "allgather":
+                    send = torch.randn(count // world, device="cuda").to(dt)
+                    recv = torch.empty(count, device="cuda", dtype=dt)
+                elif op == "reducescatter":
+                    send = torch.randn(count, device="cuda").to(dt)
+                    recv = torch.empty(count // world, device="cuda", dtype=dt)
+                else:
+                    send = torch.randn(count, device="cuda").to(dt)
+                    recv = send.clone() if op == "broadcast" else torch.empty_like(send)
+                row = {"op": op, "dtype": dname, "bytes": count * es, "n": world}
+                for libname in a.libs.split(","):
+                    fn = make_call(libname, op, comm, send, recv, world)
+                    us = time_graph(fn, a.iters, a.warmup)
+                    t = torch.tensor([us], device="cuda")
+                    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                    us = t.item()
+                    algbw = count * es / (us * 1e3)
+                    row[libname + "_us"] = round(us, 2)
+                    row[libname + "_busbw"] = round(algbw * bus_factor(op, world), 2)
+                rows.append(row)
+                if rank == 0:
+                    print(json.dumps(row), flush=True)
+                size = int(size * a.f)
+    comm.destroy()
+    if rank == 0 and a.out:
+        with open(a.out, "w") as f:
+            for r in rows:
+                f.write(json.dumps(r) + "\n")
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
