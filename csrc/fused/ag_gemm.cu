@@ -1,0 +1,213 @@
+// SPDX-License-Identifier: Apache-2.0
+// All-gather fused into a column-parallel GEMM.
+//
+// Each rank holds X_shard[M/n, K] (sequence-parallel activations) and needs
+// out = AllGather(X)[M, K] * W^T.  One persistent kernel does both: two
+// extra warps per CTA first stage this rank's shard into its symmetric
+// full-X buffer, then pull every peer's shard over NVLink into the same
+// buffer, bumping a per-shard arrival counter; the TMA producer gates each A
+// tile on the counters of the shards it covers.  Tiles are visited starting
+// at the local shard, so the tensor cores start before any remote byte has
+// arrived and later shards arrive while earlier ones are multiplied.
+//
+// Remote data is read with plain per-thread loads from peer memory into
+// this GPU's memory; the TMA only ever reads local memory (and never uses
+// multicast).
+#include <cuda_runtime.h>
+
+#include "common/log.h"
+#include "fused/gemm_launch.cuh"
+#include "kernels/collectives.cuh"
+#include "runtime/comm.h"
+#include "vccl_tp.h"
+
+namespace vccl {
+namespace fused {
+
+using dev::DevComm;
+
+__device__ __forceinline__ void redAddRelease(uint32_t* p, uint32_t v, bool sys) {
+  if (sys)
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+  else
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fenceProxyAsync() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+__device__ __forceinline__ void copyWarpsBarrier() { asm volatile("bar.sync 2, 64;" ::: "memory"); }
+
+// Copy by the 64 copy-warp threads, 8 x 16 B in flight per thread.
+__device__ __forceinline__ void groupCopy(char* dst, const char* src, size_t bytes, int tid) {
+  constexpr int U = 8;
+  const size_t n16 = bytes / 16;
+  size_t i = tid;
+  for (; i + (U - 1) * 64 < n16; i += U * 64) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) v[u] = dev::ldCG(src + (i + u * 64) * 16);
+#pragma unroll
+    for (int u = 0; u < U; u++) dev::stG(dst + (i + u * 64) * 16, v[u]);
+  }
+  for (; i < n16; i += 64) dev::stG(dst + i * 16, dev::ldCG(src + i * 16));
+}
+
+struct AgHooks : gemm::NoHooks {
+  static constexpr int kExtraWarps = 2;
+  DevComm c;
+  const char* xShard;  // this rank's input rows [shardRows, K]
+  size_t xOff;         // offset of the full-X buffer in the fused region
+  int shardRows;
+  int K;
+  int startTm;         // first tile row of this rank's shard
+  uint32_t ctas;       // fixed grid size
+
+  __device__ __forceinline__ uint32_t* ctrl(int rank, size_t off) const {
+    return dev::ctrlAt<uint32_t>(c, rank, off);
+  }
+  __device__ __forceinline__ void setup(uint32_t* hs) const { hs[0] = ctrl(c.rank, dev::kAgCallsOff)[blockIdx.x]; }
+  __device__ __forceinline__ void teardown(uint32_t* hs) const {
+    ctrl(c.rank, dev::kAgCallsOff)[blockIdx.x] = hs[0] + 1u;
+  }
+  // Row tiles start at this rank's shard and wrap around.
+  __device__ __forceinline__ gemm::TileInfo tileAt(const gemm::GemmShape& s, int t, int BN) const {
+    gemm::TileInfo ti;
+    const int r = t / s.tilesN;
+    ti.tn = t % s.tilesN;
+    ti.tm = (r + startTm) % s.tilesM;
+    ti.row0 = ti.tm * gemm::kBM;
+    ti.col0 = ti.tn * BN;
+    return ti;
+  }
+  __device__ __forceinline__ bool beforeLoad(const gemm::TileInfo& ti, const gemm::GemmShape& s, uint32_t* hs,
+                                             volatile int*) const {
+    const uint32_t target = (hs[0] + 1u) * ctas;
+    const int last = (ti.row0 + gemm::kBM < s.M ? ti.row0 + gemm::kBM : s.M) - 1;
+    for (int q = ti.row0 / shardRows; q <= last / shardRows; q++) {
+      const uint32_t* flag = q == c.rank ? ctrl(c.rank, dev::kAgReadyOff) + q : ctrl(c.rank, dev::kAgLocalReadyOff) + q;
+      if (!dev::waitAtLeast(c, flag, target, dev::kWhereFused, 300 + q)) return false;
+    }
+    fenceProxyAsync();
+    return true;
+  }
+  __device__ __forceinline__ void extraRole(uint32_t* hs, volatile int* abortFlag) const {
+    const int tid = threadIdx.x - gemm::kBaseThreads;  // 0..63
+    const int n = c.nranks, me = c.rank;
+    const uint32_t k = hs[0];
+    const size_t rowBytes = static_cast<size_t>(K) * 2;
+    char* xfull = c.fused[me] + xOff;
+    __shared__ int sFail;
+    // Rows of each shard this CTA moves.
+    const int per = (shardRows + static_cast<int>(ctas) - 1) / static_cast<int>(ctas);
+    const int r0 = blockIdx.x * per < shardRows ? blockIdx.x * per : shardRows;
+    const int r1 = r0 + per < shardRows ? r0 + per : shardRows;
+    // 1. peers must have finished pulling the previous call's shard
+    if (tid == 0) {
+      sFail = 0;
+      for (int p = 0; p < n; p++)
+        if (p != me && !dev::waitAtLeast(c, ctrl(me, dev::kAgTakenOff) + p, k * ctas, dev::kWhereFused, 400 + p))
+          sFail = 1;
+    }
+    copyWarpsBarrier();
+    if (sFail) {
+      *abortFlag = 1;
+      return;
+    }
+    // 2. stage my slice of my shard, announce it to everyone (me included)
+    if (r1 > r0)
+      groupCopy(xfull + (static_cast<size_t>(me) * shardRows + r0) * rowBytes, xShard + r0 * rowBytes,
+                (r1 - r0) * rowBytes, tid);
+    copyWarpsBarrier();
+    if (tid == 0) {
+      fenceProxyAsync();
+      dev::fenceSys();
+      for (int p = 0; p < n; p++) redAddRelease(ctrl(p, dev::kAgReadyOff) + me, 1u, true);
+    }
+    // 3. pull my slice of every peer's shard
+    for (int s = 1; s < n; s++) {
+      const int q = (me + s) % n;
+      if (tid == 0 && !dev::waitAtLeast(c, ctrl(me, dev::kAgReadyOff) + q, (k + 1u) * ctas, dev::kWhereFused, 500 + q))
+        sFail = 1;
+      copyWarpsBarrier();
+      if (sFail || *abortFlag) {
+        *abortFlag = 1;
+        return;
+      }
+      const size_t off = (static_cast<size_t>(q) * shardRows + r0) * rowBytes;
+      if (r1 > r0) groupCopy(xfull + off, c.fused[q] + xOff + off, (r1 - r0) * rowBytes, tid);
+      copyWarpsBarrier();
+      if (tid == 0) {
+        fenceProxyAsync();
+        redAddRelease(ctrl(me, dev::kAgLocalReadyOff) + q, 1u, false);
+        dev::fenceSys();
+        redAddRelease(ctrl(q, dev::kAgTakenOff) + me, 1u, true);
+      }
+    }
+  }
+};
+
+}  // namespace fused
+}  // namespace vccl
+
+using namespace vccl;
+
+extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, void* out, int M, int N, int K,
+                                          int siluMul, vcclComm_t comm, vcclStream_t stream) {
+  if (comm == nullptr || xShard == nullptr || W == nullptr || out == nullptr || M <= 0 || N <= 0 || K <= 0)
+    return vcclInvalidArgument;
+  if ((N % 32) != 0 || (K % 8) != 0 ||
+      ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(xShard)) & 15u) != 0)
+    return vcclInvalidArgument;
+  if (comm->aborted.load() || !comm->dev) return vcclInvalidUsage;
+  const int n = comm->nranks;
+  if (M % n != 0) {
+    VERR("vcclAllGatherGemm: M (%d) must be divisible by the number of ranks (%d)", M, n);
+    return vcclInvalidArgument;
+  }
+  vcclResult_t st = comm->pollDeviceStatus();
+  if (st != vcclSuccess) {
+    comm->noteError(st);
+    return vcclInvalidUsage;
+  }
+  cudaSetDevice(comm->dev->device);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int bnEnv = static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN"));
+  cudaError_t e;
+  if (n == 1) {
+    if (siluMul) {
+      gemm::EpiSiluMul epi{static_cast<__nv_bfloat16*>(out), N / 2};
+      e = gemm::launchGemm(xShard, W, M, N, K, epi, gemm::NoHooks{}, s, bnEnv, 0);
+    } else {
+      gemm::EpiStore epi{static_cast<__nv_bfloat16*>(out), N};
+      e = gemm::launchGemm(xShard, W, M, N, K, epi, gemm::NoHooks{}, s, bnEnv, 0);
+    }
+    return e == cudaSuccess ? vcclSuccess : vcclInvalidArgument;
+  }
+  const dev::DevComm& dc = comm->dev->dc;
+  const size_t xOff = dc.fusedBytes / 2;
+  if (static_cast<size_t>(M) * K * 2 > dc.fusedBytes - xOff) {
+    VERR("vcclAllGatherGemm: gathered input (%zu bytes) exceeds VCCL_FUSED_BUFFSIZE/2",
+         static_cast<size_t>(M) * K * 2);
+    return vcclInvalidArgument;
+  }
+  const int ctas = gemm::smCount();
+  fused::AgHooks hooks;
+  hooks.c = dc;
+  hooks.xShard = static_cast<const char*>(xShard);
+  hooks.xOff = xOff;
+  hooks.shardRows = M / n;
+  hooks.K = K;
+  hooks.startTm = (comm->rank * (M / n)) / gemm::kBM;
+  hooks.ctas = static_cast<uint32_t>(ctas);
+  const char* xfull = dc.fused[comm->rank] + xOff;
+  if (siluMul) {
+    gemm::EpiSiluMul epi{static_cast<__nv_bfloat16*>(out), N / 2};
+    e = gemm::launchGemm(xfull, W, M, N, K, epi, hooks, s, bnEnv, -ctas);
+  } else {
+    gemm::EpiStore epi{static_cast<__nv_bfloat16*>(out), N};
+    e = gemm::launchGemm(xfull, W, M, N, K, epi, hooks, s, bnEnv, -ctas);
+  }
+  if (e != cudaSuccess) {
+    VERR("vcclAllGatherGemm launch: %s", cudaGetErrorString(e));
+    return vcclInvalidArgument;
+  }
+  return vcclSuccess;
+}

@@ -1,14 +1,13 @@
 // SPDX-License-Identifier: Apache-2.0
 // Host side of the tcgen05 GEMM: tensor-map construction, tile-width
-// selection and launch.
+// selection and the plain / SiLU*mul entry points.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
 
 #include "common/log.h"
-#include "fused/gemm_host.h"
-#include "kernels/gemm_sm100.cuh"
+#include "fused/gemm_launch.cuh"
 #include "runtime/cudrv.h"
 #include "vccl_tp.h"
 
@@ -57,52 +56,12 @@ int pickBN(int M, int N) {
 int* errorFlag() {
   static int* p = nullptr;
   static std::once_flag once;
-  std::call_once(once, [] { cudaMalloc(&p, sizeof(int) * 64); cudaMemset(p, 0, sizeof(int) * 64); });
+  std::call_once(once, [] {
+    cudaMalloc(&p, sizeof(int) * 64);
+    cudaMemset(p, 0, sizeof(int) * 64);
+  });
   return p;
 }
-
-template <int BN, int STAGES, typename Epi, typename Hooks>
-cudaError_t launchT(const CUtensorMap& ma, const CUtensorMap& mb, const GemmShape& s, const Epi& epi,
-                    const Hooks& hooks, int grid, cudaStream_t st) {
-  using L = Smem<BN, STAGES>;
-  auto kern = gemmKernel<BN, STAGES, Epi, Hooks>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
-  kern<<<grid, kThreads, L::kBytes, st>>>(ma, mb, s, epi, hooks, errorFlag());
-  return cudaGetLastError();
-}
-
-template <typename Epi, typename Hooks>
-cudaError_t launchGemm(const void* A, const void* B, int M, int N, int K, const Epi& epi, const Hooks& hooks,
-                       cudaStream_t st, int bnOverride, int gridCap) {
-  const int bn = bnOverride > 0 ? bnOverride : pickBN(M, N);
-  CUtensorMap ma, mb;
-  if (!makeMapKMajor(&ma, A, M, K, kBM) || !makeMapKMajor(&mb, B, N, K, bn)) return cudaErrorInvalidValue;
-  GemmShape s;
-  s.M = M;
-  s.N = N;
-  s.K = K;
-  s.tilesM = (M + kBM - 1) / kBM;
-  s.tilesN = (N + bn - 1) / bn;
-  int grid = s.tilesM * s.tilesN;
-  int cap = gridCap > 0 ? gridCap : smCount();
-  if (grid > cap) grid = cap;
-  switch (bn) {
-    case 256: return launchT<256, 4>(ma, mb, s, epi, hooks, grid, st);
-    case 128: return launchT<128, 6>(ma, mb, s, epi, hooks, grid, st);
-    case 64: return launchT<64, 8>(ma, mb, s, epi, hooks, grid, st);
-    default: return launchT<32, 8>(ma, mb, s, epi, hooks, grid, st);
-  }
-}
-
-template cudaError_t launchGemm<EpiStore, NoHooks>(const void*, const void*, int, int, int, const EpiStore&,
-                                                   const NoHooks&, cudaStream_t, int, int);
-template cudaError_t launchGemm<EpiSiluMul, NoHooks>(const void*, const void*, int, int, int, const EpiSiluMul&,
-                                                     const NoHooks&, cudaStream_t, int, int);
 
 }  // namespace gemm
 }  // namespace vccl

@@ -16,10 +16,6 @@ int smCount();
 int pickBN(int M, int N);
 int* errorFlag();
 
-template <typename Epi, typename Hooks>
-cudaError_t launchGemm(const void* A, const void* B, int M, int N, int K, const Epi& epi, const Hooks& hooks,
-                       cudaStream_t st, int bnOverride, int gridCap);
-
 inline long envLongGemm(const char* name) {
   const char* v = std::getenv(name);
   return v ? std::strtol(v, nullptr, 10) : 0;

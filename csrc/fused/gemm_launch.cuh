@@ -1,0 +1,62 @@
+// SPDX-License-Identifier: Apache-2.0
+// Launch template shared by every GEMM-based kernel (plain, SiLU*mul,
+// GEMM + reduce-scatter, all-gather + GEMM).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "fused/gemm_host.h"
+#include "kernels/gemm_sm100.cuh"
+
+namespace vccl {
+namespace gemm {
+
+template <int BN, int STAGES, typename Epi, typename Hooks>
+cudaError_t launchT(const CUtensorMap& ma, const CUtensorMap& mb, const GemmShape& s, const Epi& epi,
+                    const Hooks& hooks, int grid, cudaStream_t st) {
+  using L = Smem<BN, STAGES>;
+  auto kern = gemmKernel<BN, STAGES, Epi, Hooks>;
+  static unsigned long long attrDone = 0;  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attrDone & (1ull << (dev & 63)))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    if (e != cudaSuccess) return e;
+    attrDone |= 1ull << (dev & 63);
+  }
+  kern<<<grid, kBaseThreads + 32 * Hooks::kExtraWarps, L::kBytes, st>>>(ma, mb, s, epi, hooks, errorFlag());
+  return cudaGetLastError();
+}
+
+// gridCap > 0: at most that many CTAs; gridCap < 0: exactly -gridCap CTAs
+// (fused kernels count on a fixed grid); 0: one CTA per SM at most.
+template <typename Epi, typename Hooks>
+cudaError_t launchGemm(const void* A, const void* B, int M, int N, int K, const Epi& epi, const Hooks& hooks,
+                       cudaStream_t st, int bnOverride, int gridCap) {
+  const int bn = bnOverride > 0 ? bnOverride : pickBN(M, N);
+  CUtensorMap ma, mb;
+  if (!makeMapKMajor(&ma, A, M, K, kBM) || !makeMapKMajor(&mb, B, N, K, bn)) return cudaErrorInvalidValue;
+  GemmShape s;
+  s.M = M;
+  s.N = N;
+  s.K = K;
+  s.tilesM = (M + kBM - 1) / kBM;
+  s.tilesN = (N + bn - 1) / bn;
+  int grid = s.tilesM * s.tilesN;
+  if (gridCap < 0) {
+    grid = -gridCap;
+  } else {
+    const int cap = gridCap > 0 ? gridCap : smCount();
+    if (grid > cap) grid = cap;
+  }
+  switch (bn) {
+    case 256: return launchT<256, 4>(ma, mb, s, epi, hooks, grid, st);
+    case 128: return launchT<128, 6>(ma, mb, s, epi, hooks, grid, st);
+    case 64: return launchT<64, 8>(ma, mb, s, epi, hooks, grid, st);
+    default: return launchT<32, 8>(ma, mb, s, epi, hooks, grid, st);
+  }
+}
+
+}  // namespace gemm
+}  // namespace vccl

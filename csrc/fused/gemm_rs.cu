@@ -1,0 +1,190 @@
+// SPDX-License-Identifier: Apache-2.0
+// Row-parallel GEMM fused with reduce-scatter over NVLink.
+//
+// Every rank computes its partial product P = A * W^T.  Row r of P belongs
+// to rank r / (M / n).  Instead of writing P to memory and running a
+// reduce-scatter afterwards, the GEMM epilogue stores each finished tile
+// directly into the owner's staging slot for this source rank (a plain
+// store over NVLink for remote owners), so the transfer of early tiles
+// overlaps the tensor-core work on later ones.  A short local kernel then
+// sums the n slots of the rows this rank owns.
+//
+// Synchronisation is device-side and CUDA-graph safe: every GEMM CTA (the
+// grid is always one CTA per SM) bumps a "done" counter on every rank after
+// its stores; the reduction waits for n x CTAs of this call; after reducing,
+// every reduction block bumps a "free" counter on every rank, which the next
+// call's GEMM waits for before storing into that rank's slots.
+#include <cuda_runtime.h>
+
+#include "common/log.h"
+#include "fused/gemm_launch.cuh"
+#include "kernels/collectives.cuh"
+#include "runtime/comm.h"
+#include "vccl_tp.h"
+
+namespace vccl {
+namespace fused {
+
+using dev::DevComm;
+
+__device__ __forceinline__ void redAddReleaseSys(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void epilogueBarrier() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Store a 16-column chunk of one accumulator row as bf16 to `dst`.
+__device__ __forceinline__ void storeRow16(char* dst, const uint32_t (&r)[16]) {
+  uint4 o0, o1;
+  o0.x = gemm::packBf16(__uint_as_float(r[0]), __uint_as_float(r[1]));
+  o0.y = gemm::packBf16(__uint_as_float(r[2]), __uint_as_float(r[3]));
+  o0.z = gemm::packBf16(__uint_as_float(r[4]), __uint_as_float(r[5]));
+  o0.w = gemm::packBf16(__uint_as_float(r[6]), __uint_as_float(r[7]));
+  o1.x = gemm::packBf16(__uint_as_float(r[8]), __uint_as_float(r[9]));
+  o1.y = gemm::packBf16(__uint_as_float(r[10]), __uint_as_float(r[11]));
+  o1.z = gemm::packBf16(__uint_as_float(r[12]), __uint_as_float(r[13]));
+  o1.w = gemm::packBf16(__uint_as_float(r[14]), __uint_as_float(r[15]));
+  reinterpret_cast<uint4*>(dst)[0] = o0;
+  reinterpret_cast<uint4*>(dst)[1] = o1;
+}
+
+struct EpiPushRS {
+  char* dest[dev::kMaxRanks];  // owner q's slot for this source rank
+  int rowsPerRank;
+  int ldn;  // N
+  template <int BN>
+  __device__ __forceinline__ void operator()(uint32_t tmemAcc, const gemm::TileInfo& ti, const gemm::GemmShape& s,
+                                             int laneRow) const {
+    const int row = ti.row0 + laneRow;
+    const int owner = row < s.M ? row / rowsPerRank : 0;
+    char* base = dest[owner] + static_cast<size_t>(row - owner * rowsPerRank) * ldn * 2;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      uint32_t r[16];
+      sm100::tmemLoad16(tmemAcc + c, r);
+      sm100::tmemLoadWait();
+      const int col = ti.col0 + c;
+      if (row < s.M && col < s.N) storeRow16(base + static_cast<size_t>(col) * 2, r);
+    }
+  }
+};
+
+struct RsHooks : gemm::NoHooks {
+  DevComm c;
+  uint32_t reduceBlocks;
+  __device__ __forceinline__ bool beforeTiles(uint32_t*, volatile int* abortFlag) const {
+    __shared__ int sFail;
+    if (threadIdx.x == 64) {
+      sFail = 0;
+      const uint32_t k = dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsGemmCallsOff)[blockIdx.x];
+      const uint32_t* freeCnt = dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsFreeOff);
+      for (int q = 0; q < c.nranks; q++)
+        if (!dev::waitAtLeast(c, freeCnt + q, k * reduceBlocks, dev::kWhereFused, 100 + q)) sFail = 1;
+    }
+    epilogueBarrier();
+    return sFail == 0 && !*abortFlag;
+  }
+  __device__ __forceinline__ void afterTiles(uint32_t*, volatile int*) const {
+    epilogueBarrier();
+    if (threadIdx.x == 64) {
+      dev::fenceSys();
+      for (int q = 0; q < c.nranks; q++) redAddReleaseSys(dev::ctrlAt<uint32_t>(c, q, dev::kRsDoneOff) + c.rank, 1u);
+      dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsGemmCallsOff)[blockIdx.x] += 1u;
+    }
+  }
+};
+
+// out[rowsPerRank, N] = sum over sources of my slots.
+__global__ void __launch_bounds__(512) rsReduce(DevComm c, char* out, size_t elems, size_t slotBytes,
+                                                uint32_t gemmCtas) {
+  __shared__ uint32_t sK;
+  __shared__ int sFail;
+  const int n = c.nranks, me = c.rank;
+  if (threadIdx.x == 0) {
+    sK = dev::ctrlAt<uint32_t>(c, me, dev::kRsReduceCallsOff)[blockIdx.x];
+    sFail = 0;
+  }
+  __syncthreads();
+  const uint32_t k = sK;
+  if (threadIdx.x < n) {
+    const uint32_t* done = dev::ctrlAt<uint32_t>(c, me, dev::kRsDoneOff);
+    if (!dev::waitAtLeast(c, done + threadIdx.x, (k + 1u) * gemmCtas, dev::kWhereFused, 200 + threadIdx.x))
+      sFail = 1;
+  }
+  __syncthreads();
+  if (sFail) return;
+  size_t lo, hi;
+  dev::blockRange(elems, gridDim.x, blockIdx.x, 8, &lo, &hi);
+  if (lo < hi) {
+    const char* slots = c.fused[me];
+    dev::reduceInto<__nv_bfloat16, dev::kSum, true>(
+        n, me, out + lo * 2, nullptr, slots + me * slotBytes + lo * 2,
+        [&](int p) { return slots + p * slotBytes + lo * 2; }, hi - lo, false, 1.0, false);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    dev::fenceSys();
+    for (int q = 0; q < n; q++) redAddReleaseSys(dev::ctrlAt<uint32_t>(c, q, dev::kRsFreeOff) + me, 1u);
+    dev::ctrlAt<uint32_t>(c, me, dev::kRsReduceCallsOff)[blockIdx.x] = k + 1u;
+  }
+}
+
+}  // namespace fused
+}  // namespace vccl
+
+using namespace vccl;
+
+extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void* out, int M, int N, int K,
+                                              vcclComm_t comm, vcclStream_t stream) {
+  if (comm == nullptr || A == nullptr || W == nullptr || out == nullptr || M <= 0 || N <= 0 || K <= 0)
+    return vcclInvalidArgument;
+  if ((N % 16) != 0 || (K % 8) != 0 || (reinterpret_cast<uintptr_t>(out) & 15u) != 0) return vcclInvalidArgument;
+  if (comm->aborted.load() || !comm->dev) return vcclInvalidUsage;
+  const int n = comm->nranks;
+  if (M % n != 0) {
+    VERR("vcclGemmReduceScatter: M (%d) must be divisible by the number of ranks (%d)", M, n);
+    return vcclInvalidArgument;
+  }
+  vcclResult_t st = comm->pollDeviceStatus();
+  if (st != vcclSuccess) {
+    comm->noteError(st);
+    return vcclInvalidUsage;
+  }
+  cudaSetDevice(comm->dev->device);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int bnEnv = static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN"));
+  if (n == 1) {
+    gemm::EpiStore epi{static_cast<__nv_bfloat16*>(out), N};
+    cudaError_t e = gemm::launchGemm(A, W, M, N, K, epi, gemm::NoHooks{}, s, bnEnv, 0);
+    return e == cudaSuccess ? vcclSuccess : vcclInvalidArgument;
+  }
+  const int rowsPerRank = M / n;
+  const size_t slotBytes = (static_cast<size_t>(rowsPerRank) * N * 2 + 255) / 256 * 256;
+  const dev::DevComm& dc = comm->dev->dc;
+  if (slotBytes * n > dc.fusedBytes / 2) {
+    VERR("vcclGemmReduceScatter: %zu staging bytes exceed VCCL_FUSED_BUFFSIZE/2", slotBytes * n);
+    return vcclInvalidArgument;
+  }
+  const int ctas = gemm::smCount();
+  if (ctas > dev::kMaxFusedCtas) return vcclInternalError;
+  fused::EpiPushRS epi;
+  for (int q = 0; q < dev::kMaxRanks; q++) epi.dest[q] = q < n ? dc.fused[q] + comm->rank * slotBytes : nullptr;
+  epi.rowsPerRank = rowsPerRank;
+  epi.ldn = N;
+  fused::RsHooks hooks;
+  hooks.c = dc;
+  hooks.reduceBlocks = static_cast<uint32_t>(dev::kFusedReduceBlocks);
+  cudaError_t e = gemm::launchGemm(A, W, M, N, K, epi, hooks, s, bnEnv, -ctas);
+  if (e != cudaSuccess) {
+    VERR("vcclGemmReduceScatter GEMM launch: %s", cudaGetErrorString(e));
+    return vcclInvalidArgument;
+  }
+  fused::rsReduce<<<dev::kFusedReduceBlocks, 512, 0, s>>>(dc, static_cast<char*>(out),
+                                                          static_cast<size_t>(rowsPerRank) * N, slotBytes,
+                                                          static_cast<uint32_t>(ctas));
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    VERR("vcclGemmReduceScatter reduce launch: %s", cudaGetErrorString(e));
+    return vcclUnhandledError;
+  }
+  return vcclSuccess;
+}

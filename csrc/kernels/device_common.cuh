@@ -35,6 +35,18 @@ constexpr size_t kP2pRecvdOff = kP2pSentOff + kMaxRanks * kMaxChannels * 8; // l
 constexpr size_t kFusedEpochOff = 16384;                              // u32[kMaxBlocks], local (fused kernels)
 constexpr size_t kFusedFlagsOff = 20480;                              // u32[kMaxBlocks][kMaxRanks], written by peers
 constexpr size_t kMoeCountsOff = 32768;                               // u32[2][kMaxRanks][64], written by peers
+// Fused GEMM + reduce-scatter / all-gather + GEMM counters (monotonic).
+constexpr int kMaxFusedCtas = 256;
+constexpr int kFusedReduceBlocks = 64;
+constexpr size_t kRsDoneOff = 65536;                        // u32[kMaxRanks]: peers' GEMM CTAs finished pushing
+constexpr size_t kRsFreeOff = kRsDoneOff + 64;              // u32[kMaxRanks]: peers finished reducing my pushes
+constexpr size_t kRsGemmCallsOff = kRsDoneOff + 256;        // u32[kMaxFusedCtas], local
+constexpr size_t kRsReduceCallsOff = kRsGemmCallsOff + 1024; // u32[kFusedReduceBlocks], local
+constexpr size_t kAgReadyOff = 69632;                       // u32[kMaxRanks]: peer staged its shard
+constexpr size_t kAgTakenOff = kAgReadyOff + 64;            // u32[kMaxRanks]: peer finished pulling my shard
+constexpr size_t kAgCallsOff = kAgReadyOff + 256;           // u32[kMaxFusedCtas], local
+constexpr size_t kAgLocalReadyOff = kAgCallsOff + 1024;     // u32[kMaxRanks], local: shard copied into full X
+constexpr size_t kMoeOff = 73728;                           // MoE dispatch/combine counters
 constexpr size_t kCtrlHeader = 1 << 20;
 
 constexpr size_t kLLMaxBytes = 256 << 10;               // largest LL payload per rank
@@ -57,6 +69,8 @@ struct DevComm {
   char* data[kMaxRanks];  // every rank's data allocation, mapped here
   char* mcData;           // multicast address of the data allocations, or null
   size_t dataBytes;
+  char* fused[kMaxRanks]; // every rank's fused-op region (GEMM+RS, AG+GEMM, MoE)
+  size_t fusedBytes;
   uint32_t* status;              // host-mapped, written by kernels
   const uint32_t* abortWord;     // host-mapped, written by vcclCommAbort
   uint64_t timeoutNs;
@@ -113,15 +127,25 @@ __device__ __forceinline__ bool shouldGiveUp(const DevComm& c, uint64_t start, u
   return false;
 }
 
-// Spin until *flag - target >= 0 (wrapping compare).  False on timeout/abort.
+__device__ __forceinline__ uint32_t ldRelaxedSys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Spin until *flag - target >= 0 (wrapping compare), then acquire.  Polls
+// with relaxed loads and fences once.  False on timeout/abort.
 __device__ __forceinline__ bool waitAtLeast(const DevComm& c, const uint32_t* flag, uint32_t target,
                                             uint32_t where, uint32_t detail) {
-  if (static_cast<int32_t>(ldAcquireSys(flag) - target) >= 0) return true;
-  const uint64_t start = globalTimerNs();
-  for (uint32_t spin = 1;; ++spin) {
-    if (static_cast<int32_t>(ldAcquireSys(flag) - target) >= 0) return true;
-    if ((spin & 255u) == 0u && shouldGiveUp(c, start, where, detail)) return false;
+  if (static_cast<int32_t>(ldRelaxedSys(flag) - target) < 0) {
+    const uint64_t start = globalTimerNs();
+    for (uint32_t spin = 1;; ++spin) {
+      if (static_cast<int32_t>(ldRelaxedSys(flag) - target) >= 0) break;
+      if ((spin & 255u) == 0u && shouldGiveUp(c, start, where, detail)) return false;
+    }
   }
+  fenceSys();
+  return true;
 }
 __device__ __forceinline__ bool waitAtLeast64(const DevComm& c, const uint64_t* flag,
                                               uint64_t target, uint32_t where, uint32_t detail) {

@@ -13,8 +13,11 @@
 //              lanes 32*(w%4)..+31 = tile rows), apply the Epilogue policy,
 //              hand the accumulator back.  Two accumulators alternate so
 //              the epilogue of tile i overlaps the MMAs of tile i+1.
-// Epilogue policies are how the fused kernels (SiLU*mul, reduce-scatter
-// pushes to peer GPUs) reuse this mainloop.
+//   warps 6+   optional extra warps run Policy::extraRole (used by the
+//              all-gather + GEMM kernel to pull remote shards).
+// The Policy decides the tile order, may gate a tile's loads on data
+// arrival, and runs code before/after the epilogue's tiles; this is how the
+// fused kernels reuse the mainloop.
 #pragma once
 
 #include <cuda.h>
@@ -28,7 +31,7 @@ namespace gemm {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // one 128-byte swizzle atom of bf16
-constexpr int kThreads = 192;
+constexpr int kBaseThreads = 192;
 
 template <int BN, int STAGES>
 struct Smem {
@@ -48,16 +51,6 @@ struct GemmShape {
   int M, N, K;
   int tilesM, tilesN;
 };
-
-// Tile order: consecutive CTAs share the B (weight) tile.
-__device__ __forceinline__ TileInfo tileAt(const GemmShape& s, int t, int BN) {
-  TileInfo ti;
-  ti.tn = t / s.tilesM;
-  ti.tm = t % s.tilesM;
-  ti.row0 = ti.tm * kBM;
-  ti.col0 = ti.tn * BN;
-  return ti;
-}
 
 __device__ __forceinline__ uint32_t packBf16(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
@@ -138,17 +131,30 @@ struct EpiSiluMul {
   }
 };
 
-// Hooks a fused kernel may provide around the tile loop (no-ops here).
+// Default policy: tiles in N-major order (consecutive CTAs share the B
+// tile), no gating, no extra warps.  `hs` is per-CTA shared scratch.
 struct NoHooks {
-  // Called by every epilogue thread before the first tile.  Return false to
-  // abandon the kernel.
-  __device__ __forceinline__ bool beforeTiles(volatile int*) const { return true; }
-  // Called by every epilogue thread after its last tile (all its stores done).
-  __device__ __forceinline__ void afterTiles(volatile int*) const {}
+  static constexpr int kExtraWarps = 0;
+  __device__ __forceinline__ void setup(uint32_t*) const {}
+  __device__ __forceinline__ void teardown(uint32_t*) const {}
+  __device__ __forceinline__ TileInfo tileAt(const GemmShape& s, int t, int BN) const {
+    TileInfo ti;
+    ti.tn = t / s.tilesM;
+    ti.tm = t % s.tilesM;
+    ti.row0 = ti.tm * kBM;
+    ti.col0 = ti.tn * BN;
+    return ti;
+  }
+  __device__ __forceinline__ bool beforeLoad(const TileInfo&, const GemmShape&, uint32_t*, volatile int*) const {
+    return true;
+  }
+  __device__ __forceinline__ bool beforeTiles(uint32_t*, volatile int*) const { return true; }
+  __device__ __forceinline__ void afterTiles(uint32_t*, volatile int*) const {}
+  __device__ __forceinline__ void extraRole(uint32_t*, volatile int*) const {}
 };
 
 template <int BN, int STAGES, typename Epi, typename Hooks = NoHooks>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBaseThreads + 32 * Hooks::kExtraWarps, 1)
     gemmKernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, GemmShape s,
                Epi epi, Hooks hooks, int* errorFlag) {
   using L = Smem<BN, STAGES>;
@@ -161,6 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drainBar = accEmpty + 2;
   uint32_t* tmemSlot = reinterpret_cast<uint32_t*>(drainBar + 1);
   volatile int* abortFlag = reinterpret_cast<volatile int*>(tmemSlot + 1);
+  uint32_t* hs = tmemSlot + 2;  // 8 words of policy scratch
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -177,6 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     sm100::mbarInit(drainBar, 1);
     *abortFlag = 0;
+    hooks.setup(hs);
     sm100::fenceBarrierInit();
   }
   if (warp == 1) {
@@ -200,7 +208,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t issued = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < numTiles && ok; t += gridDim.x) {
-        const TileInfo ti = tileAt(s, t, BN);
+        const TileInfo ti = hooks.tileAt(s, t, BN);
+        if (!hooks.beforeLoad(ti, s, hs, abortFlag)) {
+          *abortFlag = 1;
+          ok = false;
+          break;
+        }
         for (int kb = 0; kb < numK; kb++) {
           if (!sm100::mbarWait(&emptyBar[stage], phase ^ 1u, abortFlag)) {
             ok = false;
@@ -286,13 +299,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::mbarWait(drainBar, 0, &never, 200000000ull);
       }
     }
-  } else {
+  } else if (warp < 6) {
     // ---------------- epilogue (warps 2..5) ----------------
     const int quarter = warp & 3;             // TMEM lane quarter this warp may access
     const int laneRow = quarter * 32 + lane;  // tile row of this thread
     int acc = 0;
     uint32_t accPhase = 0;
-    bool ok = hooks.beforeTiles(abortFlag);
+    bool ok = hooks.beforeTiles(hs, abortFlag);
     if (!ok) *abortFlag = 1;
     for (int t = blockIdx.x; t < numTiles && ok; t += gridDim.x) {
       if (!sm100::mbarWait(&accFull[acc], accPhase, abortFlag)) {
@@ -300,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       sm100::tcFenceAfter();
-      const TileInfo ti = tileAt(s, t, BN);
+      const TileInfo ti = hooks.tileAt(s, t, BN);
       const uint32_t tmemAcc = tmemBase + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
       epi.template operator()<BN>(tmemAcc, ti, s, laneRow);
       sm100::tcFenceBefore();
@@ -311,11 +324,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         accPhase ^= 1u;
       }
     }
-    if (ok) hooks.afterTiles(abortFlag);
+    if (ok) hooks.afterTiles(hs, abortFlag);
+  } else {
+    // ---------------- extra warps (policy) ----------------
+    hooks.extraRole(hs, abortFlag);
   }
 
   __syncthreads();
-  if (*abortFlag && threadIdx.x == 0 && errorFlag) atomicExch(errorFlag, 1);
+  if (threadIdx.x == 0) {
+    if (*abortFlag) {
+      if (errorFlag) atomicExch(errorFlag, 1);
+    } else {
+      hooks.teardown(hs);
+    }
+  }
   if (warp == 1) {
     sm100::tcFenceAfter();
     sm100::tmemDealloc(tmemBase, kTmemCols);

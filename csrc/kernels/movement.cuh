@@ -42,6 +42,55 @@ __global__ void __launch_bounds__(512) allGatherPull(DevComm c, const char* send
   }
 }
 
+// LL all-gather: every rank stores its block as LL lines into every peer's
+// slot; one NVLink hop, no barrier.  bytes % 8 == 0, 8-byte aligned buffers,
+// bytes <= kLLMaxBytes.
+__global__ void __launch_bounds__(512) allGatherLL(DevComm c, const char* send, char* recv, size_t bytes) {
+  const uint32_t e = llEpoch(c);
+  const uint32_t par = e & 1u;
+  const int n = c.nranks, me = c.rank;
+  const size_t words = bytes / 8;
+  size_t w0, w1;
+  blockRange(words, gridDim.x, blockIdx.x, 1, &w0, &w1);
+  char* own = recv + me * bytes;
+  for (size_t w = w0 + threadIdx.x; w < w1; w += blockDim.x) {
+    const uint64_t word = *reinterpret_cast<const uint64_t*>(send + w * 8);
+    for (int k = 1; k < n; k++) llPut(c, (me + k) % n, par, e, w, word);
+    if (own != send) *reinterpret_cast<uint64_t*>(own + w * 8) = word;
+  }
+  for (size_t w = w0 + threadIdx.x; w < w1; w += blockDim.x) {
+    for (int k = 1; k < n; k++) {
+      const int p = (me + k) % n;
+      uint64_t v;
+      if (!llWait(c, llSlot(c, me, par, p) + w * 16, e, &v)) return;
+      *reinterpret_cast<uint64_t*>(recv + p * bytes + w * 8) = v;
+    }
+  }
+}
+
+// LL broadcast: the root stores LL lines into every peer's slot.
+__global__ void __launch_bounds__(512) broadcastLL(DevComm c, const char* send, char* recv, size_t bytes, int root) {
+  const uint32_t e = llEpoch(c);
+  const uint32_t par = e & 1u;
+  const int n = c.nranks, me = c.rank;
+  const size_t words = bytes / 8;
+  size_t w0, w1;
+  blockRange(words, gridDim.x, blockIdx.x, 1, &w0, &w1);
+  if (me == root) {
+    for (size_t w = w0 + threadIdx.x; w < w1; w += blockDim.x) {
+      const uint64_t word = *reinterpret_cast<const uint64_t*>(send + w * 8);
+      for (int k = 1; k < n; k++) llPut(c, (me + k) % n, par, e, w, word);
+      if (recv != send) *reinterpret_cast<uint64_t*>(recv + w * 8) = word;
+    }
+    return;
+  }
+  for (size_t w = w0 + threadIdx.x; w < w1; w += blockDim.x) {
+    uint64_t v;
+    if (!llWait(c, llSlot(c, me, par, root) + w * 16, e, &v)) return;
+    *reinterpret_cast<uint64_t*>(recv + w * 8) = v;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Broadcast.  Pull: root stages, everyone pulls.  NVLS: root stores once
 // through the multicast address, every rank copies out locally.

@@ -224,6 +224,7 @@ LaunchCtx launchCtx(vcclComm_t comm, cudaStream_t s) {
   lc.stream = s;
   lc.nblocks = comm->dev->nblocks;
   lc.nvls = comm->dev->nvls;
+  lc.llMax = comm->dev->llMaxBytes;
   return lc;
 }
 
@@ -247,7 +248,11 @@ ArAlgo pickAllReduce(const HostOp& h, size_t bytes) {
     return ArAlgo::TwoShot;
   }
   if (llOk && bytes <= ds.llMaxBytes) return ArAlgo::LL;
-  if (nvlsOk && bytes >= envBytes("VCCL_NVLS_MIN", 512u << 10)) return ArAlgo::Nvls;
+  // Per GPU, NVLS moves (1 + 1/n) S each way against 2 (n-1)/n S for the
+  // two-shot: it only wins from four ranks on.
+  if (nvlsOk && h.comm->nranks >= envLong("VCCL_NVLS_MIN_RANKS", 4) &&
+      bytes >= envBytes("VCCL_NVLS_MIN", 512u << 10))
+    return ArAlgo::Nvls;
   return ArAlgo::TwoShot;
 }
 
@@ -377,7 +382,8 @@ vcclResult_t launchColl(const HostOp& h) {
     case Kind::Broadcast: {
       const size_t bytes = h.count * es;
       std::string force = envStr("VCCL_BROADCAST_ALGO", "");
-      bool nv = lc.nvls && (force == "nvls" || (force.empty() && bytes >= (256u << 10)));
+      // The root sends S through the switch instead of (n-1) S to the peers.
+      bool nv = lc.nvls && (force == "nvls" || (force.empty() && n >= 3 && bytes >= (256u << 10)));
       return cudaToVccl(launchBroadcast(lc, h.send, h.recv, bytes, h.root, nv), "broadcast launch");
     }
     default: return vcclInternalError;

@@ -45,6 +45,7 @@ struct DeviceState {
   cudaStream_t stream = nullptr;   // internal stream (blocking helpers)
   SymmetricBuffer ctrl;
   SymmetricBuffer data;
+  SymmetricBuffer fused;           // staging owned by the fused TP kernels
   bool nvls = false;
   uint32_t* hostStatus = nullptr;  // pinned + mapped
   uint32_t* devStatus = nullptr;

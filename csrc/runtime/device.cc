@@ -265,18 +265,20 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
     }
     dataBytes = roundUp(dataBytes, dataAlign);
     const size_t ctrlBytes = roundUp(dev::kCtrlBytes, gran);
-    struct Sizes { uint64_t ctrl, data; } mine{ctrlBytes, dataBytes};
+    const size_t fusedBytes = roundUp(envBytes("VCCL_FUSED_BUFFSIZE", 512u << 20), gran);
+    struct Sizes { uint64_t ctrl, data, fused; } mine{ctrlBytes, dataBytes, fusedBytes};
     std::vector<Sizes> all(n);
     all[me] = mine;
     VTRY(bs->allGather(all.data(), sizeof(Sizes)));
     for (const Sizes& s : all) {
-      if (s.ctrl != mine.ctrl || s.data != mine.data) {
+      if (s.ctrl != mine.ctrl || s.data != mine.data || s.fused != mine.fused) {
         VERR("ranks disagree on workspace sizes (check VCCL_BUFFSIZE on every rank)");
         return vcclInvalidUsage;
       }
     }
     VTRY(symmetricAlloc(bs, ds.get(), ctrlBytes, gran, &ds->ctrl));
     VTRY(symmetricAlloc(bs, ds.get(), dataBytes, dataAlign, &ds->data));
+    VTRY(symmetricAlloc(bs, ds.get(), fusedBytes, gran, &ds->fused));
     CUDART_TRY(cudaMemset(reinterpret_cast<void*>(ds->ctrl.va[me]), 0, dev::kCtrlHeader));
     CUDART_TRY(cudaMemset(reinterpret_cast<void*>(ds->ctrl.va[me] + dev::kLLOff), 0xff, dev::kLLBytes));
     CUDART_TRY(cudaDeviceSynchronize());
@@ -293,7 +295,9 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
   for (int p = 0; p < n && n > 1; p++) {
     dc.ctrl[p] = reinterpret_cast<char*>(ds->ctrl.va[p]);
     dc.data[p] = reinterpret_cast<char*>(ds->data.va[p]);
+    dc.fused[p] = reinterpret_cast<char*>(ds->fused.va[p]);
   }
+  dc.fusedBytes = ds->fused.bytes;
   dc.mcData = ds->nvls ? reinterpret_cast<char*>(ds->data.mcVa) : nullptr;
   dc.dataBytes = ds->data.bytes;
   dc.status = ds->devStatus;
@@ -315,6 +319,7 @@ void deviceStateDestroy(DeviceState* ds, Bootstrap* bs, bool peersAlive) {
   if (d) {
     multicastTeardown(d, ds);
     symmetricFree(d, bs ? bs->rank() : 0, &ds->data);
+    symmetricFree(d, bs ? bs->rank() : 0, &ds->fused);
     symmetricFree(d, bs ? bs->rank() : 0, &ds->ctrl);
   }
   if (ds->hostStatus) cudaFreeHost(ds->hostStatus);

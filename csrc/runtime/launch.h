@@ -18,7 +18,12 @@ struct LaunchCtx {
   cudaStream_t stream;
   int nblocks;     // max grid of barrier kernels
   bool nvls;
+  size_t llMax;    // largest per-rank payload sent with the LL protocol
 };
+
+inline bool aligned8(const void* a, const void* b) {
+  return ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 7u) == 0;
+}
 
 // redKind: dev::kSum/kProd/kMax/kMin.  Returns cudaErrorInvalidValue for an
 // unsupported combination (the caller picks another algorithm).

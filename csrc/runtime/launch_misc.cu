@@ -21,6 +21,13 @@ __global__ void scaleCopyKernel(T* dst, const T* src, size_t n, double s) {
 cudaError_t launchReduceScatter(const LaunchCtx& lc, vcclDataType_t dt, int redKind, const dev::CollArgs& a) {
   const size_t esz = vcclTypeSize(dt);
   const int n = lc.dc.nranks;
+  const size_t chunkBytes = a.count * esz;
+  if (chunkBytes <= lc.llMax && chunkBytes % 8 == 0 && aligned8(a.send, a.recv)) {
+    VCCL_DISPATCH_TYPE(dt, VCCL_DISPATCH_OP(redKind, {
+      dev::reduceScatterLL<T, K><<<dev::kLLBlocks, kThreads, 0, lc.stream>>>(lc.dc, a);
+    }))
+    return cudaGetLastError();
+  }
   const bool vec = ((reinterpret_cast<uintptr_t>(a.send) | reinterpret_cast<uintptr_t>(a.recv)) & 15u) == 0 &&
                    (a.count * esz) % 16 == 0;
   const size_t pk = 16 / esz;
@@ -37,6 +44,11 @@ cudaError_t launchReduceScatter(const LaunchCtx& lc, vcclDataType_t dt, int redK
 }
 
 cudaError_t launchAllGather(const LaunchCtx& lc, const void* send, void* recv, size_t bytes) {
+  if (bytes <= lc.llMax && bytes % 8 == 0 && aligned8(send, recv)) {
+    dev::allGatherLL<<<dev::kLLBlocks, kThreads, 0, lc.stream>>>(lc.dc, static_cast<const char*>(send),
+                                                                  static_cast<char*>(recv), bytes);
+    return cudaGetLastError();
+  }
   const int g = gridFor(bytes, lc.nblocks);
   dev::allGatherPull<<<g, kThreads, 0, lc.stream>>>(lc.dc, static_cast<const char*>(send),
                                                     static_cast<char*>(recv), bytes);
@@ -45,6 +57,11 @@ cudaError_t launchAllGather(const LaunchCtx& lc, const void* send, void* recv, s
 
 cudaError_t launchBroadcast(const LaunchCtx& lc, const void* send, void* recv, size_t bytes, int root,
                             bool useNvls) {
+  if (bytes <= lc.llMax && bytes % 8 == 0 && aligned8(send, recv)) {
+    dev::broadcastLL<<<dev::kLLBlocks, kThreads, 0, lc.stream>>>(lc.dc, static_cast<const char*>(send),
+                                                                  static_cast<char*>(recv), bytes, root);
+    return cudaGetLastError();
+  }
   const int g = gridFor(bytes, lc.nblocks);
   if (useNvls && lc.nvls)
     dev::broadcastNvls<<<g, kThreads, 0, lc.stream>>>(lc.dc, static_cast<const char*>(send),

@@ -137,10 +137,10 @@ def _declare_extensions(h: ctypes.CDLL) -> None:
     ext = {
         "vcclAllReduceAddRMSNorm": [P, P, P, P, Z, Z, F, I, P, P],
         "vcclGemmBf16": [P, P, P, I, I, I, P],
-        "vcclGemmReduceScatter": [P, P, P, P, I, I, I, P, P],
-        "vcclAllGatherGemm": [P, P, P, P, I, I, I, I, P, P],
-        "vcclSiluMul": [P, P, I, I, P],
-        "vcclMoeDispatchFp8": [P, P, P, P, P, I, I, I, I, P, P],
+        "vcclGemmSiluMul": [P, P, P, I, I, I, P],
+        "vcclGemmReduceScatter": [P, P, P, I, I, I, P, P],
+        "vcclAllGatherGemm": [P, P, P, I, I, I, I, P, P],
+        "vcclMoeDispatchFp8": [P, P, P, P, P, P, P, I, I, I, I, I, P, P],
         "vcclMoeCombine": [P, P, P, P, P, I, I, I, I, P, P],
     }
     for name, args in ext.items():
