@@ -1,0 +1,295 @@
+# SPDX-License-Identifier: Apache-2.0
+"""Flagship benchmark: Llama-3-8B-shaped tensor-parallel MLP layer.
+
+    python bench.py --gpus N --steps K --warmup W            # this library
+    python bench.py --impl reference --gpus N --steps K ...   # the reference
+
+For N > 1 launch with torchrun (one process per GPU, 127.0.0.1 rendezvous).
+
+Step = one sequence-parallel MLP layer at TP = N over T = --tokens tokens:
+all-gather of the [T/N, 4096] activation shards fused into the gate/up
+tcgen05 GEMM (+ SiLU*mul), then the down GEMM fused with the reduce-scatter.
+Inputs are synthetic N(0,1) bf16 activations and random N(0, 0.02) weights
+of the Llama-3-8B MLP (hidden 4096, intermediate 14336).
+
+Metric (lower is better): layer latency in microseconds = mean device time
+of exactly K steps (CUDA events around each step, L2 flushed with a 256 MiB
+write between steps), max over ranks.  Also reported: the same layer with
+NCCL + cuBLAS, the latency at other token counts, all-reduce bus bandwidth,
+the end-to-end latency through the public API including the pinned H2D
+copy of the input shard and the D2H read of the output shard, SM clocks
+sampled during the timed region, and the kernel launch count.
+
+The reference arm runs the reference library unmodified (built from
+source into baseline/_ref): its VcclCommunicator all-gather /
+reduce-scatter over TCP with torch CPU GEMMs, the reference's own way of
+running this layer (its e2e TP test).  Host wall-clock, fp32 (CPU).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+from datetime import timedelta
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+HIDDEN, INTER = 4096, 14336
+METRIC = "tp_mlp_layer_latency_us"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["vccl", "reference"], default="vccl")
+    ap.add_argument("--tokens", type=int, default=8192)
+    ap.add_argument("--sweep", default="1,32,512,8192", help="token counts also reported")
+    ap.add_argument("--no-extras", action="store_true")
+    return ap.parse_args()
+
+
+def env_ranks():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def config(args, n, dtype, l2="flushed (256 MiB write) between timed steps"):
+    return {
+        "model": "Llama-3-8B MLP layer (hidden 4096, intermediate 14336), sequence-parallel tensor parallel",
+        "global_batch": 1,
+        "seq_len": args.tokens,
+        "tokens_per_step": args.tokens,
+        "parallelism": f"tp{n}",
+        "dtype": dtype,
+        "l2": l2,
+    }
+
+
+# ---------------------------------------------------------------------------
+def run_vccl(args) -> int:
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, ROOT)
+    os.environ.setdefault("VCCL_SOCKET_ADDR", "127.0.0.1")
+    import vkccl_b200 as v
+    from vkccl_b200.models.llama_mlp import MLPConfig, TPLlamaMLP
+    from vkccl_b200.utils.timing import ClockSampler, L2Flusher, NvmlClockSampler, max_over_ranks, time_steps
+
+    rank, world, local = env_ranks()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=300))
+        raw = torch.zeros(v.UNIQUE_ID_BYTES, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            raw.copy_(torch.frombuffer(bytearray(v.get_unique_id().to_bytes()), dtype=torch.uint8).cuda())
+        dist.broadcast(raw, 0)
+        uid = v.UniqueId.from_bytes(bytes(raw.cpu().numpy()))
+    else:
+        uid = v.get_unique_id()
+    comm = v.Communicator(world, uid, rank, cuda_device=local)
+    mlp = TPLlamaMLP(comm, MLPConfig(HIDDEN, INTER), seed=0)
+    flush = L2Flusher()
+    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+
+    def shard(tokens):
+        return torch.randn(tokens // world, HIDDEN, device="cuda", generator=gen).bfloat16()
+
+    def measure(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        times = time_steps(fn, steps, flush)
+        return max_over_ranks(sum(times) / len(times))
+
+    # numerics: fused path vs NCCL + cuBLAS on the headline shape
+    x = shard(args.tokens)
+    y = mlp.forward(x)
+    yr = mlp.forward_nccl(x)
+    torch.cuda.synchronize()
+    rel_err = ((y.float() - yr.float()).norm() / (yr.float().norm() + 1e-12)).item()
+    rel_err = max_over_ranks(rel_err)
+
+    # headline: exactly K timed steps, clocks sampled during them
+    sampler = NvmlClockSampler(local)
+    if not sampler.ok:
+        sampler = ClockSampler(50)
+    for _ in range(args.warmup):
+        mlp.forward(x)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        sampler.start()
+    times = time_steps(lambda: mlp.forward(x), args.steps, flush)
+    clocks = sampler.stop() if rank == 0 else {}
+    value = max_over_ranks(sum(times) / len(times))
+    per_step_launches = 3 if world > 1 else 2
+
+    # end to end through the public API: pinned H2D input, forward, D2H output
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+    xd = torch.empty_like(x)
+
+    def e2e_step():
+        xd.copy_(xh, non_blocking=True)
+        out = mlp.forward(xd)
+        yh.copy_(out, non_blocking=True)
+
+    e2e = measure(e2e_step, args.steps, args.warmup)
+    nccl_us = measure(lambda: mlp.forward_nccl(x), args.steps, args.warmup)
+
+    extras = {}
+    if not args.no_extras:
+        sweep = {}
+        for t in [int(s) for s in args.sweep.split(",") if s]:
+            if t % world or t == args.tokens:
+                continue
+            xs = shard(t)
+            sweep[str(t)] = {"vccl_us": round(measure(lambda: mlp.forward(xs), args.steps, args.warmup), 2),
+                             "nccl_cublas_us": round(measure(lambda: mlp.forward_nccl(xs), args.steps, args.warmup), 2)}
+        sweep[str(args.tokens)] = {"vccl_us": round(value, 2), "nccl_cublas_us": round(nccl_us, 2)}
+        extras["latency_by_tokens"] = sweep
+        if world > 1:
+            extras["allreduce_busbw_GBps"] = allreduce_busbw(comm, world, measure)
+    flops = mlp.flops(args.tokens)
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "us",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(value / 1000.0, 4),
+            "higher_is_better": False,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic N(0,1) activations, random N(0,0.02) weights",
+            "config": config(args, world, "bf16"),
+            "clocks": clocks,
+            "e2e": {"value": round(e2e, 2), "unit": "us",
+                    "h2d_bytes_per_step": x.numel() * x.element_size(),
+                    "d2h_bytes_per_step": y.numel() * y.element_size()},
+            "gpu_launches": per_step_launches * args.steps,
+            "nccl_cublas_us": round(nccl_us, 2),
+            "speedup_vs_nccl_cublas": round(nccl_us / value, 3),
+            "achieved_tflops": round(flops / (value * 1e-6) / 1e12, 1),
+            "rel_err_vs_nccl_cublas": rel_err,
+            **extras,
+        }
+        print(json.dumps(line), flush=True)
+    comm.destroy()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def allreduce_busbw(comm, world, measure):
+    import torch
+    import torch.distributed as dist
+
+    out = {}
+    for size in (1 << 20, 16 << 20, 256 << 20):
+        a = torch.randn(size // 2, device="cuda").bfloat16()
+        b = torch.empty_like(a)
+        f = 2.0 * (world - 1) / world
+        tv = measure(lambda: comm.all_reduce(a, b), 10, 3)
+        tn = measure(lambda: dist.all_reduce(a), 10, 3)
+        out[f"{size >> 20}MiB"] = {"vccl": round(size / (tv * 1e3) * f, 1), "nccl": round(size / (tn * 1e3) * f, 1)}
+    return out
+
+
+# ---------------------------------------------------------------------------
+def run_reference(args) -> int:
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    lib = os.path.join(ref, "build", "libvccl.so")
+    rank, world, _ = env_ranks()
+    if not os.path.exists(lib) or not os.path.isdir(os.path.join(ref, "vccl")):
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref not built (cmake build of "
+                              "/root/reference plus its python package; see DESIGN.md)"}))
+        return 0
+    os.environ["VCCL_LIBRARY"] = lib
+    os.environ.setdefault("VCCL_SOCKET_ADDR", "127.0.0.1")
+    os.environ.setdefault("GLOO_SOCKET_IFNAME", "lo")
+    sys.path.insert(0, ref)
+    import torch
+    import torch.distributed as dist
+
+    torch.set_num_threads(max(1, (os.cpu_count() or 8) // max(1, world)))
+    if world > 1:
+        dist.init_process_group("gloo", timeout=timedelta(seconds=600))
+    else:
+        import socket
+
+        with socket.socket() as s:
+            s.bind(("127.0.0.1", 0))
+            port = s.getsockname()[1]
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    from vccl.torch_comm import VcclCommunicator  # the reference's own communicator
+
+    comm = VcclCommunicator(dist.group.WORLD)
+    g = torch.Generator().manual_seed(rank)
+    inter = INTER // world
+    wg = torch.randn(inter, HIDDEN, generator=g) * 0.02
+    wu = torch.randn(inter, HIDDEN, generator=g) * 0.02
+    wd = torch.randn(HIDDEN, inter, generator=g) * 0.02
+    x_shard = torch.randn(args.tokens // world, HIDDEN, generator=g)
+
+    def step():
+        x = comm.all_gather(x_shard, dim=0)
+        h = torch.nn.functional.silu(x @ wg.T) * (x @ wu.T)
+        return comm.reduce_scatter(h @ wd.T, dim=0)
+
+    for _ in range(args.warmup):
+        step()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    us = (time.perf_counter() - t0) / args.steps * 1e6
+    t = torch.tensor([us], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    us = t.item()
+    if rank == 0:
+        print(json.dumps({
+            "impl": "reference",
+            "metric": METRIC,
+            "value": round(us, 1),
+            "unit": "us",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(us / 1000.0, 3),
+            "higher_is_better": False,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "fp32",
+            "data": "synthetic N(0,1) activations, random N(0,0.02) weights",
+            "config": config(args, world, "fp32 (reference host path: torch CPU GEMMs + vccl TCP collectives)",
+                             l2="not applicable (host path)"),
+            "timing": "host wall clock, mean of K steps, max over ranks (the reference has no device path)",
+        }), flush=True)
+    comm.destroy()
+    dist.destroy_process_group()
+    return 0
+
+
+def main() -> int:
+    args = parse()
+    if args.tokens % args.gpus:
+        raise SystemExit("--tokens must be divisible by --gpus")
+    return run_reference(args) if args.impl == "reference" else run_vccl(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

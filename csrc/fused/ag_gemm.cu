@@ -58,6 +58,7 @@ struct AgHooks : gemm::NoHooks {
   int shardRows;
   int K;
   int startTm;         // first tile row of this rank's shard
+  int groupRows;       // row tiles per tile group (divides the shard's tiles when possible)
   uint32_t ctas;       // fixed grid size
 
   __device__ __forceinline__ uint32_t* ctrl(int rank, size_t off) const {
@@ -67,12 +68,18 @@ struct AgHooks : gemm::NoHooks {
   __device__ __forceinline__ void teardown(uint32_t* hs) const {
     ctrl(c.rank, dev::kAgCallsOff)[blockIdx.x] = hs[0] + 1u;
   }
-  // Row tiles start at this rank's shard and wrap around.
+  // Row tiles start at this rank's shard and wrap around.  They are walked
+  // in groups of `groupRows` row tiles; inside a group consecutive CTAs
+  // share a weight tile, so a wave of CTAs reads each B tile once per group
+  // instead of once per row tile.
   __device__ __forceinline__ gemm::TileInfo tileAt(const gemm::GemmShape& s, int t, int BN) const {
     gemm::TileInfo ti;
-    const int r = t / s.tilesN;
-    ti.tn = t % s.tilesN;
-    ti.tm = (r + startTm) % s.tilesM;
+    const int groupTiles = groupRows * s.tilesN;
+    const int g = t / groupTiles;
+    const int rowsHere = s.tilesM - g * groupRows < groupRows ? s.tilesM - g * groupRows : groupRows;
+    const int local = t - g * groupTiles;
+    ti.tn = local / rowsHere;
+    ti.tm = (g * groupRows + local % rowsHere + startTm) % s.tilesM;
     ti.row0 = ti.tm * gemm::kBM;
     ti.col0 = ti.tn * BN;
     return ti;
@@ -196,6 +203,16 @@ extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, voi
   hooks.shardRows = M / n;
   hooks.K = K;
   hooks.startTm = (comm->rank * (M / n)) / gemm::kBM;
+  // Shard-aligned groups of up to 16 row tiles (the rotation by startTm then
+  // keeps groups inside shards); ragged shards fall back to one row per group.
+  const int shardTiles = (M / n) % gemm::kBM == 0 ? (M / n) / gemm::kBM : 0;
+  int groupRows = 1;
+  for (int gsz = 16; gsz >= 1; gsz /= 2)
+    if (shardTiles > 0 && shardTiles % gsz == 0) {
+      groupRows = gsz;
+      break;
+    }
+  hooks.groupRows = groupRows;
   hooks.ctas = static_cast<uint32_t>(ctas);
   const char* xfull = dc.fused[comm->rank] + xOff;
   if (siluMul) {

@@ -113,133 +113,6 @@ __device__ __forceinline__ char* llSlot(const DevComm& c, int owner, uint32_t pa
   return c.ctrl[owner] + kLLOff + (static_cast<size_t>(parity) * kMaxRanks + src) * kLLSlotBytes;
 }
 
-// Wait for a complete LL line of epoch e; false on timeout/abort.
-__device__ __forceinline__ bool llWait(const DevComm& c, const char* p, uint32_t e, uint64_t* out) {
-  uint4 v = ldVolatile16(p);
-  if (v.y != e || v.w != e) {
-    const uint64_t start = globalTimerNs();
-    for (uint32_t spin = 1;; ++spin) {
-      v = ldVolatile16(p);
-      if (v.y == e && v.w == e) break;
-      if ((spin & 1023u) == 0u && shouldGiveUp(c, start, kWhereLL, 0)) return false;
-    }
-  }
-  *out = static_cast<uint64_t>(v.x) | (static_cast<uint64_t>(v.z) << 32);
-  return true;
-}
-
-template <typename T, int K>
-__global__ void __launch_bounds__(512) allReduceLL(DevComm c, CollArgs a) {
-  __shared__ uint32_t sE;
-  const int blk = blockIdx.x;
-  if (threadIdx.x == 0) {
-    uint32_t* ep = ctrlAt<uint32_t>(c, c.rank, kLLEpochOff) + blk;
-    sE = *ep + 1u;
-    *ep = sE;
-  }
-  __syncthreads();
-  const uint32_t e = sE;
-  const uint32_t par = e & 1u;
-  const size_t bytes = a.count * sizeof(T);
-  const size_t words = (bytes + 7) / 8;
-  size_t w0, w1;
-  blockRange(words, gridDim.x, blk, 1, &w0, &w1);
-  const int n = c.nranks, me = c.rank;
-
-  for (size_t w = w0 + threadIdx.x; w < w1; w += blockDim.x) {
-    uint64_t word = readWord(a.send, w, bytes);
-    if (a.premul) {
-      WordPack<T> p;
-      p.load(word);
-      p.scale(a.scalar);
-      word = p.pack();
-    }
-    const uint4 line = make_uint4(static_cast<uint32_t>(word), e, static_cast<uint32_t>(word >> 32), e);
-    for (int k = 1; k < n; k++) {
-      int p = me + k;
-      if (p >= n) p -= n;
-      stVolatile16(llSlot(c, p, par, me) + w * 16, line);
-    }
-  }
-  for (size_t w = w0 + threadIdx.x; w < w1; w += blockDim.x) {
-    WordPack<T> acc;
-    acc.load(readWord(a.send, w, bytes));
-    if (a.premul) acc.scale(a.scalar);
-    bool ok = true;
-    for (int k = 1; k < n && ok; k++) {
-      int p = me + k;
-      if (p >= n) p -= n;
-      uint64_t v;
-      ok = llWait(c, llSlot(c, me, par, p) + w * 16, e, &v);
-      if (ok) acc.template fold<K>(v);
-    }
-    if (!ok) break;
-    if (a.avg) acc.scale(1.0 / n);
-    writeWord(a.recv, w, bytes, acc.pack());
-  }
-}
-
-// Block-level LL epoch: every LL kernel runs with kLLBlocks blocks, so each
-// block's counter advances once per LL launch on every rank.
-__device__ __forceinline__ uint32_t llEpoch(const DevComm& c) {
-  __shared__ uint32_t sE;
-  if (threadIdx.x == 0) {
-    uint32_t* ep = ctrlAt<uint32_t>(c, c.rank, kLLEpochOff) + blockIdx.x;
-    sE = *ep + 1u;
-    *ep = sE;
-  }
-  __syncthreads();
-  return sE;
-}
-
-__device__ __forceinline__ void llPut(const DevComm& c, int peer, uint32_t par, uint32_t e, size_t w,
-                                      uint64_t word) {
-  const uint4 line = make_uint4(static_cast<uint32_t>(word), e, static_cast<uint32_t>(word >> 32), e);
-  stVolatile16(llSlot(c, peer, par, c.rank) + w * 16, line);
-}
-
-// LL reduce-scatter: chunk q (recvcount elements) goes to rank q as LL
-// lines; q folds them into its own chunk.  recvcount*sizeof(T) must be a
-// multiple of 8 and fit kLLMaxBytes; send/recv 8-byte aligned.
-template <typename T, int K>
-__global__ void __launch_bounds__(512) reduceScatterLL(DevComm c, CollArgs a) {
-  const uint32_t e = llEpoch(c);
-  const uint32_t par = e & 1u;
-  const int n = c.nranks, me = c.rank;
-  const size_t bytes = a.count * sizeof(T);
-  const size_t words = bytes / 8;
-  size_t w0, w1;
-  blockRange(words, gridDim.x, blockIdx.x, 1, &w0, &w1);
-  for (size_t w = w0 + threadIdx.x; w < w1; w += blockDim.x) {
-    for (int k = 1; k < n; k++) {
-      const int q = (me + k) % n;
-      uint64_t word = *reinterpret_cast<const uint64_t*>(a.send + q * bytes + w * 8);
-      if (a.premul) {
-        WordPack<T> p;
-        p.load(word);
-        p.scale(a.scalar);
-        word = p.pack();
-      }
-      llPut(c, q, par, e, w, word);
-    }
-  }
-  for (size_t w = w0 + threadIdx.x; w < w1; w += blockDim.x) {
-    WordPack<T> acc;
-    acc.load(*reinterpret_cast<const uint64_t*>(a.send + me * bytes + w * 8));
-    if (a.premul) acc.scale(a.scalar);
-    bool ok = true;
-    for (int k = 1; k < n && ok; k++) {
-      const int p = (me + k) % n;
-      uint64_t v;
-      ok = llWait(c, llSlot(c, me, par, p) + w * 16, e, &v);
-      if (ok) acc.template fold<K>(v);
-    }
-    if (!ok) break;
-    if (a.avg) acc.scale(1.0 / n);
-    *reinterpret_cast<uint64_t*>(a.recv + w * 8) = acc.pack();
-  }
-}
-
 // ---------------------------------------------------------------------------
 // Two-shot all-reduce / reduce.  Staging: n input slots + 1 result slot of
 // slotElems elements each.  root < 0: all-reduce; else only root gathers.
@@ -477,3 +350,5 @@ __global__ void __launch_bounds__(512) reduceScatterPush(DevComm c, CollArgs a, 
 
 }  // namespace dev
 }  // namespace vccl
+
+#include "kernels/ll.cuh"

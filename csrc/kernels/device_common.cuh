@@ -20,7 +20,7 @@ namespace dev {
 
 constexpr int kMaxRanks = 8;     // one NVSwitch domain of an HGX B200 board
 constexpr int kMaxBlocks = 128;  // largest grid of a barrier-based kernel
-constexpr int kLLBlocks = 16;    // fixed grid of the LL kernels
+constexpr int kLLBlocks = 64;    // fixed grid of the LL kernels
 constexpr int kMaxChannels = 8;  // point-to-point channels per peer
 constexpr int kP2pSlots = 4;     // ring depth of one channel
 
@@ -49,13 +49,14 @@ constexpr size_t kAgLocalReadyOff = kAgCallsOff + 1024;     // u32[kMaxRanks], l
 constexpr size_t kMoeOff = 73728;                           // MoE dispatch/combine counters
 constexpr size_t kCtrlHeader = 1 << 20;
 
-constexpr size_t kLLMaxBytes = 256 << 10;               // largest LL payload per rank
+constexpr size_t kLLMaxBytes = 1 << 20;                 // largest LL payload per source rank
 constexpr size_t kLLSlotBytes = 2 * kLLMaxBytes;        // LL lines carry 8 payload bytes per 16
 constexpr size_t kLLOff = kCtrlHeader;                  // [parity][src rank][slot]
 constexpr size_t kLLBytes = 2 * kMaxRanks * kLLSlotBytes;
+constexpr size_t kLLResOff = kLLOff + kLLBytes;         // second LL hop (two-shot LL), same shape
 
 constexpr size_t kP2pSlotBytes = 512 << 10;
-constexpr size_t kP2pOff = kLLOff + kLLBytes;           // [src rank][channel][slot]
+constexpr size_t kP2pOff = kLLResOff + kLLBytes;        // [src rank][channel][slot]
 constexpr size_t kP2pBytes = size_t(kMaxRanks) * kMaxChannels * kP2pSlots * kP2pSlotBytes;
 constexpr size_t kCtrlBytes = kP2pOff + kP2pBytes;
 
@@ -147,6 +148,20 @@ __device__ __forceinline__ bool waitAtLeast(const DevComm& c, const uint32_t* fl
   fenceSys();
   return true;
 }
+__device__ __forceinline__ void stReleaseSys32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Spin with acquire loads until *flag - target >= 0.  False on timeout/abort.
+__device__ __forceinline__ bool waitAcquire(const DevComm& c, const uint32_t* flag, uint32_t target, uint32_t where,
+                                            uint32_t detail) {
+  if (static_cast<int32_t>(ldAcquireSys(flag) - target) >= 0) return true;
+  const uint64_t start = globalTimerNs();
+  for (uint32_t spin = 1;; ++spin) {
+    if (static_cast<int32_t>(ldAcquireSys(flag) - target) >= 0) return true;
+    if ((spin & 255u) == 0u && shouldGiveUp(c, start, where, detail)) return false;
+  }
+}
+
 __device__ __forceinline__ bool waitAtLeast64(const DevComm& c, const uint64_t* flag,
                                               uint64_t target, uint32_t where, uint32_t detail) {
   if (ldAcquireSys64(flag) >= target) return true;
@@ -181,11 +196,13 @@ __device__ __forceinline__ bool blockBarrier(const DevComm& c, int blk, uint32_t
   __syncthreads();
   const int t = threadIdx.x;
   if (t < c.nranks) {
+    // Release store / acquire poll: measured about half the latency of a
+    // fence.acq_rel.sys on each side.  The release is cumulative over the
+    // block's writes ordered before it by the bar.sync above.
     const uint32_t e = sEpoch;
-    fenceSys();
-    stRelaxedSys(ctrlAt<uint32_t>(c, t, flagsOff) + blk * kMaxRanks + c.rank, e);
+    stReleaseSys32(ctrlAt<uint32_t>(c, t, flagsOff) + blk * kMaxRanks + c.rank, e);
     const uint32_t* mine = ctrlAt<uint32_t>(c, c.rank, flagsOff) + blk * kMaxRanks + t;
-    if (!waitAtLeast(c, mine, e, where, static_cast<uint32_t>(t))) sFailed = 1;
+    if (!waitAcquire(c, mine, e, where, static_cast<uint32_t>(t))) sFailed = 1;
   }
   __syncthreads();
   return sFailed == 0;

@@ -53,22 +53,44 @@ __global__ void __launch_bounds__(512) allGatherLL(DevComm c, const char* send, 
   size_t w0, w1;
   blockRange(words, gridDim.x, blockIdx.x, 1, &w0, &w1);
   char* own = recv + me * bytes;
-  for (size_t w = w0 + threadIdx.x; w < w1; w += blockDim.x) {
-    const uint64_t word = *reinterpret_cast<const uint64_t*>(send + w * 8);
-    for (int k = 1; k < n; k++) llPut(c, (me + k) % n, par, e, w, word);
-    if (own != send) *reinterpret_cast<uint64_t*>(own + w * 8) = word;
-  }
-  for (size_t w = w0 + threadIdx.x; w < w1; w += blockDim.x) {
+  constexpr int U = kLLUnroll;
+  const size_t nthr = blockDim.x;
+  for (size_t b = w0 + threadIdx.x; b < w1; b += U * nthr) {
+    uint64_t word[U];
+#pragma unroll
+    for (int u = 0; u < U; u++)
+      if (b + u * nthr < w1) word[u] = *reinterpret_cast<const uint64_t*>(send + (b + u * nthr) * 8);
     for (int k = 1; k < n; k++) {
-      const int p = (me + k) % n;
-      uint64_t v;
-      if (!llWait(c, llSlot(c, me, par, p) + w * 16, e, &v)) return;
-      *reinterpret_cast<uint64_t*>(recv + p * bytes + w * 8) = v;
+      char* dst = llSlot(c, (me + k) % n, par, me);
+#pragma unroll
+      for (int u = 0; u < U; u++)
+        if (b + u * nthr < w1) stVolatile16(dst + (b + u * nthr) * 16, llLine(word[u], e));
+    }
+    if (own != send) {
+#pragma unroll
+      for (int u = 0; u < U; u++)
+        if (b + u * nthr < w1) *reinterpret_cast<uint64_t*>(own + (b + u * nthr) * 8) = word[u];
+    }
+  }
+  for (int k = 1; k < n; k++) {
+    const int p = (me + k) % n;
+    const char* src = llSlot(c, me, par, p);
+    for (size_t b = w0 + threadIdx.x; b < w1; b += U * nthr) {
+      uint64_t v[U];
+      if (!llWaitU<U>(c, src, b, nthr, w1, e, v)) return;
+#pragma unroll
+      for (int u = 0; u < U; u++)
+        if (b + u * nthr < w1) *reinterpret_cast<uint64_t*>(recv + p * bytes + (b + u * nthr) * 8) = v[u];
     }
   }
 }
 
-// LL broadcast: the root stores LL lines into every peer's slot.
+// LL broadcast: the root stores LL lines into every peer's slot.  Reusing
+// an LL slot two calls later is safe only if, in every LL call, each rank
+// hears from every other rank (then finishing call k+1 proves every peer
+// finished call k).  Broadcast data only flows from the root, so every
+// rank also exchanges a one-line token with every peer, in the second-hop
+// LL region that broadcast does not otherwise use.
 __global__ void __launch_bounds__(512) broadcastLL(DevComm c, const char* send, char* recv, size_t bytes, int root) {
   const uint32_t e = llEpoch(c);
   const uint32_t par = e & 1u;
@@ -76,18 +98,44 @@ __global__ void __launch_bounds__(512) broadcastLL(DevComm c, const char* send, 
   const size_t words = bytes / 8;
   size_t w0, w1;
   blockRange(words, gridDim.x, blockIdx.x, 1, &w0, &w1);
-  if (me == root) {
-    for (size_t w = w0 + threadIdx.x; w < w1; w += blockDim.x) {
-      const uint64_t word = *reinterpret_cast<const uint64_t*>(send + w * 8);
-      for (int k = 1; k < n; k++) llPut(c, (me + k) % n, par, e, w, word);
-      if (recv != send) *reinterpret_cast<uint64_t*>(recv + w * 8) = word;
-    }
-    return;
+  const int p = threadIdx.x;
+  if (p < n && p != me) {
+    const uint4 token = make_uint4(0, e, 0, e);
+    stVolatile16(llResSlot(c, p, par, me) + blockIdx.x * 16, token);
   }
-  for (size_t w = w0 + threadIdx.x; w < w1; w += blockDim.x) {
-    uint64_t v;
-    if (!llWait(c, llSlot(c, me, par, root) + w * 16, e, &v)) return;
-    *reinterpret_cast<uint64_t*>(recv + w * 8) = v;
+  constexpr int U = kLLUnroll;
+  const size_t nthr = blockDim.x;
+  if (me == root) {
+    for (size_t b = w0 + threadIdx.x; b < w1; b += U * nthr) {
+      uint64_t word[U];
+#pragma unroll
+      for (int u = 0; u < U; u++)
+        if (b + u * nthr < w1) word[u] = *reinterpret_cast<const uint64_t*>(send + (b + u * nthr) * 8);
+      for (int k = 1; k < n; k++) {
+        char* dst = llSlot(c, (me + k) % n, par, me);
+#pragma unroll
+        for (int u = 0; u < U; u++)
+          if (b + u * nthr < w1) stVolatile16(dst + (b + u * nthr) * 16, llLine(word[u], e));
+      }
+      if (recv != send) {
+#pragma unroll
+        for (int u = 0; u < U; u++)
+          if (b + u * nthr < w1) *reinterpret_cast<uint64_t*>(recv + (b + u * nthr) * 8) = word[u];
+      }
+    }
+  } else {
+    const char* src = llSlot(c, me, par, root);
+    for (size_t b = w0 + threadIdx.x; b < w1; b += U * nthr) {
+      uint64_t v[U];
+      if (!llWaitU<U>(c, src, b, nthr, w1, e, v)) return;
+#pragma unroll
+      for (int u = 0; u < U; u++)
+        if (b + u * nthr < w1) *reinterpret_cast<uint64_t*>(recv + (b + u * nthr) * 8) = v[u];
+    }
+  }
+  if (p < n && p != me) {
+    uint64_t token;
+    llWait(c, llResSlot(c, me, par, p) + blockIdx.x * 16, e, &token);
   }
 }
 

@@ -240,14 +240,20 @@ ArAlgo pickAllReduce(const HostOp& h, size_t bytes) {
   const bool llOk = bytes <= dev::kLLMaxBytes &&
                     ((reinterpret_cast<uintptr_t>(h.send) | reinterpret_cast<uintptr_t>(h.recv)) & 7u) == 0;
   const bool nvlsOk = ds.nvls && nvlsSupports(h.dt, h.redKind);
+  const int n = h.comm->nranks;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(h.send) | reinterpret_cast<uintptr_t>(h.recv)) & 7u) == 0;
+  const bool ll2Ok = aligned && ((bytes + 7) / 8 + n - 1) / n * 8 <= dev::kLLMaxBytes;
   if (force == "ll" || force == "oneshot" || force == "recdouble") {
     if (llOk) return ArAlgo::LL;
+  } else if (force == "ll2") {
+    if (ll2Ok) return ArAlgo::LL2;
   } else if (force == "nvls") {
     if (nvlsOk) return ArAlgo::Nvls;
   } else if (force == "twoshot" || force == "ring") {
     return ArAlgo::TwoShot;
   }
   if (llOk && bytes <= ds.llMaxBytes) return ArAlgo::LL;
+  if (ll2Ok && bytes <= ds.ll2MaxBytes) return ArAlgo::LL2;
   // Per GPU, NVLS moves (1 + 1/n) S each way against 2 (n-1)/n S for the
   // two-shot: it only wins from four ranks on.
   if (nvlsOk && h.comm->nranks >= envLong("VCCL_NVLS_MIN_RANKS", 4) &&

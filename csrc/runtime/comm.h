@@ -53,7 +53,8 @@ struct DeviceState {
   uint32_t* devAbort = nullptr;
   dev::DevComm dc{};
   int nblocks = 32;                // grid of barrier-based kernels
-  size_t llMaxBytes = 0;           // LL all-reduce threshold
+  size_t llMaxBytes = 0;           // one-hop LL threshold (per-rank payload)
+  size_t ll2MaxBytes = 0;          // two-hop LL all-reduce threshold
 };
 
 struct CustomOp {

@@ -19,10 +19,6 @@ __device__ __forceinline__ uint32_t ldAcquireSys32(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void stReleaseSys32(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
 template <int V>
 __device__ __forceinline__ bool benchBarrier(const DevComm& c, uint32_t e) {
   const int t = threadIdx.x;

@@ -232,8 +232,12 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
   ds->nblocks = static_cast<int>(envLong("VCCL_NBLOCKS", 64));
   if (ds->nblocks < 1) ds->nblocks = 1;
   if (ds->nblocks > dev::kMaxBlocks) ds->nblocks = dev::kMaxBlocks;
-  ds->llMaxBytes = envBytes("VCCL_LL_MAX", 64u << 10);
+  // One-hop LL sends (n-1) x 2 x payload from every rank, so its useful range
+  // shrinks with the rank count.
+  const size_t llDefault = n <= 2 ? (1u << 20) : n <= 4 ? (512u << 10) : (256u << 10);
+  ds->llMaxBytes = envBytes("VCCL_LL_MAX", llDefault);
   if (ds->llMaxBytes > dev::kLLMaxBytes) ds->llMaxBytes = dev::kLLMaxBytes;
+  ds->ll2MaxBytes = envBytes("VCCL_LL2_MAX", 4u << 20);
 
   if (n > 1) {
     if (n > dev::kMaxRanks) {
@@ -280,7 +284,7 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
     VTRY(symmetricAlloc(bs, ds.get(), dataBytes, dataAlign, &ds->data));
     VTRY(symmetricAlloc(bs, ds.get(), fusedBytes, gran, &ds->fused));
     CUDART_TRY(cudaMemset(reinterpret_cast<void*>(ds->ctrl.va[me]), 0, dev::kCtrlHeader));
-    CUDART_TRY(cudaMemset(reinterpret_cast<void*>(ds->ctrl.va[me] + dev::kLLOff), 0xff, dev::kLLBytes));
+    CUDART_TRY(cudaMemset(reinterpret_cast<void*>(ds->ctrl.va[me] + dev::kLLOff), 0xff, 2 * dev::kLLBytes));
     CUDART_TRY(cudaDeviceSynchronize());
     VTRY(bs->barrier());
     if (everyone(bs, mcCap != 0)) ds->nvls = multicastSetup(bs, ds.get()) == vcclSuccess;

@@ -11,7 +11,7 @@
 
 namespace vccl {
 
-enum class ArAlgo : int { LL = 0, TwoShot = 1, Nvls = 2 };
+enum class ArAlgo : int { LL = 0, TwoShot = 1, Nvls = 2, LL2 = 3 };
 
 struct LaunchCtx {
   dev::DevComm dc;

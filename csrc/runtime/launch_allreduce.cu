@@ -38,6 +38,16 @@ cudaError_t launchAllReduce(const LaunchCtx& lc, ArAlgo algo, vcclDataType_t dt,
     }))
     return cudaGetLastError();
   }
+  if (algo == ArAlgo::LL2) {
+    const size_t words = (bytes + 7) / 8;
+    if ((words + n - 1) / n * 8 > dev::kLLMaxBytes ||
+        ((reinterpret_cast<uintptr_t>(a.send) | reinterpret_cast<uintptr_t>(a.recv)) & 7u) != 0 || a.root >= 0)
+      return cudaErrorInvalidValue;
+    VCCL_DISPATCH_TYPE(dt, VCCL_DISPATCH_OP(redKind, {
+      dev::allReduceLL2<T, K><<<dev::kLLBlocks, kThreads, 0, lc.stream>>>(lc.dc, a);
+    }))
+    return cudaGetLastError();
+  }
   if (algo == ArAlgo::Nvls) {
     if (!lc.nvls || !nvlsSupports(dt, redKind) || a.root >= 0) return cudaErrorInvalidValue;
     const size_t roundBytes = (lc.dc.dataBytes - 16 * dev::kMaxRanks) / 16 * 16;

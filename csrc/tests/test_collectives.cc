@@ -348,7 +348,7 @@ void algoAB(vcclComm_t c, int me, int n, size_t cnt) {
   std::vector<float> s(cnt), r(cnt);
   fill(s.data(), vcclFloat32, me, cnt);
   for (vcclRedOp_t op : {vcclSum, vcclMax}) {
-    for (const char* algo : {"ring", "recdouble", "twoshot", "ll", "nvls"}) {
+    for (const char* algo : {"ring", "recdouble", "twoshot", "ll", "ll2", "nvls"}) {
       setenv("VCCL_ALLREDUCE_ALGO", algo, 1);
       std::fill(r.begin(), r.end(), -7.0f);
       EXPECT_OK(vcclAllReduce(s.data(), r.data(), cnt, vcclFloat32, op, c));
@@ -370,7 +370,7 @@ void deviceSweep(vcclComm_t c, int me, int n) {
       cudaMalloc(&ds, cnt * es);
       cudaMalloc(&dr, cnt * es);
       cudaMemcpy(ds, h.data(), cnt * es, cudaMemcpyHostToDevice);
-      for (const char* algo : {"", "ll", "twoshot", "nvls"}) {
+      for (const char* algo : {"", "ll", "ll2", "twoshot", "nvls"}) {
         if (*algo) setenv("VCCL_ALLREDUCE_ALGO", algo, 1);
         else unsetenv("VCCL_ALLREDUCE_ALGO");
         cudaMemset(dr, 0, cnt * es);

@@ -30,3 +30,19 @@ def test_fused_tp_ops(nranks):
     p = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=900)
     assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-6000:]
     assert p.stdout.count("fused ok") == nranks
+
+
+@pytest.mark.parametrize("nranks", [2, 4, 8])
+def test_back_to_back_stress(nranks):
+    """Unsynchronised streams of mixed collectives and graph replays."""
+    if gpu_count() < nranks:
+        pytest.skip(f"needs {nranks} GPUs")
+    port = free_port()
+    env = dict(os.environ, VCCL_COMM_ID=f"127.0.0.1:{free_port()}", VCCL_SOCKET_ADDR="127.0.0.1",
+               VCCL_TIMEOUT="20")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={nranks}",
+           "--master-addr=127.0.0.1", f"--master-port={port}",
+           os.path.join(ROOT, "tests", "workers", "stress_worker.py")]
+    p = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=900)
+    assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-6000:]
+    assert p.stdout.count("stress ok") == nranks

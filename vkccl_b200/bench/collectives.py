@@ -99,6 +99,7 @@ def main() -> int:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--libs", default="vccl,nccl")
+    ap.add_argument("--algos", default="", help="also time these forced all-reduce algorithms")
     ap.add_argument("--out", default="")
     a = ap.parse_args()
 
@@ -135,15 +136,24 @@ def main() -> int:
                     send = torch.randn(count, device="cuda").to(dt)
                     recv = send.clone() if op == "broadcast" else torch.empty_like(send)
                 row = {"op": op, "dtype": dname, "bytes": count * es, "n": world}
-                for libname in a.libs.split(","):
+                variants = [(lib_, None) for lib_ in a.libs.split(",")]
+                if op == "allreduce" and a.algos:
+                    variants += [("vccl", algo) for algo in a.algos.split(",")]
+                for libname, algo in variants:
+                    if algo:
+                        os.environ["VCCL_ALLREDUCE_ALGO"] = algo
                     fn = make_call(libname, op, comm, send, recv, world)
                     us = time_graph(fn, a.iters, a.warmup)
+                    os.environ.pop("VCCL_ALLREDUCE_ALGO", None)
+                    if libname == "vccl" and comm.async_error() != 0:
+                        raise RuntimeError(f"vccl async error during {op} {count * es} B: {comm.last_error()}")
                     t = torch.tensor([us], device="cuda")
                     dist.all_reduce(t, op=dist.ReduceOp.MAX)
                     us = t.item()
                     algbw = count * es / (us * 1e3)
-                    row[libname + "_us"] = round(us, 2)
-                    row[libname + "_busbw"] = round(algbw * bus_factor(op, world), 2)
+                    key = libname + ("_" + algo if algo else "")
+                    row[key + "_us"] = round(us, 2)
+                    row[key + "_busbw"] = round(algbw * bus_factor(op, world), 2)
                 rows.append(row)
                 if rank == 0:
                     print(json.dumps(row), flush=True)
