@@ -156,6 +156,7 @@ def run_vccl(args) -> int:
                              "nccl_cublas_us": round(measure(lambda: mlp.forward_nccl(xs), args.steps, args.warmup), 2)}
         sweep[str(args.tokens)] = {"vccl_us": round(value, 2), "nccl_cublas_us": round(nccl_us, 2)}
         extras["latency_by_tokens"] = sweep
+        extras["breakdown_us"] = breakdown(mlp, x, world, measure)
         if world > 1:
             extras["allreduce_busbw_GBps"] = allreduce_busbw(comm, world, measure)
     flops = mlp.flops(args.tokens)
@@ -191,6 +192,25 @@ def run_vccl(args) -> int:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def breakdown(mlp, x, world, measure):
+    """Each fused kernel alone, next to the same GEMM with no communication."""
+    import torch
+
+    from vkccl_b200.ops.fused import all_gather_gemm, gemm_reduce_scatter
+    from vkccl_b200.ops.gemm import gemm_bf16, gemm_silu_mul
+
+    rows = x.shape[0] * world
+    xfull = torch.randn(rows, x.shape[1], device="cuda").bfloat16()
+    h = torch.empty((rows, mlp.inter_shard), dtype=torch.bfloat16, device="cuda")
+    out = {
+        "ag_gemm_silu": measure(lambda: all_gather_gemm(mlp.comm, x, mlp.w_gate_up, silu_mul=True, out=h), 10, 3),
+        "gemm_silu_local": measure(lambda: gemm_silu_mul(xfull, mlp.w_gate_up, out=h), 10, 3),
+        "gemm_rs": measure(lambda: gemm_reduce_scatter(mlp.comm, h, mlp.w_down), 10, 3),
+        "gemm_local": measure(lambda: gemm_bf16(h, mlp.w_down), 10, 3),
+    }
+    return {k: round(v, 2) for k, v in out.items()}
 
 
 def allreduce_busbw(comm, world, measure):

@@ -86,11 +86,14 @@ struct AgHooks : gemm::NoHooks {
   }
   __device__ __forceinline__ bool beforeLoad(const gemm::TileInfo& ti, const gemm::GemmShape& s, uint32_t* hs,
                                              volatile int*) const {
-    const uint32_t target = (hs[0] + 1u) * ctas;
+    const uint32_t k = hs[0];
     const int last = (ti.row0 + gemm::kBM < s.M ? ti.row0 + gemm::kBM : s.M) - 1;
     for (int q = ti.row0 / shardRows; q <= last / shardRows; q++) {
-      const uint32_t* flag = q == c.rank ? ctrl(c.rank, dev::kAgReadyOff) + q : ctrl(c.rank, dev::kAgLocalReadyOff) + q;
-      if (!dev::waitAtLeast(c, flag, target, dev::kWhereFused, 300 + q)) return false;
+      // Own shard: staged by every CTA (ready[me] bumps once per call);
+      // remote shard q: every CTA pulled its slice (local counter).
+      const bool own = q == c.rank;
+      const uint32_t* flag = own ? ctrl(c.rank, dev::kAgReadyOff) + q : ctrl(c.rank, dev::kAgLocalReadyOff) + q;
+      if (!dev::waitAcquire(c, flag, own ? k + 1u : (k + 1u) * ctas, dev::kWhereFused, 300 + q)) return false;
     }
     fenceProxyAsync();
     return true;
@@ -106,11 +109,12 @@ struct AgHooks : gemm::NoHooks {
     const int per = (shardRows + static_cast<int>(ctas) - 1) / static_cast<int>(ctas);
     const int r0 = blockIdx.x * per < shardRows ? blockIdx.x * per : shardRows;
     const int r1 = r0 + per < shardRows ? r0 + per : shardRows;
-    // 1. peers must have finished pulling the previous call's shard
+    // 1. every peer must have finished pulling the previous call's shard
+    //    (taken[p] counts calls in which rank p pulled all of my shard)
     if (tid == 0) {
       sFail = 0;
       for (int p = 0; p < n; p++)
-        if (p != me && !dev::waitAtLeast(c, ctrl(me, dev::kAgTakenOff) + p, k * ctas, dev::kWhereFused, 400 + p))
+        if (p != me && !dev::waitAcquire(c, ctrl(me, dev::kAgTakenOff) + p, k, dev::kWhereFused, 400 + p))
           sFail = 1;
     }
     copyWarpsBarrier();
@@ -118,7 +122,8 @@ struct AgHooks : gemm::NoHooks {
       *abortFlag = 1;
       return;
     }
-    // 2. stage my slice of my shard, announce it to everyone (me included)
+    // 2. stage my slice of my shard; the last CTA to finish announces the
+    //    shard to every rank once (me included)
     if (r1 > r0)
       groupCopy(xfull + (static_cast<size_t>(me) * shardRows + r0) * rowBytes, xShard + r0 * rowBytes,
                 (r1 - r0) * rowBytes, tid);
@@ -126,12 +131,15 @@ struct AgHooks : gemm::NoHooks {
     if (tid == 0) {
       fenceProxyAsync();
       dev::fenceSys();
-      for (int p = 0; p < n; p++) redAddRelease(ctrl(p, dev::kAgReadyOff) + me, 1u, true);
+      const uint32_t old = atomicAdd(ctrl(me, dev::kAgStagedOff), 1u);
+      if (old + 1u == (k + 1u) * ctas)
+        for (int p = 0; p < n; p++) redAddRelease(ctrl(p, dev::kAgReadyOff) + me, 1u, true);
     }
-    // 3. pull my slice of every peer's shard
+    // 3. pull my slice of every peer's shard; the last CTA to finish a shard
+    //    tells its owner it may be overwritten
     for (int s = 1; s < n; s++) {
       const int q = (me + s) % n;
-      if (tid == 0 && !dev::waitAtLeast(c, ctrl(me, dev::kAgReadyOff) + q, (k + 1u) * ctas, dev::kWhereFused, 500 + q))
+      if (tid == 0 && !dev::waitAcquire(c, ctrl(me, dev::kAgReadyOff) + q, k + 1u, dev::kWhereFused, 500 + q))
         sFail = 1;
       copyWarpsBarrier();
       if (sFail || *abortFlag) {
@@ -143,9 +151,9 @@ struct AgHooks : gemm::NoHooks {
       copyWarpsBarrier();
       if (tid == 0) {
         fenceProxyAsync();
-        redAddRelease(ctrl(me, dev::kAgLocalReadyOff) + q, 1u, false);
-        dev::fenceSys();
-        redAddRelease(ctrl(q, dev::kAgTakenOff) + me, 1u, true);
+        __threadfence();
+        const uint32_t old = atomicAdd(ctrl(me, dev::kAgLocalReadyOff) + q, 1u);
+        if (old + 1u == (k + 1u) * ctas) redAddRelease(ctrl(q, dev::kAgTakenOff) + me, 1u, true);
       }
     }
   }

@@ -77,7 +77,7 @@ struct NormArgs {
   float eps;
 };
 
-// LL variant.  Grid = kLLBlocks CTAs in clusters of 8; every CTA bumps its LL
+// LL variant.  Grid = the communicator's llBlocks CTAs in clusters of 8; every CTA bumps its LL
 // epoch once.  rows*hidden*2 <= kLLMaxBytes, hidden % (4*8) == 0.
 constexpr int kMaxWordsPerThread = 4;
 
@@ -308,7 +308,7 @@ extern "C" vcclResult_t vcclAllReduceAddRMSNorm(const void* partial, void* resid
     dev::addRmsNormLocal<<<grid, dev::kNormThreads, 0, s>>>(a);
   } else if (bytes <= comm->dev->llMaxBytes * 4 && bytes <= dev::kLLMaxBytes &&
              hidden / 4 / dev::kClusterCtas <= dev::kNormThreads * dev::kMaxWordsPerThread) {
-    dev::arRmsNormLL<<<dev::kLLBlocks, dev::kNormThreads, 0, s>>>(comm->dev->dc, a);
+    dev::arRmsNormLL<<<comm->dev->llBlocks, dev::kNormThreads, 0, s>>>(comm->dev->dc, a);
   } else {
     const size_t maxRows = (rows + n - 1) / n;
     const size_t slotRows = comm->dev->dc.dataBytes / (n + 2) / (hidden * 2);

@@ -71,6 +71,8 @@ struct EpiPushRS {
 struct RsHooks : gemm::NoHooks {
   DevComm c;
   uint32_t reduceBlocks;
+  // Every rank's reduction must have consumed the previous call's pushes
+  // (free[q] counts calls rank q has finished reducing).
   __device__ __forceinline__ bool beforeTiles(uint32_t*, volatile int* abortFlag) const {
     __shared__ int sFail;
     if (threadIdx.x == 64) {
@@ -78,17 +80,26 @@ struct RsHooks : gemm::NoHooks {
       const uint32_t k = dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsGemmCallsOff)[blockIdx.x];
       const uint32_t* freeCnt = dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsFreeOff);
       for (int q = 0; q < c.nranks; q++)
-        if (!dev::waitAtLeast(c, freeCnt + q, k * reduceBlocks, dev::kWhereFused, 100 + q)) sFail = 1;
+        if (!dev::waitAcquire(c, freeCnt + q, k, dev::kWhereFused, 100 + q)) sFail = 1;
     }
     epilogueBarrier();
     return sFail == 0 && !*abortFlag;
   }
+  // Each CTA makes its pushes visible system-wide and counts itself locally;
+  // the last CTA of the call tells every rank once (done[me] += 1).
   __device__ __forceinline__ void afterTiles(uint32_t*, volatile int*) const {
     epilogueBarrier();
     if (threadIdx.x == 64) {
+      uint32_t* calls = dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsGemmCallsOff) + blockIdx.x;
+      const uint32_t k = *calls;
       dev::fenceSys();
-      for (int q = 0; q < c.nranks; q++) redAddReleaseSys(dev::ctrlAt<uint32_t>(c, q, dev::kRsDoneOff) + c.rank, 1u);
-      dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsGemmCallsOff)[blockIdx.x] += 1u;
+      const uint32_t old = atomicAdd(dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsLocalDoneOff), 1u);
+      if (old + 1u == (k + 1u) * gridDim.x) {
+        dev::fenceSys();
+        for (int q = 0; q < c.nranks; q++)
+          redAddReleaseSys(dev::ctrlAt<uint32_t>(c, q, dev::kRsDoneOff) + c.rank, 1u);
+      }
+      *calls = k + 1u;
     }
   }
 };
@@ -105,10 +116,10 @@ __global__ void __launch_bounds__(512) rsReduce(DevComm c, char* out, size_t ele
   }
   __syncthreads();
   const uint32_t k = sK;
+  (void)gemmCtas;
   if (threadIdx.x < n) {
     const uint32_t* done = dev::ctrlAt<uint32_t>(c, me, dev::kRsDoneOff);
-    if (!dev::waitAtLeast(c, done + threadIdx.x, (k + 1u) * gemmCtas, dev::kWhereFused, 200 + threadIdx.x))
-      sFail = 1;
+    if (!dev::waitAcquire(c, done + threadIdx.x, k + 1u, dev::kWhereFused, 200 + threadIdx.x)) sFail = 1;
   }
   __syncthreads();
   if (sFail) return;
@@ -122,8 +133,12 @@ __global__ void __launch_bounds__(512) rsReduce(DevComm c, char* out, size_t ele
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    dev::fenceSys();
-    for (int q = 0; q < n; q++) redAddReleaseSys(dev::ctrlAt<uint32_t>(c, q, dev::kRsFreeOff) + me, 1u);
+    // Slot reads are done; the last block of the call frees the slots on
+    // every rank (free[me] += 1).
+    __threadfence();
+    const uint32_t old = atomicAdd(dev::ctrlAt<uint32_t>(c, me, dev::kRsLocalFreeOff), 1u);
+    if (old + 1u == (k + 1u) * gridDim.x)
+      for (int q = 0; q < n; q++) redAddReleaseSys(dev::ctrlAt<uint32_t>(c, q, dev::kRsFreeOff) + me, 1u);
     dev::ctrlAt<uint32_t>(c, me, dev::kRsReduceCallsOff)[blockIdx.x] = k + 1u;
   }
 }

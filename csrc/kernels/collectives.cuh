@@ -44,7 +44,7 @@ __device__ __forceinline__ void blockRange(size_t total, int parts, int idx, siz
 }
 
 // ---------------------------------------------------------------------------
-// LL one-shot all-reduce.  Grid is always kLLBlocks so every block's epoch
+// LL one-shot all-reduce.  Grid is always the communicator's llBlocks so every block's epoch
 // advances once per launch (epochs are equal across blocks and ranks).
 // send/recv must be 8-byte aligned and count*sizeof(T) <= kLLMaxBytes.
 // ---------------------------------------------------------------------------

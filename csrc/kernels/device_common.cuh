@@ -20,14 +20,15 @@ namespace dev {
 
 constexpr int kMaxRanks = 8;     // one NVSwitch domain of an HGX B200 board
 constexpr int kMaxBlocks = 128;  // largest grid of a barrier-based kernel
-constexpr int kLLBlocks = 64;    // fixed grid of the LL kernels
+constexpr int kLLBlocks = 64;    // default grid of the LL kernels (VCCL_LL_BLOCKS, <= kMaxLLBlocks)
+constexpr int kMaxLLBlocks = 256;
 constexpr int kMaxChannels = 8;  // point-to-point channels per peer
 constexpr int kP2pSlots = 4;     // ring depth of one channel
 
 // ---- ctrl allocation layout (byte offsets) ---------------------------------
 constexpr size_t kBarFlagsOff = 0;                                    // u32[kMaxBlocks][kMaxRanks], written by peers
 constexpr size_t kBarEpochOff = kBarFlagsOff + kMaxBlocks * kMaxRanks * 4;  // u32[kMaxBlocks], local
-constexpr size_t kLLEpochOff = kBarEpochOff + kMaxBlocks * 4;         // u32[kLLBlocks], local
+constexpr size_t kLLEpochOff = kBarEpochOff + kMaxBlocks * 4;         // u32[kMaxLLBlocks], local
 constexpr size_t kP2pHeadOff = 8192;                                  // u64[kMaxRanks][kMaxChannels], written by senders
 constexpr size_t kP2pTailOff = kP2pHeadOff + kMaxRanks * kMaxChannels * 8;  // written by receivers
 constexpr size_t kP2pSentOff = kP2pTailOff + kMaxRanks * kMaxChannels * 8;  // local
@@ -46,6 +47,9 @@ constexpr size_t kAgReadyOff = 69632;                       // u32[kMaxRanks]: p
 constexpr size_t kAgTakenOff = kAgReadyOff + 64;            // u32[kMaxRanks]: peer finished pulling my shard
 constexpr size_t kAgCallsOff = kAgReadyOff + 256;           // u32[kMaxFusedCtas], local
 constexpr size_t kAgLocalReadyOff = kAgCallsOff + 1024;     // u32[kMaxRanks], local: shard copied into full X
+constexpr size_t kAgStagedOff = kAgLocalReadyOff + 64;      // u32, local: CTAs that staged their slice
+constexpr size_t kRsLocalDoneOff = kRsReduceCallsOff + 256; // u32, local: GEMM CTAs done pushing
+constexpr size_t kRsLocalFreeOff = kRsLocalDoneOff + 4;     // u32, local: reduce blocks done
 constexpr size_t kMoeOff = 73728;                           // MoE dispatch/combine counters
 constexpr size_t kCtrlHeader = 1 << 20;
 

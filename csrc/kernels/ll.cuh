@@ -5,7 +5,7 @@
 // line match.  NVLink delivers each 8-byte half atomically, which is all
 // the protocol relies on.
 //
-// Every LL kernel runs with exactly kLLBlocks blocks and bumps each block's
+// Every LL kernel runs with the communicator's LL grid (llBlocks) and bumps each block's
 // epoch once, so epochs agree across blocks, ranks and kernel kinds.  A slot
 // of parity p is rewritten two LL launches later; that is safe because in
 // every LL launch each rank receives from every other rank, so finishing

@@ -225,6 +225,7 @@ LaunchCtx launchCtx(vcclComm_t comm, cudaStream_t s) {
   lc.nblocks = comm->dev->nblocks;
   lc.nvls = comm->dev->nvls;
   lc.llMax = comm->dev->llMaxBytes;
+  lc.llBlocks = comm->dev->llBlocks;
   return lc;
 }
 

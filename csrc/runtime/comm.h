@@ -54,6 +54,7 @@ struct DeviceState {
   dev::DevComm dc{};
   int nblocks = 32;                // grid of barrier-based kernels
   size_t llMaxBytes = 0;           // one-hop LL threshold (per-rank payload)
+  int llBlocks = 64;               // grid of every LL kernel, a multiple of 8
   size_t ll2MaxBytes = 0;          // two-hop LL all-reduce threshold
 };
 

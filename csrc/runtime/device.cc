@@ -238,6 +238,11 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
   ds->llMaxBytes = envBytes("VCCL_LL_MAX", llDefault);
   if (ds->llMaxBytes > dev::kLLMaxBytes) ds->llMaxBytes = dev::kLLMaxBytes;
   ds->ll2MaxBytes = envBytes("VCCL_LL2_MAX", 4u << 20);
+  // LL epochs are per block, so every rank must launch the same LL grid; the
+  // fused LL kernels run in clusters of 8, hence the multiple of 8.
+  long llb = envLong("VCCL_LL_BLOCKS", dev::kLLBlocks);
+  llb = llb < 8 ? 8 : llb > dev::kMaxLLBlocks ? dev::kMaxLLBlocks : llb;
+  ds->llBlocks = static_cast<int>(llb / 8 * 8);
 
   if (n > 1) {
     if (n > dev::kMaxRanks) {
@@ -270,13 +275,15 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
     dataBytes = roundUp(dataBytes, dataAlign);
     const size_t ctrlBytes = roundUp(dev::kCtrlBytes, gran);
     const size_t fusedBytes = roundUp(envBytes("VCCL_FUSED_BUFFSIZE", 512u << 20), gran);
-    struct Sizes { uint64_t ctrl, data, fused; } mine{ctrlBytes, dataBytes, fusedBytes};
+    struct Sizes { uint64_t ctrl, data, fused, llBlocks; } mine{ctrlBytes, dataBytes, fusedBytes,
+                                                                 static_cast<uint64_t>(ds->llBlocks)};
     std::vector<Sizes> all(n);
     all[me] = mine;
     VTRY(bs->allGather(all.data(), sizeof(Sizes)));
     for (const Sizes& s : all) {
-      if (s.ctrl != mine.ctrl || s.data != mine.data || s.fused != mine.fused) {
-        VERR("ranks disagree on workspace sizes (check VCCL_BUFFSIZE on every rank)");
+      if (s.ctrl != mine.ctrl || s.data != mine.data || s.fused != mine.fused || s.llBlocks != mine.llBlocks) {
+        VERR("ranks disagree on workspace sizes (check VCCL_BUFFSIZE, VCCL_FUSED_BUFFSIZE and VCCL_LL_BLOCKS "
+             "on every rank)");
         return vcclInvalidUsage;
       }
     }

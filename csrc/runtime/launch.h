@@ -19,6 +19,7 @@ struct LaunchCtx {
   int nblocks;     // max grid of barrier kernels
   bool nvls;
   size_t llMax;    // largest per-rank payload sent with the LL protocol
+  int llBlocks;    // grid of every LL kernel (fixed per communicator)
 };
 
 inline bool aligned8(const void* a, const void* b) {

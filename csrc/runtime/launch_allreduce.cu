@@ -34,7 +34,7 @@ cudaError_t launchAllReduce(const LaunchCtx& lc, ArAlgo algo, vcclDataType_t dt,
         ((reinterpret_cast<uintptr_t>(a.send) | reinterpret_cast<uintptr_t>(a.recv)) & 7u) != 0 || a.root >= 0)
       return cudaErrorInvalidValue;
     VCCL_DISPATCH_TYPE(dt, VCCL_DISPATCH_OP(redKind, {
-      dev::allReduceLL<T, K><<<dev::kLLBlocks, kThreads, 0, lc.stream>>>(lc.dc, a);
+      dev::allReduceLL<T, K><<<lc.llBlocks, kThreads, 0, lc.stream>>>(lc.dc, a);
     }))
     return cudaGetLastError();
   }
@@ -44,7 +44,7 @@ cudaError_t launchAllReduce(const LaunchCtx& lc, ArAlgo algo, vcclDataType_t dt,
         ((reinterpret_cast<uintptr_t>(a.send) | reinterpret_cast<uintptr_t>(a.recv)) & 7u) != 0 || a.root >= 0)
       return cudaErrorInvalidValue;
     VCCL_DISPATCH_TYPE(dt, VCCL_DISPATCH_OP(redKind, {
-      dev::allReduceLL2<T, K><<<dev::kLLBlocks, kThreads, 0, lc.stream>>>(lc.dc, a);
+      dev::allReduceLL2<T, K><<<lc.llBlocks, kThreads, 0, lc.stream>>>(lc.dc, a);
     }))
     return cudaGetLastError();
   }

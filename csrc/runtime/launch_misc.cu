@@ -24,7 +24,7 @@ cudaError_t launchReduceScatter(const LaunchCtx& lc, vcclDataType_t dt, int redK
   const size_t chunkBytes = a.count * esz;
   if (chunkBytes <= lc.llMax && chunkBytes % 8 == 0 && aligned8(a.send, a.recv)) {
     VCCL_DISPATCH_TYPE(dt, VCCL_DISPATCH_OP(redKind, {
-      dev::reduceScatterLL<T, K><<<dev::kLLBlocks, kThreads, 0, lc.stream>>>(lc.dc, a);
+      dev::reduceScatterLL<T, K><<<lc.llBlocks, kThreads, 0, lc.stream>>>(lc.dc, a);
     }))
     return cudaGetLastError();
   }
@@ -45,7 +45,7 @@ cudaError_t launchReduceScatter(const LaunchCtx& lc, vcclDataType_t dt, int redK
 
 cudaError_t launchAllGather(const LaunchCtx& lc, const void* send, void* recv, size_t bytes) {
   if (bytes <= lc.llMax && bytes % 8 == 0 && aligned8(send, recv)) {
-    dev::allGatherLL<<<dev::kLLBlocks, kThreads, 0, lc.stream>>>(lc.dc, static_cast<const char*>(send),
+    dev::allGatherLL<<<lc.llBlocks, kThreads, 0, lc.stream>>>(lc.dc, static_cast<const char*>(send),
                                                                   static_cast<char*>(recv), bytes);
     return cudaGetLastError();
   }
@@ -58,7 +58,7 @@ cudaError_t launchAllGather(const LaunchCtx& lc, const void* send, void* recv, s
 cudaError_t launchBroadcast(const LaunchCtx& lc, const void* send, void* recv, size_t bytes, int root,
                             bool useNvls) {
   if (bytes <= lc.llMax && bytes % 8 == 0 && aligned8(send, recv)) {
-    dev::broadcastLL<<<dev::kLLBlocks, kThreads, 0, lc.stream>>>(lc.dc, static_cast<const char*>(send),
+    dev::broadcastLL<<<lc.llBlocks, kThreads, 0, lc.stream>>>(lc.dc, static_cast<const char*>(send),
                                                                   static_cast<char*>(recv), bytes, root);
     return cudaGetLastError();
   }
