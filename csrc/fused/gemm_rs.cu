@@ -9,11 +9,13 @@
 // overlaps the tensor-core work on later ones.  A short local kernel then
 // sums the n slots of the rows this rank owns.
 //
-// Synchronisation is device-side and CUDA-graph safe: every GEMM CTA (the
-// grid is always one CTA per SM) bumps a "done" counter on every rank after
-// its stores; the reduction waits for n x CTAs of this call; after reducing,
-// every reduction block bumps a "free" counter on every rank, which the next
-// call's GEMM waits for before storing into that rank's slots.
+// Synchronisation is device-side and CUDA-graph safe and costs a constant
+// number of system-scope operations per call: every GEMM CTA (the grid is
+// always one CTA per SM) counts itself on a local counter after its
+// stores, and the last one bumps done[me] on every rank once; the
+// reduction waits for done[p] of this call from every source; its last
+// block bumps free[me] on every rank, which the next call's GEMM waits for
+// before storing into that rank's slots.
 #include <cuda_runtime.h>
 
 #include "common/log.h"
@@ -32,21 +34,8 @@ __device__ __forceinline__ void redAddReleaseSys(uint32_t* p, uint32_t v) {
 }
 __device__ __forceinline__ void epilogueBarrier() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-// Store a 16-column chunk of one accumulator row as bf16 to `dst`.
-__device__ __forceinline__ void storeRow16(char* dst, const uint32_t (&r)[16]) {
-  uint4 o0, o1;
-  o0.x = gemm::packBf16(__uint_as_float(r[0]), __uint_as_float(r[1]));
-  o0.y = gemm::packBf16(__uint_as_float(r[2]), __uint_as_float(r[3]));
-  o0.z = gemm::packBf16(__uint_as_float(r[4]), __uint_as_float(r[5]));
-  o0.w = gemm::packBf16(__uint_as_float(r[6]), __uint_as_float(r[7]));
-  o1.x = gemm::packBf16(__uint_as_float(r[8]), __uint_as_float(r[9]));
-  o1.y = gemm::packBf16(__uint_as_float(r[10]), __uint_as_float(r[11]));
-  o1.z = gemm::packBf16(__uint_as_float(r[12]), __uint_as_float(r[13]));
-  o1.w = gemm::packBf16(__uint_as_float(r[14]), __uint_as_float(r[15]));
-  reinterpret_cast<uint4*>(dst)[0] = o0;
-  reinterpret_cast<uint4*>(dst)[1] = o1;
-}
-
+// Each tile row goes to its owner's slot; rows leave the SM as contiguous
+// 128-byte segments (see gemm::storeAccRows).
 struct EpiPushRS {
   char* dest[dev::kMaxRanks];  // owner q's slot for this source rank
   int rowsPerRank;
@@ -54,17 +43,11 @@ struct EpiPushRS {
   template <int BN>
   __device__ __forceinline__ void operator()(uint32_t tmemAcc, const gemm::TileInfo& ti, const gemm::GemmShape& s,
                                              int laneRow) const {
-    const int row = ti.row0 + laneRow;
-    const int owner = row < s.M ? row / rowsPerRank : 0;
-    char* base = dest[owner] + static_cast<size_t>(row - owner * rowsPerRank) * ldn * 2;
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      uint32_t r[16];
-      sm100::tmemLoad16(tmemAcc + c, r);
-      sm100::tmemLoadWait();
-      const int col = ti.col0 + c;
-      if (row < s.M && col < s.N) storeRow16(base + static_cast<size_t>(col) * 2, r);
-    }
+    const size_t pitch = static_cast<size_t>(ldn) * 2;
+    gemm::storeAccRows<BN>(tmemAcc, ti, s, laneRow, [&](int row) {
+      const int owner = row / rowsPerRank;
+      return dest[owner] + static_cast<size_t>(row - owner * rowsPerRank) * pitch;
+    });
   }
 };
 

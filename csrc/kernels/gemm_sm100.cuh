@@ -57,6 +57,75 @@ __device__ __forceinline__ uint32_t packBf16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// ---- epilogue output path ------------------------------------------------------
+// tcgen05.ld leaves one tile row per thread, so storing straight from
+// registers makes every warp store instruction touch 32 different rows.
+// Over NVLink that becomes 32 small write packets.  Instead each epilogue
+// warp stages a 32-row x (NC x 16 B) slice in shared memory and writes it
+// back row-contiguously: NC lanes per row, 32/NC rows per instruction, so a
+// row segment of up to 128 B leaves as one request.  Chunks are XOR-swizzled
+// by row so both the row-per-thread writes and the row-contiguous reads are
+// free of bank conflicts.
+__device__ __forceinline__ uint4* warpStage() {
+  __shared__ __align__(128) uint4 stageBuf[4][32 * 8];  // 4 KB per epilogue warp
+  return stageBuf[(threadIdx.x >> 5) & 3];
+}
+
+template <int NC>
+__device__ __forceinline__ void stagePut(uint4* st, int lane, int j, uint4 v) {
+  st[lane * NC + (j ^ (lane & (NC - 1)))] = v;
+}
+
+// dst(rowInWarp, chunk, value) is called for every staged 16-byte chunk.
+template <int NC, typename Dst>
+__device__ __forceinline__ void stageFlush(const uint4* st, int lane, Dst&& dst) {
+  __syncwarp();
+  constexpr int kRows = 32 / NC;
+#pragma unroll
+  for (int i = 0; i < NC; i++) {
+    const int rr = i * kRows + lane / NC;
+    const int ch = lane % NC;
+    dst(rr, ch, st[rr * NC + (ch ^ (rr & (NC - 1)))]);
+  }
+  __syncwarp();
+}
+
+__device__ __forceinline__ uint4 packChunk(const uint32_t* r) {
+  uint4 o;
+  o.x = packBf16(__uint_as_float(r[0]), __uint_as_float(r[1]));
+  o.y = packBf16(__uint_as_float(r[2]), __uint_as_float(r[3]));
+  o.z = packBf16(__uint_as_float(r[4]), __uint_as_float(r[5]));
+  o.w = packBf16(__uint_as_float(r[6]), __uint_as_float(r[7]));
+  return o;
+}
+
+// Write the tile's accumulator as bf16 through the row stage.  rowBase(row)
+// returns the byte address of column 0 of `row` (any memory this GPU can
+// store to).  Columns are checked per 8-element chunk (N % 8 == 0).
+template <int BN, typename RowBase>
+__device__ __forceinline__ void storeAccRows(uint32_t tmemAcc, const TileInfo& ti, const GemmShape& s, int laneRow,
+                                             RowBase&& rowBase) {
+  constexpr int CW = BN < 64 ? BN : 64;  // accumulator columns per pass
+  constexpr int NC = CW / 8;             // 16-byte chunks per row per pass
+  uint4* st = warpStage();
+  const int lane = laneRow & 31;
+  const int warpRow0 = ti.row0 + (laneRow & ~31);
+#pragma unroll 1
+  for (int c = 0; c < BN; c += CW) {
+    uint32_t r[CW];
+#pragma unroll
+    for (int i = 0; i < CW / 16; i++) sm100::tmemLoad16p(tmemAcc + c + 16 * i, r + 16 * i);
+    sm100::tmemLoadWait();
+#pragma unroll
+    for (int j = 0; j < NC; j++) stagePut<NC>(st, lane, j, packChunk(r + 8 * j));
+    const int col0 = ti.col0 + c;
+    stageFlush<NC>(st, lane, [&](int rr, int ch, uint4 v) {
+      const int row = warpRow0 + rr, col = col0 + ch * 8;
+      if (row < s.M && col < s.N) *reinterpret_cast<uint4*>(rowBase(row) + static_cast<size_t>(col) * 2) = v;
+    });
+  }
+}
+
 // Plain store of the accumulator to C (row-major, ldc elements).
 struct EpiStore {
   __nv_bfloat16* C;
@@ -64,28 +133,9 @@ struct EpiStore {
   template <int BN>
   __device__ __forceinline__ void operator()(uint32_t tmemAcc, const TileInfo& ti, const GemmShape& s,
                                              int laneRow) const {
-    const int row = ti.row0 + laneRow;
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      uint32_t r[16];
-      sm100::tmemLoad16(tmemAcc + c, r);
-      sm100::tmemLoadWait();
-      const int col = ti.col0 + c;
-      if (row < s.M && col < s.N) {
-        uint4 o0, o1;
-        o0.x = packBf16(__uint_as_float(r[0]), __uint_as_float(r[1]));
-        o0.y = packBf16(__uint_as_float(r[2]), __uint_as_float(r[3]));
-        o0.z = packBf16(__uint_as_float(r[4]), __uint_as_float(r[5]));
-        o0.w = packBf16(__uint_as_float(r[6]), __uint_as_float(r[7]));
-        o1.x = packBf16(__uint_as_float(r[8]), __uint_as_float(r[9]));
-        o1.y = packBf16(__uint_as_float(r[10]), __uint_as_float(r[11]));
-        o1.z = packBf16(__uint_as_float(r[12]), __uint_as_float(r[13]));
-        o1.w = packBf16(__uint_as_float(r[14]), __uint_as_float(r[15]));
-        uint4* dst = reinterpret_cast<uint4*>(C + static_cast<size_t>(row) * ldc + col);
-        dst[0] = o0;
-        dst[1] = o1;
-      }
-    }
+    char* base = reinterpret_cast<char*>(C);
+    const size_t pitch = static_cast<size_t>(ldc) * 2;
+    storeAccRows<BN>(tmemAcc, ti, s, laneRow, [&](int row) { return base + row * pitch; });
   }
 };
 
@@ -99,34 +149,36 @@ struct EpiSiluMul {
   template <int BN>
   __device__ __forceinline__ void operator()(uint32_t tmemAcc, const TileInfo& ti, const GemmShape& s,
                                              int laneRow) const {
-    const int row = ti.row0 + laneRow;
+    constexpr int CW = BN < 128 ? BN : 128;  // accumulator columns per pass
+    constexpr int NC = CW / 16;              // 16-byte output chunks per row per pass
+    uint4* st = warpStage();
+    const int lane = laneRow & 31;
+    const int warpRow0 = ti.row0 + (laneRow & ~31);
+    char* base = reinterpret_cast<char*>(C);
+    const size_t pitch = static_cast<size_t>(ldc) * 2;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      uint32_t g[16], u[16];
-      sm100::tmemLoad16(tmemAcc + c, g);
-      sm100::tmemLoad16(tmemAcc + c + 16, u);
-      sm100::tmemLoadWait();
-      const int col = (ti.col0 + c) / 2;
-      if (row < s.M && col < s.N / 2) {
-        float o[16];
+    for (int c = 0; c < BN; c += CW) {
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-          const float x = __uint_as_float(g[i]);
-          o[i] = x / (1.0f + __expf(-x)) * __uint_as_float(u[i]);
+      for (int j = 0; j < CW / 32; j++) {
+        uint32_t g[16], u[16];
+        sm100::tmemLoad16(tmemAcc + c + 32 * j, g);
+        sm100::tmemLoad16(tmemAcc + c + 32 * j + 16, u);
+        sm100::tmemLoadWait();
+        uint32_t o[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const float x0 = __uint_as_float(g[2 * i]), x1 = __uint_as_float(g[2 * i + 1]);
+          o[i] = packBf16(x0 / (1.0f + __expf(-x0)) * __uint_as_float(u[2 * i]),
+                          x1 / (1.0f + __expf(-x1)) * __uint_as_float(u[2 * i + 1]));
         }
-        uint4 o0, o1;
-        o0.x = packBf16(o[0], o[1]);
-        o0.y = packBf16(o[2], o[3]);
-        o0.z = packBf16(o[4], o[5]);
-        o0.w = packBf16(o[6], o[7]);
-        o1.x = packBf16(o[8], o[9]);
-        o1.y = packBf16(o[10], o[11]);
-        o1.z = packBf16(o[12], o[13]);
-        o1.w = packBf16(o[14], o[15]);
-        uint4* dst = reinterpret_cast<uint4*>(C + static_cast<size_t>(row) * ldc + col);
-        dst[0] = o0;
-        dst[1] = o1;
+        stagePut<NC>(st, lane, 2 * j, make_uint4(o[0], o[1], o[2], o[3]));
+        stagePut<NC>(st, lane, 2 * j + 1, make_uint4(o[4], o[5], o[6], o[7]));
       }
+      const int col0 = (ti.col0 + c) / 2;
+      stageFlush<NC>(st, lane, [&](int rr, int ch, uint4 v) {
+        const int row = warpRow0 + rr, col = col0 + ch * 8;
+        if (row < s.M && col < s.N / 2) *reinterpret_cast<uint4*>(base + row * pitch + static_cast<size_t>(col) * 2) = v;
+      });
     }
   }
 };
