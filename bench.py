@@ -101,11 +101,11 @@ def run_vccl(args) -> int:
     def shard(tokens):
         return torch.randn(tokens // world, HIDDEN, device="cuda", generator=gen).bfloat16()
 
-    def measure(fn, steps, warmup):
+    def measure(fn, steps, warmup, align_ranks=False):
         for _ in range(warmup):
             fn()
         torch.cuda.synchronize()
-        times = time_steps(fn, steps, flush)
+        times = time_steps(fn, steps, flush, align_ranks)
         return max_over_ranks(sum(times) / len(times))
 
     # numerics: fused path vs NCCL + cuBLAS on the headline shape
@@ -195,7 +195,12 @@ def run_vccl(args) -> int:
 
 
 def breakdown(mlp, x, world, measure):
-    """Each fused kernel alone, next to the same GEMM with no communication."""
+    """Each fused kernel alone, next to the same GEMM with no communication.
+
+    Every step starts with the ranks aligned (device sync + barrier outside
+    the timed region), as inside the layer where each fused kernel follows
+    one that synchronised the ranks.
+    """
     import torch
 
     from vkccl_b200.ops.fused import all_gather_gemm, gemm_reduce_scatter
@@ -205,10 +210,11 @@ def breakdown(mlp, x, world, measure):
     xfull = torch.randn(rows, x.shape[1], device="cuda").bfloat16()
     h = torch.empty((rows, mlp.inter_shard), dtype=torch.bfloat16, device="cuda")
     out = {
-        "ag_gemm_silu": measure(lambda: all_gather_gemm(mlp.comm, x, mlp.w_gate_up, silu_mul=True, out=h), 10, 3),
-        "gemm_silu_local": measure(lambda: gemm_silu_mul(xfull, mlp.w_gate_up, out=h), 10, 3),
-        "gemm_rs": measure(lambda: gemm_reduce_scatter(mlp.comm, h, mlp.w_down), 10, 3),
-        "gemm_local": measure(lambda: gemm_bf16(h, mlp.w_down), 10, 3),
+        "ag_gemm_silu": measure(lambda: all_gather_gemm(mlp.comm, x, mlp.w_gate_up, silu_mul=True, out=h), 10, 3,
+                                True),
+        "gemm_silu_local": measure(lambda: gemm_silu_mul(xfull, mlp.w_gate_up, out=h), 10, 3, True),
+        "gemm_rs": measure(lambda: gemm_reduce_scatter(mlp.comm, h, mlp.w_down), 10, 3, True),
+        "gemm_local": measure(lambda: gemm_bf16(h, mlp.w_down), 10, 3, True),
     }
     return {k: round(v, 2) for k, v in out.items()}
 

@@ -82,6 +82,9 @@ struct AgHooks : gemm::NoHooks {
     ti.tm = (g * groupRows + local % rowsHere + startTm) % s.tilesM;
     ti.row0 = ti.tm * gemm::kBM;
     ti.col0 = ti.tn * BN;
+    ti.ks = 0;
+    ti.kb0 = 0;
+    ti.kb1 = s.numK();
     return ti;
   }
   __device__ __forceinline__ bool beforeLoad(const gemm::TileInfo& ti, const gemm::GemmShape& s, uint32_t* hs,
@@ -93,13 +96,13 @@ struct AgHooks : gemm::NoHooks {
       // remote shard q: every CTA pulled its slice (local counter).
       const bool own = q == c.rank;
       const uint32_t* flag = own ? ctrl(c.rank, dev::kAgReadyOff) + q : ctrl(c.rank, dev::kAgLocalReadyOff) + q;
-      if (!dev::waitAcquire(c, flag, own ? k + 1u : (k + 1u) * ctas, dev::kWhereFused, 300 + q)) return false;
+      if (!dev::waitAcquire(c, flag, own ? k + 1u : (k + 1u) * ctas, dev::kWhereFused, 300 + q, 64)) return false;
     }
     fenceProxyAsync();
     return true;
   }
   __device__ __forceinline__ void extraRole(uint32_t* hs, volatile int* abortFlag) const {
-    const int tid = threadIdx.x - gemm::kBaseThreads;  // 0..63
+    const int tid = threadIdx.x - gemm::baseThreads<AgHooks>();  // 0..63
     const int n = c.nranks, me = c.rank;
     const uint32_t k = hs[0];
     const size_t rowBytes = static_cast<size_t>(K) * 2;
@@ -114,7 +117,7 @@ struct AgHooks : gemm::NoHooks {
     if (tid == 0) {
       sFail = 0;
       for (int p = 0; p < n; p++)
-        if (p != me && !dev::waitAcquire(c, ctrl(me, dev::kAgTakenOff) + p, k, dev::kWhereFused, 400 + p))
+        if (p != me && !dev::waitAcquire(c, ctrl(me, dev::kAgTakenOff) + p, k, dev::kWhereFused, 400 + p, 64))
           sFail = 1;
     }
     copyWarpsBarrier();
@@ -139,7 +142,7 @@ struct AgHooks : gemm::NoHooks {
     //    tells its owner it may be overwritten
     for (int s = 1; s < n; s++) {
       const int q = (me + s) % n;
-      if (tid == 0 && !dev::waitAcquire(c, ctrl(me, dev::kAgReadyOff) + q, k + 1u, dev::kWhereFused, 500 + q))
+      if (tid == 0 && !dev::waitAcquire(c, ctrl(me, dev::kAgReadyOff) + q, k + 1u, dev::kWhereFused, 500 + q, 64))
         sFail = 1;
       copyWarpsBarrier();
       if (sFail || *abortFlag) {

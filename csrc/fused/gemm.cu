@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "common/log.h"
@@ -53,14 +54,62 @@ int pickBN(int M, int N) {
   return 32;
 }
 
+SplitPlan planSplitK(int M, int N, int K) {
+  const int sms = smCount();
+  const int tilesM = (M + kBM - 1) / kBM;
+  const int numK = (K + kBK - 1) / kBK;
+  const int tiles = tilesM * ((N + 127) / 128);
+  if (tilesM > 2 || tiles * 2 > sms) return {0, 1};
+  int splits = sms / tiles;
+  if (splits > numK / 4) splits = numK / 4;  // at least 4 k-blocks per split
+  if (splits > 16) splits = 16;
+  if (splits < 2) return {0, 1};
+  return {128, splits};
+}
+
+namespace {
+__global__ void __launch_bounds__(256) splitReduceKernel(const float4* ws, int splits, size_t n4, size_t stride4,
+                                                         uint2* out) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    float4 a = ws[i];
+    for (int sp = 1; sp < splits; sp++) {
+      const float4 b = ws[sp * stride4 + i];
+      a.x += b.x;
+      a.y += b.y;
+      a.z += b.z;
+      a.w += b.w;
+    }
+    out[i] = make_uint2(packBf16(a.x, a.y), packBf16(a.z, a.w));
+  }
+}
+}  // namespace
+
+cudaError_t launchSplitReduce(const float* ws, int splits, size_t elems, void* out, cudaStream_t st) {
+  const size_t n4 = elems / 4;
+  size_t blocks = (n4 + 255) / 256;
+  if (blocks > static_cast<size_t>(smCount()) * 4) blocks = static_cast<size_t>(smCount()) * 4;
+  if (blocks == 0) blocks = 1;
+  splitReduceKernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(reinterpret_cast<const float4*>(ws), splits, n4,
+                                                                   n4, static_cast<uint2*>(out));
+  return cudaGetLastError();
+}
+
+// One abort flag per device (kernels only ever write their own device's).
 int* errorFlag() {
-  static int* p = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaMalloc(&p, sizeof(int) * 64);
+  static std::mutex mu;
+  static int* flags[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 63;
+  std::lock_guard<std::mutex> lock(mu);
+  if (flags[dev] == nullptr) {
+    int* p = nullptr;
+    if (cudaMalloc(&p, sizeof(int) * 64) != cudaSuccess) return nullptr;
     cudaMemset(p, 0, sizeof(int) * 64);
-  });
-  return p;
+    flags[dev] = p;
+  }
+  return flags[dev];
 }
 
 }  // namespace gemm
@@ -72,9 +121,32 @@ extern "C" {
 
 vcclResult_t vcclGemmBf16(const void* A, const void* W, void* C, int M, int N, int K, vcclStream_t stream) {
   if (!A || !W || !C || M <= 0 || N <= 0 || K <= 0 || (N % 16) != 0 || (K % 8) != 0) return vcclInvalidArgument;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int bnEnv = static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN"));
+  const char* sk = std::getenv("VCCL_GEMM_SPLITK");
+  const gemm::SplitPlan plan = (bnEnv > 0 || (sk && sk[0] == '0')) ? gemm::SplitPlan{0, 1} : gemm::planSplitK(M, N, K);
+  if (plan.splits > 1) {
+    // Decode shapes: split K across more CTAs; fp32 partials live in a
+    // stream-ordered scratch buffer for the duration of the call.
+    const size_t elems = static_cast<size_t>(M) * N;
+    float* ws = nullptr;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws), elems * plan.splits * sizeof(float), st);
+    if (e != cudaSuccess) {
+      VERR("vcclGemmBf16 split-K scratch: %s", cudaGetErrorString(e));
+      return vcclSystemError;
+    }
+    gemm::EpiPartialF32 epi{ws, N, elems};
+    e = gemm::launchGemm(A, W, M, N, K, epi, gemm::NoHooks{}, st, plan.bn, 0, plan.splits);
+    if (e == cudaSuccess) e = gemm::launchSplitReduce(ws, plan.splits, elems, C, st);
+    cudaFreeAsync(ws, st);
+    if (e != cudaSuccess) {
+      VERR("vcclGemmBf16 (split-K %d): %s", plan.splits, cudaGetErrorString(e));
+      return vcclInvalidArgument;
+    }
+    return vcclSuccess;
+  }
   gemm::EpiStore epi{static_cast<__nv_bfloat16*>(C), N};
-  cudaError_t e = gemm::launchGemm(A, W, M, N, K, epi, gemm::NoHooks{}, reinterpret_cast<cudaStream_t>(stream),
-                                   static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN")), 0);
+  cudaError_t e = gemm::launchGemm(A, W, M, N, K, epi, gemm::NoHooks{}, st, bnEnv, 0);
   if (e != cudaSuccess) {
     VERR("vcclGemmBf16: %s", cudaGetErrorString(e));
     return vcclInvalidArgument;

@@ -16,6 +16,18 @@ int smCount();
 int pickBN(int M, int N);
 int* errorFlag();
 
+// Split-K plan for GEMMs with too few output tiles to fill the GPU (decode
+// shapes): 128-wide tiles, K split so tiles x splits approaches one wave.
+// splits == 1 means no split.
+struct SplitPlan {
+  int bn;
+  int splits;
+};
+SplitPlan planSplitK(int M, int N, int K);
+
+// out[i] = bf16(sum over s < splits of ws[s * elems + i]); elems % 4 == 0.
+cudaError_t launchSplitReduce(const float* ws, int splits, size_t elems, void* out, cudaStream_t st);
+
 inline long envLongGemm(const char* name) {
   const char* v = std::getenv(name);
   return v ? std::strtol(v, nullptr, 10) : 0;

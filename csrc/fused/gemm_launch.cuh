@@ -14,8 +14,8 @@ namespace gemm {
 
 template <int BN, int STAGES, typename Epi, typename Hooks>
 cudaError_t launchT(const CUtensorMap& ma, const CUtensorMap& mb, const GemmShape& s, const Epi& epi,
-                    const Hooks& hooks, int grid, cudaStream_t st) {
-  using L = Smem<BN, STAGES>;
+                    const Hooks& hooks, int grid, cudaStream_t st, int* flag) {
+  using L = Smem<BN, STAGES, 4 * Hooks::kEpiGroups>;
   auto kern = gemmKernel<BN, STAGES, Epi, Hooks>;
   static unsigned long long attrDone = 0;  // one bit per device
   int dev = 0;
@@ -25,15 +25,18 @@ cudaError_t launchT(const CUtensorMap& ma, const CUtensorMap& mb, const GemmShap
     if (e != cudaSuccess) return e;
     attrDone |= 1ull << (dev & 63);
   }
-  kern<<<grid, kBaseThreads + 32 * Hooks::kExtraWarps, L::kBytes, st>>>(ma, mb, s, epi, hooks, errorFlag());
+  kern<<<grid, ctaThreads<Hooks>(), L::kBytes, st>>>(ma, mb, s, epi, hooks, flag);
   return cudaGetLastError();
 }
 
 // gridCap > 0: at most that many CTAs; gridCap < 0: exactly -gridCap CTAs
 // (fused kernels count on a fixed grid); 0: one CTA per SM at most.
+// splits > 1 runs split-K (only with NoHooks tile order and EpiPartialF32).
+// flag: device word the kernel sets if it abandons its work (nullptr: the
+// per-device flag of errorFlag()).
 template <typename Epi, typename Hooks>
 cudaError_t launchGemm(const void* A, const void* B, int M, int N, int K, const Epi& epi, const Hooks& hooks,
-                       cudaStream_t st, int bnOverride, int gridCap) {
+                       cudaStream_t st, int bnOverride, int gridCap, int splits = 1, int* flag = nullptr) {
   const int bn = bnOverride > 0 ? bnOverride : pickBN(M, N);
   CUtensorMap ma, mb;
   if (!makeMapKMajor(&ma, A, M, K, kBM) || !makeMapKMajor(&mb, B, N, K, bn)) return cudaErrorInvalidValue;
@@ -43,18 +46,21 @@ cudaError_t launchGemm(const void* A, const void* B, int M, int N, int K, const 
   s.K = K;
   s.tilesM = (M + kBM - 1) / kBM;
   s.tilesN = (N + bn - 1) / bn;
-  int grid = s.tilesM * s.tilesN;
+  s.splits = splits < 1 ? 1 : splits;
+  if (s.splits > s.numK()) return cudaErrorInvalidValue;
+  int grid = s.tilesM * s.tilesN * s.splits;
   if (gridCap < 0) {
     grid = -gridCap;
   } else {
     const int cap = gridCap > 0 ? gridCap : smCount();
     if (grid > cap) grid = cap;
   }
+  if (flag == nullptr) flag = errorFlag();
   switch (bn) {
-    case 256: return launchT<256, 4>(ma, mb, s, epi, hooks, grid, st);
-    case 128: return launchT<128, 6>(ma, mb, s, epi, hooks, grid, st);
-    case 64: return launchT<64, 8>(ma, mb, s, epi, hooks, grid, st);
-    default: return launchT<32, 8>(ma, mb, s, epi, hooks, grid, st);
+    case 256: return launchT<256, 4>(ma, mb, s, epi, hooks, grid, st, flag);
+    case 128: return launchT<128, 6>(ma, mb, s, epi, hooks, grid, st, flag);
+    case 64: return launchT<64, 8>(ma, mb, s, epi, hooks, grid, st, flag);
+    default: return launchT<32, 8>(ma, mb, s, epi, hooks, grid, st, flag);
   }
 }
 

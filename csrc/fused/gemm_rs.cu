@@ -32,7 +32,13 @@ using dev::DevComm;
 __device__ __forceinline__ void redAddReleaseSys(uint32_t* p, uint32_t v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ void epilogueBarrier() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Two epilogue warpgroups (8 warps) share each tile: the pushes over NVLink
+// are what bounds this kernel, so twice the threads keep twice the stores in
+// flight.
+constexpr int kRsEpiGroups = 2;
+__device__ __forceinline__ void epilogueBarrier() {
+  asm volatile("bar.sync 1, %0;" ::"n"(128 * kRsEpiGroups) : "memory");
+}
 
 // Each tile row goes to its owner's slot; rows leave the SM as contiguous
 // 128-byte segments (see gemm::storeAccRows).
@@ -40,11 +46,11 @@ struct EpiPushRS {
   char* dest[dev::kMaxRanks];  // owner q's slot for this source rank
   int rowsPerRank;
   int ldn;  // N
-  template <int BN>
+  template <int SPAN>
   __device__ __forceinline__ void operator()(uint32_t tmemAcc, const gemm::TileInfo& ti, const gemm::GemmShape& s,
-                                             int laneRow) const {
+                                             int laneRow, int cBegin, uint4* st) const {
     const size_t pitch = static_cast<size_t>(ldn) * 2;
-    gemm::storeAccRows<BN>(tmemAcc, ti, s, laneRow, [&](int row) {
+    gemm::storeAccRows<SPAN>(tmemAcc, ti, s, laneRow, cBegin, st, [&](int row) {
       const int owner = row / rowsPerRank;
       return dest[owner] + static_cast<size_t>(row - owner * rowsPerRank) * pitch;
     });
@@ -52,6 +58,7 @@ struct EpiPushRS {
 };
 
 struct RsHooks : gemm::NoHooks {
+  static constexpr int kEpiGroups = kRsEpiGroups;
   DevComm c;
   uint32_t reduceBlocks;
   // Every rank's reduction must have consumed the previous call's pushes
@@ -63,7 +70,7 @@ struct RsHooks : gemm::NoHooks {
       const uint32_t k = dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsGemmCallsOff)[blockIdx.x];
       const uint32_t* freeCnt = dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsFreeOff);
       for (int q = 0; q < c.nranks; q++)
-        if (!dev::waitAcquire(c, freeCnt + q, k, dev::kWhereFused, 100 + q)) sFail = 1;
+        if (!dev::waitAcquire(c, freeCnt + q, k, dev::kWhereFused, 100 + q, 64)) sFail = 1;
     }
     epilogueBarrier();
     return sFail == 0 && !*abortFlag;
@@ -102,7 +109,7 @@ __global__ void __launch_bounds__(512) rsReduce(DevComm c, char* out, size_t ele
   (void)gemmCtas;
   if (threadIdx.x < n) {
     const uint32_t* done = dev::ctrlAt<uint32_t>(c, me, dev::kRsDoneOff);
-    if (!dev::waitAcquire(c, done + threadIdx.x, k + 1u, dev::kWhereFused, 200 + threadIdx.x)) sFail = 1;
+    if (!dev::waitAcquire(c, done + threadIdx.x, k + 1u, dev::kWhereFused, 200 + threadIdx.x, 32)) sFail = 1;
   }
   __syncthreads();
   if (sFail) return;

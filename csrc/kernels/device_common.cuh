@@ -155,14 +155,26 @@ __device__ __forceinline__ bool waitAtLeast(const DevComm& c, const uint32_t* fl
 __device__ __forceinline__ void stReleaseSys32(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// Spin with acquire loads until *flag - target >= 0.  False on timeout/abort.
+// Spin until *flag - target >= 0, then acquire.  The spin polls with
+// relaxed loads and the final check is one acquire load: the flags are
+// monotonic counters bumped by release RMWs, so the acquire load reads a
+// value of the same release sequence and synchronises with its writer.
+// Acquire loads in the spin itself were measured to disturb the memory
+// system when hundreds of threads of a persistent kernel wait at once.
+// backoffNs > 0 sleeps between polls after the first few hundred (for
+// waits that are expected to be long, e.g. a GEMM waiting for remote data).
+// False on timeout/abort.
 __device__ __forceinline__ bool waitAcquire(const DevComm& c, const uint32_t* flag, uint32_t target, uint32_t where,
-                                            uint32_t detail) {
+                                            uint32_t detail, uint32_t backoffNs = 0) {
   if (static_cast<int32_t>(ldAcquireSys(flag) - target) >= 0) return true;
   const uint64_t start = globalTimerNs();
   for (uint32_t spin = 1;; ++spin) {
-    if (static_cast<int32_t>(ldAcquireSys(flag) - target) >= 0) return true;
+    if (static_cast<int32_t>(ldRelaxedSys(flag) - target) >= 0) {
+      (void)ldAcquireSys(flag);
+      return true;
+    }
     if ((spin & 255u) == 0u && shouldGiveUp(c, start, where, detail)) return false;
+    if (backoffNs != 0u && spin > 256u) __nanosleep(backoffNs);
   }
 }
 

@@ -31,25 +31,42 @@ namespace gemm {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // one 128-byte swizzle atom of bf16
-constexpr int kBaseThreads = 192;
+// Threads of a CTA before the policy's extra warps: producer, MMA issuer and
+// 4 x kEpiGroups epilogue warps.
+template <typename Hooks>
+__host__ __device__ constexpr int baseThreads() {
+  return 64 + 128 * Hooks::kEpiGroups;
+}
+template <typename Hooks>
+__host__ __device__ constexpr int ctaThreads() {
+  return baseThreads<Hooks>() + 32 * Hooks::kExtraWarps;
+}
 
-template <int BN, int STAGES>
+constexpr int kWarpStageBytes = 32 * 8 * 16;  // epilogue row stage: 32 rows x 128 B per warp
+
+template <int BN, int STAGES, int EPI_WARPS = 4>
 struct Smem {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarOff = STAGES * kStageBytes;
+  static constexpr int kRowStageOff = STAGES * kStageBytes;
+  static constexpr int kBarOff = kRowStageOff + EPI_WARPS * kWarpStageBytes;
   static constexpr int kBytes = kBarOff + 256 + 1024;  // + barriers + alignment slack
+  static_assert(kBytes <= 232448, "shared memory budget of one CTA");
 };
 
 struct TileInfo {
-  int tm, tn;  // tile coordinates
+  int tm, tn;    // tile coordinates
   int row0, col0;
+  int ks;        // K split of this tile (0 without split-K)
+  int kb0, kb1;  // k-blocks [kb0, kb1) accumulated into this tile
 };
 
 struct GemmShape {
   int M, N, K;
   int tilesM, tilesN;
+  int splits;  // K splits (1: every tile covers all of K)
+  __host__ __device__ int numK() const { return (K + kBK - 1) / kBK; }
 };
 
 __device__ __forceinline__ uint32_t packBf16(float a, float b) {
@@ -66,11 +83,6 @@ __device__ __forceinline__ uint32_t packBf16(float a, float b) {
 // row segment of up to 128 B leaves as one request.  Chunks are XOR-swizzled
 // by row so both the row-per-thread writes and the row-contiguous reads are
 // free of bank conflicts.
-__device__ __forceinline__ uint4* warpStage() {
-  __shared__ __align__(128) uint4 stageBuf[4][32 * 8];  // 4 KB per epilogue warp
-  return stageBuf[(threadIdx.x >> 5) & 3];
-}
-
 template <int NC>
 __device__ __forceinline__ void stagePut(uint4* st, int lane, int j, uint4 v) {
   st[lane * NC + (j ^ (lane & (NC - 1)))] = v;
@@ -99,19 +111,19 @@ __device__ __forceinline__ uint4 packChunk(const uint32_t* r) {
   return o;
 }
 
-// Write the tile's accumulator as bf16 through the row stage.  rowBase(row)
-// returns the byte address of column 0 of `row` (any memory this GPU can
-// store to).  Columns are checked per 8-element chunk (N % 8 == 0).
-template <int BN, typename RowBase>
+// Write accumulator columns [cBegin, cBegin + SPAN) of the tile as bf16
+// through the warp's row stage `st`.  rowBase(row) returns the byte address
+// of column 0 of `row` (any memory this GPU can store to).  Columns are
+// checked per 8-element chunk (N % 8 == 0).
+template <int SPAN, typename RowBase>
 __device__ __forceinline__ void storeAccRows(uint32_t tmemAcc, const TileInfo& ti, const GemmShape& s, int laneRow,
-                                             RowBase&& rowBase) {
-  constexpr int CW = BN < 64 ? BN : 64;  // accumulator columns per pass
-  constexpr int NC = CW / 8;             // 16-byte chunks per row per pass
-  uint4* st = warpStage();
+                                             int cBegin, uint4* st, RowBase&& rowBase) {
+  constexpr int CW = SPAN < 64 ? SPAN : 64;  // accumulator columns per pass
+  constexpr int NC = CW / 8;                 // 16-byte chunks per row per pass
   const int lane = laneRow & 31;
   const int warpRow0 = ti.row0 + (laneRow & ~31);
 #pragma unroll 1
-  for (int c = 0; c < BN; c += CW) {
+  for (int c = cBegin; c < cBegin + SPAN; c += CW) {
     uint32_t r[CW];
 #pragma unroll
     for (int i = 0; i < CW / 16; i++) sm100::tmemLoad16p(tmemAcc + c + 16 * i, r + 16 * i);
@@ -127,15 +139,50 @@ __device__ __forceinline__ void storeAccRows(uint32_t tmemAcc, const TileInfo& t
 }
 
 // Plain store of the accumulator to C (row-major, ldc elements).
+// Every epilogue functor writes accumulator columns [cBegin, cBegin + SPAN)
+// of the tile rows owned by the calling thread's warp.
 struct EpiStore {
   __nv_bfloat16* C;
   int ldc;
-  template <int BN>
-  __device__ __forceinline__ void operator()(uint32_t tmemAcc, const TileInfo& ti, const GemmShape& s,
-                                             int laneRow) const {
+  template <int SPAN>
+  __device__ __forceinline__ void operator()(uint32_t tmemAcc, const TileInfo& ti, const GemmShape& s, int laneRow,
+                                             int cBegin, uint4* st) const {
     char* base = reinterpret_cast<char*>(C);
     const size_t pitch = static_cast<size_t>(ldc) * 2;
-    storeAccRows<BN>(tmemAcc, ti, s, laneRow, [&](int row) { return base + row * pitch; });
+    storeAccRows<SPAN>(tmemAcc, ti, s, laneRow, cBegin, st, [&](int row) { return base + row * pitch; });
+  }
+};
+
+// Split-K partial: writes the fp32 accumulator of split ti.ks to
+// ws[ks][row][col] (row-major, ldn columns); a reduction kernel sums the
+// splits.  Rows leave as 128-byte segments (32 floats).
+struct EpiPartialF32 {
+  float* ws;
+  int ldn;
+  size_t splitElems;  // elements per split slice (M * ldn)
+  template <int SPAN>
+  __device__ __forceinline__ void operator()(uint32_t tmemAcc, const TileInfo& ti, const GemmShape& s, int laneRow,
+                                             int cBegin, uint4* st) const {
+    constexpr int CW = SPAN < 32 ? SPAN : 32;  // accumulator columns per pass
+    constexpr int NC = CW / 4;                 // 16-byte chunks per row per pass
+    const int lane = laneRow & 31;
+    const int warpRow0 = ti.row0 + (laneRow & ~31);
+    float* base = ws + static_cast<size_t>(ti.ks) * splitElems;
+#pragma unroll 1
+    for (int c = cBegin; c < cBegin + SPAN; c += CW) {
+      uint32_t r[CW];
+#pragma unroll
+      for (int i = 0; i < CW / 16; i++) sm100::tmemLoad16p(tmemAcc + c + 16 * i, r + 16 * i);
+      sm100::tmemLoadWait();
+#pragma unroll
+      for (int j = 0; j < NC; j++) stagePut<NC>(st, lane, j, make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]));
+      const int col0 = ti.col0 + c;
+      stageFlush<NC>(st, lane, [&](int rr, int ch, uint4 v) {
+        const int row = warpRow0 + rr, col = col0 + ch * 4;
+        if (row < s.M && col < s.N)
+          *reinterpret_cast<uint4*>(base + static_cast<size_t>(row) * ldn + col) = v;
+      });
+    }
   }
 };
 
@@ -146,18 +193,18 @@ struct EpiStore {
 struct EpiSiluMul {
   __nv_bfloat16* C;
   int ldc;
-  template <int BN>
-  __device__ __forceinline__ void operator()(uint32_t tmemAcc, const TileInfo& ti, const GemmShape& s,
-                                             int laneRow) const {
-    constexpr int CW = BN < 128 ? BN : 128;  // accumulator columns per pass
-    constexpr int NC = CW / 16;              // 16-byte output chunks per row per pass
-    uint4* st = warpStage();
+  template <int SPAN>
+  __device__ __forceinline__ void operator()(uint32_t tmemAcc, const TileInfo& ti, const GemmShape& s, int laneRow,
+                                             int cBegin, uint4* st) const {
+    static_assert(SPAN % 32 == 0, "gate/up pairs span 32 accumulator columns");
+    constexpr int CW = SPAN < 128 ? SPAN : 128;  // accumulator columns per pass
+    constexpr int NC = CW / 16;                  // 16-byte output chunks per row per pass
     const int lane = laneRow & 31;
     const int warpRow0 = ti.row0 + (laneRow & ~31);
     char* base = reinterpret_cast<char*>(C);
     const size_t pitch = static_cast<size_t>(ldc) * 2;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += CW) {
+    for (int c = cBegin; c < cBegin + SPAN; c += CW) {
 #pragma unroll
       for (int j = 0; j < CW / 32; j++) {
         uint32_t g[16], u[16];
@@ -187,14 +234,23 @@ struct EpiSiluMul {
 // tile), no gating, no extra warps.  `hs` is per-CTA shared scratch.
 struct NoHooks {
   static constexpr int kExtraWarps = 0;
+  static constexpr int kEpiGroups = 1;  // epilogue warpgroups; each takes BN / kEpiGroups columns
   __device__ __forceinline__ void setup(uint32_t*) const {}
   __device__ __forceinline__ void teardown(uint32_t*) const {}
+  // With split-K, tile t covers output tile t % (tilesM * tilesN) over the
+  // k-blocks of split t / (tilesM * tilesN).
   __device__ __forceinline__ TileInfo tileAt(const GemmShape& s, int t, int BN) const {
     TileInfo ti;
-    ti.tn = t / s.tilesM;
-    ti.tm = t % s.tilesM;
+    const int mn = s.tilesM * s.tilesN;
+    ti.ks = t / mn;
+    const int r = t - ti.ks * mn;
+    ti.tn = r / s.tilesM;
+    ti.tm = r % s.tilesM;
     ti.row0 = ti.tm * kBM;
     ti.col0 = ti.tn * BN;
+    const int nk = s.numK();
+    ti.kb0 = ti.ks * nk / s.splits;
+    ti.kb1 = (ti.ks + 1) * nk / s.splits;
     return ti;
   }
   __device__ __forceinline__ bool beforeLoad(const TileInfo&, const GemmShape&, uint32_t*, volatile int*) const {
@@ -206,10 +262,12 @@ struct NoHooks {
 };
 
 template <int BN, int STAGES, typename Epi, typename Hooks = NoHooks>
-__global__ void __launch_bounds__(kBaseThreads + 32 * Hooks::kExtraWarps, 1)
+__global__ void __launch_bounds__(ctaThreads<Hooks>(), 1)
     gemmKernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, GemmShape s,
                Epi epi, Hooks hooks, int* errorFlag) {
-  using L = Smem<BN, STAGES>;
+  constexpr int kEpiWarps = 4 * Hooks::kEpiGroups;
+  constexpr int kSpan = BN / Hooks::kEpiGroups;
+  using L = Smem<BN, STAGES, kEpiWarps>;
   extern __shared__ __align__(1024) uint8_t smemRaw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smemRaw) + 1023) & ~uintptr_t(1023));
   uint64_t* fullBar = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
@@ -232,7 +290,7 @@ __global__ void __launch_bounds__(kBaseThreads + 32 * Hooks::kExtraWarps, 1)
     }
     for (int i = 0; i < 2; i++) {
       sm100::mbarInit(&accFull[i], 1);
-      sm100::mbarInit(&accEmpty[i], 4);
+      sm100::mbarInit(&accEmpty[i], kEpiWarps);
     }
     sm100::mbarInit(drainBar, 1);
     *abortFlag = 0;
@@ -247,8 +305,7 @@ __global__ void __launch_bounds__(kBaseThreads + 32 * Hooks::kExtraWarps, 1)
   __syncthreads();
   sm100::tcFenceAfter();
   const uint32_t tmemBase = *tmemSlot;
-  const int numTiles = s.tilesM * s.tilesN;
-  const int numK = (s.K + kBK - 1) / kBK;
+  const int numTiles = s.tilesM * s.tilesN * s.splits;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -266,7 +323,7 @@ __global__ void __launch_bounds__(kBaseThreads + 32 * Hooks::kExtraWarps, 1)
           ok = false;
           break;
         }
-        for (int kb = 0; kb < numK; kb++) {
+        for (int kb = ti.kb0; kb < ti.kb1; kb++) {
           if (!sm100::mbarWait(&emptyBar[stage], phase ^ 1u, abortFlag)) {
             ok = false;
             break;
@@ -315,7 +372,8 @@ __global__ void __launch_bounds__(kBaseThreads + 32 * Hooks::kExtraWarps, 1)
         }
         sm100::tcFenceAfter();
         const uint32_t tmemAcc = tmemBase + acc * BN;
-        for (int kb = 0; kb < numK; kb++) {
+        const TileInfo ti = hooks.tileAt(s, t, BN);
+        for (int kb = ti.kb0; kb < ti.kb1; kb++) {
           if (!sm100::mbarWait(&fullBar[stage], phase, abortFlag)) {
             ok = false;
             break;
@@ -328,7 +386,7 @@ __global__ void __launch_bounds__(kBaseThreads + 32 * Hooks::kExtraWarps, 1)
 #pragma unroll
           for (int k = 0; k < kBK / 16; k++) {
             // +32 bytes per K=16 step inside the swizzle atom (descriptor units of 16 B).
-            sm100::mmaBf16(tmemAcc, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            sm100::mmaBf16(tmemAcc, ad + 2 * k, bd + 2 * k, idesc, (kb != ti.kb0 || k != 0) ? 1u : 0u);
           }
           anyIssued = true;
           sm100::mmaCommit(&emptyBar[stage]);
@@ -351,10 +409,12 @@ __global__ void __launch_bounds__(kBaseThreads + 32 * Hooks::kExtraWarps, 1)
         sm100::mbarWait(drainBar, 0, &never, 200000000ull);
       }
     }
-  } else if (warp < 6) {
-    // ---------------- epilogue (warps 2..5) ----------------
+  } else if (warp < 2 + kEpiWarps) {
+    // ---------------- epilogue (warps 2 .. 1 + kEpiWarps) ----------------
     const int quarter = warp & 3;             // TMEM lane quarter this warp may access
     const int laneRow = quarter * 32 + lane;  // tile row of this thread
+    const int cBegin = ((warp - 2) / 4) * kSpan;
+    uint4* rowStage = reinterpret_cast<uint4*>(smem + L::kRowStageOff + (warp - 2) * kWarpStageBytes);
     int acc = 0;
     uint32_t accPhase = 0;
     bool ok = hooks.beforeTiles(hs, abortFlag);
@@ -367,7 +427,7 @@ __global__ void __launch_bounds__(kBaseThreads + 32 * Hooks::kExtraWarps, 1)
       sm100::tcFenceAfter();
       const TileInfo ti = hooks.tileAt(s, t, BN);
       const uint32_t tmemAcc = tmemBase + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
-      epi.template operator()<BN>(tmemAcc, ti, s, laneRow);
+      epi.template operator()<kSpan>(tmemAcc, ti, s, laneRow, cBegin, rowStage);
       sm100::tcFenceBefore();
       __syncwarp();
       if (lane == 0) sm100::mbarArrive(&accEmpty[acc]);

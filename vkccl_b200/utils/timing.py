@@ -30,12 +30,24 @@ class L2Flusher:
         self.buf.fill_(0)
 
 
-def time_steps(step: Callable[[], None], steps: int, flush: Optional[L2Flusher] = None) -> list:
-    """Per-step device times in microseconds (events around each step)."""
+def time_steps(step: Callable[[], None], steps: int, flush: Optional[L2Flusher] = None,
+               align_ranks: bool = False) -> list:
+    """Per-step device times in microseconds (events around each step).
+
+    align_ranks: synchronize the device and barrier all ranks before every
+    step (outside the timed events), so each step starts with the ranks
+    aligned, as it would after a preceding collective.
+    """
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     torch.cuda.synchronize()
     for i in range(steps):
+        if align_ranks:
+            import torch.distributed as dist
+
+            torch.cuda.synchronize()
+            if dist.is_initialized() and dist.get_world_size() > 1:
+                dist.barrier()
         if flush is not None:
             flush()
         starts[i].record()
