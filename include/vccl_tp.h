@@ -19,6 +19,16 @@ extern "C" {
  * N % 16 == 0, 16-byte aligned pointers). */
 vcclResult_t vcclGemmBf16(const void* A, const void* W, void* C, int M, int N, int K, vcclStream_t stream);
 
+/* vcclGemmBf16 for callers that must not allocate device memory (no
+ * counterpart in the reference).  Same arguments and results; the split-K
+ * scratch of decode shapes and the abort flag live in one fixed 8 MiB
+ * device array instead of allocations.  A shape whose split-K partials need
+ * more than 8 MiB returns vcclInvalidArgument.  The first call on each
+ * device resolves the array's address; make it before any stream capture.
+ * Calls that may overlap in time on one device (different streams or host
+ * threads) share the array and race; calls on one stream are safe. */
+vcclResult_t vcclGemmBf16NoAlloc(const void* A, const void* W, void* C, int M, int N, int K, vcclStream_t stream);
+
 /* H[M,N/2] = silu(A W_g^T) * (A W_u^T), with W[N,K] holding gate and up rows
  * interleaved in groups of 16 (vcclInterleaveGateUp layout). */
 vcclResult_t vcclGemmSiluMul(const void* A, const void* W, void* H, int M, int N, int K, vcclStream_t stream);

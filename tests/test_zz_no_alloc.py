@@ -1,0 +1,73 @@
+# SPDX-License-Identifier: Apache-2.0
+"""vcclGemmBf16NoAlloc, called through its exported C symbol.
+
+Two calls in a row on the same stream must each match vcclGemmBf16 on the
+same inputs (and the fp32 reference), for decode shapes that take the
+split-K path through the fixed scratch and for a shape that does not.  A
+shape whose split-K partials exceed the fixed scratch is rejected.
+
+Named test_zz_* so it is collected last; it must pass alone too.
+"""
+
+import ctypes
+
+import pytest
+import torch
+
+from conftest import gpu_count
+
+pytestmark = pytest.mark.gpu
+
+INVALID_ARGUMENT = 4
+
+
+def _lib():
+    from vkccl_b200._lib import lib
+
+    h = lib()
+    fn = h.vcclGemmBf16NoAlloc
+    fn.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]
+    fn.restype = ctypes.c_int
+    return h
+
+
+def _call(fn, a, w, c):
+    m, k = a.shape
+    n = w.shape[0]
+    return fn(a.data_ptr(), w.data_ptr(), c.data_ptr(), m, n, k, torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 8192, 8192), (32, 4096, 1792), (200, 1536, 8192), (512, 1024, 1024)])
+def test_no_alloc_matches_gemm(m, n, k):
+    if gpu_count() == 0:
+        pytest.skip("no GPU")
+    h = _lib()
+    g = torch.Generator(device="cuda").manual_seed(7 * m + n + k)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.02).bfloat16()
+    ref_lib = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    assert _call(h.vcclGemmBf16, a, w, ref_lib) == 0
+    outs = []
+    for _ in range(2):
+        c = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+        assert _call(h.vcclGemmBf16NoAlloc, a, w, c) == 0
+        outs.append(c)
+    torch.cuda.synchronize()
+    ref = a.float() @ w.float().T
+    scale = ref.abs().max().item() + 1e-6
+    for c in outs:
+        assert torch.isfinite(c.float()).all()
+        assert (c.float() - ref_lib.float()).abs().max().item() <= 1e-2 * scale + 1e-3
+        assert (c.float() - ref).abs().max().item() <= 1e-2 * scale + 1e-3
+
+
+def test_no_alloc_rejects_oversized_scratch():
+    if gpu_count() == 0:
+        pytest.skip("no GPU")
+    h = _lib()
+    # 2 row tiles x 10 column tiles -> 7 K splits x 256 x 1280 fp32 = 9.2 MB > 8 MiB.
+    m, n, k = 256, 1280, 8192
+    a = torch.zeros(m, k, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(n, k, dtype=torch.bfloat16, device="cuda")
+    c = torch.zeros(m, n, dtype=torch.bfloat16, device="cuda")
+    assert _call(h.vcclGemmBf16NoAlloc, a, w, c) == INVALID_ARGUMENT
