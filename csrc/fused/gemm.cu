@@ -5,7 +5,9 @@
 #include <cuda_runtime.h>
 
 #include <cstdlib>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "common/log.h"
 #include "fused/gemm_launch.cuh"
@@ -95,6 +97,32 @@ cudaError_t launchSplitReduce(const float* ws, int splits, size_t elems, void* o
   return cudaGetLastError();
 }
 
+// Split-K scratch, cached per (device, stream) so steady-state calls
+// allocate nothing: calls on one stream are ordered, and calls on different
+// streams use different buffers.  A call that needs more than the cached
+// size waits for its stream, frees the old buffer and allocates a larger one.
+// Not used while the stream is being captured (see vcclGemmBf16).
+float* splitScratch(cudaStream_t st, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto& e = cache[{dev, st}];
+  if (e.second < bytes) {
+    if (e.first != nullptr) {
+      cudaStreamSynchronize(st);
+      cudaFree(e.first);
+      e = {nullptr, 0};
+    }
+    const size_t sz = (bytes + (1u << 20) - 1) / (1u << 20) * (1u << 20);
+    void* p = nullptr;
+    if (cudaMalloc(&p, sz) != cudaSuccess) return nullptr;
+    e = {p, sz};
+  }
+  return static_cast<float*>(e.first);
+}
+
 // One abort flag per device (kernels only ever write their own device's).
 int* errorFlag() {
   static std::mutex mu;
@@ -126,19 +154,30 @@ vcclResult_t vcclGemmBf16(const void* A, const void* W, void* C, int M, int N, i
   const char* sk = std::getenv("VCCL_GEMM_SPLITK");
   const gemm::SplitPlan plan = (bnEnv > 0 || (sk && sk[0] == '0')) ? gemm::SplitPlan{0, 1} : gemm::planSplitK(M, N, K);
   if (plan.splits > 1) {
-    // Decode shapes: split K across more CTAs; fp32 partials live in a
-    // stream-ordered scratch buffer for the duration of the call.
+    // Decode shapes: split K across more CTAs.  The fp32 partials live in a
+    // scratch buffer cached for this stream; while the stream is being
+    // captured into a CUDA graph they come from a stream-ordered allocation
+    // instead (a memory node of the graph), since nothing may be allocated
+    // synchronously then.
     const size_t elems = static_cast<size_t>(M) * N;
+    const size_t bytes = elems * plan.splits * sizeof(float);
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cap);
+    const bool capturing = cap != cudaStreamCaptureStatusNone;
     float* ws = nullptr;
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws), elems * plan.splits * sizeof(float), st);
-    if (e != cudaSuccess) {
-      VERR("vcclGemmBf16 split-K scratch: %s", cudaGetErrorString(e));
+    if (capturing) {
+      if (cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, st) != cudaSuccess) ws = nullptr;
+    } else {
+      ws = gemm::splitScratch(st, bytes);
+    }
+    if (ws == nullptr) {
+      VERR("vcclGemmBf16: cannot allocate %zu bytes of split-K scratch", bytes);
       return vcclSystemError;
     }
     gemm::EpiPartialF32 epi{ws, N, elems};
-    e = gemm::launchGemm(A, W, M, N, K, epi, gemm::NoHooks{}, st, plan.bn, 0, plan.splits);
+    cudaError_t e = gemm::launchGemm(A, W, M, N, K, epi, gemm::NoHooks{}, st, plan.bn, 0, plan.splits);
     if (e == cudaSuccess) e = gemm::launchSplitReduce(ws, plan.splits, elems, C, st);
-    cudaFreeAsync(ws, st);
+    if (capturing) cudaFreeAsync(ws, st);
     if (e != cudaSuccess) {
       VERR("vcclGemmBf16 (split-K %d): %s", plan.splits, cudaGetErrorString(e));
       return vcclInvalidArgument;

@@ -24,6 +24,7 @@ struct SplitPlan {
   int splits;
 };
 SplitPlan planSplitK(int M, int N, int K);
+float* splitScratch(cudaStream_t st, size_t bytes);
 
 // out[i] = bf16(sum over s < splits of ws[s * elems + i]); elems % 4 == 0.
 cudaError_t launchSplitReduce(const float* ws, int splits, size_t elems, void* out, cudaStream_t st);

@@ -3,9 +3,10 @@
 // not allocate device memory.
 //
 // vcclGemmBf16 runs decode-shaped GEMMs (few output tiles) as split-K: each
-// K split writes fp32 partials to scratch taken from the stream-ordered
-// allocator, and a second kernel sums them into the bf16 output.  It also
-// allocates a small per-device abort flag on first use.  Some callers cannot
+// K split writes fp32 partials to a scratch buffer that it allocates per
+// stream (and reallocates when a larger shape comes), and a second kernel
+// sums them into the bf16 output.  It also allocates a small per-device
+// abort flag on first use.  Some callers cannot
 // allow either allocation: code that runs inside a custom allocator's hook
 // (allocating there re-enters the allocator), an out-of-memory handler that
 // must still make progress, or a server that reserved all free device memory

@@ -20,6 +20,7 @@ enum Where : uint32_t {
   kWhereP2pSend = 7,
   kWhereP2pRecv = 8,
   kWhereFused = 9,
+  kWhereMoe = 10,
 };
 
 struct CollArgs {

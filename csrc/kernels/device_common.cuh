@@ -51,6 +51,11 @@ constexpr size_t kAgStagedOff = kAgLocalReadyOff + 64;      // u32, local: CTAs 
 constexpr size_t kRsLocalDoneOff = kRsReduceCallsOff + 256; // u32, local: GEMM CTAs done pushing
 constexpr size_t kRsLocalFreeOff = kRsLocalDoneOff + 4;     // u32, local: reduce blocks done
 constexpr size_t kMoeOff = 73728;                           // MoE dispatch/combine counters
+constexpr size_t kMoeDispDoneOff = kMoeOff;                 // u32[kMaxRanks], written by peers
+constexpr size_t kMoeCombDoneOff = kMoeOff + 64;            // u32[kMaxRanks], written by peers
+constexpr size_t kMoeDispEpochOff = kMoeOff + 128;          // u32, local: dispatch calls finished
+constexpr size_t kMoeCombEpochOff = kMoeOff + 132;          // u32, local: combine calls finished
+constexpr size_t kMoeBlocksOff = kMoeOff + 192;             // u32[4], local: per-kernel block counters
 constexpr size_t kCtrlHeader = 1 << 20;
 
 constexpr size_t kLLMaxBytes = 1 << 20;                 // largest LL payload per source rank
@@ -65,7 +70,7 @@ constexpr size_t kP2pBytes = size_t(kMaxRanks) * kMaxChannels * kP2pSlots * kP2p
 constexpr size_t kCtrlBytes = kP2pOff + kP2pBytes;
 
 // Status words (host-mapped): [0] error code, [1] where, [2] rank, [3] detail.
-enum : uint32_t { kOk = 0, kErrTimeout = 1, kErrAborted = 2, kErrBadArg = 3 };
+enum : uint32_t { kOk = 0, kErrTimeout = 1, kErrAborted = 2, kErrBadArg = 3, kErrCapacity = 4 };
 
 struct DevComm {
   int rank;
@@ -74,8 +79,10 @@ struct DevComm {
   char* data[kMaxRanks];  // every rank's data allocation, mapped here
   char* mcData;           // multicast address of the data allocations, or null
   size_t dataBytes;
-  char* fused[kMaxRanks]; // every rank's fused-op region (GEMM+RS, AG+GEMM, MoE)
+  char* fused[kMaxRanks]; // every rank's fused-op region (GEMM+RS, AG+GEMM)
   size_t fusedBytes;
+  char* moe[kMaxRanks];   // every rank's MoE dispatch/combine region (allocated on first use)
+  size_t moeBytes;
   uint32_t* status;              // host-mapped, written by kernels
   const uint32_t* abortWord;     // host-mapped, written by vcclCommAbort
   uint64_t timeoutNs;

@@ -45,7 +45,8 @@ vcclResult_t vcclComm::pollDeviceStatus() {
   if (code == vccl::dev::kOk) return vcclSuccess;
   static const char* const kWhere[] = {"?", "start barrier", "LL wait", "push barrier",
                                        "reduce barrier", "NVLS barrier", "gather barrier",
-                                       "send slot wait", "recv data wait", "fused kernel wait"};
+                                       "send slot wait", "recv data wait", "fused kernel wait",
+                                       "MoE dispatch/combine"};
   uint32_t where = s[1];
   const char* w = where < sizeof(kWhere) / sizeof(kWhere[0]) ? kWhere[where] : "?";
   if (code == vccl::dev::kErrAborted) {
@@ -56,6 +57,11 @@ vcclResult_t vcclComm::pollDeviceStatus() {
     VERR("rank %d: device wait timed out (%s, peer slot %u); a peer is dead or stuck "
          "(VCCL_TIMEOUT=%ds)", rank, w, s[3], vccl::watchdogSeconds());
     return vcclSystemError;
+  }
+  if (code == vccl::dev::kErrCapacity) {
+    VERR("rank %d: MoE dispatch received more rows than its capacity (%u rows routed here); rows past the "
+         "capacity were dropped", rank, s[3]);
+    return vcclInvalidUsage;
   }
   VERR("rank %d: kernel reported error %u (%s)", rank, code, w);
   return vcclInternalError;

@@ -46,6 +46,9 @@ struct DeviceState {
   SymmetricBuffer ctrl;
   SymmetricBuffer data;
   SymmetricBuffer fused;           // staging owned by the fused TP kernels
+  SymmetricBuffer moe;             // MoE dispatch/combine region (first use)
+  void* moeLocal = nullptr;        // single-rank MoE region (plain allocation)
+  size_t gran = 0;                 // VMM allocation granularity
   bool nvls = false;
   uint32_t* hostStatus = nullptr;  // pinned + mapped
   uint32_t* devStatus = nullptr;
@@ -76,6 +79,10 @@ struct Registration {
 };
 
 vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<DeviceState>* out);
+// Make sure the MoE region holds at least `bytes` on every rank.  Collective
+// when it allocates: every rank must call it with the same size (the MoE
+// entry points derive it from arguments that must agree across ranks).
+vcclResult_t deviceStateEnsureMoe(DeviceState* ds, Bootstrap* bs, size_t bytes);
 void deviceStateDestroy(DeviceState* ds, Bootstrap* bs, bool peersAlive);
 
 }  // namespace vccl

@@ -9,7 +9,9 @@
 // Kernels then load and store peer memory directly over NVLink.
 #include <unistd.h>
 
+#include <algorithm>
 #include <cstring>
+#include <vector>
 
 #include "common/env.h"
 #include "common/log.h"
@@ -255,6 +257,7 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
     size_t gran = 0;
     CU_TRY(d->memGranularity(&gran, &prop, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED));
     size_t dataAlign = gran;
+    ds->gran = gran;
     const bool tryNvls = envLong("VCCL_NVLS_ENABLE", 1) != 0 && d->mcCreate != nullptr;
     int mcCap = 0;
     if (tryNvls) d->deviceGetAttribute(&mcCap, CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED, ds->cuDevice);
@@ -318,6 +321,43 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
   return vcclSuccess;
 }
 
+vcclResult_t deviceStateEnsureMoe(DeviceState* ds, Bootstrap* bs, size_t bytes) {
+  if (ds->dc.moeBytes >= bytes) return vcclSuccess;
+  cudaSetDevice(ds->device);
+  const size_t want = std::max(bytes, envBytes("VCCL_MOE_BUFFSIZE", 256u << 20));
+  const int n = bs->nranks(), me = bs->rank();
+  if (n == 1) {
+    void* p = nullptr;
+    CUDART_TRY(cudaMalloc(&p, want));
+    if (ds->moeLocal) cudaFree(ds->moeLocal);
+    ds->moeLocal = p;
+    ds->dc.moe[0] = static_cast<char*>(p);
+    ds->dc.moeBytes = want;
+    return vcclSuccess;
+  }
+  const size_t size = roundUp(want, ds->gran);
+  std::vector<uint64_t> all(n);
+  all[me] = size;
+  VTRY(bs->allGather(all.data(), sizeof(uint64_t)));
+  for (uint64_t v : all) {
+    if (v != size) {
+      VERR("ranks disagree on the MoE region size (capacity, hidden size and VCCL_MOE_BUFFSIZE must match)");
+      return vcclInvalidUsage;
+    }
+  }
+  if (ds->moe.bytes) {
+    // Growing: every rank finishes its work in the old region first.
+    CUDART_TRY(cudaDeviceSynchronize());
+    VTRY(bs->barrier());
+    symmetricFree(driverApi(), me, &ds->moe);
+  }
+  VTRY(symmetricAlloc(bs, ds, size, ds->gran, &ds->moe));
+  for (int p = 0; p < n; p++) ds->dc.moe[p] = reinterpret_cast<char*>(ds->moe.va[p]);
+  ds->dc.moeBytes = size;
+  VINFO("rank %d: MoE region %zu MiB", me, size >> 20);
+  return vcclSuccess;
+}
+
 void deviceStateDestroy(DeviceState* ds, Bootstrap* bs, bool peersAlive) {
   if (ds == nullptr) return;
   const DriverApi* d = driverApi();
@@ -331,8 +371,11 @@ void deviceStateDestroy(DeviceState* ds, Bootstrap* bs, bool peersAlive) {
     multicastTeardown(d, ds);
     symmetricFree(d, bs ? bs->rank() : 0, &ds->data);
     symmetricFree(d, bs ? bs->rank() : 0, &ds->fused);
+    symmetricFree(d, bs ? bs->rank() : 0, &ds->moe);
     symmetricFree(d, bs ? bs->rank() : 0, &ds->ctrl);
   }
+  if (ds->moeLocal) cudaFree(ds->moeLocal);
+  ds->moeLocal = nullptr;
   if (ds->hostStatus) cudaFreeHost(ds->hostStatus);
   if (ds->hostAbort) cudaFreeHost(ds->hostAbort);
   if (ds->stream) cudaStreamDestroy(ds->stream);

@@ -3,8 +3,10 @@
 
     python -m vkccl_b200.bench.gemm_one --m 8192 --n 3584 --k 4096 [--silu] [--iters 3]
 
-Prints the CUDA-event time of the last launch next to torch.matmul (cuBLAS)
-and the achieved TFLOP/s.
+Prints the best CUDA-event time of one launch next to torch.matmul (cuBLAS)
+and the achieved TFLOP/s.  With --graph, `iters` launches are captured in
+one CUDA graph and the replay time is divided by `iters` (kernel time
+without host launch overhead, inputs L2-warm), for both libraries.
 """
 
 from __future__ import annotations
@@ -24,6 +26,7 @@ def main() -> None:
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--silu", action="store_true")
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--graph", action="store_true")
     a = ap.parse_args()
     a_ = torch.randn(a.m, a.k, device="cuda").bfloat16()
     w = (torch.randn(a.n, a.k, device="cuda") * 0.02).bfloat16()
@@ -44,10 +47,26 @@ def main() -> None:
             best = min(best, e0.elapsed_time(e1) * 1000)
         return best
 
-    t_ours = timed(ours)
-    t_cublas = timed(lambda: a_ @ w.T)
+    def graphed(fn):
+        fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(a.iters):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1) * 1000 / a.iters
+
+    t_ours = (graphed if a.graph else timed)(ours)
+    t_cublas = (graphed if a.graph else timed)(lambda: a_ @ w.T)
     flops = 2.0 * a.m * a.n * a.k
-    print(json.dumps({"m": a.m, "n": a.n, "k": a.k, "silu": a.silu, "ours_us": round(t_ours, 2),
+    print(json.dumps({"m": a.m, "n": a.n, "k": a.k, "silu": a.silu, "graph": a.graph, "ours_us": round(t_ours, 2),
                       "cublas_us": round(t_cublas, 2), "ours_tflops": round(flops / t_ours / 1e6, 1),
                       "cublas_tflops": round(flops / t_cublas / 1e6, 1)}))
 

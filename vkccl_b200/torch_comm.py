@@ -233,22 +233,29 @@ class VcclCommunicator(DeviceCommunicatorBase):
                  is_sequence_parallel: bool = False, extra_tensors: Optional[list] = None):
         """Send every (token, expert) pair to the rank owning the expert.
 
-        Experts are split evenly over ranks.  Returns the received tokens
-        (fp8 e4m3 with 1x128 block scales dequantised to bf16 on arrival),
-        their routing weights and expert ids; the layout needed by
-        ``combine`` is remembered.
+        Experts (``self.num_experts``, default one per rank) are split
+        evenly over ranks.  Returns the received rows (fp8 e4m3 with 1x128
+        block scales on the wire, dequantised to bf16 on arrival), their
+        routing weights and global expert ids, trimmed to the received
+        count (one host synchronisation); ``combine`` takes the expert
+        outputs in the same row order.
         """
         from vkccl_b200.ops.moe import moe_dispatch
 
-        self._moe_state, recv_x, recv_w, recv_ids = moe_dispatch(self.vccl, hidden_states, topk_weights, topk_ids)
+        d = moe_dispatch(self.vccl, hidden_states.contiguous(), topk_weights, topk_ids,
+                         num_experts=getattr(self, "num_experts", None) or self.world_size)
+        self._moe_state = d
+        n = d.count()
+        out = (d.recv_x[:n], d.recv_w[:n], d.recv_ids()[:n])
         if extra_tensors is not None:
-            return recv_x, recv_w, recv_ids, extra_tensors
-        return recv_x, recv_w, recv_ids
+            return (*out, extra_tensors)
+        return out
 
     def combine(self, hidden_states: torch.Tensor, is_sequence_parallel: bool = False) -> torch.Tensor:
+        """out[t] = sum_k w[t, k] * expert_out(t, k) on the tokens' own ranks."""
         from vkccl_b200.ops.moe import moe_combine
 
-        return moe_combine(self.vccl, self._moe_state, hidden_states)
+        return moe_combine(self.vccl, self._moe_state, hidden_states.contiguous())
 
     def destroy(self) -> None:
         if getattr(self, "vccl", None) is not None:
