@@ -19,6 +19,7 @@
 #include "fused/gemm_launch.cuh"
 #include "kernels/collectives.cuh"
 #include "runtime/comm.h"
+#include "runtime/launch.h"
 #include "vccl_tp.h"
 
 namespace vccl {
@@ -48,6 +49,13 @@ __device__ __forceinline__ void groupCopy(char* dst, const char* src, size_t byt
     for (int u = 0; u < U; u++) dev::stG(dst + (i + u * 64) * 16, v[u]);
   }
   for (; i < n16; i += 64) dev::stG(dst + i * 16, dev::ldCG(src + i * 16));
+}
+
+// Row count up to which the fused entry points run the collective and the
+// GEMM as separate kernels (VCCL_FUSED_SMALL_M, default 512).
+int smallRows() {
+  const char* e = std::getenv("VCCL_FUSED_SMALL_M");
+  return e != nullptr ? static_cast<int>(std::strtol(e, nullptr, 10)) : 512;
 }
 
 struct AgHooks : gemm::NoHooks {
@@ -198,6 +206,30 @@ extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, voi
       e = gemm::launchGemm(xShard, W, M, N, K, epi, gemm::NoHooks{}, s, bnEnv, 0);
     }
     return e == cudaSuccess ? vcclSuccess : vcclInvalidArgument;
+  }
+  if (M <= fused::smallRows()) {
+    // Few rows (decode, short prefills): the gather is a few hundred KB, so
+    // an LL all-gather into local scratch followed by a (split-K) GEMM beats
+    // the persistent fused kernel, whose per-call synchronisation and
+    // mostly idle tiles dominate at this size.
+    const size_t xBytes = (static_cast<size_t>(M) * K * 2 + 255) / 256 * 256;
+    const size_t wsBytes = gemm::gemmAutoScratchBytes(M, N, K, bnEnv, true);
+    gemm::Scratch sc;
+    if (!gemm::acquireScratch(s, xBytes + wsBytes, &sc)) {
+      VERR("vcclAllGatherGemm: cannot allocate %zu bytes of scratch", xBytes + wsBytes);
+      return vcclSystemError;
+    }
+    char* xfull = static_cast<char*>(sc.p);
+    e = launchAllGather(launchCtxFor(*comm->dev, s), xShard, xfull, static_cast<size_t>(M / n) * K * 2);
+    if (e == cudaSuccess)
+      e = gemm::gemmAuto(xfull, W, out, M, N, K, siluMul != 0, s, bnEnv, true,
+                         reinterpret_cast<float*>(xfull + xBytes));
+    gemm::releaseScratch(sc);
+    if (e != cudaSuccess) {
+      VERR("vcclAllGatherGemm (small): %s", cudaGetErrorString(e));
+      return vcclInvalidArgument;
+    }
+    return vcclSuccess;
   }
   const dev::DevComm& dc = comm->dev->dc;
   const size_t xOff = dc.fusedBytes / 2;

@@ -85,7 +85,43 @@ __global__ void __launch_bounds__(256) splitReduceKernel(const float4* ws, int s
     out[i] = make_uint2(packBf16(a.x, a.y), packBf16(a.z, a.w));
   }
 }
+
+// Partials hold gate and up columns interleaved in groups of 16 (see
+// EpiSiluMul); out[m][j] = silu(gate) * up with j = 16 g + w taking gate
+// column 32 g + w and up column 32 g + 16 + w.  Four outputs per thread.
+__global__ void __launch_bounds__(256) splitReduceSiluKernel(const float* ws, int splits, int M, int N,
+                                                             size_t stride, uint2* out) {
+  const int half = N / 2;
+  const size_t n4 = static_cast<size_t>(M) * half / 4;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t o = i * 4;
+    const int m = static_cast<int>(o / half), j = static_cast<int>(o % half);
+    const size_t gcol = static_cast<size_t>(m) * N + (j / 16) * 32 + (j % 16);
+    float4 g = *reinterpret_cast<const float4*>(ws + gcol);
+    float4 u = *reinterpret_cast<const float4*>(ws + gcol + 16);
+    for (int sp = 1; sp < splits; sp++) {
+      const float4 g2 = *reinterpret_cast<const float4*>(ws + sp * stride + gcol);
+      const float4 u2 = *reinterpret_cast<const float4*>(ws + sp * stride + gcol + 16);
+      g.x += g2.x, g.y += g2.y, g.z += g2.z, g.w += g2.w;
+      u.x += u2.x, u.y += u2.y, u.z += u2.z, u.w += u2.w;
+    }
+    auto f = [](float x, float y) { return x / (1.0f + __expf(-x)) * y; };
+    out[i] = make_uint2(packBf16(f(g.x, u.x), f(g.y, u.y)), packBf16(f(g.z, u.z), f(g.w, u.w)));
+  }
+}
 }  // namespace
+
+cudaError_t launchSplitReduceSilu(const float* ws, int splits, int M, int N, void* out, cudaStream_t st) {
+  const size_t n4 = static_cast<size_t>(M) * (N / 2) / 4;
+  size_t blocks = (n4 + 255) / 256;
+  if (blocks > static_cast<size_t>(smCount()) * 4) blocks = static_cast<size_t>(smCount()) * 4;
+  if (blocks == 0) blocks = 1;
+  splitReduceSiluKernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(ws, splits, M, N,
+                                                                       static_cast<size_t>(M) * N,
+                                                                       static_cast<uint2*>(out));
+  return cudaGetLastError();
+}
 
 cudaError_t launchSplitReduce(const float* ws, int splits, size_t elems, void* out, cudaStream_t st) {
   const size_t n4 = elems / 4;
@@ -123,6 +159,60 @@ float* splitScratch(cudaStream_t st, size_t bytes) {
   return static_cast<float*>(e.first);
 }
 
+bool acquireScratch(cudaStream_t st, size_t bytes, Scratch* out) {
+  out->p = nullptr;
+  out->async = false;
+  out->st = st;
+  if (bytes == 0) return true;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(st, &cap);
+  if (cap != cudaStreamCaptureStatusNone) {
+    // While the stream is captured into a CUDA graph nothing may be
+    // allocated synchronously; a stream-ordered allocation becomes a memory
+    // node of the graph.
+    if (cudaMallocAsync(&out->p, bytes, st) != cudaSuccess) return false;
+    out->async = true;
+    return true;
+  }
+  out->p = splitScratch(st, bytes);
+  return out->p != nullptr;
+}
+
+void releaseScratch(const Scratch& s) {
+  if (s.async && s.p != nullptr) cudaFreeAsync(s.p, s.st);
+}
+
+SplitPlan planFor(int M, int N, int K, int bnOverride, bool allowSplit) {
+  const char* sk = std::getenv("VCCL_GEMM_SPLITK");
+  if (!allowSplit || bnOverride > 0 || (sk && sk[0] == '0')) return {0, 1};
+  return planSplitK(M, N, K);
+}
+
+size_t gemmAutoScratchBytes(int M, int N, int K, int bnOverride, bool allowSplit) {
+  const SplitPlan plan = planFor(M, N, K, bnOverride, allowSplit);
+  return plan.splits > 1 ? static_cast<size_t>(M) * N * plan.splits * sizeof(float) : 0;
+}
+
+cudaError_t gemmAuto(const void* A, const void* W, void* C, int M, int N, int K, bool siluMul, cudaStream_t st,
+                     int bnOverride, bool allowSplit, float* ws) {
+  const SplitPlan plan = planFor(M, N, K, bnOverride, allowSplit);
+  if (plan.splits > 1) {
+    if (ws == nullptr) return cudaErrorInvalidValue;
+    const size_t elems = static_cast<size_t>(M) * N;
+    EpiPartialF32 epi{ws, N, elems};
+    cudaError_t e = launchGemm(A, W, M, N, K, epi, NoHooks{}, st, plan.bn, 0, plan.splits);
+    if (e != cudaSuccess) return e;
+    return siluMul ? launchSplitReduceSilu(ws, plan.splits, M, N, C, st)
+                   : launchSplitReduce(ws, plan.splits, elems, C, st);
+  }
+  if (siluMul) {
+    EpiSiluMul epi{static_cast<__nv_bfloat16*>(C), N / 2};
+    return launchGemm(A, W, M, N, K, epi, NoHooks{}, st, bnOverride, 0);
+  }
+  EpiStore epi{static_cast<__nv_bfloat16*>(C), N};
+  return launchGemm(A, W, M, N, K, epi, NoHooks{}, st, bnOverride, 0);
+}
+
 // One abort flag per device (kernels only ever write their own device's).
 int* errorFlag() {
   static std::mutex mu;
@@ -147,62 +237,37 @@ using namespace vccl;
 
 extern "C" {
 
-vcclResult_t vcclGemmBf16(const void* A, const void* W, void* C, int M, int N, int K, vcclStream_t stream) {
-  if (!A || !W || !C || M <= 0 || N <= 0 || K <= 0 || (N % 16) != 0 || (K % 8) != 0) return vcclInvalidArgument;
+namespace {
+vcclResult_t gemmEntry(const char* what, const void* A, const void* W, void* C, int M, int N, int K, bool siluMul,
+                       vcclStream_t stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int bnEnv = static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN"));
-  const char* sk = std::getenv("VCCL_GEMM_SPLITK");
-  const gemm::SplitPlan plan = (bnEnv > 0 || (sk && sk[0] == '0')) ? gemm::SplitPlan{0, 1} : gemm::planSplitK(M, N, K);
-  if (plan.splits > 1) {
-    // Decode shapes: split K across more CTAs.  The fp32 partials live in a
-    // scratch buffer cached for this stream; while the stream is being
-    // captured into a CUDA graph they come from a stream-ordered allocation
-    // instead (a memory node of the graph), since nothing may be allocated
-    // synchronously then.
-    const size_t elems = static_cast<size_t>(M) * N;
-    const size_t bytes = elems * plan.splits * sizeof(float);
-    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-    cudaStreamIsCapturing(st, &cap);
-    const bool capturing = cap != cudaStreamCaptureStatusNone;
-    float* ws = nullptr;
-    if (capturing) {
-      if (cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, st) != cudaSuccess) ws = nullptr;
-    } else {
-      ws = gemm::splitScratch(st, bytes);
-    }
-    if (ws == nullptr) {
-      VERR("vcclGemmBf16: cannot allocate %zu bytes of split-K scratch", bytes);
-      return vcclSystemError;
-    }
-    gemm::EpiPartialF32 epi{ws, N, elems};
-    cudaError_t e = gemm::launchGemm(A, W, M, N, K, epi, gemm::NoHooks{}, st, plan.bn, 0, plan.splits);
-    if (e == cudaSuccess) e = gemm::launchSplitReduce(ws, plan.splits, elems, C, st);
-    if (capturing) cudaFreeAsync(ws, st);
-    if (e != cudaSuccess) {
-      VERR("vcclGemmBf16 (split-K %d): %s", plan.splits, cudaGetErrorString(e));
-      return vcclInvalidArgument;
-    }
-    return vcclSuccess;
+  // Decode shapes split K across more CTAs; the fp32 partials live in
+  // per-stream scratch (a graph memory node while the stream is captured).
+  gemm::Scratch sc;
+  const size_t bytes = gemm::gemmAutoScratchBytes(M, N, K, bnEnv, true);
+  if (!gemm::acquireScratch(st, bytes, &sc)) {
+    VERR("%s: cannot allocate %zu bytes of split-K scratch", what, bytes);
+    return vcclSystemError;
   }
-  gemm::EpiStore epi{static_cast<__nv_bfloat16*>(C), N};
-  cudaError_t e = gemm::launchGemm(A, W, M, N, K, epi, gemm::NoHooks{}, st, bnEnv, 0);
+  cudaError_t e = gemm::gemmAuto(A, W, C, M, N, K, siluMul, st, bnEnv, true, static_cast<float*>(sc.p));
+  gemm::releaseScratch(sc);
   if (e != cudaSuccess) {
-    VERR("vcclGemmBf16: %s", cudaGetErrorString(e));
+    VERR("%s: %s", what, cudaGetErrorString(e));
     return vcclInvalidArgument;
   }
   return vcclSuccess;
 }
+}  // namespace
+
+vcclResult_t vcclGemmBf16(const void* A, const void* W, void* C, int M, int N, int K, vcclStream_t stream) {
+  if (!A || !W || !C || M <= 0 || N <= 0 || K <= 0 || (N % 16) != 0 || (K % 8) != 0) return vcclInvalidArgument;
+  return gemmEntry("vcclGemmBf16", A, W, C, M, N, K, false, stream);
+}
 
 vcclResult_t vcclGemmSiluMul(const void* A, const void* W, void* H, int M, int N, int K, vcclStream_t stream) {
   if (!A || !W || !H || M <= 0 || N <= 0 || K <= 0 || (N % 32) != 0 || (K % 8) != 0) return vcclInvalidArgument;
-  gemm::EpiSiluMul epi{static_cast<__nv_bfloat16*>(H), N / 2};
-  cudaError_t e = gemm::launchGemm(A, W, M, N, K, epi, gemm::NoHooks{}, reinterpret_cast<cudaStream_t>(stream),
-                                   static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN")), 0);
-  if (e != cudaSuccess) {
-    VERR("vcclGemmSiluMul: %s", cudaGetErrorString(e));
-    return vcclInvalidArgument;
-  }
-  return vcclSuccess;
+  return gemmEntry("vcclGemmSiluMul", A, W, H, M, N, K, true, stream);
 }
 
 }  // extern "C"

@@ -26,6 +26,27 @@ struct SplitPlan {
 SplitPlan planSplitK(int M, int N, int K);
 float* splitScratch(cudaStream_t st, size_t bytes);
 
+// Scratch for one call on `st`: the per-stream cached buffer, or a
+// stream-ordered allocation while `st` is being captured (released with
+// releaseScratch after the call's launches).
+struct Scratch {
+  void* p = nullptr;
+  bool async = false;
+  cudaStream_t st = nullptr;
+};
+bool acquireScratch(cudaStream_t st, size_t bytes, Scratch* out);
+void releaseScratch(const Scratch& s);
+
+// Split-K (or not) plan honouring VCCL_GEMM_BN / VCCL_GEMM_SPLITK.
+SplitPlan planFor(int M, int N, int K, int bnOverride, bool allowSplit);
+// fp32 scratch gemmAuto needs for this shape (0 without split-K).
+size_t gemmAutoScratchBytes(int M, int N, int K, int bnOverride, bool allowSplit);
+// C = A W^T (bf16), or silu(gate) * up with C of N/2 columns, split-K for
+// decode shapes; ws must hold gemmAutoScratchBytes bytes when that is > 0.
+cudaError_t gemmAuto(const void* A, const void* W, void* C, int M, int N, int K, bool siluMul, cudaStream_t st,
+                     int bnOverride, bool allowSplit, float* ws);
+cudaError_t launchSplitReduceSilu(const float* ws, int splits, int M, int N, void* out, cudaStream_t st);
+
 // out[i] = bf16(sum over s < splits of ws[s * elems + i]); elems % 4 == 0.
 cudaError_t launchSplitReduce(const float* ws, int splits, size_t elems, void* out, cudaStream_t st);
 

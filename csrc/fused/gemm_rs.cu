@@ -22,10 +22,13 @@
 #include "fused/gemm_launch.cuh"
 #include "kernels/collectives.cuh"
 #include "runtime/comm.h"
+#include "runtime/launch.h"
 #include "vccl_tp.h"
 
 namespace vccl {
 namespace fused {
+
+int smallRows();  // ag_gemm.cu
 
 using dev::DevComm;
 
@@ -163,6 +166,36 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
     return e == cudaSuccess ? vcclSuccess : vcclInvalidArgument;
   }
   const int rowsPerRank = M / n;
+  if (M <= fused::smallRows() && (static_cast<size_t>(rowsPerRank) * N * 2) % 8 == 0) {
+    // Few rows: (split-K) GEMM into local scratch, then the LL or push
+    // reduce-scatter; cheaper than the persistent fused kernel at this size.
+    const size_t pBytes = (static_cast<size_t>(M) * N * 2 + 255) / 256 * 256;
+    const size_t wsBytes = gemm::gemmAutoScratchBytes(M, N, K, bnEnv, true);
+    gemm::Scratch sc;
+    if (!gemm::acquireScratch(s, pBytes + wsBytes, &sc)) {
+      VERR("vcclGemmReduceScatter: cannot allocate %zu bytes of scratch", pBytes + wsBytes);
+      return vcclSystemError;
+    }
+    char* p = static_cast<char*>(sc.p);
+    cudaError_t e = gemm::gemmAuto(A, W, p, M, N, K, false, s, bnEnv, true, reinterpret_cast<float*>(p + pBytes));
+    if (e == cudaSuccess) {
+      dev::CollArgs a{};
+      a.send = p;
+      a.recv = static_cast<char*>(out);
+      a.count = static_cast<size_t>(rowsPerRank) * N;
+      a.root = -1;
+      a.premul = 0;
+      a.avg = 0;
+      a.scalar = 1.0;
+      e = launchReduceScatter(launchCtxFor(*comm->dev, s), vcclBfloat16, dev::kSum, a);
+    }
+    gemm::releaseScratch(sc);
+    if (e != cudaSuccess) {
+      VERR("vcclGemmReduceScatter (small): %s", cudaGetErrorString(e));
+      return vcclInvalidArgument;
+    }
+    return vcclSuccess;
+  }
   const size_t slotBytes = (static_cast<size_t>(rowsPerRank) * N * 2 + 255) / 256 * 256;
   const dev::DevComm& dc = comm->dev->dc;
   if (slotBytes * n > dc.fusedBytes / 2) {

@@ -23,6 +23,18 @@
 #include "runtime/launch.h"
 
 namespace vccl {
+
+LaunchCtx launchCtxFor(const DeviceState& ds, cudaStream_t s) {
+  LaunchCtx lc;
+  lc.dc = ds.dc;
+  lc.stream = s;
+  lc.nblocks = ds.nblocks;
+  lc.nvls = ds.nvls;
+  lc.llMax = ds.llMaxBytes;
+  lc.llBlocks = ds.llBlocks;
+  return lc;
+}
+
 namespace {
 
 enum class Kind { AllReduce, Reduce, AllGather, ReduceScatter, Broadcast, Gather, Scatter, AllToAllv, Send, Recv };
@@ -218,16 +230,7 @@ vcclResult_t prepareBuffers(HostOp& h, Staging& st) {
   return vcclSuccess;
 }
 
-LaunchCtx launchCtx(vcclComm_t comm, cudaStream_t s) {
-  LaunchCtx lc;
-  lc.dc = comm->dev->dc;
-  lc.stream = s;
-  lc.nblocks = comm->dev->nblocks;
-  lc.nvls = comm->dev->nvls;
-  lc.llMax = comm->dev->llMaxBytes;
-  lc.llBlocks = comm->dev->llBlocks;
-  return lc;
-}
+LaunchCtx launchCtx(vcclComm_t comm, cudaStream_t s) { return launchCtxFor(*comm->dev, s); }
 
 vcclResult_t cudaToVccl(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return vcclSuccess;

@@ -22,6 +22,10 @@ struct LaunchCtx {
   int llBlocks;    // grid of every LL kernel (fixed per communicator)
 };
 
+struct DeviceState;
+// Launch context of a communicator's device state on stream s.
+LaunchCtx launchCtxFor(const DeviceState& ds, cudaStream_t s);
+
 inline bool aligned8(const void* a, const void* b) {
   return ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 7u) == 0;
 }
