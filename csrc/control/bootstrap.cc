@@ -54,13 +54,13 @@ uint64_t hostFingerprint() {
   return h;
 }
 
-vcclResult_t makeUniqueId(vcclUniqueId* out) {
+vcclResult_t makeUniqueId(vcclUniqueId* out, bool allowFixed) {
   memset(out->internal, 0, sizeof(out->internal));
   IdLayout id{};
   id.magic = kIdMagic;
   id.version = VCCL_VERSION_CODE;
 
-  std::string fixed = envStr("VCCL_COMM_ID", "");
+  std::string fixed = allowFixed ? envStr("VCCL_COMM_ID", "") : std::string();
   if (!fixed.empty()) {
     // Every rank computes the same id; rank 0 binds the port when it joins.
     if (parseEndpoint(fixed.c_str(), &id.root) != vcclSuccess) {

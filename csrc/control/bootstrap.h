@@ -37,7 +37,9 @@ static_assert(sizeof(IdLayout) <= VCCL_UNIQUE_ID_BYTES, "id too large");
 constexpr uint32_t kIdMagic = 0x3262766bu;            // "kvb2" little endian
 constexpr uint64_t kEnvNonce = 0x454e562d43434c56ull;  // ids from VCCL_COMM_ID
 
-vcclResult_t makeUniqueId(vcclUniqueId* out);
+// allowFixed: honour VCCL_COMM_ID (the job's first communicator).  Ids made
+// for communicators created later (split) always get a fresh port.
+vcclResult_t makeUniqueId(vcclUniqueId* out, bool allowFixed = true);
 
 struct RankInfo {
   uint64_t hostHash;

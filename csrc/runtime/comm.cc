@@ -292,7 +292,7 @@ vcclResult_t vcclCommSplit(vcclComm_t comm, int color, int key, vcclComm_t* newc
   // The first member of each group creates the id; everyone publishes.
   std::vector<vcclUniqueId> ids(comm->nranks);
   memset(ids.data(), 0, ids.size() * sizeof(vcclUniqueId));
-  if (myNew == 0) VTRY(vcclGetUniqueId(&ids[comm->rank]));
+  if (myNew == 0) VTRY(vccl::makeUniqueId(&ids[comm->rank], false));
   VTRY(comm->bootstrap->allGather(ids.data(), sizeof(vcclUniqueId)));
   if (color < 0) return vcclSuccess;
   if (comm->dev) cudaSetDevice(comm->dev->device);

@@ -1,0 +1,192 @@
+# SPDX-License-Identifier: Apache-2.0
+"""Python layer on the CPU (no GPU): bindings, control-plane communicators in
+several processes, single-rank host collectives, and the host-side helpers of
+the fused ops.
+
+Multi-process cases run control-plane-only communicators (VCCL_NO_DEVICE=1)
+over the TCP bootstrap on 127.0.0.1, as the reference's Python suites run
+their ranks as local processes (reference: python/tests/test_bindings.py).
+"""
+
+import multiprocessing as mp
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import free_port
+
+
+def _env(port=None):
+    os.environ["VCCL_NO_DEVICE"] = "1"
+    os.environ["VCCL_SOCKET_ADDR"] = "127.0.0.1"
+    os.environ.setdefault("VCCL_DEBUG", "ERROR")
+    if port is not None:
+        os.environ["VCCL_COMM_ID"] = f"127.0.0.1:{port}"
+
+
+def test_metadata():
+    import vkccl_b200 as v
+    from vkccl_b200._lib import lib
+
+    assert v.version() > 0
+    sizes = {v.DataType.INT8: 1, v.DataType.UINT8: 1, v.DataType.INT32: 4, v.DataType.UINT32: 4,
+             v.DataType.INT64: 8, v.DataType.UINT64: 8, v.DataType.FLOAT16: 2, v.DataType.FLOAT32: 4,
+             v.DataType.FLOAT64: 8, v.DataType.BFLOAT16: 2}
+    for dt, sz in sizes.items():
+        assert v.type_size(dt) == sz
+    for code in range(7):
+        assert lib().vcclGetErrorString(code)
+
+
+def test_unique_id_roundtrip():
+    _env()
+    import vkccl_b200 as v
+
+    uid = v.get_unique_id()
+    assert len(uid.to_bytes()) == v.UNIQUE_ID_BYTES
+    assert v.UniqueId.from_hex(uid.hex()).to_bytes() == uid.to_bytes()
+    assert v.UniqueId.from_bytes(uid.to_bytes()).hex() == uid.hex()
+    with pytest.raises(ValueError):
+        v.UniqueId.from_bytes(b"short")
+
+
+def test_comm_id_derives_same_id():
+    port = free_port()
+    _env(port)
+    import vkccl_b200 as v
+
+    try:
+        a, b = v.get_unique_id(), v.get_unique_id()
+        assert a.to_bytes() == b.to_bytes()
+    finally:
+        os.environ.pop("VCCL_COMM_ID", None)
+
+
+def _rank_body(rank, nranks, port, q):
+    try:
+        _env(port)
+        import vkccl_b200 as v
+
+        uid = v.get_unique_id()
+        comm = v.Communicator(nranks, uid, rank)
+        assert comm.rank == rank and comm.nranks == nranks
+        # even / odd split, ranks ordered by key (reverse rank)
+        sub = comm.split(rank % 2, nranks - rank)
+        members = [r for r in range(nranks) if r % 2 == rank % 2]
+        exp_rank = sorted(members, key=lambda r: nranks - r).index(rank)
+        assert sub is not None and sub.nranks == len(members) and sub.rank == exp_rank, (sub.nranks, sub.rank)
+        # NOCOLOR takes part and gets no communicator
+        none = comm.split(-1 if rank == 0 else 0, rank)
+        assert (none is None) == (rank == 0)
+        op = comm.create_premul_sum(0.5, v.DataType.FLOAT32)
+        comm.destroy_op(op)
+        assert comm.async_error() == 0
+        if none is not None:
+            none.destroy()
+        sub.destroy()
+        comm.destroy()
+        q.put((rank, "ok"))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e)))
+
+
+def test_control_plane_multiprocess():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    n = 3
+    port = free_port()
+    ps = [ctx.Process(target=_rank_body, args=(r, n, port, q)) for r in range(n)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(n))
+    for p in ps:
+        p.join(timeout=60)
+    assert all(v == "ok" for v in res.values()), res
+
+
+def test_single_rank_host_collectives():
+    _env()
+    import vkccl_b200 as v
+
+    comm = v.Communicator(1, v.get_unique_id(), 0)
+    try:
+        x = np.arange(1, 1025, dtype=np.float32)
+        y = np.empty_like(x)
+        comm.all_reduce(x, y)
+        assert np.array_equal(x, y)
+        comm.all_reduce(x, y, op=v.RedOp.AVG)
+        assert np.array_equal(x, y)
+        op = comm.create_premul_sum(2.0, v.DataType.FLOAT32)
+        comm.all_reduce(x, y, op=op)
+        assert np.array_equal(2 * x, y)
+        comm.destroy_op(op)
+        g = np.empty_like(x)
+        comm.all_gather(x, g)
+        assert np.array_equal(x, g)
+        t = torch.arange(64, dtype=torch.int32)
+        comm.broadcast(t, 0)
+        assert torch.equal(t, torch.arange(64, dtype=torch.int32))
+    finally:
+        comm.destroy()
+
+
+def test_interleave_gate_up_layout():
+    from vkccl_b200.ops.gemm import interleave_gate_up
+
+    i, k = 64, 8
+    wg = torch.arange(i * k, dtype=torch.float32).reshape(i, k)
+    wu = -wg
+    w = interleave_gate_up(wg, wu)
+    assert w.shape == (2 * i, k)
+    for blk in range(i // 16):
+        assert torch.equal(w[32 * blk:32 * blk + 16], wg[16 * blk:16 * blk + 16])
+        assert torch.equal(w[32 * blk + 16:32 * blk + 32], wu[16 * blk:16 * blk + 16])
+    with pytest.raises(ValueError):
+        interleave_gate_up(wg[:10], wu[:10])
+
+
+def _e4m3_rne(v: np.ndarray) -> np.ndarray:
+    """Round float32 values (|v| <= 448) to e4m3 with ties to even, from first principles."""
+    out = np.zeros_like(v)
+    a = np.abs(v).astype(np.float64)
+    nz = a > 0
+    e = np.floor(np.log2(np.where(nz, a, 1.0)))
+    e = np.maximum(e, -6.0)            # subnormals share the smallest exponent
+    step = 2.0 ** (e - 3)              # 3 mantissa bits
+    q = a / step
+    r = np.floor(q)
+    frac = q - r
+    r = np.where((frac > 0.5) | ((frac == 0.5) & (r % 2 == 1)), r + 1, r)
+    out = np.sign(v) * np.minimum(r * step, 448.0)
+    return out.astype(np.float32)
+
+
+def test_fp8_block_quant_reference_is_round_to_nearest_even():
+    from vkccl_b200.ops.moe import quantize_dequantize_reference
+
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(16, 512, generator=g).bfloat16()
+    got = quantize_dequantize_reference(x).float().numpy()
+    xf = x.float().numpy().reshape(16, 4, 128)
+    amax = np.abs(xf).max(-1, keepdims=True)
+    scale = np.where(amax > 0, amax / np.float32(448.0), np.float32(1.0)).astype(np.float32)
+    q = _e4m3_rne((xf / scale).astype(np.float32))
+    ref = torch.from_numpy((q * scale).reshape(16, 512)).bfloat16().float().numpy()
+    assert np.array_equal(got, ref)
+
+
+def test_moe_default_capacity():
+    from vkccl_b200.ops.moe import default_capacity
+
+    assert default_capacity(4096, 2, 8) == 8192  # T * topk dominates
+    assert default_capacity(4096, 2, 1) == 16384
+    assert default_capacity(0, 2, 8) == 1
+
+
+def test_mlp_flops():
+    from vkccl_b200.models.llama_mlp import MLPConfig
+
+    cfg = MLPConfig(4096, 14336)
+    assert cfg.hidden == 4096 and cfg.intermediate == 14336
