@@ -190,3 +190,46 @@ def test_mlp_flops():
 
     cfg = MLPConfig(4096, 14336)
     assert cfg.hidden == 4096 and cfg.intermediate == 14336
+
+
+def test_parallel_layout_and_buckets():
+    from vkccl_b200.parallel import group_layout, plan_buckets
+
+    assert [group_layout(8, r, 4) for r in (0, 3, 4, 7)] == [(0, 0, 0, 0), (0, 3, 3, 0), (1, 0, 0, 1), (1, 3, 3, 1)]
+    with pytest.raises(ValueError):
+        group_layout(8, 0, 3)
+    f32, bf = torch.float32, torch.bfloat16
+    # visited last to first; a dtype change or a full bucket closes it
+    assert plan_buckets([10, 20, 1000, 5], [f32, f32, f32, bf], 200) == [[3], [2], [1, 0]]
+    assert plan_buckets([4, 4, 4], [f32] * 3, 32) == [[2, 1], [0]]
+
+
+def _groups_body(rank, nranks, port, q):
+    try:
+        _env(port)
+        import vkccl_b200 as v
+        from vkccl_b200.parallel import ParallelGroups
+
+        comm = v.Communicator(nranks, v.get_unique_id(), rank)
+        pg = ParallelGroups.build(comm, 2)
+        assert (pg.tp.nranks, pg.tp.rank) == (2, rank % 2)
+        assert (pg.dp.nranks, pg.dp.rank) == (nranks // 2, rank // 2)
+        pg.destroy()
+        comm.destroy()
+        q.put((rank, "ok"))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e)))
+
+
+def test_parallel_groups_multiprocess():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    n = 4
+    port = free_port()
+    ps = [ctx.Process(target=_groups_body, args=(r, n, port, q)) for r in range(n)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(n))
+    for p in ps:
+        p.join(timeout=60)
+    assert all(v == "ok" for v in res.values()), res
