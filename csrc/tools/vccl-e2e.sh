@@ -1,0 +1,29 @@
+#!/usr/bin/env bash
+# SPDX-License-Identifier: Apache-2.0
+# Single-node bring-up check: run vccl-bench with --check for every op at
+# 1, 2, 4 and 8 ranks (one forked rank per GPU), each run on a fresh
+# VCCL_COMM_ID port so a previous run's socket cannot collide with it.
+#
+#   csrc/tools/vccl-e2e.sh [max bytes] [iters]          (defaults 64M, 20)
+set -euo pipefail
+here=$(cd "$(dirname "$0")/../.." && pwd)
+bench=$here/vkccl_b200/_native/bin/vccl-bench
+max=${1:-64M}
+iters=${2:-20}
+ngpu=$(nvidia-smi -L 2>/dev/null | wc -l || echo 0)
+port=${VCCL_PORT:-5555}
+export VCCL_SOCKET_ADDR=${VCCL_SOCKET_ADDR:-127.0.0.1}
+status=0
+for n in 1 2 4 8; do
+  [ "$n" -le "$ngpu" ] || continue
+  for op in allreduce allgather reducescatter broadcast; do
+    port=$((port + 1))
+    if ! VCCL_COMM_ID=127.0.0.1:$port "$bench" --launch "$n" --op "$op" -b 8 -e "$max" -f 4 \
+         --iters "$iters" --check > /tmp/vccl-e2e-$n-$op.log 2>&1; then
+      echo "FAIL n=$n $op (see /tmp/vccl-e2e-$n-$op.log)"; status=1
+    else
+      echo "ok   n=$n $op"
+    fi
+  done
+done
+exit $status

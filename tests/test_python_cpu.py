@@ -233,3 +233,49 @@ def test_parallel_groups_multiprocess():
     for p in ps:
         p.join(timeout=60)
     assert all(v == "ok" for v in res.values()), res
+
+
+def test_compat_package_names():
+    import importlib
+    import sys
+
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "compat"))
+    try:
+        sys.modules.pop("vccl", None)
+        vccl = importlib.import_module("vccl")
+        import vkccl_b200
+
+        assert vccl.Communicator is vkccl_b200.Communicator
+        for name in ("UniqueId", "DataType", "RedOp", "VcclError", "get_unique_id", "group_start", "group_end"):
+            assert getattr(vccl, name) is getattr(vkccl_b200, name)
+        assert vccl.UNIQUE_ID_BYTES == 128
+        tc = importlib.import_module("vccl.torch_comm")
+        assert tc.VcclCommunicator.__name__ == "VcclCommunicator"
+    finally:
+        sys.path.pop(0)
+        sys.modules.pop("vccl", None)
+        sys.modules.pop("vccl.torch_comm", None)
+
+
+def test_vllm_plugin_patches_cuda_platform(monkeypatch):
+    import sys
+    import types
+
+    from vkccl_b200.integration import vllm_plugin
+
+    class FakeCudaPlatform:
+        @classmethod
+        def get_device_communicator_cls(cls):
+            return "vllm.distributed.device_communicators.cuda_communicator.CudaCommunicator"
+
+    fake_cuda = types.ModuleType("vllm.platforms.cuda")
+    fake_cuda.CudaPlatform = FakeCudaPlatform
+    fake_platforms = types.ModuleType("vllm.platforms")
+    fake_platforms.cuda = fake_cuda
+    monkeypatch.setitem(sys.modules, "vllm.platforms", fake_platforms)
+    monkeypatch.setitem(sys.modules, "vllm.platforms.cuda", fake_cuda)
+    monkeypatch.setenv("VKCCL_VLLM", "0")
+    assert vllm_plugin.register() is False
+    monkeypatch.setenv("VKCCL_VLLM", "1")
+    assert vllm_plugin.register() is True
+    assert FakeCudaPlatform.get_device_communicator_cls() == "vkccl_b200.torch_comm.VcclCommunicator"
