@@ -48,3 +48,20 @@ clean:
 	rm -rf $(OUT)/obj $(OUT)/bin $(OUT)/libvccl.so
 
 .PHONY: all clean
+
+# Host-only control plane (no CUDA) built with sanitizers for the CPU race
+# checks: `make sanitize` -> bin/test_bootstrap_threads_{tsan,asan}.
+CTRL_SRC := csrc/common/types.cc csrc/common/env.cc csrc/common/log.cc csrc/common/net.cc csrc/control/bootstrap.cc
+SAN_FLAGS := -std=c++17 -O1 -g -Iinclude -Icsrc -pthread
+
+$(BIN)/test_bootstrap_threads_tsan: csrc/tests/test_bootstrap_threads.cc $(CTRL_SRC) $(HDRS)
+	@mkdir -p $(BIN)
+	g++ $(SAN_FLAGS) -fsanitize=thread csrc/tests/test_bootstrap_threads.cc $(CTRL_SRC) -o $@
+
+$(BIN)/test_bootstrap_threads_asan: csrc/tests/test_bootstrap_threads.cc $(CTRL_SRC) $(HDRS)
+	@mkdir -p $(BIN)
+	g++ $(SAN_FLAGS) -fsanitize=address,undefined csrc/tests/test_bootstrap_threads.cc $(CTRL_SRC) -o $@
+
+sanitize: $(BIN)/test_bootstrap_threads_tsan $(BIN)/test_bootstrap_threads_asan
+
+.PHONY: sanitize

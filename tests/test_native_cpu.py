@@ -24,3 +24,18 @@ def test_bootstrap_rejects_stray_client():
 
 def test_control_plane_suite():
     assert "control-plane: OK" in _run("test_control")
+
+
+def test_control_plane_under_sanitizers():
+    """Threaded bootstrap rounds, fd exchange and abort under TSan and ASan/UBSan."""
+    import shutil
+
+    if shutil.which("g++") is None:
+        import pytest
+
+        pytest.skip("no host C++ compiler")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    subprocess.run(["make", "-s", "sanitize"], cwd=root, check=True, capture_output=True, timeout=600)
+    for name in ("test_bootstrap_threads_tsan", "test_bootstrap_threads_asan"):
+        out = _run(name, timeout=300)
+        assert "bootstrap-threads: OK" in out
