@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include "common/log.h"
+#include "common/trace.h"
 #include "fused/gemm_launch.cuh"
 #include "kernels/collectives.cuh"
 #include "runtime/comm.h"
@@ -177,6 +178,7 @@ using namespace vccl;
 
 extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, void* out, int M, int N, int K,
                                           int siluMul, vcclComm_t comm, vcclStream_t stream) {
+  TraceRange trace("vccl AllGatherGemm");
   if (comm == nullptr || xShard == nullptr || W == nullptr || out == nullptr || M <= 0 || N <= 0 || K <= 0)
     return vcclInvalidArgument;
   if ((N % 32) != 0 || (K % 8) != 0 ||

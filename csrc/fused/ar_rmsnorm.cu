@@ -23,6 +23,7 @@
 #include <cuda_runtime.h>
 
 #include "common/log.h"
+#include "common/trace.h"
 #include "kernels/collectives.cuh"
 #include "runtime/comm.h"
 #include "vccl_tp.h"
@@ -282,6 +283,7 @@ using namespace vccl;
 extern "C" vcclResult_t vcclAllReduceAddRMSNorm(const void* partial, void* residual, const void* weight, void* out,
                                                 size_t rows, size_t hidden, float eps, vcclDataType_t datatype,
                                                 vcclComm_t comm, vcclStream_t stream) {
+  TraceRange trace("vccl AllReduceAddRMSNorm");
   if (comm == nullptr || partial == nullptr || residual == nullptr || weight == nullptr || out == nullptr)
     return vcclInvalidArgument;
   if (datatype != vcclBfloat16 || hidden % 32 != 0 || hidden > 32768 || rows == 0) {

@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 
 #include "common/log.h"
+#include "common/trace.h"
 #include "fused/gemm_launch.cuh"
 #include "kernels/collectives.cuh"
 #include "runtime/comm.h"
@@ -143,6 +144,7 @@ using namespace vccl;
 
 extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void* out, int M, int N, int K,
                                               vcclComm_t comm, vcclStream_t stream) {
+  TraceRange trace("vccl GemmReduceScatter");
   if (comm == nullptr || A == nullptr || W == nullptr || out == nullptr || M <= 0 || N <= 0 || K <= 0)
     return vcclInvalidArgument;
   if ((N % 16) != 0 || (K % 8) != 0 || (reinterpret_cast<uintptr_t>(out) & 15u) != 0) return vcclInvalidArgument;

@@ -37,6 +37,7 @@
 #include <cuda_runtime.h>
 
 #include "common/log.h"
+#include "common/trace.h"
 #include "kernels/collectives.cuh"
 #include "runtime/comm.h"
 #include "vccl_tp.h"
@@ -570,6 +571,7 @@ using namespace vccl;
 extern "C" vcclResult_t vcclMoeDispatchFp8(const void* x, const int* topkIds, const float* topkW, void* recvX,
                                            int* recvMeta, float* recvW, int* recvCount, int T, int H, int topk,
                                            int numExperts, int capacity, vcclComm_t comm, vcclStream_t stream) {
+  TraceRange trace("vccl MoeDispatchFp8");
   if (comm == nullptr || !x || !topkIds || !topkW || !recvX || !recvMeta || !recvW || !recvCount) {
     return vcclInvalidArgument;
   }
@@ -620,6 +622,7 @@ extern "C" vcclResult_t vcclMoeDispatchFp8(const void* x, const int* topkIds, co
 extern "C" vcclResult_t vcclMoeCombine(const void* expertOut, const int* recvMeta, const float* recvW,
                                        const int* recvCount, void* out, int T, int H, int topk, int capacity,
                                        vcclComm_t comm, vcclStream_t stream) {
+  TraceRange trace("vccl MoeCombine");
   if (comm == nullptr || !expertOut || !recvMeta || !recvW || !recvCount || !out) return vcclInvalidArgument;
   if (T < 0 || H <= 0 || H % 128 != 0 || topk < 1 || topk > moe::kMaxTopk || capacity < 1 ||
       static_cast<long long>(T) * topk > capacity || !moe::aligned16(expertOut) || !moe::aligned16(out) ||

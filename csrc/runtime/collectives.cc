@@ -19,6 +19,7 @@
 
 #include "common/env.h"
 #include "common/log.h"
+#include "common/trace.h"
 #include "runtime/comm.h"
 #include "runtime/launch.h"
 
@@ -354,12 +355,39 @@ bool usesP2pKernel(Kind k) {
 }
 
 // Launch one non-p2p collective (device pointers by now).
+const char* kindName(Kind k) {
+  switch (k) {
+    case Kind::AllReduce: return "vccl AllReduce";
+    case Kind::Reduce: return "vccl Reduce";
+    case Kind::AllGather: return "vccl AllGather";
+    case Kind::ReduceScatter: return "vccl ReduceScatter";
+    case Kind::Broadcast: return "vccl Broadcast";
+    case Kind::Gather: return "vccl Gather";
+    case Kind::Scatter: return "vccl Scatter";
+    case Kind::AllToAllv: return "vccl AllToAllv";
+    case Kind::Send: return "vccl Send";
+    case Kind::Recv: return "vccl Recv";
+  }
+  return "vccl";
+}
+
+const char* algoName(ArAlgo a) {
+  switch (a) {
+    case ArAlgo::LL: return "one-shot LL";
+    case ArAlgo::LL2: return "two-hop LL";
+    case ArAlgo::Nvls: return "NVLS multimem";
+    case ArAlgo::TwoShot: return "two-shot";
+  }
+  return "?";
+}
+
 vcclResult_t launchColl(const HostOp& h) {
   vcclComm_t comm = h.comm;
   const size_t es = vcclTypeSize(h.dt);
   const int n = comm->nranks;
   cudaStream_t s = h.stream;
   if (h.count == 0) return vcclSuccess;
+  TraceRange trace(kindName(h.kind));
   if (n == 1) {
     double scale = h.premul ? h.scalar : 1.0;
     switch (h.kind) {
@@ -375,6 +403,7 @@ vcclResult_t launchColl(const HostOp& h) {
   switch (h.kind) {
     case Kind::AllReduce: {
       ArAlgo algo = pickAllReduce(h, h.count * es);
+      noteAlgorithm("all-reduce", algoName(algo), n, h.count * es);
       cudaError_t e = launchAllReduce(lc, algo, h.dt, h.redKind, a);
       if (e == cudaErrorInvalidValue && algo != ArAlgo::TwoShot) {
         cudaGetLastError();
@@ -386,14 +415,17 @@ vcclResult_t launchColl(const HostOp& h) {
       a.root = h.root;
       return cudaToVccl(launchAllReduce(lc, ArAlgo::TwoShot, h.dt, h.redKind, a), "reduce launch");
     case Kind::ReduceScatter:
+      noteAlgorithm("reduce-scatter", h.count * es <= lc.llMax ? "LL" : "push", n, h.count * es);
       return cudaToVccl(launchReduceScatter(lc, h.dt, h.redKind, a), "reduce-scatter launch");
     case Kind::AllGather:
+      noteAlgorithm("all-gather", h.count * es <= lc.llMax ? "LL" : "pull", n, h.count * es);
       return cudaToVccl(launchAllGather(lc, h.send, h.recv, h.count * es), "all-gather launch");
     case Kind::Broadcast: {
       const size_t bytes = h.count * es;
       std::string force = envStr("VCCL_BROADCAST_ALGO", "");
       // The root sends S through the switch instead of (n-1) S to the peers.
       bool nv = lc.nvls && (force == "nvls" || (force.empty() && n >= 3 && bytes >= (256u << 10)));
+      noteAlgorithm("broadcast", bytes <= lc.llMax ? "LL" : nv ? "NVLS multimem" : "pull", n, bytes);
       return cudaToVccl(launchBroadcast(lc, h.send, h.recv, bytes, h.root, nv), "broadcast launch");
     }
     default: return vcclInternalError;
