@@ -158,7 +158,7 @@ def run_vccl(args) -> int:
         extras["latency_by_tokens"] = sweep
         extras["breakdown_us"] = breakdown(mlp, x, world, measure)
         if world > 1:
-            extras["allreduce_busbw_GBps"] = allreduce_busbw(comm, world, measure)
+            extras["allreduce_busbw_GBps"] = allreduce_busbw(comm, world, measure, flush)
     flops = mlp.flops(args.tokens)
     if rank == 0:
         line = {
@@ -219,7 +219,7 @@ def breakdown(mlp, x, world, measure):
     return {k: round(v, 2) for k, v in out.items()}
 
 
-def allreduce_busbw(comm, world, measure):
+def allreduce_busbw(comm, world, measure, flush):
     import torch
     import torch.distributed as dist
 
@@ -229,6 +229,12 @@ def allreduce_busbw(comm, world, measure):
         b = torch.empty_like(a)
         f = 2.0 * (world - 1) / world
         tv = measure(lambda: comm.all_reduce(a, b), 10, 3)
+        if os.environ.get("VKCCL_BENCH_STEPS"):
+            from vkccl_b200.utils.timing import time_steps
+
+            steps = time_steps(lambda: comm.all_reduce(a, b), 10, flush)
+            print(json.dumps({"rank": dist.get_rank(), "size": size, "steps_us": [round(t, 1) for t in steps]}),
+                  file=sys.stderr, flush=True)
         tn = measure(lambda: dist.all_reduce(a), 10, 3)
         out[f"{size >> 20}MiB"] = {"vccl": round(size / (tv * 1e3) * f, 1), "nccl": round(size / (tn * 1e3) * f, 1)}
     return out

@@ -56,17 +56,37 @@ int pickBN(int M, int N) {
   return 32;
 }
 
+// Decode shapes (at most two 128-row tiles) stream the weights once; their
+// time is set by how evenly the work spreads over the SMs.  Split K so that
+// tiles x splits fills whole waves of the persistent grid, keeping at least
+// 4 k-blocks per split and the fp32 partials below a quarter of the weight
+// bytes (M x N x splits x 4 <= N x K x 2 / 4).
 SplitPlan planSplitK(int M, int N, int K) {
   const int sms = smCount();
   const int tilesM = (M + kBM - 1) / kBM;
+  if (tilesM > 2) return {0, 1};
   const int numK = (K + kBK - 1) / kBK;
   const int tiles = tilesM * ((N + 127) / 128);
-  if (tilesM > 2 || tiles * 2 > sms) return {0, 1};
-  int splits = sms / tiles;
-  if (splits > numK / 4) splits = numK / 4;  // at least 4 k-blocks per split
-  if (splits > 16) splits = 16;
-  if (splits < 2) return {0, 1};
-  return {128, splits};
+  int maxS = numK / 4;
+  if (maxS > 16) maxS = 16;
+  const int byPartials = K / (8 * M);
+  if (maxS > byPartials) maxS = byPartials;
+  auto waste = [&](int s) {
+    const int units = tiles * s;
+    const int waves = (units + sms - 1) / sms;
+    return static_cast<double>(waves) * sms / units;
+  };
+  int best = 1;
+  double bestWaste = waste(1);
+  for (int s = 2; s <= maxS; s++) {
+    const double w = waste(s);
+    if (w < bestWaste - 0.03) {
+      best = s;
+      bestWaste = w;
+    }
+  }
+  if (best < 2) return {0, 1};
+  return {128, best};
 }
 
 namespace {

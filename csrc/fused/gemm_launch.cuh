@@ -39,7 +39,8 @@ cudaError_t launchGemm(const void* A, const void* B, int M, int N, int K, const 
                        cudaStream_t st, int bnOverride, int gridCap, int splits = 1, int* flag = nullptr) {
   const int bn = bnOverride > 0 ? bnOverride : pickBN(M, N);
   CUtensorMap ma, mb;
-  if (!makeMapKMajor(&ma, A, M, K, kBM) || !makeMapKMajor(&mb, B, N, K, bn)) return cudaErrorInvalidValue;
+  const int aRows = M >= kBM ? kBM : (M + 7) / 8 * 8;
+  if (!makeMapKMajor(&ma, A, M, K, aRows) || !makeMapKMajor(&mb, B, N, K, bn)) return cudaErrorInvalidValue;
   GemmShape s;
   s.M = M;
   s.N = N;
@@ -47,6 +48,7 @@ cudaError_t launchGemm(const void* A, const void* B, int M, int N, int K, const 
   s.tilesM = (M + kBM - 1) / kBM;
   s.tilesN = (N + bn - 1) / bn;
   s.splits = splits < 1 ? 1 : splits;
+  s.aRows = aRows;
   if (s.splits > s.numK()) return cudaErrorInvalidValue;
   int grid = s.tilesM * s.tilesN * s.splits;
   if (gridCap < 0) {

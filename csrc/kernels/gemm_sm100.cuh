@@ -66,6 +66,11 @@ struct GemmShape {
   int M, N, K;
   int tilesM, tilesN;
   int splits;  // K splits (1: every tile covers all of K)
+  // Rows of A the TMA box carries (a multiple of 8, at most kBM).  Decode
+  // shapes load only their M rows instead of a zero-filled 128-row tile; the
+  // MMA still reads 128 rows, and the accumulator rows past M are never
+  // stored.
+  int aRows;
   __host__ __device__ int numK() const { return (K + kBK - 1) / kBK; }
 };
 
@@ -330,7 +335,7 @@ __global__ void __launch_bounds__(ctaThreads<Hooks>(), 1)
           }
           uint8_t* a = smem + stage * L::kStageBytes;
           uint8_t* b = a + L::kABytes;
-          sm100::mbarArriveExpectTx(&fullBar[stage], L::kStageBytes);
+          sm100::mbarArriveExpectTx(&fullBar[stage], static_cast<uint32_t>(s.aRows * kBK * 2 + L::kBBytes));
           sm100::tmaLoad2d(a, &mapA, &fullBar[stage], kb * kBK, ti.row0);
           sm100::tmaLoad2d(b, &mapB, &fullBar[stage], kb * kBK, ti.col0);
           issued++;

@@ -65,8 +65,8 @@ def test_no_alloc_rejects_oversized_scratch():
     if gpu_count() == 0:
         pytest.skip("no GPU")
     h = _lib()
-    # 2 row tiles x 10 column tiles -> 7 K splits x 256 x 1280 fp32 = 9.2 MB > 8 MiB.
-    m, n, k = 256, 1280, 8192
+    # 2 row tiles x 20 column tiles, K split 11 ways -> 256 x 2560 x 11 fp32 = 28.8 MB > 8 MiB.
+    m, n, k = 256, 2560, 32768
     a = torch.zeros(m, k, dtype=torch.bfloat16, device="cuda")
     w = torch.zeros(n, k, dtype=torch.bfloat16, device="cuda")
     c = torch.zeros(m, n, dtype=torch.bfloat16, device="cuda")

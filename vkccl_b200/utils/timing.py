@@ -30,17 +30,31 @@ class L2Flusher:
         self.buf.fill_(0)
 
 
+def gpu_lead(ms: float = 5.0) -> None:
+    """Keep the stream busy for about `ms` so the host can enqueue the timed
+    steps before the GPU reaches them: a host pause (Python GC, page faults)
+    between an event record and the next launch then cannot land inside a
+    timed interval."""
+    sleep = getattr(torch.cuda, "_sleep", None)
+    if sleep is not None:
+        sleep(int(ms * 2.0e6))  # cycles at ~2 GHz
+
+
 def time_steps(step: Callable[[], None], steps: int, flush: Optional[L2Flusher] = None,
                align_ranks: bool = False) -> list:
     """Per-step device times in microseconds (events around each step).
 
-    align_ranks: synchronize the device and barrier all ranks before every
-    step (outside the timed events), so each step starts with the ranks
-    aligned, as it would after a preceding collective.
+    The steps are enqueued behind a short GPU sleep (gpu_lead) so host
+    latency stays out of the timed intervals.  align_ranks: synchronize the
+    device and barrier all ranks before every step (outside the timed
+    events), so each step starts with the ranks aligned, as it would after a
+    preceding collective.
     """
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     torch.cuda.synchronize()
+    if not align_ranks:
+        gpu_lead(2.0 + 0.2 * steps)
     for i in range(steps):
         if align_ranks:
             import torch.distributed as dist
@@ -48,6 +62,7 @@ def time_steps(step: Callable[[], None], steps: int, flush: Optional[L2Flusher] 
             torch.cuda.synchronize()
             if dist.is_initialized() and dist.get_world_size() > 1:
                 dist.barrier()
+            gpu_lead(0.5)
         if flush is not None:
             flush()
         starts[i].record()
