@@ -52,13 +52,6 @@ __device__ __forceinline__ void groupCopy(char* dst, const char* src, size_t byt
   for (; i < n16; i += 64) dev::stG(dst + i * 16, dev::ldCG(src + i * 16));
 }
 
-// Row count up to which the fused entry points run the collective and the
-// GEMM as separate kernels (VCCL_FUSED_SMALL_M, default 512).
-int smallRows() {
-  const char* e = std::getenv("VCCL_FUSED_SMALL_M");
-  return e != nullptr ? static_cast<int>(std::strtol(e, nullptr, 10)) : 512;
-}
-
 struct AgHooks : gemm::NoHooks {
   static constexpr int kExtraWarps = 2;
   DevComm c;
@@ -209,7 +202,7 @@ extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, voi
     }
     return e == cudaSuccess ? vcclSuccess : vcclInvalidArgument;
   }
-  if (M <= fused::smallRows()) {
+  if (M <= comm->dev->fusedSmallRows) {
     // Few rows (decode, short prefills): the gather is a few hundred KB, so
     // an LL all-gather into local scratch followed by a (split-K) GEMM beats
     // the persistent fused kernel, whose per-call synchronisation and

@@ -29,7 +29,6 @@
 namespace vccl {
 namespace fused {
 
-int smallRows();  // ag_gemm.cu
 
 using dev::DevComm;
 
@@ -64,7 +63,6 @@ struct EpiPushRS {
 struct RsHooks : gemm::NoHooks {
   static constexpr int kEpiGroups = kRsEpiGroups;
   DevComm c;
-  uint32_t reduceBlocks;
   // Every rank's reduction must have consumed the previous call's pushes
   // (free[q] counts calls rank q has finished reducing).
   __device__ __forceinline__ bool beforeTiles(uint32_t*, volatile int* abortFlag) const {
@@ -99,8 +97,7 @@ struct RsHooks : gemm::NoHooks {
 };
 
 // out[rowsPerRank, N] = sum over sources of my slots.
-__global__ void __launch_bounds__(512) rsReduce(DevComm c, char* out, size_t elems, size_t slotBytes,
-                                                uint32_t gemmCtas) {
+__global__ void __launch_bounds__(512) rsReduce(DevComm c, char* out, size_t elems, size_t slotBytes) {
   __shared__ uint32_t sK;
   __shared__ int sFail;
   const int n = c.nranks, me = c.rank;
@@ -110,7 +107,6 @@ __global__ void __launch_bounds__(512) rsReduce(DevComm c, char* out, size_t ele
   }
   __syncthreads();
   const uint32_t k = sK;
-  (void)gemmCtas;
   if (threadIdx.x < n) {
     const uint32_t* done = dev::ctrlAt<uint32_t>(c, me, dev::kRsDoneOff);
     if (!dev::waitAcquire(c, done + threadIdx.x, k + 1u, dev::kWhereFused, 200 + threadIdx.x, 32)) sFail = 1;
@@ -168,7 +164,7 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
     return e == cudaSuccess ? vcclSuccess : vcclInvalidArgument;
   }
   const int rowsPerRank = M / n;
-  if (M <= fused::smallRows() && (static_cast<size_t>(rowsPerRank) * N * 2) % 8 == 0) {
+  if (M <= comm->dev->fusedSmallRows && (static_cast<size_t>(rowsPerRank) * N * 2) % 8 == 0) {
     // Few rows: (split-K) GEMM into local scratch, then the LL or push
     // reduce-scatter; cheaper than the persistent fused kernel at this size.
     const size_t pBytes = (static_cast<size_t>(M) * N * 2 + 255) / 256 * 256;
@@ -212,15 +208,13 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
   epi.ldn = N;
   fused::RsHooks hooks;
   hooks.c = dc;
-  hooks.reduceBlocks = static_cast<uint32_t>(dev::kFusedReduceBlocks);
   cudaError_t e = gemm::launchGemm(A, W, M, N, K, epi, hooks, s, bnEnv, -ctas);
   if (e != cudaSuccess) {
     VERR("vcclGemmReduceScatter GEMM launch: %s", cudaGetErrorString(e));
     return vcclInvalidArgument;
   }
   fused::rsReduce<<<dev::kFusedReduceBlocks, 512, 0, s>>>(dc, static_cast<char*>(out),
-                                                          static_cast<size_t>(rowsPerRank) * N, slotBytes,
-                                                          static_cast<uint32_t>(ctas));
+                                                          static_cast<size_t>(rowsPerRank) * N, slotBytes);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     VERR("vcclGemmReduceScatter reduce launch: %s", cudaGetErrorString(e));

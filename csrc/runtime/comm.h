@@ -58,6 +58,7 @@ struct DeviceState {
   int nblocks = 32;                // grid of barrier-based kernels
   size_t llMaxBytes = 0;           // one-hop LL threshold (per-rank payload)
   int llBlocks = 64;               // grid of every LL kernel, a multiple of 8
+  int fusedSmallRows = 512;        // fused TP calls up to this many rows run unfused
   size_t ll2MaxBytes = 0;          // two-hop LL all-reduce threshold
 };
 

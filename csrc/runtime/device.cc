@@ -245,6 +245,9 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
   long llb = envLong("VCCL_LL_BLOCKS", dev::kLLBlocks);
   llb = llb < 8 ? 8 : llb > dev::kMaxLLBlocks ? dev::kMaxLLBlocks : llb;
   ds->llBlocks = static_cast<int>(llb / 8 * 8);
+  // Every rank must pick the same path for a fused call, so this is agreed
+  // on below with the workspace sizes.
+  ds->fusedSmallRows = static_cast<int>(envLong("VCCL_FUSED_SMALL_M", 512));
 
   if (n > 1) {
     if (n > dev::kMaxRanks) {
@@ -278,15 +281,17 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
     dataBytes = roundUp(dataBytes, dataAlign);
     const size_t ctrlBytes = roundUp(dev::kCtrlBytes, gran);
     const size_t fusedBytes = roundUp(envBytes("VCCL_FUSED_BUFFSIZE", 512u << 20), gran);
-    struct Sizes { uint64_t ctrl, data, fused, llBlocks; } mine{ctrlBytes, dataBytes, fusedBytes,
-                                                                 static_cast<uint64_t>(ds->llBlocks)};
+    struct Sizes { uint64_t ctrl, data, fused, llBlocks, smallRows; } mine{
+        ctrlBytes, dataBytes, fusedBytes, static_cast<uint64_t>(ds->llBlocks),
+        static_cast<uint64_t>(static_cast<int64_t>(ds->fusedSmallRows))};
     std::vector<Sizes> all(n);
     all[me] = mine;
     VTRY(bs->allGather(all.data(), sizeof(Sizes)));
     for (const Sizes& s : all) {
-      if (s.ctrl != mine.ctrl || s.data != mine.data || s.fused != mine.fused || s.llBlocks != mine.llBlocks) {
-        VERR("ranks disagree on workspace sizes (check VCCL_BUFFSIZE, VCCL_FUSED_BUFFSIZE and VCCL_LL_BLOCKS "
-             "on every rank)");
+      if (s.ctrl != mine.ctrl || s.data != mine.data || s.fused != mine.fused || s.llBlocks != mine.llBlocks ||
+          s.smallRows != mine.smallRows) {
+        VERR("ranks disagree on workspace sizes (check VCCL_BUFFSIZE, VCCL_FUSED_BUFFSIZE, VCCL_LL_BLOCKS and "
+             "VCCL_FUSED_SMALL_M on every rank)");
         return vcclInvalidUsage;
       }
     }
