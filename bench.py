@@ -183,6 +183,7 @@ def run_vccl(args) -> int:
             "nccl_cublas_us": round(nccl_us, 2),
             "speedup_vs_nccl_cublas": round(nccl_us / value, 3),
             "achieved_tflops": round(flops / (value * 1e-6) / 1e12, 1),
+            "roofline": roofline(flops, args.tokens, world, value),
             "rel_err_vs_nccl_cublas": rel_err,
             **extras,
         }
@@ -192,6 +193,34 @@ def run_vccl(args) -> int:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+NVLINK_GBS = 770.0  # measured peer copy, GB/s per direction per GPU
+
+
+def measured_peaks():
+    """bf16 sustained TFLOP/s and HBM GB/s measured on this pool, or the stated fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops_sustained"]), float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1400.0, 6650.0, "fallback"
+
+
+def roofline(flops, tokens, world, measured_us):
+    """The layer's roofline on one GPU: the slower of its GEMM FLOPs at the
+    sustained bf16 peak and the bytes that must cross NVLink (all-gather in,
+    reduce-scatter out: (n-1)/n of the [T, 4096] bf16 activations each way)
+    at the measured per-direction link bandwidth."""
+    tflops, _, src = measured_peaks()
+    compute_us = flops / world / (tflops * 1e12) * 1e6
+    link_bytes = (world - 1) / world * tokens * HIDDEN * 2 if world > 1 else 0.0
+    link_us = link_bytes / (NVLINK_GBS * 1e9) * 1e6
+    bound = max(compute_us, link_us)
+    return {"compute_us": round(compute_us, 1), "nvlink_us": round(link_us, 1),
+            "bound": "compute" if compute_us >= link_us else "nvlink",
+            "fraction": round(bound / measured_us, 3), "peaks": src}
 
 
 def breakdown(mlp, x, world, measure):

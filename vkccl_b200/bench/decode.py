@@ -69,7 +69,17 @@ def main() -> int:
     dist.broadcast(raw, 0)
     comm = v.Communicator(world, v.UniqueId.from_bytes(bytes(raw.cpu().numpy())), rank, cuda_device=local)
     model = TPLlamaDecode(comm, DecodeConfig(layers=a.layers), seed=0)
-    out = {"bench": "llama70b_tp_decode_step", "n": world, "layers": a.layers, "results": {}}
+    # HBM roofline: every step streams this rank's weights once.
+    wbytes = sum(t.numel() * t.element_size() for L in model.layers for t in L.values())
+    hbm_gbs = 6463.7
+    try:
+        with open(os.path.join(os.environ.get("GRAFT_REPO_ROOT", "."), "MEASURED_PEAKS.json")) as f:
+            hbm_gbs = float(json.load(f)["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        pass
+    roof_us = wbytes / (hbm_gbs * 1e9) * 1e6
+    out = {"bench": "llama70b_tp_decode_step", "n": world, "layers": a.layers,
+           "weight_bytes_per_gpu": wbytes, "hbm_roofline_us": round(roof_us, 1), "results": {}}
     for b in (int(s) for s in a.batch.split(",")):
         g = torch.Generator(device="cuda").manual_seed(11 + b)  # same on every rank
         x0 = torch.randn(b, 8192, device="cuda", generator=g).bfloat16()
@@ -83,7 +93,8 @@ def main() -> int:
         t_v = graph_time(lambda: model.step(xv, xn0), a.iters, a.warmup)
         t_n = graph_time(lambda: model.step_nccl(xr, xn0), a.iters, a.warmup)
         out["results"][str(b)] = {"vccl_us": round(t_v, 1), "nccl_cublas_us": round(t_n, 1),
-                                  "speedup": round(t_n / t_v, 3), "rel_diff_final_state": err}
+                                  "speedup": round(t_n / t_v, 3), "roofline_fraction": round(roof_us / t_v, 3),
+                                  "rel_diff_final_state": err}
         if rank == 0:
             print(json.dumps({"batch": b, **out["results"][str(b)]}), flush=True)
     if rank == 0:

@@ -139,11 +139,20 @@ def main() -> int:
     recv = d.count()
     rows = torch.tensor([recv], device="cuda")
     dist.all_reduce(rows, op=dist.ReduceOp.MAX)
+    # Rooflines: the bytes each GPU must send over NVLink (pairs routed to other
+    # ranks; fp8 row + scales + metadata on dispatch, bf16 row on combine) at
+    # the measured 770 GB/s per direction.
+    remote = (world - 1) / world * T * topk
+    disp_us = remote * (H + H // 128 * 4 + 20) / 770e9 * 1e6
+    comb_us = remote * H * 2 / 770e9 * 1e6
     if rank == 0:
         print(json.dumps({"bench": "moe_dispatch_combine", "n": world, "tokens_per_rank": T, "hidden": H,
                           "topk": topk, "experts": E, "capacity": cap, "max_rows_received": int(rows.item()),
                           "vccl_dispatch_us": round(t_vd, 1), "vccl_combine_us": round(t_vc, 1),
-                          "nccl_dispatch_us": round(t_nd, 1), "nccl_combine_us": round(t_nc, 1)}), flush=True)
+                          "nccl_dispatch_us": round(t_nd, 1), "nccl_combine_us": round(t_nc, 1),
+                          "nvlink_roofline_us": {"dispatch": round(disp_us, 1), "combine": round(comb_us, 1)},
+                          "roofline_fraction": {"dispatch": round(disp_us / t_vd, 3),
+                                                "combine": round(comb_us / t_vc, 3)}}), flush=True)
     comm.destroy()
     dist.barrier()
     dist.destroy_process_group()
