@@ -67,10 +67,10 @@ class TPLlamaDecode:
                 "ln2": (1 + 0.02 * torch.randn(h, generator=g, device=device)).bfloat16(),
             })
 
-    def step(self, x: torch.Tensor, x_norm: torch.Tensor) -> torch.Tensor:
+    def step(self, x: torch.Tensor, x_norm: torch.Tensor, n_layers: int | None = None) -> torch.Tensor:
         """One decode step; x (residual) is updated in place, returns the final normed state."""
         c = self.comm
-        for L in self.layers:
+        for L in self.layers[:n_layers]:
             qkv = gemm_bf16(x_norm, L["qkv"])
             part = gemm_bf16(qkv[:, : self.attn_out].contiguous(), L["o"])
             x_norm = all_reduce_add_rms_norm(c, part, x, L["ln1"], self.cfg.eps)
@@ -79,7 +79,7 @@ class TPLlamaDecode:
             x_norm = all_reduce_add_rms_norm(c, part, x, L["ln2"], self.cfg.eps)
         return x_norm
 
-    def step_nccl(self, x: torch.Tensor, x_norm: torch.Tensor, group=None) -> torch.Tensor:
+    def step_nccl(self, x: torch.Tensor, x_norm: torch.Tensor, group=None, n_layers: int | None = None) -> torch.Tensor:
         import torch.distributed as dist
 
         n = self.comm.nranks
@@ -91,7 +91,7 @@ class TPLlamaDecode:
             xf = x.float()
             return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.cfg.eps) * weight.float()).bfloat16()
 
-        for L in self.layers:
+        for L in self.layers[:n_layers]:
             qkv = x_norm @ L["qkv"].T
             part = qkv[:, : self.attn_out] @ L["o"].T
             x_norm = ar_norm(part, L["ln1"])
