@@ -1,0 +1,51 @@
+# SPDX-License-Identifier: Apache-2.0
+"""bench.py's reference arm and JSON contract, on the CPU.
+
+The reference arm runs the reference library (its own build under
+baseline/_ref) through its own VcclCommunicator over gloo with torch CPU
+GEMMs; here on a small token count.  Skipped when that build is absent.
+"""
+
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+from conftest import ROOT, free_port
+
+
+def _reference_built():
+    return os.path.exists(os.path.join(ROOT, "baseline", "_ref", "build", "libvccl.so"))
+
+
+@pytest.mark.skipif(not _reference_built(), reason="reference build not present")
+@pytest.mark.parametrize("nranks", [1, 2])
+def test_reference_arm_prints_contract_line(nranks):
+    cmd = [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--gpus", str(nranks),
+           "--tokens", "64", "--steps", "2", "--warmup", "1"]
+    if nranks > 1:
+        cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={nranks}",
+               "--master-addr=127.0.0.1", f"--master-port={free_port()}"] + cmd[1:]
+    env = dict(os.environ, VCCL_SOCKET_ADDR="127.0.0.1")
+    p = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert p.returncode == 0, p.stderr[-3000:]
+    lines = [json.loads(line) for line in p.stdout.splitlines() if line.startswith("{")]
+    assert len(lines) == 1
+    d = lines[0]
+    assert d["impl"] == "reference" and d["n_gpus"] == nranks and d["steps"] == 2 and d["warmup"] == 1
+    assert d["metric"] == "tp_mlp_layer_latency_us" and d["value"] > 0 and d["higher_is_better"] is False
+
+
+def test_roofline_helper():
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    b = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(b)
+    flops = 2.0 * 8192 * 4096 * 14336 * 3
+    r = b.roofline(flops, 8192, 8, 500.0)
+    assert r["bound"] == "compute" and 0 < r["fraction"] < 1
+    assert r["nvlink_us"] > 0
+    assert b.roofline(flops, 8192, 1, 500.0)["nvlink_us"] == 0
