@@ -70,24 +70,10 @@ struct AgHooks : gemm::NoHooks {
   __device__ __forceinline__ void teardown(uint32_t* hs) const {
     ctrl(c.rank, dev::kAgCallsOff)[blockIdx.x] = hs[0] + 1u;
   }
-  // Row tiles start at this rank's shard and wrap around.  They are walked
-  // in groups of `groupRows` row tiles; inside a group consecutive CTAs
-  // share a weight tile, so a wave of CTAs reads each B tile once per group
-  // instead of once per row tile.
+  // Row tiles start at this rank's shard and wrap around, in groups that
+  // share weight tiles (see gemm::groupedTile).
   __device__ __forceinline__ gemm::TileInfo tileAt(const gemm::GemmShape& s, int t, int BN) const {
-    gemm::TileInfo ti;
-    const int groupTiles = groupRows * s.tilesN;
-    const int g = t / groupTiles;
-    const int rowsHere = s.tilesM - g * groupRows < groupRows ? s.tilesM - g * groupRows : groupRows;
-    const int local = t - g * groupTiles;
-    ti.tn = local / rowsHere;
-    ti.tm = (g * groupRows + local % rowsHere + startTm) % s.tilesM;
-    ti.row0 = ti.tm * gemm::kBM;
-    ti.col0 = ti.tn * BN;
-    ti.ks = 0;
-    ti.kb0 = 0;
-    ti.kb1 = s.numK();
-    return ti;
+    return gemm::groupedTile(s, t, BN, groupRows, startTm);
   }
   __device__ __forceinline__ bool beforeLoad(const gemm::TileInfo& ti, const gemm::GemmShape& s, uint32_t* hs,
                                              volatile int*) const {

@@ -88,9 +88,12 @@ __device__ __forceinline__ uint32_t packBf16(float a, float b) {
 // row segment of up to 128 B leaves as one request.  Chunks are XOR-swizzled
 // by row so both the row-per-thread writes and the row-contiguous reads are
 // free of bank conflicts.
+// Slot of (row, chunk) in a warp's stage of 32 rows x NC 16-byte chunks.
+__host__ __device__ constexpr int stageSlot(int nc, int row, int chunk) { return row * nc + (chunk ^ (row & (nc - 1))); }
+
 template <int NC>
 __device__ __forceinline__ void stagePut(uint4* st, int lane, int j, uint4 v) {
-  st[lane * NC + (j ^ (lane & (NC - 1)))] = v;
+  st[stageSlot(NC, lane, j)] = v;
 }
 
 // dst(rowInWarp, chunk, value) is called for every staged 16-byte chunk.
@@ -102,7 +105,7 @@ __device__ __forceinline__ void stageFlush(const uint4* st, int lane, Dst&& dst)
   for (int i = 0; i < NC; i++) {
     const int rr = i * kRows + lane / NC;
     const int ch = lane % NC;
-    dst(rr, ch, st[rr * NC + (ch ^ (rr & (NC - 1)))]);
+    dst(rr, ch, st[stageSlot(NC, rr, ch)]);
   }
   __syncwarp();
 }
@@ -235,6 +238,45 @@ struct EpiSiluMul {
   }
 };
 
+// Tile orders (host and device, so CPU tests can check them).
+//
+// splitKTile: N-major order (consecutive CTAs share the B tile); with
+// split-K, tile t covers output tile t % (tilesM * tilesN) over the k-blocks
+// of split t / (tilesM * tilesN).
+__host__ __device__ inline TileInfo splitKTile(const GemmShape& s, int t, int BN) {
+  TileInfo ti;
+  const int mn = s.tilesM * s.tilesN;
+  ti.ks = t / mn;
+  const int r = t - ti.ks * mn;
+  ti.tn = r / s.tilesM;
+  ti.tm = r % s.tilesM;
+  ti.row0 = ti.tm * kBM;
+  ti.col0 = ti.tn * BN;
+  const int nk = s.numK();
+  ti.kb0 = ti.ks * nk / s.splits;
+  ti.kb1 = (ti.ks + 1) * nk / s.splits;
+  return ti;
+}
+
+// groupedTile: row tiles start at startTm and wrap around; they are walked
+// in groups of groupRows row tiles, and inside a group consecutive tiles
+// share a column tile, so a wave of CTAs reads each B tile once per group.
+__host__ __device__ inline TileInfo groupedTile(const GemmShape& s, int t, int BN, int groupRows, int startTm) {
+  TileInfo ti;
+  const int groupTiles = groupRows * s.tilesN;
+  const int g = t / groupTiles;
+  const int rowsHere = s.tilesM - g * groupRows < groupRows ? s.tilesM - g * groupRows : groupRows;
+  const int local = t - g * groupTiles;
+  ti.tn = local / rowsHere;
+  ti.tm = (g * groupRows + local % rowsHere + startTm) % s.tilesM;
+  ti.row0 = ti.tm * kBM;
+  ti.col0 = ti.tn * BN;
+  ti.ks = 0;
+  ti.kb0 = 0;
+  ti.kb1 = s.numK();
+  return ti;
+}
+
 // Default policy: tiles in N-major order (consecutive CTAs share the B
 // tile), no gating, no extra warps.  `hs` is per-CTA shared scratch.
 struct NoHooks {
@@ -245,18 +287,7 @@ struct NoHooks {
   // With split-K, tile t covers output tile t % (tilesM * tilesN) over the
   // k-blocks of split t / (tilesM * tilesN).
   __device__ __forceinline__ TileInfo tileAt(const GemmShape& s, int t, int BN) const {
-    TileInfo ti;
-    const int mn = s.tilesM * s.tilesN;
-    ti.ks = t / mn;
-    const int r = t - ti.ks * mn;
-    ti.tn = r / s.tilesM;
-    ti.tm = r % s.tilesM;
-    ti.row0 = ti.tm * kBM;
-    ti.col0 = ti.tn * BN;
-    const int nk = s.numK();
-    ti.kb0 = ti.ks * nk / s.splits;
-    ti.kb1 = (ti.ks + 1) * nk / s.splits;
-    return ti;
+    return splitKTile(s, t, BN);
   }
   __device__ __forceinline__ bool beforeLoad(const TileInfo&, const GemmShape&, uint32_t*, volatile int*) const {
     return true;

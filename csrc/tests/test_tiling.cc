@@ -1,0 +1,144 @@
+// SPDX-License-Identifier: Apache-2.0
+// Index arithmetic of the GEMM kernels, checked on the host (no GPU):
+//  * splitKTile visits every (row tile, column tile, K split) exactly once and
+//    the K splits of a tile partition its k-blocks;
+//  * groupedTile (all-gather + GEMM order) is a permutation of the tiles for
+//    every shard rotation, and starts with the first rank-owned row tile;
+//  * the epilogue row stage: every (row, chunk) has its own slot, and each
+//    8-lane phase of both the row-per-thread writes and the row-contiguous
+//    reads touches 8 different 16-byte bank groups;
+//  * planSplitK keeps its bounds (4+ k-blocks per split, <= 16 splits,
+//    partials <= a quarter of the weight bytes).
+#include <cstdio>
+#include <set>
+#include <tuple>
+#include <vector>
+
+#include "fused/gemm_host.h"
+#include "kernels/gemm_sm100.cuh"
+
+using namespace vccl::gemm;
+
+namespace {
+int gFail = 0;
+#define EXPECT(c, ...)                                          \
+  do {                                                          \
+    if (!(c)) {                                                 \
+      std::fprintf(stderr, "FAIL %s:%d: ", __FILE__, __LINE__); \
+      std::fprintf(stderr, __VA_ARGS__);                        \
+      std::fprintf(stderr, "\n");                               \
+      gFail++;                                                  \
+    }                                                           \
+  } while (0)
+
+GemmShape shape(int M, int N, int K, int BN, int splits) {
+  GemmShape s{};
+  s.M = M;
+  s.N = N;
+  s.K = K;
+  s.tilesM = (M + kBM - 1) / kBM;
+  s.tilesN = (N + BN - 1) / BN;
+  s.splits = splits;
+  s.aRows = M >= kBM ? kBM : (M + 7) / 8 * 8;
+  return s;
+}
+
+void checkSplitK() {
+  for (int M : {1, 100, 128, 300, 1024})
+    for (int N : {32, 512, 3584})
+      for (int K : {64, 1000, 4096})
+        for (int BN : {32, 64, 128, 256})
+          for (int splits : {1, 2, 3, 5, 16}) {
+            GemmShape s = shape(M, N, K, BN, splits);
+            if (splits > s.numK()) continue;
+            std::vector<int> kbCover(static_cast<size_t>(s.tilesM) * s.tilesN * s.numK(), 0);
+            std::set<std::tuple<int, int, int>> seen;
+            for (int t = 0; t < s.tilesM * s.tilesN * splits; t++) {
+              TileInfo ti = splitKTile(s, t, BN);
+              EXPECT(seen.insert({ti.tm, ti.tn, ti.ks}).second, "tile visited twice");
+              EXPECT(ti.row0 == ti.tm * kBM && ti.col0 == ti.tn * BN, "tile origin");
+              EXPECT(ti.kb0 < ti.kb1, "empty K range (M=%d N=%d K=%d splits=%d)", M, N, K, splits);
+              for (int kb = ti.kb0; kb < ti.kb1; kb++)
+                kbCover[(static_cast<size_t>(ti.tm) * s.tilesN + ti.tn) * s.numK() + kb]++;
+            }
+            for (int c : kbCover) EXPECT(c == 1, "k-block covered %d times", c);
+          }
+}
+
+void checkGrouped() {
+  for (int ranks : {1, 2, 4, 8})
+    for (int shardTiles : {1, 2, 3, 8, 16})
+      for (int N : {256, 3584, 7168}) {
+        const int M = ranks * shardTiles * kBM;
+        GemmShape s = shape(M, N, 4096, 256, 1);
+        int groupRows = 1;
+        for (int g = 16; g >= 1; g /= 2)
+          if (shardTiles % g == 0) {
+            groupRows = g;
+            break;
+          }
+        for (int r = 0; r < ranks; r++) {
+          const int startTm = r * shardTiles;
+          std::set<std::pair<int, int>> seen;
+          for (int t = 0; t < s.tilesM * s.tilesN; t++) {
+            TileInfo ti = groupedTile(s, t, 256, groupRows, startTm);
+            EXPECT(ti.tm >= 0 && ti.tm < s.tilesM && ti.tn >= 0 && ti.tn < s.tilesN, "tile out of range");
+            EXPECT(seen.insert({ti.tm, ti.tn}).second, "grouped tile visited twice");
+            EXPECT(ti.kb0 == 0 && ti.kb1 == s.numK(), "grouped tiles cover all of K");
+          }
+          EXPECT(static_cast<int>(seen.size()) == s.tilesM * s.tilesN, "grouped order misses tiles");
+          EXPECT(groupedTile(s, 0, 256, groupRows, startTm).tm == startTm, "first tile is the own shard's");
+        }
+      }
+}
+
+void checkStage() {
+  for (int nc : {2, 4, 8}) {
+    std::set<int> slots;
+    for (int row = 0; row < 32; row++)
+      for (int ch = 0; ch < nc; ch++) {
+        const int sl = stageSlot(nc, row, ch);
+        EXPECT(sl >= 0 && sl < 32 * nc && slots.insert(sl).second, "stage slot collision (nc=%d)", nc);
+      }
+    // writes: lane = row, one instruction per chunk j; phases of 8 lanes
+    for (int j = 0; j < nc; j++)
+      for (int ph = 0; ph < 4; ph++) {
+        std::set<int> banks;
+        for (int l = ph * 8; l < ph * 8 + 8; l++) banks.insert(stageSlot(nc, l, j) % 8);
+        if (nc == 8) EXPECT(banks.size() == 8, "write phase bank conflict");
+      }
+    // reads: instruction i, lane -> (row i*(32/nc) + lane/nc, chunk lane%nc)
+    const int rows = 32 / nc;
+    for (int i = 0; i < nc; i++)
+      for (int ph = 0; ph < 4; ph++) {
+        std::set<int> banks;
+        for (int l = ph * 8; l < ph * 8 + 8; l++) banks.insert(stageSlot(nc, i * rows + l / nc, l % nc) % 8);
+        if (nc == 8) EXPECT(banks.size() == 8, "read phase bank conflict");
+      }
+  }
+}
+
+void checkPlan() {
+  for (int M : {1, 16, 32, 64, 128, 200, 256, 300})
+    for (int N : {512, 1536, 3584, 8192, 28672})
+      for (int K : {256, 1792, 4096, 8192, 14336}) {
+        SplitPlan p = planSplitK(M, N, K);
+        const int numK = (K + kBK - 1) / kBK;
+        if (p.splits <= 1) continue;
+        EXPECT((M + kBM - 1) / kBM <= 2, "split-K only for decode shapes");
+        EXPECT(p.splits <= 16 && numK / p.splits >= 4, "split bounds M=%d N=%d K=%d s=%d", M, N, K, p.splits);
+        EXPECT(static_cast<double>(M) * N * p.splits * 4 <= static_cast<double>(N) * K * 2 / 4 + 1,
+               "partials above a quarter of the weights (M=%d N=%d K=%d s=%d)", M, N, K, p.splits);
+        EXPECT(p.bn == 128, "split-K tile width");
+      }
+}
+}  // namespace
+
+int main() {
+  checkSplitK();
+  checkGrouped();
+  checkStage();
+  checkPlan();
+  std::printf("tiling: %s\n", gFail == 0 ? "OK" : "FAIL");
+  return gFail == 0 ? 0 : 1;
+}

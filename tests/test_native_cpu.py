@@ -39,3 +39,8 @@ def test_control_plane_under_sanitizers():
     for name in ("test_bootstrap_threads_tsan", "test_bootstrap_threads_asan"):
         out = _run(name, timeout=300)
         assert "bootstrap-threads: OK" in out
+
+
+def test_gemm_index_arithmetic():
+    """Tile orders, split-K coverage, epilogue stage slots and split plans (host build of the device math)."""
+    assert "tiling: OK" in _run("test_tiling")
