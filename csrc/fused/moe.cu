@@ -150,6 +150,19 @@ __device__ __forceinline__ void fromFp8x8(uint2 q, float (&f)[8]) {
   }
 }
 
+// Chunks of 256 elements (8 per lane) each warp keeps in flight per row.
+constexpr int kChunkUnroll = 4;
+
+// Load this lane's 16 bytes of kChunkUnroll consecutive 256-element chunks
+// (zeros past the row end) before any of them is used.
+__device__ __forceinline__ void loadChunks(const uint4* row, int c0, int H, int lane, uint4 (&raw)[kChunkUnroll]) {
+#pragma unroll
+  for (int u = 0; u < kChunkUnroll; u++) {
+    const int col = c0 + u * 256 + lane * 8;
+    raw[u] = col < H ? row[col / 8] : make_uint4(0, 0, 0, 0);
+  }
+}
+
 // Quantise the 8 values of this lane; the 16 lanes of a half-warp share one
 // 128-element block (all 32 lanes must call this).
 __device__ __forceinline__ uint2 quantize8(float (&f)[8], bool active, float* scaleOut) {
@@ -310,26 +323,28 @@ __global__ void __launch_bounds__(kThreads) moePush(DevComm c, const __nv_bfloat
       }
     }
     const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H);
-    for (int c0 = 0; c0 < H; c0 += 256) {
-      const int col = c0 + lane * 8;
-      const bool active = col < H;
-      float f[8];
-      if (active) {
-        unpackBf16x8(xr[col / 8], f);
-      } else {
+    for (int c0 = 0; c0 < H; c0 += 256 * kChunkUnroll) {
+      uint4 raw[kChunkUnroll];
+      loadChunks(xr, c0, H, lane, raw);
 #pragma unroll
-        for (int i = 0; i < 8; i++) f[i] = 0.0f;
-      }
-      float scale;
-      const uint2 q = quantize8(f, active, &scale);
-      if (active) {
+      for (int u = 0; u < kChunkUnroll; u++) {
+        if (c0 + u * 256 >= H) break;  // warp-uniform
+        const int col = c0 + u * 256 + lane * 8;
+        const bool active = col < H;
+        float f[8];
+        unpackBf16x8(raw[u], f);
+        float scale;
+        const uint2 q = quantize8(f, active, &scale);
+        if (active) {
 #pragma unroll
-        for (int k = 0; k < kMaxTopk; k++) {
-          if (pos[k] < 0) continue;
-          char* db = c.moe[dst[k]];
-          *reinterpret_cast<uint2*>(db + L.rxData + static_cast<size_t>(pos[k]) * H + col) = q;
-          if ((lane & 15) == 0)
-            *reinterpret_cast<float*>(db + L.rxScale + (static_cast<size_t>(pos[k]) * nb + col / 128) * 4) = scale;
+          for (int k = 0; k < kMaxTopk; k++) {
+            if (pos[k] < 0) continue;
+            char* db = c.moe[dst[k]];
+            *reinterpret_cast<uint2*>(db + L.rxData + static_cast<size_t>(pos[k]) * H + col) = q;
+            if ((lane & 15) == 0)
+              *reinterpret_cast<float*>(db + L.rxScale + (static_cast<size_t>(pos[k]) * nb + col / 128) * 4) =
+                  scale;
+          }
         }
       }
     }
@@ -387,16 +402,27 @@ __global__ void __launch_bounds__(kThreads) moeReceive(DevComm c, Layout L, __nv
   for (int i = gw; i < recv; i += nw) {
     const char* row = base + L.rxData + static_cast<size_t>(i) * H;
     const float* sc = reinterpret_cast<const float*>(base + L.rxScale) + static_cast<size_t>(i) * nb;
-    for (int c0 = 0; c0 < H; c0 += 256) {
-      const int col = c0 + lane * 8;
-      if (col < H) {
-        const uint2 q = __ldcg(reinterpret_cast<const uint2*>(row + col));
-        const float s = __ldcg(sc + col / 128);
-        float f[8];
-        fromFp8x8(q, f);
+    for (int c0 = 0; c0 < H; c0 += 256 * kChunkUnroll) {
+      uint2 q[kChunkUnroll];
+      float sv[kChunkUnroll];
 #pragma unroll
-        for (int j = 0; j < 8; j++) f[j] *= s;
-        *reinterpret_cast<uint4*>(recvX + static_cast<size_t>(i) * H + col) = packBf16x8(f);
+      for (int u = 0; u < kChunkUnroll; u++) {
+        const int col = c0 + u * 256 + lane * 8;
+        if (col < H) {
+          q[u] = __ldcg(reinterpret_cast<const uint2*>(row + col));
+          sv[u] = __ldcg(sc + col / 128);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kChunkUnroll; u++) {
+        const int col = c0 + u * 256 + lane * 8;
+        if (col < H) {
+          float f[8];
+          fromFp8x8(q[u], f);
+#pragma unroll
+          for (int j = 0; j < 8; j++) f[j] *= sv[u];
+          *reinterpret_cast<uint4*>(recvX + static_cast<size_t>(i) * H + col) = packBf16x8(f);
+        }
       }
     }
     if (lane == 0) {
@@ -429,14 +455,19 @@ __global__ void __launch_bounds__(kThreads) moeCombinePush(DevComm c, Layout L, 
     if (meta.x < 0 || meta.x >= n || meta.z < 0 || meta.z >= topk || slot < 0 || slot >= srcTokensCap) continue;
     char* dst = c.moe[meta.x] + L.comb + static_cast<size_t>(slot) * H * 2;
     const uint4* yr = reinterpret_cast<const uint4*>(y + static_cast<size_t>(i) * H);
-    for (int c0 = 0; c0 < H; c0 += 256) {
-      const int col = c0 + lane * 8;
-      if (col < H) {
-        float f[8];
-        unpackBf16x8(yr[col / 8], f);
+    for (int c0 = 0; c0 < H; c0 += 256 * kChunkUnroll) {
+      uint4 raw[kChunkUnroll];
+      loadChunks(yr, c0, H, lane, raw);
 #pragma unroll
-        for (int j = 0; j < 8; j++) f[j] *= wt;
-        *reinterpret_cast<uint4*>(dst + static_cast<size_t>(col) * 2) = packBf16x8(f);
+      for (int u = 0; u < kChunkUnroll; u++) {
+        const int col = c0 + u * 256 + lane * 8;
+        if (col < H) {
+          float f[8];
+          unpackBf16x8(raw[u], f);
+#pragma unroll
+          for (int j = 0; j < 8; j++) f[j] *= wt;
+          *reinterpret_cast<uint4*>(dst + static_cast<size_t>(col) * 2) = packBf16x8(f);
+        }
       }
     }
   }
@@ -506,23 +537,24 @@ __global__ void __launch_bounds__(kThreads) moeLocalDispatch(const __nv_bfloat16
   for (int i = gw; i < P; i += nw) {
     const int t = i / topk;
     const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H);
-    for (int c0 = 0; c0 < H; c0 += 256) {
-      const int col = c0 + lane * 8;
-      const bool active = col < H;
-      float f[8];
-      if (active) {
-        unpackBf16x8(xr[col / 8], f);
-      } else {
+    for (int c0 = 0; c0 < H; c0 += 256 * kChunkUnroll) {
+      uint4 raw[kChunkUnroll];
+      loadChunks(xr, c0, H, lane, raw);
 #pragma unroll
-        for (int j = 0; j < 8; j++) f[j] = 0.0f;
-      }
-      float scale;
-      const uint2 q = quantize8(f, active, &scale);
-      if (active) {
-        fromFp8x8(q, f);
+      for (int u = 0; u < kChunkUnroll; u++) {
+        if (c0 + u * 256 >= H) break;  // warp-uniform
+        const int col = c0 + u * 256 + lane * 8;
+        const bool active = col < H;
+        float f[8];
+        unpackBf16x8(raw[u], f);
+        float scale;
+        const uint2 q = quantize8(f, active, &scale);
+        if (active) {
+          fromFp8x8(q, f);
 #pragma unroll
-        for (int j = 0; j < 8; j++) f[j] *= scale;
-        *reinterpret_cast<uint4*>(recvX + static_cast<size_t>(i) * H + col) = packBf16x8(f);
+          for (int j = 0; j < 8; j++) f[j] *= scale;
+          *reinterpret_cast<uint4*>(recvX + static_cast<size_t>(i) * H + col) = packBf16x8(f);
+        }
       }
     }
     if (lane == 0) {
