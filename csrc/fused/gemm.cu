@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdlib>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -233,21 +234,45 @@ cudaError_t gemmAuto(const void* A, const void* W, void* C, int M, int N, int K,
   return launchGemm(A, W, M, N, K, epi, NoHooks{}, st, bnOverride, 0);
 }
 
-// One abort flag per device (kernels only ever write their own device's).
-int* errorFlag() {
-  static std::mutex mu;
-  static int* flags[64] = {};
+// One abort flag per device in pinned, mapped host memory: a GEMM that
+// abandons its tiles (a pipeline wait ran out) sets it, and the next GEMM
+// call on that device reads it without synchronising.
+namespace {
+std::mutex gFlagMu;
+int* gHostFlags[64] = {};
+int* gDevFlags[64] = {};
+
+int currentDevice() {
   int dev = 0;
   cudaGetDevice(&dev);
-  dev &= 63;
-  std::lock_guard<std::mutex> lock(mu);
-  if (flags[dev] == nullptr) {
-    int* p = nullptr;
-    if (cudaMalloc(&p, sizeof(int) * 64) != cudaSuccess) return nullptr;
-    cudaMemset(p, 0, sizeof(int) * 64);
-    flags[dev] = p;
+  return dev & 63;
+}
+}  // namespace
+
+int* errorFlag() {
+  const int dev = currentDevice();
+  std::lock_guard<std::mutex> lock(gFlagMu);
+  if (gDevFlags[dev] == nullptr) {
+    int* h = nullptr;
+    if (cudaHostAlloc(reinterpret_cast<void**>(&h), sizeof(int) * 16, cudaHostAllocMapped | cudaHostAllocPortable) !=
+        cudaSuccess)
+      return nullptr;
+    memset(h, 0, sizeof(int) * 16);
+    int* d = nullptr;
+    if (cudaHostGetDevicePointer(reinterpret_cast<void**>(&d), h, 0) != cudaSuccess) return nullptr;
+    gHostFlags[dev] = h;
+    gDevFlags[dev] = d;
   }
-  return flags[dev];
+  return gDevFlags[dev];
+}
+
+bool takeAbortFlag() {
+  const int dev = currentDevice();
+  std::lock_guard<std::mutex> lock(gFlagMu);
+  volatile int* h = gHostFlags[dev];
+  if (h == nullptr || *h == 0) return false;
+  *h = 0;
+  return true;
 }
 
 }  // namespace gemm
@@ -261,6 +286,11 @@ namespace {
 vcclResult_t gemmEntry(const char* what, const void* A, const void* W, void* C, int M, int N, int K, bool siluMul,
                        vcclStream_t stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (gemm::takeAbortFlag()) {
+    VERR("%s: an earlier GEMM on this device abandoned its tiles (a pipeline wait ran out); its output is invalid",
+         what);
+    return vcclInternalError;
+  }
   const int bnEnv = static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN"));
   // Decode shapes split K across more CTAs; the fp32 partials live in
   // per-stream scratch (a graph memory node while the stream is captured).

@@ -15,6 +15,9 @@ bool makeMapKMajor(CUtensorMap* map, const void* base, int rows, int K, int boxR
 int smCount();
 int pickBN(int M, int N);
 int* errorFlag();
+// True (once) if a GEMM on the current device set its abort flag since the
+// last call; reads pinned host memory, no synchronisation.
+bool takeAbortFlag();
 
 // Split-K plan for GEMMs with too few output tiles to fill the GPU (decode
 // shapes): 128-wide tiles, K split so tiles x splits approaches one wave.

@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(ctaThreads<Hooks>(), 1)
   __syncthreads();
   if (threadIdx.x == 0) {
     if (*abortFlag) {
-      if (errorFlag) atomicExch(errorFlag, 1);
+      if (errorFlag) *reinterpret_cast<volatile int*>(errorFlag) = 1;  // may live in mapped host memory
     } else {
       hooks.teardown(hs);
     }
