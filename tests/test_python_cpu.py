@@ -279,3 +279,54 @@ def test_vllm_plugin_patches_cuda_platform(monkeypatch):
     monkeypatch.setenv("VKCCL_VLLM", "1")
     assert vllm_plugin.register() is True
     assert FakeCudaPlatform.get_device_communicator_cls() == "vkccl_b200.torch_comm.VcclCommunicator"
+
+
+class _MirrorComm:
+    """Stands in for a 2-rank vccl communicator whose peer holds the same
+    tensors as this rank: all-gather repeats the local data, reduce-scatter
+    returns twice this rank's chunk.  Enough to check the layout logic of
+    VcclCommunicator (dims, padding, movedim) on the CPU."""
+
+    def __init__(self, rank):
+        self.rank = rank
+
+    def all_gather(self, send, recv, sendcount=None, dtype=None):
+        flat = send.reshape(-1)
+        recv.view(2, -1).copy_(torch.stack([flat, flat]))
+
+    def reduce_scatter(self, send, recv, recvcount=None, dtype=None):
+        n = recv.numel()
+        recv.reshape(-1).copy_(2 * send.reshape(-1)[self.rank * n:(self.rank + 1) * n])
+
+    def all_reduce(self, send, recv=None, count=None, dtype=None):
+        (send if recv is None else recv).mul_(2)
+
+
+def _mirror_communicator(rank):
+    from vkccl_b200.torch_comm import VcclCommunicator
+
+    c = VcclCommunicator.__new__(VcclCommunicator)
+    c.world_size, c.rank_in_group, c.vccl, c._outputs = 2, rank, _MirrorComm(rank), {}
+    return c
+
+
+@pytest.mark.parametrize("dim", [0, 1, 2, -1])
+def test_torch_comm_gather_scatter_layouts(dim):
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(4, 6, 8, generator=g)
+    for rank in (0, 1):
+        c = _mirror_communicator(rank)
+        assert torch.equal(c.all_gather(x, dim), torch.cat([x, x], dim))
+        d = dim % 3
+        chunk = x.chunk(2, d)[rank]
+        assert torch.equal(c.reduce_scatter(x, dim), 2 * chunk)
+        # uneven variant: both mirrored "ranks" send this rank's rows, padded to the largest size
+        sizes = [3, 1]
+        mine = x[: sizes[rank]]
+        padded = torch.zeros((3,) + tuple(x.shape[1:]))
+        padded[: sizes[rank]] = mine
+        got = c.all_gatherv(mine, 0, sizes)
+        assert torch.equal(got, torch.cat([padded[: sizes[0]], padded[: sizes[1]]], 0))
+    y = torch.arange(12.0).reshape(6, 2)
+    c = _mirror_communicator(0)
+    assert torch.equal(c.reduce_scatterv(y, 0, [4, 2]), 2 * y[:4])

@@ -151,7 +151,7 @@ class VcclCommunicator(DeviceCommunicatorBase):
         assert -input_.dim() <= dim < input_.dim()
         if dim < 0:
             dim += input_.dim()
-        src = input_.movedim(0, dim).contiguous()
+        src = input_.movedim(dim, 0).contiguous()
         assert src.shape[0] % ws == 0
         out = torch.empty((src.shape[0] // ws,) + tuple(src.shape[1:]), dtype=src.dtype, device=src.device)
         self.vccl.reduce_scatter(src, out, recvcount=out.numel(), dtype=vccl_dtype(src))
