@@ -180,8 +180,8 @@ def test_fp8_block_quant_reference_is_round_to_nearest_even():
 def test_moe_default_capacity():
     from vkccl_b200.ops.moe import default_capacity
 
-    assert default_capacity(4096, 2, 8) == 8192  # T * topk dominates
-    assert default_capacity(4096, 2, 1) == 16384
+    assert default_capacity(4096, 2, 8) == 16384  # twice the average load of T * topk rows
+    assert default_capacity(4096, 2, 1) == 8192   # one rank receives exactly its own pairs
     assert default_capacity(0, 2, 8) == 1
 
 

@@ -15,7 +15,8 @@ moe_combine(comm, dispatch, expert_out)
 
 The row count stays on the device; ``MoeDispatch.count()`` reads it (one
 host synchronisation).  Buffers are sized by ``capacity`` (rows a rank may
-receive, at least T * topk); every rank must pass the same capacity, hidden
+receive, at least T * topk; the default is twice the average load); every
+rank must pass the same capacity, hidden
 size, topk and number of experts.  Call combine once per dispatch.
 """
 
@@ -56,9 +57,9 @@ class MoeDispatch:
 
 
 def default_capacity(tokens: int, topk: int, nranks: int) -> int:
-    """Room for twice the average load per rank, and at least T * topk."""
-    pairs = tokens * topk
-    return max(pairs, 2 * ((pairs + nranks - 1) // nranks), 1)
+    """Room for twice the average load: with every rank routing T * topk
+    pairs, a rank receives T * topk rows on average."""
+    return max(2 * tokens * topk, 1) if nranks > 1 else max(tokens * topk, 1)
 
 
 def moe_dispatch(comm, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
