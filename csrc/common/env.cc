@@ -1,4 +1,7 @@
 // SPDX-License-Identifier: Apache-2.0
+// Environment parsing and the watchdog budget: VCCL_TIMEOUT in seconds,
+// default 60 as in the reference code (reference: src/util/deadline.h:10-56),
+// plus the device-side budget derived from it.
 #include "common/env.h"
 
 #include <cstdlib>

@@ -1,4 +1,7 @@
 // SPDX-License-Identifier: Apache-2.0
+// Logging: VCCL_DEBUG levels, "vccl [pid] LEVEL: msg" on stderr, and the
+// thread-local text of the last error for vcclGetLastError (reference:
+// src/util/log.cc:12-44, src/util/log.h:24-43).
 #include "common/log.h"
 
 #include <strings.h>

@@ -1,4 +1,8 @@
 // SPDX-License-Identifier: Apache-2.0
+// Sockets for the control plane: advertised address choice, listen /
+// connect with retry, exact-size send and receive, and descriptor passing
+// over Unix sockets (reference: src/util/socket.cc:89-339 for the TCP part;
+// the SCM_RIGHTS part has no counterpart there).
 #include "common/net.h"
 
 #include <arpa/inet.h>

@@ -1,4 +1,6 @@
 // SPDX-License-Identifier: Apache-2.0
+// Unique id, rendezvous through the root, allGather / barrier / broadcast and
+// descriptor exchange (reference: src/core/bootstrap.cc:85-272).
 #include "control/bootstrap.h"
 
 #include <arpa/inet.h>

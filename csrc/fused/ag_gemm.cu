@@ -1,5 +1,7 @@
 // SPDX-License-Identifier: Apache-2.0
-// All-gather fused into a column-parallel GEMM.
+// All-gather fused into a column-parallel GEMM.  The reference's TP test
+// gathers with a separate all_gather before the CPU GEMM (reference:
+// python/tests/test_e2e_tp.py:60-85, python/vccl/torch_comm.py:141-158).
 //
 // Each rank holds X_shard[M/n, K] (sequence-parallel activations) and needs
 // out = AllGather(X)[M, K] * W^T.  One persistent kernel does both: two

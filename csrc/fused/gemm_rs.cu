@@ -1,5 +1,8 @@
 // SPDX-License-Identifier: Apache-2.0
-// Row-parallel GEMM fused with reduce-scatter over NVLink.
+// Row-parallel GEMM fused with reduce-scatter over NVLink.  The reference has
+// no fused path; its TP test runs the row-parallel projection as a CPU GEMM
+// followed by a separate all-reduce (reference:
+// python/tests/test_e2e_tp.py:60-85).
 //
 // Every rank computes its partial product P = A * W^T.  Row r of P belongs
 // to rank r / (M / n).  Instead of writing P to memory and running a

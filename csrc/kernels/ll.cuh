@@ -14,6 +14,11 @@
 // Loads and stores are batched kLLUnroll deep per thread: an LL kernel is
 // otherwise bound by one outstanding memory operation per thread.
 //
+// These replace the reference's latency path for small messages, the
+// recursive-doubling all-gather / all-reduce below its RD_MAX thresholds
+// (reference: src/core/collectives.cc:156-184, :359-400): NVSwitch gives
+// every pair full bandwidth, so one hop to every peer beats a log-step tree.
+//
 // Included at the end of collectives.cuh.
 #pragma once
 

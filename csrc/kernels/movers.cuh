@@ -1,5 +1,9 @@
 // SPDX-License-Identifier: Apache-2.0
-// Block-level data movers with deep memory-level parallelism.
+// Block-level data movers with deep memory-level parallelism: the device
+// counterparts of the reference's host reduction and scaling helpers
+// (reference: src/core/reduce.cc:234-408, cpuReduce / cpuScaledAccumulate /
+// cpuScaleCopy / cpuScale), with PreMulSum scaling fused into the load and
+// average scaling into the store.
 //
 // NVLink loads take on the order of a microsecond to return, so a block
 // that keeps one 16-byte load per thread in flight moves only ~8 KiB per

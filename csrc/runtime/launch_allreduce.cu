@@ -1,5 +1,8 @@
 // SPDX-License-Identifier: Apache-2.0
-// All-reduce / reduce launchers (LL, two-shot, NVLS).
+// All-reduce / reduce launchers (LL, two-hop LL, two-shot, NVLS); the
+// algorithm is chosen in collectives.cc, as the reference's dispatcher
+// chooses ring or recursive doubling (reference:
+// src/core/collectives.cc:505-555, reduce chain :557-620).
 #include "kernels/collectives.cuh"
 #include "runtime/dispatch.cuh"
 #include "runtime/launch.h"

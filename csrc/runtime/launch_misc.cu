@@ -1,6 +1,8 @@
 // SPDX-License-Identifier: Apache-2.0
 // Reduce-scatter, all-gather, broadcast, point-to-point and single-rank
-// launchers.
+// launchers (reference counterparts: src/core/collectives.cc:283-349
+// reduce-scatter, :243-281 all-gather dispatcher, :622-649 broadcast chain,
+// :651-740 gather / scatter / all-to-all, :886-905 send / recv).
 #include "kernels/movement.cuh"
 #include "runtime/dispatch.cuh"
 #include "runtime/launch.h"

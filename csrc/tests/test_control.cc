@@ -1,6 +1,8 @@
 // SPDX-License-Identifier: Apache-2.0
 // Control-plane suite (CPU only; VCCL_NO_DEVICE=1 forces control-plane
-// communicators even on GPU machines).
+// communicators even on GPU machines).  Mirrors the parts of the reference's
+// suite that need no data plane (reference: tests/test_collectives.cc:
+// 355-466 PreMulSum / split / misc, :542-612 kill-a-rank, :618-647 InitAll).
 //
 // Covers what needs no data plane: error strings and type sizes, version,
 // group nesting rules, init / split (even-odd and NOCOLOR) / InitAll

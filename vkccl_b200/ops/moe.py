@@ -1,6 +1,10 @@
 # SPDX-License-Identifier: Apache-2.0
 """Expert-parallel MoE dispatch / combine (stream-ordered on torch's current stream).
 
+The reference offers only vcclAllToAll(v) for this (reference:
+src/core/collectives.cc:708-740); routing, quantisation and the top-k sum
+are fused into the transfers here.
+
 moe_dispatch(comm, x, topk_weights, topk_ids, num_experts, capacity)
     Every (token, k) pair travels to the rank that owns expert topk_ids[t, k]
     (experts split evenly over ranks), quantised to fp8 e4m3 with one scale

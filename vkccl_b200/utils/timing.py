@@ -1,6 +1,10 @@
 # SPDX-License-Identifier: Apache-2.0
 """Device timing, L2 flushing and clock sampling for benchmarks.
 
+The reference's bench times rank 0's host wall clock (reference:
+bench/vccl_bench.cc:211-221); here every number is device time, the
+maximum over ranks.
+
 * Times are CUDA-event durations on the launching stream, taken after
   warm-up with a synchronize on both sides; multi-GPU numbers are the
   maximum over ranks.
