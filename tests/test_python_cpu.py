@@ -330,3 +330,99 @@ def test_torch_comm_gather_scatter_layouts(dim):
     y = torch.arange(12.0).reshape(6, 2)
     c = _mirror_communicator(0)
     assert torch.equal(c.reduce_scatterv(y, 0, [4, 2]), 2 * y[:4])
+
+
+class _ThreadWorld:
+    """n in-process "ranks" (threads) exchanging tensors, standing in for the
+    library's all-to-all and send/recv to check the sequence-parallel
+    layout logic on the CPU."""
+
+    def __init__(self, n):
+        import threading
+
+        self.n = n
+        self.barrier = threading.Barrier(n)
+        self.blocks = [None] * n
+        self.mail = {}
+        self.cv = threading.Condition()
+
+
+class _ThreadComm:
+    def __init__(self, world, rank):
+        self.w, self.rank, self.nranks = world, rank, world.n
+
+    def all_to_all(self, send, recv, count=None, dtype=None):
+        w = self.w
+        w.blocks[self.rank] = send.reshape(w.n, -1).clone()
+        w.barrier.wait()
+        recv.view(w.n, -1).copy_(torch.stack([w.blocks[i][self.rank] for i in range(w.n)]))
+        w.barrier.wait()
+
+    def send(self, buf, peer, count=None, dtype=None):
+        with self.w.cv:
+            self.w.mail[(self.rank, peer)] = buf.clone()
+            self.w.cv.notify_all()
+
+    def recv(self, buf, peer, count=None, dtype=None):
+        with self.w.cv:
+            self.w.cv.wait_for(lambda: (peer, self.rank) in self.w.mail, timeout=30)
+            buf.copy_(self.w.mail.pop((peer, self.rank)))
+
+
+def _run_ranks(n, body):
+    import threading
+
+    world = _ThreadWorld(n)
+    out, errs = [None] * n, []
+
+    def run(r):
+        try:
+            out[r] = body(_ThreadComm(world, r))
+        except Exception as e:  # noqa: BLE001
+            errs.append(repr(e))
+
+    ts = [threading.Thread(target=run, args=(r,)) for r in range(n)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join(timeout=60)
+    assert not errs, errs
+    return out
+
+
+@pytest.mark.parametrize("n", [1, 2, 4])
+def test_ulysses_round_trip(n):
+    from vkccl_b200.parallel.sequence import ulysses_heads_to_seq, ulysses_seq_to_heads
+
+    S, H, D = 8 * n, 4 * n, 3
+    full = torch.randn(S, H, D, generator=torch.Generator().manual_seed(1))
+    s_loc, h_loc = S // n, H // n
+
+    def body(c):
+        mine = full[c.rank * s_loc:(c.rank + 1) * s_loc]
+        heads = ulysses_seq_to_heads(c, mine)
+        assert torch.equal(heads, full[:, c.rank * h_loc:(c.rank + 1) * h_loc])
+        return ulysses_heads_to_seq(c, heads)
+
+    outs = _run_ranks(n, body)
+    for r in range(n):
+        assert torch.equal(outs[r], full[r * s_loc:(r + 1) * s_loc])
+
+
+def test_ring_pass_visits_every_block():
+    from vkccl_b200.parallel.sequence import ring_pass, ring_schedule
+
+    n = 4
+    blocks = [torch.full((5,), float(r)) for r in range(n)]
+
+    def body(c):
+        held = blocks[c.rank]
+        seen = [int(held[0])]
+        for _ in range(n - 1):
+            held = ring_pass(c, held)
+            seen.append(int(held[0]))
+        return seen
+
+    outs = _run_ranks(n, body)
+    for r in range(n):
+        assert tuple(outs[r]) == ring_schedule(n, r)
