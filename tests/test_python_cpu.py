@@ -360,13 +360,13 @@ class _ThreadComm:
 
     def send(self, buf, peer, count=None, dtype=None):
         with self.w.cv:
-            self.w.mail[(self.rank, peer)] = buf.clone()
+            self.w.mail.setdefault((self.rank, peer), []).append(buf.clone())  # FIFO per (src, dst)
             self.w.cv.notify_all()
 
     def recv(self, buf, peer, count=None, dtype=None):
         with self.w.cv:
-            self.w.cv.wait_for(lambda: (peer, self.rank) in self.w.mail, timeout=30)
-            buf.copy_(self.w.mail.pop((peer, self.rank)))
+            assert self.w.cv.wait_for(lambda: self.w.mail.get((peer, self.rank)), timeout=30), "recv timed out"
+            buf.copy_(self.w.mail[(peer, self.rank)].pop(0))
 
 
 def _run_ranks(n, body):
