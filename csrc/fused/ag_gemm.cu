@@ -64,13 +64,27 @@ struct AgHooks : gemm::NoHooks {
   int startTm;         // first tile row of this rank's shard
   int groupRows;       // row tiles per tile group (divides the shard's tiles when possible)
   uint32_t ctas;       // fixed grid size
+  // Optional event trace (VCCL_FUSED_TRACE=1), kFusedTraceSlots times per CTA
+  // from %globaltimer: 0 kernel start, 1 previous call's shard taken by every
+  // peer, 2 own slice staged, 3..9 pull of the s-th peer shard done,
+  // 10..17 first tile of the s-th shard (own shard s = 0) released to the
+  // TMA producer, 18 kernel end.
+  unsigned long long* trace;
+
+  __device__ __forceinline__ void mark(int slot) const {
+    if (trace != nullptr) trace[blockIdx.x * dev::kFusedTraceSlots + slot] = dev::globalTimerNs();
+  }
 
   __device__ __forceinline__ uint32_t* ctrl(int rank, size_t off) const {
     return dev::ctrlAt<uint32_t>(c, rank, off);
   }
-  __device__ __forceinline__ void setup(uint32_t* hs) const { hs[0] = ctrl(c.rank, dev::kAgCallsOff)[blockIdx.x]; }
+  __device__ __forceinline__ void setup(uint32_t* hs) const {
+    hs[0] = ctrl(c.rank, dev::kAgCallsOff)[blockIdx.x];
+    mark(0);
+  }
   __device__ __forceinline__ void teardown(uint32_t* hs) const {
     ctrl(c.rank, dev::kAgCallsOff)[blockIdx.x] = hs[0] + 1u;
+    mark(18);
   }
   // Row tiles start at this rank's shard and wrap around, in groups that
   // share weight tiles (see gemm::groupedTile).
@@ -87,6 +101,11 @@ struct AgHooks : gemm::NoHooks {
       const bool own = q == c.rank;
       const uint32_t* flag = own ? ctrl(c.rank, dev::kAgReadyOff) + q : ctrl(c.rank, dev::kAgLocalReadyOff) + q;
       if (!dev::waitAcquire(c, flag, own ? k + 1u : (k + 1u) * ctas, dev::kWhereFused, 300 + q, 64)) return false;
+      if (trace != nullptr) {
+        unsigned long long* t = trace + blockIdx.x * dev::kFusedTraceSlots;
+        const int slot = 10 + (q - c.rank + c.nranks) % c.nranks;
+        if (t[slot] < t[0]) t[slot] = dev::globalTimerNs();  // first release of this shard in this call
+      }
     }
     fenceProxyAsync();
     return true;
@@ -115,6 +134,7 @@ struct AgHooks : gemm::NoHooks {
       *abortFlag = 1;
       return;
     }
+    if (tid == 0) mark(1);
     // 2. stage my slice of my shard; the last CTA to finish announces the
     //    shard to every rank once (me included)
     if (r1 > r0)
@@ -127,6 +147,7 @@ struct AgHooks : gemm::NoHooks {
       const uint32_t old = atomicAdd(ctrl(me, dev::kAgStagedOff), 1u);
       if (old + 1u == (k + 1u) * ctas)
         for (int p = 0; p < n; p++) redAddRelease(ctrl(p, dev::kAgReadyOff) + me, 1u, true);
+      mark(2);
     }
     // 3. pull my slice of every peer's shard; the last CTA to finish a shard
     //    tells its owner it may be overwritten
@@ -147,6 +168,7 @@ struct AgHooks : gemm::NoHooks {
         __threadfence();
         const uint32_t old = atomicAdd(ctrl(me, dev::kAgLocalReadyOff) + q, 1u);
         if (old + 1u == (k + 1u) * ctas) redAddRelease(ctrl(q, dev::kAgTakenOff) + me, 1u, true);
+        mark(2 + s);
       }
     }
   }
@@ -240,6 +262,7 @@ extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, voi
     }
   hooks.groupRows = groupRows;
   hooks.ctas = static_cast<uint32_t>(ctas);
+  hooks.trace = comm->dev->fusedTrace;
   const char* xfull = dc.fused[comm->rank] + xOff;
   if (siluMul) {
     gemm::EpiSiluMul epi{static_cast<__nv_bfloat16*>(out), N / 2};

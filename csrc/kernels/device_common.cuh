@@ -38,6 +38,7 @@ constexpr size_t kFusedFlagsOff = 20480;                              // u32[kMa
 constexpr size_t kMoeCountsOff = 32768;                               // u32[2][kMaxRanks][64], written by peers
 // Fused GEMM + reduce-scatter / all-gather + GEMM counters (monotonic).
 constexpr int kMaxFusedCtas = 256;
+constexpr int kFusedTraceSlots = 32;  // event times per CTA in the optional AG+GEMM trace
 constexpr int kFusedReduceBlocks = 64;
 constexpr size_t kRsDoneOff = 65536;                        // u32[kMaxRanks]: peers' GEMM CTAs finished pushing
 constexpr size_t kRsFreeOff = kRsDoneOff + 64;              // u32[kMaxRanks]: peers finished reducing my pushes

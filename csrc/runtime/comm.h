@@ -59,6 +59,7 @@ struct DeviceState {
   size_t llMaxBytes = 0;           // one-hop LL threshold (per-rank payload)
   int llBlocks = 64;               // grid of every LL kernel, a multiple of 8
   int fusedSmallRows = 512;        // fused TP calls up to this many rows run unfused
+  unsigned long long* fusedTrace = nullptr;  // per-CTA event times of the last AG+GEMM (VCCL_FUSED_TRACE=1)
   size_t ll2MaxBytes = 0;          // two-hop LL all-reduce threshold
 };
 

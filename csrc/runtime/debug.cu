@@ -94,3 +94,21 @@ extern "C" vcclResult_t vcclxBarrierBench(vcclComm_t comm, int iters, int nblock
   *usPerBarrier = ms * 1000.0f / iters;
   return comm->pollDeviceStatus();
 }
+
+// Copy the optional all-gather + GEMM event trace of the last call
+// (VCCL_FUSED_TRACE=1 at communicator creation): *ctas rows of
+// kFusedTraceSlots %globaltimer values (ns) per CTA; see AgHooks::trace
+// for the slot meanings.  Synchronises the device.
+extern "C" vcclResult_t vcclxFusedTrace(vcclComm_t comm, unsigned long long* out, int* ctas) {
+  if (comm == nullptr || out == nullptr || ctas == nullptr || !comm->dev) return vcclInvalidArgument;
+  if (comm->dev->fusedTrace == nullptr) return vcclInvalidUsage;
+  cudaSetDevice(comm->dev->device);
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, comm->dev->device);
+  if (sms > vccl::dev::kMaxFusedCtas) sms = vccl::dev::kMaxFusedCtas;
+  if (cudaMemcpy(out, comm->dev->fusedTrace, static_cast<size_t>(sms) * vccl::dev::kFusedTraceSlots * 8,
+                 cudaMemcpyDeviceToHost) != cudaSuccess)
+    return vcclUnhandledError;
+  *ctas = sms;
+  return vcclSuccess;
+}

@@ -307,6 +307,12 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
           ctrlBytes >> 20, dataBytes >> 20, ds->nvls ? "on" : "off");
   }
 
+  if (envLong("VCCL_FUSED_TRACE", 0) != 0) {
+    const size_t tb = static_cast<size_t>(dev::kMaxFusedCtas) * dev::kFusedTraceSlots * 8;
+    CUDART_TRY(cudaMalloc(reinterpret_cast<void**>(&ds->fusedTrace), tb));
+    CUDART_TRY(cudaMemset(ds->fusedTrace, 0, tb));
+  }
+
   dev::DevComm& dc = ds->dc;
   memset(&dc, 0, sizeof(dc));
   dc.rank = me;
@@ -381,6 +387,8 @@ void deviceStateDestroy(DeviceState* ds, Bootstrap* bs, bool peersAlive) {
   }
   if (ds->moeLocal) cudaFree(ds->moeLocal);
   ds->moeLocal = nullptr;
+  if (ds->fusedTrace) cudaFree(ds->fusedTrace);
+  ds->fusedTrace = nullptr;
   if (ds->hostStatus) cudaFreeHost(ds->hostStatus);
   if (ds->hostAbort) cudaFreeHost(ds->hostAbort);
   if (ds->stream) cudaStreamDestroy(ds->stream);

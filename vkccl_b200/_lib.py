@@ -138,6 +138,7 @@ def _declare_extensions(h: ctypes.CDLL) -> None:
         "vcclAllReduceAddRMSNorm": [P, P, P, P, Z, Z, F, I, P, P],
         "vcclGemmBf16": [P, P, P, I, I, I, P],
         "vcclGemmBf16NoAlloc": [P, P, P, I, I, I, P],
+        "vcclxFusedTrace": [P, P, P],
         "vcclGemmSiluMul": [P, P, P, I, I, I, P],
         "vcclGemmReduceScatter": [P, P, P, I, I, I, P, P],
         "vcclAllGatherGemm": [P, P, P, I, I, I, I, P, P],

@@ -433,6 +433,21 @@ class Communicator:
     def finalize(self) -> None:
         _check(lib().vcclCommFinalize(self._comm), "vcclCommFinalize", self._comm)
 
+    def fused_trace(self):
+        """Per-CTA event times (ns) of the last all-gather + GEMM call, as a
+        [ctas, 32] numpy array, when the communicator was created with
+        VCCL_FUSED_TRACE=1; None otherwise.  Slots: 0 start, 1 previous call's
+        shard taken by every peer, 2 own slice staged, 3..9 s-th peer shard
+        pulled, 10..17 first tile of the s-th shard released, 18 end."""
+        import numpy as np
+
+        out = np.zeros((256, 32), dtype=np.uint64)
+        ctas = ctypes.c_int(0)
+        r = lib().vcclxFusedTrace(self._comm, out.ctypes.data, ctypes.byref(ctas))
+        if r != 0:
+            return None
+        return out[: ctas.value].copy()
+
     def last_error(self) -> str:
         return lib().vcclGetLastError(self._comm).decode(errors="replace")
 
