@@ -276,8 +276,8 @@ def run_reference(args) -> int:
     rank, world, _ = env_ranks()
     if not os.path.exists(lib) or not os.path.isdir(os.path.join(ref, "vccl")):
         if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref not built (cmake build of "
-                              "/root/reference plus its python package; see DESIGN.md)"}))
+            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref not built (the reference's own "
+                              "CMake build and its unmodified python package are expected there)"}))
         return 0
     os.environ["VCCL_LIBRARY"] = lib
     os.environ.setdefault("VCCL_SOCKET_ADDR", "127.0.0.1")
