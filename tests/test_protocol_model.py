@@ -388,3 +388,75 @@ def test_model_detects_single_buffered_ll():
             return True
 
     assert any(broken(seed) for seed in range(200))
+
+
+# ---------------------------------------------------------------------------
+# LL broadcast: data flows only from the root, so every rank also exchanges a
+# one-line token with every peer (csrc/kernels/movement.cuh, broadcastLL)
+# ---------------------------------------------------------------------------
+def run_ll_bcast(n, calls, seed, tokens=True):
+    sim = Sim(seed)
+    epoch = defaultdict(int)
+    data, data_read = {}, {}   # (dst, parity) -> epoch of the root's lines / epoch the reader took
+    tok = {}                   # (dst, parity, src) -> epoch
+    errors = []
+    root = 0
+
+    def make(r):
+        def mk(k):
+            live = {"done": 0, "count": 1}
+
+            def block():
+                epoch[r] += 1
+                e = epoch[r]
+                par = e & 1
+                if tokens:
+                    for p in range(n):
+                        if p != r:
+                            tok[(p, par, r)] = e
+                if r == root:
+                    for p in range(n):
+                        if p != r:
+                            prev = data.get((p, par))
+                            if prev is not None and data_read.get((p, par)) != prev:
+                                errors.append(f"root epoch {e} overwrote unread epoch {prev} at rank {p}")
+                            data[(p, par)] = e
+                            yield lambda: True
+                else:
+                    yield lambda: data.get((r, par)) == e
+                    yield lambda: True
+                    if data.get((r, par)) != e:
+                        errors.append(f"rank {r} epoch {e}: lines changed before they were read")
+                    data_read[(r, par)] = e
+                if tokens:
+                    for p in range(n):
+                        if p != r:
+                            yield lambda p=p: tok.get((r, par, p)) == e
+                live["done"] += 1
+
+            live["procs"] = [block()]
+            return live
+        return mk
+
+    for r in range(n):
+        sim.spawn(kernel_chain(sim, calls, make(r)))
+    sim.run()
+    return errors
+
+
+@pytest.mark.parametrize("n", [2, 3, 8])
+def test_ll_broadcast_token_protocol(n):
+    for seed in range(200):
+        assert run_ll_bcast(n, calls=6, seed=seed) == []
+
+
+def test_model_detects_broadcast_without_tokens():
+    """Without the token exchange the root can run two calls ahead and
+    overwrite lines a slow rank has not read (the bug the tokens fixed)."""
+    def broken(seed):
+        try:
+            return bool(run_ll_bcast(3, calls=6, seed=seed, tokens=False))
+        except Deadlock:
+            return True
+
+    assert any(broken(seed) for seed in range(300))
