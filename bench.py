@@ -78,12 +78,15 @@ def run_vccl(args) -> int:
     os.environ.setdefault("VCCL_SOCKET_ADDR", "127.0.0.1")
     import vkccl_b200 as v
     from vkccl_b200.models.llama_mlp import MLPConfig, TPLlamaMLP
-    from vkccl_b200.utils.timing import ClockSampler, L2Flusher, NvmlClockSampler, max_over_ranks, time_steps
+    from vkccl_b200.utils.timing import (ClockSampler, L2Flusher, NvmlClockSampler, bind_to_gpu_cpus,
+                                         max_over_ranks, time_steps)
 
     rank, world, local = env_ranks()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
     torch.cuda.set_device(local)
+    # Host buffers on the GPU's NUMA node: the end-to-end copies then stay on one socket.
+    numa_bound = bind_to_gpu_cpus(local)
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=300))
         raw = torch.zeros(v.UNIQUE_ID_BYTES, dtype=torch.uint8, device="cuda")
@@ -174,7 +177,8 @@ def run_vccl(args) -> int:
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic N(0,1) activations, random N(0,0.02) weights",
-            "config": config(args, world, "bf16"),
+            "config": {**config(args, world, "bf16"),
+                       "host_cpus": "GPU-local NUMA cores (NVML affinity)" if numa_bound else "unrestricted"},
             "clocks": clocks,
             "e2e": {"value": round(e2e, 2), "unit": "us",
                     "h2d_bytes_per_step": x.numel() * x.element_size(),

@@ -119,6 +119,43 @@ class ClockSampler:
         return summarize(self.out)
 
 
+def _nvml_handle(device_index: int):
+    """NVML handle of a CUDA device (matched by PCI bus id, so it honours
+    CUDA_VISIBLE_DEVICES), or None."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(device_index)
+        bus = f"{getattr(props, 'pci_domain_id', 0):08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+    except Exception:  # noqa: BLE001 - no NVML
+        return None
+
+
+def bind_to_gpu_cpus(device_index: int) -> bool:
+    """Restrict this process to the CPU cores NVML reports as closest to the
+    GPU, so pinned host buffers (allocated on first touch) sit on the GPU's
+    NUMA node and host-device copies do not cross sockets.  Read-only NVML
+    query; returns False (and changes nothing) when it is unavailable."""
+    import os
+
+    got = _nvml_handle(device_index)
+    if got is None:
+        return False
+    nv, h = got
+    try:
+        words = nv.nvmlDeviceGetCpuAffinity(h, 16)
+        cpus = {64 * w + b for w, mask in enumerate(words) for b in range(64) if (int(mask) >> b) & 1}
+        cpus &= set(range(os.cpu_count() or 1))
+        if not cpus:
+            return False
+        os.sched_setaffinity(0, cpus)
+        return True
+    except Exception:  # noqa: BLE001
+        return False
+
+
 class NvmlClockSampler:
     """Samples this process's GPU through NVML every `period_s` on a thread.
 
@@ -138,18 +175,14 @@ class NvmlClockSampler:
         self._stop = threading.Event()
         self._thread = None
         self.ok = False
-        try:
-            import pynvml
-
-            pynvml.nvmlInit()
-            props = torch.cuda.get_device_properties(device_index)
-            bus = f"{getattr(props, 'pci_domain_id', 0):08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
-            self.nvml = pynvml
-            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
-            self.ok = True
-        except Exception:  # noqa: BLE001 - no NVML: report unavailable
-            self.ok = False
+        got = _nvml_handle(device_index)
+        if got is not None:
+            try:
+                self.nvml, self.handle = got
+                self.max_mhz = self.nvml.nvmlDeviceGetMaxClockInfo(self.handle, self.nvml.NVML_CLOCK_SM)
+                self.ok = True
+            except Exception:  # noqa: BLE001 - no NVML: report unavailable
+                self.ok = False
 
     def _run(self):
         nv = self.nvml
