@@ -32,6 +32,7 @@ LaunchCtx launchCtxFor(const DeviceState& ds, cudaStream_t s) {
   lc.nblocks = ds.nblocks;
   lc.nvls = ds.nvls;
   lc.llMax = ds.llMaxBytes;
+  lc.llAgMax = ds.llAgMaxBytes;
   lc.llBlocks = ds.llBlocks;
   return lc;
 }
@@ -418,7 +419,7 @@ vcclResult_t launchColl(const HostOp& h) {
       noteAlgorithm("reduce-scatter", h.count * es <= lc.llMax ? "LL" : "push", n, h.count * es);
       return cudaToVccl(launchReduceScatter(lc, h.dt, h.redKind, a), "reduce-scatter launch");
     case Kind::AllGather:
-      noteAlgorithm("all-gather", h.count * es <= lc.llMax ? "LL" : "pull", n, h.count * es);
+      noteAlgorithm("all-gather", h.count * es <= lc.llAgMax ? "LL" : "pull", n, h.count * es);
       return cudaToVccl(launchAllGather(lc, h.send, h.recv, h.count * es), "all-gather launch");
     case Kind::Broadcast: {
       const size_t bytes = h.count * es;

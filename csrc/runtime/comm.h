@@ -57,6 +57,7 @@ struct DeviceState {
   dev::DevComm dc{};
   int nblocks = 32;                // grid of barrier-based kernels
   size_t llMaxBytes = 0;           // one-hop LL threshold (per-rank payload)
+  size_t llAgMaxBytes = 0;         // LL threshold of all-gather (per-rank payload)
   int llBlocks = 64;               // grid of every LL kernel, a multiple of 8
   int fusedSmallRows = 512;        // fused TP calls up to this many rows run unfused
   unsigned long long* fusedTrace = nullptr;  // per-CTA event times of the last AG+GEMM (VCCL_FUSED_TRACE=1)

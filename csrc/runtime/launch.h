@@ -19,6 +19,7 @@ struct LaunchCtx {
   int nblocks;     // max grid of barrier kernels
   bool nvls;
   size_t llMax;    // largest per-rank payload sent with the LL protocol
+  size_t llAgMax;  // the same for all-gather (no reduction, so LL pays off further)
   int llBlocks;    // grid of every LL kernel (fixed per communicator)
 };
 

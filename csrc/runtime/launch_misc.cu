@@ -46,7 +46,7 @@ cudaError_t launchReduceScatter(const LaunchCtx& lc, vcclDataType_t dt, int redK
 }
 
 cudaError_t launchAllGather(const LaunchCtx& lc, const void* send, void* recv, size_t bytes) {
-  if (bytes <= lc.llMax && bytes % 8 == 0 && aligned8(send, recv)) {
+  if (bytes <= lc.llAgMax && bytes % 8 == 0 && aligned8(send, recv)) {
     dev::allGatherLL<<<lc.llBlocks, kThreads, 0, lc.stream>>>(lc.dc, static_cast<const char*>(send),
                                                                   static_cast<char*>(recv), bytes);
     return cudaGetLastError();
