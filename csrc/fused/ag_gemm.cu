@@ -32,9 +32,9 @@ using dev::DevComm;
 
 __device__ __forceinline__ void redAddRelease(uint32_t* p, uint32_t v, bool sys) {
   if (sys)
-    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+    dev::redAddReleaseSys(p, v);
   else
-    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+    dev::redAddReleaseGpu(p, v);
 }
 __device__ __forceinline__ void fenceProxyAsync() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 __device__ __forceinline__ void copyWarpsBarrier() { asm volatile("bar.sync 2, 64;" ::: "memory"); }

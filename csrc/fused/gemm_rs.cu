@@ -35,9 +35,7 @@ namespace fused {
 
 using dev::DevComm;
 
-__device__ __forceinline__ void redAddReleaseSys(uint32_t* p, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
+using dev::redAddReleaseSys;
 // Two epilogue warpgroups (8 warps) share each tile: the pushes over NVLink
 // are what bounds this kernel, so twice the threads keep twice the stores in
 // flight.

@@ -88,9 +88,7 @@ Layout layoutFor(int cap, int H) {
   return L;
 }
 
-__device__ __forceinline__ void redAddReleaseSys(uint32_t* p, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
+using dev::redAddReleaseSys;
 
 __device__ __forceinline__ uint32_t* ctrl32(const DevComm& c, int rank, size_t off) {
   return dev::ctrlAt<uint32_t>(c, rank, off);

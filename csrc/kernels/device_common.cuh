@@ -112,6 +112,13 @@ __device__ __forceinline__ void stReleaseSys64(uint64_t* p, uint64_t v) {
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ void fenceSys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+// Release increment of a counter another GPU (sys) or this GPU (gpu) polls.
+__device__ __forceinline__ void redAddReleaseSys(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void redAddReleaseGpu(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ void fenceProxyAlias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
 
 // Record the first failure.  Status lives in host-mapped memory: plain
