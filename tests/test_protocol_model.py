@@ -460,3 +460,58 @@ def test_model_detects_broadcast_without_tokens():
             return True
 
     assert any(broken(seed) for seed in range(300))
+
+
+# ---------------------------------------------------------------------------
+# point-to-point slot ring (csrc/kernels/movement.cuh, p2pKernel): per (peer,
+# channel) a sender and a receiver walk one sequence of chunks; the sender
+# waits until the receiver freed the slot it is about to reuse.
+# ---------------------------------------------------------------------------
+def run_p2p_ring(msgs, slots, seed):
+    """msgs: chunk counts of consecutive messages on one (sender, receiver, channel)."""
+    sim = Sim(seed)
+    head = [0]   # written by the sender: chunks published
+    tail = [0]   # written by the receiver: chunks consumed
+    ring = {}    # slot -> sequence number it holds
+    errors = []
+    state = {"sent": 0, "recvd": 0}
+
+    def sender():
+        for m in msgs:
+            base = state["sent"]
+            for q in range(m):
+                seq = base + q
+                if seq >= slots:
+                    yield lambda seq=seq: tail[0] >= seq - slots + 1
+                held = ring.get(seq % slots)
+                if held is not None and held >= tail[0]:
+                    errors.append(f"chunk {seq} overwrote unread chunk {held}")
+                ring[seq % slots] = seq
+                yield lambda: True
+                head[0] = seq + 1
+            state["sent"] = base + m
+
+    def receiver():
+        for m in msgs:
+            base = state["recvd"]
+            for q in range(m):
+                seq = base + q
+                yield lambda seq=seq: head[0] >= seq + 1
+                yield lambda: True
+                if ring.get(seq % slots) != seq:
+                    errors.append(f"read chunk {ring.get(seq % slots)} for {seq}")
+                tail[0] = seq + 1
+            state["recvd"] = base + m
+
+    sim.spawn(sender())
+    sim.spawn(receiver())
+    sim.run()
+    return errors
+
+
+@pytest.mark.parametrize("slots", [1, 2, 4])
+def test_p2p_ring_protocol(slots):
+    rng = random.Random(slots)
+    for seed in range(200):
+        msgs = [rng.randint(1, 9) for _ in range(rng.randint(1, 5))]
+        assert run_p2p_ring(msgs, slots, seed) == []
