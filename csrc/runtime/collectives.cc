@@ -243,6 +243,7 @@ vcclResult_t cudaToVccl(cudaError_t e, const char* what) {
 ArAlgo pickAllReduce(const HostOp& h, size_t bytes) {
   const DeviceState& ds = *h.comm->dev;
   std::string force = envStr("VCCL_ALLREDUCE_ALGO", "");
+  if (force.empty() && !ds.tuning.empty()) force = tunedAlgorithm(ds.tuning, "allreduce", h.comm->nranks, bytes);
   const bool llOk = bytes <= dev::kLLMaxBytes &&
                     ((reinterpret_cast<uintptr_t>(h.send) | reinterpret_cast<uintptr_t>(h.recv)) & 7u) == 0;
   const bool nvlsOk = ds.nvls && nvlsSupports(h.dt, h.redKind);
@@ -424,6 +425,7 @@ vcclResult_t launchColl(const HostOp& h) {
     case Kind::Broadcast: {
       const size_t bytes = h.count * es;
       std::string force = envStr("VCCL_BROADCAST_ALGO", "");
+      if (force.empty() && !comm->dev->tuning.empty()) force = tunedAlgorithm(comm->dev->tuning, "broadcast", n, bytes);
       // The root sends S through the switch instead of (n-1) S to the peers.
       bool nv = lc.nvls && (force == "nvls" || (force.empty() && n >= 3 && bytes >= (256u << 10)));
       noteAlgorithm("broadcast", bytes <= lc.llMax ? "LL" : nv ? "NVLS multimem" : "pull", n, bytes);

@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "control/bootstrap.h"
+#include "runtime/tuning.h"
 #include "kernels/device_common.cuh"
 #include "vccl.h"
 
@@ -61,6 +62,7 @@ struct DeviceState {
   int llBlocks = 64;               // grid of every LL kernel, a multiple of 8
   int fusedSmallRows = 512;        // fused TP calls up to this many rows run unfused
   unsigned long long* fusedTrace = nullptr;  // per-CTA event times of the last AG+GEMM (VCCL_FUSED_TRACE=1)
+  std::vector<TuningRule> tuning;  // measured algorithm table (VCCL_TUNING_FILE)
   size_t ll2MaxBytes = 0;          // two-hop LL all-reduce threshold
 };
 

@@ -245,6 +245,10 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
   // all-reduce (same traffic) took 33 us where the pull all-gather took
   // 73 us, so all-gather stays on LL up to the LL slot size.
   ds->llAgMaxBytes = envBytes("VCCL_LL_AG_MAX", dev::kLLMaxBytes);
+  {
+    const std::string tf = envStr("VCCL_TUNING_FILE", "");
+    if (!tf.empty()) ds->tuning = loadTuningFile(tf.c_str());
+  }
   if (ds->llAgMaxBytes > dev::kLLMaxBytes) ds->llAgMaxBytes = dev::kLLMaxBytes;
   // LL epochs are per block, so every rank must launch the same LL grid; the
   // fused LL kernels run in clusters of 8, hence the multiple of 8.
@@ -287,17 +291,25 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
     dataBytes = roundUp(dataBytes, dataAlign);
     const size_t ctrlBytes = roundUp(dev::kCtrlBytes, gran);
     const size_t fusedBytes = roundUp(envBytes("VCCL_FUSED_BUFFSIZE", 512u << 20), gran);
-    struct Sizes { uint64_t ctrl, data, fused, llBlocks, smallRows; } mine{
+    // Every rank must choose the same algorithm for a call: the tuning table
+    // takes part in the agreement through a hash of its rules.
+    uint64_t tuneHash = 1469598103934665603ull;
+    for (const TuningRule& r : ds->tuning) {
+      const std::string line = r.op + " " + std::to_string(r.nranks) + " " + std::to_string(r.maxBytes) + " " + r.algo;
+      for (unsigned char ch : line) tuneHash = (tuneHash ^ ch) * 1099511628211ull;
+      tuneHash = (tuneHash ^ '\n') * 1099511628211ull;
+    }
+    struct Sizes { uint64_t ctrl, data, fused, llBlocks, smallRows, tuning; } mine{
         ctrlBytes, dataBytes, fusedBytes, static_cast<uint64_t>(ds->llBlocks),
-        static_cast<uint64_t>(static_cast<int64_t>(ds->fusedSmallRows))};
+        static_cast<uint64_t>(static_cast<int64_t>(ds->fusedSmallRows)), tuneHash};
     std::vector<Sizes> all(n);
     all[me] = mine;
     VTRY(bs->allGather(all.data(), sizeof(Sizes)));
     for (const Sizes& s : all) {
       if (s.ctrl != mine.ctrl || s.data != mine.data || s.fused != mine.fused || s.llBlocks != mine.llBlocks ||
-          s.smallRows != mine.smallRows) {
-        VERR("ranks disagree on workspace sizes (check VCCL_BUFFSIZE, VCCL_FUSED_BUFFSIZE, VCCL_LL_BLOCKS and "
-             "VCCL_FUSED_SMALL_M on every rank)");
+          s.smallRows != mine.smallRows || s.tuning != mine.tuning) {
+        VERR("ranks disagree on workspace sizes or algorithm tables (check VCCL_BUFFSIZE, VCCL_FUSED_BUFFSIZE, "
+             "VCCL_LL_BLOCKS, VCCL_FUSED_SMALL_M and VCCL_TUNING_FILE on every rank)");
         return vcclInvalidUsage;
       }
     }

@@ -44,3 +44,8 @@ def test_control_plane_under_sanitizers():
 def test_gemm_index_arithmetic():
     """Tile orders, split-K coverage, epilogue stage slots and split plans (host build of the device math)."""
     assert "tiling: OK" in _run("test_tiling")
+
+
+def test_tuning_tables():
+    """VCCL_TUNING_FILE parsing and rule lookup."""
+    assert "tuning: OK" in _run("test_tuning")

@@ -426,3 +426,17 @@ def test_ring_pass_visits_every_block():
     outs = _run_ranks(n, body)
     for r in range(n):
         assert tuple(outs[r]) == ring_schedule(n, r)
+
+
+def test_tuning_table_from_sweep():
+    from vkccl_b200.bench.collectives import tuning_table
+
+    rows = [
+        {"op": "allreduce", "bytes": 4096, "vccl_us": 5, "vccl_ll_us": 5.0, "vccl_twoshot_us": 20.0},
+        {"op": "allreduce", "bytes": 65536, "vccl_us": 6, "vccl_ll_us": 6.0, "vccl_twoshot_us": 21.0},
+        {"op": "allreduce", "bytes": 4 << 20, "vccl_us": 20, "vccl_ll2_us": 20.0, "vccl_ll_us": 33.0},
+        {"op": "allreduce", "bytes": 256 << 20, "vccl_us": 800, "vccl_nvls_us": 790.0, "vccl_twoshot_us": 900.0},
+        {"op": "allgather", "bytes": 4096, "vccl_us": 8},
+    ]
+    lines = [ln for ln in tuning_table(rows, 8).splitlines() if not ln.startswith("#")]
+    assert lines == ["allreduce 8 65536 ll", "allreduce 8 4194304 ll2", "allreduce 8 0 nvls"]

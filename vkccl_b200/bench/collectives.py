@@ -64,6 +64,28 @@ def make_call(lib: str, op: str, comm, send, recv, n):
     return lambda: comm.broadcast(recv, 0, count=recv.numel(), dtype=dt)
 
 
+def tuning_table(rows, world: int) -> str:
+    """VCCL_TUNING_FILE rules from a sweep: for each all-reduce size, the
+    fastest algorithm timed (vccl_<algo>_us columns); consecutive sizes with
+    the same winner merge into one rule whose max_bytes is the largest size.
+    The last rule has no size limit."""
+    best = []
+    for r in sorted((r for r in rows if r["op"] == "allreduce"), key=lambda r: r["bytes"]):
+        algos = {k[len("vccl_"):-len("_us")]: v for k, v in r.items()
+                 if k.startswith("vccl_") and k.endswith("_us") and k != "vccl_us"}
+        if not algos:
+            continue
+        name = min(algos, key=algos.get)
+        if best and best[-1][1] == name:
+            best[-1] = (r["bytes"], name)
+        else:
+            best.append((r["bytes"], name))
+    lines = ["# op ranks max_bytes algorithm  (measured by vkccl_b200.bench.collectives)"]
+    for i, (size, name) in enumerate(best):
+        lines.append(f"allreduce {world} {0 if i == len(best) - 1 else size} {name}")
+    return "\n".join(lines) + "\n"
+
+
 def time_graph(fn, iters: int, warmup: int) -> float:
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
@@ -101,6 +123,7 @@ def main() -> int:
     ap.add_argument("--libs", default="vccl,nccl")
     ap.add_argument("--algos", default="", help="also time these forced all-reduce algorithms")
     ap.add_argument("--out", default="")
+    ap.add_argument("--tune-out", default="", help="write a VCCL_TUNING_FILE table from the --algos sweep")
     a = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -159,6 +182,9 @@ def main() -> int:
                     print(json.dumps(row), flush=True)
                 size = int(size * a.f)
     comm.destroy()
+    if rank == 0 and a.tune_out:
+        with open(a.tune_out, "w") as f:
+            f.write(tuning_table(rows, world))
     if rank == 0 and a.out:
         with open(a.out, "w") as f:
             for r in rows:
