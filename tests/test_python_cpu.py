@@ -306,7 +306,7 @@ def _mirror_communicator(rank):
     from vkccl_b200.torch_comm import VcclCommunicator
 
     c = VcclCommunicator.__new__(VcclCommunicator)
-    c.world_size, c.rank_in_group, c.vccl, c._outputs = 2, rank, _MirrorComm(rank), {}
+    c.world_size, c.rank_in_group, c.vccl = 2, rank, _MirrorComm(rank)
     return c
 
 

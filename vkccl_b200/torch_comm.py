@@ -12,8 +12,8 @@ through the library.  Differences that follow from the B200 data plane:
   reference's CPU test flow usable.
 * The reference's persistent registered staging buffer per (role, shape,
   dtype) existed to amortise RDMA registration; here the library's
-  symmetric workspace already plays that role, so output buffers are only
-  cached to keep addresses stable for CUDA graphs.
+  symmetric workspace plays that role, and outputs are fresh tensors (under
+  CUDA graph capture they come from the graph's memory pool).
 * Adds what vLLM 0.22's base class exposes beyond the reference:
   ``all_gatherv``, ``reduce_scatterv``, ``gather``, ``batch_isend_irecv``,
   ``dispatch`` / ``combine`` for expert parallelism, and the fused
@@ -93,17 +93,7 @@ class VcclCommunicator(DeviceCommunicatorBase):
         if isinstance(self.device, torch.device) and self.device.type == "cuda":
             cuda_dev = self.device.index if self.device.index is not None else torch.cuda.current_device()
         self.vccl = _c.Communicator(self.world_size, uid, self.rank_in_group, cuda_device=cuda_dev)
-        self._outputs: dict = {}
 
-    # -- helpers -----------------------------------------------------------------
-    def _out(self, role: str, shape, like: torch.Tensor) -> torch.Tensor:
-        """Output buffer cached per (role, shape, dtype, device)."""
-        key = (role, tuple(shape), like.dtype, like.device)
-        t = self._outputs.get(key)
-        if t is None:
-            t = torch.empty(shape, dtype=like.dtype, device=like.device)
-            self._outputs[key] = t
-        return t
 
     # -- collectives -------------------------------------------------------------
     def all_reduce(self, input_: torch.Tensor) -> torch.Tensor:
@@ -259,6 +249,5 @@ class VcclCommunicator(DeviceCommunicatorBase):
 
     def destroy(self) -> None:
         if getattr(self, "vccl", None) is not None:
-            self._outputs = {}
             self.vccl.destroy()
             self.vccl = None
