@@ -204,8 +204,9 @@ class Communicator:
             if cuda_device is not None:
                 import torch
 
+                # Makes the device's primary context current on this thread; the
+                # library (its own static CUDA runtime) finds the device from it.
                 torch.cuda.set_device(cuda_device)
-                _cudart_set_device(cuda_device)
             cfg = _Config(ctypes.sizeof(_Config), 1 if blocking else 0, 0)
             _check(lib().vcclCommInitRankConfig(ctypes.byref(self._comm), nranks, unique_id, rank,
                                                 ctypes.byref(cfg)), "vcclCommInitRank")
@@ -486,14 +487,3 @@ def init_all(ndev: int, devlist: Optional[Sequence[int]] = None) -> List[Communi
     dl = (ctypes.c_int * ndev)(*devlist) if devlist is not None else None
     _check(lib().vcclCommInitAll(arr, ndev, dl), "vcclCommInitAll")
     return [Communicator(ndev, None, i, _handle=arr[i]) for i in range(ndev)]
-
-
-def _cudart_set_device(dev: int) -> None:
-    """Make `dev` current for the library's own CUDA runtime as well."""
-    # libvccl links the CUDA runtime statically; its notion of the current
-    # device is per thread and separate from torch's, so set it explicitly.
-    fn = getattr(lib(), "vcclSetCudaDevice", None)
-    if fn is not None:
-        fn.argtypes = [ctypes.c_int]
-        fn.restype = ctypes.c_int
-        fn(dev)

@@ -32,7 +32,8 @@ def gemm_bf16(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None)
     n = w.shape[0]
     if out is None:
         out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
-    _check(lib().vcclGemmBf16(a.data_ptr(), w.data_ptr(), out.data_ptr(), m, n, k, _stream()), "vcclGemmBf16")
+    with torch.cuda.device(a.device):  # the library launches on the thread's current device
+        _check(lib().vcclGemmBf16(a.data_ptr(), w.data_ptr(), out.data_ptr(), m, n, k, _stream()), "vcclGemmBf16")
     return out
 
 
@@ -53,6 +54,7 @@ def gemm_silu_mul(a: torch.Tensor, w_gu: torch.Tensor, out: torch.Tensor | None 
     n = w_gu.shape[0]
     if out is None:
         out = torch.empty((m, n // 2), dtype=torch.bfloat16, device=a.device)
-    _check(lib().vcclGemmSiluMul(a.data_ptr(), w_gu.data_ptr(), out.data_ptr(), m, n, k, _stream()),
-           "vcclGemmSiluMul")
+    with torch.cuda.device(a.device):
+        _check(lib().vcclGemmSiluMul(a.data_ptr(), w_gu.data_ptr(), out.data_ptr(), m, n, k, _stream()),
+               "vcclGemmSiluMul")
     return out
