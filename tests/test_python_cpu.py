@@ -440,3 +440,38 @@ def test_tuning_table_from_sweep():
     ]
     lines = [ln for ln in tuning_table(rows, 8).splitlines() if not ln.startswith("#")]
     assert lines == ["allreduce 8 65536 ll", "allreduce 8 4194304 ll2", "allreduce 8 0 nvls"]
+
+
+def test_buffer_info_validation():
+    import vkccl_b200 as v
+
+    t = torch.arange(12, dtype=torch.float32).reshape(3, 4)
+    b = v.buffer_info(t, False)
+    assert b.nbytes == 48 and b.dtype == v.DataType.FLOAT32 and not b.cuda
+    with pytest.raises(ValueError):
+        v.buffer_info(t.T, False)  # non-contiguous
+    a = np.zeros(5, dtype=np.float64)
+    assert v.buffer_info(a, True).dtype == v.DataType.FLOAT64
+    ro = np.zeros(3)
+    ro.setflags(write=False)
+    with pytest.raises(ValueError):
+        v.buffer_info(ro, True)
+    assert v.buffer_info(bytearray(16), True).nbytes == 16
+    assert v.buffer_info(None, False).addr == 0
+
+
+def test_single_rank_count_and_dtype_rules():
+    _env()
+    import vkccl_b200 as v
+
+    comm = v.Communicator(1, v.get_unique_id(), 0)
+    try:
+        x = bytearray(64)
+        with pytest.raises(ValueError):
+            comm.all_reduce(x)  # dtype cannot be inferred from a bytearray
+        y = bytearray(64)
+        comm.all_reduce(x, y, count=16, dtype=v.DataType.FLOAT32)
+        with pytest.raises(ValueError):
+            comm.all_reduce(12345, count=None, dtype=v.DataType.FLOAT32)  # raw address needs a count
+    finally:
+        comm.destroy()
