@@ -42,7 +42,10 @@ vcclResult_t vcclAllReduceAddRMSNorm(const void* partial, void* residual, const 
 /* Row-parallel GEMM fused with reduce-scatter over the communicator:
  * every rank computes P = A[M,K] W[N,K]^T, rows of P are owned by rank
  * (row / (M / nranks)); out[M/nranks, N] = sum over ranks of the owned rows.
- * Tiles are pushed to their owner over NVLink from the GEMM epilogue. */
+ * Tiles are pushed to their owner over NVLink from the GEMM epilogue.  Calls
+ * with at most VCCL_FUSED_SMALL_M rows (default 512) run as a (split-K)
+ * GEMM into scratch followed by the LL or push reduce-scatter.  Every rank
+ * calls with the same M, N, K; M % nranks == 0, N % 16 == 0, K % 8 == 0. */
 vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void* out, int M, int N, int K,
                                    vcclComm_t comm, vcclStream_t stream);
 
@@ -50,22 +53,30 @@ vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void* out, int 
  * rank, out = AllGather(X)[M,K] W[N,K]^T.  With siluMul != 0 the epilogue
  * applies silu(gate)*up (W interleaved as for vcclGemmSiluMul; out has N/2
  * columns).  Remote shards are pulled into local memory by copy warps while
- * the tensor cores work on the shards already present. */
+ * the tensor cores work on the shards already present.  Calls with at most
+ * VCCL_FUSED_SMALL_M rows run as an LL all-gather into scratch followed by a
+ * (split-K) GEMM. */
 vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, void* out, int M, int N, int K, int siluMul,
                                vcclComm_t comm, vcclStream_t stream);
 
 /* Expert-parallel MoE dispatch with fp8 e4m3 1x128 block quantisation.
  * x[T,H] bf16, topkIds[T,topk] int32 (global expert ids), topkW[T,topk] f32,
- * experts split evenly over ranks.  recvX receives the bf16 (dequantised)
- * rows this rank's experts must process, in (source rank, token, k) order;
- * recvMeta[i] = {source rank, source token, k, local expert}; *recvCount is
- * written on the device.  capacity bounds rows per rank. */
+ * experts split evenly over ranks.  Rows cross NVLink as e4m3 with one f32
+ * scale (amax / 448) per 128 elements; recvX receives them dequantised to
+ * bf16, the rows this rank's experts must process, in (source rank, token, k)
+ * order; recvMeta[i] = {source rank, source token, k, local expert},
+ * recvW[i] its routing weight; *recvCount is written on the device.
+ * capacity bounds the rows a rank receives (and T * topk <= capacity); rows
+ * past it are dropped and reported as an error.  Every rank passes the same
+ * H, topk, numExperts and capacity.  H % 128 == 0, topk <= 8. */
 vcclResult_t vcclMoeDispatchFp8(const void* x, const int* topkIds, const float* topkW, void* recvX, int* recvMeta,
                                 float* recvW, int* recvCount, int T, int H, int topk, int numExperts, int capacity,
                                 vcclComm_t comm, vcclStream_t stream);
 
-/* Inverse of dispatch: expertOut[rows,H] (bf16) travels back to the source
- * ranks and out[T,H] = sum_k topkW[t,k] * expertOut(t,k). */
+/* Inverse of dispatch: expertOut[rows,H] (bf16, in the received row order)
+ * is scaled by recvW on the expert rank, travels back to the source ranks,
+ * and out[T,H] = sum_k topkW[t,k] * expertOut(t,k).  One combine per
+ * dispatch. */
 vcclResult_t vcclMoeCombine(const void* expertOut, const int* recvMeta, const float* recvW, const int* recvCount,
                             void* out, int T, int H, int topk, int capacity, vcclComm_t comm,
                             vcclStream_t stream);
