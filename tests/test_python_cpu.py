@@ -34,6 +34,9 @@ def test_metadata():
     sizes = {v.DataType.INT8: 1, v.DataType.UINT8: 1, v.DataType.INT32: 4, v.DataType.UINT32: 4,
              v.DataType.INT64: 8, v.DataType.UINT64: 8, v.DataType.FLOAT16: 2, v.DataType.FLOAT32: 4,
              v.DataType.FLOAT64: 8, v.DataType.BFLOAT16: 2}
+    sizes[v.DataType.FLOAT8E4M3] = 1  # additions after the reference's ten types
+    sizes[v.DataType.FLOAT8E5M2] = 1
+    assert int(v.DataType.FLOAT8E4M3) == 10 and int(v.DataType.FLOAT8E5M2) == 11
     for dt, sz in sizes.items():
         assert v.type_size(dt) == sz
     for code in range(7):
