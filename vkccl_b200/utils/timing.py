@@ -147,7 +147,7 @@ def bind_to_gpu_cpus(device_index: int) -> bool:
     try:
         words = nv.nvmlDeviceGetCpuAffinity(h, 16)
         cpus = {64 * w + b for w, mask in enumerate(words) for b in range(64) if (int(mask) >> b) & 1}
-        cpus &= set(range(os.cpu_count() or 1))
+        cpus &= set(os.sched_getaffinity(0))  # stay inside the cores this process may use
         if not cpus:
             return False
         os.sched_setaffinity(0, cpus)
