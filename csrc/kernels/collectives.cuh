@@ -43,6 +43,18 @@ __device__ __forceinline__ void blockRange(size_t total, int parts, int idx, siz
   *hi = b < total ? b : total;
 }
 
+// Block `idx`'s part of a round of `m` units, split as a round of `full`
+// units would be (full >= m).  Multi-round kernels split every round of a
+// launch the same way, so block b only ever touches its own bytes of the
+// staging region: a short last round must not hand block b bytes that a
+// slower block b' (which block b never synchronises with) still reads.
+__device__ __forceinline__ void roundRange(size_t full, size_t m, int parts, int idx, size_t align, size_t* lo,
+                                           size_t* hi) {
+  blockRange(full, parts, idx, align, lo, hi);
+  if (*hi > m) *hi = m;
+  if (*lo > *hi) *lo = *hi;
+}
+
 // ---------------------------------------------------------------------------
 // LL one-shot all-reduce.  Grid is always the communicator's llBlocks so every block's epoch
 // advances once per launch (epochs are equal across blocks and ranks).
@@ -125,12 +137,15 @@ __global__ void __launch_bounds__(512) allReduceTwoShot(DevComm c, CollArgs a, s
   const size_t slotBytes = slotElems * esz;
   if (!blockBarrier(c, blk, kWhereStart)) return;
   const size_t roundElems = slotElems * n;
+  // Chunk size and block split are fixed for the launch (a short last
+  // round is clipped, not re-split), so every block keeps its own slots.
+  const size_t first = a.count < roundElems ? a.count : roundElems;
+  size_t ce = (first + n - 1) / n;
+  ce = (ce + PK - 1) / PK * PK;
+  size_t s0, s1;
+  blockRange(ce, G, blk, PK, &s0, &s1);
   for (size_t base = 0; base < a.count; base += roundElems) {
     const size_t m = (a.count - base) < roundElems ? (a.count - base) : roundElems;
-    size_t ce = (m + n - 1) / n;
-    ce = (ce + PK - 1) / PK * PK;
-    size_t s0, s1;
-    blockRange(ce, G, blk, PK, &s0, &s1);
     // 1. push my contribution to chunk q into rank q's slot `me`
     for (int k = 1; k < n; k++) {
       const int q = (me + k) % n;
@@ -228,24 +243,28 @@ __device__ __forceinline__ void multimemStore16(char* p, const uint4& v) {
 
 // Copy `elems` elements with optional scaling; any alignment on the user side.
 template <typename T>
-__device__ __forceinline__ void copyInScaled(char* dst, const char* src, size_t elems, bool doScale, double s) {
+__device__ __forceinline__ void copyInScaled(char* dst, const char* src, size_t elems, bool doScale, double s,
+                                             size_t tid, size_t nthr) {
   if (!doScale) {
-    copyAny(dst, src, elems * sizeof(T));
+    copyAny(dst, src, elems * sizeof(T), tid, nthr);
   } else if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15u) == 0) {
-    copyScaled<T, true>(dst, src, elems, true, s);
+    copyScaled<T, true>(dst, src, elems, true, s, tid, nthr);
   } else {
-    copyScaled<T, false>(dst, src, elems, true, s);
+    copyScaled<T, false>(dst, src, elems, true, s, tid, nthr);
   }
+}
+template <typename T>
+__device__ __forceinline__ void copyInScaled(char* dst, const char* src, size_t elems, bool doScale, double s) {
+  copyInScaled<T>(dst, src, elems, doScale, s, threadIdx.x, blockDim.x);
 }
 
 // Reduce [lo, hi) of the multicast region through the switch and store the
-// result back to every rank's copy (16-byte units, several in flight).
-template <typename T, int K>
-__device__ __forceinline__ void nvlsReduceRange(char* mc, size_t lo, size_t hi, bool avg, int n) {
-  constexpr int U = 4;
-  const size_t nthr = blockDim.x;
+// result back to every rank's copy (16-byte units, U in flight per thread).
+template <typename T, int K, int U = 4>
+__device__ __forceinline__ void nvlsReduceRange(char* mc, size_t lo, size_t hi, bool avg, int n, size_t tid,
+                                                size_t nthr) {
   const size_t units = (hi - lo + 15) / 16;
-  size_t i = threadIdx.x;
+  size_t i = tid;
   for (; i + (U - 1) * nthr < units; i += U * nthr) {
     uint4 v[U];
 #pragma unroll
@@ -261,16 +280,29 @@ __device__ __forceinline__ void nvlsReduceRange(char* mc, size_t lo, size_t hi, 
       multimemStore16(mc + lo + (i + u * nthr) * 16, v[u]);
     }
   }
-  for (; i < units; i += nthr) {
-    uint4 v = Multimem<T, K>::ldReduce(mc + lo + i * 16);
-    if (avg) {
-      Pack<T> p;
-      p.load(v);
-      p.scale(1.0 / n);
-      v = p.pack();
+  // Fewer than U * nthr units remain: one guarded batch keeps every
+  // thread's remaining loads in flight together.
+  if (i < units) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; u++)
+      if (i + u * nthr < units) v[u] = Multimem<T, K>::ldReduce(mc + lo + (i + u * nthr) * 16);
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      if (i + u * nthr >= units) break;
+      if (avg) {
+        Pack<T> p;
+        p.load(v[u]);
+        p.scale(1.0 / n);
+        v[u] = p.pack();
+      }
+      multimemStore16(mc + lo + (i + u * nthr) * 16, v[u]);
     }
-    multimemStore16(mc + lo + i * 16, v);
   }
+}
+template <typename T, int K>
+__device__ __forceinline__ void nvlsReduceRange(char* mc, size_t lo, size_t hi, bool avg, int n) {
+  nvlsReduceRange<T, K>(mc, lo, hi, avg, n, threadIdx.x, blockDim.x);
 }
 
 template <typename T, int K>
@@ -280,12 +312,16 @@ __global__ void __launch_bounds__(512) allReduceNvls(DevComm c, CollArgs a, size
   const size_t total = a.count * esz;
   if (!blockBarrier(c, blk, kWhereStart)) return;
   char* local = c.data[me];
-  for (size_t off = 0; off < total; off += roundBytes) {
-    const size_t m = (total - off) < roundBytes ? (total - off) : roundBytes;
-    size_t cb = (m + n - 1) / n;
-    cb = (cb + 15) / 16 * 16;
-    size_t s0, s1;
-    blockRange(cb, G, blk, 16, &s0, &s1);
+  // One chunk size for every round of the launch (see roundRange): a single
+  // round takes ceil(total / n) rounded up to 16 bytes (n * cb fits because
+  // roundBytes leaves 16 bytes per rank spare), longer messages full rounds.
+  size_t cb = total <= roundBytes ? (total + n - 1) / n : roundBytes / n;
+  cb = total <= roundBytes ? (cb + 15) / 16 * 16 : cb / 16 * 16;
+  const size_t step = cb * n;
+  size_t s0, s1;
+  blockRange(cb, G, blk, 16, &s0, &s1);
+  for (size_t off = 0; off < total; off += step) {
+    const size_t m = (total - off) < step ? (total - off) : step;
     // 1. copy in: my sub-slice of every chunk
     for (int q = 0; q < n; q++) {
       const size_t lo = q * cb + s0;
@@ -314,6 +350,86 @@ __global__ void __launch_bounds__(512) allReduceNvls(DevComm c, CollArgs a, size
 }
 
 // ---------------------------------------------------------------------------
+// Pipelined NVLS all-reduce.  The message is cut into pieces of n * cb bytes
+// (cb per rank chunk, a multiple of 16) that rotate through kPipeSlots
+// staging slots of slotBytes.  Step s copies piece s in, reduces piece s-1
+// through the switch and copies piece s-2 out, each with its own warps, and
+// then meets the peers once, so the HBM copies of one piece overlap the
+// NVLink traffic of the next.  Block b owns the same bytes
+// [q*cb + s0, q*cb + s1) of every slot for every piece, so blocks never
+// touch each other's staging, and the barrier after each step orders block
+// b's uses of a slot across ranks:
+//   reduce(p)   at step p+1 reads what every rank copied in at step p,
+//   copy-out(p) at step p+2 reads what the owners stored at step p+1,
+//   copy-in(p+3) at step p+3 refills the slot after both.
+// The three uses within a step are on three different slots.
+// Warps [0, kPipeInWarps) copy in, the next kPipeRedWarps reduce, the rest
+// (of the 16 launched) copy out.
+// ---------------------------------------------------------------------------
+constexpr int kPipeSlots = 3;
+constexpr int kPipeInWarps = 4;
+constexpr int kPipeRedWarps = 8;
+constexpr int kPipeThreads = 512;
+
+template <typename T, int K>
+__global__ void __launch_bounds__(kPipeThreads) allReduceNvlsPipe(DevComm c, CollArgs a, size_t cb,
+                                                                  size_t slotBytes) {
+  const int blk = blockIdx.x, G = gridDim.x, n = c.nranks, me = c.rank;
+  const size_t esz = sizeof(T);
+  const size_t total = a.count * esz;
+  const size_t piece = cb * n;
+  const size_t P = (total + piece - 1) / piece;
+  const int warp = static_cast<int>(threadIdx.x) / 32;
+  const int role = warp < kPipeInWarps ? 0 : (warp < kPipeInWarps + kPipeRedWarps ? 1 : 2);
+  const int roleBase = role == 0 ? 0 : (role == 1 ? kPipeInWarps : kPipeInWarps + kPipeRedWarps);
+  const int roleWarps = role == 0 ? kPipeInWarps : (role == 1 ? kPipeRedWarps : 16 - kPipeInWarps - kPipeRedWarps);
+  const size_t tid = threadIdx.x - roleBase * 32;
+  const size_t nthr = static_cast<size_t>(roleWarps) * 32;
+  size_t s0, s1;
+  blockRange(cb, G, blk, 16, &s0, &s1);
+  if (!blockBarrier(c, blk, kWhereStart)) return;
+  char* local = c.data[me];
+  for (size_t st = 0; st < P + 2; st++) {
+    if (role == 0 && st < P) {
+      const size_t off = st * piece;
+      const size_t m = (total - off) < piece ? (total - off) : piece;
+      char* slot = local + (st % kPipeSlots) * slotBytes;
+      for (int q = 0; q < n; q++) {
+        const size_t lo = q * cb + s0;
+        const size_t hiRaw = q * cb + s1;
+        const size_t hi = hiRaw < m ? hiRaw : m;
+        if (lo < hi) copyInScaled<T>(slot + lo, a.send + off + lo, (hi - lo) / esz, a.premul, a.scalar, tid, nthr);
+      }
+    } else if (role == 1 && st >= 1 && st <= P) {
+      if constexpr (HasMultimem<T, K>::value) {
+        const size_t p = st - 1;
+        const size_t off = p * piece;
+        const size_t m = (total - off) < piece ? (total - off) : piece;
+        const size_t lo = me * cb + s0;
+        const size_t hiRaw = me * cb + s1;
+        const size_t hi = hiRaw < m ? hiRaw : m;
+        if (lo < hi)
+          nvlsReduceRange<T, K, 8>(c.mcData + (p % kPipeSlots) * slotBytes, lo, hi, a.avg != 0, n, tid, nthr);
+      }
+    } else if (role == 2 && st >= 2) {
+      const size_t p = st - 2;
+      const size_t off = p * piece;
+      const size_t m = (total - off) < piece ? (total - off) : piece;
+      const char* slot = local + (p % kPipeSlots) * slotBytes;
+      for (int q = 0; q < n; q++) {
+        const size_t lo = q * cb + s0;
+        const size_t hiRaw = q * cb + s1;
+        const size_t hi = hiRaw < m ? hiRaw : m;
+        if (lo < hi) copyAny(a.recv + off + lo, slot + lo, hi - lo, tid, nthr);
+      }
+    }
+    if (st == P + 1) break;  // the last step only copies out
+    fenceProxyAlias();
+    if (!blockBarrier(c, blk, kWhereNvls)) return;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Reduce-scatter: push chunk q to rank q's slot, reduce locally.
 // ---------------------------------------------------------------------------
 template <typename T, int K, bool VEC>
@@ -326,10 +442,11 @@ __global__ void __launch_bounds__(512) reduceScatterPush(DevComm c, CollArgs a, 
   if (!blockBarrier(c, blk, kWhereStart)) return;
   const size_t rc = a.count;
   int k = 0;
+  const size_t full = rc < slotElems ? rc : slotElems;
   for (size_t base = 0; base < rc; base += slotElems, k++) {
     const size_t m = (rc - base) < slotElems ? (rc - base) : slotElems;
     size_t s0, s1;
-    blockRange(m, G, blk, PK, &s0, &s1);
+    roundRange(full, m, G, blk, PK, &s0, &s1);
     const size_t hoff = (k & 1) * half;
     if (s0 < s1) {
       for (int s = 1; s < n; s++) {

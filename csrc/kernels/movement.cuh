@@ -26,7 +26,7 @@ __global__ void __launch_bounds__(512) allGatherPull(DevComm c, const char* send
   for (size_t off = 0; off < bytes; off += half, k++) {
     const size_t m = (bytes - off) < half ? (bytes - off) : half;
     size_t lo, hi;
-    blockRange(m, G, blk, 16, &lo, &hi);
+    roundRange(bytes < half ? bytes : half, m, G, blk, 16, &lo, &hi);
     const size_t hoff = (k & 1) * half;
     if (lo < hi) {
       copyAny(c.data[me] + hoff + lo, send + off + lo, hi - lo);
@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(512) broadcastPull(DevComm c, const char* send
   for (size_t off = 0; off < bytes; off += half, k++) {
     const size_t m = (bytes - off) < half ? (bytes - off) : half;
     size_t lo, hi;
-    blockRange(m, G, blk, 16, &lo, &hi);
+    roundRange(bytes < half ? bytes : half, m, G, blk, 16, &lo, &hi);
     const size_t hoff = (k & 1) * half;
     if (me == root && lo < hi) {
       copyAny(c.data[root] + hoff + lo, send + off + lo, hi - lo);
@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(512) broadcastNvls(DevComm c, const char* send
   for (size_t off = 0; off < bytes; off += half, k++) {
     const size_t m = (bytes - off) < half ? (bytes - off) : half;
     size_t lo, hi;
-    blockRange(m, G, blk, 16, &lo, &hi);
+    roundRange(bytes < half ? bytes : half, m, G, blk, 16, &lo, &hi);
     const size_t hoff = (k & 1) * half;
     if (me == root && lo < hi) {
       const bool al = (reinterpret_cast<uintptr_t>(send + off) & 15u) == 0;

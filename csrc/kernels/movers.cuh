@@ -21,10 +21,13 @@ namespace dev {
 
 constexpr int kUnroll = 8;
 
+// Every mover takes the calling thread's index `tid` among the `nthr`
+// threads that share the work; the short forms use the whole block.  A
+// kernel that splits its warps into roles passes each role's own range.
+
 // n16 16-byte units, dst and src 16-byte aligned.
-__device__ __forceinline__ void copy16(char* dst, const char* src, size_t n16) {
-  const size_t nthr = blockDim.x;
-  size_t i = threadIdx.x;
+__device__ __forceinline__ void copy16(char* dst, const char* src, size_t n16, size_t tid, size_t nthr) {
+  size_t i = tid;
   for (; i + (kUnroll - 1) * nthr < n16; i += kUnroll * nthr) {
     uint4 v[kUnroll];
 #pragma unroll
@@ -35,35 +38,43 @@ __device__ __forceinline__ void copy16(char* dst, const char* src, size_t n16) {
   for (; i < n16; i += nthr) stG(dst + i * 16, ldCG(src + i * 16));
 }
 
+__device__ __forceinline__ void copy16(char* dst, const char* src, size_t n16) {
+  copy16(dst, src, n16, threadIdx.x, blockDim.x);
+}
+
 // Byte copy choosing the widest access the alignment allows.
-__device__ __forceinline__ void copyAny(char* dst, const char* src, size_t n) {
+__device__ __forceinline__ void copyAny(char* dst, const char* src, size_t n, size_t tid, size_t nthr) {
   if (n == 0 || dst == src) return;
   const uintptr_t al = reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src);
   if ((al & 15u) == 0) {
-    copy16(dst, src, n / 16);
-    for (size_t i = n / 16 * 16 + threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+    copy16(dst, src, n / 16, tid, nthr);
+    for (size_t i = n / 16 * 16 + tid; i < n; i += nthr) dst[i] = src[i];
   } else if ((al & 3u) == 0) {
     const uint32_t* s = reinterpret_cast<const uint32_t*>(src);
     uint32_t* d = reinterpret_cast<uint32_t*>(dst);
-    for (size_t i = threadIdx.x; i < n / 4; i += blockDim.x) d[i] = s[i];
-    for (size_t i = n / 4 * 4 + threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+    for (size_t i = tid; i < n / 4; i += nthr) d[i] = s[i];
+    for (size_t i = n / 4 * 4 + tid; i < n; i += nthr) dst[i] = src[i];
   } else {
-    for (size_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+    for (size_t i = tid; i < n; i += nthr) dst[i] = src[i];
   }
+}
+__device__ __forceinline__ void copyAny(char* dst, const char* src, size_t n) {
+  copyAny(dst, src, n, threadIdx.x, blockDim.x);
 }
 
 // dst[i] = src[i] * s (PreMulSum contribution) for `elems` elements.
 template <typename T, bool VEC>
-__device__ __forceinline__ void copyScaled(char* dst, const char* src, size_t elems, bool doScale, double s) {
+__device__ __forceinline__ void copyScaled(char* dst, const char* src, size_t elems, bool doScale, double s,
+                                           size_t tid, size_t nthr) {
   if (!doScale) {
     if constexpr (VEC) {
-      copy16(dst, src, elems * sizeof(T) / 16);
+      copy16(dst, src, elems * sizeof(T) / 16, tid, nthr);
       const size_t done = elems * sizeof(T) / 16 * 16 / sizeof(T);
       const T* sp = reinterpret_cast<const T*>(src);
       T* dp = reinterpret_cast<T*>(dst);
-      for (size_t i = done + threadIdx.x; i < elems; i += blockDim.x) dp[i] = sp[i];
+      for (size_t i = done + tid; i < elems; i += nthr) dp[i] = sp[i];
     } else {
-      copyAny(dst, src, elems * sizeof(T));
+      copyAny(dst, src, elems * sizeof(T), tid, nthr);
     }
     return;
   }
@@ -71,8 +82,7 @@ __device__ __forceinline__ void copyScaled(char* dst, const char* src, size_t el
   if constexpr (VEC) {
     constexpr int N = 16 / sizeof(T);
     const size_t packs = elems / N;
-    const size_t nthr = blockDim.x;
-    size_t i = threadIdx.x;
+    size_t i = tid;
     for (; i + (kUnroll - 1) * nthr < packs; i += kUnroll * nthr) {
       uint4 v[kUnroll];
 #pragma unroll
@@ -85,7 +95,11 @@ __device__ __forceinline__ void copyScaled(char* dst, const char* src, size_t el
   }
   const T* sp = reinterpret_cast<const T*>(src);
   T* dp = reinterpret_cast<T*>(dst);
-  for (size_t i = done + threadIdx.x; i < elems; i += blockDim.x) dp[i] = scaledElem<T>(sp[i], true, s);
+  for (size_t i = done + tid; i < elems; i += nthr) dp[i] = scaledElem<T>(sp[i], true, s);
+}
+template <typename T, bool VEC>
+__device__ __forceinline__ void copyScaled(char* dst, const char* src, size_t elems, bool doScale, double s) {
+  copyScaled<T, VEC>(dst, src, elems, doScale, s, threadIdx.x, blockDim.x);
 }
 
 // out[i] = fold(own[i] * premul?, slots[p][i] for p != me) * (1/n if avg).

@@ -34,6 +34,7 @@ LaunchCtx launchCtxFor(const DeviceState& ds, cudaStream_t s) {
   lc.llMax = ds.llMaxBytes;
   lc.llAgMax = ds.llAgMaxBytes;
   lc.llBlocks = ds.llBlocks;
+  lc.nvlsPieces = ds.nvlsPieces;
   return lc;
 }
 
@@ -256,6 +257,8 @@ ArAlgo pickAllReduce(const HostOp& h, size_t bytes) {
     if (ll2Ok) return ArAlgo::LL2;
   } else if (force == "nvls") {
     if (nvlsOk) return ArAlgo::Nvls;
+  } else if (force == "nvls_pipe") {
+    if (nvlsOk) return ArAlgo::NvlsPipe;
   } else if (force == "twoshot" || force == "ring") {
     return ArAlgo::TwoShot;
   }
@@ -265,7 +268,7 @@ ArAlgo pickAllReduce(const HostOp& h, size_t bytes) {
   // two-shot: it only wins from four ranks on.
   if (nvlsOk && h.comm->nranks >= envLong("VCCL_NVLS_MIN_RANKS", 4) &&
       bytes >= envBytes("VCCL_NVLS_MIN", 512u << 10))
-    return ArAlgo::Nvls;
+    return ds.nvlsPipeMin != 0 && bytes >= ds.nvlsPipeMin ? ArAlgo::NvlsPipe : ArAlgo::Nvls;
   return ArAlgo::TwoShot;
 }
 
@@ -378,6 +381,7 @@ const char* algoName(ArAlgo a) {
     case ArAlgo::LL: return "one-shot LL";
     case ArAlgo::LL2: return "two-hop LL";
     case ArAlgo::Nvls: return "NVLS multimem";
+    case ArAlgo::NvlsPipe: return "NVLS multimem, pipelined";
     case ArAlgo::TwoShot: return "two-shot";
   }
   return "?";

@@ -64,6 +64,8 @@ struct DeviceState {
   unsigned long long* fusedTrace = nullptr;  // per-CTA event times of the last AG+GEMM (VCCL_FUSED_TRACE=1)
   std::vector<TuningRule> tuning;  // measured algorithm table (VCCL_TUNING_FILE)
   size_t ll2MaxBytes = 0;          // two-hop LL all-reduce threshold
+  size_t nvlsPipeMin = 0;          // pipelined NVLS all-reduce from this size (0: only when asked for)
+  int nvlsPieces = 4;              // pieces of a pipelined NVLS all-reduce
 };
 
 struct CustomOp {

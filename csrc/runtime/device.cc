@@ -240,6 +240,12 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
   ds->llMaxBytes = envBytes("VCCL_LL_MAX", llDefault);
   if (ds->llMaxBytes > dev::kLLMaxBytes) ds->llMaxBytes = dev::kLLMaxBytes;
   ds->ll2MaxBytes = envBytes("VCCL_LL2_MAX", 4u << 20);
+  // Pipelined NVLS all-reduce: off by default until it is measured on this
+  // machine; VCCL_NVLS_PIPE_MIN=<bytes> turns it on from that size, and
+  // VCCL_ALLREDUCE_ALGO=nvls_pipe or a tuning rule picks it per call.
+  ds->nvlsPipeMin = envBytes("VCCL_NVLS_PIPE_MIN", 0);
+  ds->nvlsPieces = static_cast<int>(envLong("VCCL_NVLS_PIECES", 4));
+  if (ds->nvlsPieces < 1) ds->nvlsPieces = 1;
   // An LL all-gather moves the same (n-1) x 2 x payload as the one-shot LL
   // all-reduce and needs no barrier.  At 8 ranks with 1 MiB per rank the LL
   // all-reduce (same traffic) took 33 us where the pull all-gather took

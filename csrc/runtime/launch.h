@@ -11,7 +11,7 @@
 
 namespace vccl {
 
-enum class ArAlgo : int { LL = 0, TwoShot = 1, Nvls = 2, LL2 = 3 };
+enum class ArAlgo : int { LL = 0, TwoShot = 1, Nvls = 2, LL2 = 3, NvlsPipe = 4 };
 
 struct LaunchCtx {
   dev::DevComm dc;
@@ -21,6 +21,7 @@ struct LaunchCtx {
   size_t llMax;    // largest per-rank payload sent with the LL protocol
   size_t llAgMax;  // the same for all-gather (no reduction, so LL pays off further)
   int llBlocks;    // grid of every LL kernel (fixed per communicator)
+  int nvlsPieces;  // pieces of a pipelined NVLS all-reduce
 };
 
 struct DeviceState;
@@ -46,6 +47,10 @@ cudaError_t launchScaleCopy(cudaStream_t s, vcclDataType_t dt, void* dst, const 
                             double scale);
 
 bool nvlsSupports(vcclDataType_t dt, int redKind);
+// Pipelined NVLS all-reduce geometry: bytes per staging slot, and the per-rank
+// chunk of one piece (a multiple of 16, n * chunk fits in a slot).
+size_t nvlsPipeSlotBytes(size_t dataBytes);
+size_t nvlsPipeChunk(size_t bytes, int n, int pieces, size_t dataBytes);
 int gridFor(size_t bytes, int maxBlocks);
 
 }  // namespace vccl

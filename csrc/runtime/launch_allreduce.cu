@@ -21,6 +21,18 @@ int gridFor(size_t bytes, int maxBlocks) {
   return static_cast<int>(g);
 }
 
+size_t nvlsPipeSlotBytes(size_t dataBytes) {
+  return (dataBytes - 16 * dev::kMaxRanks) / dev::kPipeSlots / 16 * 16;
+}
+
+size_t nvlsPipeChunk(size_t bytes, int n, int pieces, size_t dataBytes) {
+  const size_t maxCb = nvlsPipeSlotBytes(dataBytes) / n / 16 * 16;
+  const size_t piece = (bytes + pieces - 1) / pieces;
+  size_t cb = ((piece + n - 1) / n + 15) / 16 * 16;
+  if (cb > maxCb) cb = maxCb;
+  return cb < 16 ? 16 : cb;
+}
+
 bool nvlsSupports(vcclDataType_t dt, int k) {
   if (k == dev::kSum) return dt == vcclFloat32 || dt == vcclBfloat16 || dt == vcclFloat16;
   if (k == dev::kMin || k == dev::kMax) return dt == vcclBfloat16 || dt == vcclFloat16;
@@ -69,6 +81,32 @@ cudaError_t launchAllReduce(const LaunchCtx& lc, ArAlgo algo, vcclDataType_t dt,
         VCCL_DISPATCH_OP(redKind, {
           if constexpr (dev::HasMultimem<__half, K>::value)
             dev::allReduceNvls<__half, K><<<g, kThreads, 0, lc.stream>>>(lc.dc, a, roundBytes);
+        })
+        break;
+      default:
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+  }
+  if (algo == ArAlgo::NvlsPipe) {
+    if (!lc.nvls || !nvlsSupports(dt, redKind) || a.root >= 0) return cudaErrorInvalidValue;
+    const size_t cb = nvlsPipeChunk(bytes, n, lc.nvlsPieces, lc.dc.dataBytes);
+    const size_t slotBytes = nvlsPipeSlotBytes(lc.dc.dataBytes);
+    const int g = gridFor(bytes / n, lc.nblocks);
+    switch (dt) {
+      case vcclFloat32:
+        dev::allReduceNvlsPipe<float, dev::kSum><<<g, dev::kPipeThreads, 0, lc.stream>>>(lc.dc, a, cb, slotBytes);
+        break;
+      case vcclBfloat16:
+        VCCL_DISPATCH_OP(redKind, {
+          if constexpr (dev::HasMultimem<__nv_bfloat16, K>::value)
+            dev::allReduceNvlsPipe<__nv_bfloat16, K><<<g, dev::kPipeThreads, 0, lc.stream>>>(lc.dc, a, cb, slotBytes);
+        })
+        break;
+      case vcclFloat16:
+        VCCL_DISPATCH_OP(redKind, {
+          if constexpr (dev::HasMultimem<__half, K>::value)
+            dev::allReduceNvlsPipe<__half, K><<<g, dev::kPipeThreads, 0, lc.stream>>>(lc.dc, a, cb, slotBytes);
         })
         break;
       default:

@@ -348,7 +348,7 @@ void algoAB(vcclComm_t c, int me, int n, size_t cnt) {
   std::vector<float> s(cnt), r(cnt);
   fill(s.data(), vcclFloat32, me, cnt);
   for (vcclRedOp_t op : {vcclSum, vcclMax}) {
-    for (const char* algo : {"ring", "recdouble", "twoshot", "ll", "ll2", "nvls"}) {
+    for (const char* algo : {"ring", "recdouble", "twoshot", "ll", "ll2", "nvls", "nvls_pipe"}) {
       setenv("VCCL_ALLREDUCE_ALGO", algo, 1);
       std::fill(r.begin(), r.end(), -7.0f);
       EXPECT_OK(vcclAllReduce(s.data(), r.data(), cnt, vcclFloat32, op, c));
@@ -370,7 +370,7 @@ void deviceSweep(vcclComm_t c, int me, int n) {
       cudaMalloc(&ds, cnt * es);
       cudaMalloc(&dr, cnt * es);
       cudaMemcpy(ds, h.data(), cnt * es, cudaMemcpyHostToDevice);
-      for (const char* algo : {"", "ll", "ll2", "twoshot", "nvls"}) {
+      for (const char* algo : {"", "ll", "ll2", "twoshot", "nvls", "nvls_pipe"}) {
         if (*algo) setenv("VCCL_ALLREDUCE_ALGO", algo, 1);
         else unsetenv("VCCL_ALLREDUCE_ALGO");
         cudaMemset(dr, 0, cnt * es);
@@ -420,6 +420,41 @@ void deviceSweep(vcclComm_t c, int me, int n) {
   }
 }
 
+// Messages larger than the staging region: the two-shot and NVLS kernels run
+// several rounds with a short last one, the pipelined NVLS kernel reuses its
+// slots.  Checked on a stride plus the whole tail.
+void multiRound(vcclComm_t c, int me, int n) {
+  const size_t cnt = (80u << 20) + 4099;  // > 320 MiB of fp32
+  const size_t bytes = cnt * sizeof(float);
+  std::vector<float> h(cnt), out(cnt);
+  fill(h.data(), vcclFloat32, me, cnt);
+  void *ds = nullptr, *dr = nullptr;
+  if (cudaMalloc(&ds, bytes) != cudaSuccess || cudaMalloc(&dr, bytes) != cudaSuccess) {
+    std::fprintf(stderr, "FAIL multi-round: no device memory\n");
+    gFail++;
+    return;
+  }
+  cudaMemcpy(ds, h.data(), bytes, cudaMemcpyHostToDevice);
+  for (const char* algo : {"twoshot", "nvls", "nvls_pipe"}) {
+    setenv("VCCL_ALLREDUCE_ALGO", algo, 1);
+    cudaMemset(dr, 0, bytes);
+    EXPECT_OK(vcclAllReduceAsync(ds, dr, cnt, vcclFloat32, vcclSum, c, nullptr));
+    cudaDeviceSynchronize();
+    cudaMemcpy(out.data(), dr, bytes, cudaMemcpyDeviceToHost);
+    for (size_t i = 0; i < cnt; i += (i + 70000 < cnt ? 997 : 1)) {
+      if (!near(out[i], expect(vcclSum, n, i), vcclFloat32)) {
+        std::fprintf(stderr, "FAIL multi-round allreduce algo=%s i=%zu got %g want %g\n", algo, i, out[i],
+                     expect(vcclSum, n, i));
+        gFail++;
+        break;
+      }
+    }
+  }
+  unsetenv("VCCL_ALLREDUCE_ALGO");
+  cudaFree(ds);
+  cudaFree(dr);
+}
+
 int rankMain(int me, int n, const vcclUniqueId& id, bool full) {
   cudaSetDevice(me);
   vcclComm_t c = nullptr;
@@ -457,6 +492,7 @@ int rankMain(int me, int n, const vcclUniqueId& id, bool full) {
   algoAB(c, me, n, 1000);
   algoAB(c, me, n, 70000);
   if (full) deviceSweep(c, me, n);
+  if (full) multiRound(c, me, n);
   EXPECT_OK(vcclCommDestroy(c));
   if (gFail) std::fprintf(stderr, "rank %d/%d: %d failures\n", me, n, gFail);
   return gFail ? 1 : 0;

@@ -515,3 +515,207 @@ def test_p2p_ring_protocol(slots):
     for seed in range(200):
         msgs = [rng.randint(1, 9) for _ in range(rng.randint(1, 5))]
         assert run_p2p_ring(msgs, slots, seed) == []
+
+
+# ---------------------------------------------------------------------------
+# NVLS all-reduce staging (csrc/kernels/collectives.cuh, allReduceNvls and
+# allReduceNvlsPipe).  Sizes are in 16-byte units.  Each staging unit of each
+# rank holds (call, piece, phase): 'in' after the copy-in, 'red' after the
+# owner's multimem store, 'out' once the copy-out has read it.  Block b of
+# every rank meets only block b of the others (blockBarrier).
+# ---------------------------------------------------------------------------
+def block_range(total, parts, idx):
+    per = -(-total // parts)
+    lo = min(per * idx, total)
+    return lo, min(lo + per, total)
+
+
+class StagingModel:
+    def __init__(self, n, blocks, seed):
+        self.sim = Sim(seed)
+        self.n, self.blocks = n, blocks
+        self.cell = {}                 # (rank, unit) -> (call, piece, phase)
+        self.bar = defaultdict(int)    # (rank, block) -> barriers passed
+        self.errors = []
+
+    def barrier(self, r, b):
+        self.bar[(r, b)] += 1
+        t = self.bar[(r, b)]
+        yield lambda: all(self.bar[(q, b)] >= t for q in range(self.n))
+
+    def copy_in(self, r, unit, k, p):
+        old = self.cell.get((r, unit))
+        if old is not None and old[2] != "out":
+            self.errors.append(f"rank {r} call {k} piece {p} overwrote unit {unit} holding {old}")
+        self.cell[(r, unit)] = (k, p, "in")
+
+    def reduce(self, unit, k, p):
+        """multimem.ld_reduce of one unit, then (later) the multimem store."""
+        for q in range(self.n):
+            if self.cell.get((q, unit)) != (k, p, "in"):
+                self.errors.append(f"call {k} piece {p} reduced unit {unit} of rank {q}: {self.cell.get((q, unit))}")
+        yield lambda: True
+        for q in range(self.n):
+            self.cell[(q, unit)] = (k, p, "red")
+
+    def copy_out(self, r, unit, k, p):
+        if self.cell.get((r, unit)) != (k, p, "red"):
+            self.errors.append(f"rank {r} call {k} piece {p} copied out unit {unit}: {self.cell.get((r, unit))}")
+        self.cell[(r, unit)] = (k, p, "out")
+
+    def run(self, calls, block_fn):
+        def make(r):
+            def mk(k):
+                live = {"done": 0, "count": self.blocks}
+
+                def blk(b):
+                    yield from block_fn(r, b, k)
+                    live["done"] += 1
+
+                live["procs"] = [blk(b) for b in range(self.blocks)]
+                return live
+            return mk
+
+        for r in range(self.n):
+            self.sim.spawn(kernel_chain(self.sim, calls, make(r)))
+        self.sim.run()
+        return self.errors
+
+
+def run_nvls_rounds(n, blocks, total, round_units, calls, seed, fixed_split=True):
+    """allReduceNvls: copy in, barrier, reduce own chunk, barrier, copy out,
+    round after round through one staging region."""
+    M = StagingModel(n, blocks, seed)
+    rng = M.sim.rng
+    if fixed_split:
+        cb = -(-total // n) if total <= round_units else round_units // n
+    step = None
+
+    def block_fn(r, b, k):
+        yield from M.barrier(r, b)
+        off, p = 0, 0
+        while off < total:
+            if fixed_split:
+                cbr = cb
+                m = min(total - off, cb * n)
+            else:  # split every round afresh (the short last round re-splits)
+                m = min(total - off, round_units)
+                cbr = -(-m // n)
+            s0, s1 = block_range(cbr, blocks, b)
+            ins = [q * cbr + u for q in range(n) for u in range(s0, s1) if q * cbr + u < m]
+            rng.shuffle(ins)
+            for unit in ins:
+                yield lambda: True
+                M.copy_in(r, unit, k, p)
+            yield from M.barrier(r, b)
+            for unit in range(r * cbr + s0, min(r * cbr + s1, m)):
+                yield lambda: True
+                yield from M.reduce(unit, k, p)
+            yield from M.barrier(r, b)
+            for unit in ins:
+                yield lambda: True
+                M.copy_out(r, unit, k, p)
+            off += m
+            p += 1
+
+    return M.run(calls, block_fn)
+
+
+def run_nvls_pipe(n, blocks, total, slot_units, pieces, calls, seed):
+    """allReduceNvlsPipe: three slots; step s copies piece s in, reduces piece
+    s-1 and copies piece s-2 out (three warp roles, interleaved at random),
+    then one barrier."""
+    M = StagingModel(n, blocks, seed)
+    rng = M.sim.rng
+    cb = min(-(-(-(-total // pieces)) // n), slot_units // n)
+    cb = max(cb, 1)
+    piece = cb * n
+    P = -(-total // piece)
+
+    def m_of(p):
+        return min(piece, total - p * piece)
+
+    def block_fn(r, b, k):
+        s0, s1 = block_range(cb, blocks, b)
+        yield from M.barrier(r, b)
+        for st in range(P + 2):
+            ops = []
+            if st < P:
+                ops += [("in", st, (st % 3) * slot_units + q * cb + u)
+                        for q in range(n) for u in range(s0, s1) if q * cb + u < m_of(st)]
+            if 1 <= st <= P:
+                p = st - 1
+                ops += [("red", p, (p % 3) * slot_units + r * cb + u)
+                        for u in range(s0, s1) if r * cb + u < m_of(p)]
+            if st >= 2:
+                p = st - 2
+                ops += [("out", p, (p % 3) * slot_units + q * cb + u)
+                        for q in range(n) for u in range(s0, s1) if q * cb + u < m_of(p)]
+            rng.shuffle(ops)
+            for kind, p, unit in ops:
+                yield lambda: True
+                if kind == "in":
+                    M.copy_in(r, unit, k, p)
+                elif kind == "red":
+                    yield from M.reduce(unit, k, p)
+                else:
+                    M.copy_out(r, unit, k, p)
+            if st == P + 1:
+                break
+            yield from M.barrier(r, b)
+
+    return M.run(calls, block_fn)
+
+
+@pytest.mark.parametrize("n,blocks,total", [(2, 2, 37), (3, 3, 50), (4, 2, 29)])
+def test_nvls_round_protocol(n, blocks, total):
+    for seed in range(60):
+        assert run_nvls_rounds(n, blocks, total, round_units=16, calls=3, seed=seed) == []
+
+
+def test_model_detects_resplit_last_round():
+    """Splitting the short last round afresh hands a block units that a slower
+    block still reads; the checker must see it (the kernels keep the split)."""
+    assert any(run_nvls_rounds(2, 3, 37, round_units=16, calls=2, seed=s, fixed_split=False) for s in range(300))
+
+
+@pytest.mark.parametrize("n,blocks,total,pieces", [(2, 2, 37, 4), (3, 2, 50, 3), (4, 3, 64, 4), (2, 3, 9, 4),
+                                                   (3, 1, 200, 2)])
+def test_nvls_pipe_protocol(n, blocks, total, pieces):
+    for seed in range(60):
+        assert run_nvls_pipe(n, blocks, total, slot_units=24, pieces=pieces, calls=3, seed=seed) == []
+
+
+def test_model_detects_two_slot_pipe():
+    """With two slots, copy-in of piece s lands in the slot whose piece s-2 is
+    still being copied out in the same step."""
+    def two_slots(seed):
+        M = StagingModel(2, 1, seed)
+        rng = M.sim.rng
+        n, cb, P = 2, 2, 4
+
+        def block_fn(r, b, k):
+            yield from M.barrier(r, b)
+            for st in range(P + 2):
+                ops = []
+                if st < P:
+                    ops += [("in", st, (st % 2) * 8 + u) for u in range(n * cb)]
+                if 1 <= st <= P:
+                    ops += [("red", st - 1, ((st - 1) % 2) * 8 + r * cb + u) for u in range(cb)]
+                if st >= 2:
+                    ops += [("out", st - 2, ((st - 2) % 2) * 8 + u) for u in range(n * cb)]
+                rng.shuffle(ops)
+                for kind, p, unit in ops:
+                    yield lambda: True
+                    if kind == "in":
+                        M.copy_in(r, unit, k, p)
+                    elif kind == "red":
+                        yield from M.reduce(unit, k, p)
+                    else:
+                        M.copy_out(r, unit, k, p)
+                if st < P + 1:
+                    yield from M.barrier(r, b)
+
+        return M.run(2, block_fn)
+
+    assert any(two_slots(s) for s in range(100))
