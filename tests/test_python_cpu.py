@@ -478,3 +478,36 @@ def test_single_rank_count_and_dtype_rules():
             comm.all_reduce(12345, count=None, dtype=v.DataType.FLOAT32)  # raw address needs a count
     finally:
         comm.destroy()
+
+
+def test_row_groups_and_host_pipeline():
+    from vkccl_b200.utils.host_pipeline import row_groups, run_rows
+
+    for rows in (1, 7, 8, 9, 64, 1000, 1024, 8192):
+        for groups in (1, 2, 3, 4, 8):
+            parts = row_groups(rows, groups)
+            assert parts[0][0] == 0 and parts[-1][1] == rows
+            assert all(p[1] == q[0] for p, q in zip(parts, parts[1:]))
+            assert 1 <= len(parts) <= groups
+            assert all((b - a) % 8 == 0 for a, b in parts[:-1])
+            assert all(b > a for a, b in parts)
+    assert row_groups(1024, 4) == [(0, 256), (256, 512), (512, 768), (768, 1024)]
+    assert row_groups(0, 4) == []
+
+    w = torch.randn(16, 5)
+    x = torch.randn(100, 16)
+    out = torch.empty(100, 5)
+    calls = []
+
+    def fn(t):
+        calls.append(t.shape[0])
+        return t @ w
+
+    for g in (1, 3, 4):
+        calls.clear()
+        out.zero_()
+        run_rows(fn, x, out, groups=g, device="cpu")
+        torch.testing.assert_close(out, x @ w)
+        assert sum(calls) == 100 and len(calls) == len(row_groups(100, g))
+    with pytest.raises(ValueError):
+        run_rows(fn, x, torch.empty(99, 5), groups=2, device="cpu")

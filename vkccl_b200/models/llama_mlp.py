@@ -64,6 +64,23 @@ class TPLlamaMLP:
         all_gather_gemm(self.comm, x_shard, self.w_gate_up, silu_mul=True, out=h)
         return gemm_reduce_scatter(self.comm, h, self.w_down)
 
+    def forward_host(self, x_host: torch.Tensor, out_host: torch.Tensor | None = None,
+                     groups: int = 1) -> torch.Tensor:
+        """Host-to-host layer: pinned x_shard [T/n, hidden] in, y_shard out.
+
+        The MLP treats tokens independently, so with groups > 1 the shard
+        runs as that many token groups (the same split on every rank) and the
+        PCIe copies of neighbouring groups overlap the layer's kernels
+        (vkccl_b200.utils.host_pipeline).  Stream-ordered: synchronise the
+        current stream before reading the result.
+        """
+        from vkccl_b200.utils.host_pipeline import run_rows
+
+        if out_host is None:
+            out_host = torch.empty((x_host.shape[0], self.cfg.hidden), dtype=torch.bfloat16,
+                                   pin_memory=torch.cuda.is_available())
+        return run_rows(self.forward, x_host, out_host, groups=groups, device=self.w_down.device)
+
     def forward_nccl(self, x_shard: torch.Tensor, group=None) -> torch.Tensor:
         """Same layer with torch.distributed (NCCL) collectives and cuBLAS GEMMs."""
         import torch.distributed as dist
