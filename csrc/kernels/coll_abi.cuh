@@ -21,6 +21,7 @@ enum Where : uint32_t {
   kWhereP2pRecv = 8,
   kWhereFused = 9,
   kWhereMoe = 10,
+  kWhereWindow = 11,
 };
 
 struct CollArgs {
@@ -30,6 +31,28 @@ struct CollArgs {
   int root;       // Reduce/Bcast root; -1 for all-reduce
   int premul;     // scale own contribution by `scalar`
   int avg;        // post-scale by 1/nranks
+  double scalar;
+};
+
+// Collectives on registered windows (csrc/kernels/window.cuh).
+struct WinDesc {
+  uint64_t sendOff;
+  uint64_t recvOff;
+  uint64_t count;
+  double scalar;  // PreMulSum factor of this rank's contribution (1 otherwise)
+};
+static_assert(sizeof(WinDesc) * kMaxBlocks <= 8192, "window descriptors fit their ctrl range");
+
+struct WinArgs {
+  const char* send[kMaxRanks];  // every rank's send buffer in this address space ([rank] = own)
+  char* recv[kMaxRanks];        // every rank's receive buffer ([rank] = own)
+  const char* mcSend;           // multicast address of the send buffers, or null
+  char* mcRecv;                 // multicast address of the receive buffers, or null
+  uint64_t sendOff;             // offsets inside the windows (agreement check)
+  uint64_t recvOff;
+  size_t count;                 // all-reduce: elements; all-gather: bytes per rank; reduce-scatter: recvcount
+  int premul;
+  int avg;
   double scalar;
 };
 

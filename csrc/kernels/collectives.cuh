@@ -258,17 +258,19 @@ __device__ __forceinline__ void copyInScaled(char* dst, const char* src, size_t 
   copyInScaled<T>(dst, src, elems, doScale, s, threadIdx.x, blockDim.x);
 }
 
-// Reduce [lo, hi) of the multicast region through the switch and store the
-// result back to every rank's copy (16-byte units, U in flight per thread).
+// Reduce bytes [lo, hi) of the multicast source through the switch and store
+// the result to the same bytes of the multicast destination, i.e. of every
+// rank's copy (16-byte units, U in flight per thread; the last unit is
+// rounded up to 16 bytes).
 template <typename T, int K, int U = 4>
-__device__ __forceinline__ void nvlsReduceRange(char* mc, size_t lo, size_t hi, bool avg, int n, size_t tid,
-                                                size_t nthr) {
+__device__ __forceinline__ void nvlsReduceRange(const char* mcSrc, char* mcDst, size_t lo, size_t hi, bool avg,
+                                                int n, size_t tid, size_t nthr) {
   const size_t units = (hi - lo + 15) / 16;
   size_t i = tid;
   for (; i + (U - 1) * nthr < units; i += U * nthr) {
     uint4 v[U];
 #pragma unroll
-    for (int u = 0; u < U; u++) v[u] = Multimem<T, K>::ldReduce(mc + lo + (i + u * nthr) * 16);
+    for (int u = 0; u < U; u++) v[u] = Multimem<T, K>::ldReduce(mcSrc + lo + (i + u * nthr) * 16);
 #pragma unroll
     for (int u = 0; u < U; u++) {
       if (avg) {
@@ -277,7 +279,7 @@ __device__ __forceinline__ void nvlsReduceRange(char* mc, size_t lo, size_t hi, 
         p.scale(1.0 / n);
         v[u] = p.pack();
       }
-      multimemStore16(mc + lo + (i + u * nthr) * 16, v[u]);
+      multimemStore16(mcDst + lo + (i + u * nthr) * 16, v[u]);
     }
   }
   // Fewer than U * nthr units remain: one guarded batch keeps every
@@ -286,7 +288,7 @@ __device__ __forceinline__ void nvlsReduceRange(char* mc, size_t lo, size_t hi, 
     uint4 v[U];
 #pragma unroll
     for (int u = 0; u < U; u++)
-      if (i + u * nthr < units) v[u] = Multimem<T, K>::ldReduce(mc + lo + (i + u * nthr) * 16);
+      if (i + u * nthr < units) v[u] = Multimem<T, K>::ldReduce(mcSrc + lo + (i + u * nthr) * 16);
 #pragma unroll
     for (int u = 0; u < U; u++) {
       if (i + u * nthr >= units) break;
@@ -296,13 +298,19 @@ __device__ __forceinline__ void nvlsReduceRange(char* mc, size_t lo, size_t hi, 
         p.scale(1.0 / n);
         v[u] = p.pack();
       }
-      multimemStore16(mc + lo + (i + u * nthr) * 16, v[u]);
+      multimemStore16(mcDst + lo + (i + u * nthr) * 16, v[u]);
     }
   }
 }
+// In place: the staging region is both source and destination.
+template <typename T, int K, int U = 4>
+__device__ __forceinline__ void nvlsReduceRange(char* mc, size_t lo, size_t hi, bool avg, int n, size_t tid,
+                                                size_t nthr) {
+  nvlsReduceRange<T, K, U>(mc, mc, lo, hi, avg, n, tid, nthr);
+}
 template <typename T, int K>
 __device__ __forceinline__ void nvlsReduceRange(char* mc, size_t lo, size_t hi, bool avg, int n) {
-  nvlsReduceRange<T, K>(mc, lo, hi, avg, n, threadIdx.x, blockDim.x);
+  nvlsReduceRange<T, K>(mc, mc, lo, hi, avg, n, threadIdx.x, blockDim.x);
 }
 
 template <typename T, int K>

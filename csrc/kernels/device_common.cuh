@@ -57,6 +57,7 @@ constexpr size_t kMoeCombDoneOff = kMoeOff + 64;            // u32[kMaxRanks], w
 constexpr size_t kMoeDispEpochOff = kMoeOff + 128;          // u32, local: dispatch calls finished
 constexpr size_t kMoeCombEpochOff = kMoeOff + 132;          // u32, local: combine calls finished
 constexpr size_t kMoeBlocksOff = kMoeOff + 192;             // u32[4], local: per-kernel block counters
+constexpr size_t kWinDescOff = 81920;                       // WinDesc[kMaxBlocks], read by peers (window calls)
 constexpr size_t kCtrlHeader = 1 << 20;
 
 constexpr size_t kLLMaxBytes = 1 << 20;                 // largest LL payload per source rank

@@ -387,6 +387,81 @@ const char* algoName(ArAlgo a) {
   return "?";
 }
 
+// Zero-copy path for buffers in registered windows (runtime/window.cc):
+// all-reduce with both buffers in windows, all-gather with the receive
+// buffer in one, reduce-scatter with the send buffer in one.  Messages the
+// LL protocol handles stay on it.  Every rank decides alike: the windows,
+// offsets and counts agree across ranks by the window rule (the kernels
+// check it).
+bool windowCollective(const HostOp& h, const LaunchCtx& lc, vcclResult_t* out) {
+  vcclComm_t comm = h.comm;
+  const DeviceState& ds = *comm->dev;
+  if (!ds.windowsEnabled) return false;
+  const size_t es = vcclTypeSize(h.dt);
+  const int n = comm->nranks, me = comm->rank;
+  const size_t bytes = h.count * es;
+  dev::WinArgs w{};
+  w.count = h.count;
+  w.premul = h.premul ? 1 : 0;
+  w.avg = h.avg ? 1 : 0;
+  w.scalar = h.scalar;
+  auto bindSend = [&](const Window* win) {
+    w.sendOff = static_cast<uint64_t>(h.send - win->base);
+    for (int q = 0; q < n; q++) w.send[q] = win->peer[q] + w.sendOff;
+    w.mcSend = win->mc ? win->mc + w.sendOff : nullptr;
+  };
+  auto bindRecv = [&](const Window* win) {
+    w.recvOff = static_cast<uint64_t>(h.recv - win->base);
+    for (int q = 0; q < n; q++) w.recv[q] = win->peer[q] + w.recvOff;
+    w.mcRecv = win->mc ? win->mc + w.recvOff : nullptr;
+  };
+  const bool switchRanks = n >= ds.windowNvlsMinRanks;
+  cudaError_t e = cudaSuccess;
+  switch (h.kind) {
+    case Kind::AllReduce: {
+      if (bytes <= ds.llMaxBytes) return false;
+      const Window* ws = comm->findWindow(h.send, bytes);
+      const Window* wr = comm->findWindow(h.recv, bytes);
+      if (ws == nullptr || wr == nullptr) return false;
+      bindSend(ws);
+      bindRecv(wr);
+      bool sw = switchRanks && w.mcSend != nullptr && w.mcRecv != nullptr;
+      e = launchAllReduceWindow(lc, h.dt, h.redKind, w, sw);
+      if (e == cudaErrorInvalidValue && sw) {  // datatype, operation or alignment the switch cannot take
+        cudaGetLastError();
+        sw = false;
+        e = launchAllReduceWindow(lc, h.dt, h.redKind, w, false);
+      }
+      noteAlgorithm("all-reduce", sw ? "window NVLS" : "window two-shot", n, bytes);
+      *out = cudaToVccl(e, "window all-reduce launch");
+      return true;
+    }
+    case Kind::AllGather: {
+      if (bytes <= lc.llAgMax) return false;
+      const Window* wr = comm->findWindow(h.recv, bytes * n);
+      if (wr == nullptr) return false;
+      bindRecv(wr);
+      w.send[me] = h.send;  // the send buffer is read locally only
+      w.count = bytes;
+      noteAlgorithm("all-gather", w.mcRecv ? "window multimem push" : "window push", n, bytes);
+      *out = cudaToVccl(launchAllGatherWindow(lc, w), "window all-gather launch");
+      return true;
+    }
+    case Kind::ReduceScatter: {
+      if (bytes <= lc.llMax) return false;
+      const Window* ws = comm->findWindow(h.send, bytes * n);
+      if (ws == nullptr) return false;
+      bindSend(ws);
+      w.recv[me] = h.recv;  // written locally only
+      noteAlgorithm("reduce-scatter", switchRanks && w.mcSend ? "window NVLS" : "window pull", n, bytes);
+      *out = cudaToVccl(launchReduceScatterWindow(lc, h.dt, h.redKind, w, switchRanks), "window reduce-scatter launch");
+      return true;
+    }
+    default:
+      return false;
+  }
+}
+
 vcclResult_t launchColl(const HostOp& h) {
   vcclComm_t comm = h.comm;
   const size_t es = vcclTypeSize(h.dt);
@@ -405,6 +480,8 @@ vcclResult_t launchColl(const HostOp& h) {
     }
   }
   LaunchCtx lc = launchCtx(comm, s);
+  vcclResult_t winResult = vcclSuccess;
+  if (!comm->windows.empty() && windowCollective(h, lc, &winResult)) return winResult;
   dev::CollArgs a{h.send, h.recv, h.count, -1, h.premul ? 1 : 0, h.avg ? 1 : 0, h.scalar};
   switch (h.kind) {
     case Kind::AllReduce: {

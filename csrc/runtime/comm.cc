@@ -19,6 +19,7 @@
 
 #include "common/env.h"
 #include "common/log.h"
+#include "kernels/coll_abi.cuh"
 #include "runtime/comm.h"
 #include "runtime/cudrv.h"
 
@@ -46,7 +47,7 @@ vcclResult_t vcclComm::pollDeviceStatus() {
   static const char* const kWhere[] = {"?", "start barrier", "LL wait", "push barrier",
                                        "reduce barrier", "NVLS barrier", "gather barrier",
                                        "send slot wait", "recv data wait", "fused kernel wait",
-                                       "MoE dispatch/combine"};
+                                       "MoE dispatch/combine", "window collective"};
   uint32_t where = s[1];
   const char* w = where < sizeof(kWhere) / sizeof(kWhere[0]) ? kWhere[where] : "?";
   if (code == vccl::dev::kErrAborted) {
@@ -61,6 +62,11 @@ vcclResult_t vcclComm::pollDeviceStatus() {
   if (code == vccl::dev::kErrCapacity) {
     VERR("rank %d: MoE dispatch received more rows than its capacity (%u rows routed here); rows past the "
          "capacity were dropped", rank, s[3]);
+    return vcclInvalidUsage;
+  }
+  if (code == vccl::dev::kErrBadArg && where == vccl::dev::kWhereWindow) {
+    VERR("rank %d: a collective on registered windows was called with different offsets or counts on "
+         "different ranks (block %u); nothing was transferred", rank, s[3]);
     return vcclInvalidUsage;
   }
   VERR("rank %d: kernel reported error %u (%s)", rank, code, w);
@@ -86,6 +92,35 @@ struct Alloc {
   CUmemGenericAllocationHandle handle;
 };
 std::map<void*, Alloc> gAllocs;
+
+}  // namespace
+
+namespace vccl {
+bool findDeviceAllocation(const void* p, size_t bytes, void** base, size_t* allocBytes,
+                          CUmemGenericAllocationHandle* handle) {
+  std::lock_guard<std::mutex> g(gAllocMu);
+  auto it = gAllocs.upper_bound(const_cast<void*>(p));
+  if (it == gAllocs.begin()) return false;
+  --it;
+  const char* b = static_cast<const char*>(it->first);
+  const char* q = static_cast<const char*>(p);
+  if (!it->second.device || q < b || q + bytes > b + it->second.bytes) return false;
+  *base = it->first;
+  *allocBytes = it->second.bytes;
+  *handle = it->second.handle;
+  return true;
+}
+}  // namespace vccl
+
+const vccl::Window* vcclComm::findWindow(const void* p, size_t bytes) {
+  std::lock_guard<std::mutex> g(regMu);
+  const char* q = static_cast<const char*>(p);
+  for (const vccl::Window* w : windows)
+    if (q >= w->base && q + bytes <= w->base + w->bytes) return w;
+  return nullptr;
+}
+
+namespace {
 
 vcclResult_t checkConfig(const vcclConfig_t* cfg) {
   if (cfg == nullptr) return vcclSuccess;
@@ -326,6 +361,15 @@ vcclResult_t vcclCommDestroy(vcclComm_t comm) {
       delete r;
     }
     comm->regs.clear();
+    if (!comm->windows.empty() && comm->dev) {
+      cudaSetDevice(comm->dev->device);
+      cudaDeviceSynchronize();  // no kernel of this process still reads a peer's window
+      for (vccl::Window* w : comm->windows) {
+        vccl::windowRelease(comm->dev.get(), comm->rank, w);
+        delete w;
+      }
+    }
+    comm->windows.clear();
   }
   if (comm->dev) {
     vccl::deviceStateDestroy(comm->dev.get(), comm->bootstrap.get(), !comm->aborted.load());

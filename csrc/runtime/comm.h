@@ -66,6 +66,8 @@ struct DeviceState {
   size_t ll2MaxBytes = 0;          // two-hop LL all-reduce threshold
   size_t nvlsPipeMin = 0;          // pipelined NVLS all-reduce from this size (0: only when asked for)
   int nvlsPieces = 4;              // pieces of a pipelined NVLS all-reduce
+  bool windowsEnabled = true;      // zero-copy kernels for buffers in registered windows (VCCL_WINDOW)
+  int windowNvlsMinRanks = 3;      // window collectives go through the switch from this many ranks
 };
 
 struct CustomOp {
@@ -84,6 +86,40 @@ struct Registration {
   size_t importedBytes = 0;
   cudaExternalMemory_t extMem = nullptr;      // external-memory import we own
 };
+
+// A registered window: user memory from vcclMemAlloc that every rank has
+// mapped (and, when the node supports NVLS, bound to a multicast object), so
+// collectives on it read and write the peers' buffers in place.
+struct Window {
+  char* base = nullptr;  // this rank's window
+  size_t bytes = 0;
+  std::vector<char*> peer;  // every rank's window in this address space ([rank] = base)
+  std::vector<CUdeviceptr> peerVa;  // mappings of the peers' whole allocations
+  std::vector<size_t> peerVaBytes;
+  std::vector<CUmemGenericAllocationHandle> peerHandle;
+  CUmemGenericAllocationHandle localHandle = 0;  // the allocation's handle (owned by vcclMemAlloc)
+  size_t localOffset = 0;                        // window offset inside that allocation
+  CUmemGenericAllocationHandle mcHandle = 0;
+  CUdeviceptr mcVa = 0;
+  size_t mcBytes = 0;
+  bool mcBound = false;
+  char* mc = nullptr;  // multicast address of the window, or null
+};
+
+// The vcclMemAlloc device allocation holding [p, p + bytes): its base,
+// size and VMM handle.  False for anything else.
+bool findDeviceAllocation(const void* p, size_t bytes, void** base, size_t* allocBytes,
+                          CUmemGenericAllocationHandle* handle);
+// Shared set-up steps of the symmetric workspaces (device.cc), also used by
+// window registration.
+struct DriverApi;
+vcclResult_t mapForDevice(const DriverApi* d, CUmemGenericAllocationHandle h, size_t bytes, size_t align,
+                          int device, CUdeviceptr* va);
+bool everyone(Bootstrap* bs, bool mine);
+// Release a window's multicast binding, or that and its peer mappings
+// (local steps only).
+void windowReleaseMulticast(DeviceState* ds, Window* w);
+void windowRelease(DeviceState* ds, int me, Window* w);
 
 vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<DeviceState>* out);
 // Make sure the MoE region holds at least `bytes` on every rank.  Collective
@@ -111,6 +147,10 @@ struct vcclComm {
 
   std::mutex regMu;
   std::vector<vccl::Registration*> regs;
+  std::vector<vccl::Window*> windows;  // guarded by regMu
+
+  // The window holding [p, p + bytes), or null (collective buffer lookup).
+  const vccl::Window* findWindow(const void* p, size_t bytes);
 
   int device() const { return dev ? dev->device : -1; }
 

@@ -39,17 +39,7 @@ namespace {
     }                                                                         \
   } while (0)
 
-size_t roundUp(size_t x, size_t a) { return (x + a - 1) / a * a; }
-
-CUmemAllocationProp exportableProp(int device) {
-  CUmemAllocationProp prop;
-  memset(&prop, 0, sizeof(prop));
-  prop.type = CU_MEM_ALLOCATION_TYPE_PINNED;
-  prop.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
-  prop.location.id = device;
-  prop.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
-  return prop;
-}
+}  // namespace
 
 vcclResult_t mapForDevice(const DriverApi* d, CUmemGenericAllocationHandle h, size_t bytes,
                           size_t align, int device, CUdeviceptr* va) {
@@ -75,6 +65,31 @@ vcclResult_t mapForDevice(const DriverApi* d, CUmemGenericAllocationHandle h, si
     return vcclSystemError;
   }
   return vcclSuccess;
+}
+
+// Every rank reports success of a step; all ranks learn whether everyone
+// succeeded (so that optional features are enabled or skipped together).
+bool everyone(Bootstrap* bs, bool mine) {
+  std::vector<uint8_t> v(bs->nranks(), 0);
+  v[bs->rank()] = mine ? 1 : 0;
+  if (bs->allGather(v.data(), 1) != vcclSuccess) return false;
+  for (uint8_t x : v)
+    if (!x) return false;
+  return true;
+}
+
+namespace {
+
+size_t roundUp(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+CUmemAllocationProp exportableProp(int device) {
+  CUmemAllocationProp prop;
+  memset(&prop, 0, sizeof(prop));
+  prop.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+  prop.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+  prop.location.id = device;
+  prop.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+  return prop;
 }
 
 // Allocate `bytes` (already rounded) on this device, export, exchange, map
@@ -126,17 +141,6 @@ void symmetricFree(const DriverApi* d, int me, SymmetricBuffer* b) {
   b->va.clear();
   b->handles.clear();
   b->localHandle = 0;
-}
-
-// Every rank reports success of a step; all ranks learn whether everyone
-// succeeded (so that optional features are enabled or skipped together).
-bool everyone(Bootstrap* bs, bool mine) {
-  std::vector<uint8_t> v(bs->nranks(), 0);
-  v[bs->rank()] = mine ? 1 : 0;
-  if (bs->allGather(v.data(), 1) != vcclSuccess) return false;
-  for (uint8_t x : v)
-    if (!x) return false;
-  return true;
 }
 
 void multicastTeardown(const DriverApi* d, DeviceState* ds) {
@@ -245,6 +249,10 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
   // VCCL_ALLREDUCE_ALGO=nvls_pipe or a tuning rule picks it per call.
   ds->nvlsPipeMin = envBytes("VCCL_NVLS_PIPE_MIN", 0);
   ds->nvlsPieces = static_cast<int>(envLong("VCCL_NVLS_PIECES", 4));
+  ds->windowsEnabled = envLong("VCCL_WINDOW", 1) != 0;
+  // Per GPU, the switch moves about S each way for a window all-reduce of
+  // S bytes against 2 (n-1)/n S for the point-to-point kernel.
+  ds->windowNvlsMinRanks = static_cast<int>(envLong("VCCL_WINDOW_NVLS_MIN_RANKS", 3));
   if (ds->nvlsPieces < 1) ds->nvlsPieces = 1;
   // An LL all-gather moves the same (n-1) x 2 x payload as the one-shot LL
   // all-reduce and needs no barrier.  At 8 ranks with 1 MiB per rank the LL

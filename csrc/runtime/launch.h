@@ -42,6 +42,13 @@ cudaError_t launchAllGather(const LaunchCtx& lc, const void* send, void* recv, s
 cudaError_t launchBroadcast(const LaunchCtx& lc, const void* send, void* recv, size_t bytes, int root,
                             bool useNvls);
 cudaError_t launchP2p(const LaunchCtx& lc, const dev::P2pPlan& plan);
+// Zero-copy collectives on registered windows; viaSwitch picks the NVLS
+// (multimem) kernel where the buffers, datatype and operation allow it.
+cudaError_t launchAllReduceWindow(const LaunchCtx& lc, vcclDataType_t dt, int redKind, const dev::WinArgs& w,
+                                  bool viaSwitch);
+cudaError_t launchAllGatherWindow(const LaunchCtx& lc, const dev::WinArgs& w);
+cudaError_t launchReduceScatterWindow(const LaunchCtx& lc, vcclDataType_t dt, int redKind, const dev::WinArgs& w,
+                                      bool viaSwitch);
 // Single-rank helpers: dst = src * scale (float types) or plain copy.
 cudaError_t launchScaleCopy(cudaStream_t s, vcclDataType_t dt, void* dst, const void* src, size_t count,
                             double scale);

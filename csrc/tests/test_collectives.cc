@@ -24,6 +24,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <string>
 #include <vector>
 
@@ -455,6 +456,101 @@ void multiRound(vcclComm_t c, int me, int n) {
   cudaFree(dr);
 }
 
+// Zero-copy collectives on registered windows: all-reduce (point-to-point
+// or through the switch, fp32 / bf16, in place, PreMulSum, average, a
+// buffer off the 16-byte grid), all-gather into a window, reduce-scatter
+// out of one.  Every size is past the LL thresholds so the window kernels
+// run.
+bool checkDevice(const void* dptr, vcclDataType_t dt, size_t cnt, const char* what,
+                 const std::function<float(size_t)>& want) {
+  std::vector<char> h(cnt * vcclTypeSize(dt));
+  cudaMemcpy(h.data(), dptr, h.size(), cudaMemcpyDeviceToHost);
+  for (size_t i = 0; i < cnt; i += (i + 5000 < cnt ? 61 : 1)) {
+    if (!near(get(h.data(), dt, i), want(i), dt)) {
+      std::fprintf(stderr, "FAIL window %s i=%zu got %g want %g\n", what, i, get(h.data(), dt, i), want(i));
+      gFail++;
+      return false;
+    }
+  }
+  return true;
+}
+
+void windowTest(vcclComm_t c, int me, int n) {
+  if (n < 2) return;
+  const size_t cnt = (4u << 20) + 5;
+  const size_t winBytes = (cnt + 64) * 4 * static_cast<size_t>(n);
+  void *a = nullptr, *b = nullptr;
+  EXPECT_OK(vcclMemAlloc(&a, winBytes));
+  EXPECT_OK(vcclMemAlloc(&b, winBytes));
+  vcclWindow_t wa = nullptr, wb = nullptr;
+  EXPECT_OK(vcclCommWindowRegister(c, a, winBytes, &wa, 0));
+  EXPECT_OK(vcclCommWindowRegister(c, b, winBytes, &wb, 0));
+  if (wa == nullptr || wb == nullptr) return;
+  auto upload = [&](void* dst, vcclDataType_t dt, size_t count, size_t off) {
+    std::vector<char> h(count * vcclTypeSize(dt));
+    fill(h.data(), dt, me, count, off);
+    cudaMemcpy(dst, h.data(), h.size(), cudaMemcpyHostToDevice);
+  };
+  char* A = static_cast<char*>(a);
+  char* B = static_cast<char*>(b);
+  // all-reduce, fp32 and bf16, out of place
+  for (vcclDataType_t dt : {vcclFloat32, vcclBfloat16}) {
+    upload(A, dt, cnt, 0);
+    cudaMemset(B, 0, cnt * vcclTypeSize(dt));
+    EXPECT_OK(vcclAllReduce(A, B, cnt, dt, vcclSum, c));
+    checkDevice(B, dt, cnt, "allreduce", [&](size_t i) { return expect(vcclSum, n, i); });
+  }
+  // in place, max
+  upload(B, vcclFloat32, cnt, 0);
+  EXPECT_OK(vcclAllReduce(B, B, cnt, vcclFloat32, vcclMax, c));
+  checkDevice(B, vcclFloat32, cnt, "allreduce in place max", [&](size_t i) { return expect(vcclMax, n, i); });
+  // PreMulSum (point-to-point kernel) and average (switch kernel when bound)
+  float k = 0.5f;
+  vcclRedOp_t pm;
+  EXPECT_OK(vcclRedOpCreatePreMulSum(&pm, &k, vcclFloat32, vcclScalarHostImmediate, c));
+  upload(A, vcclFloat32, cnt, 0);
+  EXPECT_OK(vcclAllReduce(A, B, cnt, vcclFloat32, pm, c));
+  checkDevice(B, vcclFloat32, cnt, "allreduce premulsum", [&](size_t i) { return 0.5f * expect(vcclSum, n, i); });
+  EXPECT_OK(vcclRedOpDestroy(pm, c));
+  EXPECT_OK(vcclAllReduce(A, B, cnt, vcclFloat32, vcclAvg, c));
+  checkDevice(B, vcclFloat32, cnt, "allreduce avg", [&](size_t i) { return expect(vcclAvg, n, i); });
+  // off the 16-byte grid (element kernels)
+  upload(A + 4, vcclFloat32, cnt - 1, 0);
+  EXPECT_OK(vcclAllReduce(A + 4, B + 4, cnt - 1, vcclFloat32, vcclSum, c));
+  checkDevice(B + 4, vcclFloat32, cnt - 1, "allreduce unaligned", [&](size_t i) { return expect(vcclSum, n, i); });
+  // all-gather into window B from a plain buffer
+  const size_t per = cnt / n;
+  void* local = nullptr;
+  cudaMalloc(&local, per * 4);
+  upload(local, vcclFloat32, per, 0);
+  EXPECT_OK(vcclAllGather(local, B, per, vcclFloat32, c));
+  for (int p = 0; p < n; p++) {
+    std::vector<float> g(per);
+    cudaMemcpy(g.data(), B + p * per * 4, per * 4, cudaMemcpyDeviceToHost);
+    for (size_t i = 0; i < per; i += 97)
+      if (!near(g[i], val(p, i), vcclFloat32)) {
+        std::fprintf(stderr, "FAIL window allgather from rank %d i=%zu\n", p, i);
+        gFail++;
+        break;
+      }
+  }
+  // reduce-scatter out of window A into the plain buffer
+  upload(A, vcclFloat32, per * n, 0);
+  EXPECT_OK(vcclReduceScatter(A, local, per, vcclFloat32, vcclSum, c));
+  checkDevice(local, vcclFloat32, per, "reducescatter", [&](size_t i) { return expect(vcclSum, n, me * per + i); });
+  cudaFree(local);
+  EXPECT_OK(vcclCommWindowDeregister(c, wa));
+  EXPECT_OK(vcclCommWindowDeregister(c, wb));
+  EXPECT_OK(vcclMemFree(a));
+  EXPECT_OK(vcclMemFree(b));
+  // not from vcclMemAlloc: refused on every rank
+  void* plain = nullptr;
+  cudaMalloc(&plain, 1 << 20);
+  vcclWindow_t wp = nullptr;
+  EXPECT(vcclCommWindowRegister(c, plain, 1 << 20, &wp, 0) == vcclInvalidArgument, "plain cudaMalloc window");
+  cudaFree(plain);
+}
+
 int rankMain(int me, int n, const vcclUniqueId& id, bool full) {
   cudaSetDevice(me);
   vcclComm_t c = nullptr;
@@ -493,6 +589,7 @@ int rankMain(int me, int n, const vcclUniqueId& id, bool full) {
   algoAB(c, me, n, 70000);
   if (full) deviceSweep(c, me, n);
   if (full) multiRound(c, me, n);
+  if (full) windowTest(c, me, n);
   EXPECT_OK(vcclCommDestroy(c));
   if (gFail) std::fprintf(stderr, "rank %d/%d: %d failures\n", me, n, gFail);
   return gFail ? 1 : 0;

@@ -256,6 +256,24 @@ vcclResult_t vcclCommRegisterDmaBuf(vcclComm_t comm, int fd, uint64_t offset,
                                     size_t bytes, void** ptr,
                                     vcclMemHandle_t* handle);
 
+/* ── Windows (an addition: zero-copy collectives) ───────────────────────
+ * Collective: every rank calls it, in the same order, with a buffer of the
+ * same `size` that lies inside a vcclMemAlloc device allocation.  Every
+ * rank then maps every peer's buffer, and when the node supports NVLS the
+ * buffers are also bound to one multicast object (unless flags has
+ * VCCL_WIN_NO_MULTICAST).  All-reduce with both buffers in windows,
+ * all-gather with the receive buffer in a window and reduce-scatter with
+ * the send buffer in a window then read and write the peers' buffers in
+ * place (no staging copies).  Rule for those calls: every rank passes
+ * buffers at the same offsets of its windows and the same count; calls
+ * that break it fail with vcclInvalidUsage on every rank and move no data.
+ * Deregister is collective as well and must precede vcclMemFree. */
+typedef void* vcclWindow_t;
+#define VCCL_WIN_NO_MULTICAST 0x1
+vcclResult_t vcclCommWindowRegister(vcclComm_t comm, void* buff, size_t size,
+                                    vcclWindow_t* win, int flags);
+vcclResult_t vcclCommWindowDeregister(vcclComm_t comm, vcclWindow_t win);
+
 const char* vcclGetErrorString(vcclResult_t result);
 const char* vcclGetLastError(vcclComm_t comm);
 size_t vcclTypeSize(vcclDataType_t datatype);

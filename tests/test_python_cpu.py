@@ -8,6 +8,7 @@ over the TCP bootstrap on 127.0.0.1, as the reference's Python suites run
 their ranks as local processes (reference: python/tests/test_bindings.py).
 """
 
+import ctypes
 import multiprocessing as mp
 import os
 
@@ -511,3 +512,22 @@ def test_row_groups_and_host_pipeline():
         assert sum(calls) == 100 and len(calls) == len(row_groups(100, g))
     with pytest.raises(ValueError):
         run_rows(fn, x, torch.empty(99, 5), groups=2, device="cpu")
+
+
+def test_window_api_without_device():
+    """Windows need the device data plane: a control-plane communicator
+    refuses them with vcclInvalidUsage, and nothing leaks."""
+    _env()
+    import vkccl_b200 as v
+
+    comm = v.Communicator(1, v.get_unique_id(), 0)
+    try:
+        buf = np.zeros(1024, dtype=np.float32)
+        with pytest.raises(v.VcclError) as ei:
+            comm.window_register(buf)
+        assert ei.value.result == 5  # vcclInvalidUsage
+        with pytest.raises(v.VcclError):
+            comm.window_deregister(ctypes.c_void_p(0))
+        assert comm.WIN_NO_MULTICAST == 1
+    finally:
+        comm.destroy()

@@ -1,0 +1,63 @@
+# SPDX-License-Identifier: Apache-2.0
+"""Per-rank body of the window GPU test (run by torchrun): torch tensors on
+vcclMemAlloc memory, registered as windows, through all-reduce, all-gather
+and reduce-scatter, against locally computed sums."""
+
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+
+import vkccl_b200 as v  # noqa: E402
+
+
+def main():
+    dist.init_process_group("gloo")
+    rank, n = dist.get_rank(), dist.get_world_size()
+    torch.cuda.set_device(rank)
+    uid = [v.get_unique_id().to_bytes() if rank == 0 else None]
+    dist.broadcast_object_list(uid, 0)
+    comm = v.Communicator(n, v.UniqueId.from_bytes(uid[0]), rank, cuda_device=rank)
+    count = 3 << 20  # past every LL threshold
+    send = v.mem_alloc_tensor((count,), torch.bfloat16)
+    recv = v.mem_alloc_tensor((count,), torch.bfloat16)
+    ws = comm.window_register(send)
+    wr = comm.window_register(recv)
+
+    def inputs(r):
+        g = torch.Generator(device="cuda").manual_seed(100 + r)
+        return torch.randn(count, device="cuda", generator=g).bfloat16()
+
+    total = sum(inputs(r).float() for r in range(n))
+    send.copy_(inputs(rank))
+    comm.all_reduce(send, recv)
+    torch.cuda.synchronize()
+    err = (recv.float() - total).abs().max().item()
+    assert err <= 0.05 * total.abs().max().item(), f"window all_reduce err {err}"
+
+    per = count // n
+    comm.all_gather(send[:per], recv[: per * n])
+    torch.cuda.synchronize()
+    for r in range(n):
+        assert torch.equal(recv[r * per:(r + 1) * per], inputs(r)[:per]), f"window all_gather block {r}"
+
+    out = torch.empty(per, dtype=torch.bfloat16, device="cuda")
+    comm.reduce_scatter(send[: per * n], out)
+    torch.cuda.synchronize()
+    want = total[rank * per:(rank + 1) * per]
+    err = (out.float() - want).abs().max().item()
+    assert err <= 0.05 * want.abs().max().item(), f"window reduce_scatter err {err}"
+
+    comm.window_deregister(ws)
+    comm.window_deregister(wr)
+    del send, recv
+    comm.destroy()
+    dist.destroy_process_group()
+    print(f"rank {rank}: window ok", flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -26,6 +26,7 @@ from vkccl_b200.comm import (
     group_start,
     init_all,
     mem_alloc,
+    mem_alloc_tensor,
     mem_free,
     type_size,
     version,
@@ -46,6 +47,7 @@ __all__ = [
     "init_all",
     "library_path",
     "mem_alloc",
+    "mem_alloc_tensor",
     "mem_free",
     "type_size",
     "version",

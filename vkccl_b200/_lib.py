@@ -116,6 +116,8 @@ def _declare(h: ctypes.CDLL) -> None:
         "vcclCommRegister": [P, P, Z, c.POINTER(P)],
         "vcclCommDeregister": [P, P],
         "vcclCommRegisterDmaBuf": [P, I, c.c_uint64, Z, c.POINTER(P), c.POINTER(P)],
+        "vcclCommWindowRegister": [P, P, Z, c.POINTER(P), I],
+        "vcclCommWindowDeregister": [P, P],
         "vcclTypeSize": [I],
         "vcclGetErrorString": [I],
         "vcclGetLastError": [P],

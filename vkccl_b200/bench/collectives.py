@@ -6,6 +6,11 @@ Launch one process per GPU:
     torchrun --nproc-per-node N --master-addr 127.0.0.1 -m vkccl_b200.bench.collectives \
         --ops allreduce,allgather,reducescatter,broadcast --dtypes bf16,f32 -b 8 -e 1G
 
+--window adds a "vcclwin" column: the same vccl call on buffers inside
+registered windows (vcclMemAlloc memory mapped by every rank), which runs
+the zero-copy kernels (all-reduce, all-gather, reduce-scatter).  NCCL runs
+on plain torch tensors in every column.
+
 Every number is device time from CUDA events on the launching stream,
 averaged over --iters launches captured in one CUDA graph (so host launch
 overhead is excluded for both libraries), reported as the maximum over
@@ -124,6 +129,7 @@ def main() -> int:
     ap.add_argument("--algos", default="", help="also time these forced all-reduce algorithms")
     ap.add_argument("--out", default="")
     ap.add_argument("--tune-out", default="", help="write a VCCL_TUNING_FILE table from the --algos sweep")
+    ap.add_argument("--window", action="store_true", help="also time vccl on registered-window buffers")
     a = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -139,6 +145,12 @@ def main() -> int:
     comm = vc.Communicator(world, vc.UniqueId.from_bytes(bytes(raw.cpu().numpy())), rank, cuda_device=local)
     rows = []
     lo, hi = parse_size(a.b), parse_size(a.e)
+    wins = None
+    if a.window:
+        # two windows of the largest message, viewed as each size and dtype
+        wbytes = (hi + 4096) // 16 * 16 + 16
+        wsend, wrecv = vc.mem_alloc_tensor((wbytes,), torch.uint8), vc.mem_alloc_tensor((wbytes,), torch.uint8)
+        wins = (wsend, wrecv, comm.window_register(wsend), comm.window_register(wrecv))
     for op in a.ops.split(","):
         for dname in a.dtypes.split(","):
             dt = DT[dname]
@@ -160,12 +172,20 @@ def main() -> int:
                     recv = send.clone() if op == "broadcast" else torch.empty_like(send)
                 row = {"op": op, "dtype": dname, "bytes": count * es, "n": world}
                 variants = [(lib_, None) for lib_ in a.libs.split(",")]
+                if wins is not None and op != "broadcast":
+                    variants.append(("vcclwin", None))
                 if op == "allreduce" and a.algos:
                     variants += [("vccl", algo) for algo in a.algos.split(",")]
                 for libname, algo in variants:
                     if algo:
                         os.environ["VCCL_ALLREDUCE_ALGO"] = algo
-                    fn = make_call(libname, op, comm, send, recv, world)
+                    if libname == "vcclwin":
+                        ws = wins[0][: send.numel() * es].view(dt)
+                        wr = wins[1][: recv.numel() * es].view(dt)
+                        ws.copy_(send)
+                        fn = make_call("vccl", op, comm, ws, wr, world)
+                    else:
+                        fn = make_call(libname, op, comm, send, recv, world)
                     us = time_graph(fn, a.iters, a.warmup)
                     os.environ.pop("VCCL_ALLREDUCE_ALGO", None)
                     if libname == "vccl" and comm.async_error() != 0:
@@ -181,6 +201,10 @@ def main() -> int:
                 if rank == 0:
                     print(json.dumps(row), flush=True)
                 size = int(size * a.f)
+    if wins is not None:
+        comm.window_deregister(wins[2])
+        comm.window_deregister(wins[3])
+        wins = None
     comm.destroy()
     if rank == 0 and a.tune_out:
         with open(a.tune_out, "w") as f:

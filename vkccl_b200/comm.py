@@ -184,6 +184,41 @@ def mem_free(addr: int) -> None:
     _check(lib().vcclMemFree(ctypes.c_void_p(addr)), "vcclMemFree")
 
 
+class _DeviceAlloc:
+    """Owns one vcclMemAlloc allocation and exposes it through
+    __cuda_array_interface__.  torch.as_tensor keeps this object alive for
+    as long as the tensor's storage lives, so the memory is freed with the
+    last view of the tensor."""
+
+    def __init__(self, nbytes: int):
+        self.addr = mem_alloc(nbytes)
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (self.addr, False),
+                                         "version": 3, "strides": None}
+
+    def __del__(self) -> None:
+        if getattr(self, "addr", 0):
+            try:
+                mem_free(self.addr)
+            except Exception:  # interpreter shutdown: the process is going away anyway
+                pass
+            self.addr = 0
+
+
+def mem_alloc_tensor(shape: Sequence[int], dtype: Any, device: Any = None):
+    """A torch tensor on the current CUDA device backed by vcclMemAlloc
+    memory (exportable, so it can be registered as a window).  Deregister any
+    window on it before the last view of the tensor goes away."""
+    import math
+
+    import torch
+
+    if device is not None:
+        torch.cuda.set_device(torch.device(device))
+    nbytes = max(1, math.prod(shape)) * torch.empty((), dtype=dtype).element_size()
+    raw = torch.as_tensor(_DeviceAlloc(nbytes), device="cuda")
+    return raw.view(dtype)[: math.prod(shape)].view(*shape)
+
+
 class _Config(ctypes.Structure):
     _fields_ = [("size", ctypes.c_size_t), ("blocking", ctypes.c_int), ("splitShare", ctypes.c_int)]
 
@@ -468,6 +503,24 @@ class Communicator:
 
     def deregister(self, handle: ctypes.c_void_p) -> None:
         _check(lib().vcclCommDeregister(self._comm, handle), "vcclCommDeregister", self._comm)
+
+    # -- windows (zero-copy collectives) -----------------------------------------
+    WIN_NO_MULTICAST = 0x1
+
+    def window_register(self, buf: Any, nbytes: Optional[int] = None, flags: int = 0) -> ctypes.c_void_p:
+        """Collective: map `buf` (vcclMemAlloc memory, e.g. from mem_alloc_tensor;
+        the same size on every rank) into every rank.  Collectives on buffers
+        inside windows then read and write the peers' buffers in place; every
+        rank must pass buffers at the same offsets of its windows."""
+        b = buffer_info(buf, True)
+        h = ctypes.c_void_p()
+        _check(lib().vcclCommWindowRegister(self._comm, b.addr, nbytes or b.nbytes, ctypes.byref(h), flags),
+               "vcclCommWindowRegister", self._comm)
+        return h
+
+    def window_deregister(self, handle: ctypes.c_void_p) -> None:
+        """Collective: undo window_register (before the memory is freed)."""
+        _check(lib().vcclCommWindowDeregister(self._comm, handle), "vcclCommWindowDeregister", self._comm)
 
     def destroy(self) -> None:
         if self._comm:
