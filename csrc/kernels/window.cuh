@@ -55,8 +55,8 @@ __device__ __forceinline__ bool winStart(const DevComm& c, int blk, const WinArg
 
 // Sum of every rank's element i (each scaled by its factor), read at
 // send[q] + srcOff, for elements [lo, hi), stored to every rank's recv (or
-// to this rank's only).  The sources are read starting with this rank, in
-// the same order on every rank for a given element.
+// to this rank's only).  Only this rank reduces these elements; it folds
+// the sources starting with its own.
 template <typename T, int K, bool VEC>
 __device__ __forceinline__ void winReduceBroadcast(const WinArgs& w, size_t srcOff, int n, int me, size_t lo,
                                                    size_t hi, const double* scalars, bool out0Only) {
