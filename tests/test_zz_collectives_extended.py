@@ -1,0 +1,27 @@
+# SPDX-License-Identifier: Apache-2.0
+"""The native suite's extended mode (csrc/tests/test_collectives.cc,
+`--extended`): the pipelined NVLS all-reduce, messages larger than the
+staging region (multi-round two-shot / NVLS / pipelined NVLS) and the
+zero-copy window collectives.  Kept apart from the main matrix so that a
+failure here cannot hide the main matrix's result under `pytest -x`."""
+
+import os
+import subprocess
+
+import pytest
+
+from conftest import BIN, gpu_count
+
+pytestmark = pytest.mark.gpu
+
+
+def test_collectives_extended():
+    n = gpu_count()
+    if n == 0:
+        pytest.skip("no GPU")
+    env = dict(os.environ, VCCL_SOCKET_ADDR="127.0.0.1", VCCL_DEBUG="ERROR", VCCL_TIMEOUT="60")
+    p = subprocess.run([os.path.join(BIN, "test_collectives"), str(min(n, 8)), "--extended"], env=env,
+                       capture_output=True, text=True, timeout=1200)
+    print(p.stdout)
+    assert p.returncode == 0, p.stdout + p.stderr[-4000:]
+    assert "all tests passed" in p.stdout
