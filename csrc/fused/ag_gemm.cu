@@ -228,7 +228,7 @@ extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, voi
     e = launchAllGather(launchCtxFor(*comm->dev, s), xShard, xfull, static_cast<size_t>(M / n) * K * 2);
     if (e == cudaSuccess)
       e = gemm::gemmAuto(xfull, W, out, M, N, K, siluMul != 0, s, bnEnv, true,
-                         reinterpret_cast<float*>(xfull + xBytes));
+                         reinterpret_cast<float*>(xfull + xBytes), sc.sems);
     gemm::releaseScratch(sc);
     if (e != cudaSuccess) {
       VERR("vcclAllGatherGemm (small): %s", cudaGetErrorString(e));

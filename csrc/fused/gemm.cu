@@ -180,10 +180,38 @@ float* splitScratch(cudaStream_t st, size_t bytes) {
   return static_cast<float*>(e.first);
 }
 
+bool splitFixupEnabled() {
+  static const bool on = envLongGemm("VCCL_GEMM_SPLIT_FIXUP") != 0;
+  return on;
+}
+
+// Fix-up semaphores, cached per (device, stream) like the scratch; zeroed
+// once, and every call leaves them at zero.
+uint32_t* splitSems(cudaStream_t st) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, uint32_t*> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  uint32_t*& p = cache[{dev, st}];
+  if (p == nullptr) {
+    void* q = nullptr;
+    if (cudaMalloc(&q, kSemSlots * sizeof(uint32_t)) != cudaSuccess) return nullptr;
+    if (cudaMemset(q, 0, kSemSlots * sizeof(uint32_t)) != cudaSuccess) {
+      cudaFree(q);
+      return nullptr;
+    }
+    p = static_cast<uint32_t*>(q);
+  }
+  return p;
+}
+
 bool acquireScratch(cudaStream_t st, size_t bytes, Scratch* out) {
   out->p = nullptr;
   out->async = false;
   out->st = st;
+  out->sems = nullptr;
+  out->semsAsync = false;
   if (bytes == 0) return true;
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   cudaStreamIsCapturing(st, &cap);
@@ -193,14 +221,27 @@ bool acquireScratch(cudaStream_t st, size_t bytes, Scratch* out) {
     // node of the graph.
     if (cudaMallocAsync(&out->p, bytes, st) != cudaSuccess) return false;
     out->async = true;
+    if (splitFixupEnabled()) {
+      void* q = nullptr;
+      if (cudaMallocAsync(&q, kSemSlots * sizeof(uint32_t), st) == cudaSuccess) {
+        if (cudaMemsetAsync(q, 0, kSemSlots * sizeof(uint32_t), st) == cudaSuccess) {
+          out->sems = static_cast<uint32_t*>(q);
+          out->semsAsync = true;
+        } else {
+          cudaFreeAsync(q, st);
+        }
+      }
+    }
     return true;
   }
   out->p = splitScratch(st, bytes);
+  if (splitFixupEnabled()) out->sems = splitSems(st);
   return out->p != nullptr;
 }
 
 void releaseScratch(const Scratch& s) {
   if (s.async && s.p != nullptr) cudaFreeAsync(s.p, s.st);
+  if (s.semsAsync && s.sems != nullptr) cudaFreeAsync(s.sems, s.st);
 }
 
 SplitPlan planFor(int M, int N, int K, int bnOverride, bool allowSplit) {
@@ -215,12 +256,20 @@ size_t gemmAutoScratchBytes(int M, int N, int K, int bnOverride, bool allowSplit
 }
 
 cudaError_t gemmAuto(const void* A, const void* W, void* C, int M, int N, int K, bool siluMul, cudaStream_t st,
-                     int bnOverride, bool allowSplit, float* ws) {
+                     int bnOverride, bool allowSplit, float* ws, uint32_t* sems) {
   const SplitPlan plan = planFor(M, N, K, bnOverride, allowSplit);
   if (plan.splits > 1) {
     if (ws == nullptr) return cudaErrorInvalidValue;
     const size_t elems = static_cast<size_t>(M) * N;
     EpiPartialF32 epi{ws, N, elems};
+    const int tiles = ((M + kBM - 1) / kBM) * ((N + plan.bn - 1) / plan.bn);
+    if (sems != nullptr && M <= kFixupMaxRows && tiles * 4 <= kSemSlots) {
+      auto* out = static_cast<__nv_bfloat16*>(C);
+      if (siluMul) return launchGemm(A, W, M, N, K, EpiSplitFixup<true>{epi, sems, out}, NoHooks{}, st, plan.bn, 0,
+                                     plan.splits);
+      return launchGemm(A, W, M, N, K, EpiSplitFixup<false>{epi, sems, out}, NoHooks{}, st, plan.bn, 0,
+                        plan.splits);
+    }
     cudaError_t e = launchGemm(A, W, M, N, K, epi, NoHooks{}, st, plan.bn, 0, plan.splits);
     if (e != cudaSuccess) return e;
     return siluMul ? launchSplitReduceSilu(ws, plan.splits, M, N, C, st)
@@ -300,7 +349,7 @@ vcclResult_t gemmEntry(const char* what, const void* A, const void* W, void* C, 
     VERR("%s: cannot allocate %zu bytes of split-K scratch", what, bytes);
     return vcclSystemError;
   }
-  cudaError_t e = gemm::gemmAuto(A, W, C, M, N, K, siluMul, st, bnEnv, true, static_cast<float*>(sc.p));
+  cudaError_t e = gemm::gemmAuto(A, W, C, M, N, K, siluMul, st, bnEnv, true, static_cast<float*>(sc.p), sc.sems);
   gemm::releaseScratch(sc);
   if (e != cudaSuccess) {
     VERR("%s: %s", what, cudaGetErrorString(e));

@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <cstdlib>
 
 namespace vccl {
@@ -36,9 +37,21 @@ struct Scratch {
   void* p = nullptr;
   bool async = false;
   cudaStream_t st = nullptr;
+  // Split-K fix-up semaphores (zero between calls), when the in-kernel
+  // reduction is enabled: per stream, or a stream-ordered zeroed
+  // allocation while `st` is being captured.
+  uint32_t* sems = nullptr;
+  bool semsAsync = false;
 };
 bool acquireScratch(cudaStream_t st, size_t bytes, Scratch* out);
 void releaseScratch(const Scratch& s);
+
+// In-kernel split-K reduction (EpiSplitFixup) for GEMMs of at most
+// kFixupMaxRows rows, when VCCL_GEMM_SPLIT_FIXUP=1; semaphores for up to
+// kSemSlots / 4 output tiles.
+constexpr int kFixupMaxRows = 8;
+constexpr int kSemSlots = 4096;
+bool splitFixupEnabled();
 
 // Split-K (or not) plan honouring VCCL_GEMM_BN / VCCL_GEMM_SPLITK.
 SplitPlan planFor(int M, int N, int K, int bnOverride, bool allowSplit);
@@ -46,8 +59,9 @@ SplitPlan planFor(int M, int N, int K, int bnOverride, bool allowSplit);
 size_t gemmAutoScratchBytes(int M, int N, int K, int bnOverride, bool allowSplit);
 // C = A W^T (bf16), or silu(gate) * up with C of N/2 columns, split-K for
 // decode shapes; ws must hold gemmAutoScratchBytes bytes when that is > 0.
+// With `sems` (Scratch::sems) small split-K GEMMs reduce inside the kernel.
 cudaError_t gemmAuto(const void* A, const void* W, void* C, int M, int N, int K, bool siluMul, cudaStream_t st,
-                     int bnOverride, bool allowSplit, float* ws);
+                     int bnOverride, bool allowSplit, float* ws, uint32_t* sems = nullptr);
 cudaError_t launchSplitReduceSilu(const float* ws, int splits, int M, int N, void* out, cudaStream_t st);
 
 // out[i] = bf16(sum over s < splits of ws[s * elems + i]); elems % 4 == 0.

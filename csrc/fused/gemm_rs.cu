@@ -176,7 +176,8 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
       return vcclSystemError;
     }
     char* p = static_cast<char*>(sc.p);
-    cudaError_t e = gemm::gemmAuto(A, W, p, M, N, K, false, s, bnEnv, true, reinterpret_cast<float*>(p + pBytes));
+    cudaError_t e =
+        gemm::gemmAuto(A, W, p, M, N, K, false, s, bnEnv, true, reinterpret_cast<float*>(p + pBytes), sc.sems);
     if (e == cudaSuccess) {
       dev::CollArgs a{};
       a.send = p;

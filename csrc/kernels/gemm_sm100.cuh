@@ -194,6 +194,105 @@ struct EpiPartialF32 {
   }
 };
 
+// Split-K with the reduction inside the GEMM, for decode shapes (a few
+// rows, so a tile's fix-up is a short job for one warp).  Every split stores its
+// fp32 partial as EpiPartialF32 does; then each epilogue warp that holds
+// valid rows counts itself on the (tile, lane quarter) semaphore, and the
+// warp of the split that arrives last sums those rows' partials in split
+// order (the order of the separate reduction kernel, so the results are the
+// same bits) and writes bf16 C, or silu(gate) * up for the interleaved
+// gate/up layout of EpiSiluMul.  This saves the reduction kernel's launch
+// and its pass over the partials.  Only warp-level synchronisation is used.
+// The semaphores are zero before a call and the last arriver puts its
+// semaphore back to zero.  One epilogue warpgroup only (NoHooks);
+// `afterTile` runs once the accumulator has been handed back, so the fix-up
+// overlaps the next tile's MMAs.
+template <bool SILU>
+struct EpiSplitFixup {
+  static constexpr bool kAfterTile = true;
+  EpiPartialF32 part;
+  uint32_t* sem;      // [tilesM * tilesN][4]: per output tile and TMEM lane quarter
+  __nv_bfloat16* C;   // [M, N] (or [M, N / 2] with SILU)
+  template <int SPAN>
+  __device__ __forceinline__ void operator()(uint32_t tmemAcc, const TileInfo& ti, const GemmShape& s, int laneRow,
+                                             int cBegin, uint4* st) const {
+    part.template operator()<SPAN>(tmemAcc, ti, s, laneRow, cBegin, st);
+  }
+  // One epilogue warp: `quarter` is its TMEM lane quarter (tile rows
+  // 32 * quarter ... + 31), `lane` its lane.
+  template <int BN>
+  __device__ __forceinline__ void afterTile(const TileInfo& ti, const GemmShape& s, int quarter, int lane) const {
+    const int r0 = ti.row0 + 32 * quarter;
+    if (r0 >= s.M) return;  // no valid rows: this warp stored nothing and counts nothing
+    const int rows = s.M - r0 < 32 ? s.M - r0 : 32;
+    __syncwarp();  // every lane's partial stores are issued
+    uint32_t last = 0;
+    if (lane == 0) {
+      __threadfence();  // ... and visible device-wide before the count
+      uint32_t* cnt = sem + (ti.tm * s.tilesN + ti.tn) * 4 + quarter;
+      last = atomicAdd(cnt, 1u) == static_cast<uint32_t>(s.splits - 1) ? 1u : 0u;
+      if (last) {
+        *cnt = 0u;        // every split of this call has counted: ready for the next call
+        __threadfence();  // order the other splits' partials before the loads below
+      }
+    }
+    if (__shfl_sync(0xffffffffu, last, 0) == 0u) return;
+    __syncwarp();  // lane 0's acquire (the fence after the count) orders the whole warp's loads
+    const size_t ldn = static_cast<size_t>(part.ldn);
+    const float* base = part.ws + static_cast<size_t>(r0) * ldn;
+    if constexpr (!SILU) {
+      constexpr int G = BN / 4;  // float4 groups per tile row
+      for (int idx = lane; idx < rows * G; idx += 32) {
+        const int r = idx / G;
+        const int col = ti.col0 + 4 * (idx - r * G);
+        if (col >= s.N) continue;
+        const float* p = base + r * ldn + col;
+        float4 a = __ldcg(reinterpret_cast<const float4*>(p));
+        for (int k = 1; k < s.splits; k++) {
+          const float4 b = __ldcg(reinterpret_cast<const float4*>(p + k * part.splitElems));
+          a.x += b.x;
+          a.y += b.y;
+          a.z += b.z;
+          a.w += b.w;
+        }
+        *reinterpret_cast<uint2*>(C + static_cast<size_t>(r0 + r) * s.N + col) =
+            make_uint2(packBf16(a.x, a.y), packBf16(a.z, a.w));
+      }
+    } else {
+      constexpr int G = BN / 8;  // groups of 4 outputs per tile row (BN / 2 outputs)
+      const int half = s.N / 2;
+      for (int idx = lane; idx < rows * G; idx += 32) {
+        const int r = idx / G;
+        const int jl = 4 * (idx - r * G);  // output column inside the tile
+        const int gcol = ti.col0 + (jl / 16) * 32 + (jl % 16);
+        const int j = ti.col0 / 2 + jl;    // output column
+        if (j >= half) continue;
+        const float* p = base + r * ldn + gcol;
+        float4 g = __ldcg(reinterpret_cast<const float4*>(p));
+        float4 u = __ldcg(reinterpret_cast<const float4*>(p + 16));
+        for (int k = 1; k < s.splits; k++) {
+          const float4 g2 = __ldcg(reinterpret_cast<const float4*>(p + k * part.splitElems));
+          const float4 u2 = __ldcg(reinterpret_cast<const float4*>(p + k * part.splitElems + 16));
+          g.x += g2.x, g.y += g2.y, g.z += g2.z, g.w += g2.w;
+          u.x += u2.x, u.y += u2.y, u.z += u2.z, u.w += u2.w;
+        }
+        auto f = [](float x, float y) { return x / (1.0f + __expf(-x)) * y; };
+        *reinterpret_cast<uint2*>(C + static_cast<size_t>(r0 + r) * half + j) =
+            make_uint2(packBf16(f(g.x, u.x), f(g.y, u.y)), packBf16(f(g.z, u.z), f(g.w, u.w)));
+      }
+    }
+  }
+};
+
+template <typename E, typename = void>
+struct HasAfterTile {
+  static constexpr bool value = false;
+};
+template <typename E>
+struct HasAfterTile<E, decltype((void)E::kAfterTile)> {
+  static constexpr bool value = E::kAfterTile;
+};
+
 // Gate/up epilogue.  B holds the gate and up projections interleaved in
 // groups of 16 rows (g0..15, u0..15, g16..31, u16..31, ...), so every
 // 32-column slice of the accumulator is (16 gate, 16 up) of the same output
@@ -467,6 +566,7 @@ __global__ void __launch_bounds__(ctaThreads<Hooks>(), 1)
       sm100::tcFenceBefore();
       __syncwarp();
       if (lane == 0) sm100::mbarArrive(&accEmpty[acc]);
+      if constexpr (HasAfterTile<Epi>::value) epi.template afterTile<BN>(ti, s, quarter, lane);
       if (++acc == 2) {
         acc = 0;
         accPhase ^= 1u;
