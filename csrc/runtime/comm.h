@@ -97,6 +97,7 @@ struct Window {
   std::vector<CUdeviceptr> peerVa;  // mappings of the peers' whole allocations
   std::vector<size_t> peerVaBytes;
   std::vector<CUmemGenericAllocationHandle> peerHandle;
+  std::vector<void*> ipcBase;  // peers' cudaMalloc allocations opened by IPC handle (cudaMalloc windows)
   CUmemGenericAllocationHandle localHandle = 0;  // the allocation's handle (owned by vcclMemAlloc)
   size_t localOffset = 0;                        // window offset inside that allocation
   CUmemGenericAllocationHandle mcHandle = 0;

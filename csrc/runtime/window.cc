@@ -4,13 +4,19 @@
 // The reference's vcclCommRegister pins a buffer for its own transport and
 // is a local call (reference: src/core/comm.cc:180-244); vcclCommRegister
 // keeps that meaning here.  vcclCommWindowRegister is the collective
-// counterpart that lets kernels touch the buffer from every GPU: each rank
-// exports the VMM handle of the vcclMemAlloc allocation that holds its
-// buffer, the handles travel over the bootstrap's Unix sockets (SCM_RIGHTS,
-// like the workspaces), every rank maps every peer's allocation, and when
-// the node supports NVLS the windows are also bound to one multicast object.
+// counterpart that lets kernels touch the buffer from every GPU.  For a
+// buffer inside a vcclMemAlloc allocation each rank exports the VMM handle,
+// the handles travel over the bootstrap's Unix sockets (SCM_RIGHTS, like
+// the workspaces), every rank maps every peer's allocation, and when the
+// node supports NVLS the windows are also bound to one multicast object.
+// A buffer from plain cudaMalloc (a PyTorch tensor, say) goes through CUDA
+// IPC instead: its allocation's IPC handle is all-gathered and every rank
+// opens the peers' handles; such windows have no multicast binding and
+// need one process per rank.
 // Collectives whose buffers lie in windows then run the zero-copy kernels of
 // csrc/kernels/window.cuh.
+#include <unistd.h>
+
 #include <algorithm>
 #include <cstring>
 #include <memory>
@@ -28,11 +34,15 @@ namespace {
 
 size_t roundUpTo(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+enum WinKind : uint32_t { kWinNone = 0, kWinVmm = 1, kWinIpc = 2 };
+
 struct WinInfo {
   uint64_t size;        // window bytes
   uint64_t offset;      // window offset inside the rank's allocation
   uint64_t allocBytes;  // the rank's allocation
-  uint64_t ok;          // the buffer lies in a vcclMemAlloc device allocation
+  uint32_t kind;        // WinKind
+  int32_t pid;
+  cudaIpcMemHandle_t ipc;  // kWinIpc: handle of the allocation
 };
 
 // Bind every rank's window to one multicast object (rank 0 creates it).
@@ -126,6 +136,10 @@ void windowRelease(DeviceState* ds, int me, Window* w) {
   const DriverApi* d = driverApi();
   if (d == nullptr) return;
   windowReleaseMulticast(ds, w);
+  for (size_t p = 0; p < w->ipcBase.size(); p++) {
+    if (static_cast<int>(p) != me && w->ipcBase[p] != nullptr) cudaIpcCloseMemHandle(w->ipcBase[p]);
+    w->ipcBase[p] = nullptr;
+  }
   for (size_t p = 0; p < w->peerVa.size(); p++) {
     if (static_cast<int>(p) == me) continue;
     if (w->peerVa[p]) {
@@ -161,20 +175,46 @@ extern "C" vcclResult_t vcclCommWindowRegister(vcclComm_t comm, void* buff, size
   void* allocBase = nullptr;
   size_t allocBytes = 0;
   CUmemGenericAllocationHandle h = 0;
-  const bool found = findDeviceAllocation(buff, size, &allocBase, &allocBytes, &h);
   std::vector<WinInfo> info(n);
-  info[me] = {size, found ? static_cast<uint64_t>(static_cast<char*>(buff) - static_cast<char*>(allocBase)) : 0,
-              allocBytes, found ? 1u : 0u};
+  WinInfo& mine = info[me];
+  memset(&mine, 0, sizeof(mine));
+  mine.size = size;
+  mine.pid = static_cast<int32_t>(getpid());
+  if (findDeviceAllocation(buff, size, &allocBase, &allocBytes, &h)) {
+    mine.kind = kWinVmm;
+  } else {
+    // Plain device memory: the allocation around the buffer, by IPC handle.
+    CUdeviceptr base = 0;
+    size_t bytes = 0;
+    if (d->memGetAddressRange(&base, &bytes, reinterpret_cast<CUdeviceptr>(buff)) == CUDA_SUCCESS &&
+        reinterpret_cast<CUdeviceptr>(buff) + size <= base + bytes &&
+        cudaIpcGetMemHandle(&mine.ipc, reinterpret_cast<void*>(base)) == cudaSuccess) {
+      mine.kind = kWinIpc;
+      allocBase = reinterpret_cast<void*>(base);
+      allocBytes = bytes;
+    }
+    cudaGetLastError();
+  }
+  mine.offset = mine.kind ? static_cast<uint64_t>(static_cast<char*>(buff) - static_cast<char*>(allocBase)) : 0;
+  mine.allocBytes = allocBytes;
   vcclResult_t res = bs->allGather(info.data(), sizeof(WinInfo));
   if (res != vcclSuccess) return res;
   for (int p = 0; p < n; p++) {
-    if (!info[p].ok) {
-      VERR("vcclCommWindowRegister: rank %d's buffer is not inside a vcclMemAlloc device allocation", p);
+    if (info[p].kind == kWinNone) {
+      VERR("vcclCommWindowRegister: rank %d's buffer is neither vcclMemAlloc nor cudaMalloc device memory", p);
+      return vcclInvalidArgument;
+    }
+    if (info[p].kind != info[0].kind) {
+      VERR("vcclCommWindowRegister: every rank must pass the same kind of memory (vcclMemAlloc or cudaMalloc)");
       return vcclInvalidArgument;
     }
     if (info[p].size != size) {
       VERR("vcclCommWindowRegister: window sizes differ (%zu on rank %d, %zu here)",
            static_cast<size_t>(info[p].size), p, size);
+      return vcclInvalidArgument;
+    }
+    if (info[p].kind == kWinIpc && p != me && info[p].pid == mine.pid) {
+      VERR("vcclCommWindowRegister: cudaMalloc windows need one process per rank (use vcclMemAlloc memory)");
       return vcclInvalidArgument;
     }
   }
@@ -188,7 +228,33 @@ extern "C" vcclResult_t vcclCommWindowRegister(vcclComm_t comm, void* buff, size
   w->peerVa.assign(n, 0);
   w->peerVaBytes.assign(n, 0);
   w->peerHandle.assign(n, 0);
+  w->ipcBase.assign(n, nullptr);
   w->peer[me] = w->base;
+
+  if (mine.kind == kWinIpc) {
+    bool ok = true;
+    for (int p = 0; p < n && ok; p++) {
+      if (p == me) continue;
+      ok = cudaIpcOpenMemHandle(&w->ipcBase[p], info[p].ipc, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+      if (ok) w->peer[p] = static_cast<char*>(w->ipcBase[p]) + info[p].offset;
+    }
+    cudaGetLastError();
+    if (!everyone(bs, ok)) {
+      windowRelease(ds, me, w.get());
+      VERR("vcclCommWindowRegister: opening a peer's IPC handle failed on some rank");
+      return vcclSystemError;
+    }
+    res = bs->barrier();
+    if (res != vcclSuccess) {
+      windowRelease(ds, me, w.get());
+      return res;
+    }
+    VINFO("window registered: %zu bytes of cudaMalloc memory, point-to-point", size);
+    std::lock_guard<std::mutex> g(comm->regMu);
+    comm->windows.push_back(w.get());
+    *win = w.release();
+    return vcclSuccess;
+  }
 
   int fd = -1;
   bool ok = d->memExport(&fd, h, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0) == CUDA_SUCCESS;

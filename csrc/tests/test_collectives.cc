@@ -543,12 +543,23 @@ void windowTest(vcclComm_t c, int me, int n) {
   EXPECT_OK(vcclCommWindowDeregister(c, wb));
   EXPECT_OK(vcclMemFree(a));
   EXPECT_OK(vcclMemFree(b));
-  // not from vcclMemAlloc: refused on every rank
+  // plain cudaMalloc memory: a point-to-point window through CUDA IPC
   void* plain = nullptr;
-  cudaMalloc(&plain, 1 << 20);
+  cudaMalloc(&plain, winBytes);
   vcclWindow_t wp = nullptr;
-  EXPECT(vcclCommWindowRegister(c, plain, 1 << 20, &wp, 0) == vcclInvalidArgument, "plain cudaMalloc window");
+  EXPECT_OK(vcclCommWindowRegister(c, plain, winBytes, &wp, 0));
+  if (wp != nullptr) {
+    char* P = static_cast<char*>(plain);
+    const size_t ro = (cnt * 4 + 4095) / 4096 * 4096;
+    upload(P, vcclFloat32, cnt, 0);
+    EXPECT_OK(vcclAllReduce(P, P + ro, cnt, vcclFloat32, vcclSum, c));
+    checkDevice(P + ro, vcclFloat32, cnt, "allreduce cudaMalloc window", [&](size_t i) { return expect(vcclSum, n, i); });
+    EXPECT_OK(vcclCommWindowDeregister(c, wp));
+  }
   cudaFree(plain);
+  // host memory: refused on every rank
+  std::vector<char> host(1 << 20);
+  EXPECT(vcclCommWindowRegister(c, host.data(), host.size(), &wp, 0) == vcclInvalidArgument, "host window");
 }
 
 // The pipelined NVLS all-reduce on the device-buffer sweep sizes.

@@ -54,6 +54,16 @@ def main():
     comm.window_deregister(ws)
     comm.window_deregister(wr)
     del send, recv
+
+    # a tensor from PyTorch's own allocator (cudaMalloc): a window through CUDA IPC
+    both = torch.empty(2 * count, dtype=torch.bfloat16, device="cuda")
+    wb = comm.window_register(both)
+    both[:count].copy_(inputs(rank))
+    comm.all_reduce(both[:count], both[count:])
+    torch.cuda.synchronize()
+    err = (both[count:].float() - total).abs().max().item()
+    assert err <= 0.05 * total.abs().max().item(), f"cudaMalloc window all_reduce err {err}"
+    comm.window_deregister(wb)
     comm.destroy()
     dist.destroy_process_group()
     print(f"rank {rank}: window ok", flush=True)
