@@ -29,31 +29,11 @@
 #include "kernels/device_common.cuh"
 #include "kernels/dtypes.cuh"
 #include "kernels/movers.cuh"
+#include "kernels/ranges.cuh"
 
 namespace vccl {
 namespace dev {
 
-__device__ __forceinline__ void blockRange(size_t total, int parts, int idx, size_t align, size_t* lo,
-                                           size_t* hi) {
-  size_t per = (total + parts - 1) / parts;
-  per = (per + align - 1) / align * align;
-  size_t a = per * static_cast<size_t>(idx);
-  *lo = a < total ? a : total;
-  size_t b = *lo + per;
-  *hi = b < total ? b : total;
-}
-
-// Block `idx`'s part of a round of `m` units, split as a round of `full`
-// units would be (full >= m).  Multi-round kernels split every round of a
-// launch the same way, so block b only ever touches its own bytes of the
-// staging region: a short last round must not hand block b bytes that a
-// slower block b' (which block b never synchronises with) still reads.
-__device__ __forceinline__ void roundRange(size_t full, size_t m, int parts, int idx, size_t align, size_t* lo,
-                                           size_t* hi) {
-  blockRange(full, parts, idx, align, lo, hi);
-  if (*hi > m) *hi = m;
-  if (*lo > *hi) *lo = *hi;
-}
 
 // ---------------------------------------------------------------------------
 // LL one-shot all-reduce.  Grid is always the communicator's llBlocks so every block's epoch
@@ -320,11 +300,8 @@ __global__ void __launch_bounds__(512) allReduceNvls(DevComm c, CollArgs a, size
   const size_t total = a.count * esz;
   if (!blockBarrier(c, blk, kWhereStart)) return;
   char* local = c.data[me];
-  // One chunk size for every round of the launch (see roundRange): a single
-  // round takes ceil(total / n) rounded up to 16 bytes (n * cb fits because
-  // roundBytes leaves 16 bytes per rank spare), longer messages full rounds.
-  size_t cb = total <= roundBytes ? (total + n - 1) / n : roundBytes / n;
-  cb = total <= roundBytes ? (cb + 15) / 16 * 16 : cb / 16 * 16;
+  // One chunk size for every round of the launch (see roundRange).
+  const size_t cb = nvlsRoundChunk(total, n, roundBytes);
   const size_t step = cb * n;
   size_t s0, s1;
   blockRange(cb, G, blk, 16, &s0, &s1);

@@ -133,8 +133,7 @@ __global__ void __launch_bounds__(512) allReduceWin(DevComm c, WinArgs w) {
   const int blk = blockIdx.x, G = gridDim.x, n = c.nranks, me = c.rank;
   if (!winStart(c, blk, w, sScale)) return;
   constexpr size_t PK = VEC ? 16 / sizeof(T) : 1;
-  size_t ce = (w.count + n - 1) / n;
-  ce = (ce + PK - 1) / PK * PK;
+  const size_t ce = winChunk(w.count, n, PK);
   size_t s0, s1;
   blockRange(ce, G, blk, PK, &s0, &s1);
   const size_t lo = me * ce + s0;
@@ -155,8 +154,7 @@ __global__ void __launch_bounds__(512) allReduceWinNvls(DevComm c, WinArgs w) {
   if (!winStart(c, blk, w, sScale)) return;
   if constexpr (HasMultimem<T, K>::value) {
     const size_t total = w.count * sizeof(T);
-    size_t cb = (total + n - 1) / n;
-    cb = (cb + 15) / 16 * 16;
+    const size_t cb = winChunk(total, n, 16);
     size_t s0, s1;
     blockRange(cb, G, blk, 16, &s0, &s1);
     const size_t lo = me * cb + s0;

@@ -49,3 +49,9 @@ def test_gemm_index_arithmetic():
 def test_tuning_tables():
     """VCCL_TUNING_FILE parsing and rule lookup."""
     assert "tuning: OK" in _run("test_tuning")
+
+
+def test_collective_index_arithmetic():
+    """Coverage and staging bounds of the staged, pipelined-NVLS and window kernels' splits, with a
+    negative control for re-split rounds (csrc/tests/test_coll_index.cc)."""
+    assert "all checks passed" in _run("test_coll_index")
