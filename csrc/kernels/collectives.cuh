@@ -120,8 +120,7 @@ __global__ void __launch_bounds__(512) allReduceTwoShot(DevComm c, CollArgs a, s
   // Chunk size and block split are fixed for the launch (a short last
   // round is clipped, not re-split), so every block keeps its own slots.
   const size_t first = a.count < roundElems ? a.count : roundElems;
-  size_t ce = (first + n - 1) / n;
-  ce = (ce + PK - 1) / PK * PK;
+  const size_t ce = rankChunk(first, n, PK);
   size_t s0, s1;
   blockRange(ce, G, blk, PK, &s0, &s1);
   for (size_t base = 0; base < a.count; base += roundElems) {

@@ -41,8 +41,9 @@ __host__ __device__ __forceinline__ size_t nvlsRoundChunk(size_t total, int n, s
   return roundBytes / n / 16 * 16;
 }
 
-// Per-rank chunk (elements, a multiple of pk) of a window all-reduce.
-__host__ __device__ __forceinline__ size_t winChunk(size_t count, int n, size_t pk) {
+// Per-rank chunk (units, a multiple of pk) when `count` units are split
+// among n ranks (two-shot rounds, window all-reduce).
+__host__ __device__ __forceinline__ size_t rankChunk(size_t count, int n, size_t pk) {
   return ((count + n - 1) / n + pk - 1) / pk * pk;
 }
 

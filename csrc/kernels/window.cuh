@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(512) allReduceWin(DevComm c, WinArgs w) {
   const int blk = blockIdx.x, G = gridDim.x, n = c.nranks, me = c.rank;
   if (!winStart(c, blk, w, sScale)) return;
   constexpr size_t PK = VEC ? 16 / sizeof(T) : 1;
-  const size_t ce = winChunk(w.count, n, PK);
+  const size_t ce = rankChunk(w.count, n, PK);
   size_t s0, s1;
   blockRange(ce, G, blk, PK, &s0, &s1);
   const size_t lo = me * ce + s0;
@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(512) allReduceWinNvls(DevComm c, WinArgs w) {
   if (!winStart(c, blk, w, sScale)) return;
   if constexpr (HasMultimem<T, K>::value) {
     const size_t total = w.count * sizeof(T);
-    const size_t cb = winChunk(total, n, 16);
+    const size_t cb = rankChunk(total, n, 16);
     size_t s0, s1;
     blockRange(cb, G, blk, 16, &s0, &s1);
     const size_t lo = me * cb + s0;

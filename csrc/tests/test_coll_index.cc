@@ -73,6 +73,52 @@ void checkNvlsRounds(size_t total, int n, int G, size_t dataBytes) {
            total, n, G, b, in[b], red[b], out[b]);
 }
 
+// Two-shot all-reduce (allReduceTwoShot): rounds of n chunks of ce
+// elements; block b pushes [s0, s1) of chunk q into slot `me` of rank q at
+// the same chunk-relative offsets in every round.
+void checkTwoShot(size_t count, int n, int G, size_t slotElems, size_t pk) {
+  const size_t roundElems = slotElems * n;
+  const size_t first = count < roundElems ? count : roundElems;
+  const size_t ce = rankChunk(first, n, pk);
+  EXPECT(ce <= slotElems, "chunk %zu exceeds the slot %zu", ce, slotElems);
+  std::vector<unsigned char> done(count, 0);
+  for (size_t base = 0; base < count; base += roundElems) {
+    const size_t m = (count - base) < roundElems ? (count - base) : roundElems;
+    for (int blk = 0; blk < G; blk++) {
+      size_t s0, s1;
+      blockRange(ce, G, blk, pk, &s0, &s1);
+      for (int q = 0; q < n; q++) {
+        const size_t lo = q * ce + s0, hiRaw = q * ce + s1, hi = hiRaw < m ? hiRaw : m;
+        for (size_t e = lo; e < hi; e++) done[base + e]++;
+        if (lo < hi) EXPECT(s0 + (hi - lo) <= s1 && s1 <= slotElems, "slot range of block %d", blk);
+      }
+    }
+  }
+  for (size_t e = 0; e < count; e++)
+    EXPECT(done[e] == 1, "two-shot count=%zu n=%d G=%d element %zu done %d", count, n, G, e, done[e]);
+}
+
+// Reduce-scatter push and all-gather pull: rounds of at most `slot` units,
+// every round split as the first (roundRange).
+void checkRoundSplit(size_t total, int G, size_t slot, size_t align) {
+  const size_t full = total < slot ? total : slot;
+  std::vector<unsigned char> done(total, 0);
+  std::vector<int> owner(slot, -1);
+  for (size_t base = 0; base < total; base += slot) {
+    const size_t m = (total - base) < slot ? (total - base) : slot;
+    for (int blk = 0; blk < G; blk++) {
+      size_t s0, s1;
+      roundRange(full, m, G, blk, align, &s0, &s1);
+      for (size_t e = s0; e < s1; e++) {
+        done[base + e]++;
+        EXPECT(owner[e] == -1 || owner[e] == blk, "slot unit %zu used by blocks %d and %d", e, owner[e], blk);
+        owner[e] = blk;
+      }
+    }
+  }
+  for (size_t e = 0; e < total; e++) EXPECT(done[e] == 1, "round split total=%zu G=%d unit %zu", total, G, e);
+}
+
 // Negative control: splitting every round afresh (the chunk recomputed from
 // the round's own size) hands some staging bytes to different blocks in
 // different rounds; the owner check above must be able to see that.
@@ -133,7 +179,7 @@ void checkNvlsPipe(size_t total, int n, int G, int pieces, size_t dataBytes) {
 // Window all-reduce (allReduceWin + winReduceBroadcast): rank chunks of ce
 // elements, block ranges aligned to the pack, packs then an element tail.
 void checkWindowAllReduce(size_t count, int n, int G, size_t pk) {
-  const size_t ce = winChunk(count, n, pk);
+  const size_t ce = rankChunk(count, n, pk);
   std::vector<unsigned char> done(count, 0);
   for (int me = 0; me < n; me++)
     for (int blk = 0; blk < G; blk++) {
@@ -193,6 +239,13 @@ int main() {
         checkNvlsRounds(total, n, G, small);
         for (int pieces : {1, 2, 4, 7}) checkNvlsPipe(total, n, G, pieces, small);
       }
+  for (int n : {2, 3, 8})
+    for (int G : {1, 5, 16})
+      for (size_t count : {size_t(1), size_t(999), size_t(5000), size_t(40000)})
+        for (size_t pk : {size_t(1), size_t(8)}) checkTwoShot(count, n, G, 2048, pk);
+  for (int G : {1, 6, 16})
+    for (size_t total : {size_t(10), size_t(4096), size_t(5000), size_t(30001)})
+      for (size_t align : {size_t(1), size_t(16)}) checkRoundSplit(total, G, 4096, align);
   for (int n : {2, 5, 8})
     for (int G : {1, 4, 13})
       for (size_t count : {size_t(1), size_t(7), size_t(64), size_t(1000), size_t(4099), size_t(33333)})
