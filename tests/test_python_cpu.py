@@ -531,3 +531,31 @@ def test_window_api_without_device():
         assert comm.WIN_NO_MULTICAST == 1
     finally:
         comm.destroy()
+
+
+def test_grad_buckets_single_rank_host():
+    """GradBuckets on a one-rank control-plane communicator: average leaves
+    the gradients as they are, PreMulSum scales them; host tensors use no window."""
+    _env()
+    import vkccl_b200 as v
+    from vkccl_b200.parallel import GradBuckets
+
+    comm = v.Communicator(1, v.get_unique_id(), 0)
+    try:
+        torch.manual_seed(0)
+        params = [torch.nn.Parameter(torch.randn(n)) for n in (5, 300, 7, 64)]
+        for p in params:
+            p.grad = torch.randn_like(p)
+        want = [p.grad.clone() for p in params]
+        gb = GradBuckets(comm, params, bucket_bytes=1024)
+        assert len(gb.plan) > 1
+        gb.all_reduce()
+        for p, w in zip(params, want):
+            assert torch.equal(p.grad, w)
+        gb.all_reduce(premul=0.5)
+        for p, w in zip(params, want):
+            torch.testing.assert_close(p.grad, 0.5 * w)
+        assert gb._window is None
+        gb.close()
+    finally:
+        comm.destroy()

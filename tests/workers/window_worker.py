@@ -1,7 +1,8 @@
 # SPDX-License-Identifier: Apache-2.0
 """Per-rank body of the window GPU test (run by torchrun): torch tensors on
-vcclMemAlloc memory, registered as windows, through all-reduce, all-gather
-and reduce-scatter, against locally computed sums."""
+vcclMemAlloc memory and from PyTorch's allocator, registered as windows,
+through all-reduce, all-gather and reduce-scatter, and GradBuckets on its
+registered bucket buffer, against locally computed results."""
 
 import os
 import sys
@@ -64,6 +65,27 @@ def main():
     err = (both[count:].float() - total).abs().max().item()
     assert err <= 0.05 * total.abs().max().item(), f"cudaMalloc window all_reduce err {err}"
     comm.window_deregister(wb)
+
+    # data-parallel gradient buckets on one registered buffer
+    from vkccl_b200.parallel import GradBuckets
+
+    sizes = [1 << 20, 4099, 3 << 18, 77]
+    params = [torch.nn.Parameter(torch.zeros(s, device="cuda")) for s in sizes]
+
+    def grads(r):
+        g = torch.Generator(device="cuda").manual_seed(500 + r)
+        return [torch.randn(s, device="cuda", generator=g) for s in sizes]
+
+    for p, g in zip(params, grads(rank)):
+        p.grad = g
+    gb = GradBuckets(comm, params, bucket_bytes=2 << 20)
+    gb.all_reduce()
+    torch.cuda.synchronize()
+    assert gb._window is not None
+    mean = [sum(gs) / n for gs in zip(*[grads(r) for r in range(n)])]
+    for p, m in zip(params, mean):
+        torch.testing.assert_close(p.grad, m, rtol=1e-5, atol=1e-6)
+    gb.close()
     comm.destroy()
     dist.destroy_process_group()
     print(f"rank {rank}: window ok", flush=True)

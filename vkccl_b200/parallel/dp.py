@@ -8,6 +8,12 @@ and unpacked.  The reference offers the primitives (avg, PreMulSum;
 reference: src/core/collectives.cc:85-98, src/core/comm.cc:264-319) and
 leaves bucketing to the caller; on NVLink, buckets of a few MiB keep each
 all-reduce on the bandwidth-optimal algorithm while bounding launch count.
+
+On CUDA the buckets are views of one buffer that every rank registers as a
+window (the bucket plan, hence every offset, is the same on every rank), so
+each bucket's all-reduce runs in place on the peers' buffers instead of
+staging through the library's workspace.  `close()` deregisters it
+(collective, like the registration on the first all_reduce).
 """
 
 from __future__ import annotations
@@ -43,17 +49,47 @@ def plan_buckets(sizes: Sequence[int], dtypes: Sequence[torch.dtype], bucket_byt
 class GradBuckets:
     """All-reduce the .grad of `params` over `comm` (average by default)."""
 
-    def __init__(self, comm, params: Sequence[torch.nn.Parameter], bucket_bytes: int = 16 << 20):
+    def __init__(self, comm, params: Sequence[torch.nn.Parameter], bucket_bytes: int = 16 << 20,
+                 use_window: bool = True):
         self.comm = comm
         self.params = [p for p in params if p.requires_grad]
         self.plan = plan_buckets([p.numel() for p in self.params], [p.dtype for p in self.params], bucket_bytes)
         self._flat: Dict[int, torch.Tensor] = {}
+        self.use_window = use_window
+        self._window = None  # (backing uint8 tensor, handle)
+
+    def _window_buffers(self, device: torch.device) -> None:
+        """One registered buffer holding every bucket (256-byte aligned views)."""
+        from vkccl_b200.comm import mem_alloc_tensor
+
+        offsets, total = [], 0
+        for idx in self.plan:
+            p0 = self.params[idx[0]]
+            nbytes = sum(self.params[i].numel() for i in idx) * p0.element_size()
+            offsets.append((total, nbytes, p0.dtype))
+            total += (nbytes + 255) // 256 * 256
+        backing = mem_alloc_tensor((max(total, 256),), torch.uint8, device=device)
+        handle = self.comm.window_register(backing)
+        for b, (off, nbytes, dt) in enumerate(offsets):
+            self._flat[b] = backing[off:off + nbytes].view(dt)
+        self._window = (backing, handle)
+
+    def close(self) -> None:
+        """Deregister the bucket window (collective: every rank calls it)."""
+        if self._window is not None:
+            self.comm.window_deregister(self._window[1])
+            self._window = None
+            self._flat.clear()
 
     def all_reduce(self, premul: float = 0.0) -> None:
         """Average gradients; with premul != 0, sum of premul * grad instead."""
         from vkccl_b200.comm import DataType, RedOp
         from vkccl_b200.torch_comm import vccl_dtype
 
+        dev = self.params[0].device if self.params else torch.device("cpu")
+        if (self.use_window and self._window is None and dev.type == "cuda"
+                and hasattr(self.comm, "window_register")):
+            self._window_buffers(dev)
         for b, idx in enumerate(self.plan):
             grads = [self.params[i].grad for i in idx]
             if any(g is None for g in grads):
