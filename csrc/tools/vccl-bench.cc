@@ -7,7 +7,9 @@
 // --warmup, --dtype, --check, --op allreduce|allgather|reducescatter|
 // broadcast|alltoall.  Differences: buffers are device memory, time is
 // measured with CUDA events on the launching stream and reported as the
-// maximum over ranks, and --algo forces an all-reduce algorithm.
+// maximum over ranks, --algo forces an all-reduce algorithm, --graph times a
+// captured loop, and --window puts both buffers in registered windows
+// (vcclMemAlloc + vcclCommWindowRegister: the zero-copy kernels).
 // Multi-process launch: VCCL_RANK / VCCL_NRANKS and VCCL_COMM_ID or
 // VCCL_ID_FILE, as in the reference.
 #include <cuda_runtime.h>
@@ -34,6 +36,7 @@ struct Opts {
   int iters = 20, warmup = 3, launch = 0;
   bool check = false;
   bool graph = false;
+  bool window = false;
   vcclDataType_t dt = vcclFloat32;
   std::string algo;
 };
@@ -57,7 +60,8 @@ double busFactor(const std::string& op, int n) {
   std::fprintf(stderr,
                "usage: vccl-bench [--launch N] [--op allreduce|allgather|reducescatter|broadcast|alltoall]\n"
                "                  [-b min] [-e max] [-f factor] [--iters N] [--warmup N]\n"
-               "                  [--dtype f32|f16|bf16|f64] [--algo ll|twoshot|nvls] [--check]\n");
+               "                  [--dtype f32|f16|bf16|f64] [--algo ll|twoshot|nvls|nvls_pipe] [--check]\n"
+               "                  [--graph] [--window]\n");
   std::exit(2);
 }
 
@@ -128,8 +132,18 @@ int runRank(const Opts& o, int rank, int n, const vcclUniqueId& id) {
   void *s = nullptr, *r = nullptr;
   size_t cap = o.maxBytes + 4096;
   if (o.op == "allgather") cap = o.maxBytes + 4096;
-  cudaMalloc(&s, cap);
-  cudaMalloc(&r, cap);
+  vcclWindow_t ws = nullptr, wr = nullptr;
+  if (o.window) {
+    if (vcclMemAlloc(&s, cap) != vcclSuccess || vcclMemAlloc(&r, cap) != vcclSuccess ||
+        vcclCommWindowRegister(c, s, cap, &ws, 0) != vcclSuccess ||
+        vcclCommWindowRegister(c, r, cap, &wr, 0) != vcclSuccess) {
+      std::fprintf(stderr, "rank %d: window set-up failed: %s\n", rank, vcclGetLastError(c));
+      return 1;
+    }
+  } else {
+    cudaMalloc(&s, cap);
+    cudaMalloc(&r, cap);
+  }
   cudaMemset(s, 0, cap);
   if (o.check && checkF32(o, c, rank, n, static_cast<float*>(s), static_cast<float*>(r), o.maxBytes)) return 1;
   cudaStream_t st;
@@ -206,8 +220,15 @@ int runRank(const Opts& o, int rank, int n, const vcclUniqueId& id) {
       std::printf("%14zu %12.2f %12.2f %12.2f\n", static_cast<size_t>(eff), us, algbw, algbw * busFactor(o.op, n));
     }
   }
-  cudaFree(s);
-  cudaFree(r);
+  if (o.window) {
+    vcclCommWindowDeregister(c, ws);
+    vcclCommWindowDeregister(c, wr);
+    vcclMemFree(s);
+    vcclMemFree(r);
+  } else {
+    cudaFree(s);
+    cudaFree(r);
+  }
   cudaFree(tMax);
   vcclCommDestroy(c);
   return 0;
@@ -263,6 +284,7 @@ int main(int argc, char** argv) {
     else if (a == "--launch") o.launch = std::atoi(next());
     else if (a == "--check") o.check = true;
     else if (a == "--graph") o.graph = true;
+    else if (a == "--window") o.window = true;
     else if (a == "--algo") o.algo = next();
     else if (a == "--dtype") {
       std::string d = next();
