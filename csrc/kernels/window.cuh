@@ -206,6 +206,27 @@ __global__ void __launch_bounds__(512) allGatherWin(DevComm c, WinArgs w) {
   (void)blockBarrier(c, blk, kWhereWindow);
 }
 
+// All-to-all with equal blocks, receive buffer in a window: every rank
+// writes its block q straight into rank q's receive buffer at offset
+// rank * bytes (one NVLink write per byte, no slot ring, no copy-out).
+// w.count = bytes per block; w.send[me] is the local send buffer.
+__global__ void __launch_bounds__(512) allToAllWin(DevComm c, WinArgs w) {
+  __shared__ double sScale[kMaxRanks];
+  const int blk = blockIdx.x, G = gridDim.x, n = c.nranks, me = c.rank;
+  if (!winStart(c, blk, w, sScale)) return;
+  const size_t bytes = w.count;
+  size_t lo, hi;
+  blockRange(bytes, G, blk, 16, &lo, &hi);
+  if (lo < hi) {
+    for (int k = 0; k < n; k++) {
+      int q = me + k;
+      if (q >= n) q -= n;
+      copyAny(w.recv[q] + me * bytes + lo, w.send[me] + q * bytes + lo, hi - lo);
+    }
+  }
+  (void)blockBarrier(c, blk, kWhereWindow);
+}
+
 // Reduce-scatter, send buffer in a window: rank r reduces its chunk
 // (elements [r*count, (r+1)*count) of every send buffer) straight from the
 // peers, through the switch when the send buffers are multicast-bound (and

@@ -462,6 +462,35 @@ bool windowCollective(const HostOp& h, const LaunchCtx& lc, vcclResult_t* out) {
   }
 }
 
+// Zero-copy all-to-all: equal blocks (vcclAllToAll's layout) with the
+// receive buffer in a registered window; every rank writes its blocks into
+// the peers' receive buffers.  The window, or null when this does not apply
+// (the slot-ring kernel runs).  Decided on the caller's pointers, before any
+// staging: a receive buffer in a window is device memory.
+const Window* windowForAllToAll(const HostOp& h) {
+  vcclComm_t comm = h.comm;
+  const int n = comm->nranks;
+  if (!comm->dev || !comm->dev->windowsEnabled || n == 1 || comm->windows.empty()) return nullptr;
+  const size_t cnt = h.sc[0];
+  for (int q = 0; q < n; q++)
+    if (h.sc[q] != cnt || h.rc[q] != cnt || h.sd[q] != q * cnt || h.rd[q] != q * cnt) return nullptr;
+  const size_t bytes = cnt * vcclTypeSize(h.dt);
+  return bytes == 0 ? nullptr : comm->findWindow(h.recv, bytes * n);
+}
+
+vcclResult_t windowAllToAll(const HostOp& h, const Window* wr) {
+  vcclComm_t comm = h.comm;
+  const int n = comm->nranks, me = comm->rank;
+  const size_t bytes = h.sc[0] * vcclTypeSize(h.dt);
+  dev::WinArgs w{};
+  w.recvOff = static_cast<uint64_t>(h.recv - wr->base);
+  for (int q = 0; q < n; q++) w.recv[q] = wr->peer[q] + w.recvOff;
+  w.send[me] = h.send;
+  w.count = bytes;
+  noteAlgorithm("all-to-all", "window push", n, bytes * n);
+  return cudaToVccl(launchAllToAllWindow(launchCtx(comm, h.stream), w), "window all-to-all launch");
+}
+
 vcclResult_t launchColl(const HostOp& h) {
   vcclComm_t comm = h.comm;
   const size_t es = vcclTypeSize(h.dt);
@@ -568,6 +597,15 @@ vcclResult_t launchOps(vcclComm_t comm, std::vector<HostOp>& ops, std::vector<Pe
   while (i < ops.size()) {
     HostOp& h = ops[i];
     Staging st;
+    const Window* a2aWin = h.kind == Kind::AllToAllv ? windowForAllToAll(h) : nullptr;
+    if (a2aWin != nullptr) {
+      VTRY(prepareBuffers(h, st));  // a host send buffer is staged; the receive buffer is device memory
+      VTRY(windowAllToAll(h, a2aWin));
+      VTRY(st.finish(h.stream));
+      if (h.sync) waits->push_back({comm, h.stream});
+      i++;
+      continue;
+    }
     if (usesP2pKernel(h.kind)) {
       if (comm->nranks == 1) {
         // Only self copies exist (gather/scatter/all-to-all on one rank).

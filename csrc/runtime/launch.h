@@ -47,6 +47,7 @@ cudaError_t launchP2p(const LaunchCtx& lc, const dev::P2pPlan& plan);
 cudaError_t launchAllReduceWindow(const LaunchCtx& lc, vcclDataType_t dt, int redKind, const dev::WinArgs& w,
                                   bool viaSwitch);
 cudaError_t launchAllGatherWindow(const LaunchCtx& lc, const dev::WinArgs& w);
+cudaError_t launchAllToAllWindow(const LaunchCtx& lc, const dev::WinArgs& w);
 cudaError_t launchReduceScatterWindow(const LaunchCtx& lc, vcclDataType_t dt, int redKind, const dev::WinArgs& w,
                                       bool viaSwitch);
 // Single-rank helpers: dst = src * scale (float types) or plain copy.

@@ -69,6 +69,12 @@ cudaError_t launchAllGatherWindow(const LaunchCtx& lc, const dev::WinArgs& w) {
   return cudaGetLastError();
 }
 
+cudaError_t launchAllToAllWindow(const LaunchCtx& lc, const dev::WinArgs& w) {
+  const int g = gridFor(w.count * lc.dc.nranks, lc.nblocks);
+  dev::allToAllWin<<<g, kThreads, 0, lc.stream>>>(lc.dc, w);
+  return cudaGetLastError();
+}
+
 cudaError_t launchReduceScatterWindow(const LaunchCtx& lc, vcclDataType_t dt, int redKind, const dev::WinArgs& w,
                                       bool viaSwitch) {
   const size_t esz = vcclTypeSize(dt);

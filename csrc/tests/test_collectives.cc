@@ -538,6 +538,22 @@ void windowTest(vcclComm_t c, int me, int n) {
   upload(A, vcclFloat32, per * n, 0);
   EXPECT_OK(vcclReduceScatter(A, local, per, vcclFloat32, vcclSum, c));
   checkDevice(local, vcclFloat32, per, "reducescatter", [&](size_t i) { return expect(vcclSum, n, me * per + i); });
+  // all-to-all into window B from window A (equal blocks): block q of rank p
+  // lands in rank q's block p
+  upload(A, vcclFloat32, per * n, 0);
+  EXPECT_OK(vcclAllToAll(A, B, per, vcclFloat32, c));
+  for (int p = 0; p < n; p++) {
+    std::vector<float> g(per);
+    cudaMemcpy(g.data(), B + p * per * 4, per * 4, cudaMemcpyDeviceToHost);
+    std::vector<float> want(per * n);
+    fill(want.data(), vcclFloat32, p, per * n);
+    for (size_t i = 0; i < per; i += 89)
+      if (!near(g[i], want[me * per + i], vcclFloat32)) {
+        std::fprintf(stderr, "FAIL window alltoall block from rank %d i=%zu\n", p, i);
+        gFail++;
+        break;
+      }
+  }
   cudaFree(local);
   EXPECT_OK(vcclCommWindowDeregister(c, wa));
   EXPECT_OK(vcclCommWindowDeregister(c, wb));

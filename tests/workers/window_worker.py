@@ -52,6 +52,12 @@ def main():
     err = (out.float() - want).abs().max().item()
     assert err <= 0.05 * want.abs().max().item(), f"window reduce_scatter err {err}"
 
+    # all-to-all with equal blocks into the receive window
+    comm.all_to_all(send[: per * n], recv[: per * n])
+    torch.cuda.synchronize()
+    for r in range(n):
+        assert torch.equal(recv[r * per:(r + 1) * per], inputs(r)[rank * per:(rank + 1) * per]), f"all_to_all {r}"
+
     comm.window_deregister(ws)
     comm.window_deregister(wr)
     del send, recv
