@@ -206,6 +206,36 @@ __global__ void __launch_bounds__(512) allGatherWin(DevComm c, WinArgs w) {
   (void)blockBarrier(c, blk, kWhereWindow);
 }
 
+// Broadcast, receive buffer in a window: the root writes its buffer into
+// every rank's receive buffer, with one multimem.st per 16 bytes when the
+// receive buffers are multicast-bound (one copy leaves the root), else with a
+// store per rank.  The other ranks only take part in the barriers.
+__global__ void __launch_bounds__(512) broadcastWin(DevComm c, WinArgs w, int root) {
+  __shared__ double sScale[kMaxRanks];
+  const int blk = blockIdx.x, G = gridDim.x, n = c.nranks, me = c.rank;
+  if (!winStart(c, blk, w, sScale)) return;
+  const size_t bytes = w.count;
+  size_t lo, hi;
+  blockRange(bytes, G, blk, 16, &lo, &hi);
+  if (me == root && lo < hi) {
+    const char* src = w.send[me] + lo;
+    if (w.mcRecv != nullptr) {
+      // bytes, the send buffer and the receive offset are multiples of 16 here
+      char* dst = w.mcRecv + lo;
+      for (size_t i = threadIdx.x; i < (hi - lo) / 16; i += blockDim.x)
+        multimemStore16(dst + i * 16, ldCG(src + i * 16));
+    } else {
+      for (int k = 0; k < n; k++) {
+        int q = me + k;
+        if (q >= n) q -= n;
+        copyAny(w.recv[q] + lo, src, hi - lo);
+      }
+    }
+  }
+  fenceProxyAlias();
+  (void)blockBarrier(c, blk, kWhereWindow);
+}
+
 // All-to-all with equal blocks, receive buffer in a window: every rank
 // writes its block q straight into rank q's receive buffer at offset
 // rank * bytes (one NVLink write per byte, no slot ring, no copy-out).

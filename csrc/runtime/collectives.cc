@@ -447,6 +447,17 @@ bool windowCollective(const HostOp& h, const LaunchCtx& lc, vcclResult_t* out) {
       *out = cudaToVccl(launchAllGatherWindow(lc, w), "window all-gather launch");
       return true;
     }
+    case Kind::Broadcast: {
+      if (bytes <= lc.llMax) return false;
+      const Window* wr = comm->findWindow(h.recv, bytes);
+      if (wr == nullptr) return false;
+      bindRecv(wr);
+      w.send[me] = h.send;  // read on the root only
+      w.count = bytes;
+      noteAlgorithm("broadcast", w.mcRecv ? "window multimem" : "window push", n, bytes);
+      *out = cudaToVccl(launchBroadcastWindow(lc, w, h.root), "window broadcast launch");
+      return true;
+    }
     case Kind::ReduceScatter: {
       if (bytes <= lc.llMax) return false;
       const Window* ws = comm->findWindow(h.send, bytes * n);

@@ -48,6 +48,7 @@ cudaError_t launchAllReduceWindow(const LaunchCtx& lc, vcclDataType_t dt, int re
                                   bool viaSwitch);
 cudaError_t launchAllGatherWindow(const LaunchCtx& lc, const dev::WinArgs& w);
 cudaError_t launchAllToAllWindow(const LaunchCtx& lc, const dev::WinArgs& w);
+cudaError_t launchBroadcastWindow(const LaunchCtx& lc, const dev::WinArgs& w, int root);
 cudaError_t launchReduceScatterWindow(const LaunchCtx& lc, vcclDataType_t dt, int redKind, const dev::WinArgs& w,
                                       bool viaSwitch);
 // Single-rank helpers: dst = src * scale (float types) or plain copy.

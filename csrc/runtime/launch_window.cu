@@ -69,6 +69,17 @@ cudaError_t launchAllGatherWindow(const LaunchCtx& lc, const dev::WinArgs& w) {
   return cudaGetLastError();
 }
 
+cudaError_t launchBroadcastWindow(const LaunchCtx& lc, const dev::WinArgs& w, int root) {
+  const int g = gridFor(w.count, lc.nblocks);
+  dev::WinArgs v = w;
+  if (v.mcRecv != nullptr && (w.count % 16 != 0 || !aligned16(w.send[lc.dc.rank]) || !aligned16(w.mcRecv)))
+    v.mcRecv = nullptr;
+  // Every rank must pick the same kernel shape; only the root reads mcRecv,
+  // so the choice above matters on the root alone.
+  dev::broadcastWin<<<g, kThreads, 0, lc.stream>>>(lc.dc, v, root);
+  return cudaGetLastError();
+}
+
 cudaError_t launchAllToAllWindow(const LaunchCtx& lc, const dev::WinArgs& w) {
   const int g = gridFor(w.count * lc.dc.nranks, lc.nblocks);
   dev::allToAllWin<<<g, kThreads, 0, lc.stream>>>(lc.dc, w);

@@ -538,6 +538,20 @@ void windowTest(vcclComm_t c, int me, int n) {
   upload(A, vcclFloat32, per * n, 0);
   EXPECT_OK(vcclReduceScatter(A, local, per, vcclFloat32, vcclSum, c));
   checkDevice(local, vcclFloat32, per, "reducescatter", [&](size_t i) { return expect(vcclSum, n, me * per + i); });
+  // broadcast from the last rank into window B
+  if (me == n - 1) upload(local, vcclFloat32, per, 0);
+  EXPECT_OK(vcclBroadcast(local, B, per, vcclFloat32, n - 1, c));
+  {
+    std::vector<float> g(per), want(per);
+    cudaMemcpy(g.data(), B, per * 4, cudaMemcpyDeviceToHost);
+    fill(want.data(), vcclFloat32, n - 1, per);
+    for (size_t i = 0; i < per; i += 53)
+      if (!near(g[i], want[i], vcclFloat32)) {
+        std::fprintf(stderr, "FAIL window broadcast i=%zu\n", i);
+        gFail++;
+        break;
+      }
+  }
   // all-to-all into window B from window A (equal blocks): block q of rank p
   // lands in rank q's block p
   upload(A, vcclFloat32, per * n, 0);

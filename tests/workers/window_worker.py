@@ -52,6 +52,13 @@ def main():
     err = (out.float() - want).abs().max().item()
     assert err <= 0.05 * want.abs().max().item(), f"window reduce_scatter err {err}"
 
+    # broadcast from the last rank into the receive window
+    if rank == n - 1:
+        recv[:per].copy_(inputs(rank)[:per])
+    comm.broadcast(recv[:per], n - 1)  # in place
+    torch.cuda.synchronize()
+    assert torch.equal(recv[:per], inputs(n - 1)[:per]), "window broadcast"
+
     # all-to-all with equal blocks into the receive window
     comm.all_to_all(send[: per * n], recv[: per * n])
     torch.cuda.synchronize()
