@@ -8,7 +8,7 @@ Launch one process per GPU:
 
 --window adds a "vcclwin" column: the same vccl call on buffers inside
 registered windows (vcclMemAlloc memory mapped by every rank), which runs
-the zero-copy kernels (all-reduce, all-gather, reduce-scatter).  NCCL runs
+the zero-copy kernels (all-reduce, all-gather, reduce-scatter, broadcast).  NCCL runs
 on plain torch tensors in every column.
 
 Every number is device time from CUDA events on the launching stream,
@@ -172,7 +172,7 @@ def main() -> int:
                     recv = send.clone() if op == "broadcast" else torch.empty_like(send)
                 row = {"op": op, "dtype": dname, "bytes": count * es, "n": world}
                 variants = [(lib_, None) for lib_ in a.libs.split(",")]
-                if wins is not None and op != "broadcast":
+                if wins is not None:
                     variants.append(("vcclwin", None))
                 if op == "allreduce" and a.algos:
                     variants += [("vccl", algo) for algo in a.algos.split(",")]
