@@ -528,6 +528,9 @@ def test_window_api_without_device():
         assert ei.value.result == 5  # vcclInvalidUsage
         with pytest.raises(v.VcclError):
             comm.window_deregister(ctypes.c_void_p(0))
+        with pytest.raises(v.VcclError):
+            with comm.window(buf):
+                pass
         assert comm.WIN_NO_MULTICAST == 1
     finally:
         comm.destroy()

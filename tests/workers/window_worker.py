@@ -71,13 +71,12 @@ def main():
 
     # a tensor from PyTorch's own allocator (cudaMalloc): a window through CUDA IPC
     both = torch.empty(2 * count, dtype=torch.bfloat16, device="cuda")
-    wb = comm.window_register(both)
-    both[:count].copy_(inputs(rank))
-    comm.all_reduce(both[:count], both[count:])
-    torch.cuda.synchronize()
+    with comm.window(both):
+        both[:count].copy_(inputs(rank))
+        comm.all_reduce(both[:count], both[count:])
+        torch.cuda.synchronize()
     err = (both[count:].float() - total).abs().max().item()
     assert err <= 0.05 * total.abs().max().item(), f"cudaMalloc window all_reduce err {err}"
-    comm.window_deregister(wb)
 
     # data-parallel gradient buckets on one registered buffer
     from vkccl_b200.parallel import GradBuckets

@@ -522,6 +522,11 @@ class Communicator:
         """Collective: undo window_register (before the memory is freed)."""
         _check(lib().vcclCommWindowDeregister(self._comm, handle), "vcclCommWindowDeregister", self._comm)
 
+    def window(self, buf: Any, nbytes: Optional[int] = None, flags: int = 0) -> "_WindowScope":
+        """`with comm.window(t): ...` registers `t` for the block (collective on
+        entry and exit)."""
+        return _WindowScope(self, buf, nbytes, flags)
+
     def destroy(self) -> None:
         if self._comm:
             lib().vcclCommDestroy(self._comm)
@@ -532,6 +537,21 @@ class Communicator:
 
     def __exit__(self, *exc: Any) -> None:
         self.destroy()
+
+
+class _WindowScope:
+    def __init__(self, comm: "Communicator", buf: Any, nbytes: Optional[int], flags: int):
+        self.comm, self.buf, self.nbytes, self.flags = comm, buf, nbytes, flags
+        self.handle: Optional[ctypes.c_void_p] = None
+
+    def __enter__(self) -> ctypes.c_void_p:
+        self.handle = self.comm.window_register(self.buf, self.nbytes, self.flags)
+        return self.handle
+
+    def __exit__(self, *exc: Any) -> None:
+        if self.handle is not None:
+            self.comm.window_deregister(self.handle)
+            self.handle = None
 
 
 def init_all(ndev: int, devlist: Optional[Sequence[int]] = None) -> List[Communicator]:
