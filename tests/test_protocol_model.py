@@ -719,3 +719,50 @@ def test_model_detects_two_slot_pipe():
         return M.run(2, block_fn)
 
     assert any(two_slots(s) for s in range(100))
+
+
+# ---------------------------------------------------------------------------
+# Window collectives (csrc/kernels/window.cuh): each block publishes its
+# call's descriptor in its own ctrl slot, meets the peers (start barrier),
+# reads every peer's descriptor, moves data in place on the peers' buffers,
+# and meets them again (end barrier) before the kernel may end.
+# ---------------------------------------------------------------------------
+def run_window(n, blocks, calls, seed, end_barrier=True):
+    M = StagingModel(n, blocks, seed)
+    desc = {}                 # (rank, block) -> call number published
+    data = {}                 # (rank, block) -> call whose data the buffer holds / "reading"
+    errors = M.errors
+
+    def block_fn(r, b, k):
+        desc[(r, b)] = k
+        yield from M.barrier(r, b)
+        for q in range(n):
+            yield lambda: True
+            if desc.get((q, b)) != k:
+                errors.append(f"rank {r} block {b} call {k} read rank {q}'s descriptor of call {desc.get((q, b))}")
+        # write my piece of every rank's receive buffer, read every send buffer
+        for q in range(n):
+            yield lambda: True
+            if data.get(("send", q, b), k) not in (k,):
+                errors.append(f"rank {r} call {k} read rank {q}'s send buffer holding call {data.get(('send', q, b))}")
+        if end_barrier:
+            yield from M.barrier(r, b)
+        # after the kernel the rank's next call refills its send buffer
+        data[("send", r, b)] = k + 1
+
+    for r in range(n):
+        for b in range(blocks):
+            data[("send", r, b)] = 0
+    return M.run(calls, block_fn)
+
+
+@pytest.mark.parametrize("n,blocks", [(2, 1), (3, 2), (4, 3)])
+def test_window_protocol(n, blocks):
+    for seed in range(100):
+        assert run_window(n, blocks, calls=4, seed=seed) == []
+
+
+def test_model_detects_window_without_end_barrier():
+    """Without the end barrier a rank refills its send buffer for the next
+    call while a peer still reads it."""
+    assert any(run_window(3, 1, 4, seed=s, end_barrier=False) for s in range(200))
