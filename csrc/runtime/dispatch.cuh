@@ -33,6 +33,41 @@
       return cudaErrorInvalidValue;                                   \
   }
 
+// (datatype, reduction) pairs the switch can reduce with multimem.ld_reduce
+// (dev::HasMultimem): binds T and K for the body; anything else returns
+// cudaErrorInvalidValue.  Used where nvlsSupports() has already been checked.
+#define VCCL_DISPATCH_MULTIMEM(dt, op, ...)                              \
+  switch (dt) {                                                          \
+    case vcclFloat32: {                                                  \
+      using T = float;                                                   \
+      constexpr int K = vccl::dev::kSum;                                 \
+      if ((op) != K) return cudaErrorInvalidValue;                       \
+      __VA_ARGS__;                                                       \
+    } break;                                                             \
+    case vcclBfloat16: {                                                 \
+      using T = __nv_bfloat16;                                           \
+      VCCL_DISPATCH_OP(op, {                                             \
+        if constexpr (vccl::dev::HasMultimem<T, K>::value) {             \
+          __VA_ARGS__;                                                   \
+        } else {                                                         \
+          return cudaErrorInvalidValue;                                  \
+        }                                                                \
+      })                                                                 \
+    } break;                                                             \
+    case vcclFloat16: {                                                  \
+      using T = __half;                                                  \
+      VCCL_DISPATCH_OP(op, {                                             \
+        if constexpr (vccl::dev::HasMultimem<T, K>::value) {             \
+          __VA_ARGS__;                                                   \
+        } else {                                                         \
+          return cudaErrorInvalidValue;                                  \
+        }                                                                \
+      })                                                                 \
+    } break;                                                             \
+    default:                                                             \
+      return cudaErrorInvalidValue;                                      \
+  }
+
 #define VCCL_OP_CASE(v, ...)    \
   case v: {                     \
     constexpr int K = v;        \

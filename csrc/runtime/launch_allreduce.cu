@@ -67,25 +67,9 @@ cudaError_t launchAllReduce(const LaunchCtx& lc, ArAlgo algo, vcclDataType_t dt,
     if (!lc.nvls || !nvlsSupports(dt, redKind) || a.root >= 0) return cudaErrorInvalidValue;
     const size_t roundBytes = (lc.dc.dataBytes - 16 * dev::kMaxRanks) / 16 * 16;
     const int g = gridFor(bytes / n, lc.nblocks);
-    switch (dt) {
-      case vcclFloat32:
-        dev::allReduceNvls<float, dev::kSum><<<g, kThreads, 0, lc.stream>>>(lc.dc, a, roundBytes);
-        break;
-      case vcclBfloat16:
-        VCCL_DISPATCH_OP(redKind, {
-          if constexpr (dev::HasMultimem<__nv_bfloat16, K>::value)
-            dev::allReduceNvls<__nv_bfloat16, K><<<g, kThreads, 0, lc.stream>>>(lc.dc, a, roundBytes);
-        })
-        break;
-      case vcclFloat16:
-        VCCL_DISPATCH_OP(redKind, {
-          if constexpr (dev::HasMultimem<__half, K>::value)
-            dev::allReduceNvls<__half, K><<<g, kThreads, 0, lc.stream>>>(lc.dc, a, roundBytes);
-        })
-        break;
-      default:
-        return cudaErrorInvalidValue;
-    }
+    VCCL_DISPATCH_MULTIMEM(dt, redKind, {
+      dev::allReduceNvls<T, K><<<g, kThreads, 0, lc.stream>>>(lc.dc, a, roundBytes);
+    })
     return cudaGetLastError();
   }
   if (algo == ArAlgo::NvlsPipe) {
@@ -93,25 +77,9 @@ cudaError_t launchAllReduce(const LaunchCtx& lc, ArAlgo algo, vcclDataType_t dt,
     const size_t cb = nvlsPipeChunk(bytes, n, lc.nvlsPieces, lc.dc.dataBytes);
     const size_t slotBytes = nvlsPipeSlotBytes(lc.dc.dataBytes);
     const int g = gridFor(bytes / n, lc.nblocks);
-    switch (dt) {
-      case vcclFloat32:
-        dev::allReduceNvlsPipe<float, dev::kSum><<<g, dev::kPipeThreads, 0, lc.stream>>>(lc.dc, a, cb, slotBytes);
-        break;
-      case vcclBfloat16:
-        VCCL_DISPATCH_OP(redKind, {
-          if constexpr (dev::HasMultimem<__nv_bfloat16, K>::value)
-            dev::allReduceNvlsPipe<__nv_bfloat16, K><<<g, dev::kPipeThreads, 0, lc.stream>>>(lc.dc, a, cb, slotBytes);
-        })
-        break;
-      case vcclFloat16:
-        VCCL_DISPATCH_OP(redKind, {
-          if constexpr (dev::HasMultimem<__half, K>::value)
-            dev::allReduceNvlsPipe<__half, K><<<g, dev::kPipeThreads, 0, lc.stream>>>(lc.dc, a, cb, slotBytes);
-        })
-        break;
-      default:
-        return cudaErrorInvalidValue;
-    }
+    VCCL_DISPATCH_MULTIMEM(dt, redKind, {
+      dev::allReduceNvlsPipe<T, K><<<g, dev::kPipeThreads, 0, lc.stream>>>(lc.dc, a, cb, slotBytes);
+    })
     return cudaGetLastError();
   }
   // Two-shot (all-reduce, or reduce when a.root >= 0).

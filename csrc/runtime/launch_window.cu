@@ -24,25 +24,7 @@ cudaError_t launchAllReduceWindow(const LaunchCtx& lc, vcclDataType_t dt, int re
     if (w.mcSend == nullptr || w.mcRecv == nullptr || w.premul || !nvlsSupports(dt, redKind) || bytes % 16 != 0 ||
         !aligned16(w.mcSend) || !aligned16(w.mcRecv))
       return cudaErrorInvalidValue;
-    switch (dt) {
-      case vcclFloat32:
-        dev::allReduceWinNvls<float, dev::kSum><<<g, kThreads, 0, lc.stream>>>(lc.dc, w);
-        break;
-      case vcclBfloat16:
-        VCCL_DISPATCH_OP(redKind, {
-          if constexpr (dev::HasMultimem<__nv_bfloat16, K>::value)
-            dev::allReduceWinNvls<__nv_bfloat16, K><<<g, kThreads, 0, lc.stream>>>(lc.dc, w);
-        })
-        break;
-      case vcclFloat16:
-        VCCL_DISPATCH_OP(redKind, {
-          if constexpr (dev::HasMultimem<__half, K>::value)
-            dev::allReduceWinNvls<__half, K><<<g, kThreads, 0, lc.stream>>>(lc.dc, w);
-        })
-        break;
-      default:
-        return cudaErrorInvalidValue;
-    }
+    VCCL_DISPATCH_MULTIMEM(dt, redKind, { dev::allReduceWinNvls<T, K><<<g, kThreads, 0, lc.stream>>>(lc.dc, w); })
     return cudaGetLastError();
   }
   // Vector path when every rank's buffers sit on 16-byte boundaries (the
