@@ -61,7 +61,56 @@ struct EpiPushRS {
   }
 };
 
-struct RsHooks : gemm::NoHooks {
+// Same pushes through the TMA (VCCL_RS_TMA=1): each epilogue warp stages a
+// 32-row x 64-column bf16 box in its row stage (whose XOR layout is the
+// TMA's 128-byte swizzle) and one lane stores it into the owner's slot with
+// cp.async.bulk.tensor, so the warp moves on while the copy engine writes
+// over NVLink.  One tensor map per owner (its slot for this source rank,
+// [rowsPerRank, N], box 64 x 32); plain stores, no multicast.  Needs
+// 64-column passes (tile width / epilogue groups >= 64) and rowsPerRank a
+// multiple of 32 (a warp's 32 rows then have one owner).
+struct EpiPushRSTma {
+  CUtensorMap map[dev::kMaxRanks];
+  int rowsPerRank;
+  template <int SPAN>
+  __device__ __forceinline__ void operator()(uint32_t tmemAcc, const gemm::TileInfo& ti, const gemm::GemmShape& s,
+                                             int laneRow, int cBegin, uint4* st) const {
+    // launchGemm instantiates every tile width; the host only picks this
+    // epilogue for widths whose per-group span is a multiple of 64.
+    if constexpr (SPAN % 64 == 0) store<SPAN>(tmemAcc, ti, s, laneRow, cBegin, st);
+  }
+  template <int SPAN>
+  __device__ __forceinline__ void store(uint32_t tmemAcc, const gemm::TileInfo& ti, const gemm::GemmShape& s,
+                                        int laneRow, int cBegin, uint4* st) const {
+    const int lane = laneRow & 31;
+    const int warpRow0 = ti.row0 + (laneRow & ~31);
+    if (warpRow0 >= s.M) return;  // M is a multiple of 32 here: a warp's rows are all valid or all past M
+    const int owner = warpRow0 / rowsPerRank;
+    const int slotRow = warpRow0 - owner * rowsPerRank;
+#pragma unroll 1
+    for (int c = cBegin; c < cBegin + SPAN; c += 64) {
+      uint32_t r[64];
+#pragma unroll
+      for (int i = 0; i < 4; i++) sm100::tmemLoad16p(tmemAcc + c + 16 * i, r + 16 * i);
+      sm100::tmemLoadWait();
+      if (lane == 0) sm100::bulkWaitRead0();  // the previous box has left the stage
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 8; j++) gemm::stagePut<8>(st, lane, j, gemm::packChunk(r + 8 * j));
+      sm100::fenceProxyAsyncShared();
+      __syncwarp();
+      if (lane == 0) {
+        sm100::tmaStore2d(&map[owner], st, ti.col0 + c, slotRow);
+        sm100::bulkCommit();
+      }
+    }
+    if (lane == 0) sm100::bulkWaitRead0();  // the stage is free when the tile is handed back
+    __syncwarp();
+  }
+};
+
+template <bool kTmaStores>
+struct RsHooksT : gemm::NoHooks {
   static constexpr int kEpiGroups = kRsEpiGroups;
   DevComm c;
   // Every rank's reduction must have consumed the previous call's pushes
@@ -81,6 +130,14 @@ struct RsHooks : gemm::NoHooks {
   // Each CTA makes its pushes visible system-wide and counts itself locally;
   // the last CTA of the call tells every rank once (done[me] += 1).
   __device__ __forceinline__ void afterTiles(uint32_t*, volatile int*) const {
+    if constexpr (kTmaStores) {
+      // this warp's TMA stores have written their data, ordered before the release below
+      if ((threadIdx.x & 31) == 0) {
+        sm100::bulkWaitAll0();
+        sm100::fenceProxyAsyncGlobal();
+      }
+      __syncwarp();
+    }
     epilogueBarrier();
     if (threadIdx.x == 64) {
       uint32_t* calls = dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsGemmCallsOff) + blockIdx.x;
@@ -96,6 +153,8 @@ struct RsHooks : gemm::NoHooks {
     }
   }
 };
+
+using RsHooks = RsHooksT<false>;
 
 // out[rowsPerRank, N] = sum over sources of my slots.
 __global__ void __launch_bounds__(512) rsReduce(DevComm c, char* out, size_t elems, size_t slotBytes) {
@@ -204,13 +263,29 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
   }
   const int ctas = gemm::smCount();
   if (ctas > dev::kMaxFusedCtas) return vcclInternalError;
-  fused::EpiPushRS epi;
-  for (int q = 0; q < dev::kMaxRanks; q++) epi.dest[q] = q < n ? dc.fused[q] + comm->rank * slotBytes : nullptr;
-  epi.rowsPerRank = rowsPerRank;
-  epi.ldn = N;
-  fused::RsHooks hooks;
-  hooks.c = dc;
-  cudaError_t e = gemm::launchGemm(A, W, M, N, K, epi, hooks, s, bnEnv, -ctas);
+  cudaError_t e = cudaSuccess;
+  const int bn = bnEnv > 0 ? bnEnv : gemm::pickBN(M, N);
+  bool tma = gemm::envLongGemm("VCCL_RS_TMA") != 0 && bn / fused::kRsEpiGroups >= 64 && rowsPerRank % 32 == 0;
+  if (tma) {
+    fused::EpiPushRSTma epi{};
+    epi.rowsPerRank = rowsPerRank;
+    for (int q = 0; q < n && tma; q++)
+      tma = gemm::makeMapKMajor(&epi.map[q], dc.fused[q] + comm->rank * slotBytes, rowsPerRank, N, 32);
+    if (tma) {
+      fused::RsHooksT<true> hooks;
+      hooks.c = dc;
+      e = gemm::launchGemm(A, W, M, N, K, epi, hooks, s, bn, -ctas);
+    }
+  }
+  if (!tma) {
+    fused::EpiPushRS epi;
+    for (int q = 0; q < dev::kMaxRanks; q++) epi.dest[q] = q < n ? dc.fused[q] + comm->rank * slotBytes : nullptr;
+    epi.rowsPerRank = rowsPerRank;
+    epi.ldn = N;
+    fused::RsHooks hooks;
+    hooks.c = dc;
+    e = gemm::launchGemm(A, W, M, N, K, epi, hooks, s, bnEnv, -ctas);
+  }
   if (e != cudaSuccess) {
     VERR("vcclGemmReduceScatter GEMM launch: %s", cudaGetErrorString(e));
     return vcclInvalidArgument;

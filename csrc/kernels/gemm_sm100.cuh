@@ -399,7 +399,7 @@ struct NoHooks {
 template <int BN, int STAGES, typename Epi, typename Hooks = NoHooks>
 __global__ void __launch_bounds__(ctaThreads<Hooks>(), 1)
     gemmKernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, GemmShape s,
-               Epi epi, Hooks hooks, int* errorFlag) {
+               const __grid_constant__ Epi epi, Hooks hooks, int* errorFlag) {
   constexpr int kEpiWarps = 4 * Hooks::kEpiGroups;
   constexpr int kSpan = BN / Hooks::kEpiGroups;
   using L = Smem<BN, STAGES, kEpiWarps>;

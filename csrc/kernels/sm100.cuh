@@ -86,6 +86,27 @@ __device__ __forceinline__ void tmaLoad2d(void* smemDst, const CUtensorMap* map,
       : "memory");
 }
 
+// TMA store of a box from shared memory (this CTA's) to global memory, in
+// the calling thread's bulk async-group.  The tensor map may describe a
+// peer's memory mapped into this address space (a plain store, no multicast).
+__device__ __forceinline__ void tmaStore2d(const CUtensorMap* map, const void* smemSrc, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smemAddr(smemSrc)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulkCommit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Every committed bulk store of this thread has finished reading shared memory.
+__device__ __forceinline__ void bulkWaitRead0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Every committed bulk store of this thread has completed its writes.
+__device__ __forceinline__ void bulkWaitAll0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Generic-proxy shared-memory writes become visible to the async proxy (TMA).
+__device__ __forceinline__ void fenceProxyAsyncShared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Async-proxy global writes (TMA stores) are ordered with later generic accesses.
+__device__ __forceinline__ void fenceProxyAsyncGlobal() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 // ---- TMEM ----------------------------------------------------------------------
 // Warp-wide.  Writes the allocated TMEM address to *dstSmem.
 __device__ __forceinline__ void tmemAlloc(uint32_t* dstSmem, uint32_t ncols) {
