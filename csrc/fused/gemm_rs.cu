@@ -88,7 +88,7 @@ struct EpiPushRSTma {
     const int owner = warpRow0 / rowsPerRank;
     const int slotRow = warpRow0 - owner * rowsPerRank;
 #pragma unroll 1
-    for (int c = cBegin; c < cBegin + SPAN; c += 64) {
+    for (int c = cBegin; c < cBegin + SPAN && ti.col0 + c < s.N; c += 64) {  // no store starts past N
       uint32_t r[64];
 #pragma unroll
       for (int i = 0; i < 4; i++) sm100::tmemLoad16p(tmemAcc + c + 16 * i, r + 16 * i);
