@@ -11,8 +11,9 @@
 // node supports NVLS the windows are also bound to one multicast object.
 // A buffer from plain cudaMalloc (a PyTorch tensor, say) goes through CUDA
 // IPC instead: its allocation's IPC handle is all-gathered and every rank
-// opens the peers' handles; such windows have no multicast binding and
-// need one process per rank.
+// opens the peers' handles (ranks of the same process, from
+// vcclCommInitAll, use each other's pointers directly with peer access
+// enabled); such windows have no multicast binding.
 // Collectives whose buffers lie in windows then run the zero-copy kernels of
 // csrc/kernels/window.cuh.
 #include <unistd.h>
@@ -42,6 +43,9 @@ struct WinInfo {
   uint64_t allocBytes;  // the rank's allocation
   uint32_t kind;        // WinKind
   int32_t pid;
+  int32_t device;       // CUDA device of the rank
+  int32_t pad;
+  uint64_t rawBase;     // kWinIpc: the allocation's address in its own process
   cudaIpcMemHandle_t ipc;  // kWinIpc: handle of the allocation
 };
 
@@ -180,6 +184,7 @@ extern "C" vcclResult_t vcclCommWindowRegister(vcclComm_t comm, void* buff, size
   memset(&mine, 0, sizeof(mine));
   mine.size = size;
   mine.pid = static_cast<int32_t>(getpid());
+  mine.device = ds->device;
   if (findDeviceAllocation(buff, size, &allocBase, &allocBytes, &h)) {
     mine.kind = kWinVmm;
   } else {
@@ -190,6 +195,7 @@ extern "C" vcclResult_t vcclCommWindowRegister(vcclComm_t comm, void* buff, size
         reinterpret_cast<CUdeviceptr>(buff) + size <= base + bytes &&
         cudaIpcGetMemHandle(&mine.ipc, reinterpret_cast<void*>(base)) == cudaSuccess) {
       mine.kind = kWinIpc;
+      mine.rawBase = static_cast<uint64_t>(base);
       allocBase = reinterpret_cast<void*>(base);
       allocBytes = bytes;
     }
@@ -213,10 +219,6 @@ extern "C" vcclResult_t vcclCommWindowRegister(vcclComm_t comm, void* buff, size
            static_cast<size_t>(info[p].size), p, size);
       return vcclInvalidArgument;
     }
-    if (info[p].kind == kWinIpc && p != me && info[p].pid == mine.pid) {
-      VERR("vcclCommWindowRegister: cudaMalloc windows need one process per rank (use vcclMemAlloc memory)");
-      return vcclInvalidArgument;
-    }
   }
 
   auto w = std::make_unique<Window>();
@@ -235,6 +237,14 @@ extern "C" vcclResult_t vcclCommWindowRegister(vcclComm_t comm, void* buff, size
     bool ok = true;
     for (int p = 0; p < n && ok; p++) {
       if (p == me) continue;
+      if (info[p].pid == mine.pid) {
+        // Same process (vcclCommInitAll): the peer's pointer is valid here
+        // once this device may access the peer's.
+        const cudaError_t pe = cudaDeviceEnablePeerAccess(info[p].device, 0);
+        ok = pe == cudaSuccess || pe == cudaErrorPeerAccessAlreadyEnabled;
+        if (ok) w->peer[p] = reinterpret_cast<char*>(info[p].rawBase) + info[p].offset;
+        continue;
+      }
       ok = cudaIpcOpenMemHandle(&w->ipcBase[p], info[p].ipc, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
       if (ok) w->peer[p] = static_cast<char*>(w->ipcBase[p]) + info[p].offset;
     }

@@ -26,6 +26,7 @@
 #include <cstring>
 #include <functional>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "vccl.h"
@@ -775,6 +776,52 @@ int initAll(int ndev) {
   return bad ? 1 : 0;
 }
 
+// Windows between ranks of one process (vcclCommInitAll): a cudaMalloc
+// buffer per device, registered and all-reduced from one thread per rank
+// (registration is collective, so every rank must be inside the call).
+int initAllWindow(int ndev) {
+  std::vector<vcclComm_t> comms(ndev, nullptr);
+  if (vcclCommInitAll(comms.data(), ndev, nullptr) != vcclSuccess) {
+    std::printf("init-all window: FAIL (init)\n");
+    return 1;
+  }
+  const size_t cnt = (2u << 20) + 3;
+  std::vector<int> bad(ndev, 0);
+  std::vector<std::thread> th;
+  for (int d = 0; d < ndev; d++)
+    th.emplace_back([&, d]() {
+      cudaSetDevice(d);
+      char* buf = nullptr;
+      const size_t ro = (cnt * 4 + 4095) / 4096 * 4096;
+      cudaMalloc(&buf, ro + cnt * 4);
+      std::vector<float> h(cnt);
+      fill(h.data(), vcclFloat32, d, cnt);
+      cudaMemcpy(buf, h.data(), cnt * 4, cudaMemcpyHostToDevice);
+      vcclWindow_t w = nullptr;
+      if (vcclCommWindowRegister(comms[d], buf, ro + cnt * 4, &w, 0) != vcclSuccess) {
+        bad[d]++;
+      } else {
+        if (vcclAllReduce(buf, buf + ro, cnt, vcclFloat32, vcclSum, comms[d]) != vcclSuccess) bad[d]++;
+        cudaMemcpy(h.data(), buf + ro, cnt * 4, cudaMemcpyDeviceToHost);
+        for (size_t i = 0; i < cnt; i += 31)
+          if (!near(h[i], expect(vcclSum, ndev, i), vcclFloat32)) {
+            bad[d]++;
+            break;
+          }
+        if (vcclCommWindowDeregister(comms[d], w) != vcclSuccess) bad[d]++;
+      }
+      cudaFree(buf);
+    });
+  for (auto& t : th) t.join();
+  int total = 0;
+  for (int d = 0; d < ndev; d++) {
+    total += bad[d];
+    vcclCommDestroy(comms[d]);
+  }
+  std::printf("init-all window allreduce (%d devices): %s\n", ndev, total ? "FAIL" : "OK");
+  return total ? 1 : 0;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -808,6 +855,13 @@ int main(int argc, char** argv) {
     if (maxRanks >= 2) fails += forkRanks(2, true);
     if (maxRanks > 2) fails += forkRanks(maxRanks, true);
     if (maxRanks == 1) fails += forkRanks(1, true);
+    if (maxRanks >= 2) {
+      pid_t p = fork();
+      if (p == 0) _exit(initAllWindow(std::min(maxRanks, 4)));
+      int st = 0;
+      waitpid(p, &st, 0);
+      if (!WIFEXITED(st) || WEXITSTATUS(st) != 0) fails++;
+    }
     if (fails == 0) std::printf("all tests passed\n");
     return fails ? 1 : 0;
   }

@@ -259,8 +259,8 @@ vcclResult_t vcclCommRegisterDmaBuf(vcclComm_t comm, int fd, uint64_t offset,
 /* ── Windows (an addition: zero-copy collectives) ───────────────────────
  * Collective: every rank calls it, in the same order, with a buffer of the
  * same `size` that lies inside a vcclMemAlloc device allocation (or, on
- * every rank alike, inside plain cudaMalloc memory: opened by CUDA IPC, one
- * process per rank, no multicast).  Every rank then maps every peer's
+ * every rank alike, inside plain cudaMalloc memory: opened by CUDA IPC, or
+ * used directly between ranks of one process, no multicast).  Every rank then maps every peer's
  * buffer, and for vcclMemAlloc memory on a node that supports NVLS the
  * buffers are also bound to one multicast object (unless flags has
  * VCCL_WIN_NO_MULTICAST).  All-reduce with both buffers in windows,
