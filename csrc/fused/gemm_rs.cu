@@ -44,20 +44,40 @@ __device__ __forceinline__ void epilogueBarrier() {
   asm volatile("bar.sync 1, %0;" ::"n"(128 * kRsEpiGroups) : "memory");
 }
 
+// Optional event trace (VCCL_FUSED_TRACE=1), in the per-CTA slots the
+// all-gather + GEMM trace leaves free (%globaltimer ns): 20 GEMM epilogue
+// start, 21 previous call's slots freed by every rank, 22 sum over tiles of
+// one epilogue warp's push time, 23 tiles pushed, 24 every tile pushed,
+// 25 done signalled; reduce blocks: 26 every source's pushes arrived,
+// 27 reduction written.
+constexpr int kRsTraceStart = 20, kRsTraceFreed = 21, kRsTracePushNs = 22, kRsTraceTiles = 23,
+              kRsTraceTilesDone = 24, kRsTraceSignalled = 25, kRsTraceArrived = 26, kRsTraceReduced = 27;
+__device__ __forceinline__ void rsMark(unsigned long long* trace, int slot) {
+  if (trace != nullptr) trace[blockIdx.x * dev::kFusedTraceSlots + slot] = dev::globalTimerNs();
+}
+
 // Each tile row goes to its owner's slot; rows leave the SM as contiguous
 // 128-byte segments (see gemm::storeAccRows).
 struct EpiPushRS {
   char* dest[dev::kMaxRanks];  // owner q's slot for this source rank
   int rowsPerRank;
   int ldn;  // N
+  unsigned long long* trace;  // optional event trace (one warp's push time per tile)
   template <int SPAN>
   __device__ __forceinline__ void operator()(uint32_t tmemAcc, const gemm::TileInfo& ti, const gemm::GemmShape& s,
                                              int laneRow, int cBegin, uint4* st) const {
+    const bool timed = trace != nullptr && laneRow == 0 && cBegin == 0;
+    const unsigned long long t0 = timed ? dev::globalTimerNs() : 0ull;
     const size_t pitch = static_cast<size_t>(ldn) * 2;
     gemm::storeAccRows<SPAN>(tmemAcc, ti, s, laneRow, cBegin, st, [&](int row) {
       const int owner = row / rowsPerRank;
       return dest[owner] + static_cast<size_t>(row - owner * rowsPerRank) * pitch;
     });
+    if (timed) {
+      unsigned long long* t = trace + blockIdx.x * dev::kFusedTraceSlots;
+      t[kRsTracePushNs] += dev::globalTimerNs() - t0;
+      t[kRsTraceTiles] += 1;
+    }
   }
 };
 
@@ -72,6 +92,7 @@ struct EpiPushRS {
 struct EpiPushRSTma {
   CUtensorMap map[dev::kMaxRanks];
   int rowsPerRank;
+  unsigned long long* trace;  // optional event trace (one warp's staging time per tile)
   template <int SPAN>
   __device__ __forceinline__ void operator()(uint32_t tmemAcc, const gemm::TileInfo& ti, const gemm::GemmShape& s,
                                              int laneRow, int cBegin, uint4* st) const {
@@ -85,6 +106,8 @@ struct EpiPushRSTma {
     const int lane = laneRow & 31;
     const int warpRow0 = ti.row0 + (laneRow & ~31);
     if (warpRow0 >= s.M) return;  // M is a multiple of 32 here: a warp's rows are all valid or all past M
+    const bool timed = trace != nullptr && laneRow == 0 && cBegin == 0;
+    const unsigned long long t0 = timed ? dev::globalTimerNs() : 0ull;
     const int owner = warpRow0 / rowsPerRank;
     const int slotRow = warpRow0 - owner * rowsPerRank;
 #pragma unroll 1
@@ -106,6 +129,11 @@ struct EpiPushRSTma {
     }
     if (lane == 0) sm100::bulkWaitRead0();  // the stage is free when the tile is handed back
     __syncwarp();
+    if (timed) {
+      unsigned long long* t = trace + blockIdx.x * dev::kFusedTraceSlots;
+      t[kRsTracePushNs] += dev::globalTimerNs() - t0;
+      t[kRsTraceTiles] += 1;
+    }
   }
 };
 
@@ -113,16 +141,24 @@ template <bool kTmaStores>
 struct RsHooksT : gemm::NoHooks {
   static constexpr int kEpiGroups = kRsEpiGroups;
   DevComm c;
+  unsigned long long* trace;  // optional event trace
   // Every rank's reduction must have consumed the previous call's pushes
   // (free[q] counts calls rank q has finished reducing).
   __device__ __forceinline__ bool beforeTiles(uint32_t*, volatile int* abortFlag) const {
     __shared__ int sFail;
     if (threadIdx.x == 64) {
       sFail = 0;
+      if (trace != nullptr) {
+        unsigned long long* t = trace + blockIdx.x * dev::kFusedTraceSlots;
+        t[kRsTracePushNs] = 0;
+        t[kRsTraceTiles] = 0;
+      }
+      rsMark(trace, kRsTraceStart);
       const uint32_t k = dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsGemmCallsOff)[blockIdx.x];
       const uint32_t* freeCnt = dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsFreeOff);
       for (int q = 0; q < c.nranks; q++)
         if (!dev::waitAcquire(c, freeCnt + q, k, dev::kWhereFused, 100 + q, 64)) sFail = 1;
+      rsMark(trace, kRsTraceFreed);
     }
     epilogueBarrier();
     return sFail == 0 && !*abortFlag;
@@ -140,6 +176,7 @@ struct RsHooksT : gemm::NoHooks {
     }
     epilogueBarrier();
     if (threadIdx.x == 64) {
+      rsMark(trace, kRsTraceTilesDone);
       uint32_t* calls = dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsGemmCallsOff) + blockIdx.x;
       const uint32_t k = *calls;
       dev::fenceSys();
@@ -150,6 +187,7 @@ struct RsHooksT : gemm::NoHooks {
           redAddReleaseSys(dev::ctrlAt<uint32_t>(c, q, dev::kRsDoneOff) + c.rank, 1u);
       }
       *calls = k + 1u;
+      rsMark(trace, kRsTraceSignalled);
     }
   }
 };
@@ -157,7 +195,8 @@ struct RsHooksT : gemm::NoHooks {
 using RsHooks = RsHooksT<false>;
 
 // out[rowsPerRank, N] = sum over sources of my slots.
-__global__ void __launch_bounds__(512) rsReduce(DevComm c, char* out, size_t elems, size_t slotBytes) {
+__global__ void __launch_bounds__(512) rsReduce(DevComm c, char* out, size_t elems, size_t slotBytes,
+                                                unsigned long long* trace) {
   __shared__ uint32_t sK;
   __shared__ int sFail;
   const int n = c.nranks, me = c.rank;
@@ -173,6 +212,7 @@ __global__ void __launch_bounds__(512) rsReduce(DevComm c, char* out, size_t ele
   }
   __syncthreads();
   if (sFail) return;
+  if (threadIdx.x == 0) rsMark(trace, kRsTraceArrived);
   size_t lo, hi;
   dev::blockRange(elems, gridDim.x, blockIdx.x, 8, &lo, &hi);
   if (lo < hi) {
@@ -190,6 +230,7 @@ __global__ void __launch_bounds__(512) rsReduce(DevComm c, char* out, size_t ele
     if (old + 1u == (k + 1u) * gridDim.x)
       for (int q = 0; q < n; q++) redAddReleaseSys(dev::ctrlAt<uint32_t>(c, q, dev::kRsFreeOff) + me, 1u);
     dev::ctrlAt<uint32_t>(c, me, dev::kRsReduceCallsOff)[blockIdx.x] = k + 1u;
+    rsMark(trace, kRsTraceReduced);
   }
 }
 
@@ -269,11 +310,13 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
   if (tma) {
     fused::EpiPushRSTma epi{};
     epi.rowsPerRank = rowsPerRank;
+    epi.trace = comm->dev->fusedTrace;
     for (int q = 0; q < n && tma; q++)
       tma = gemm::makeMapKMajor(&epi.map[q], dc.fused[q] + comm->rank * slotBytes, rowsPerRank, N, 32);
     if (tma) {
       fused::RsHooksT<true> hooks;
       hooks.c = dc;
+      hooks.trace = comm->dev->fusedTrace;
       e = gemm::launchGemm(A, W, M, N, K, epi, hooks, s, bn, -ctas);
     }
   }
@@ -282,16 +325,18 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
     for (int q = 0; q < dev::kMaxRanks; q++) epi.dest[q] = q < n ? dc.fused[q] + comm->rank * slotBytes : nullptr;
     epi.rowsPerRank = rowsPerRank;
     epi.ldn = N;
+    epi.trace = comm->dev->fusedTrace;
     fused::RsHooks hooks;
     hooks.c = dc;
+    hooks.trace = comm->dev->fusedTrace;
     e = gemm::launchGemm(A, W, M, N, K, epi, hooks, s, bnEnv, -ctas);
   }
   if (e != cudaSuccess) {
     VERR("vcclGemmReduceScatter GEMM launch: %s", cudaGetErrorString(e));
     return vcclInvalidArgument;
   }
-  fused::rsReduce<<<dev::kFusedReduceBlocks, 512, 0, s>>>(dc, static_cast<char*>(out),
-                                                          static_cast<size_t>(rowsPerRank) * N, slotBytes);
+  fused::rsReduce<<<dev::kFusedReduceBlocks, 512, 0, s>>>(
+      dc, static_cast<char*>(out), static_cast<size_t>(rowsPerRank) * N, slotBytes, comm->dev->fusedTrace);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     VERR("vcclGemmReduceScatter reduce launch: %s", cudaGetErrorString(e));

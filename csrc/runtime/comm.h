@@ -61,7 +61,7 @@ struct DeviceState {
   size_t llAgMaxBytes = 0;         // LL threshold of all-gather (per-rank payload)
   int llBlocks = 64;               // grid of every LL kernel, a multiple of 8
   int fusedSmallRows = 512;        // fused TP calls up to this many rows run unfused
-  unsigned long long* fusedTrace = nullptr;  // per-CTA event times of the last AG+GEMM (VCCL_FUSED_TRACE=1)
+  unsigned long long* fusedTrace = nullptr;  // per-CTA event times of the fused kernels (VCCL_FUSED_TRACE=1)
   std::vector<TuningRule> tuning;  // measured algorithm table (VCCL_TUNING_FILE)
   size_t ll2MaxBytes = 0;          // two-hop LL all-reduce threshold
   size_t nvlsPipeMin = 0;          // pipelined NVLS all-reduce from this size (0: only when asked for)

@@ -95,10 +95,11 @@ extern "C" vcclResult_t vcclxBarrierBench(vcclComm_t comm, int iters, int nblock
   return comm->pollDeviceStatus();
 }
 
-// Copy the optional all-gather + GEMM event trace of the last call
-// (VCCL_FUSED_TRACE=1 at communicator creation): *ctas rows of
-// kFusedTraceSlots %globaltimer values (ns) per CTA; see AgHooks::trace
-// for the slot meanings.  Synchronises the device.
+// Copy the optional fused-kernel event trace (VCCL_FUSED_TRACE=1 at
+// communicator creation): *ctas rows of kFusedTraceSlots %globaltimer
+// values (ns) per CTA, slots 0-18 from the last all-gather + GEMM (see
+// AgHooks::trace) and 20-27 from the last GEMM + reduce-scatter (see
+// fused/gemm_rs.cu).  Synchronises the device.
 extern "C" vcclResult_t vcclxFusedTrace(vcclComm_t comm, unsigned long long* out, int* ctas) {
   if (comm == nullptr || out == nullptr || ctas == nullptr || !comm->dev) return vcclInvalidArgument;
   if (comm->dev->fusedTrace == nullptr) return vcclInvalidUsage;

@@ -562,3 +562,15 @@ def test_grad_buckets_single_rank_host():
         gb.close()
     finally:
         comm.destroy()
+
+
+def test_rs_trace_summary():
+    """The GEMM + reduce-scatter trace reader on a synthetic trace."""
+    from vkccl_b200.bench.rs_trace import summarise
+
+    t = np.zeros((148, 32), dtype=np.uint64)
+    t[:, 20], t[:, 21], t[:, 22], t[:, 23], t[:, 24], t[:, 25] = 1000, 3000, 50000, 7, 200000, 201000
+    t[:64, 26], t[:64, 27] = 205000, 215000
+    s = summarise(t)
+    assert s["freed_wait_us"] == 2.0 and s["tiles_us"] == 197.0 and s["tiles_per_cta"] == 7.0
+    assert abs(s["push_per_tile_us"] - 50 / 7) < 0.01 and s["reduce_us"] == 10.0 and s["gemm_end_us"] == 200.0
