@@ -47,8 +47,29 @@ int smCount() {
   return n;
 }
 
+int pickBNWaves(int M, int N, int sms) {
+  const int tm = (M + kBM - 1) / kBM;
+  double best = 0.0;
+  int bestBn = 256;
+  for (int bn : {256, 128, 64, 32}) {
+    const int tiles = tm * ((N + bn - 1) / bn);
+    const int waves = (tiles + sms - 1) / sms;
+    // A narrower tile re-reads its A rows once more per column tile and
+    // runs shorter MMA chains; charge it a little per halving.
+    const double charge = bn >= 256 ? 1.0 : bn == 128 ? 1.05 : bn == 64 ? 1.15 : 1.35;
+    const double cost = static_cast<double>(waves) * bn * charge;
+    if (bn == 256 || cost < best - 1e-9) {
+      best = cost;
+      bestBn = bn;
+    }
+  }
+  return bestBn;
+}
+
 int pickBN(int M, int N) {
   const int sms = smCount();
+  static const bool byWaves = envLongGemm("VCCL_GEMM_PICK_WAVES") != 0;
+  if (byWaves) return pickBNWaves(M, N, sms);
   const int tm = (M + kBM - 1) / kBM;
   for (int bn : {256, 128, 64}) {
     const int tiles = tm * ((N + bn - 1) / bn);

@@ -14,7 +14,11 @@ namespace gemm {
 // K-major bf16 tensor map for rows x K with a (64 x boxRows) box, 128B swizzle.
 bool makeMapKMajor(CUtensorMap* map, const void* base, int rows, int K, int boxRows);
 int smCount();
+// Output tile width: by default the widest whose tiles fill every SM; with
+// VCCL_GEMM_PICK_WAVES=1 the one with the shortest makespan (waves x width,
+// with a small charge for narrow tiles), pickBNWaves.
 int pickBN(int M, int N);
+int pickBNWaves(int M, int N, int sms);
 int* errorFlag();
 // True (once) if a GEMM on the current device set its abort flag since the
 // last call; reads pinned host memory, no synchronisation.

@@ -132,10 +132,28 @@ void checkPlan() {
         EXPECT(p.bn == 128, "split-K tile width");
       }
 }
+// Makespan tile widths: the TP-8 gate/up shard (896 tiles at 256 = 6.05
+// waves) goes to 128; full-wave shapes stay at 256; a 512-row GEMM takes one
+// wave of 128-wide tiles instead of two of 64; one-wave decode shapes take
+// the narrowest tile.
+void checkPickWaves() {
+  EXPECT(pickBNWaves(8192, 3584, 148) == 128, "8192x3584 -> %d", pickBNWaves(8192, 3584, 148));
+  EXPECT(pickBNWaves(8192, 4096, 148) == 256, "8192x4096 -> %d", pickBNWaves(8192, 4096, 148));
+  EXPECT(pickBNWaves(8192, 28672, 148) == 256, "8192x28672 -> %d", pickBNWaves(8192, 28672, 148));
+  EXPECT(pickBNWaves(512, 3584, 148) == 128, "512x3584 -> %d", pickBNWaves(512, 3584, 148));
+  EXPECT(pickBNWaves(1, 512, 148) == 32, "1x512 -> %d", pickBNWaves(1, 512, 148));
+  for (int M : {1, 128, 1000, 8192})
+    for (int N : {256, 1024, 3584, 4096, 14336})
+      for (int sms : {132, 148}) {
+        const int bn = pickBNWaves(M, N, sms);
+        EXPECT(bn == 256 || bn == 128 || bn == 64 || bn == 32, "width %d", bn);
+      }
+}
 }  // namespace
 
 int main() {
   checkSplitK();
+  checkPickWaves();
   checkGrouped();
   checkStage();
   checkPlan();
