@@ -3,9 +3,10 @@
 // tcgen05 MMA, written as inline PTX.
 //
 // Rules this file enforces for the whole code base:
-//   * TMA loads never use .multicast::cluster (kernels here also run on
+//   * TMA loads never use cluster multicast (kernels here also run on
 //     multi-GPU communicators, and a multicast load whose tensor map reaches
-//     peer memory is unsafe on this platform).
+//     peer memory is unsafe on this platform).  TMA stores may target peer
+//     memory (plain stores).
 //   * kind::f16 MMAs take A and B of the same type (both bf16).
 //   * Every mbarrier wait is bounded: after ~2 s it reports failure and the
 //     caller unwinds (frees TMEM, returns) instead of spinning forever.
