@@ -59,6 +59,7 @@ constexpr size_t kMoeCombEpochOff = kMoeOff + 132;          // u32, local: combi
 constexpr size_t kMoeBlocksOff = kMoeOff + 192;             // u32[4], local: per-kernel block counters
 constexpr size_t kWinDescOff = 81920;                       // WinDesc[kMaxBlocks], read by peers (window calls)
 constexpr size_t kCtrlHeader = 1 << 20;
+constexpr unsigned char kGuardByte = 0xA5;  // fill of the debug guard regions (VCCL_GUARDS=1)
 
 constexpr size_t kLLMaxBytes = 1 << 20;                 // largest LL payload per source rank
 constexpr size_t kLLSlotBytes = 2 * kLLMaxBytes;        // LL lines carry 8 payload bytes per 16

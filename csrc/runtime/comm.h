@@ -29,6 +29,7 @@ namespace vccl {
 // One cuMem allocation per rank, exported to and mapped by every rank.
 struct SymmetricBuffer {
   size_t bytes = 0;
+  size_t usable = 0;  // bytes the kernels use; [usable, bytes) is a guard region (VCCL_GUARDS=1)
   size_t align = 0;
   CUmemGenericAllocationHandle localHandle = 0;
   std::vector<CUmemGenericAllocationHandle> handles;  // per rank (imported for peers)

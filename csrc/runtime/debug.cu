@@ -8,6 +8,7 @@
 // correct one.  Waits are bounded like every other wait in the library.
 #include <cuda_runtime.h>
 
+#include "common/env.h"
 #include "kernels/collectives.cuh"
 #include "runtime/comm.h"
 
@@ -112,4 +113,44 @@ extern "C" vcclResult_t vcclxFusedTrace(vcclComm_t comm, unsigned long long* out
     return vcclUnhandledError;
   *ctas = sms;
   return vcclSuccess;
+}
+
+namespace {
+__global__ void guardScan(const unsigned char* p, size_t n, unsigned long long* bad) {
+  unsigned long long mine = 0;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    mine += p[i] != vccl::dev::kGuardByte;
+  if (mine) atomicAdd(bad, mine);
+}
+}  // namespace
+
+// Debug layout check (VCCL_GUARDS=1 at communicator creation): counts the
+// bytes of this rank's guard regions (past the ctrl, data and fused-op
+// regions the kernels use) that no longer hold the fill pattern, i.e. bytes
+// some kernel wrote out of bounds.  Synchronises the device.
+// vcclInvalidUsage when the communicator has no guards.
+extern "C" vcclResult_t vcclxCheckGuards(vcclComm_t comm, unsigned long long* badBytes) {
+  if (comm == nullptr || badBytes == nullptr) return vcclInvalidArgument;
+  if (!comm->dev || vccl::envLong("VCCL_GUARDS", 0) == 0) return vcclInvalidUsage;
+  vccl::DeviceState* ds = comm->dev.get();
+  cudaSetDevice(ds->device);
+  unsigned long long* d = nullptr;
+  if (cudaMalloc(&d, sizeof(*d)) != cudaSuccess) return vcclSystemError;
+  cudaMemset(d, 0, sizeof(*d));
+  const int me = comm->rank;
+  bool any = false;
+  for (const vccl::SymmetricBuffer* b : {&ds->ctrl, &ds->data, &ds->fused}) {
+    if (b->va.empty() || b->bytes <= b->usable) continue;
+    const unsigned char* p = reinterpret_cast<const unsigned char*>(b->va[me]) + b->usable;
+    guardScan<<<64, 256>>>(p, b->bytes - b->usable, d);
+    any = true;
+  }
+  cudaError_t e = cudaDeviceSynchronize();
+  unsigned long long h = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&h, d, sizeof(h), cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  if (e != cudaSuccess) return vcclUnhandledError;
+  *badBytes = h;
+  return any ? vcclSuccess : vcclInvalidUsage;
 }

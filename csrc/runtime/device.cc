@@ -303,8 +303,17 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
         mcCap = 0;
     }
     dataBytes = roundUp(dataBytes, dataAlign);
-    const size_t ctrlBytes = roundUp(dev::kCtrlBytes, gran);
-    const size_t fusedBytes = roundUp(envBytes("VCCL_FUSED_BUFFSIZE", 512u << 20), gran);
+    size_t fusedBytes = roundUp(envBytes("VCCL_FUSED_BUFFSIZE", 512u << 20), gran);
+    // Debug layout (VCCL_GUARDS=1): every region gets a guard of at least
+    // 1 MiB past the bytes the kernels use, filled with a pattern that
+    // vcclxCheckGuards verifies, so a kernel writing past its region's end
+    // shows up as an error code instead of silent corruption.
+    const size_t guard = envLong("VCCL_GUARDS", 0) != 0 ? (1u << 20) : 0;
+    const size_t ctrlUsable = guard ? dev::kCtrlBytes : roundUp(dev::kCtrlBytes, gran);
+    const size_t dataUsable = dataBytes, fusedUsable = fusedBytes;
+    const size_t ctrlBytes = roundUp(ctrlUsable + guard, gran);
+    dataBytes = roundUp(dataUsable + guard, dataAlign);
+    fusedBytes = roundUp(fusedUsable + guard, gran);
     // Every rank must choose the same algorithm for a call: the tuning table
     // takes part in the agreement through a hash of its rules.
     uint64_t tuneHash = 1469598103934665603ull;
@@ -330,6 +339,14 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
     VTRY(symmetricAlloc(bs, ds.get(), ctrlBytes, gran, &ds->ctrl));
     VTRY(symmetricAlloc(bs, ds.get(), dataBytes, dataAlign, &ds->data));
     VTRY(symmetricAlloc(bs, ds.get(), fusedBytes, gran, &ds->fused));
+    ds->ctrl.usable = ctrlUsable;
+    ds->data.usable = dataUsable;
+    ds->fused.usable = fusedUsable;
+    for (SymmetricBuffer* b : {&ds->ctrl, &ds->data, &ds->fused}) {
+      if (guard && b->bytes > b->usable)
+        CUDART_TRY(cudaMemset(reinterpret_cast<char*>(b->va[me]) + b->usable, dev::kGuardByte,
+                              b->bytes - b->usable));
+    }
     CUDART_TRY(cudaMemset(reinterpret_cast<void*>(ds->ctrl.va[me]), 0, dev::kCtrlHeader));
     CUDART_TRY(cudaMemset(reinterpret_cast<void*>(ds->ctrl.va[me] + dev::kLLOff), 0xff, 2 * dev::kLLBytes));
     CUDART_TRY(cudaDeviceSynchronize());
@@ -354,9 +371,9 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
     dc.data[p] = reinterpret_cast<char*>(ds->data.va[p]);
     dc.fused[p] = reinterpret_cast<char*>(ds->fused.va[p]);
   }
-  dc.fusedBytes = ds->fused.bytes;
+  dc.fusedBytes = ds->fused.usable ? ds->fused.usable : ds->fused.bytes;
   dc.mcData = ds->nvls ? reinterpret_cast<char*>(ds->data.mcVa) : nullptr;
-  dc.dataBytes = ds->data.bytes;
+  dc.dataBytes = ds->data.usable ? ds->data.usable : ds->data.bytes;
   dc.status = ds->devStatus;
   dc.abortWord = ds->devAbort;
   dc.timeoutNs = deviceTimeoutNs();

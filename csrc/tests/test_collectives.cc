@@ -31,6 +31,9 @@
 
 #include "vccl.h"
 
+// Debug entry point (csrc/runtime/debug.cu): overwritten guard bytes.
+extern "C" vcclResult_t vcclxCheckGuards(vcclComm_t comm, unsigned long long* badBytes);
+
 namespace {
 
 int gFail = 0;
@@ -634,6 +637,11 @@ int rankMain(int me, int n, const vcclUniqueId& id, bool full) {
     nvlsPipeSweep(c, me, n);
     multiRound(c, me, n);
     windowTest(c, me, n);
+    if (std::getenv("VCCL_GUARDS") != nullptr && n > 1) {
+      unsigned long long bad = 0;
+      EXPECT_OK(vcclxCheckGuards(c, &bad));
+      EXPECT(bad == 0, "kernels wrote past their regions");
+    }
     EXPECT_OK(vcclCommDestroy(c));
     if (gFail) std::fprintf(stderr, "rank %d/%d: %d failures (extended)\n", me, n, gFail);
     return gFail ? 1 : 0;

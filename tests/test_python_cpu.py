@@ -532,6 +532,7 @@ def test_window_api_without_device():
             with comm.window(buf):
                 pass
         assert comm.WIN_NO_MULTICAST == 1
+        assert comm.check_guards() is None  # no device plane, no guard regions
     finally:
         comm.destroy()
 

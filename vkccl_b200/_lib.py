@@ -141,6 +141,7 @@ def _declare_extensions(h: ctypes.CDLL) -> None:
         "vcclGemmBf16": [P, P, P, I, I, I, P],
         "vcclGemmBf16NoAlloc": [P, P, P, I, I, I, P],
         "vcclxFusedTrace": [P, P, P],
+        "vcclxCheckGuards": [P, c.POINTER(c.c_ulonglong)],
         "vcclGemmSiluMul": [P, P, P, I, I, I, P],
         "vcclGemmReduceScatter": [P, P, P, I, I, I, P, P],
         "vcclAllGatherGemm": [P, P, P, I, I, I, I, P, P],

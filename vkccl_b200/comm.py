@@ -470,11 +470,12 @@ class Communicator:
         _check(lib().vcclCommFinalize(self._comm), "vcclCommFinalize", self._comm)
 
     def fused_trace(self):
-        """Per-CTA event times (ns) of the last all-gather + GEMM call, as a
-        [ctas, 32] numpy array, when the communicator was created with
-        VCCL_FUSED_TRACE=1; None otherwise.  Slots: 0 start, 1 previous call's
-        shard taken by every peer, 2 own slice staged, 3..9 s-th peer shard
-        pulled, 10..17 first tile of the s-th shard released, 18 end."""
+        """Per-CTA event times (ns) of the fused kernels, as a [ctas, 32]
+        numpy array, when the communicator was created with
+        VCCL_FUSED_TRACE=1; None otherwise.  Last all-gather + GEMM: 0 start,
+        1 previous call's shard taken by every peer, 2 own slice staged, 3..9
+        s-th peer shard pulled, 10..17 first tile of the s-th shard released,
+        18 end.  Last GEMM + reduce-scatter: 20-27 (vkccl_b200.bench.rs_trace)."""
         import numpy as np
 
         out = np.zeros((256, 32), dtype=np.uint64)
@@ -483,6 +484,15 @@ class Communicator:
         if r != 0:
             return None
         return out[: ctas.value].copy()
+
+    def check_guards(self) -> Optional[int]:
+        """Bytes of this rank's debug guard regions that some kernel overwrote
+        (communicator created with VCCL_GUARDS=1; synchronises the device),
+        or None without guards."""
+        bad = ctypes.c_ulonglong(0)
+        if lib().vcclxCheckGuards(self._comm, ctypes.byref(bad)) != 0:
+            return None
+        return int(bad.value)
 
     def last_error(self) -> str:
         return lib().vcclGetLastError(self._comm).decode(errors="replace")
