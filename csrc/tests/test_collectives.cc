@@ -752,6 +752,72 @@ int runKill(int n) {
   return bad ? 1 : 0;
 }
 
+// vcclCommAbort from another thread while a kernel waits: rank 1 never
+// launches the collective (its failure is injected on the host), so rank 0's
+// kernel waits for it; a thread of rank 0 aborts after 300 ms, the kernel
+// sees the host-mapped abort word and returns well before the (30 s)
+// timeout, and the communicator is latched.  NVLS off, as for kill-a-rank.
+int abortRank(int me, int n, const vcclUniqueId& id) {
+  cudaSetDevice(me);
+  vcclComm_t c = nullptr;
+  if (vcclCommInitRank(&c, n, id, me) != vcclSuccess) return 2;
+  const size_t cnt = 1u << 20;
+  float* d = nullptr;
+  cudaMalloc(&d, cnt * 4);
+  cudaMemset(d, 0, cnt * 4);
+  int rc = 0;
+  if (me == 0) {
+    cudaStream_t st;
+    cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    auto t0 = std::chrono::steady_clock::now();
+    std::thread aborter([c]() {
+      std::this_thread::sleep_for(std::chrono::milliseconds(300));
+      vcclCommAbort(c);
+    });
+    const vcclResult_t r0 = vcclAllReduceAsync(d, d, cnt, vcclFloat32, vcclSum, c, st);
+    cudaStreamSynchronize(st);
+    aborter.join();
+    const double secs =
+        std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    const vcclResult_t r1 = vcclAllReduce(d, d, cnt, vcclFloat32, vcclSum, c);
+    vcclResult_t ae = vcclSuccess;
+    vcclCommGetAsyncError(c, &ae);
+    const bool ok = r0 == vcclSuccess && r1 == vcclInvalidUsage && ae != vcclSuccess && secs < 10.0;
+    if (!ok) std::fprintf(stderr, "abort rank 0: launch=%d next=%d async=%d after %.1f s\n", r0, r1, ae, secs);
+    rc = ok ? 0 : 1;
+    cudaStreamDestroy(st);
+  } else {
+    std::this_thread::sleep_for(std::chrono::milliseconds(2000));  // skips the collective
+  }
+  cudaFree(d);
+  vcclCommDestroy(c);
+  return rc;
+}
+
+int runAbort(int n) {
+  setenv("VCCL_TIMEOUT", "30", 1);
+  setenv("VCCL_NVLS_ENABLE", "0", 1);
+  vcclUniqueId id;
+  if (vcclGetUniqueId(&id) != vcclSuccess) return 1;
+  std::vector<pid_t> pids;
+  for (int r = 0; r < n; r++) {
+    pid_t p = fork();
+    if (p == 0) _exit(abortRank(r, n, id));
+    pids.push_back(p);
+  }
+  int bad = 0;
+  for (pid_t p : pids) {
+    int st = 0;
+    waitpid(p, &st, 0);
+    if (!WIFEXITED(st) || WEXITSTATUS(st) != 0) bad++;
+  }
+  unsetenv("VCCL_TIMEOUT");
+  unsetenv("VCCL_NVLS_ENABLE");
+  std::printf("abort while a kernel waits (nranks=%d): %s\n", n, bad ? "FAIL" : "OK");
+  std::fflush(stdout);
+  return bad ? 1 : 0;
+}
+
 int initAll(int ndev) {
   std::vector<vcclComm_t> comms(ndev, nullptr);
   if (vcclCommInitAll(comms.data(), ndev, nullptr) != vcclSuccess) {
@@ -863,6 +929,7 @@ int main(int argc, char** argv) {
     if (maxRanks >= 2) fails += forkRanks(2, true);
     if (maxRanks > 2) fails += forkRanks(maxRanks, true);
     if (maxRanks == 1) fails += forkRanks(1, true);
+    if (maxRanks >= 2) fails += runAbort(2);
     if (maxRanks >= 2) {
       pid_t p = fork();
       if (p == 0) _exit(initAllWindow(std::min(maxRanks, 4)));
