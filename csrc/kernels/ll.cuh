@@ -31,11 +31,17 @@ __device__ __forceinline__ char* llResSlot(const DevComm& c, int owner, uint32_t
   return c.ctrl[owner] + kLLResOff + (static_cast<size_t>(parity) * kMaxRanks + src) * kLLSlotBytes;
 }
 
+// Epochs run 1, 2, ..., 2^32 - 1, then 2, 3, ...: they never take the
+// value 0 the slots are filled with at set-up (a line no peer has written
+// yet can never look current, even after the counter wraps), and the wrap
+// keeps odd and even epochs alternating, so a slot of one parity is still
+// rewritten only every second launch.
 __device__ __forceinline__ uint32_t llEpoch(const DevComm& c) {
   __shared__ uint32_t sE;
   if (threadIdx.x == 0) {
     uint32_t* ep = ctrlAt<uint32_t>(c, c.rank, kLLEpochOff) + blockIdx.x;
     sE = *ep + 1u;
+    if (sE == 0u) sE = 2u;
     *ep = sE;
   }
   __syncthreads();

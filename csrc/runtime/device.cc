@@ -348,7 +348,8 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
                               b->bytes - b->usable));
     }
     CUDART_TRY(cudaMemset(reinterpret_cast<void*>(ds->ctrl.va[me]), 0, dev::kCtrlHeader));
-    CUDART_TRY(cudaMemset(reinterpret_cast<void*>(ds->ctrl.va[me] + dev::kLLOff), 0xff, 2 * dev::kLLBytes));
+    // LL lines start with flag 0, an epoch no LL launch ever uses.
+    CUDART_TRY(cudaMemset(reinterpret_cast<void*>(ds->ctrl.va[me] + dev::kLLOff), 0, 2 * dev::kLLBytes));
     CUDART_TRY(cudaDeviceSynchronize());
     VTRY(bs->barrier());
     if (everyone(bs, mcCap != 0)) ds->nvls = multicastSetup(bs, ds.get()) == vcclSuccess;

@@ -217,9 +217,15 @@ def run_gemm_rs(n, ctas, blocks, calls, seed):
 # ---------------------------------------------------------------------------
 # LL one-shot all-reduce (one block; the protocol is per block)
 # ---------------------------------------------------------------------------
-def run_ll(n, calls, seed, parities=2):
+def next_ll_epoch(e, wrap_to=2):
+    """csrc/kernels/ll.cuh llEpoch: 32-bit counter that skips 0 on the wrap."""
+    e = (e + 1) & 0xFFFFFFFF
+    return wrap_to if e == 0 else e
+
+
+def run_ll(n, calls, seed, parities=2, start=0, wrap_to=2):
     sim = Sim(seed)
-    epoch = defaultdict(int)   # rank -> epoch of its last LL launch
+    epoch = defaultdict(lambda: start)  # rank -> epoch of its last LL launch
     slots = {}                 # (dst, parity, src) -> epoch written
     consumed = {}              # (dst, parity, src) -> epoch the reader has taken out
     errors = []
@@ -229,7 +235,7 @@ def run_ll(n, calls, seed, parities=2):
             live = {"done": 0, "count": 1}
 
             def block():
-                epoch[r] += 1
+                epoch[r] = next_ll_epoch(epoch[r], wrap_to)
                 e = epoch[r]
                 par = e % parities
                 for p in range(n):
@@ -376,6 +382,26 @@ def test_model_detects_a_broken_protocol():
         return errors
 
     assert any(broken(3, 2, 4, seed) for seed in range(200))
+
+
+@pytest.mark.parametrize("n", [2, 3])
+def test_ll_protocol_across_epoch_wrap(n):
+    """Launches crossing the 32-bit epoch wrap (2^32-1 -> 2) keep the parity
+    alternation and never see a line of an older launch as current."""
+    for seed in range(150):
+        assert run_ll(n, calls=6, seed=seed, start=0xFFFFFFFF - 3) == []
+
+
+def test_model_detects_parity_break_at_wrap():
+    """Wrapping to 1 instead of 2 would give two consecutive launches the same
+    parity; the checker must see the overwrite."""
+    def broken(seed):
+        try:
+            return bool(run_ll(3, calls=6, seed=seed, start=0xFFFFFFFF - 3, wrap_to=1))
+        except Deadlock:
+            return True
+
+    assert any(broken(seed) for seed in range(200))
 
 
 def test_model_detects_single_buffered_ll():
