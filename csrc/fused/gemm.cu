@@ -179,14 +179,27 @@ cudaError_t launchSplitReduce(const float* ws, int splits, size_t elems, void* o
 // allocate nothing: calls on one stream are ordered, and calls on different
 // streams use different buffers.  A call that needs more than the cached
 // size waits for its stream, frees the old buffer and allocates a larger one.
+// At most kCachedStreams streams per device get a cached buffer (nothing
+// tells the library when a stream is destroyed, so the cache must not grow
+// with every stream a program ever creates); calls on other streams use a
+// stream-ordered allocation, as while capturing.  nullptr means "not cached".
 // Not used while the stream is being captured (see vcclGemmBf16).
+constexpr size_t kCachedStreams = 16;
+
 float* splitScratch(cudaStream_t st, size_t bytes) {
   static std::mutex mu;
   static std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> cache;
+  static std::map<int, size_t> perDevice;
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
-  auto& e = cache[{dev, st}];
+  auto it = cache.find({dev, st});
+  if (it == cache.end()) {
+    if (perDevice[dev] >= kCachedStreams) return nullptr;
+    perDevice[dev]++;
+    it = cache.emplace(std::make_pair(dev, st), std::make_pair(nullptr, size_t{0})).first;
+  }
+  auto& e = it->second;
   if (e.second < bytes) {
     if (e.first != nullptr) {
       cudaStreamSynchronize(st);
@@ -211,10 +224,17 @@ bool splitFixupEnabled() {
 uint32_t* splitSems(cudaStream_t st) {
   static std::mutex mu;
   static std::map<std::pair<int, cudaStream_t>, uint32_t*> cache;
+  static std::map<int, size_t> perDevice;
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
-  uint32_t*& p = cache[{dev, st}];
+  auto it = cache.find({dev, st});
+  if (it == cache.end()) {
+    if (perDevice[dev] >= kCachedStreams) return nullptr;
+    perDevice[dev]++;
+    it = cache.emplace(std::make_pair(dev, st), nullptr).first;
+  }
+  uint32_t*& p = it->second;
   if (p == nullptr) {
     void* q = nullptr;
     if (cudaMalloc(&q, kSemSlots * sizeof(uint32_t)) != cudaSuccess) return nullptr;
@@ -256,8 +276,18 @@ bool acquireScratch(cudaStream_t st, size_t bytes, Scratch* out) {
     return true;
   }
   out->p = splitScratch(st, bytes);
+  if (out->p == nullptr) {
+    // Not a cached stream (or its allocation failed): a stream-ordered
+    // allocation released after the call.
+    if (cudaMallocAsync(&out->p, bytes, st) != cudaSuccess) {
+      out->p = nullptr;
+      return false;
+    }
+    out->async = true;
+    return true;  // no fix-up semaphores: the reduction kernel runs
+  }
   if (splitFixupEnabled()) out->sems = splitSems(st);
-  return out->p != nullptr;
+  return true;
 }
 
 void releaseScratch(const Scratch& s) {
