@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <map>
@@ -243,7 +244,10 @@ vcclResult_t cudaToVccl(cudaError_t e, const char* what) {
 
 ArAlgo pickAllReduce(const HostOp& h, size_t bytes) {
   const DeviceState& ds = *h.comm->dev;
-  std::string force = envStr("VCCL_ALLREDUCE_ALGO", "");
+  // Read on every call (tests and sweeps switch it between calls); no
+  // allocation unless it is set.
+  const char* forced = std::getenv("VCCL_ALLREDUCE_ALGO");
+  std::string force = forced != nullptr ? forced : "";
   if (force.empty() && !ds.tuning.empty()) force = tunedAlgorithm(ds.tuning, "allreduce", h.comm->nranks, bytes);
   const bool llOk = bytes <= dev::kLLMaxBytes &&
                     ((reinterpret_cast<uintptr_t>(h.send) | reinterpret_cast<uintptr_t>(h.recv)) & 7u) == 0;
@@ -266,8 +270,7 @@ ArAlgo pickAllReduce(const HostOp& h, size_t bytes) {
   if (ll2Ok && bytes <= ds.ll2MaxBytes) return ArAlgo::LL2;
   // Per GPU, NVLS moves (1 + 1/n) S each way against 2 (n-1)/n S for the
   // two-shot: it only wins from four ranks on.
-  if (nvlsOk && h.comm->nranks >= envLong("VCCL_NVLS_MIN_RANKS", 4) &&
-      bytes >= envBytes("VCCL_NVLS_MIN", 512u << 10))
+  if (nvlsOk && h.comm->nranks >= ds.nvlsMinRanks && bytes >= ds.nvlsMinBytes)
     return ds.nvlsPipeMin != 0 && bytes >= ds.nvlsPipeMin ? ArAlgo::NvlsPipe : ArAlgo::Nvls;
   return ArAlgo::TwoShot;
 }

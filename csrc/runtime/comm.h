@@ -65,6 +65,8 @@ struct DeviceState {
   unsigned long long* fusedTrace = nullptr;  // per-CTA event times of the fused kernels (VCCL_FUSED_TRACE=1)
   std::vector<TuningRule> tuning;  // measured algorithm table (VCCL_TUNING_FILE)
   size_t ll2MaxBytes = 0;          // two-hop LL all-reduce threshold
+  int nvlsMinRanks = 4;            // NVLS all-reduce from this many ranks (VCCL_NVLS_MIN_RANKS) ...
+  size_t nvlsMinBytes = 512u << 10;  // ... and this size (VCCL_NVLS_MIN)
   size_t nvlsPipeMin = 0;          // pipelined NVLS all-reduce from this size (0: only when asked for)
   int nvlsPieces = 4;              // pieces of a pipelined NVLS all-reduce
   bool windowsEnabled = true;      // zero-copy kernels for buffers in registered windows (VCCL_WINDOW)

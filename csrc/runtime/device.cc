@@ -247,6 +247,8 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
   // Pipelined NVLS all-reduce: off by default until it is measured on this
   // machine; VCCL_NVLS_PIPE_MIN=<bytes> turns it on from that size, and
   // VCCL_ALLREDUCE_ALGO=nvls_pipe or a tuning rule picks it per call.
+  ds->nvlsMinRanks = static_cast<int>(envLong("VCCL_NVLS_MIN_RANKS", 4));
+  ds->nvlsMinBytes = envBytes("VCCL_NVLS_MIN", 512u << 10);
   ds->nvlsPipeMin = envBytes("VCCL_NVLS_PIPE_MIN", 0);
   ds->nvlsPieces = static_cast<int>(envLong("VCCL_NVLS_PIECES", 4));
   ds->windowsEnabled = envLong("VCCL_WINDOW", 1) != 0;
