@@ -316,14 +316,21 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
     const size_t ctrlBytes = roundUp(ctrlUsable + guard, gran);
     dataBytes = roundUp(dataUsable + guard, dataAlign);
     fusedBytes = roundUp(fusedUsable + guard, gran);
-    // Every rank must choose the same algorithm for a call: the tuning table
-    // takes part in the agreement through a hash of its rules.
+    // Every rank must choose the same algorithm and grid for a call: the
+    // tuning table and every setting that steers the choice take part in the
+    // agreement through a hash.
     uint64_t tuneHash = 1469598103934665603ull;
-    for (const TuningRule& r : ds->tuning) {
-      const std::string line = r.op + " " + std::to_string(r.nranks) + " " + std::to_string(r.maxBytes) + " " + r.algo;
+    auto mix = [&](const std::string& line) {
       for (unsigned char ch : line) tuneHash = (tuneHash ^ ch) * 1099511628211ull;
       tuneHash = (tuneHash ^ '\n') * 1099511628211ull;
-    }
+    };
+    for (const TuningRule& r : ds->tuning)
+      mix(r.op + " " + std::to_string(r.nranks) + " " + std::to_string(r.maxBytes) + " " + r.algo);
+    mix("nblocks " + std::to_string(ds->nblocks) + " ll " + std::to_string(ds->llMaxBytes) + " ll2 " +
+        std::to_string(ds->ll2MaxBytes) + " llag " + std::to_string(ds->llAgMaxBytes) + " nvls " +
+        std::to_string(ds->nvlsMinRanks) + " " + std::to_string(ds->nvlsMinBytes) + " pipe " +
+        std::to_string(ds->nvlsPipeMin) + " " + std::to_string(ds->nvlsPieces) + " win " +
+        std::to_string(ds->windowsEnabled ? 1 : 0) + " " + std::to_string(ds->windowNvlsMinRanks));
     struct Sizes { uint64_t ctrl, data, fused, llBlocks, smallRows, tuning; } mine{
         ctrlBytes, dataBytes, fusedBytes, static_cast<uint64_t>(ds->llBlocks),
         static_cast<uint64_t>(static_cast<int64_t>(ds->fusedSmallRows)), tuneHash};
@@ -333,8 +340,9 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
     for (const Sizes& s : all) {
       if (s.ctrl != mine.ctrl || s.data != mine.data || s.fused != mine.fused || s.llBlocks != mine.llBlocks ||
           s.smallRows != mine.smallRows || s.tuning != mine.tuning) {
-        VERR("ranks disagree on workspace sizes or algorithm tables (check VCCL_BUFFSIZE, VCCL_FUSED_BUFFSIZE, "
-             "VCCL_LL_BLOCKS, VCCL_FUSED_SMALL_M and VCCL_TUNING_FILE on every rank)");
+        VERR("ranks disagree on workspace sizes or algorithm settings (check VCCL_BUFFSIZE, VCCL_FUSED_BUFFSIZE, "
+             "VCCL_GUARDS, VCCL_LL_BLOCKS, VCCL_NBLOCKS, VCCL_FUSED_SMALL_M, the VCCL_LL_* / VCCL_NVLS_* / "
+             "VCCL_WINDOW* thresholds and VCCL_TUNING_FILE on every rank)");
         return vcclInvalidUsage;
       }
     }
