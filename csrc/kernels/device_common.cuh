@@ -33,8 +33,6 @@ constexpr size_t kP2pHeadOff = 8192;                                  // u64[kMa
 constexpr size_t kP2pTailOff = kP2pHeadOff + kMaxRanks * kMaxChannels * 8;  // written by receivers
 constexpr size_t kP2pSentOff = kP2pTailOff + kMaxRanks * kMaxChannels * 8;  // local
 constexpr size_t kP2pRecvdOff = kP2pSentOff + kMaxRanks * kMaxChannels * 8; // local
-constexpr size_t kFusedEpochOff = 16384;                              // u32[kMaxBlocks], local (fused kernels)
-constexpr size_t kFusedFlagsOff = 20480;                              // u32[kMaxBlocks][kMaxRanks], written by peers
 constexpr size_t kMoeCountsOff = 32768;                               // u32[2][kMaxRanks][64], written by peers
 // Fused GEMM + reduce-scatter / all-gather + GEMM counters (monotonic).
 constexpr int kMaxFusedCtas = 256;
