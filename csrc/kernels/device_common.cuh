@@ -248,31 +248,8 @@ __device__ __forceinline__ uint4 ldCG(const void* p) {
                : "memory");
   return v;
 }
-__device__ __forceinline__ uint4 ldNC(const void* p) {
-  return __ldg(reinterpret_cast<const uint4*>(p));
-}
 __device__ __forceinline__ void stG(void* p, const uint4& v) {
   *reinterpret_cast<uint4*>(p) = v;
-}
-
-// Grid-stride byte copy with the widest access the alignment allows.
-__device__ __forceinline__ void copyBytes(char* dst, const char* src, size_t n, size_t tid,
-                                          size_t nthr) {
-  if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15u) == 0) {
-    const size_t nv = n / 16;
-    const uint4* s = reinterpret_cast<const uint4*>(src);
-    uint4* d = reinterpret_cast<uint4*>(dst);
-    for (size_t i = tid; i < nv; i += nthr) d[i] = ldCG(s + i);
-    for (size_t i = nv * 16 + tid; i < n; i += nthr) dst[i] = src[i];
-  } else if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 3u) == 0) {
-    const size_t nw = n / 4;
-    const uint32_t* s = reinterpret_cast<const uint32_t*>(src);
-    uint32_t* d = reinterpret_cast<uint32_t*>(dst);
-    for (size_t i = tid; i < nw; i += nthr) d[i] = s[i];
-    for (size_t i = nw * 4 + tid; i < n; i += nthr) dst[i] = src[i];
-  } else {
-    for (size_t i = tid; i < n; i += nthr) dst[i] = src[i];
-  }
 }
 
 }  // namespace dev
