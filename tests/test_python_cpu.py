@@ -575,3 +575,23 @@ def test_rs_trace_summary():
     s = summarise(t)
     assert s["freed_wait_us"] == 2.0 and s["tiles_us"] == 197.0 and s["tiles_per_cta"] == 7.0
     assert abs(s["push_per_tile_us"] - 50 / 7) < 0.01 and s["reduce_us"] == 10.0 and s["gemm_end_us"] == 200.0
+
+
+def test_single_rank_all_to_all_v_and_finalize():
+    """all_to_all_v on a one-rank host communicator copies the block at the
+    given displacements; finalize succeeds."""
+    _env()
+    import vkccl_b200 as v
+
+    comm = v.Communicator(1, v.get_unique_id(), 0)
+    try:
+        x = np.arange(10, dtype=np.float32)
+        y = np.full(12, -1.0, dtype=np.float32)
+        comm.all_to_all_v(x, [4], [3], y, [4], [5])
+        assert np.array_equal(y[5:9], x[3:7])
+        assert np.all(y[:5] == -1) and np.all(y[9:] == -1)
+        with pytest.raises(ValueError):
+            comm.all_to_all_v(bytearray(8), [1], [0], bytearray(8), [1], [0])
+        comm.finalize()
+    finally:
+        comm.destroy()
