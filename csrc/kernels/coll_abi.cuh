@@ -56,6 +56,11 @@ struct WinArgs {
   double scalar;
 };
 
+// Element counts and displacements of one rank's all-to-all(v) call.
+struct A2aTable {
+  uint64_t sc[kMaxRanks], sd[kMaxRanks], rc[kMaxRanks], rd[kMaxRanks];
+};
+
 constexpr int kMaxP2pOps = 160;
 constexpr int kMaxP2pWork = 160;
 enum P2pKind : int { kP2pSend = 0, kP2pRecv = 1, kP2pCopy = 2 };

@@ -56,6 +56,7 @@ constexpr size_t kMoeDispEpochOff = kMoeOff + 128;          // u32, local: dispa
 constexpr size_t kMoeCombEpochOff = kMoeOff + 132;          // u32, local: combine calls finished
 constexpr size_t kMoeBlocksOff = kMoeOff + 192;             // u32[4], local: per-kernel block counters
 constexpr size_t kWinDescOff = 81920;                       // WinDesc[kMaxBlocks], read by peers (window calls)
+constexpr size_t kWinA2aOff = 90112;                        // u64[kMaxBlocks][kMaxRanks][2]: all-to-all(v) receive table
 constexpr size_t kCtrlHeader = 1 << 20;
 constexpr unsigned char kGuardByte = 0xA5;  // fill of the debug guard regions (VCCL_GUARDS=1)
 

@@ -236,23 +236,45 @@ __global__ void __launch_bounds__(512) broadcastWin(DevComm c, WinArgs w, int ro
   (void)blockBarrier(c, blk, kWhereWindow);
 }
 
-// All-to-all with equal blocks, receive buffer in a window: every rank
-// writes its block q straight into rank q's receive buffer at offset
-// rank * bytes (one NVLink write per byte, no slot ring, no copy-out).
-// w.count = bytes per block; w.send[me] is the local send buffer.
-__global__ void __launch_bounds__(512) allToAllWin(DevComm c, WinArgs w) {
+// All-to-all(v), receive buffer in a window: every rank publishes where it
+// wants each source's block (its receive count and displacement for that
+// source) before the start barrier; every sender reads its entry at each
+// destination, checks that its send count matches, and writes its block
+// straight into the destination's receive buffer.  w.recv[q] is rank q's
+// receive buffer, w.send[me] the local send buffer; counts are in elements
+// of esz bytes.  A count mismatch is recorded as an error; the ranks that
+// saw none still meet at the end barrier, whose waits then run out.
+__global__ void __launch_bounds__(512) allToAllvWin(DevComm c, WinArgs w, A2aTable t, int esz) {
   __shared__ double sScale[kMaxRanks];
+  __shared__ uint64_t sDispl[kMaxRanks];
+  __shared__ int sBad;
   const int blk = blockIdx.x, G = gridDim.x, n = c.nranks, me = c.rank;
+  if (threadIdx.x < n) {
+    uint64_t* e = ctrlAt<uint64_t>(c, me, kWinA2aOff) + (static_cast<size_t>(blk) * kMaxRanks + threadIdx.x) * 2;
+    e[0] = t.rc[threadIdx.x];
+    e[1] = t.rd[threadIdx.x];
+  }
+  if (threadIdx.x == 0) sBad = 0;
+  // winStart's barrier begins with a block-wide sync and releases the table too.
   if (!winStart(c, blk, w, sScale)) return;
-  const size_t bytes = w.count;
-  size_t lo, hi;
-  blockRange(bytes, G, blk, 16, &lo, &hi);
-  if (lo < hi) {
-    for (int k = 0; k < n; k++) {
-      int q = me + k;
-      if (q >= n) q -= n;
-      copyAny(w.recv[q] + me * bytes + lo, w.send[me] + q * bytes + lo, hi - lo);
-    }
+  if (threadIdx.x < n) {
+    const volatile uint64_t* e =
+        ctrlAt<uint64_t>(c, threadIdx.x, kWinA2aOff) + (static_cast<size_t>(blk) * kMaxRanks + me) * 2;
+    if (e[0] != t.sc[threadIdx.x]) sBad = 1;
+    sDispl[threadIdx.x] = e[1];
+  }
+  __syncthreads();
+  if (sBad) {
+    if (threadIdx.x == 0) recordFailure(c, kErrBadArg, kWhereWindow, static_cast<uint32_t>(blk));
+    return;
+  }
+  for (int k = 0; k < n; k++) {
+    int q = me + k;
+    if (q >= n) q -= n;
+    const size_t bytes = t.sc[q] * esz;
+    size_t lo, hi;
+    blockRange(bytes, G, blk, 16, &lo, &hi);
+    if (lo < hi) copyAny(w.recv[q] + sDispl[q] * esz + lo, w.send[me] + t.sd[q] * esz + lo, hi - lo);
   }
   (void)blockBarrier(c, blk, kWhereWindow);
 }

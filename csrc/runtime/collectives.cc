@@ -476,33 +476,44 @@ bool windowCollective(const HostOp& h, const LaunchCtx& lc, vcclResult_t* out) {
   }
 }
 
-// Zero-copy all-to-all: equal blocks (vcclAllToAll's layout) with the
-// receive buffer in a registered window; every rank writes its blocks into
-// the peers' receive buffers.  The window, or null when this does not apply
-// (the slot-ring kernel runs).  Decided on the caller's pointers, before any
-// staging: a receive buffer in a window is device memory.
+// Zero-copy all-to-all(v) with the receive buffer in a registered window:
+// every rank writes its blocks straight into the peers' receive buffers, at
+// the displacements each receiver publishes on the device.  The window, or
+// null when this does not apply (the slot-ring kernel runs).  Decided on the
+// caller's pointers, before any staging: a receive buffer in a window is
+// device memory.  Every rank takes the same path: windows are registered,
+// and the receive buffer lies in one on every rank (the window rule).
 const Window* windowForAllToAll(const HostOp& h) {
   vcclComm_t comm = h.comm;
   const int n = comm->nranks;
   if (!comm->dev || !comm->dev->windowsEnabled || n == 1 || comm->windows.empty()) return nullptr;
-  const size_t cnt = h.sc[0];
-  for (int q = 0; q < n; q++)
-    if (h.sc[q] != cnt || h.rc[q] != cnt || h.sd[q] != q * cnt || h.rd[q] != q * cnt) return nullptr;
-  const size_t bytes = cnt * vcclTypeSize(h.dt);
-  return bytes == 0 ? nullptr : comm->findWindow(h.recv, bytes * n);
+  size_t extent = 0;
+  for (int q = 0; q < n; q++) extent = std::max(extent, h.rd[q] + h.rc[q]);
+  const size_t es = vcclTypeSize(h.dt);
+  return extent == 0 ? nullptr : comm->findWindow(h.recv, extent * es);
 }
 
 vcclResult_t windowAllToAll(const HostOp& h, const Window* wr) {
   vcclComm_t comm = h.comm;
   const int n = comm->nranks, me = comm->rank;
-  const size_t bytes = h.sc[0] * vcclTypeSize(h.dt);
+  const size_t es = vcclTypeSize(h.dt);
   dev::WinArgs w{};
   w.recvOff = static_cast<uint64_t>(h.recv - wr->base);
   for (int q = 0; q < n; q++) w.recv[q] = wr->peer[q] + w.recvOff;
   w.send[me] = h.send;
-  w.count = bytes;
-  noteAlgorithm("all-to-all", "window push", n, bytes * n);
-  return cudaToVccl(launchAllToAllWindow(launchCtx(comm, h.stream), w), "window all-to-all launch");
+  dev::A2aTable t{};
+  size_t total = 0;
+  for (int q = 0; q < n; q++) {
+    t.sc[q] = h.sc[q];
+    t.sd[q] = h.sd[q];
+    t.rc[q] = h.rc[q];
+    t.rd[q] = h.rd[q];
+    total += h.sc[q] * es;
+  }
+  w.count = 0;  // counts differ per rank; the table check covers them
+  noteAlgorithm("all-to-all(v)", "window push", n, total);
+  return cudaToVccl(launchAllToAllvWindow(launchCtx(comm, h.stream), w, t, static_cast<int>(es)),
+                    "window all-to-all(v) launch");
 }
 
 vcclResult_t launchColl(const HostOp& h) {

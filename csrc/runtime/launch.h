@@ -47,7 +47,7 @@ cudaError_t launchP2p(const LaunchCtx& lc, const dev::P2pPlan& plan);
 cudaError_t launchAllReduceWindow(const LaunchCtx& lc, vcclDataType_t dt, int redKind, const dev::WinArgs& w,
                                   bool viaSwitch);
 cudaError_t launchAllGatherWindow(const LaunchCtx& lc, const dev::WinArgs& w);
-cudaError_t launchAllToAllWindow(const LaunchCtx& lc, const dev::WinArgs& w);
+cudaError_t launchAllToAllvWindow(const LaunchCtx& lc, const dev::WinArgs& w, const dev::A2aTable& t, int esz);
 cudaError_t launchBroadcastWindow(const LaunchCtx& lc, const dev::WinArgs& w, int root);
 cudaError_t launchReduceScatterWindow(const LaunchCtx& lc, vcclDataType_t dt, int redKind, const dev::WinArgs& w,
                                       bool viaSwitch);

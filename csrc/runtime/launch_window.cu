@@ -62,9 +62,10 @@ cudaError_t launchBroadcastWindow(const LaunchCtx& lc, const dev::WinArgs& w, in
   return cudaGetLastError();
 }
 
-cudaError_t launchAllToAllWindow(const LaunchCtx& lc, const dev::WinArgs& w) {
-  const int g = gridFor(w.count * lc.dc.nranks, lc.nblocks);
-  dev::allToAllWin<<<g, kThreads, 0, lc.stream>>>(lc.dc, w);
+cudaError_t launchAllToAllvWindow(const LaunchCtx& lc, const dev::WinArgs& w, const dev::A2aTable& t, int esz) {
+  // Block counts differ between ranks, so the grid cannot follow them: every
+  // rank launches the full barrier grid (block b meets block b of the peers).
+  dev::allToAllvWin<<<lc.nblocks, kThreads, 0, lc.stream>>>(lc.dc, w, t, esz);
   return cudaGetLastError();
 }
 

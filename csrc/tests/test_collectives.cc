@@ -572,6 +572,38 @@ void windowTest(vcclComm_t c, int me, int n) {
         break;
       }
   }
+  // all-to-all(v) with uneven blocks into window B: rank p sends
+  // 1000 (p + 1) + 7 q elements to rank q, packed in its send buffer
+  {
+    auto blk = [](int p, int q) { return static_cast<size_t>(1000 * (p + 1) + 7 * q); };
+    std::vector<size_t> sc(n), sd(n), rc(n), rd(n);
+    size_t so = 0, ro = 0;
+    for (int q = 0; q < n; q++) {
+      sc[q] = blk(me, q);
+      sd[q] = so;
+      so += sc[q];
+      rc[q] = blk(q, me);
+      rd[q] = ro;
+      ro += rc[q];
+    }
+    void* sbuf = nullptr;
+    cudaMalloc(&sbuf, so * 4);
+    upload(sbuf, vcclFloat32, so, 0);
+    EXPECT_OK(vcclAllToAllv(sbuf, sc.data(), sd.data(), B, rc.data(), rd.data(), vcclFloat32, c));
+    std::vector<float> g(ro);
+    cudaMemcpy(g.data(), B, ro * 4, cudaMemcpyDeviceToHost);
+    for (int p = 0; p < n; p++) {
+      size_t psd = 0;  // where rank p's block for me starts in its send buffer
+      for (int q = 0; q < me; q++) psd += blk(p, q);
+      for (size_t i = 0; i < rc[p]; i += 13)
+        if (!near(g[rd[p] + i], val(p, psd + i), vcclFloat32)) {
+          std::fprintf(stderr, "FAIL window alltoallv from rank %d i=%zu\n", p, i);
+          gFail++;
+          break;
+        }
+    }
+    cudaFree(sbuf);
+  }
   cudaFree(local);
   EXPECT_OK(vcclCommWindowDeregister(c, wa));
   EXPECT_OK(vcclCommWindowDeregister(c, wb));

@@ -264,8 +264,8 @@ vcclResult_t vcclCommRegisterDmaBuf(vcclComm_t comm, int fd, uint64_t offset,
  * buffer, and for vcclMemAlloc memory on a node that supports NVLS the
  * buffers are also bound to one multicast object (unless flags has
  * VCCL_WIN_NO_MULTICAST).  All-reduce with both buffers in windows,
- * all-gather, broadcast and all-to-all (equal blocks) with the receive
- * buffer in a window and reduce-scatter with the send buffer in a window
+ * all-gather, broadcast and all-to-all(v) with the receive buffer in a
+ * window and reduce-scatter with the send buffer in a window
  * then read and write the peers' buffers in place (no staging copies).  Rule for those calls: every rank passes
  * buffers at the same offsets of its windows and the same count; calls
  * that break it fail with vcclInvalidUsage on every rank and move no data.
