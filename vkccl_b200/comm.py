@@ -518,10 +518,13 @@ class Communicator:
     WIN_NO_MULTICAST = 0x1
 
     def window_register(self, buf: Any, nbytes: Optional[int] = None, flags: int = 0) -> ctypes.c_void_p:
-        """Collective: map `buf` (vcclMemAlloc memory, e.g. from mem_alloc_tensor;
-        the same size on every rank) into every rank.  Collectives on buffers
-        inside windows then read and write the peers' buffers in place; every
-        rank must pass buffers at the same offsets of its windows."""
+        """Collective: map `buf` (the same size on every rank) into every rank.
+        vcclMemAlloc memory (mem_alloc_tensor) is also bound to an NVLS
+        multicast object; an ordinary CUDA tensor is shared by CUDA IPC.
+        Collectives on buffers inside windows then read and write the peers'
+        buffers in place; every rank must pass buffers at the same offsets of
+        its windows.  Keep the memory alive (for a PyTorch tensor: the tensor,
+        and no torch.cuda.empty_cache()) until window_deregister."""
         b = buffer_info(buf, True)
         h = ctypes.c_void_p()
         _check(lib().vcclCommWindowRegister(self._comm, b.addr, nbytes or b.nbytes, ctypes.byref(h), flags),
