@@ -595,3 +595,20 @@ def test_single_rank_all_to_all_v_and_finalize():
         comm.finalize()
     finally:
         comm.destroy()
+
+
+def test_bindings_declare_every_header_function():
+    """Every function of include/vccl.h and include/vccl_tp.h has a ctypes
+    prototype in vkccl_b200/_lib.py, and the built library exports it."""
+    import re
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    hdr = "".join(open(os.path.join(root, "include", h)).read() for h in ("vccl.h", "vccl_tp.h"))
+    names = sorted(set(re.findall(r"\b(vccl[A-Z]\w*)\s*\(", hdr)))
+    assert len(names) > 40
+    src = open(os.path.join(root, "vkccl_b200", "_lib.py")).read()
+    assert [n for n in names if f'"{n}"' not in src] == []
+    from vkccl_b200._lib import lib
+
+    h = lib()
+    assert [n for n in names if not hasattr(h, n)] == []
