@@ -49,6 +49,11 @@ using dev::DevComm;
 
 constexpr int kMaxTopk = 8;
 constexpr int kGrid = 256;       // fixed grid of the push/receive/reduce kernels (block counters)
+// The single-rank kernels keep no block counters, so their grid can fill
+// the GPU: 4 blocks of 256 threads per SM, as many as the dispatch kernel's
+// 64 registers per thread allow (the dispatch profile showed 22 % of the
+// warp slots in use with kGrid, latency-bound).
+constexpr int kLocalBlocksPerSm = 4;
 constexpr int kThreads = 256;    // 8 warps
 constexpr float kFp8Max = 448.0f;
 
@@ -524,6 +529,16 @@ __global__ void __launch_bounds__(kThreads) moeCombineReduce(DevComm c, Layout L
 // ---------------------------------------------------------------------------
 // single rank: the same quantise / dequantise and weighted sum, locally
 // ---------------------------------------------------------------------------
+int localGrid() {
+  static const int g = [] {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms * kLocalBlocksPerSm;
+  }();
+  return g;
+}
+
 __global__ void __launch_bounds__(kThreads) moeLocalDispatch(const __nv_bfloat16* x, const int* ids, const float* w,
                                                              int T, int H, int topk, int numExperts,
                                                              __nv_bfloat16* recvX, int* recvMeta, float* recvW,
@@ -629,7 +644,7 @@ extern "C" vcclResult_t vcclMoeDispatchFp8(const void* x, const int* topkIds, co
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   auto* rx = static_cast<__nv_bfloat16*>(recvX);
   if (n == 1) {
-    moe::moeLocalDispatch<<<moe::kGrid, moe::kThreads, 0, s>>>(xb, topkIds, topkW, T, H, topk, numExperts, rx,
+    moe::moeLocalDispatch<<<moe::localGrid(), moe::kThreads, 0, s>>>(xb, topkIds, topkW, T, H, topk, numExperts, rx,
                                                                recvMeta, recvW, recvCount);
     return cudaGetLastError() == cudaSuccess ? vcclSuccess : vcclUnhandledError;
   }
@@ -672,7 +687,7 @@ extern "C" vcclResult_t vcclMoeCombine(const void* expertOut, const int* recvMet
   const auto* y = static_cast<const __nv_bfloat16*>(expertOut);
   auto* o = static_cast<__nv_bfloat16*>(out);
   if (comm->nranks == 1) {
-    moe::moeLocalCombine<<<moe::kGrid, moe::kThreads, 0, s>>>(y, recvW, o, T, H, topk);
+    moe::moeLocalCombine<<<moe::localGrid(), moe::kThreads, 0, s>>>(y, recvW, o, T, H, topk);
     return cudaGetLastError() == cudaSuccess ? vcclSuccess : vcclUnhandledError;
   }
   const moe::Layout L = moe::layoutFor(capacity, H);
