@@ -58,6 +58,15 @@ constexpr size_t kMoeBlocksOff = kMoeOff + 192;             // u32[4], local: pe
 constexpr size_t kWinDescOff = 81920;                       // WinDesc[kMaxBlocks], read by peers (window calls)
 constexpr size_t kWinA2aOff = 90112;                        // u64[kMaxBlocks][kMaxRanks][2]: all-to-all(v) receive table
 constexpr size_t kCtrlHeader = 1 << 20;
+// The header's ranges must not overlap.
+static_assert(kLLEpochOff + kMaxLLBlocks * 4 <= kP2pHeadOff, "epochs overlap the p2p counters");
+static_assert(kP2pRecvdOff + kMaxRanks * kMaxChannels * 8 <= kMoeCountsOff, "p2p counters overlap the MoE rows");
+static_assert(kMoeCountsOff + 2 * kMaxRanks * 64 * 4 <= kRsDoneOff, "MoE rows overlap the fused counters");
+static_assert(kRsLocalFreeOff + 4 <= kAgReadyOff, "reduce-scatter counters overlap the all-gather counters");
+static_assert(kAgStagedOff + 4 <= kMoeOff, "all-gather counters overlap the MoE counters");
+static_assert(kMoeBlocksOff + 16 <= kWinDescOff, "MoE counters overlap the window descriptors");
+static_assert(kWinDescOff + kMaxBlocks * 32 <= kWinA2aOff, "window descriptors overlap the all-to-all tables");
+static_assert(kWinA2aOff + kMaxBlocks * kMaxRanks * 16 <= kCtrlHeader, "all-to-all tables leave the header");
 constexpr unsigned char kGuardByte = 0xA5;  // fill of the debug guard regions (VCCL_GUARDS=1)
 
 constexpr size_t kLLMaxBytes = 1 << 20;                 // largest LL payload per source rank
