@@ -313,6 +313,9 @@ __global__ void __launch_bounds__(512) allReduceNvls(DevComm c, CollArgs a, size
       const size_t hi = hiRaw < m ? hiRaw : m;
       if (lo < hi) copyInScaled<T>(local + lo, a.send + off + lo, (hi - lo) / esz, a.premul, a.scalar);
     }
+    // The copy-in wrote through this GPU's own address; the peers read it
+    // through the multicast address (another alias of the same memory).
+    fenceProxyAlias();
     if (!blockBarrier(c, blk, kWhereNvls)) return;
     // 2. reduce my chunk through the switch and broadcast the result
     if constexpr (HasMultimem<T, K>::value) {
