@@ -11,6 +11,7 @@
 #include "common/env.h"
 #include "kernels/collectives.cuh"
 #include "runtime/comm.h"
+#include "vccl_x.h"
 
 namespace vccl {
 namespace dev {

@@ -30,9 +30,7 @@
 #include <vector>
 
 #include "vccl.h"
-
-// Debug entry point (csrc/runtime/debug.cu): overwritten guard bytes.
-extern "C" vcclResult_t vcclxCheckGuards(vcclComm_t comm, unsigned long long* badBytes);
+#include "vccl_x.h"
 
 namespace {
 

@@ -12,8 +12,7 @@
 #include <vector>
 
 #include "vccl.h"
-
-extern "C" vcclResult_t vcclxBarrierBench(vcclComm_t comm, int iters, int nblocks, int variant, float* us);
+#include "vccl_x.h"
 
 static int runRank(int r, int n, const vcclUniqueId& id) {
   setvbuf(stdout, nullptr, _IOLBF, 0);

@@ -142,6 +142,7 @@ def _declare_extensions(h: ctypes.CDLL) -> None:
         "vcclGemmBf16NoAlloc": [P, P, P, I, I, I, P],
         "vcclxFusedTrace": [P, P, P],
         "vcclxCheckGuards": [P, c.POINTER(c.c_ulonglong)],
+        "vcclxBarrierBench": [P, I, I, I, c.POINTER(F)],
         "vcclGemmSiluMul": [P, P, P, I, I, I, P],
         "vcclGemmReduceScatter": [P, P, P, I, I, I, P, P],
         "vcclAllGatherGemm": [P, P, P, I, I, I, I, P, P],
