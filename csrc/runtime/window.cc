@@ -297,9 +297,9 @@ extern "C" vcclResult_t vcclCommWindowRegister(vcclComm_t comm, void* buff, size
     return vcclSystemError;
   }
   const bool wantMc = ds->nvls && (flags & VCCL_WIN_NO_MULTICAST) == 0 && envLong("VCCL_WINDOW_NVLS", 1) != 0;
-  // Every rank sees the same ds->nvls, flags are required to agree, so all
-  // ranks take (or skip) the multicast steps together.
-  if (wantMc && !windowMulticast(bs, ds, w.get(), info))
+  // The flags and VCCL_WINDOW_NVLS are per rank; the ranks agree first, so
+  // that all of them take (or skip) the multicast steps together.
+  if (everyone(bs, wantMc) && !windowMulticast(bs, ds, w.get(), info))
     VINFO("window of %zu bytes: no multicast binding, point-to-point only", size);
   res = bs->barrier();
   if (res != vcclSuccess) {
