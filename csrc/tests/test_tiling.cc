@@ -100,6 +100,17 @@ void checkStage() {
         const int sl = stageSlot(nc, row, ch);
         EXPECT(sl >= 0 && sl < 32 * nc && slots.insert(sl).second, "stage slot collision (nc=%d)", nc);
       }
+    // With 8 chunks (128-byte rows) the stage is the layout a TMA tile store
+    // with 128-byte swizzle reads from a 1024-byte aligned box: byte address
+    // bits [4,7) are XORed with bits [7,10).
+    if (nc == 8)
+      for (int row = 0; row < 32; row++)
+        for (int ch = 0; ch < 8; ch++) {
+          const int plain = row * 128 + ch * 16;
+          const int swz = plain ^ (((plain >> 7) & 7) << 4);
+          EXPECT(stageSlot(8, row, ch) * 16 == swz, "stage differs from the 128-byte swizzle at row %d chunk %d",
+                 row, ch);
+        }
     // writes: lane = row, one instruction per chunk j; phases of 8 lanes
     for (int j = 0; j < nc; j++)
       for (int ph = 0; ph < 4; ph++) {
