@@ -655,15 +655,24 @@ vcclResult_t launchOps(vcclComm_t comm, std::vector<HostOp>& ops, std::vector<Pe
         while (j < ops.size() && isP2pKind(ops[j].kind)) j++;
       cudaStream_t s = ops[i].stream;
       bool anySync = false;
-      // Order every stream of the run before the kernel and after it.
-      std::vector<cudaEvent_t> evs;
+      // Order every stream of the run before the kernel and after it (the
+      // events are destroyed on every exit; a destroyed event that a stream
+      // still waits on completes as recorded).
+      struct Events {
+        std::vector<cudaEvent_t> v;
+        ~Events() {
+          for (cudaEvent_t e : v) cudaEventDestroy(e);
+        }
+      } evs;
+      std::vector<cudaStream_t> others;  // the run's streams other than s (each op is moved onto s below)
       for (size_t k = i; k < j; k++) {
-        if (ops[k].stream != s) {
-          cudaEvent_t ev;
-          cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-          cudaEventRecord(ev, ops[k].stream);
-          cudaStreamWaitEvent(s, ev, 0);
-          evs.push_back(ev);
+        if (ops[k].stream != s && std::find(others.begin(), others.end(), ops[k].stream) == others.end()) {
+          others.push_back(ops[k].stream);
+          cudaEvent_t ev = nullptr;
+          VTRY(cudaToVccl(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "event"));
+          evs.v.push_back(ev);
+          VTRY(cudaToVccl(cudaEventRecord(ev, ops[k].stream), "event record"));
+          VTRY(cudaToVccl(cudaStreamWaitEvent(s, ev, 0), "stream wait"));
         }
       }
       PlanBuilder pb;
@@ -676,13 +685,12 @@ vcclResult_t launchOps(vcclComm_t comm, std::vector<HostOp>& ops, std::vector<Pe
       VTRY(pb.finalize());
       VTRY(cudaToVccl(launchP2p(launchCtx(comm, s), pb.plan), "point-to-point launch"));
       VTRY(st.finish(s));
-      if (!evs.empty()) {
-        cudaEvent_t done;
-        cudaEventCreateWithFlags(&done, cudaEventDisableTiming);
-        cudaEventRecord(done, s);
-        for (size_t k = i; k < j; k++) cudaStreamWaitEvent(ops[k].stream, done, 0);
-        cudaEventDestroy(done);
-        for (cudaEvent_t ev : evs) cudaEventDestroy(ev);
+      if (!others.empty()) {
+        cudaEvent_t done = nullptr;
+        VTRY(cudaToVccl(cudaEventCreateWithFlags(&done, cudaEventDisableTiming), "event"));
+        evs.v.push_back(done);
+        VTRY(cudaToVccl(cudaEventRecord(done, s), "event record"));
+        for (cudaStream_t o : others) VTRY(cudaToVccl(cudaStreamWaitEvent(o, done, 0), "stream wait"));
       }
       if (anySync) waits->push_back({comm, s});
       i = j;

@@ -653,6 +653,42 @@ void nvlsPipeSweep(vcclComm_t c, int me, int n) {
   }
 }
 
+// A group whose Send and Recv sit on different streams runs as one kernel
+// on the first op's stream; the other stream must still be ordered after
+// it: a copy queued on the Recv's stream right after vcclGroupEnd reads the
+// received data, not what was there before.
+void twoStreamGroup(vcclComm_t c, int me, int n) {
+  if (n < 2) return;
+  const size_t cnt = 4u << 20;  // 16 MiB of fp32: the kernel outlasts the copy's launch
+  const int next = (me + 1) % n, prev = (me + n - 1) % n;
+  std::vector<float> h(cnt);
+  fill(h.data(), vcclFloat32, me, cnt);
+  float *send = nullptr, *recv = nullptr, *host = nullptr;
+  cudaMalloc(&send, cnt * 4);
+  cudaMalloc(&recv, cnt * 4);
+  cudaMallocHost(&host, cnt * 4);
+  cudaMemcpy(send, h.data(), cnt * 4, cudaMemcpyHostToDevice);
+  cudaMemset(recv, 0, cnt * 4);
+  cudaDeviceSynchronize();
+  cudaStream_t sa, sb;
+  cudaStreamCreateWithFlags(&sa, cudaStreamNonBlocking);
+  cudaStreamCreateWithFlags(&sb, cudaStreamNonBlocking);
+  EXPECT_OK(vcclGroupStart());
+  EXPECT_OK(vcclSendAsync(send, cnt, vcclFloat32, next, c, sa));
+  EXPECT_OK(vcclRecvAsync(recv, cnt, vcclFloat32, prev, c, sb));
+  EXPECT_OK(vcclGroupEnd());
+  cudaMemcpyAsync(host, recv, cnt * 4, cudaMemcpyDeviceToHost, sb);
+  cudaStreamSynchronize(sb);
+  cudaStreamSynchronize(sa);
+  for (size_t i = 0; i < cnt; i += 4099) EXPECT_NEAR(host[i], val(prev, i), vcclFloat32, "two-stream group recv", i);
+  EXPECT_NEAR(host[cnt - 1], val(prev, cnt - 1), vcclFloat32, "two-stream group recv", cnt - 1);
+  cudaStreamDestroy(sa);
+  cudaStreamDestroy(sb);
+  cudaFreeHost(host);
+  cudaFree(send);
+  cudaFree(recv);
+}
+
 // Paths added after the main matrix was validated on B200 run in their own
 // invocation (`test_collectives N --extended`), so a failure there cannot
 // hide the main matrix's result.
@@ -667,6 +703,7 @@ int rankMain(int me, int n, const vcclUniqueId& id, bool full) {
     nvlsPipeSweep(c, me, n);
     multiRound(c, me, n);
     windowTest(c, me, n);
+    twoStreamGroup(c, me, n);
     if (std::getenv("VCCL_GUARDS") != nullptr && n > 1) {
       unsigned long long bad = 0;
       EXPECT_OK(vcclxCheckGuards(c, &bad));
