@@ -612,3 +612,25 @@ def test_bindings_declare_every_header_function():
 
     h = lib()
     assert [n for n in names if not hasattr(h, n)] == []
+
+
+def test_standalone_base_matches_vllm_base():
+    """Without vLLM the communicator derives from a stand-in whose public
+    methods are those of vLLM's DeviceCommunicatorBase; VcclCommunicator
+    overrides every data-moving one."""
+    import inspect
+
+    from vkccl_b200.torch_comm import StandaloneCommunicatorBase, VcclCommunicator
+
+    vbase = pytest.importorskip("vllm.distributed.device_communicators.base_device_communicator")
+    base_methods = {m for m, _ in inspect.getmembers(vbase.DeviceCommunicatorBase, inspect.isfunction)
+                    if not m.startswith("_")}
+    ours = {m for m, _ in inspect.getmembers(VcclCommunicator, inspect.isfunction) if not m.startswith("_")}
+    standalone = {m for m, _ in inspect.getmembers(StandaloneCommunicatorBase, inspect.isfunction)
+                  if not m.startswith("_")}
+    assert base_methods <= ours | standalone, sorted(base_methods - ours - standalone)
+    for m in ("all_reduce", "all_gather", "all_gatherv", "reduce_scatter", "reduce_scatterv", "gather",
+              "broadcast", "send", "recv", "batch_isend_irecv", "dispatch", "combine", "destroy"):
+        assert m in VcclCommunicator.__dict__, m
+    init_params = set(inspect.signature(vbase.DeviceCommunicatorBase.__init__).parameters)
+    assert init_params <= set(inspect.signature(StandaloneCommunicatorBase.__init__).parameters)

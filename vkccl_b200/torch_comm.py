@@ -33,28 +33,49 @@ from torch.distributed import ProcessGroup
 
 from vkccl_b200 import comm as _c
 
+class StandaloneCommunicatorBase:
+    """Attribute-compatible stand-in for vLLM's DeviceCommunicatorBase, used
+    when vLLM is not installed (same constructor, attributes and default
+    methods)."""
+
+    def __init__(self, cpu_group: ProcessGroup, device: Optional[torch.device] = None,
+                 device_group: Optional[ProcessGroup] = None, unique_name: str = "",
+                 global_ranks: Optional[list] = None, global_world_size: Optional[int] = None,
+                 **_: Any) -> None:
+        self.cpu_group = cpu_group
+        self.device = device if device is not None else torch.device("cpu")
+        self.device_group = device_group
+        self.unique_name = unique_name
+        self.rank = dist.get_rank(cpu_group)
+        self.world_size = dist.get_world_size(cpu_group)
+        self.ranks = dist.get_process_group_ranks(cpu_group)
+        self.global_rank = dist.get_rank()
+        self.global_world_size = dist.get_world_size()
+        self.rank_in_group = dist.get_group_rank(cpu_group, self.global_rank)
+        self.is_ep_communicator = unique_name.split(":")[0] == "ep"
+        self.use_all2all = False  # dispatch/combine are this class's own kernels
+        self.all2all_backend = None
+        self.all2all_manager = None
+
+    def dispatch_router_logits(self, hidden_states: torch.Tensor, router_logits: torch.Tensor,
+                               is_sequence_parallel: bool = False,
+                               extra_tensors: Optional[list] = None):
+        """Pass-through, as in vLLM's base class."""
+        if extra_tensors is not None:
+            return hidden_states, router_logits, extra_tensors
+        return hidden_states, router_logits
+
+    def prepare_communication_buffer_for_model(self, model: torch.nn.Module) -> None:
+        """Nothing to prepare: the MoE staging buffers are the communicator's
+        symmetric workspace, allocated at init."""
+
+
 try:  # vLLM is optional
     from vllm.distributed.device_communicators.base_device_communicator import (
         DeviceCommunicatorBase,
     )
 except Exception:  # noqa: BLE001 - any import failure means "no vLLM"
-
-    class DeviceCommunicatorBase:  # type: ignore[no-redef]
-        """Attribute-compatible stand-in for vLLM's DeviceCommunicatorBase."""
-
-        def __init__(self, cpu_group: ProcessGroup, device: Optional[torch.device] = None,
-                     device_group: Optional[ProcessGroup] = None, unique_name: str = "",
-                     **_: Any) -> None:
-            self.cpu_group = cpu_group
-            self.device = device if device is not None else torch.device("cpu")
-            self.device_group = device_group
-            self.unique_name = unique_name
-            self.rank = dist.get_rank(cpu_group)
-            self.world_size = dist.get_world_size(cpu_group)
-            self.ranks = dist.get_process_group_ranks(cpu_group)
-            self.global_rank = dist.get_rank()
-            self.global_world_size = dist.get_world_size()
-            self.rank_in_group = dist.get_group_rank(cpu_group, self.global_rank)
+    DeviceCommunicatorBase = StandaloneCommunicatorBase  # type: ignore[misc,assignment]
 
 
 _TORCH_TO_VCCL = {
