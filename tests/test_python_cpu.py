@@ -634,3 +634,35 @@ def test_standalone_base_matches_vllm_base():
         assert m in VcclCommunicator.__dict__, m
     init_params = set(inspect.signature(vbase.DeviceCommunicatorBase.__init__).parameters)
     assert init_params <= set(inspect.signature(StandaloneCommunicatorBase.__init__).parameters)
+
+
+def test_batch_isend_irecv_uses_group_ranks():
+    """torch's P2POp holds the global rank in `peer` and the group's rank in
+    `group_peer`; the communicator must address vccl ranks by the latter (a
+    pipeline group of global ranks [0, 4] has vccl ranks 0 and 1)."""
+    from types import SimpleNamespace
+
+    import torch.distributed as dist
+
+    from vkccl_b200.torch_comm import VcclCommunicator
+
+    calls = []
+
+    class Recorder:
+        def send(self, t, peer, count, dtype):
+            calls.append(("send", peer))
+
+        def recv(self, t, peer, count, dtype):
+            calls.append(("recv", peer))
+
+    c = object.__new__(VcclCommunicator)
+    c.vccl = Recorder()
+    c.ranks = [0, 4]
+    t = torch.zeros(4)
+    ops = [SimpleNamespace(op=dist.isend, tensor=t, peer=4, group_peer=1),
+           SimpleNamespace(op=dist.irecv, tensor=t, peer=4, group_peer=1),
+           SimpleNamespace(op=dist.isend, tensor=t, peer=4)]  # no group_peer: global rank 4 -> group rank 1
+    c.batch_isend_irecv(ops)
+    assert calls == [("send", 1), ("recv", 1), ("send", 1)]
+    with pytest.raises(ValueError):
+        c.batch_isend_irecv([SimpleNamespace(op=dist.isend, tensor=t, peer=3)])

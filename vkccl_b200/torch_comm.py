@@ -224,12 +224,23 @@ class VcclCommunicator(DeviceCommunicatorBase):
         with _c.group():
             for op in p2p_ops:
                 t = op.tensor
-                peer = op.peer if hasattr(op, "peer") else op.group_peer
-                name = getattr(op.op, "__name__", str(op.op))
-                if "send" in name:
+                peer = self._group_peer(op)
+                if op.op is dist.isend or "send" in getattr(op.op, "__name__", str(op.op)):
                     self.vccl.send(t, peer, count=t.numel(), dtype=vccl_dtype(t))
                 else:
                     self.vccl.recv(t, peer, count=t.numel(), dtype=vccl_dtype(t))
+
+    def _group_peer(self, op) -> int:
+        """The op's peer as a rank of this group: torch's P2POp carries it as
+        `group_peer` (its `peer` is the global rank); an op with only `peer`
+        is read as torch reads it, a global rank."""
+        gp = getattr(op, "group_peer", None)
+        if gp is not None:
+            return int(gp)
+        peer = int(op.peer)
+        if peer not in self.ranks:
+            raise ValueError(f"global rank {peer} is not in this group {self.ranks}")
+        return self.ranks.index(peer)
 
     # -- fused tensor-parallel paths ---------------------------------------------
     def all_reduce_add_rms_norm(self, partial: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
