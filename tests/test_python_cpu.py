@@ -477,6 +477,21 @@ def test_single_rank_count_and_dtype_rules():
         comm.all_reduce(x, y, count=16, dtype=v.DataType.FLOAT32)
         with pytest.raises(ValueError):
             comm.all_reduce(12345, count=None, dtype=v.DataType.FLOAT32)  # raw address needs a count
+        # buffers of known size that are too small are refused before any copy
+        big, small = torch.arange(16, dtype=torch.float32), torch.zeros(8)
+        with pytest.raises(ValueError, match="receive"):
+            comm.all_reduce(big, small)
+        with pytest.raises(ValueError, match="receive"):
+            comm.all_gather(big, small)
+        with pytest.raises(ValueError, match="send"):
+            comm.reduce_scatter(small, big)
+        with pytest.raises(ValueError, match="receive"):
+            comm.all_to_all_v(big, [16], [0], small, [16], [0])
+        with pytest.raises(ValueError, match="recvcounts"):
+            comm.all_to_all_v(big, [16], [0], big, [], [0])
+        comm.all_gather(small, big, sendcount=8)  # sizes that fit still run
+        comm.all_to_all_v(big, [8], [8], small, [8], [0])
+        assert torch.equal(small, big[8:])
     finally:
         comm.destroy()
 

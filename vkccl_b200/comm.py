@@ -270,14 +270,25 @@ class Communicator:
             n = b.nbytes // TYPE_SIZE[DataType(dt)] // scale
         return b, int(n), int(dt)
 
+    @staticmethod
+    def _need(b: _Buf, elems: int, dt: int, what: str) -> None:
+        """Refuse a buffer of known size that is too small for the call (a
+        kernel would otherwise write or read past its end).  Raw addresses
+        and absent buffers (non-root ranks) carry no size and are not checked."""
+        need = int(elems) * TYPE_SIZE[DataType(dt)]
+        if b.nbytes and b.nbytes < need:
+            raise ValueError(f"{what} buffer holds {b.nbytes} bytes; the call needs {need}")
+
     def _stream(self, bufs: Sequence[_Buf], stream: Any) -> Optional[int]:
         """Stream handle for CUDA buffers, or None for the blocking host path."""
-        if not any(b.cuda for b in bufs):
+        cuda = [b for b in bufs if b.cuda]
+        if not cuda:
             return None
         if stream is None:
             import torch
 
-            return torch.cuda.current_stream().cuda_stream
+            # the buffers' device, which need not be the current one
+            return torch.cuda.current_stream(cuda[0].device).cuda_stream
         if isinstance(stream, int):
             return stream
         return stream.cuda_stream
@@ -292,6 +303,7 @@ class Communicator:
             recv = send
         s, n, dt = self._resolve(send, count, dtype, False)
         r, _, _ = self._resolve(recv, n, dt, True)
+        self._need(r, n, dt, "receive")
         st = self._stream([s, r], stream)
         L = lib()
         if st is None:
@@ -304,6 +316,7 @@ class Communicator:
                dtype: Optional[int] = None, op: Any = RedOp.SUM, stream: Any = None) -> None:
         s, n, dt = self._resolve(send, count, dtype, False)
         r = buffer_info(recv, True)
+        self._need(r, n, dt, "receive")
         st = self._stream([s, r], stream)
         L = lib()
         if st is None:
@@ -316,6 +329,7 @@ class Communicator:
                    dtype: Optional[int] = None, stream: Any = None) -> None:
         s, n, dt = self._resolve(send, sendcount, dtype, False)
         r, _, _ = self._resolve(recv, n, dt, True)
+        self._need(r, n * self.nranks, dt, "receive")
         st = self._stream([s, r], stream)
         L = lib()
         if st is None:
@@ -328,6 +342,7 @@ class Communicator:
                        dtype: Optional[int] = None, op: Any = RedOp.SUM, stream: Any = None) -> None:
         r, n, dt = self._resolve(recv, recvcount, dtype, True)
         s, _, _ = self._resolve(send, n, dt, False)
+        self._need(s, n * self.nranks, dt, "send")
         st = self._stream([s, r], stream)
         L = lib()
         if st is None:
@@ -341,6 +356,7 @@ class Communicator:
                   recv: Any = None, stream: Any = None) -> None:
         b, n, dt = self._resolve(buf, count, dtype, True)
         r = b if recv is None else self._resolve(recv, n, dt, True)[0]
+        self._need(r, n, dt, "receive")
         st = self._stream([b, r], stream)
         L = lib()
         if st is None:
@@ -353,6 +369,7 @@ class Communicator:
                dtype: Optional[int] = None, stream: Any = None) -> None:
         s, n, dt = self._resolve(send, sendcount, dtype, False)
         r = buffer_info(recv, True)
+        self._need(r, n * self.nranks, dt, "receive")
         st = self._stream([s, r], stream)
         L = lib()
         if st is None:
@@ -364,6 +381,7 @@ class Communicator:
                 dtype: Optional[int] = None, stream: Any = None) -> None:
         r, n, dt = self._resolve(recv, recvcount, dtype, True)
         s = buffer_info(send, False)
+        self._need(s, n * self.nranks, dt, "send")
         st = self._stream([s, r], stream)
         L = lib()
         if st is None:
@@ -376,6 +394,8 @@ class Communicator:
                    stream: Any = None) -> None:
         s, n, dt = self._resolve(send, count, dtype, False, scale=self.nranks)
         r, _, _ = self._resolve(recv, n, dt, True)
+        self._need(s, n * self.nranks, dt, "send")
+        self._need(r, n * self.nranks, dt, "receive")
         st = self._stream([s, r], stream)
         L = lib()
         if st is None:
@@ -391,8 +411,14 @@ class Communicator:
         dt = dtype if dtype is not None else (s.dtype if s.dtype is not None else r.dtype)
         if dt is None:
             raise ValueError("dtype could not be inferred; pass dtype=")
+        for name, v in (("sendcounts", sendcounts), ("sdispls", sdispls), ("recvcounts", recvcounts),
+                        ("rdispls", rdispls)):
+            if len(v) != self.nranks:
+                raise ValueError(f"{name} has {len(v)} entries; the communicator has {self.nranks} ranks")
         arr = ctypes.c_size_t * self.nranks
         sc, sd, rc, rd = (arr(*[int(x) for x in v]) for v in (sendcounts, sdispls, recvcounts, rdispls))
+        self._need(s, max((sd[i] + sc[i] for i in range(self.nranks) if sc[i]), default=0), int(dt), "send")
+        self._need(r, max((rd[i] + rc[i] for i in range(self.nranks) if rc[i]), default=0), int(dt), "receive")
         st = self._stream([s, r], stream)
         L = lib()
         if st is None:
