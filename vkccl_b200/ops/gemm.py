@@ -14,8 +14,8 @@ from vkccl_b200._lib import lib
 from vkccl_b200.comm import _check
 
 
-def _stream() -> int:
-    return torch.cuda.current_stream().cuda_stream
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
 
 
 def _ok(t: torch.Tensor, name: str) -> None:
@@ -30,10 +30,16 @@ def gemm_bf16(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None)
     _ok(w, "w")
     m, k = a.shape
     n = w.shape[0]
+    if tuple(w.shape) != (n, k):
+        raise ValueError(f"w has shape {tuple(w.shape)}; expected ({n}, {k})")
     if out is None:
         out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
+    _ok(out, "out")
+    if tuple(out.shape) != (m, n):
+        raise ValueError(f"out has shape {tuple(out.shape)}; expected ({m}, {n})")
     with torch.cuda.device(a.device):  # the library launches on the thread's current device
-        _check(lib().vcclGemmBf16(a.data_ptr(), w.data_ptr(), out.data_ptr(), m, n, k, _stream()), "vcclGemmBf16")
+        _check(lib().vcclGemmBf16(a.data_ptr(), w.data_ptr(), out.data_ptr(), m, n, k, _stream(a)),
+               "vcclGemmBf16")
     return out
 
 
@@ -52,9 +58,14 @@ def gemm_silu_mul(a: torch.Tensor, w_gu: torch.Tensor, out: torch.Tensor | None 
     _ok(w_gu, "w_gu")
     m, k = a.shape
     n = w_gu.shape[0]
+    if tuple(w_gu.shape) != (n, k):
+        raise ValueError(f"w_gu has shape {tuple(w_gu.shape)}; expected ({n}, {k})")
     if out is None:
         out = torch.empty((m, n // 2), dtype=torch.bfloat16, device=a.device)
+    _ok(out, "out")
+    if tuple(out.shape) != (m, n // 2):
+        raise ValueError(f"out has shape {tuple(out.shape)}; expected ({m}, {n // 2})")
     with torch.cuda.device(a.device):
-        _check(lib().vcclGemmSiluMul(a.data_ptr(), w_gu.data_ptr(), out.data_ptr(), m, n, k, _stream()),
+        _check(lib().vcclGemmSiluMul(a.data_ptr(), w_gu.data_ptr(), out.data_ptr(), m, n, k, _stream(a)),
                "vcclGemmSiluMul")
     return out

@@ -35,8 +35,8 @@ from vkccl_b200._lib import lib
 from vkccl_b200.comm import _check
 
 
-def _stream() -> int:
-    return torch.cuda.current_stream().cuda_stream
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
 
 
 @dataclass
@@ -86,7 +86,7 @@ def moe_dispatch(comm, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: to
     count = torch.zeros((1,), dtype=torch.int32, device=dev)
     _check(lib().vcclMoeDispatchFp8(x.data_ptr(), ids.data_ptr(), w.data_ptr(), recv_x.data_ptr(),
                                     recv_meta.data_ptr(), recv_w.data_ptr(), count.data_ptr(), t, h, topk,
-                                    num_experts, capacity, comm._comm, _stream()),
+                                    num_experts, capacity, comm._comm, _stream(x)),
            "vcclMoeDispatchFp8", comm._comm)
     return MoeDispatch(recv_x, recv_meta, recv_w, count, t, topk, capacity, num_experts, comm.rank,
                        num_experts // n)
@@ -94,8 +94,9 @@ def moe_dispatch(comm, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: to
 
 def moe_combine(comm, d: MoeDispatch, expert_out: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     h = d.recv_x.shape[1]
-    if expert_out.dtype != torch.bfloat16 or not expert_out.is_contiguous() or expert_out.shape[-1] != h:
-        raise ValueError("expert_out must be a contiguous bf16 [rows, H] tensor in the received row order")
+    if (expert_out.dtype != torch.bfloat16 or not expert_out.is_cuda or not expert_out.is_contiguous()
+            or expert_out.dim() != 2 or expert_out.shape[-1] != h):
+        raise ValueError("expert_out must be a contiguous bf16 [rows, H] CUDA tensor in the received row order")
     if expert_out.shape[0] < d.capacity:
         # rows past the received count are never read, but the kernels index
         # up to the device-side count, so give them a capacity-sized buffer
@@ -104,9 +105,11 @@ def moe_combine(comm, d: MoeDispatch, expert_out: torch.Tensor, out: Optional[to
         expert_out = full
     if out is None:
         out = torch.empty((d.tokens, h), dtype=torch.bfloat16, device=expert_out.device)
+    if out.dtype != torch.bfloat16 or not out.is_cuda or not out.is_contiguous() or tuple(out.shape) != (d.tokens, h):
+        raise ValueError(f"out must be a contiguous bf16 CUDA tensor of shape {(d.tokens, h)}")
     _check(lib().vcclMoeCombine(expert_out.data_ptr(), d.recv_meta.data_ptr(), d.recv_w.data_ptr(),
                                 d.recv_count.data_ptr(), out.data_ptr(), d.tokens, h, d.topk, d.capacity,
-                                comm._comm, _stream()),
+                                comm._comm, _stream(expert_out)),
            "vcclMoeCombine", comm._comm)
     return out
 
