@@ -200,6 +200,7 @@ extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, voi
   }
   cudaSetDevice(comm->dev->device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  OrderedLaunch ord(comm->dev.get(), s);
   const int bnEnv = static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN"));
   cudaError_t e;
   if (n == 1) {

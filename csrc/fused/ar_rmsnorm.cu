@@ -301,6 +301,7 @@ extern "C" vcclResult_t vcclAllReduceAddRMSNorm(const void* partial, void* resid
   }
   cudaSetDevice(comm->dev->device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  OrderedLaunch ord(comm->dev.get(), s);
   dev::NormArgs a{static_cast<const char*>(partial), static_cast<char*>(residual), static_cast<const char*>(weight),
                   static_cast<char*>(out), static_cast<int>(rows), static_cast<int>(hidden), eps};
   const int n = comm->nranks;

@@ -258,6 +258,7 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
   }
   cudaSetDevice(comm->dev->device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  OrderedLaunch ord(comm->dev.get(), s);
   const int bnEnv = static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN"));
   if (n == 1) {
     gemm::EpiStore epi{static_cast<__nv_bfloat16*>(out), N};

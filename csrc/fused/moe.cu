@@ -641,6 +641,7 @@ extern "C" vcclResult_t vcclMoeDispatchFp8(const void* x, const int* topkIds, co
   }
   cudaSetDevice(comm->dev->device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  OrderedLaunch ord(comm->dev.get(), s);
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   auto* rx = static_cast<__nv_bfloat16*>(recvX);
   if (n == 1) {
@@ -684,6 +685,7 @@ extern "C" vcclResult_t vcclMoeCombine(const void* expertOut, const int* recvMet
   }
   cudaSetDevice(comm->dev->device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  OrderedLaunch ord(comm->dev.get(), s);
   const auto* y = static_cast<const __nv_bfloat16*>(expertOut);
   auto* o = static_cast<__nv_bfloat16*>(out);
   if (comm->nranks == 1) {

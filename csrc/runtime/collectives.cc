@@ -624,6 +624,7 @@ vcclResult_t launchOps(vcclComm_t comm, std::vector<HostOp>& ops, std::vector<Pe
     Staging st;
     const Window* a2aWin = h.kind == Kind::AllToAllv ? windowForAllToAll(h) : nullptr;
     if (a2aWin != nullptr) {
+      OrderedLaunch ord(comm->dev.get(), h.stream);
       VTRY(prepareBuffers(h, st));  // a host send buffer is staged; the receive buffer is device memory
       VTRY(windowAllToAll(h, a2aWin));
       VTRY(st.finish(h.stream));
@@ -675,6 +676,7 @@ vcclResult_t launchOps(vcclComm_t comm, std::vector<HostOp>& ops, std::vector<Pe
           VTRY(cudaToVccl(cudaStreamWaitEvent(s, ev, 0), "stream wait"));
         }
       }
+      OrderedLaunch ord(comm->dev.get(), s);
       PlanBuilder pb;
       for (size_t k = i; k < j; k++) {
         ops[k].stream = s;
@@ -696,6 +698,7 @@ vcclResult_t launchOps(vcclComm_t comm, std::vector<HostOp>& ops, std::vector<Pe
       i = j;
       continue;
     }
+    OrderedLaunch ord(comm->dev.get(), h.stream);
     VTRY(prepareBuffers(h, st));
     VTRY(launchColl(h));
     VTRY(st.finish(h.stream));

@@ -40,6 +40,17 @@ struct SymmetricBuffer {
   bool mcBound = false;
 };
 
+// Kernels of one communicator never overlap, whatever streams they are
+// issued on: they share the workspaces and barrier counters, and the fused
+// kernels hold every SM while they wait for the peers.  The event is
+// recorded after each eager launch; a launch on another stream first waits
+// for it.
+struct LaunchOrder {
+  cudaEvent_t ev = nullptr;
+  cudaStream_t stream = nullptr;  // stream of the last eager launch
+  bool valid = false;
+};
+
 struct DeviceState {
   int device = -1;
   CUdevice cuDevice = 0;
@@ -71,6 +82,26 @@ struct DeviceState {
   int nvlsPieces = 4;              // pieces of a pipelined NVLS all-reduce
   bool windowsEnabled = true;      // zero-copy kernels for buffers in registered windows (VCCL_WINDOW)
   int windowNvlsMinRanks = 3;      // window collectives go through the switch from this many ranks
+  LaunchOrder order;
+  bool orderLaunches = true;       // VCCL_LAUNCH_ORDER=0: the application keeps one stream per communicator
+};
+
+// Scope of one API call's launches on stream `s`: on entry `s` waits for the
+// communicator's previous launch when that went to another stream, on exit
+// the call's work is recorded as the new previous launch.  Streams under
+// graph capture are left alone (a capture may not wait on work outside it;
+// a graph orders its own nodes, and the application orders graph launches).
+class OrderedLaunch {
+ public:
+  OrderedLaunch(DeviceState* ds, cudaStream_t s);
+  ~OrderedLaunch();
+  OrderedLaunch(const OrderedLaunch&) = delete;
+  OrderedLaunch& operator=(const OrderedLaunch&) = delete;
+
+ private:
+  DeviceState* ds_;
+  cudaStream_t s_;
+  bool eager_ = false;
 };
 
 struct CustomOp {

@@ -252,6 +252,7 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
   ds->nvlsPipeMin = envBytes("VCCL_NVLS_PIPE_MIN", 0);
   ds->nvlsPieces = static_cast<int>(envLong("VCCL_NVLS_PIECES", 4));
   ds->windowsEnabled = envLong("VCCL_WINDOW", 1) != 0;
+  ds->orderLaunches = envLong("VCCL_LAUNCH_ORDER", 1) != 0;
   // Per GPU, the switch moves about S each way for a window all-reduce of
   // S bytes against 2 (n-1)/n S for the point-to-point kernel.
   ds->windowNvlsMinRanks = static_cast<int>(envLong("VCCL_WINDOW_NVLS_MIN_RANKS", 3));
@@ -429,6 +430,37 @@ vcclResult_t deviceStateEnsureMoe(DeviceState* ds, Bootstrap* bs, size_t bytes) 
   return vcclSuccess;
 }
 
+OrderedLaunch::OrderedLaunch(DeviceState* ds, cudaStream_t s) : ds_(ds), s_(s) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (ds == nullptr || !ds->orderLaunches) return;
+  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) {
+    cudaGetLastError();  // e.g. the legacy stream while another stream captures
+    return;
+  }
+  if (cs != cudaStreamCaptureStatusNone) return;
+  eager_ = true;
+  const LaunchOrder& o = ds->order;
+  if (o.valid && o.stream != s && cudaStreamWaitEvent(s, o.ev, 0) != cudaSuccess) cudaGetLastError();
+}
+
+OrderedLaunch::~OrderedLaunch() {
+  if (!eager_) return;
+  LaunchOrder& o = ds_->order;
+  if (o.ev == nullptr && cudaEventCreateWithFlags(&o.ev, cudaEventDisableTiming) != cudaSuccess) {
+    o.ev = nullptr;
+    o.valid = false;
+    cudaGetLastError();
+    return;
+  }
+  if (cudaEventRecord(o.ev, s_) == cudaSuccess) {
+    o.stream = s_;
+    o.valid = true;
+  } else {
+    o.valid = false;
+    cudaGetLastError();
+  }
+}
+
 void deviceStateDestroy(DeviceState* ds, Bootstrap* bs, bool peersAlive) {
   if (ds == nullptr) return;
   const DriverApi* d = driverApi();
@@ -452,6 +484,8 @@ void deviceStateDestroy(DeviceState* ds, Bootstrap* bs, bool peersAlive) {
   if (ds->hostStatus) cudaFreeHost(ds->hostStatus);
   if (ds->hostAbort) cudaFreeHost(ds->hostAbort);
   if (ds->stream) cudaStreamDestroy(ds->stream);
+  if (ds->order.ev) cudaEventDestroy(ds->order.ev);
+  ds->order = LaunchOrder{};
   ds->hostStatus = ds->hostAbort = nullptr;
   ds->stream = nullptr;
 }

@@ -689,6 +689,38 @@ void twoStreamGroup(vcclComm_t c, int me, int n) {
   cudaFree(recv);
 }
 
+// Launches of one communicator on two streams run one after the other in
+// issue order: the second all-reduce reads the first one's output without
+// any synchronisation by the caller.
+void twoStreamOrder(vcclComm_t c, int me, int n) {
+  const size_t cnt = 4u << 20;
+  std::vector<float> h(cnt);
+  fill(h.data(), vcclFloat32, me, cnt);
+  float *x = nullptr, *y = nullptr, *z = nullptr;
+  cudaMalloc(&x, cnt * 4);
+  cudaMalloc(&y, cnt * 4);
+  cudaMalloc(&z, cnt * 4);
+  cudaMemcpy(x, h.data(), cnt * 4, cudaMemcpyHostToDevice);
+  cudaMemset(y, 0, cnt * 4);
+  cudaMemset(z, 0, cnt * 4);
+  cudaDeviceSynchronize();
+  cudaStream_t sa, sb;
+  cudaStreamCreateWithFlags(&sa, cudaStreamNonBlocking);
+  cudaStreamCreateWithFlags(&sb, cudaStreamNonBlocking);
+  EXPECT_OK(vcclAllReduceAsync(x, y, cnt, vcclFloat32, vcclSum, c, sa));
+  EXPECT_OK(vcclAllReduceAsync(y, z, cnt, vcclFloat32, vcclSum, c, sb));
+  cudaStreamSynchronize(sb);
+  cudaStreamSynchronize(sa);
+  cudaMemcpy(h.data(), z, cnt * 4, cudaMemcpyDeviceToHost);
+  for (size_t i = 0; i < cnt; i += 4099)
+    EXPECT_NEAR(h[i], n * expect(vcclSum, n, i), vcclFloat32, "two-stream order", i);
+  cudaStreamDestroy(sa);
+  cudaStreamDestroy(sb);
+  cudaFree(x);
+  cudaFree(y);
+  cudaFree(z);
+}
+
 // Paths added after the main matrix was validated on B200 run in their own
 // invocation (`test_collectives N --extended`), so a failure there cannot
 // hide the main matrix's result.
@@ -704,6 +736,7 @@ int rankMain(int me, int n, const vcclUniqueId& id, bool full) {
     multiRound(c, me, n);
     windowTest(c, me, n);
     twoStreamGroup(c, me, n);
+    twoStreamOrder(c, me, n);
     if (std::getenv("VCCL_GUARDS") != nullptr && n > 1) {
       unsigned long long bad = 0;
       EXPECT_OK(vcclxCheckGuards(c, &bad));

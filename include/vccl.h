@@ -15,6 +15,9 @@
  * device pointers and host pointers are accepted; host buffers are staged
  * through device memory.  The *Async variants (additions) take a CUDA stream,
  * accept device pointers only, and return immediately (NCCL semantics).
+ * The kernels of one communicator run one after another in issue order even
+ * when the calls name different streams (a call on a new stream waits for
+ * the communicator's previous call; not applied inside CUDA-graph capture).
  */
 #ifndef VCCL_H_
 #define VCCL_H_

@@ -3,7 +3,8 @@
 `--extended`): the pipelined NVLS all-reduce, messages larger than the
 staging region (multi-round two-shot / NVLS / pipelined NVLS) and the
 zero-copy window collectives, a grouped Send/Recv whose ops sit on two
-streams (the second stream must be ordered after the kernel), with guard regions past every workspace that
+streams (the second stream must be ordered after the kernel), two all-reduces
+on two streams where the second reads the first's output, with guard regions past every workspace that
 each rank checks for out-of-bounds writes at the end, and vcclCommAbort from
 another thread while a kernel waits for a rank that skipped the call.  Kept apart from the main matrix so that a
 failure here cannot hide the main matrix's result under `pytest -x`."""
