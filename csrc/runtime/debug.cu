@@ -77,6 +77,7 @@ extern "C" vcclResult_t vcclxBarrierBench(vcclComm_t comm, int iters, int nblock
   cudaSetDevice(comm->dev->device);
   cudaStream_t s = comm->dev->stream;
   const vccl::dev::DevComm& dc = comm->dev->dc;
+  vccl::OrderedLaunch ord(comm->dev.get(), s);  // after the communicator's earlier kernels
   cudaEvent_t a, b;
   cudaEventCreate(&a);
   cudaEventCreate(&b);
