@@ -502,7 +502,13 @@ vcclResult_t vcclMemFree(void* ptr) {
     return vcclSuccess;
   }
   const vccl::DriverApi* d = vccl::driverApi();
+  // Kernels still using the memory finish first (on the allocation's device,
+  // which need not be the caller's current one).
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (cur != a.dev) cudaSetDevice(a.dev);
   cudaDeviceSynchronize();
+  if (cur != a.dev && cur >= 0) cudaSetDevice(cur);
   CUdeviceptr va = reinterpret_cast<CUdeviceptr>(ptr);
   d->memUnmap(va, a.bytes);
   d->memAddressFree(va, a.bytes);
