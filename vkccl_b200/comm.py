@@ -205,17 +205,19 @@ class _DeviceAlloc:
 
 
 def mem_alloc_tensor(shape: Sequence[int], dtype: Any, device: Any = None):
-    """A torch tensor on the current CUDA device backed by vcclMemAlloc
+    """A torch tensor on `device` (default: the current CUDA device) backed by vcclMemAlloc
     memory (exportable, so it can be registered as a window).  Deregister any
     window on it before the last view of the tensor goes away."""
     import math
 
     import torch
 
-    if device is not None:
-        torch.cuda.set_device(torch.device(device))
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
     nbytes = max(1, math.prod(shape)) * torch.empty((), dtype=dtype).element_size()
-    raw = torch.as_tensor(_DeviceAlloc(nbytes), device="cuda")
+    with torch.cuda.device(dev):  # vcclMemAlloc allocates on the current device; the caller's is restored
+        raw = torch.as_tensor(_DeviceAlloc(nbytes), device=dev)
     return raw.view(dtype)[: math.prod(shape)].view(*shape)
 
 
