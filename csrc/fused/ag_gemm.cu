@@ -199,6 +199,7 @@ extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, voi
     return vcclInvalidUsage;
   }
   cudaSetDevice(comm->dev->device);
+  if (!devicePointers(comm->dev->device, {xShard, W, out}, "vcclAllGatherGemm")) return vcclInvalidArgument;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   OrderedLaunch ord(comm->dev.get(), s);
   const int bnEnv = static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN"));

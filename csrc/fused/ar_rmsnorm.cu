@@ -300,6 +300,7 @@ extern "C" vcclResult_t vcclAllReduceAddRMSNorm(const void* partial, void* resid
     return vcclInvalidUsage;
   }
   cudaSetDevice(comm->dev->device);
+  if (!devicePointers(comm->dev->device, {partial, residual, weight, out}, "vcclAllReduceAddRMSNorm")) return vcclInvalidArgument;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   OrderedLaunch ord(comm->dev.get(), s);
   dev::NormArgs a{static_cast<const char*>(partial), static_cast<char*>(residual), static_cast<const char*>(weight),

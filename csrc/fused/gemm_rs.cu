@@ -257,6 +257,7 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
     return vcclInvalidUsage;
   }
   cudaSetDevice(comm->dev->device);
+  if (!devicePointers(comm->dev->device, {A, W, out}, "vcclGemmReduceScatter")) return vcclInvalidArgument;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   OrderedLaunch ord(comm->dev.get(), s);
   const int bnEnv = static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN"));

@@ -640,6 +640,8 @@ extern "C" vcclResult_t vcclMoeDispatchFp8(const void* x, const int* topkIds, co
     return vcclInvalidUsage;
   }
   cudaSetDevice(comm->dev->device);
+  if (!devicePointers(comm->dev->device, {x, topkIds, topkW, recvX, recvMeta, recvW, recvCount}, "vcclMoeDispatchFp8"))
+    return vcclInvalidArgument;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   OrderedLaunch ord(comm->dev.get(), s);
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
@@ -684,6 +686,8 @@ extern "C" vcclResult_t vcclMoeCombine(const void* expertOut, const int* recvMet
     return vcclInvalidUsage;
   }
   cudaSetDevice(comm->dev->device);
+  if (!devicePointers(comm->dev->device, {expertOut, recvMeta, recvW, recvCount, out}, "vcclMoeCombine"))
+    return vcclInvalidArgument;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   OrderedLaunch ord(comm->dev.get(), s);
   const auto* y = static_cast<const __nv_bfloat16*>(expertOut);

@@ -14,6 +14,7 @@
 
 #include <atomic>
 #include <cstdint>
+#include <initializer_list>
 #include <memory>
 #include <mutex>
 #include <string>
@@ -91,6 +92,12 @@ struct DeviceState {
 // the call's work is recorded as the new previous launch.  Streams under
 // graph capture are left alone (a capture may not wait on work outside it;
 // a graph orders its own nodes, and the application orders graph launches).
+// Every pointer of `ptrs` is device (or managed) memory of `device`.  The
+// fused entry points refuse anything else before a kernel or a TMA map would
+// fault on it (VCCL_CHECK_POINTERS=0 skips the check: one
+// cudaPointerGetAttributes per pointer and call).
+bool devicePointers(int device, std::initializer_list<const void*> ptrs, const char* what);
+
 class OrderedLaunch {
  public:
   OrderedLaunch(DeviceState* ds, cudaStream_t s);

@@ -430,6 +430,24 @@ vcclResult_t deviceStateEnsureMoe(DeviceState* ds, Bootstrap* bs, size_t bytes) 
   return vcclSuccess;
 }
 
+bool devicePointers(int device, std::initializer_list<const void*> ptrs, const char* what) {
+  static const bool check = envLong("VCCL_CHECK_POINTERS", 1) != 0;
+  if (!check) return true;
+  int i = 0;
+  for (const void* p : ptrs) {
+    cudaPointerAttributes at;
+    bool ok = p != nullptr && cudaPointerGetAttributes(&at, p) == cudaSuccess &&
+              ((at.type == cudaMemoryTypeDevice && at.device == device) || at.type == cudaMemoryTypeManaged);
+    if (!ok) {
+      cudaGetLastError();
+      VERR("%s: pointer argument %d is not device memory of CUDA device %d", what, i, device);
+      return false;
+    }
+    i++;
+  }
+  return true;
+}
+
 OrderedLaunch::OrderedLaunch(DeviceState* ds, cudaStream_t s) : ds_(ds), s_(s) {
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   if (ds == nullptr || !ds->orderLaunches) return;
