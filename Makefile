@@ -8,7 +8,6 @@ ARCH      ?= -gencode arch=compute_100a,code=sm_100a
 OUT       := vkccl_b200/_native
 OBJ       := $(OUT)/obj
 BIN       := $(OUT)/bin
-CUTLASS_INC ?= $(shell python3 -c "import os,site;print(os.path.join(site.getsitepackages()[0],'flashinfer','data','cutlass','include'))" 2>/dev/null)
 
 NVFLAGS := $(ARCH) -O3 -lineinfo -std=c++17 -Xcompiler -fPIC -Xcompiler -Wall \
            -Iinclude -Icsrc -I$(CUDA_HOME)/include --expt-relaxed-constexpr \
@@ -32,7 +31,7 @@ $(OBJ)/%.cc.o: csrc/%.cc $(HDRS)
 
 $(OBJ)/%.cu.o: csrc/%.cu $(HDRS)
 	@mkdir -p $(dir $@)
-	$(NVCC) $(NVFLAGS) -I$(CUTLASS_INC) -c $< -o $@
+	$(NVCC) $(NVFLAGS) -c $< -o $@
 
 $(OUT)/libvccl.so: $(LIB_OBJ)
 	$(NVCC) $(ARCH) -shared -o $@ $^ $(LDFLAGS)

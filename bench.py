@@ -217,28 +217,42 @@ NVLINK_GBS = 770.0  # measured peer copy, GB/s per direction per GPU
 
 
 def measured_peaks():
-    """bf16 sustained TFLOP/s and HBM GB/s measured on this pool, or the stated fallback."""
+    """bf16 burst and sustained TFLOP/s and HBM GB/s measured on this pool,
+    or the stated fallback."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             d = json.load(f)
-        return float(d["bf16_tflops_sustained"]), float(d["hbm_gbs"]), "measured"
+        return {"burst": float(d["bf16_tflops"]), "sustained": float(d["bf16_tflops_sustained"]),
+                "hbm": float(d["hbm_gbs"]), "src": "measured"}
     except (OSError, KeyError, ValueError):
-        return 1400.0, 6650.0, "fallback"
+        return {"burst": 1590.0, "sustained": 1400.0, "hbm": 6650.0, "src": "fallback"}
 
 
 def roofline(flops, tokens, world, measured_us):
     """The layer's roofline on one GPU: the slower of its GEMM FLOPs at the
-    sustained bf16 peak and the bytes that must cross NVLink (all-gather in,
+    bf16 peak and the bytes that must cross NVLink (all-gather in,
     reduce-scatter out: (n-1)/n of the [T, 4096] bf16 activations each way)
-    at the measured per-direction link bandwidth."""
-    tflops, _, src = measured_peaks()
-    compute_us = flops / world / (tflops * 1e12) * 1e6
+    at the measured per-direction link bandwidth.
+
+    The headline fraction divides by the BURST GEMM peak: the timed region
+    is K steps of a few milliseconds with an L2 flush between them, far
+    shorter than the seconds-long loop the sustained figure comes from.  The
+    fraction against the sustained (power-capped) peak is reported beside it.
+    """
+    pk = measured_peaks()
     link_bytes = (world - 1) / world * tokens * HIDDEN * 2 if world > 1 else 0.0
     link_us = link_bytes / (NVLINK_GBS * 1e9) * 1e6
-    bound = max(compute_us, link_us)
-    return {"compute_us": round(compute_us, 1), "nvlink_us": round(link_us, 1),
-            "bound": "compute" if compute_us >= link_us else "nvlink",
-            "fraction": round(bound / measured_us, 3), "peaks": src}
+    out = {"nvlink_us": round(link_us, 1), "peaks": pk["src"]}
+    for name in ("burst", "sustained"):
+        compute_us = flops / world / (pk[name] * 1e12) * 1e6
+        bound = max(compute_us, link_us)
+        if name == "burst":
+            out.update(compute_us=round(compute_us, 1), bound="compute" if compute_us >= link_us else "nvlink",
+                       fraction=round(bound / measured_us, 3))
+        else:
+            out.update(compute_us_sustained=round(compute_us, 1), fraction_sustained=round(bound / measured_us, 3))
+    out["rule"] = "fraction: burst bf16 peak (short timed region); fraction_sustained: power-capped peak"
+    return out
 
 
 def breakdown(mlp, x, world, measure):
@@ -357,6 +371,13 @@ def run_reference(args) -> int:
             "config": config(args, world, "fp32 (reference host path: torch CPU GEMMs + vccl TCP collectives)",
                              l2="not applicable (host path)"),
             "timing": "host wall clock, mean of K steps, max over ranks (the reference has no device path)",
+            # The reference's public path takes host tensors and returns host
+            # tensors, so its end-to-end number is the same host-to-host step
+            # time, with no device copies at all.
+            "e2e": {"value": round(us, 1), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0,
+                    "api": "vccl.torch_comm.VcclCommunicator all_gather / reduce_scatter + torch CPU GEMMs "
+                           "(host tensors in, host tensors out)"},
+            "gpu_launches": 0,
         }), flush=True)
     comm.destroy()
     dist.destroy_process_group()

@@ -113,9 +113,16 @@ SplitPlan planSplitK(int M, int N, int K) {
 
 namespace {
 __global__ void __launch_bounds__(256) splitReduceKernel(const float4* ws, int splits, size_t n4, size_t stride4,
-                                                         uint2* out) {
+                                                         uint2* out, const volatile int* abortWord) {
+  // The GEMM that wrote the partials abandoned its tiles: the partials are
+  // stale, so the output is poisoned with NaN instead of summed.
+  const bool poison = abortWord != nullptr && *abortWord != 0;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    if (poison) {
+      out[i] = make_uint2(0x7fc07fc0u, 0x7fc07fc0u);
+      continue;
+    }
     float4 a = ws[i];
     for (int sp = 1; sp < splits; sp++) {
       const float4 b = ws[sp * stride4 + i];
@@ -165,13 +172,14 @@ cudaError_t launchSplitReduceSilu(const float* ws, int splits, int M, int N, voi
   return cudaGetLastError();
 }
 
-cudaError_t launchSplitReduce(const float* ws, int splits, size_t elems, void* out, cudaStream_t st) {
+cudaError_t launchSplitReduce(const float* ws, int splits, size_t elems, void* out, cudaStream_t st,
+                              const volatile int* abortWord) {
   const size_t n4 = elems / 4;
   size_t blocks = (n4 + 255) / 256;
   if (blocks > static_cast<size_t>(smCount()) * 4) blocks = static_cast<size_t>(smCount()) * 4;
   if (blocks == 0) blocks = 1;
   splitReduceKernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(reinterpret_cast<const float4*>(ws), splits, n4,
-                                                                   n4, static_cast<uint2*>(out));
+                                                                   n4, static_cast<uint2*>(out), abortWord);
   return cudaGetLastError();
 }
 
@@ -404,7 +412,7 @@ vcclResult_t gemmEntry(const char* what, const void* A, const void* W, void* C, 
   gemm::releaseScratch(sc);
   if (e != cudaSuccess) {
     VERR("%s: %s", what, cudaGetErrorString(e));
-    return vcclInvalidArgument;
+    return gemm::launchResult(e);
   }
   return vcclSuccess;
 }

@@ -8,6 +8,8 @@
 #include <cstdint>
 #include <cstdlib>
 
+#include "vccl.h"
+
 namespace vccl {
 namespace gemm {
 
@@ -69,7 +71,18 @@ cudaError_t gemmAuto(const void* A, const void* W, void* C, int M, int N, int K,
 cudaError_t launchSplitReduceSilu(const float* ws, int splits, int M, int N, void* out, cudaStream_t st);
 
 // out[i] = bf16(sum over s < splits of ws[s * elems + i]); elems % 4 == 0.
-cudaError_t launchSplitReduce(const float* ws, int splits, size_t elems, void* out, cudaStream_t st);
+// With abortWord (a word the GEMM sets when it abandons its tiles) set when
+// the reduction runs, out is filled with NaN instead.
+cudaError_t launchSplitReduce(const float* ws, int splits, size_t elems, void* out, cudaStream_t st,
+                              const volatile int* abortWord = nullptr);
+
+// The result code of a failed GEMM launch: vcclInvalidArgument when the
+// arguments could not be described to the hardware (a tensor map the driver
+// refused, a split the shape cannot take: cudaErrorInvalidValue), otherwise
+// vcclUnhandledError (a launch or runtime failure, not the caller's mistake).
+inline vcclResult_t launchResult(cudaError_t e) {
+  return e == cudaErrorInvalidValue ? vcclInvalidArgument : vcclUnhandledError;
+}
 
 inline long envLongGemm(const char* name) {
   const char* v = std::getenv(name);

@@ -6,6 +6,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "fused/gemm_host.h"
 #include "kernels/gemm_sm100.cuh"
 
@@ -17,13 +19,14 @@ cudaError_t launchT(const CUtensorMap& ma, const CUtensorMap& mb, const GemmShap
                     const Hooks& hooks, int grid, cudaStream_t st, int* flag) {
   using L = Smem<BN, STAGES, 4 * Hooks::kEpiGroups>;
   auto kern = gemmKernel<BN, STAGES, Epi, Hooks>;
-  static unsigned long long attrDone = 0;  // one bit per device
+  static std::atomic<unsigned long long> attrDone{0};  // one bit per device; threads of any device
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(attrDone & (1ull << (dev & 63)))) {
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(attrDone.load(std::memory_order_acquire) & bit)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     if (e != cudaSuccess) return e;
-    attrDone |= 1ull << (dev & 63);
+    attrDone.fetch_or(bit, std::memory_order_release);
   }
   kern<<<grid, ctaThreads<Hooks>(), L::kBytes, st>>>(ma, mb, s, epi, hooks, flag);
   return cudaGetLastError();

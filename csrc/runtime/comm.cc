@@ -464,7 +464,12 @@ vcclResult_t vcclMemAlloc(void** ptr, size_t size) {
     acc.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
     acc.location.id = dev;
     acc.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
-    if (d->memMap(va, bytes, 0, h, 0) != CUDA_SUCCESS || d->memSetAccess(va, bytes, &acc, 1) != CUDA_SUCCESS) {
+    if (d->memMap(va, bytes, 0, h, 0) != CUDA_SUCCESS) {
+      d->memAddressFree(va, bytes);
+      d->memRelease(h);
+      return vcclSystemError;
+    }
+    if (d->memSetAccess(va, bytes, &acc, 1) != CUDA_SUCCESS) {
       d->memUnmap(va, bytes);
       d->memAddressFree(va, bytes);
       d->memRelease(h);
@@ -516,13 +521,41 @@ vcclResult_t vcclMemFree(void* ptr) {
   return vcclSuccess;
 }
 
+}  // extern "C"
+
+namespace {
+// Makes the communicator's device current for one call and gives the caller
+// back its own current device afterwards.
+class DeviceScope {
+ public:
+  explicit DeviceScope(const vcclComm* comm) {
+    if (comm == nullptr || !comm->dev) return;
+    if (cudaGetDevice(&prev_) != cudaSuccess) {
+      cudaGetLastError();
+      prev_ = -1;
+    }
+    if (prev_ != comm->dev->device) cudaSetDevice(comm->dev->device);
+  }
+  ~DeviceScope() {
+    if (prev_ >= 0) cudaSetDevice(prev_);
+  }
+  DeviceScope(const DeviceScope&) = delete;
+  DeviceScope& operator=(const DeviceScope&) = delete;
+
+ private:
+  int prev_ = -1;
+};
+}  // namespace
+
+extern "C" {
+
 vcclResult_t vcclCommRegister(vcclComm_t comm, void* buff, size_t bytes, vcclMemHandle_t* handle) {
   if (comm == nullptr || buff == nullptr || bytes == 0 || handle == nullptr) return vcclInvalidArgument;
   auto reg = std::make_unique<vccl::Registration>();
   reg->base = buff;
   reg->bytes = bytes;
+  DeviceScope scope(comm);
   if (comm->dev) {
-    cudaSetDevice(comm->dev->device);
     cudaPointerAttributes at;
     if (cudaPointerGetAttributes(&at, buff) == cudaSuccess && at.type == cudaMemoryTypeUnregistered) {
       // Host memory: pin it so staging copies are asynchronous DMA.
@@ -542,8 +575,8 @@ vcclResult_t vcclCommRegisterDmaBuf(vcclComm_t comm, int fd, uint64_t offset, si
     return vcclInvalidArgument;
   auto reg = std::make_unique<vccl::Registration>();
   const vccl::DriverApi* d = vccl::driverApi();
+  DeviceScope scope(comm);
   if (comm->dev && d) {
-    cudaSetDevice(comm->dev->device);
     // 1. A CUDA VMM export: import the allocation and map it here.
     CUmemGenericAllocationHandle h = 0;
     int dupFd = dup(fd);
@@ -631,7 +664,7 @@ vcclResult_t vcclCommDeregister(vcclComm_t comm, vcclMemHandle_t handle) {
   auto it = std::find(comm->regs.begin(), comm->regs.end(), r);
   if (it == comm->regs.end()) return vcclInvalidArgument;
   comm->regs.erase(it);
-  if (comm->dev) cudaSetDevice(comm->dev->device);
+  DeviceScope scope(comm);
   if (r->hostPinned) cudaHostUnregister(r->base);
   if (r->mapped) munmap(r->mapped, r->mappedBytes);
   if (r->extMem) cudaDestroyExternalMemory(r->extMem);

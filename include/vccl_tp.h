@@ -21,11 +21,14 @@ vcclResult_t vcclGemmBf16(const void* A, const void* W, void* C, int M, int N, i
 
 /* vcclGemmBf16 for callers that must not allocate device memory (no
  * counterpart in the reference).  Same arguments and results; the split-K
- * scratch of decode shapes and the abort flag live in one fixed 8 MiB
- * device array instead of allocations.  A shape whose split-K partials need
- * more than 8 MiB returns vcclInvalidArgument.  The first call on each
- * device resolves the array's address; make it before any stream capture.
- * Calls that may overlap in time on one device (different streams or host
+ * scratch of decode shapes lives in one fixed 8 MiB device array and the
+ * abort word in a static host page instead of allocations.  A shape whose
+ * split-K partials need more than 8 MiB returns vcclInvalidArgument.  The
+ * first call on each device does set-up (resolves the array's address,
+ * loads its module, maps the abort page); make it at start-up, before
+ * device memory is reserved and before any stream capture.  A launch that
+ * abandoned its tiles makes the next call return vcclInternalError.  Calls
+ * that may overlap in time on one device (different streams or host
  * threads) share the array and race; calls on one stream are safe. */
 vcclResult_t vcclGemmBf16NoAlloc(const void* A, const void* W, void* C, int M, int N, int K, vcclStream_t stream);
 

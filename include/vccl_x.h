@@ -29,6 +29,12 @@ vcclResult_t vcclxFusedTrace(vcclComm_t comm, unsigned long long* out, int* ctas
  * some kernel.  vcclInvalidUsage without guards. */
 vcclResult_t vcclxCheckGuards(vcclComm_t comm, unsigned long long* badBytes);
 
+/* Sets, from the host, the abort word of vcclGemmBf16NoAlloc on `device`:
+ * the state a launch that abandoned its tiles (a pipeline wait ran out)
+ * leaves behind.  The next vcclGemmBf16NoAlloc call on that device returns
+ * vcclInternalError and clears it.  For tests of that error path. */
+vcclResult_t vcclxNoAllocInjectAbort(int device);
+
 #ifdef __cplusplus
 }
 #endif

@@ -36,6 +36,9 @@ def test_reference_arm_prints_contract_line(nranks):
     d = lines[0]
     assert d["impl"] == "reference" and d["n_gpus"] == nranks and d["steps"] == 2 and d["warmup"] == 1
     assert d["metric"] == "tp_mlp_layer_latency_us" and d["value"] > 0 and d["higher_is_better"] is False
+    # host tensors in and out: the end-to-end number is the step itself, with no device copies
+    assert d["e2e"]["value"] == d["value"] and d["e2e"]["unit"] == "us"
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
 
 
 def test_roofline_helper():
@@ -47,5 +50,7 @@ def test_roofline_helper():
     flops = 2.0 * 8192 * 4096 * 14336 * 3
     r = b.roofline(flops, 8192, 8, 500.0)
     assert r["bound"] == "compute" and 0 < r["fraction"] < 1
+    # burst peak headline, sustained beside it (a larger fraction: the sustained peak is lower)
+    assert r["fraction_sustained"] > r["fraction"]
     assert r["nvlink_us"] > 0
     assert b.roofline(flops, 8192, 1, 500.0)["nvlink_us"] == 0

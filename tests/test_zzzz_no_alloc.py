@@ -4,7 +4,9 @@
 Two calls in a row on the same stream must each match vcclGemmBf16 on the
 same inputs (and the fp32 reference), for decode shapes that take the
 split-K path through the fixed scratch and for a shape that does not.  A
-shape whose split-K partials exceed the fixed scratch is rejected.
+shape whose split-K partials exceed the fixed scratch is rejected.  A warm
+call changes no device memory figure, and an abandoned launch (its abort
+word set from the host, no device fault) makes the next call fail once.
 
 Named test_zz_* so it is collected last; it must pass alone too.
 """
@@ -18,6 +20,7 @@ from conftest import gpu_count
 
 pytestmark = pytest.mark.gpu
 
+INTERNAL_ERROR = 3
 INVALID_ARGUMENT = 4
 
 
@@ -71,3 +74,39 @@ def test_no_alloc_rejects_oversized_scratch():
     w = torch.zeros(n, k, dtype=torch.bfloat16, device="cuda")
     c = torch.zeros(m, n, dtype=torch.bfloat16, device="cuda")
     assert _call(h.vcclGemmBf16NoAlloc, a, w, c) == INVALID_ARGUMENT
+
+
+def test_no_alloc_allocates_nothing_when_warm():
+    if gpu_count() == 0:
+        pytest.skip("no GPU")
+    h = _lib()
+    m, n, k = 8, 4096, 8192  # split-K: partials in the fixed scratch
+    a = torch.randn(m, k, device="cuda").bfloat16()
+    w = (torch.randn(n, k, device="cuda") * 0.02).bfloat16()
+    c = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    assert _call(h.vcclGemmBf16NoAlloc, a, w, c) == 0  # first call: set-up
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        assert _call(h.vcclGemmBf16NoAlloc, a, w, c) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+
+
+def test_no_alloc_reports_abandoned_launch_once():
+    if gpu_count() == 0:
+        pytest.skip("no GPU")
+    h = _lib()
+    m, n, k = 4, 2048, 4096
+    a = torch.randn(m, k, device="cuda").bfloat16()
+    w = (torch.randn(n, k, device="cuda") * 0.02).bfloat16()
+    c = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    assert _call(h.vcclGemmBf16NoAlloc, a, w, c) == 0
+    torch.cuda.synchronize()
+    assert h.vcclxNoAllocInjectAbort(torch.cuda.current_device()) == 0
+    assert _call(h.vcclGemmBf16NoAlloc, a, w, c) == INTERNAL_ERROR
+    assert _call(h.vcclGemmBf16NoAlloc, a, w, c) == 0  # the word was cleared
+    torch.cuda.synchronize()
+    ref = a.float() @ w.float().T
+    assert (c.float() - ref).abs().max().item() <= 1e-2 * (ref.abs().max().item() + 1e-6) + 1e-3

@@ -143,6 +143,7 @@ def _declare_extensions(h: ctypes.CDLL) -> None:
         "vcclxFusedTrace": [P, P, P],
         "vcclxCheckGuards": [P, c.POINTER(c.c_ulonglong)],
         "vcclxBarrierBench": [P, I, I, I, c.POINTER(F)],
+        "vcclxNoAllocInjectAbort": [I],
         "vcclGemmSiluMul": [P, P, P, I, I, I, P],
         "vcclGemmReduceScatter": [P, P, P, I, I, I, P, P],
         "vcclAllGatherGemm": [P, P, P, I, I, I, I, P, P],
