@@ -554,9 +554,20 @@ vcclResult_t launchColl(const HostOp& h) {
     case Kind::ReduceScatter:
       noteAlgorithm("reduce-scatter", h.count * es <= lc.llMax ? "LL" : "push", n, h.count * es);
       return cudaToVccl(launchReduceScatter(lc, h.dt, h.redKind, a), "reduce-scatter launch");
-    case Kind::AllGather:
-      noteAlgorithm("all-gather", h.count * es <= lc.llAgMax ? "LL" : "pull", n, h.count * es);
-      return cudaToVccl(launchAllGather(lc, h.send, h.recv, h.count * es), "all-gather launch");
+    case Kind::AllGather: {
+      // VCCL_ALLGATHER_ALGO forces the algorithm (read per call, as the
+      // all-reduce override is): ll / oneshot / recdouble take the LL kernel
+      // whenever the message allows it, pull / ring the pull kernel.
+      LaunchCtx agc = lc;
+      const char* forced = std::getenv("VCCL_ALLGATHER_ALGO");
+      if (forced != nullptr) {
+        const std::string f = forced;
+        if (f == "ll" || f == "oneshot" || f == "recdouble") agc.llAgMax = dev::kLLMaxBytes;
+        else if (f == "pull" || f == "ring") agc.llAgMax = 0;
+      }
+      noteAlgorithm("all-gather", h.count * es <= agc.llAgMax ? "LL" : "pull", n, h.count * es);
+      return cudaToVccl(launchAllGather(agc, h.send, h.recv, h.count * es), "all-gather launch");
+    }
     case Kind::Broadcast: {
       const size_t bytes = h.count * es;
       std::string force = envStr("VCCL_BROADCAST_ALGO", "");

@@ -261,7 +261,9 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
   // all-reduce and needs no barrier.  At 8 ranks with 1 MiB per rank the LL
   // all-reduce (same traffic) took 33 us where the pull all-gather took
   // 73 us, so all-gather stays on LL up to the LL slot size.
-  ds->llAgMaxBytes = envBytes("VCCL_LL_AG_MAX", dev::kLLMaxBytes);
+  // Per-rank payload up to which all-gather takes the LL kernel; the
+  // reference's name for its latency/bandwidth crossover is accepted too.
+  ds->llAgMaxBytes = envBytes("VCCL_LL_AG_MAX", envBytes("VCCL_ALLGATHER_RD_MAX", dev::kLLMaxBytes));
   {
     const std::string tf = envStr("VCCL_TUNING_FILE", "");
     if (!tf.empty()) ds->tuning = loadTuningFile(tf.c_str());

@@ -359,6 +359,18 @@ void algoAB(vcclComm_t c, int me, int n, size_t cnt) {
     }
     unsetenv("VCCL_ALLREDUCE_ALGO");
   }
+  // all-gather A/B (the reference forces ring vs recursive doubling; here
+  // pull vs LL), host buffers, each rank's block of cnt / n elements
+  const size_t per = cnt / n > 0 ? cnt / n : 1;
+  std::vector<float> g(per * n);
+  for (const char* algo : {"ring", "recdouble", "pull", "ll"}) {
+    setenv("VCCL_ALLGATHER_ALGO", algo, 1);
+    std::fill(g.begin(), g.end(), -7.0f);
+    EXPECT_OK(vcclAllGather(s.data(), g.data(), per, vcclFloat32, c));
+    for (int p = 0; p < n; p++)
+      for (size_t i = 0; i < per; i++) EXPECT_NEAR(g[p * per + i], val(p, i), vcclFloat32, algo, i);
+  }
+  unsetenv("VCCL_ALLGATHER_ALGO");
 }
 
 // Device-buffer sweep: every algorithm, sizes up to several staging rounds.

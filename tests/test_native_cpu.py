@@ -55,3 +55,18 @@ def test_collective_index_arithmetic():
     """Coverage and staging bounds of the staged, pipelined-NVLS and window kernels' splits, with a
     negative control for re-split rounds (csrc/tests/test_coll_index.cc)."""
     assert "all checks passed" in _run("test_coll_index")
+
+
+def _run_dmabuf(args, extra_env):
+    env = dict(os.environ, VCCL_SOCKET_ADDR="127.0.0.1", VCCL_DEBUG="ERROR", **extra_env)
+    return subprocess.run([os.path.join(BIN, "test_dmabuf")] + args, env=env, capture_output=True, text=True,
+                          timeout=300)
+
+
+def test_dmabuf_registration_control_plane():
+    """vcclCommRegisterDmaBuf's CPU-mapping route on a control-plane-only rank: a memfd, and a real
+    dmabuf from /dev/udmabuf where the kernel has it (reference: tests/test_dmabuf.cc)."""
+    p = _run_dmabuf(["1", "memfd"], {"VCCL_NO_DEVICE": "1"})
+    assert p.returncode == 0 and "dmabuf (memfd, 1 ranks): OK" in p.stdout, p.stdout + p.stderr
+    p = _run_dmabuf(["1", "udmabuf"], {"VCCL_NO_DEVICE": "1"})
+    assert p.returncode in (0, 77), p.stdout + p.stderr
