@@ -66,6 +66,50 @@ int pickBNWaves(int M, int N, int sms) {
   return bestBn;
 }
 
+int pairGroupRows() {
+  static const int g = [] {
+    const long v = envLongGemm("VCCL_GEMM_GROUP");
+    return v > 0 && v <= 64 ? static_cast<int>(v) : 8;
+  }();
+  return g;
+}
+
+int pairMode() {
+  // Read per call (tests switch it): unset or 1 = by cost, 0 = off, 2 = always.
+  const char* v = std::getenv("VCCL_GEMM_PAIR");
+  if (v == nullptr || v[0] == '\0') return 1;
+  return v[0] == '0' ? 0 : v[0] == '2' ? 2 : 1;
+}
+
+int pairMaxClusters(const void* kernel, int smemBytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find({dev, kernel});
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(smCount()), 1, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smemBytes);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  VINFO("GEMM on CTA pairs: %d pairs co-resident on device %d", n, dev);
+  cache[{dev, kernel}] = n;
+  return n;
+}
+
 int pickBN(int M, int N) {
   const int sms = smCount();
   static const bool byWaves = envLongGemm("VCCL_GEMM_PICK_WAVES") != 0;
@@ -336,9 +380,18 @@ cudaError_t gemmAuto(const void* A, const void* W, void* C, int M, int N, int K,
   }
   if (siluMul) {
     EpiSiluMul epi{static_cast<__nv_bfloat16*>(C), N / 2};
+    if (pairPreferred(M, N, bnOverride,
+                      pairMaxClusters(pairKernelFor<EpiSiluMul>(), PairSmem<kPairStages>::kBytes))) {
+      const cudaError_t e = launchGemmPair(A, W, M, N, K, epi, st);
+      if (e != cudaErrorNotSupported) return e;
+    }
     return launchGemm(A, W, M, N, K, epi, NoHooks{}, st, bnOverride, 0);
   }
   EpiStore epi{static_cast<__nv_bfloat16*>(C), N};
+  if (pairPreferred(M, N, bnOverride, pairMaxClusters(pairKernelFor<EpiStore>(), PairSmem<kPairStages>::kBytes))) {
+    const cudaError_t e = launchGemmPair(A, W, M, N, K, epi, st);
+    if (e != cudaErrorNotSupported) return e;
+  }
   return launchGemm(A, W, M, N, K, epi, NoHooks{}, st, bnOverride, 0);
 }
 

@@ -7,9 +7,11 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstring>
 
 #include "fused/gemm_host.h"
 #include "kernels/gemm_sm100.cuh"
+#include "kernels/gemm_sm100_pair.cuh"
 
 namespace vccl {
 namespace gemm {
@@ -67,6 +69,88 @@ cudaError_t launchGemm(const void* A, const void* B, int M, int N, int K, const 
     case 64: return launchT<64, 8>(ma, mb, s, epi, hooks, grid, st, flag);
     default: return launchT<32, 8>(ma, mb, s, epi, hooks, grid, st, flag);
   }
+}
+
+// ---- CTA-pair GEMM (256 x 256 tiles on two SMs) ---------------------------------
+constexpr int kPairStages = 6;
+
+// Grouping of pair-row tiles in the tile order (VCCL_GEMM_GROUP, default 8):
+// a wave of pairs then reads a compact block of A rows and B columns.
+int pairGroupRows();
+// VCCL_GEMM_PAIR: 1 (default) the pair kernel where pairPreferred says so,
+// 0 never, 2 for every shape of at least one pair tile.
+int pairMode();
+// Clusters of two that fit on the device at once with the pair kernel's
+// shared memory (0 if the device cannot run it).
+int pairMaxClusters(const void* kernel, int smemBytes);
+
+// True when the pair kernel finishes the shape in no more waves x tile width
+// than the one-SM kernel's choice: it moves a third less data per FLOP, so
+// it is taken on ties.
+inline bool pairPreferred(int M, int N, int bnOverride, int pairs) {
+  const int mode = pairMode();
+  if (mode == 0 || bnOverride > 0 || M < kPairBM || N < kPairBN || pairs <= 0) return false;
+  if (mode == 2) return true;
+  const int sms = smCount();
+  const int tiles2 = ((M + kPairBM - 1) / kPairBM) * ((N + kPairBN - 1) / kPairBN);
+  const long cost2 = static_cast<long>((tiles2 + pairs - 1) / pairs) * kPairBN;
+  const int bn = pickBN(M, N);
+  const int tiles1 = ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
+  const long cost1 = static_cast<long>((tiles1 + sms - 1) / sms) * bn;
+  return cost2 <= cost1;
+}
+
+template <typename Epi>
+const void* pairKernelFor() {
+  return reinterpret_cast<const void*>(gemmPairKernel<kPairStages, Epi>);
+}
+
+// C = A B^T on CTA pairs with epilogue `epi` (EpiStore or EpiSiluMul).
+// Returns cudaErrorNotSupported if the device cannot co-schedule the pairs.
+template <typename Epi>
+cudaError_t launchGemmPair(const void* A, const void* B, int M, int N, int K, const Epi& epi, cudaStream_t st,
+                           int* flag = nullptr) {
+  using L = PairSmem<kPairStages>;
+  auto kern = gemmPairKernel<kPairStages, Epi>;
+  static std::atomic<unsigned long long> attrDone{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(attrDone.load(std::memory_order_acquire) & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+    if (e != cudaSuccess) cudaGetLastError();
+    attrDone.fetch_or(bit, std::memory_order_release);
+  }
+  const int maxPairs = pairMaxClusters(reinterpret_cast<const void*>(kern), L::kBytes);
+  if (maxPairs <= 0) return cudaErrorNotSupported;
+  CUtensorMap ma, mb;
+  if (!makeMapKMajor(&ma, A, M, K, kBM) || !makeMapKMajor(&mb, B, N, K, kPairBN / 2)) return cudaErrorInvalidValue;
+  GemmShape s;
+  s.M = M;
+  s.N = N;
+  s.K = K;
+  s.tilesM = (M + kPairBM - 1) / kPairBM;
+  s.tilesN = (N + kPairBN - 1) / kPairBN;
+  s.splits = 1;
+  s.aRows = kBM;
+  const int tiles = s.tilesM * s.tilesN;
+  const int pairs = tiles < maxPairs ? tiles : maxPairs;
+  if (flag == nullptr) flag = errorFlag();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, ma, mb, s, epi, pairGroupRows(), flag);
 }
 
 }  // namespace gemm

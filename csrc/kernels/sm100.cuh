@@ -187,5 +187,95 @@ __device__ __forceinline__ void mmaCommit(uint64_t* bar) {
                : "memory");
 }
 
+// ---- CTA pairs (clusters of two; cta_group::2) -----------------------------------
+// Rank of this CTA in its cluster, the cluster's index and the number of clusters.
+__device__ __forceinline__ uint32_t clusterCtaRank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t clusterIdX() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t numClustersX() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// Address, in the cluster's shared window, of the variable at `local` in CTA `cta`.
+__device__ __forceinline__ uint32_t mapaShared(const void* local, uint32_t cta) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smemAddr(local)), "r"(cta));
+  return r;
+}
+// Arrive (release at cluster scope) on an mbarrier of another CTA of the cluster.
+__device__ __forceinline__ void mbarArriveCluster(uint32_t clusterAddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(clusterAddr) : "memory");
+}
+// try_wait with acquire at cluster scope: pairs with arrivals made by the
+// other CTA of the cluster.
+__device__ __forceinline__ bool mbarTryWaitCluster(uint64_t* bar, uint32_t phase) {
+  uint32_t ok = 0;
+  asm volatile(
+      "{\n .reg .pred P;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2, %3;\n selp.b32 %0, 1, 0, P;\n}\n"
+      : "=r"(ok)
+      : "r"(smemAddr(bar)), "r"(phase), "r"(1000000u)
+      : "memory");
+  return ok != 0;
+}
+// Bounded cluster-scope wait (as mbarWait).
+__device__ __forceinline__ bool mbarWaitCluster(uint64_t* bar, uint32_t phase, volatile int* abortFlag,
+                                                uint64_t limitNs = 2000000000ull) {
+  if (mbarTryWaitCluster(bar, phase)) return true;
+  const uint64_t t0 = nowNs();
+  for (;;) {
+    if (mbarTryWaitCluster(bar, phase)) return true;
+    if (*abortFlag) return false;
+    if (nowNs() - t0 > limitNs) {
+      *abortFlag = 1;
+      return false;
+    }
+  }
+}
+// Every thread of both CTAs of the cluster (all threads must call it).
+__device__ __forceinline__ void clusterSync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMEM allocation shared by the two CTAs of a pair: the same warp of both
+// CTAs issues each of these.
+__device__ __forceinline__ void tmemAllocPair(uint32_t* dstSmem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smemAddr(dstSmem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmemRelinquishPair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmemDeallocPair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// One MMA over the pair (issued by the pair's first CTA): A holds 128 rows in
+// each CTA's shared memory and B half of the N rows in each, both at the
+// descriptors' offsets; D is 128 rows x N columns in each CTA's TMEM.
+__device__ __forceinline__ void mmaBf16Pair(uint32_t tmemD, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmemD),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on the mbarrier at `bar`'s offset in every CTA of `ctaMask` once the
+// pair MMAs issued so far by this thread have completed (a commit, not a load).
+__device__ __forceinline__ void mmaCommitPair(uint64_t* bar, uint16_t ctaMask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smemAddr(bar)),
+      "h"(ctaMask)
+      : "memory");
+}
+
 }  // namespace sm100
 }  // namespace vccl

@@ -7,6 +7,8 @@
 //  * the epilogue row stage: every (row, chunk) has its own slot, and each
 //    8-lane phase of both the row-per-thread writes and the row-contiguous
 //    reads touches 8 different 16-byte bank groups;
+//  * pairTile (CTA-pair GEMM order) visits every 256 x 256 tile once for
+//    every grouping, and the two CTAs of a pair take its two 128-row halves;
 //  * planSplitK keeps its bounds (4+ k-blocks per split, <= 16 splits,
 //    partials <= a quarter of the weight bytes).
 #include <cstdio>
@@ -16,6 +18,7 @@
 
 #include "fused/gemm_host.h"
 #include "kernels/gemm_sm100.cuh"
+#include "kernels/gemm_sm100_pair.cuh"
 
 using namespace vccl::gemm;
 
@@ -41,6 +44,32 @@ GemmShape shape(int M, int N, int K, int BN, int splits) {
   s.splits = splits;
   s.aRows = M >= kBM ? kBM : (M + 7) / 8 * 8;
   return s;
+}
+
+void checkPairTiles() {
+  for (int M : {256, 1000, 8192})
+    for (int N : {256, 1040, 28672})
+      for (int group : {1, 3, 8, 64}) {
+        GemmShape s{};
+        s.M = M;
+        s.N = N;
+        s.K = 4096;
+        s.tilesM = (M + kPairBM - 1) / kPairBM;
+        s.tilesN = (N + kPairBN - 1) / kPairBN;
+        s.splits = 1;
+        s.aRows = kBM;
+        std::set<std::pair<int, int>> seen;
+        for (int t = 0; t < s.tilesM * s.tilesN; t++) {
+          const TileInfo t0 = pairTile(s, t, group, 0), t1 = pairTile(s, t, group, 1);
+          EXPECT(t0.tm >= 0 && t0.tm < s.tilesM && t0.tn >= 0 && t0.tn < s.tilesN, "pair tile out of range");
+          EXPECT(seen.insert({t0.tm, t0.tn}).second, "pair tile visited twice (M=%d N=%d group=%d)", M, N, group);
+          EXPECT(t0.tm == t1.tm && t0.tn == t1.tn, "the CTAs of a pair disagree on the tile");
+          EXPECT(t0.row0 == t0.tm * kPairBM && t1.row0 == t0.row0 + kBM, "pair row halves");
+          EXPECT(t0.col0 == t0.tn * kPairBN && t1.col0 == t0.col0, "pair columns");
+          EXPECT(t0.kb0 == 0 && t0.kb1 == s.numK(), "pair tiles cover all of K");
+        }
+        EXPECT(static_cast<int>(seen.size()) == s.tilesM * s.tilesN, "pair tiles missing");
+      }
 }
 
 void checkSplitK() {
@@ -164,6 +193,7 @@ void checkPickWaves() {
 
 int main() {
   checkSplitK();
+  checkPairTiles();
   checkPickWaves();
   checkGrouped();
   checkStage();

@@ -93,3 +93,36 @@ def test_gemm_split_k(m, n, k, monkeypatch):
     scale = ref.abs().max().item() + 1e-6
     assert (out.float() - ref).abs().max().item() <= 1e-2 * scale + 1e-3
     assert (out.float() - plain.float()).abs().max().item() <= 1e-2 * scale + 1e-3
+
+
+# The CTA-pair kernel (256 x 256 tiles over two SMs, tcgen05.mma.cta_group::2),
+# forced with VCCL_GEMM_PAIR=2, against the fp32 reference and the one-SM
+# kernel (VCCL_GEMM_PAIR=0); ragged M, N and K included.
+PAIR_SHAPES = [(256, 256, 64), (512, 768, 1024), (1000, 1040, 776), (2048, 4096, 1792), (8192, 3584, 4096)]
+
+
+@pytest.mark.parametrize("m,n,k", PAIR_SHAPES)
+@pytest.mark.parametrize("silu", [False, True])
+def test_gemm_cta_pair(m, n, k, silu, monkeypatch):
+    if gpu_count() == 0:
+        pytest.skip("no GPU")
+    from vkccl_b200.ops.gemm import gemm_bf16, gemm_silu_mul
+
+    g = torch.Generator(device="cuda").manual_seed(m + 3 * n + 5 * k + silu)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.02).bfloat16()
+    fn = gemm_silu_mul if silu else gemm_bf16
+    outs = []
+    for mode in ("2", "2", "0"):  # the pair kernel twice in a row, then the one-SM kernel
+        monkeypatch.setenv("VCCL_GEMM_PAIR", mode)
+        outs.append(fn(a, w))
+    torch.cuda.synchronize()
+    ref = _ref(a, w)
+    if silu:  # W rows interleave gate and up in groups of 16
+        r = ref.view(m, n // 32, 2, 16)
+        ref = (torch.nn.functional.silu(r[:, :, 0]) * r[:, :, 1]).reshape(m, n // 2)
+    scale = ref.abs().max().item() + 1e-6
+    for out in outs:
+        err = (out.float() - ref).abs().max().item()
+        assert err <= 1e-2 * scale + 1e-3, f"max err {err} (scale {scale})"
+    assert torch.equal(outs[0], outs[1])
