@@ -204,16 +204,8 @@ extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, voi
   OrderedLaunch ord(comm->dev.get(), s);
   const int bnEnv = static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN"));
   cudaError_t e;
-  if (n == 1) {
-    if (siluMul) {
-      gemm::EpiSiluMul epi{static_cast<__nv_bfloat16*>(out), N / 2};
-      e = gemm::launchGemm(xShard, W, M, N, K, epi, gemm::NoHooks{}, s, bnEnv, 0);
-    } else {
-      gemm::EpiStore epi{static_cast<__nv_bfloat16*>(out), N};
-      e = gemm::launchGemm(xShard, W, M, N, K, epi, gemm::NoHooks{}, s, bnEnv, 0);
-    }
-    return e == cudaSuccess ? vcclSuccess : vcclInvalidArgument;
-  }
+  if (n == 1)  // the gather is the shard itself: the plain GEMM (split-K, CTA pairs or one-SM tiles)
+    return gemm::gemmWithScratch("vcclAllGatherGemm", xShard, W, out, M, N, K, siluMul, s);
   if (M <= comm->dev->fusedSmallRows) {
     // Few rows (decode, short prefills): the gather is a few hundred KB, so
     // an LL all-gather into local scratch followed by a (split-K) GEMM beats

@@ -89,6 +89,13 @@ int pairMaxClusters(const void* kernel, int smemBytes) {
   std::lock_guard<std::mutex> lock(mu);
   auto it = cache.find({dev, kernel});
   if (it != cache.end()) return it->second;
+  // The occupancy query sees the kernel's shared-memory limit, so raise it first.
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smemBytes) != cudaSuccess) {
+    VWARN("GEMM on CTA pairs: cannot raise the shared-memory limit on device %d; one-SM tiles only", dev);
+    cudaGetLastError();
+    cache[{dev, kernel}] = 0;
+    return 0;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(smCount()), 1, 1);
   cfg.blockDim = dim3(192, 1, 1);
@@ -101,7 +108,10 @@ int pairMaxClusters(const void* kernel, int smemBytes) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+  const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+  if (e != cudaSuccess) {
+    VWARN("GEMM on CTA pairs: occupancy query failed on device %d (%s); one-SM tiles only", dev,
+          cudaGetErrorString(e));
     cudaGetLastError();
     n = 0;
   }
@@ -378,19 +388,26 @@ cudaError_t gemmAuto(const void* A, const void* W, void* C, int M, int N, int K,
     return siluMul ? launchSplitReduceSilu(ws, plan.splits, M, N, C, st)
                    : launchSplitReduce(ws, plan.splits, elems, C, st);
   }
+  // VCCL_GEMM_PAIR=2 demands the pair kernel for every shape it covers and
+  // fails (instead of falling back) where the device cannot run it.
+  const bool forcePair = pairMode() == 2 && M >= kPairBM && N >= kPairBN && bnOverride <= 0;
   if (siluMul) {
     EpiSiluMul epi{static_cast<__nv_bfloat16*>(C), N / 2};
     if (pairPreferred(M, N, bnOverride,
                       pairMaxClusters(pairKernelFor<EpiSiluMul>(), PairSmem<kPairStages>::kBytes))) {
       const cudaError_t e = launchGemmPair(A, W, M, N, K, epi, st);
-      if (e != cudaErrorNotSupported) return e;
+      if (e != cudaErrorNotSupported || forcePair) return e;
+    } else if (forcePair) {
+      return cudaErrorNotSupported;
     }
     return launchGemm(A, W, M, N, K, epi, NoHooks{}, st, bnOverride, 0);
   }
   EpiStore epi{static_cast<__nv_bfloat16*>(C), N};
   if (pairPreferred(M, N, bnOverride, pairMaxClusters(pairKernelFor<EpiStore>(), PairSmem<kPairStages>::kBytes))) {
     const cudaError_t e = launchGemmPair(A, W, M, N, K, epi, st);
-    if (e != cudaErrorNotSupported) return e;
+    if (e != cudaErrorNotSupported || forcePair) return e;
+  } else if (forcePair) {
+    return cudaErrorNotSupported;
   }
   return launchGemm(A, W, M, N, K, epi, NoHooks{}, st, bnOverride, 0);
 }
@@ -436,6 +453,26 @@ bool takeAbortFlag() {
   return true;
 }
 
+vcclResult_t gemmWithScratch(const char* what, const void* A, const void* W, void* C, int M, int N, int K,
+                             bool siluMul, cudaStream_t st) {
+  const int bnEnv = static_cast<int>(envLongGemm("VCCL_GEMM_BN"));
+  // Decode shapes split K across more CTAs; the fp32 partials live in
+  // per-stream scratch (a graph memory node while the stream is captured).
+  Scratch sc;
+  const size_t bytes = gemmAutoScratchBytes(M, N, K, bnEnv, true);
+  if (!acquireScratch(st, bytes, &sc)) {
+    VERR("%s: cannot allocate %zu bytes of split-K scratch", what, bytes);
+    return vcclSystemError;
+  }
+  cudaError_t e = gemmAuto(A, W, C, M, N, K, siluMul, st, bnEnv, true, static_cast<float*>(sc.p), sc.sems);
+  releaseScratch(sc);
+  if (e != cudaSuccess) {
+    VERR("%s: %s", what, cudaGetErrorString(e));
+    return launchResult(e);
+  }
+  return vcclSuccess;
+}
+
 }  // namespace gemm
 }  // namespace vccl
 
@@ -452,22 +489,7 @@ vcclResult_t gemmEntry(const char* what, const void* A, const void* W, void* C, 
          what);
     return vcclInternalError;
   }
-  const int bnEnv = static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN"));
-  // Decode shapes split K across more CTAs; the fp32 partials live in
-  // per-stream scratch (a graph memory node while the stream is captured).
-  gemm::Scratch sc;
-  const size_t bytes = gemm::gemmAutoScratchBytes(M, N, K, bnEnv, true);
-  if (!gemm::acquireScratch(st, bytes, &sc)) {
-    VERR("%s: cannot allocate %zu bytes of split-K scratch", what, bytes);
-    return vcclSystemError;
-  }
-  cudaError_t e = gemm::gemmAuto(A, W, C, M, N, K, siluMul, st, bnEnv, true, static_cast<float*>(sc.p), sc.sems);
-  gemm::releaseScratch(sc);
-  if (e != cudaSuccess) {
-    VERR("%s: %s", what, cudaGetErrorString(e));
-    return gemm::launchResult(e);
-  }
-  return vcclSuccess;
+  return gemm::gemmWithScratch(what, A, W, C, M, N, K, siluMul, st);
 }
 }  // namespace
 

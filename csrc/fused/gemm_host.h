@@ -76,6 +76,12 @@ cudaError_t launchSplitReduceSilu(const float* ws, int splits, int M, int N, voi
 cudaError_t launchSplitReduce(const float* ws, int splits, size_t elems, void* out, cudaStream_t st,
                               const volatile int* abortWord = nullptr);
 
+// The GEMM of vcclGemmBf16 / vcclGemmSiluMul (split-K with per-stream
+// scratch for decode shapes, CTA pairs for large ones, one-SM tiles
+// otherwise), as a vccl result; `what` names the caller in error messages.
+vcclResult_t gemmWithScratch(const char* what, const void* A, const void* W, void* C, int M, int N, int K,
+                             bool siluMul, cudaStream_t st);
+
 // The result code of a failed GEMM launch: vcclInvalidArgument when the
 // arguments could not be described to the hardware (a tensor map the driver
 // refused, a split the shape cannot take: cudaErrorInvalidValue), otherwise

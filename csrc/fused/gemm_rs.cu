@@ -261,11 +261,8 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   OrderedLaunch ord(comm->dev.get(), s);
   const int bnEnv = static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN"));
-  if (n == 1) {
-    gemm::EpiStore epi{static_cast<__nv_bfloat16*>(out), N};
-    cudaError_t e = gemm::launchGemm(A, W, M, N, K, epi, gemm::NoHooks{}, s, bnEnv, 0);
-    return e == cudaSuccess ? vcclSuccess : vcclInvalidArgument;
-  }
+  if (n == 1)  // nothing to scatter: the plain GEMM (split-K, CTA pairs or one-SM tiles)
+    return gemm::gemmWithScratch("vcclGemmReduceScatter", A, W, out, M, N, K, false, s);
   const int rowsPerRank = M / n;
   if (M <= comm->dev->fusedSmallRows && (static_cast<size_t>(rowsPerRank) * N * 2) % 8 == 0) {
     // Few rows: (split-K) GEMM into local scratch, then the LL or push
