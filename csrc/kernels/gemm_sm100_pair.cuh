@@ -15,14 +15,13 @@
 //
 // Warp roles, both CTAs (192 threads):
 //   warp 0     TMA producer: this CTA's A and B halves into a STAGES-deep
-//              ring.  Loads signal this CTA's own `full` barrier (no
-//              multicast, no cross-CTA TMA signalling).
-//   warp 1     first CTA: MMA issuer.  Its `full` barriers count two
-//              arrivals: its own producer's (with the bytes) and one
-//              forwarded by the second CTA.  Commits release the ring slot
-//              and publish the accumulator in BOTH CTAs (commit multicast).
-//              Second CTA: relay - waits for each of its own stages to land
-//              and forwards one arrival to the first CTA's barrier.
+//              ring.  Both CTAs' loads complete on the FIRST CTA's `full`
+//              barrier (the cta_group::2 load form; no multicast), whose
+//              producer expects the bytes of both.  Each CTA refills a slot
+//              once its own `empty` barrier says the MMAs have read it.
+//   warp 1     first CTA: MMA issuer.  Commits release the ring slot and
+//              publish the accumulator in BOTH CTAs (commit multicast).
+//              Second CTA: idle (it takes part in the TMEM allocation).
 //   warps 2-5  epilogue (as the one-SM kernel), on this CTA's 128 rows; the
 //              accumulator is handed back to the first CTA's `accEmpty`.
 // Every wait is bounded; a CTA that gives up unwinds, and both CTAs meet at a
@@ -86,7 +85,7 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; i++) {
-      sm100::mbarInit(&fullBar[i], first ? 2 : 1);
+      sm100::mbarInit(&fullBar[i], 1);  // the first CTA's producer (the second CTA's is unused)
       sm100::mbarInit(&emptyBar[i], 1);
     }
     for (int i = 0; i < 2; i++) {
@@ -117,7 +116,6 @@ __global__ void __launch_bounds__(192, 1)
       sm100::tmaPrefetchDesc(&mapB);
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t issued = 0;
       bool ok = true;
       for (int t = pair0; t < numTiles && ok; t += pairs) {
         const TileInfo ti = pairTile(s, t, groupRows, static_cast<int>(cta));
@@ -129,32 +127,24 @@ __global__ void __launch_bounds__(192, 1)
           }
           uint8_t* a = smem + stage * L::kStageBytes;
           uint8_t* b = a + L::kABytes;
-          sm100::mbarArriveExpectTx(&fullBar[stage], static_cast<uint32_t>(L::kABytes + L::kBBytes));
-          sm100::tmaLoad2d(a, &mapA, &fullBar[stage], kb * kBK, ti.row0);
-          sm100::tmaLoad2d(b, &mapB, &fullBar[stage], kb * kBK, bRow0);
-          issued++;
+          if (first)
+            sm100::mbarArriveExpectTx(&fullBar[stage], static_cast<uint32_t>(2 * (L::kABytes + L::kBBytes)));
+          const uint32_t bar = sm100::mapaShared(&fullBar[stage], 0);
+          sm100::tmaLoad2dPair(a, &mapA, bar, kb * kBK, ti.row0);
+          sm100::tmaLoad2dPair(b, &mapB, bar, kb * kBK, bRow0);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-      if (!ok) {
-        // Let the copies already issued land before the CTA can exit.
-        const int n = issued < static_cast<uint32_t>(STAGES) ? static_cast<int>(issued) : STAGES;
-        int s2 = stage;
-        uint32_t p2 = phase;
+      // After an abort, copies still in flight land before the final
+      // cluster barrier: every slot is waited on through its `empty`
+      // barrier only while the MMAs run, so drain through the first CTA's
+      // `full` barriers with a short bound (the peer's bytes may be owed).
+      if (!ok && first) {
         volatile int never = 0;
-        for (int i = 0; i < n; i++) {
-          if (--s2 < 0) {
-            s2 = STAGES - 1;
-            p2 ^= 1u;
-          }
-          // The first CTA's barriers also count the relay's arrival, which
-          // may never come after an abort: wait on the bytes only as long as
-          // the normal bound allows.
-          sm100::mbarWait(&fullBar[s2], p2, &never, 200000000ull);
-        }
+        for (int i = 0; i < STAGES; i++) sm100::mbarWait(&fullBar[i], 0, &never, 20000000ull);
       }
     }
   } else if (warp == 1) {
@@ -208,28 +198,6 @@ __global__ void __launch_bounds__(192, 1)
           sm100::mmaCommitPair(drainBar, 0x1);
           volatile int never = 0;
           sm100::mbarWait(drainBar, 0, &never, 200000000ull);
-        }
-      }
-    } else {
-      // ---------------- relay (second CTA) ----------------
-      if (sm100::electOne()) {
-        int stage = 0;
-        uint32_t phase = 0;
-        const int nk = s.numK();
-        for (int t = pair0; t < numTiles; t += pairs) {
-          bool ok = true;
-          for (int kb = 0; kb < nk; kb++) {
-            if (!sm100::mbarWait(&fullBar[stage], phase, abortFlag)) {
-              ok = false;
-              break;
-            }
-            sm100::mbarArriveCluster(sm100::mapaShared(&fullBar[stage], 0));
-            if (++stage == STAGES) {
-              stage = 0;
-              phase ^= 1u;
-            }
-          }
-          if (!ok) break;
         }
       }
     }

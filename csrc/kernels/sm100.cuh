@@ -239,6 +239,18 @@ __device__ __forceinline__ bool mbarWaitCluster(uint64_t* bar, uint32_t phase, v
     }
   }
 }
+// TMA tile load into this CTA's shared memory whose completion is counted on
+// an mbarrier of the pair's first CTA (`barCluster`: its shared::cluster
+// address).  The cta_group::2 form lets a pair's loads complete on one
+// barrier; no multicast.
+__device__ __forceinline__ void tmaLoad2dPair(void* smemDst, const CUtensorMap* map, uint32_t barCluster, int32_t c0,
+                                              int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smemAddr(smemDst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(barCluster), "r"(c0), "r"(c1)
+      : "memory");
+}
 // Every thread of both CTAs of the cluster (all threads must call it).
 __device__ __forceinline__ void clusterSync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");

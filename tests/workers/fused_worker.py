@@ -76,6 +76,30 @@ def main():
             ref2 = torch.nn.functional.silu(xfull @ wg.float().T) * (xfull @ wu.float().T)
             close(out2, ref2, 3e-2, f"ag+gemm silu m={m}")
 
+    # --- the bench's TP shard shapes (Llama-3-8B MLP, 8192 tokens, shards as at TP-8) -----
+    # all-gather + gate/up GEMM: [8192 / n, 4096] shards x [3584, 4096] (SiLU*mul)
+    # GEMM + reduce-scatter: [8192, 1792] x [4096, 1792] -> [8192 / n, 4096]
+    T, HID, SH = 8192, 4096, 1792
+    for rep in range(2):
+        g.manual_seed(4000 + rep)
+        shards = [torch.randn(T // world, HID, device="cuda", generator=g).bfloat16() for _ in range(world)]
+        wg = (torch.randn(SH, HID, device="cuda", generator=g) * 0.02).bfloat16()
+        wu = (torch.randn(SH, HID, device="cuda", generator=g) * 0.02).bfloat16()
+        out = all_gather_gemm(comm, shards[rank], interleave_gate_up(wg, wu), silu_mul=True)
+        torch.cuda.synchronize()
+        xfull = torch.cat(shards).float()
+        ref = torch.nn.functional.silu(xfull @ wg.float().T) * (xfull @ wu.float().T)
+        close(out, ref, 3e-2, "ag+gemm silu at the bench shard shape")
+        del xfull, ref, out
+        As = [torch.randn(T, SH, device="cuda", generator=g).bfloat16() for _ in range(world)]
+        Ws = [(torch.randn(HID, SH, device="cuda", generator=g) * 0.02).bfloat16() for _ in range(world)]
+        per = T // world
+        out = gemm_reduce_scatter(comm, As[rank], Ws[rank])
+        torch.cuda.synchronize()
+        ref = sum(a[rank * per:(rank + 1) * per].float() @ w.float().T for a, w in zip(As, Ws))
+        close(out, ref, 2e-2, "gemm+rs at the bench shard shape")
+        del As, Ws, out, ref
+
     err = comm.async_error()
     comm.destroy()
     if err != 0:
