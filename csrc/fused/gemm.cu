@@ -66,12 +66,14 @@ int pickBNWaves(int M, int N, int sms) {
   return bestBn;
 }
 
-int pairGroupRows() {
-  static const int g = [] {
-    const long v = envLongGemm("VCCL_GEMM_GROUP");
-    return v > 0 && v <= 64 ? static_cast<int>(v) : 8;
-  }();
-  return g;
+int pairGroupRows(int K) {
+  static const long env = envLongGemm("VCCL_GEMM_GROUP");
+  if (env > 0 && env <= 64) return static_cast<int>(env);
+  // Measured on B200 (gemm_one): 16 pair rows for K = 4096 (8192 x 28672:
+  // 1194 us against 1213 / 1234 us with 12 / 8), 8 for K = 14336 (8192 x
+  // 4096: 642 us against 649 / 660 us with 16 / 4).  A pair row's A strip
+  // is 256 x K x 2 bytes; longer strips want smaller groups.
+  return K <= 8192 ? 16 : 8;
 }
 
 int pairMode() {

@@ -74,9 +74,10 @@ cudaError_t launchGemm(const void* A, const void* B, int M, int N, int K, const 
 // ---- CTA-pair GEMM (256 x 256 tiles on two SMs) ---------------------------------
 constexpr int kPairStages = 6;
 
-// Grouping of pair-row tiles in the tile order (VCCL_GEMM_GROUP, default 8):
-// a wave of pairs then reads a compact block of A rows and B columns.
-int pairGroupRows();
+// Grouping of pair-row tiles in the tile order (VCCL_GEMM_GROUP overrides
+// the measured default for K): a wave of pairs then reads a compact block of
+// A rows and B columns.
+int pairGroupRows(int K);
 // VCCL_GEMM_PAIR: 1 (default) the pair kernel where pairPreferred says so,
 // 0 never, 2 for every shape of at least one pair tile.
 int pairMode();
@@ -150,7 +151,7 @@ cudaError_t launchGemmPair(const void* A, const void* B, int M, int N, int K, co
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, ma, mb, s, epi, pairGroupRows(), flag);
+  return cudaLaunchKernelEx(&cfg, kern, ma, mb, s, epi, pairGroupRows(K), flag);
 }
 
 }  // namespace gemm
