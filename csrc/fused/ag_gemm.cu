@@ -54,7 +54,7 @@ __device__ __forceinline__ void groupCopy(char* dst, const char* src, size_t byt
   for (; i < n16; i += 64) dev::stG(dst + i * 16, dev::ldCG(src + i * 16));
 }
 
-struct AgHooks : gemm::NoHooks {
+struct AgHooks : gemm::PairNoHooks {
   static constexpr int kExtraWarps = 2;
   DevComm c;
   const char* xShard;  // this rank's input rows [shardRows, K]
@@ -63,6 +63,8 @@ struct AgHooks : gemm::NoHooks {
   int K;
   int startTm;         // first tile row of this rank's shard
   int groupRows;       // row tiles per tile group (divides the shard's tiles when possible)
+  int pairStartTm;     // the same two in 256-row pair tiles (CTA-pair kernel)
+  int pairGroupRows;
   uint32_t ctas;       // fixed grid size
   // Optional event trace (VCCL_FUSED_TRACE=1), kFusedTraceSlots times per CTA
   // from %globaltimer: 0 kernel start, 1 previous call's shard taken by every
@@ -90,6 +92,9 @@ struct AgHooks : gemm::NoHooks {
   // share weight tiles (see gemm::groupedTile).
   __device__ __forceinline__ gemm::TileInfo tileAt(const gemm::GemmShape& s, int t, int BN) const {
     return gemm::groupedTile(s, t, BN, groupRows, startTm);
+  }
+  __device__ __forceinline__ gemm::TileInfo pairTileAt(const gemm::GemmShape& s, int t, int, int cta) const {
+    return gemm::pairTileFrom(s, t, pairGroupRows, pairStartTm, cta);
   }
   __device__ __forceinline__ bool beforeLoad(const gemm::TileInfo& ti, const gemm::GemmShape& s, uint32_t* hs,
                                              volatile int*) const {
@@ -237,7 +242,14 @@ extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, voi
          static_cast<size_t>(M) * K * 2);
     return vcclInvalidArgument;
   }
-  const int ctas = gemm::smCount();
+  // CTA pairs (256 x 256 tiles) where they take no more waves than one-SM
+  // tiles; either way the grid is fixed and every CTA is resident.
+  const int pairs = siluMul ? gemm::pairClustersFor<gemm::EpiSiluMul, fused::AgHooks>()
+                            : gemm::pairClustersFor<gemm::EpiStore, fused::AgHooks>();
+  // The per-CTA call counters need the same grid on every call: pairs only
+  // when they cover every SM, as the one-SM grid does.
+  const bool usePair = 2 * pairs == gemm::smCount() && gemm::pairPreferred(M, N, bnEnv, pairs);
+  const int ctas = usePair ? 2 * pairs : gemm::smCount();
   fused::AgHooks hooks;
   hooks.c = dc;
   hooks.xShard = static_cast<const char*>(xShard);
@@ -255,19 +267,29 @@ extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, voi
       break;
     }
   hooks.groupRows = groupRows;
+  hooks.pairStartTm = (comm->rank * (M / n)) / gemm::kPairBM;
+  const int shardPairTiles = (M / n) % gemm::kPairBM == 0 ? (M / n) / gemm::kPairBM : 0;
+  hooks.pairGroupRows = 1;
+  for (int gsz = 16; gsz >= 1; gsz /= 2)
+    if (shardPairTiles > 0 && shardPairTiles % gsz == 0) {
+      hooks.pairGroupRows = gsz;
+      break;
+    }
   hooks.ctas = static_cast<uint32_t>(ctas);
   hooks.trace = comm->dev->fusedTrace;
   const char* xfull = dc.fused[comm->rank] + xOff;
   if (siluMul) {
     gemm::EpiSiluMul epi{static_cast<__nv_bfloat16*>(out), N / 2};
-    e = gemm::launchGemm(xfull, W, M, N, K, epi, hooks, s, bnEnv, -ctas);
+    e = usePair ? gemm::launchGemmPair(xfull, W, M, N, K, epi, s, nullptr, hooks, pairs)
+                : gemm::launchGemm(xfull, W, M, N, K, epi, hooks, s, bnEnv, -ctas);
   } else {
     gemm::EpiStore epi{static_cast<__nv_bfloat16*>(out), N};
-    e = gemm::launchGemm(xfull, W, M, N, K, epi, hooks, s, bnEnv, -ctas);
+    e = usePair ? gemm::launchGemmPair(xfull, W, M, N, K, epi, s, nullptr, hooks, pairs)
+                : gemm::launchGemm(xfull, W, M, N, K, epi, hooks, s, bnEnv, -ctas);
   }
   if (e != cudaSuccess) {
     VERR("vcclAllGatherGemm launch: %s", cudaGetErrorString(e));
-    return vcclInvalidArgument;
+    return gemm::launchResult(e);
   }
   return vcclSuccess;
 }

@@ -83,7 +83,7 @@ int pairMode() {
   return v[0] == '0' ? 0 : v[0] == '2' ? 2 : 1;
 }
 
-int pairMaxClusters(const void* kernel, int smemBytes) {
+int pairMaxClusters(const void* kernel, int smemBytes, int threads) {
   static std::mutex mu;
   static std::map<std::pair<int, const void*>, int> cache;
   int dev = 0;
@@ -100,7 +100,7 @@ int pairMaxClusters(const void* kernel, int smemBytes) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(smCount()), 1, 1);
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(smemBytes);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -395,8 +395,7 @@ cudaError_t gemmAuto(const void* A, const void* W, void* C, int M, int N, int K,
   const bool forcePair = pairMode() == 2 && M >= kPairBM && N >= kPairBN && bnOverride <= 0;
   if (siluMul) {
     EpiSiluMul epi{static_cast<__nv_bfloat16*>(C), N / 2};
-    if (pairPreferred(M, N, bnOverride,
-                      pairMaxClusters(pairKernelFor<EpiSiluMul>(), PairSmem<kPairStages>::kBytes))) {
+    if (pairPreferred(M, N, bnOverride, pairClustersFor<EpiSiluMul>())) {
       const cudaError_t e = launchGemmPair(A, W, M, N, K, epi, st);
       if (e != cudaErrorNotSupported || forcePair) return e;
     } else if (forcePair) {
@@ -405,7 +404,7 @@ cudaError_t gemmAuto(const void* A, const void* W, void* C, int M, int N, int K,
     return launchGemm(A, W, M, N, K, epi, NoHooks{}, st, bnOverride, 0);
   }
   EpiStore epi{static_cast<__nv_bfloat16*>(C), N};
-  if (pairPreferred(M, N, bnOverride, pairMaxClusters(pairKernelFor<EpiStore>(), PairSmem<kPairStages>::kBytes))) {
+  if (pairPreferred(M, N, bnOverride, pairClustersFor<EpiStore>())) {
     const cudaError_t e = launchGemmPair(A, W, M, N, K, epi, st);
     if (e != cudaErrorNotSupported || forcePair) return e;
   } else if (forcePair) {

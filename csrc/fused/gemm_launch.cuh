@@ -82,8 +82,8 @@ int pairGroupRows(int K);
 // 0 never, 2 for every shape of at least one pair tile.
 int pairMode();
 // Clusters of two that fit on the device at once with the pair kernel's
-// shared memory (0 if the device cannot run it).
-int pairMaxClusters(const void* kernel, int smemBytes);
+// shared memory and threads (0 if the device cannot run it).
+int pairMaxClusters(const void* kernel, int smemBytes, int threads);
 
 // True when the pair kernel finishes the shape in no more waves x tile width
 // than the one-SM kernel's choice: it moves a third less data per FLOP, so
@@ -101,18 +101,26 @@ inline bool pairPreferred(int M, int N, int bnOverride, int pairs) {
   return cost2 <= cost1;
 }
 
-template <typename Epi>
-const void* pairKernelFor() {
-  return reinterpret_cast<const void*>(gemmPairKernel<kPairStages, Epi>);
+template <typename Hooks>
+using PairSmemFor = PairSmem<kPairStages, 4 * Hooks::kEpiGroups>;
+
+// Clusters of two that fit at once for this (epilogue, policy) instance.
+template <typename Epi, typename Hooks = PairNoHooks>
+int pairClustersFor() {
+  return pairMaxClusters(reinterpret_cast<const void*>(gemmPairKernel<kPairStages, Epi, Hooks>),
+                         PairSmemFor<Hooks>::kBytes, ctaThreads<Hooks>());
 }
 
-// C = A B^T on CTA pairs with epilogue `epi` (EpiStore or EpiSiluMul).
-// Returns cudaErrorNotSupported if the device cannot co-schedule the pairs.
-template <typename Epi>
+// C = A B^T on CTA pairs with epilogue `epi` and policy `hooks`.  The grid is
+// `fixedPairs` clusters when > 0 (fused kernels size their counters by it;
+// it must not exceed pairClustersFor), else one cluster per tile up to what
+// fits.  Returns cudaErrorNotSupported if the device cannot co-schedule the
+// pairs.
+template <typename Epi, typename Hooks = PairNoHooks>
 cudaError_t launchGemmPair(const void* A, const void* B, int M, int N, int K, const Epi& epi, cudaStream_t st,
-                           int* flag = nullptr) {
-  using L = PairSmem<kPairStages>;
-  auto kern = gemmPairKernel<kPairStages, Epi>;
+                           int* flag = nullptr, const Hooks& hooks = Hooks{}, int fixedPairs = 0) {
+  using L = PairSmemFor<Hooks>;
+  auto kern = gemmPairKernel<kPairStages, Epi, Hooks>;
   static std::atomic<unsigned long long> attrDone{0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -124,8 +132,8 @@ cudaError_t launchGemmPair(const void* A, const void* B, int M, int N, int K, co
     if (e != cudaSuccess) cudaGetLastError();
     attrDone.fetch_or(bit, std::memory_order_release);
   }
-  const int maxPairs = pairMaxClusters(reinterpret_cast<const void*>(kern), L::kBytes);
-  if (maxPairs <= 0) return cudaErrorNotSupported;
+  const int maxPairs = pairMaxClusters(reinterpret_cast<const void*>(kern), L::kBytes, ctaThreads<Hooks>());
+  if (maxPairs <= 0 || fixedPairs > maxPairs) return cudaErrorNotSupported;
   CUtensorMap ma, mb;
   if (!makeMapKMajor(&ma, A, M, K, kBM) || !makeMapKMajor(&mb, B, N, K, kPairBN / 2)) return cudaErrorInvalidValue;
   GemmShape s;
@@ -137,11 +145,11 @@ cudaError_t launchGemmPair(const void* A, const void* B, int M, int N, int K, co
   s.splits = 1;
   s.aRows = kBM;
   const int tiles = s.tilesM * s.tilesN;
-  const int pairs = tiles < maxPairs ? tiles : maxPairs;
+  const int pairs = fixedPairs > 0 ? fixedPairs : tiles < maxPairs ? tiles : maxPairs;
   if (flag == nullptr) flag = errorFlag();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(ctaThreads<Hooks>()), 1, 1);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -151,7 +159,7 @@ cudaError_t launchGemmPair(const void* A, const void* B, int M, int N, int K, co
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, ma, mb, s, epi, pairGroupRows(K), flag);
+  return cudaLaunchKernelEx(&cfg, kern, ma, mb, s, epi, hooks, pairGroupRows(K), flag);
 }
 
 }  // namespace gemm

@@ -138,8 +138,13 @@ struct EpiPushRSTma {
 };
 
 template <bool kTmaStores>
-struct RsHooksT : gemm::NoHooks {
+struct RsHooksT : gemm::PairNoHooks {
   static constexpr int kEpiGroups = kRsEpiGroups;
+  // Pair tiles walk all row tiles of a column before the next column, so a
+  // wave's pushes go to every owner at once (no owner's links are a hot spot).
+  __device__ __forceinline__ gemm::TileInfo pairTileAt(const gemm::GemmShape& s, int t, int, int cta) const {
+    return gemm::pairTile(s, t, s.tilesM, cta);
+  }
   DevComm c;
   unsigned long long* trace;  // optional event trace
   // Every rank's reduction must have consumed the previous call's pushes
@@ -301,11 +306,19 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
     VERR("vcclGemmReduceScatter: %zu staging bytes exceed VCCL_FUSED_BUFFSIZE/2", slotBytes * n);
     return vcclInvalidArgument;
   }
-  const int ctas = gemm::smCount();
-  if (ctas > dev::kMaxFusedCtas) return vcclInternalError;
   cudaError_t e = cudaSuccess;
-  const int bn = bnEnv > 0 ? bnEnv : gemm::pickBN(M, N);
-  bool tma = gemm::envLongGemm("VCCL_RS_TMA") != 0 && bn / fused::kRsEpiGroups >= 64 && rowsPerRank % 32 == 0;
+  bool tma = gemm::envLongGemm("VCCL_RS_TMA") != 0 && rowsPerRank % 32 == 0;
+  // CTA pairs (256 x 256 tiles) where they take no more waves than one-SM
+  // tiles; the grid is fixed either way (the done counters count CTAs).
+  const int pairs = tma ? gemm::pairClustersFor<fused::EpiPushRSTma, fused::RsHooksT<true>>()
+                        : gemm::pairClustersFor<fused::EpiPushRS, fused::RsHooks>();
+  // The per-CTA call counters need the same grid on every call: pairs only
+  // when they cover every SM, as the one-SM grid does.
+  const bool usePair = 2 * pairs == gemm::smCount() && gemm::pairPreferred(M, N, bnEnv, pairs);
+  const int ctas = usePair ? 2 * pairs : gemm::smCount();
+  if (ctas > dev::kMaxFusedCtas) return vcclInternalError;
+  const int bn = usePair ? gemm::kPairBN : bnEnv > 0 ? bnEnv : gemm::pickBN(M, N);
+  if (tma && !usePair && bn / fused::kRsEpiGroups < 64) tma = false;
   if (tma) {
     fused::EpiPushRSTma epi{};
     epi.rowsPerRank = rowsPerRank;
@@ -316,7 +329,8 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
       fused::RsHooksT<true> hooks;
       hooks.c = dc;
       hooks.trace = comm->dev->fusedTrace;
-      e = gemm::launchGemm(A, W, M, N, K, epi, hooks, s, bn, -ctas);
+      e = usePair ? gemm::launchGemmPair(A, W, M, N, K, epi, s, nullptr, hooks, pairs)
+                  : gemm::launchGemm(A, W, M, N, K, epi, hooks, s, bn, -ctas);
     }
   }
   if (!tma) {
@@ -328,11 +342,12 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
     fused::RsHooks hooks;
     hooks.c = dc;
     hooks.trace = comm->dev->fusedTrace;
-    e = gemm::launchGemm(A, W, M, N, K, epi, hooks, s, bnEnv, -ctas);
+    e = usePair ? gemm::launchGemmPair(A, W, M, N, K, epi, s, nullptr, hooks, pairs)
+                : gemm::launchGemm(A, W, M, N, K, epi, hooks, s, bnEnv, -ctas);
   }
   if (e != cudaSuccess) {
     VERR("vcclGemmReduceScatter GEMM launch: %s", cudaGetErrorString(e));
-    return vcclInvalidArgument;
+    return gemm::launchResult(e);
   }
   fused::rsReduce<<<dev::kFusedReduceBlocks, 512, 0, s>>>(
       dc, static_cast<char*>(out), static_cast<size_t>(rowsPerRank) * N, slotBytes, comm->dev->fusedTrace);

@@ -13,7 +13,8 @@
 // from both CTAs' shared memory and leave 128 rows x 256 fp32 columns in each
 // CTA's TMEM (two such accumulators alternate, all 512 columns).
 //
-// Warp roles, both CTAs (192 threads):
+// Warp roles, both CTAs (192 threads, more with a policy's epilogue groups
+// and extra warps):
 //   warp 0     TMA producer: this CTA's A and B halves into a STAGES-deep
 //              ring.  Both CTAs' loads complete on the FIRST CTA's `full`
 //              barrier (the cta_group::2 load form; no multicast), whose
@@ -23,7 +24,13 @@
 //              publish the accumulator in BOTH CTAs (commit multicast).
 //              Second CTA: idle (it takes part in the TMEM allocation).
 //   warps 2-5  epilogue (as the one-SM kernel), on this CTA's 128 rows; the
-//              accumulator is handed back to the first CTA's `accEmpty`.
+//              accumulator is handed back to the first CTA's `accEmpty`
+//              (4 more warps per extra epilogue group, each group taking a
+//              share of the 256 columns).
+//   then       the policy's extra warps (the all-gather copy warps).
+// The policy (PairNoHooks or a fused kernel's) supplies the tile order, may
+// gate each CTA's loads on data arrival, and runs code around the tiles, as
+// it does for the one-SM kernel.
 // Every wait is bounded; a CTA that gives up unwinds, and both CTAs meet at a
 // cluster barrier before TMEM is freed, so the MMAs writing the second CTA's
 // TMEM have drained first.
@@ -38,16 +45,17 @@ constexpr int kPairBM = 256;  // rows of a pair tile
 constexpr int kPairBN = 256;  // columns of a pair tile (each CTA loads half of B)
 
 // Pair tile t in grouped order: groups of `groupRows` pair-row tiles, inside a
-// group consecutive tiles walk the rows first and share a column tile.  Row 0
-// of CTA `cta` is the tile's row 0 + 128 cta.
-__host__ __device__ inline TileInfo pairTile(const GemmShape& s, int t, int groupRows, int cta) {
+// group consecutive tiles walk the rows first and share a column tile; pair
+// rows start at `startTm` and wrap around.  Row 0 of CTA `cta` is the tile's
+// row 0 + 128 cta.
+__host__ __device__ inline TileInfo pairTileFrom(const GemmShape& s, int t, int groupRows, int startTm, int cta) {
   TileInfo ti;
   const int groupTiles = groupRows * s.tilesN;
   const int g = t / groupTiles;
   const int rowsHere = s.tilesM - g * groupRows < groupRows ? s.tilesM - g * groupRows : groupRows;
   const int local = t - g * groupTiles;
   ti.tn = local / rowsHere;
-  ti.tm = g * groupRows + local % rowsHere;
+  ti.tm = (g * groupRows + local % rowsHere + startTm) % s.tilesM;
   ti.row0 = ti.tm * kPairBM + kBM * cta;
   ti.col0 = ti.tn * kPairBN;
   ti.ks = 0;
@@ -55,16 +63,28 @@ __host__ __device__ inline TileInfo pairTile(const GemmShape& s, int t, int grou
   ti.kb1 = s.numK();
   return ti;
 }
+__host__ __device__ inline TileInfo pairTile(const GemmShape& s, int t, int groupRows, int cta) {
+  return pairTileFrom(s, t, groupRows, 0, cta);
+}
 
-template <int STAGES>
-using PairSmem = Smem<kPairBN / 2, STAGES, 4>;  // A 128 x 64 + B half 128 x 64 per stage
+// The policy of the pair kernel: NoHooks' roles (gemm_sm100.cuh) plus the
+// order of the pair tiles.  Policies of the fused kernels derive from it.
+struct PairNoHooks : NoHooks {
+  __device__ __forceinline__ TileInfo pairTileAt(const GemmShape& s, int t, int groupRows, int cta) const {
+    return pairTile(s, t, groupRows, cta);
+  }
+};
 
-template <int STAGES, typename Epi>
-__global__ void __launch_bounds__(192, 1)
+template <int STAGES, int EPI_WARPS = 4>
+using PairSmem = Smem<kPairBN / 2, STAGES, EPI_WARPS>;  // A 128 x 64 + B half 128 x 64 per stage
+
+template <int STAGES, typename Epi, typename Hooks = PairNoHooks>
+__global__ void __launch_bounds__(ctaThreads<Hooks>(), 1)
     gemmPairKernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, GemmShape s,
-                   const __grid_constant__ Epi epi, int groupRows, int* errorFlag) {
-  using L = PairSmem<STAGES>;
-  constexpr int kEpiWarps = 4;
+                   const __grid_constant__ Epi epi, Hooks hooks, int groupRows, int* errorFlag) {
+  constexpr int kEpiWarps = 4 * Hooks::kEpiGroups;
+  constexpr int kSpan = kPairBN / Hooks::kEpiGroups;
+  using L = PairSmem<STAGES, kEpiWarps>;
   constexpr uint32_t kTmemCols = 2 * kPairBN;
   extern __shared__ __align__(1024) uint8_t smemRaw[];
   // The same offset in both CTAs: the MMA reads both CTAs' stages at the
@@ -77,6 +97,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* drainBar = accEmpty + 2;
   uint32_t* tmemSlot = reinterpret_cast<uint32_t*>(drainBar + 1);
   volatile int* abortFlag = reinterpret_cast<volatile int*>(tmemSlot + 1);
+  uint32_t* hs = tmemSlot + 2;  // 8 words of policy scratch
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -94,6 +115,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     sm100::mbarInit(drainBar, 1);
     *abortFlag = 0;
+    hooks.setup(hs);
     sm100::fenceBarrierInit();
   }
   if (warp == 1) {
@@ -118,7 +140,13 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int t = pair0; t < numTiles && ok; t += pairs) {
-        const TileInfo ti = pairTile(s, t, groupRows, static_cast<int>(cta));
+        const TileInfo ti = hooks.pairTileAt(s, t, groupRows, static_cast<int>(cta));
+        // The policy may hold this CTA's rows back until their data is there.
+        if (!hooks.beforeLoad(ti, s, hs, abortFlag)) {
+          *abortFlag = 1;
+          ok = false;
+          break;
+        }
         const int bRow0 = ti.tn * kPairBN + (kPairBN / 2) * static_cast<int>(cta);
         for (int kb = ti.kb0; kb < ti.kb1; kb++) {
           if (!sm100::mbarWait(&emptyBar[stage], phase ^ 1u, abortFlag)) {
@@ -201,21 +229,27 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
-  } else {
-    // ---------------- epilogue (warps 2 .. 5, both CTAs) ----------------
+  } else if (warp < 2 + kEpiWarps) {
+    // ---------------- epilogue (warps 2 .. 1 + kEpiWarps, both CTAs) ----------------
     const int quarter = warp & 3;
     const int laneRow = quarter * 32 + lane;
+    const int cBegin = ((warp - 2) / 4) * kSpan;
     uint4* rowStage = reinterpret_cast<uint4*>(smem + L::kRowStageOff + (warp - 2) * kWarpStageBytes);
     const uint32_t accEmptyFirst0 = sm100::mapaShared(&accEmpty[0], 0);
     const uint32_t accEmptyFirst1 = sm100::mapaShared(&accEmpty[1], 0);
     int acc = 0;
     uint32_t accPhase = 0;
-    for (int t = pair0; t < numTiles; t += pairs) {
-      if (!sm100::mbarWait(&accFull[acc], accPhase, abortFlag)) break;
+    bool ok = hooks.beforeTiles(hs, abortFlag);
+    if (!ok) *abortFlag = 1;
+    for (int t = pair0; t < numTiles && ok; t += pairs) {
+      if (!sm100::mbarWait(&accFull[acc], accPhase, abortFlag)) {
+        ok = false;
+        break;
+      }
       sm100::tcFenceAfter();
-      const TileInfo ti = pairTile(s, t, groupRows, static_cast<int>(cta));
+      const TileInfo ti = hooks.pairTileAt(s, t, groupRows, static_cast<int>(cta));
       const uint32_t tmemAcc = tmemBase + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kPairBN;
-      epi.template operator()<kPairBN>(tmemAcc, ti, s, laneRow, 0, rowStage);
+      epi.template operator()<kSpan>(tmemAcc, ti, s, laneRow, cBegin, rowStage);
       sm100::tcFenceBefore();
       __syncwarp();
       if (lane == 0) sm100::mbarArriveCluster(acc == 0 ? accEmptyFirst0 : accEmptyFirst1);
@@ -224,10 +258,20 @@ __global__ void __launch_bounds__(192, 1)
         accPhase ^= 1u;
       }
     }
+    if (ok) hooks.afterTiles(hs, abortFlag);
+  } else {
+    // ---------------- extra warps (policy), both CTAs ----------------
+    hooks.extraRole(hs, abortFlag);
   }
 
   __syncthreads();
-  if (threadIdx.x == 0 && *abortFlag && errorFlag) *reinterpret_cast<volatile int*>(errorFlag) = 1;
+  if (threadIdx.x == 0) {
+    if (*abortFlag) {
+      if (errorFlag) *reinterpret_cast<volatile int*>(errorFlag) = 1;  // may live in mapped host memory
+    } else {
+      hooks.teardown(hs);
+    }
+  }
   // No MMA of the pair is in flight and no CTA still signals the other.
   sm100::tcFenceBefore();
   sm100::clusterSync();
