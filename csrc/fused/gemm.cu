@@ -365,9 +365,48 @@ SplitPlan planFor(int M, int N, int K, int bnOverride, bool allowSplit) {
   return planSplitK(M, N, K);
 }
 
+PairPlan planPair(int M, int N, int K, int bnOverride, int pairs) {
+  const int mode = pairMode();
+  if (mode == 0 || bnOverride > 0 || M < kPairBM || N < kPairBN || pairs <= 0) return {false, 1};
+  const int tiles = ((M + kPairBM - 1) / kPairBM) * ((N + kPairBN - 1) / kPairBN);
+  const int nk = (K + kBK - 1) / kBK;
+  const char* sk = std::getenv("VCCL_GEMM_SPLITK");
+  const bool splitOk = !(sk && sk[0] == '0');
+  // Time model (us), B200: a pair does a 256 x 256 x K tile in about
+  // 2 * 256 * 256 * K / 21.6e12 s (1.6 PFLOP/s over 74 pairs); partials cost
+  // their write and read at ~6 TB/s plus a launch.
+  const double wave = 2.0 * kPairBM * kPairBN * K / 21.6e6;
+  double best = 1e30;
+  int bestS = 1;
+  for (int sp = 1; sp <= 4; sp++) {
+    if (sp > 1 && (!splitOk || nk / sp < 8)) break;
+    const int waves = (tiles * sp + pairs - 1) / pairs;
+    double t = waves * wave / sp;
+    if (sp > 1) t += 2.0 * M * N * 4.0 * sp / 6.0e6 + 3.0;
+    if (t < best * 0.97) {  // a split must win clearly
+      best = t;
+      bestS = sp;
+    }
+  }
+  if (mode == 2) return {true, bestS};
+  // The one-SM kernel at its tile width, ~15 % slower per FLOP (measured at
+  // the bench shapes), its own split-K only for decode shapes.
+  const int sms = smCount();
+  const int bn = pickBN(M, N);
+  const int tiles1 = ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
+  const double wave1 = 2.0 * kBM * bn * K / (1.6e15 / sms) * 1e6 * 1.15;
+  const double t1 = ((tiles1 + sms - 1) / sms) * wave1;
+  return {best <= t1, bestS};
+}
+
 size_t gemmAutoScratchBytes(int M, int N, int K, int bnOverride, bool allowSplit) {
   const SplitPlan plan = planFor(M, N, K, bnOverride, allowSplit);
-  return plan.splits > 1 ? static_cast<size_t>(M) * N * plan.splits * sizeof(float) : 0;
+  if (plan.splits > 1) return static_cast<size_t>(M) * N * plan.splits * sizeof(float);
+  if (!allowSplit) return 0;
+  // Either epilogue's pair instance: the plans agree (same shape), only the
+  // occupancy could differ, and both are one CTA per SM.
+  const PairPlan pp = planPair(M, N, K, bnOverride, pairClustersFor<EpiStore>());
+  return pp.use && pp.splits > 1 ? static_cast<size_t>(M) * N * pp.splits * sizeof(float) : 0;
 }
 
 cudaError_t gemmAuto(const void* A, const void* W, void* C, int M, int N, int K, bool siluMul, cudaStream_t st,
@@ -393,9 +432,23 @@ cudaError_t gemmAuto(const void* A, const void* W, void* C, int M, int N, int K,
   // VCCL_GEMM_PAIR=2 demands the pair kernel for every shape it covers and
   // fails (instead of falling back) where the device cannot run it.
   const bool forcePair = pairMode() == 2 && M >= kPairBM && N >= kPairBN && bnOverride <= 0;
+  const PairPlan pp = planPair(M, N, K, bnOverride, pairClustersFor<EpiStore>());
+  if (pp.use && pp.splits > 1 && allowSplit) {
+    // Split-K on pairs: fp32 partials, then the (SiLU*mul) reduction.
+    if (ws == nullptr) return cudaErrorInvalidValue;
+    const size_t elems = static_cast<size_t>(M) * N;
+    EpiPartialF32 epi{ws, N, elems};
+    cudaError_t e = launchGemmPair(A, W, M, N, K, epi, st, nullptr, PairNoHooks{}, 0, pp.splits);
+    if (e == cudaErrorNotSupported && !forcePair) {
+      e = cudaSuccess;  // fall through to the one-SM kernel below
+    } else {
+      if (e != cudaSuccess) return e;
+      return siluMul ? launchSplitReduceSilu(ws, pp.splits, M, N, C, st) : launchSplitReduce(ws, pp.splits, elems, C, st);
+    }
+  }
   if (siluMul) {
     EpiSiluMul epi{static_cast<__nv_bfloat16*>(C), N / 2};
-    if (pairPreferred(M, N, bnOverride, pairClustersFor<EpiSiluMul>())) {
+    if (pp.use) {
       const cudaError_t e = launchGemmPair(A, W, M, N, K, epi, st);
       if (e != cudaErrorNotSupported || forcePair) return e;
     } else if (forcePair) {
@@ -404,7 +457,7 @@ cudaError_t gemmAuto(const void* A, const void* W, void* C, int M, int N, int K,
     return launchGemm(A, W, M, N, K, epi, NoHooks{}, st, bnOverride, 0);
   }
   EpiStore epi{static_cast<__nv_bfloat16*>(C), N};
-  if (pairPreferred(M, N, bnOverride, pairClustersFor<EpiStore>())) {
+  if (pp.use) {
     const cudaError_t e = launchGemmPair(A, W, M, N, K, epi, st);
     if (e != cudaErrorNotSupported || forcePair) return e;
   } else if (forcePair) {

@@ -34,6 +34,12 @@ struct SplitPlan {
   int splits;
 };
 SplitPlan planSplitK(int M, int N, int K);
+// Plan of the CTA-pair kernel for a shape: whether to use it and with how
+// many K splits (fp32 partials summed by a second kernel when > 1).
+struct PairPlan {
+  bool use;
+  int splits;
+};
 float* splitScratch(cudaStream_t st, size_t bytes);
 
 // Scratch for one call on `st`: the per-stream cached buffer, or a

@@ -85,6 +85,11 @@ int pairMode();
 // shared memory and threads (0 if the device cannot run it).
 int pairMaxClusters(const void* kernel, int smemBytes, int threads);
 
+// Pair-kernel plan with split-K (plain GEMM and SiLU*mul only): the time of
+// ceil(units / pairs) waves of units of 1 / splits of a tile, plus the fp32
+// partials' HBM traffic, against the one-SM kernel's waves; see gemm.cu.
+PairPlan planPair(int M, int N, int K, int bnOverride, int pairs);
+
 // True when the pair kernel finishes the shape in no more waves x tile width
 // than the one-SM kernel's choice: it moves a third less data per FLOP, so
 // it is taken on ties.
@@ -118,7 +123,7 @@ int pairClustersFor() {
 // pairs.
 template <typename Epi, typename Hooks = PairNoHooks>
 cudaError_t launchGemmPair(const void* A, const void* B, int M, int N, int K, const Epi& epi, cudaStream_t st,
-                           int* flag = nullptr, const Hooks& hooks = Hooks{}, int fixedPairs = 0) {
+                           int* flag = nullptr, const Hooks& hooks = Hooks{}, int fixedPairs = 0, int splits = 1) {
   using L = PairSmemFor<Hooks>;
   auto kern = gemmPairKernel<kPairStages, Epi, Hooks>;
   static std::atomic<unsigned long long> attrDone{0};
@@ -142,9 +147,10 @@ cudaError_t launchGemmPair(const void* A, const void* B, int M, int N, int K, co
   s.K = K;
   s.tilesM = (M + kPairBM - 1) / kPairBM;
   s.tilesN = (N + kPairBN - 1) / kPairBN;
-  s.splits = 1;
+  s.splits = splits < 1 ? 1 : splits;
   s.aRows = kBM;
-  const int tiles = s.tilesM * s.tilesN;
+  if (s.splits > s.numK()) return cudaErrorInvalidValue;
+  const int tiles = s.tilesM * s.tilesN * s.splits;
   const int pairs = fixedPairs > 0 ? fixedPairs : tiles < maxPairs ? tiles : maxPairs;
   if (flag == nullptr) flag = errorFlag();
   cudaLaunchConfig_t cfg = {};

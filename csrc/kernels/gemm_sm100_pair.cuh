@@ -48,8 +48,13 @@ constexpr int kPairBN = 256;  // columns of a pair tile (each CTA loads half of 
 // group consecutive tiles walk the rows first and share a column tile; pair
 // rows start at `startTm` and wrap around.  Row 0 of CTA `cta` is the tile's
 // row 0 + 128 cta.
+// With split-K (s.splits > 1), work unit t covers pair tile t % (tilesM x
+// tilesN) over the k-blocks of split t / (tilesM x tilesN).
 __host__ __device__ inline TileInfo pairTileFrom(const GemmShape& s, int t, int groupRows, int startTm, int cta) {
   TileInfo ti;
+  const int mn = s.tilesM * s.tilesN;
+  const int ks = t / mn;
+  t -= ks * mn;
   const int groupTiles = groupRows * s.tilesN;
   const int g = t / groupTiles;
   const int rowsHere = s.tilesM - g * groupRows < groupRows ? s.tilesM - g * groupRows : groupRows;
@@ -58,9 +63,10 @@ __host__ __device__ inline TileInfo pairTileFrom(const GemmShape& s, int t, int 
   ti.tm = (g * groupRows + local % rowsHere + startTm) % s.tilesM;
   ti.row0 = ti.tm * kPairBM + kBM * cta;
   ti.col0 = ti.tn * kPairBN;
-  ti.ks = 0;
-  ti.kb0 = 0;
-  ti.kb1 = s.numK();
+  const int nk = s.numK();
+  ti.ks = ks;
+  ti.kb0 = ks * nk / s.splits;
+  ti.kb1 = (ks + 1) * nk / s.splits;
   return ti;
 }
 __host__ __device__ inline TileInfo pairTile(const GemmShape& s, int t, int groupRows, int cta) {
@@ -127,7 +133,7 @@ __global__ void __launch_bounds__(ctaThreads<Hooks>(), 1)
   sm100::clusterSync();
   sm100::tcFenceAfter();
   const uint32_t tmemBase = *tmemSlot;
-  const int numTiles = s.tilesM * s.tilesN;
+  const int numTiles = s.tilesM * s.tilesN * s.splits;
   const int pair0 = static_cast<int>(sm100::clusterIdX());
   const int pairs = static_cast<int>(sm100::numClustersX());
 
@@ -193,8 +199,8 @@ __global__ void __launch_bounds__(ctaThreads<Hooks>(), 1)
           }
           sm100::tcFenceAfter();
           const uint32_t tmemAcc = tmemBase + acc * kPairBN;
-          const int nk = s.numK();
-          for (int kb = 0; kb < nk; kb++) {
+          const TileInfo ti = hooks.pairTileAt(s, t, groupRows, 0);
+          for (int kb = ti.kb0; kb < ti.kb1; kb++) {
             if (!sm100::mbarWaitCluster(&fullBar[stage], phase, abortFlag)) {
               ok = false;
               break;
@@ -206,7 +212,7 @@ __global__ void __launch_bounds__(ctaThreads<Hooks>(), 1)
             const uint64_t bd = sm100::smemDescSw128(bAddr);
 #pragma unroll
             for (int k = 0; k < kBK / 16; k++)
-              sm100::mmaBf16Pair(tmemAcc, ad + 2 * k, bd + 2 * k, idesc, (kb != 0 || k != 0) ? 1u : 0u);
+              sm100::mmaBf16Pair(tmemAcc, ad + 2 * k, bd + 2 * k, idesc, (kb != ti.kb0 || k != 0) ? 1u : 0u);
             anyIssued = true;
             sm100::mmaCommitPair(&emptyBar[stage], 0x3);
             if (++stage == STAGES) {

@@ -69,6 +69,21 @@ void checkPairTiles() {
           EXPECT(t0.kb0 == 0 && t0.kb1 == s.numK(), "pair tiles cover all of K");
         }
         EXPECT(static_cast<int>(seen.size()) == s.tilesM * s.tilesN, "pair tiles missing");
+        // split-K on pairs: every (tile, split) once, the splits partition the k-blocks
+        for (int splits : {2, 3, 4}) {
+          s.splits = splits;
+          std::vector<int> cover(static_cast<size_t>(s.tilesM) * s.tilesN * s.numK(), 0);
+          for (int t = 0; t < s.tilesM * s.tilesN * splits; t++) {
+            const TileInfo ti = pairTile(s, t, group, 0);
+            EXPECT(ti.kb0 < ti.kb1 && ti.ks == t / (s.tilesM * s.tilesN), "pair split range");
+            for (int kb = ti.kb0; kb < ti.kb1; kb++)
+              cover[(static_cast<size_t>(ti.tm) * s.tilesN + ti.tn) * s.numK() + kb]++;
+          }
+          bool once = true;
+          for (int c : cover) once = once && c == 1;
+          EXPECT(once, "pair split-K covers a k-block twice or not at all (M=%d N=%d splits=%d)", M, N, splits);
+          s.splits = 1;
+        }
       }
 }
 

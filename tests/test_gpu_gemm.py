@@ -97,8 +97,11 @@ def test_gemm_split_k(m, n, k, monkeypatch):
 
 # The CTA-pair kernel (256 x 256 tiles over two SMs, tcgen05.mma.cta_group::2),
 # forced with VCCL_GEMM_PAIR=2, against the fp32 reference and the one-SM
-# kernel (VCCL_GEMM_PAIR=0); ragged M, N and K included.
-PAIR_SHAPES = [(256, 256, 64), (512, 768, 1024), (1000, 1056, 776), (2048, 4096, 1792), (8192, 3584, 4096)]
+# kernel (VCCL_GEMM_PAIR=0); ragged M, N and K included, and shapes with too
+# few pair tiles to fill the GPU, which split K on pairs.
+PAIR_SHAPES = [(256, 256, 64), (512, 768, 1024), (1000, 1056, 776), (2048, 4096, 1792), (8192, 3584, 4096),
+               # few pair tiles: split-K on pairs (2 and 4 splits), fp32 partials + reduction
+               (512, 4096, 14336), (300, 2048, 8192)]
 
 
 @pytest.mark.parametrize("m,n,k", PAIR_SHAPES)
