@@ -389,12 +389,16 @@ PairPlan planPair(int M, int N, int K, int bnOverride, int pairs) {
     }
   }
   if (mode == 2) return {true, bestS};
-  // The one-SM kernel at its tile width, ~15 % slower per FLOP (measured at
-  // the bench shapes), its own split-K only for decode shapes.
+  // The one-SM kernel at its tile width, its own split-K only for decode
+  // shapes.  Its time per wave against the ideal, measured on B200
+  // (gemm_one): 1.18x with 256-wide tiles (8192 x 28672 x 4096), 1.38x with
+  // 128 (1024 x 4096 x 14336), 2.1x with 64 (512 x 4096 x 14336); narrower
+  // tiles re-read A from shared memory for fewer columns per MMA.
   const int sms = smCount();
   const int bn = pickBN(M, N);
+  const double charge = bn >= 256 ? 1.18 : bn == 128 ? 1.38 : bn == 64 ? 2.1 : 3.0;
   const int tiles1 = ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
-  const double wave1 = 2.0 * kBM * bn * K / (1.6e15 / sms) * 1e6 * 1.15;
+  const double wave1 = 2.0 * kBM * bn * K / (1.6e15 / sms) * 1e6 * charge;
   const double t1 = ((tiles1 + sms - 1) / sms) * wave1;
   return {best <= t1, bestS};
 }
