@@ -65,6 +65,11 @@ struct AgHooks : gemm::PairNoHooks {
   int groupRows;       // row tiles per tile group (divides the shard's tiles when possible)
   int pairStartTm;     // the same two in 256-row pair tiles (CTA-pair kernel)
   int pairGroupRows;
+  // CTA-pair kernel only: this rank's shard read in place through its own
+  // tensor map, so the own tiles start without waiting for the staging copy
+  // (which the peers still pull from).  ownDirect = 0 disables it.
+  CUtensorMap ownMap;
+  int ownDirect;
   uint32_t ctas;       // fixed grid size
   // Optional event trace (VCCL_FUSED_TRACE=1), kFusedTraceSlots times per CTA
   // from %globaltimer: 0 kernel start, 1 previous call's shard taken by every
@@ -96,8 +101,22 @@ struct AgHooks : gemm::PairNoHooks {
   __device__ __forceinline__ gemm::TileInfo pairTileAt(const gemm::GemmShape& s, int t, int, int cta) const {
     return gemm::pairTileFrom(s, t, pairGroupRows, pairStartTm, cta);
   }
+  // Own-shard rows of a CTA whose 128 rows lie inside this rank's shard.
+  __device__ __forceinline__ bool ownRows(const gemm::TileInfo& ti, const gemm::GemmShape&) const {
+    return ownDirect != 0 && ti.row0 / shardRows == c.rank;
+  }
+  __device__ __forceinline__ const CUtensorMap* aMapFor(const gemm::TileInfo& ti, const CUtensorMap* mapA,
+                                                        int* row) const {
+    // ownDirect needs shardRows % 128 == 0, so a CTA's rows never straddle two shards
+    if (ownDirect != 0 && ti.row0 / shardRows == c.rank) {
+      *row = ti.row0 - c.rank * shardRows;
+      return &ownMap;
+    }
+    return mapA;
+  }
   __device__ __forceinline__ bool beforeLoad(const gemm::TileInfo& ti, const gemm::GemmShape& s, uint32_t* hs,
                                              volatile int*) const {
+    if (ownRows(ti, s)) return true;  // read in place: nothing to wait for
     const uint32_t k = hs[0];
     const int last = (ti.row0 + gemm::kBM < s.M ? ti.row0 + gemm::kBM : s.M) - 1;
     for (int q = ti.row0 / shardRows; q <= last / shardRows; q++) {
@@ -276,6 +295,9 @@ extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, voi
       break;
     }
   hooks.ctas = static_cast<uint32_t>(ctas);
+  hooks.ownDirect = 0;
+  if (usePair && gemm::envLongGemm("VCCL_AG_OWN_STAGED") == 0 && (M / n) % gemm::kBM == 0)
+    hooks.ownDirect = gemm::makeMapKMajor(&hooks.ownMap, xShard, M / n, K, gemm::kBM) ? 1 : 0;
   hooks.trace = comm->dev->fusedTrace;
   const char* xfull = dc.fused[comm->rank] + xOff;
   if (siluMul) {

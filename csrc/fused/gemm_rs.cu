@@ -199,6 +199,164 @@ struct RsHooksT : gemm::PairNoHooks {
 
 using RsHooks = RsHooksT<false>;
 
+// ---- one kernel on CTA pairs: pushes, then the reduction in the owner's epilogue ----
+//
+// Every rank walks its pair tiles starting at the rows of rank me + 1 and
+// ending with its own rows, in shard-aligned groups.  At any moment the
+// ranks push to different owners (no owner's links take every sender at
+// once), and the last tiles, this rank's own rows, push nothing.  A CTA
+// that pushed a 128-row half tile to owner q bumps q's arrival counter for
+// that half tile (release, after all eight epilogue warps stored).  For its
+// own rows the epilogue waits until the n - 1 other ranks' halves of that
+// tile have arrived, adds them (bf16, from its slots) to its fp32
+// accumulator and writes the output rows: no second kernel, and this rank's
+// own partial is never rounded to bf16 before the sum.
+//
+// Per call: CTAs first wait until every owner has read the previous call's
+// pushes (free[q]), as the two-kernel path does; after their tiles, the last
+// CTA of this rank tells every rank once that it has read its slots.
+// Counters are monotonic; the per-CTA count of pair-path calls sets the
+// arrival targets (every rank takes the same path for the same call), and
+// the GEMM call count and local done count advance as the two-kernel path
+// expects, so the two paths can alternate on one communicator.
+
+__device__ __forceinline__ uint32_t pairRsCall(const DevComm& c) {
+  return dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsPairCallsOff)[blockIdx.x];
+}
+
+struct EpiRsPair {
+  DevComm c;
+  __nv_bfloat16* out;  // [rowsPerRank, N], this rank's rows of the sum
+  size_t slotBytes;    // one source's slot in an owner's fused region
+  int rowsPerRank;
+  int ldn;             // N
+  int tilesN;          // 256-wide column tiles
+  template <int SPAN>
+  __device__ __forceinline__ void operator()(uint32_t tmemAcc, const gemm::TileInfo& ti, const gemm::GemmShape& s,
+                                             int laneRow, int cBegin, uint4* st) const {
+    if (ti.row0 >= s.M) return;  // the second CTA's half of a pair tile past M (uniform over the warps)
+    const int me = c.rank, n = c.nranks;
+    const int owner = ti.row0 / rowsPerRank;
+    const int half = ((ti.row0 - owner * rowsPerRank) / gemm::kBM) * tilesN + ti.tn;
+    const size_t pitch = static_cast<size_t>(ldn) * 2;
+    if (owner != me) {
+      char* dst = c.fused[owner] + static_cast<size_t>(me) * slotBytes;
+      gemm::storeAccRows<SPAN>(tmemAcc, ti, s, laneRow, cBegin, st, [&](int row) {
+        return dst + static_cast<size_t>(row - owner * rowsPerRank) * pitch;
+      });
+      epilogueBarrier();  // every epilogue warp's stores of this half tile are issued
+      if (threadIdx.x == 64) {
+        dev::fenceSys();
+        redAddReleaseSys(dev::ctrlAt<uint32_t>(c, owner, dev::kRsArriveOff) + half, 1u);
+      }
+      return;
+    }
+    // Own rows: wait for the other ranks' pushes of this half tile, then sum.
+    const int lane = laneRow & 31;
+    if (lane == 0) {
+      const uint32_t target = (pairRsCall(c) + 1u) * static_cast<uint32_t>(n - 1);
+      (void)dev::waitAcquire(c, dev::ctrlAt<uint32_t>(c, me, dev::kRsArriveOff) + half, target, dev::kWhereFused,
+                             600 + owner, 64);
+    }
+    __syncwarp();
+    constexpr int CW = SPAN < 64 ? SPAN : 64;
+    constexpr int NC = CW / 8;
+    const int warpRow0 = ti.row0 + (laneRow & ~31);
+    const int row = warpRow0 + lane;
+    const size_t rowOff = static_cast<size_t>(row - me * rowsPerRank) * pitch;
+    const char* slots = c.fused[me];
+    char* obase = reinterpret_cast<char*>(out);
+#pragma unroll 1
+    for (int cc = cBegin; cc < cBegin + SPAN; cc += CW) {
+      uint32_t r[CW];
+#pragma unroll
+      for (int i = 0; i < CW / 16; i++) sm100::tmemLoad16p(tmemAcc + cc + 16 * i, r + 16 * i);
+      sm100::tmemLoadWait();
+      float acc[CW];
+#pragma unroll
+      for (int i = 0; i < CW; i++) acc[i] = __uint_as_float(r[i]);
+      const int col0 = ti.col0 + cc;
+      if (row < s.M) {
+        for (int p = 0; p < n; p++) {
+          if (p == me) continue;
+          const char* src = slots + static_cast<size_t>(p) * slotBytes + rowOff + static_cast<size_t>(col0) * 2;
+#pragma unroll
+          for (int j = 0; j < NC; j++) {
+            if (col0 + 8 * j >= s.N) break;
+            const uint4 v = dev::ldCG(src + 16 * j);
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+              const float2 f = __bfloat1622float2(h[e]);
+              acc[8 * j + 2 * e] += f.x;
+              acc[8 * j + 2 * e + 1] += f.y;
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < NC; j++) {
+        uint4 o;
+        o.x = gemm::packBf16(acc[8 * j], acc[8 * j + 1]);
+        o.y = gemm::packBf16(acc[8 * j + 2], acc[8 * j + 3]);
+        o.z = gemm::packBf16(acc[8 * j + 4], acc[8 * j + 5]);
+        o.w = gemm::packBf16(acc[8 * j + 6], acc[8 * j + 7]);
+        gemm::stagePut<NC>(st, lane, j, o);
+      }
+      gemm::stageFlush<NC>(st, lane, [&](int rr, int ch, uint4 v) {
+        const int orow = warpRow0 + rr, col = col0 + ch * 8;
+        if (orow < s.M && col < s.N)
+          *reinterpret_cast<uint4*>(obase + static_cast<size_t>(orow - me * rowsPerRank) * pitch +
+                                    static_cast<size_t>(col) * 2) = v;
+      });
+    }
+  }
+};
+
+struct RsPairHooks : gemm::PairNoHooks {
+  static constexpr int kEpiGroups = kRsEpiGroups;
+  DevComm c;
+  int pairStartTm;    // first pair row: the rows of rank me + 1
+  int pairGroupRows;  // shard-aligned tile groups
+  __device__ __forceinline__ gemm::TileInfo pairTileAt(const gemm::GemmShape& s, int t, int, int cta) const {
+    return gemm::pairTileFrom(s, t, pairGroupRows, pairStartTm, cta);
+  }
+  // Every owner must have read the previous call's pushes (free[q] counts
+  // calls in which rank q finished with its slots).
+  __device__ __forceinline__ bool beforeTiles(uint32_t*, volatile int* abortFlag) const {
+    __shared__ int sFail;
+    if (threadIdx.x == 64) {
+      sFail = 0;
+      const uint32_t k = dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsGemmCallsOff)[blockIdx.x];
+      const uint32_t* freeCnt = dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsFreeOff);
+      for (int q = 0; q < c.nranks; q++)
+        if (!dev::waitAcquire(c, freeCnt + q, k, dev::kWhereFused, 100 + q, 64)) sFail = 1;
+    }
+    epilogueBarrier();
+    return sFail == 0 && !*abortFlag;
+  }
+  // This CTA's own-row tiles have read their slots; the last CTA of the call
+  // tells every rank once (free[me] += 1) and resets the CTA count.
+  __device__ __forceinline__ void afterTiles(uint32_t*, volatile int*) const {
+    epilogueBarrier();
+    if (threadIdx.x == 64) {
+      const int me = c.rank;
+      uint32_t* calls = dev::ctrlAt<uint32_t>(c, me, dev::kRsGemmCallsOff) + blockIdx.x;
+      uint32_t* pcalls = dev::ctrlAt<uint32_t>(c, me, dev::kRsPairCallsOff) + blockIdx.x;
+      atomicAdd(dev::ctrlAt<uint32_t>(c, me, dev::kRsLocalDoneOff), 1u);  // the two-kernel path's CTA count
+      *calls = *calls + 1u;
+      *pcalls = *pcalls + 1u;
+      dev::fenceSys();
+      uint32_t* cnt = dev::ctrlAt<uint32_t>(c, me, dev::kRsPairFreeOff);
+      if (atomicAdd(cnt, 1u) == gridDim.x - 1u) {
+        *cnt = 0u;  // every CTA of this call has counted (the next call starts after this kernel)
+        dev::fenceSys();
+        for (int q = 0; q < c.nranks; q++) redAddReleaseSys(dev::ctrlAt<uint32_t>(c, q, dev::kRsFreeOff) + me, 1u);
+      }
+    }
+  }
+};
+
 // out[rowsPerRank, N] = sum over sources of my slots.
 __global__ void __launch_bounds__(512) rsReduce(DevComm c, char* out, size_t elems, size_t slotBytes,
                                                 unsigned long long* trace) {
@@ -302,6 +460,41 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
   }
   const size_t slotBytes = (static_cast<size_t>(rowsPerRank) * N * 2 + 255) / 256 * 256;
   const dev::DevComm& dc = comm->dev->dc;
+  // One kernel on CTA pairs (pushes + reduction in the owner's epilogue) when
+  // the pair grid covers every SM, each CTA's 128 rows have one owner and
+  // the owner's tiles fit the arrival counters.
+  if (slotBytes * n <= dc.fusedBytes / 2 && rowsPerRank % gemm::kBM == 0 && gemm::envLongGemm("VCCL_RS_TMA") == 0 &&
+      gemm::envLongGemm("VCCL_RS_TWO_KERNELS") == 0) {
+    const int pairs = gemm::pairClustersFor<fused::EpiRsPair, fused::RsPairHooks>();
+    const int tilesN = (N + gemm::kPairBN - 1) / gemm::kPairBN;
+    if (2 * pairs == gemm::smCount() && pairs <= dev::kMaxFusedCtas / 2 &&
+        (rowsPerRank / gemm::kBM) * tilesN <= dev::kRsMaxHalves && gemm::pairPreferred(M, N, bnEnv, pairs)) {
+      fused::EpiRsPair epi;
+      epi.c = dc;
+      epi.out = static_cast<__nv_bfloat16*>(out);
+      epi.slotBytes = slotBytes;
+      epi.rowsPerRank = rowsPerRank;
+      epi.ldn = N;
+      epi.tilesN = tilesN;
+      fused::RsPairHooks hooks;
+      hooks.c = dc;
+      const int tilesM = (M + gemm::kPairBM - 1) / gemm::kPairBM;
+      hooks.pairStartTm = (((comm->rank + 1) % n) * rowsPerRank / gemm::kPairBM) % tilesM;
+      const int shardPairTiles = rowsPerRank % gemm::kPairBM == 0 ? rowsPerRank / gemm::kPairBM : 0;
+      hooks.pairGroupRows = 1;
+      for (int gsz = 16; gsz >= 1; gsz /= 2)
+        if (shardPairTiles > 0 && shardPairTiles % gsz == 0) {
+          hooks.pairGroupRows = gsz;
+          break;
+        }
+      cudaError_t e = gemm::launchGemmPair(A, W, M, N, K, epi, s, nullptr, hooks, pairs);
+      if (e != cudaSuccess) {
+        VERR("vcclGemmReduceScatter (pairs) launch: %s", cudaGetErrorString(e));
+        return gemm::launchResult(e);
+      }
+      return vcclSuccess;
+    }
+  }
   if (slotBytes * n > dc.fusedBytes / 2) {
     VERR("vcclGemmReduceScatter: %zu staging bytes exceed VCCL_FUSED_BUFFSIZE/2", slotBytes * n);
     return vcclInvalidArgument;

@@ -57,6 +57,11 @@ constexpr size_t kMoeCombEpochOff = kMoeOff + 132;          // u32, local: combi
 constexpr size_t kMoeBlocksOff = kMoeOff + 192;             // u32[4], local: per-kernel block counters
 constexpr size_t kWinDescOff = 81920;                       // WinDesc[kMaxBlocks], read by peers (window calls)
 constexpr size_t kWinA2aOff = 90112;                        // u64[kMaxBlocks][kMaxRanks][2]: all-to-all(v) receive table
+// GEMM + reduce-scatter on CTA pairs (one kernel, reduction in the owner's epilogue)
+constexpr int kRsMaxHalves = 8192;                          // 128-row x 256-column tiles of one owner's rows
+constexpr size_t kRsArriveOff = 131072;                     // u32[kRsMaxHalves], written by peers: pushes landed
+constexpr size_t kRsPairCallsOff = kRsArriveOff + kRsMaxHalves * 4;  // u32[kMaxFusedCtas], local
+constexpr size_t kRsPairFreeOff = kRsPairCallsOff + kMaxFusedCtas * 4;  // u32, local: CTAs done this call
 constexpr size_t kCtrlHeader = 1 << 20;
 // The header's ranges must not overlap.
 static_assert(kLLEpochOff + kMaxLLBlocks * 4 <= kP2pHeadOff, "epochs overlap the p2p counters");
@@ -66,7 +71,8 @@ static_assert(kRsLocalFreeOff + 4 <= kAgReadyOff, "reduce-scatter counters overl
 static_assert(kAgStagedOff + 4 <= kMoeOff, "all-gather counters overlap the MoE counters");
 static_assert(kMoeBlocksOff + 16 <= kWinDescOff, "MoE counters overlap the window descriptors");
 static_assert(kWinDescOff + kMaxBlocks * 32 <= kWinA2aOff, "window descriptors overlap the all-to-all tables");
-static_assert(kWinA2aOff + kMaxBlocks * kMaxRanks * 16 <= kCtrlHeader, "all-to-all tables leave the header");
+static_assert(kWinA2aOff + kMaxBlocks * kMaxRanks * 16 <= kRsArriveOff, "all-to-all tables overlap the arrivals");
+static_assert(kRsPairFreeOff + 4 <= kCtrlHeader, "pair reduce-scatter counters leave the header");
 constexpr unsigned char kGuardByte = 0xA5;  // fill of the debug guard regions (VCCL_GUARDS=1)
 
 constexpr size_t kLLMaxBytes = 1 << 20;                 // largest LL payload per source rank

@@ -79,6 +79,11 @@ struct PairNoHooks : NoHooks {
   __device__ __forceinline__ TileInfo pairTileAt(const GemmShape& s, int t, int groupRows, int cta) const {
     return pairTile(s, t, groupRows, cta);
   }
+  // Tensor map (and its row coordinate) this CTA reads its A rows of tile
+  // `ti` through: by default the kernel's A map at the tile's rows.
+  __device__ __forceinline__ const CUtensorMap* aMapFor(const TileInfo&, const CUtensorMap* mapA, int*) const {
+    return mapA;
+  }
 };
 
 template <int STAGES, int EPI_WARPS = 4>
@@ -87,7 +92,8 @@ using PairSmem = Smem<kPairBN / 2, STAGES, EPI_WARPS>;  // A 128 x 64 + B half 1
 template <int STAGES, typename Epi, typename Hooks = PairNoHooks>
 __global__ void __launch_bounds__(ctaThreads<Hooks>(), 1)
     gemmPairKernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, GemmShape s,
-                   const __grid_constant__ Epi epi, Hooks hooks, int groupRows, int* errorFlag) {
+                   const __grid_constant__ Epi epi, const __grid_constant__ Hooks hooks, int groupRows,
+                   int* errorFlag) {
   constexpr int kEpiWarps = 4 * Hooks::kEpiGroups;
   constexpr int kSpan = kPairBN / Hooks::kEpiGroups;
   using L = PairSmem<STAGES, kEpiWarps>;
@@ -154,6 +160,9 @@ __global__ void __launch_bounds__(ctaThreads<Hooks>(), 1)
           break;
         }
         const int bRow0 = ti.tn * kPairBN + (kPairBN / 2) * static_cast<int>(cta);
+        // The policy may read this CTA's A rows through another tensor map.
+        int aRow = ti.row0;
+        const CUtensorMap* aMap = hooks.aMapFor(ti, &mapA, &aRow);
         for (int kb = ti.kb0; kb < ti.kb1; kb++) {
           if (!sm100::mbarWait(&emptyBar[stage], phase ^ 1u, abortFlag)) {
             ok = false;
@@ -164,7 +173,7 @@ __global__ void __launch_bounds__(ctaThreads<Hooks>(), 1)
           if (first)
             sm100::mbarArriveExpectTx(&fullBar[stage], static_cast<uint32_t>(2 * (L::kABytes + L::kBBytes)));
           const uint32_t bar = sm100::mapaShared(&fullBar[stage], 0);
-          sm100::tmaLoad2dPair(a, &mapA, bar, kb * kBK, ti.row0);
+          sm100::tmaLoad2dPair(a, aMap, bar, kb * kBK, aRow);
           sm100::tmaLoad2dPair(b, &mapB, bar, kb * kBK, bRow0);
           if (++stage == STAGES) {
             stage = 0;
