@@ -215,14 +215,13 @@ using RsHooks = RsHooksT<false>;
 // Per call: CTAs first wait until every owner has read the previous call's
 // pushes (free[q]), as the two-kernel path does; after their tiles, the last
 // CTA of this rank tells every rank once that it has read its slots.
-// Counters are monotonic; the per-CTA count of pair-path calls sets the
-// arrival targets (every rank takes the same path for the same call), and
-// the GEMM call count and local done count advance as the two-kernel path
-// expects, so the two paths can alternate on one communicator.
-
-__device__ __forceinline__ uint32_t pairRsCall(const DevComm& c) {
-  return dev::ctrlAt<uint32_t>(c, c.rank, dev::kRsPairCallsOff)[blockIdx.x];
-}
+// Arrival counters are monotonic, and calls of different shapes use
+// different sets of them, so the owner keeps, per half tile, the count it has
+// already consumed: a call's pushes have all landed when the counter is
+// consumed + (n - 1) (senders of the next call wait for free[owner], which
+// comes after the owner consumed every half of this call).  The GEMM call
+// count and local done count advance as the two-kernel path expects, so the
+// two paths can alternate on one communicator.
 
 struct EpiRsPair {
   DevComm c;
@@ -253,11 +252,11 @@ struct EpiRsPair {
     }
     // Own rows: wait for the other ranks' pushes of this half tile, then sum.
     const int lane = laneRow & 31;
-    if (lane == 0) {
-      const uint32_t target = (pairRsCall(c) + 1u) * static_cast<uint32_t>(n - 1);
+    uint32_t* consumed = dev::ctrlAt<uint32_t>(c, me, dev::kRsConsumedOff) + half;
+    const uint32_t target = *consumed + static_cast<uint32_t>(n - 1);
+    if (lane == 0)
       (void)dev::waitAcquire(c, dev::ctrlAt<uint32_t>(c, me, dev::kRsArriveOff) + half, target, dev::kWhereFused,
                              600 + owner, 64);
-    }
     __syncwarp();
     constexpr int CW = SPAN < 64 ? SPAN : 64;
     constexpr int NC = CW / 8;
@@ -310,6 +309,8 @@ struct EpiRsPair {
                                     static_cast<size_t>(col) * 2) = v;
       });
     }
+    epilogueBarrier();  // every epilogue warp has read `consumed`
+    if (threadIdx.x == 64) *consumed = target;
   }
 };
 
@@ -342,10 +343,8 @@ struct RsPairHooks : gemm::PairNoHooks {
     if (threadIdx.x == 64) {
       const int me = c.rank;
       uint32_t* calls = dev::ctrlAt<uint32_t>(c, me, dev::kRsGemmCallsOff) + blockIdx.x;
-      uint32_t* pcalls = dev::ctrlAt<uint32_t>(c, me, dev::kRsPairCallsOff) + blockIdx.x;
       atomicAdd(dev::ctrlAt<uint32_t>(c, me, dev::kRsLocalDoneOff), 1u);  // the two-kernel path's CTA count
       *calls = *calls + 1u;
-      *pcalls = *pcalls + 1u;
       dev::fenceSys();
       uint32_t* cnt = dev::ctrlAt<uint32_t>(c, me, dev::kRsPairFreeOff);
       if (atomicAdd(cnt, 1u) == gridDim.x - 1u) {

@@ -60,8 +60,8 @@ constexpr size_t kWinA2aOff = 90112;                        // u64[kMaxBlocks][k
 // GEMM + reduce-scatter on CTA pairs (one kernel, reduction in the owner's epilogue)
 constexpr int kRsMaxHalves = 8192;                          // 128-row x 256-column tiles of one owner's rows
 constexpr size_t kRsArriveOff = 131072;                     // u32[kRsMaxHalves], written by peers: pushes landed
-constexpr size_t kRsPairCallsOff = kRsArriveOff + kRsMaxHalves * 4;  // u32[kMaxFusedCtas], local
-constexpr size_t kRsPairFreeOff = kRsPairCallsOff + kMaxFusedCtas * 4;  // u32, local: CTAs done this call
+constexpr size_t kRsConsumedOff = kRsArriveOff + kRsMaxHalves * 4;   // u32[kRsMaxHalves], local: arrivals used
+constexpr size_t kRsPairFreeOff = kRsConsumedOff + kRsMaxHalves * 4;  // u32, local: CTAs done this call
 constexpr size_t kCtrlHeader = 1 << 20;
 // The header's ranges must not overlap.
 static_assert(kLLEpochOff + kMaxLLBlocks * 4 <= kP2pHeadOff, "epochs overlap the p2p counters");

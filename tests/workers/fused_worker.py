@@ -100,6 +100,20 @@ def main():
         close(out, ref, 2e-2, "gemm+rs at the bench shard shape")
         del As, Ws, out, ref
 
+    # --- GEMM + reduce-scatter of changing shapes in a row (the CTA-pair path keeps
+    # per-tile arrival counts across calls whose tiles differ), against fp32
+    for m in (8192, 1024, 8192, 2048, 4096, 8192):
+        if m % world or (m // world) % 128:
+            continue
+        g.manual_seed(5000 + m)
+        As = [torch.randn(m, 512, device="cuda", generator=g).bfloat16() for _ in range(world)]
+        Ws = [(torch.randn(4096, 512, device="cuda", generator=g) * 0.05).bfloat16() for _ in range(world)]
+        per = m // world
+        out = gemm_reduce_scatter(comm, As[rank], Ws[rank])
+        torch.cuda.synchronize()
+        ref = sum(a[rank * per:(rank + 1) * per].float() @ w.float().T for a, w in zip(As, Ws))
+        close(out, ref, 2e-2, f"gemm+rs shape sequence m={m}")
+
     err = comm.async_error()
     comm.destroy()
     if err != 0:
