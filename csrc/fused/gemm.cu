@@ -362,6 +362,14 @@ void releaseScratch(const Scratch& s) {
 SplitPlan planFor(int M, int N, int K, int bnOverride, bool allowSplit) {
   const char* sk = std::getenv("VCCL_GEMM_SPLITK");
   if (!allowSplit || bnOverride > 0 || (sk && sk[0] == '0')) return {0, 1};
+  // VCCL_GEMM_SPLITS=s forces s K splits of 128-wide tiles on decode shapes
+  // (for measurements; 1 = no split).
+  const long forced = envLongGemm("VCCL_GEMM_SPLITS");
+  if (forced > 0 && (M + kBM - 1) / kBM <= 2) {
+    const int numK = (K + kBK - 1) / kBK;
+    const int sp = static_cast<int>(forced < numK ? forced : numK);
+    return sp > 1 ? SplitPlan{128, sp} : SplitPlan{0, 1};
+  }
   return planSplitK(M, N, K);
 }
 

@@ -44,12 +44,16 @@ __device__ __forceinline__ void mbarArriveExpectTx(uint64_t* bar, uint32_t bytes
 __device__ __forceinline__ void mbarArrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smemAddr(bar)) : "memory");
 }
+// try_wait without a suspend-time hint: with a long hint (1 ms was used) a
+// waiter whose phase completes late can stay suspended for most of the hint;
+// the plain form returns within the hardware's own short limit and the
+// callers loop.
 __device__ __forceinline__ bool mbarTryWait(uint64_t* bar, uint32_t phase) {
   uint32_t ok = 0;
   asm volatile(
-      "{\n .reg .pred P;\n mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n selp.b32 %0, 1, 0, P;\n}\n"
+      "{\n .reg .pred P;\n mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n selp.b32 %0, 1, 0, P;\n}\n"
       : "=r"(ok)
-      : "r"(smemAddr(bar)), "r"(phase), "r"(1000000u)
+      : "r"(smemAddr(bar)), "r"(phase)
       : "memory");
   return ok != 0;
 }
@@ -219,9 +223,9 @@ __device__ __forceinline__ void mbarArriveCluster(uint32_t clusterAddr) {
 __device__ __forceinline__ bool mbarTryWaitCluster(uint64_t* bar, uint32_t phase) {
   uint32_t ok = 0;
   asm volatile(
-      "{\n .reg .pred P;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2, %3;\n selp.b32 %0, 1, 0, P;\n}\n"
+      "{\n .reg .pred P;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n selp.b32 %0, 1, 0, P;\n}\n"
       : "=r"(ok)
-      : "r"(smemAddr(bar)), "r"(phase), "r"(1000000u)
+      : "r"(smemAddr(bar)), "r"(phase)
       : "memory");
   return ok != 0;
 }
