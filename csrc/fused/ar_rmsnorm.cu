@@ -168,6 +168,31 @@ __device__ __forceinline__ int rowBegin(int q, int rows, int n) {
 
 constexpr int kMaxPacksPerThread = 8;  // hidden <= 512 threads * 8 packs * 8 = 32768
 
+// Copies `count` rows of rowBytes (a multiple of 16) with the whole block,
+// row i from srcRow(i) to dstRow(i), keeping kCopyDepth 16-byte loads in
+// flight per thread across rows: the pushes and pulls of a block's rows to
+// and from its peers are latency-bound over NVLink when done row by row.
+constexpr int kCopyDepth = 8;
+template <typename Dst, typename Src>
+__device__ __forceinline__ void copyRows(int count, size_t rowBytes, Dst&& dstRow, Src&& srcRow) {
+  const size_t per = rowBytes / 16;
+  const size_t total = per * static_cast<size_t>(count);
+  const size_t nthr = blockDim.x;
+  for (size_t base = threadIdx.x; base < total; base += nthr * kCopyDepth) {
+    uint4 v[kCopyDepth];
+#pragma unroll
+    for (int u = 0; u < kCopyDepth; u++) {
+      const size_t i = base + u * nthr;
+      if (i < total) v[u] = ldCG(srcRow(static_cast<int>(i / per)) + (i % per) * 16);
+    }
+#pragma unroll
+    for (int u = 0; u < kCopyDepth; u++) {
+      const size_t i = base + u * nthr;
+      if (i < total) stG(dstRow(static_cast<int>(i / per)) + (i % per) * 16, v[u]);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kNormThreads) arRmsNormTwoShot(DevComm c, NormArgs a, size_t slotRows) {
   const int blk = blockIdx.x, G = gridDim.x, n = c.nranks, me = c.rank;
   const size_t rowBytes = static_cast<size_t>(a.hidden) * 2;
@@ -175,12 +200,47 @@ __global__ void __launch_bounds__(kNormThreads) arRmsNormTwoShot(DevComm c, Norm
   char* mine = c.data[me];
   __shared__ float scratch[33];
   if (!blockBarrier(c, blk, kWhereStart)) return;
-  // 1. push partial rows to their owners
-  for (int q = 0; q < n; q++) {
-    if (q == me) continue;
-    const int r0 = rowBegin(q, a.rows, n), r1 = rowBegin(q + 1, a.rows, n);
-    for (int lr = blk; r0 + lr < r1; lr += G)
-      copyAny(c.data[q] + me * slotBytes + lr * rowBytes, a.partial + (r0 + lr) * rowBytes, rowBytes);
+  // 1. push partial rows to their owners: this block's rows of every owner,
+  //    all in flight together (row j: owner q = me + 1 + j / perOwner, local
+  //    row blk + (j % perOwner) G of that owner's chunk)
+  const int perOwner = (a.rows / n + 1 + G - 1) / G;  // upper bound of this block's rows per owner
+  {
+    auto owner = [&](int j) { return (me + 1 + j / perOwner) % n; };
+    auto localRow = [&](int j) { return blk + (j % perOwner) * G; };
+    auto valid = [&](int j) {
+      const int q = owner(j);
+      return rowBegin(q, a.rows, n) + localRow(j) < rowBegin(q + 1, a.rows, n);
+    };
+    // Compact the valid (owner, row) pairs into a small table so the copy
+    // loop indexes rows directly.
+    __shared__ int sRow[kMaxRanks * 64];
+    __shared__ int sCount;
+    if (threadIdx.x == 0) {
+      int k = 0;
+      for (int j = 0; j < (n - 1) * perOwner && k < kMaxRanks * 64; j++)
+        if (valid(j)) sRow[k++] = j;
+      sCount = k;
+    }
+    __syncthreads();
+    const int total = sCount;
+    const bool fits = (n - 1) * perOwner <= kMaxRanks * 64;
+    if (fits) {
+      copyRows(
+          total, rowBytes,
+          [&](int i) { return c.data[owner(sRow[i])] + me * slotBytes + localRow(sRow[i]) * rowBytes; },
+          [&](int i) {
+            const int q = owner(sRow[i]);
+            return a.partial + (rowBegin(q, a.rows, n) + localRow(sRow[i])) * rowBytes;
+          });
+    } else {
+      for (int q = 0; q < n; q++) {
+        if (q == me) continue;
+        const int r0 = rowBegin(q, a.rows, n), r1 = rowBegin(q + 1, a.rows, n);
+        for (int lr = blk; r0 + lr < r1; lr += G)
+          copyAny(c.data[q] + me * slotBytes + lr * rowBytes, a.partial + (r0 + lr) * rowBytes, rowBytes);
+      }
+    }
+    __syncthreads();
   }
   if (!blockBarrier(c, blk, kWherePush)) return;
   // 2. reduce + residual + norm for my rows; publish x and out
@@ -226,13 +286,48 @@ __global__ void __launch_bounds__(kNormThreads) arRmsNormTwoShot(DevComm c, Norm
     }
   }
   if (!blockBarrier(c, blk, kWhereReduce)) return;
-  // 3. pull the rows owned by the other ranks
-  for (int q = 0; q < n; q++) {
-    if (q == me) continue;
-    const int r0 = rowBegin(q, a.rows, n), r1 = rowBegin(q + 1, a.rows, n);
-    for (int lr = blk; r0 + lr < r1; lr += G) {
-      copyAny(a.residual + (r0 + lr) * rowBytes, c.data[q] + n * slotBytes + lr * rowBytes, rowBytes);
-      copyAny(a.out + (r0 + lr) * rowBytes, c.data[q] + (n + 1) * slotBytes + lr * rowBytes, rowBytes);
+  // 3. pull the rows owned by the other ranks (residual and output of each),
+  //    all of this block's rows in flight together
+  {
+    __shared__ int sPull[2 * kMaxRanks * 64];
+    __shared__ int sPullCount;
+    const bool fits = 2 * (n - 1) * perOwner <= 2 * kMaxRanks * 64;
+    if (threadIdx.x == 0) {
+      int k = 0;
+      for (int j = 0; fits && j < (n - 1) * perOwner; j++) {
+        const int q = (me + 1 + j / perOwner) % n;
+        const int lr = blk + (j % perOwner) * G;
+        if (rowBegin(q, a.rows, n) + lr < rowBegin(q + 1, a.rows, n)) {
+          sPull[k++] = 2 * j;      // residual row
+          sPull[k++] = 2 * j + 1;  // output row
+        }
+      }
+      sPullCount = k;
+    }
+    __syncthreads();
+    auto ownerOf = [&](int e) { return (me + 1 + (e / 2) / perOwner) % n; };
+    auto lrOf = [&](int e) { return blk + ((e / 2) % perOwner) * G; };
+    if (fits) {
+      copyRows(
+          sPullCount, rowBytes,
+          [&](int i) {
+            const int e = sPull[i];
+            const int q = ownerOf(e);
+            return (e & 1 ? a.out : a.residual) + (rowBegin(q, a.rows, n) + lrOf(e)) * rowBytes;
+          },
+          [&](int i) {
+            const int e = sPull[i];
+            return c.data[ownerOf(e)] + ((e & 1) ? n + 1 : n) * slotBytes + lrOf(e) * rowBytes;
+          });
+    } else {
+      for (int q = 0; q < n; q++) {
+        if (q == me) continue;
+        const int r0 = rowBegin(q, a.rows, n), r1 = rowBegin(q + 1, a.rows, n);
+        for (int lr = blk; r0 + lr < r1; lr += G) {
+          copyAny(a.residual + (r0 + lr) * rowBytes, c.data[q] + n * slotBytes + lr * rowBytes, rowBytes);
+          copyAny(a.out + (r0 + lr) * rowBytes, c.data[q] + (n + 1) * slotBytes + lr * rowBytes, rowBytes);
+        }
+      }
     }
   }
 }
