@@ -133,6 +133,11 @@ def run_vccl(args) -> int:
     times = time_steps(lambda: mlp.forward(x), args.steps, flush)
     clocks = sampler.stop() if rank == 0 else {}
     value = max_over_ranks(sum(times) / len(times))
+    # spread of the K timed steps (each statistic max over ranks): a single
+    # slow step shows up here rather than only in the mean
+    srt = sorted(times)
+    step_stats = {"min": round(max_over_ranks(srt[0]), 2), "median": round(max_over_ranks(srt[len(srt) // 2]), 2),
+                  "max": round(max_over_ranks(srt[-1]), 2)}
     per_step_launches = 3 if world > 1 else 2
 
     # end to end through the public API: pinned H2D input, forward, D2H output
@@ -181,6 +186,7 @@ def run_vccl(args) -> int:
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": round(value / 1000.0, 4),
+            "steps_us": step_stats,
             "higher_is_better": False,
             "scaling": "strong",
             "vs_baseline": None,

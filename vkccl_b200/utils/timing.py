@@ -58,7 +58,9 @@ def time_steps(step: Callable[[], None], steps: int, flush: Optional[L2Flusher] 
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     torch.cuda.synchronize()
     if not align_ranks:
-        gpu_lead(2.0 + 0.2 * steps)
+        # Enough lead for the host to enqueue every step (two fused calls and a
+        # flush each, ~0.1-0.3 ms of host work) with room for a host pause.
+        gpu_lead(2.0 + 0.5 * steps)
     for i in range(steps):
         if align_ranks:
             import torch.distributed as dist
@@ -166,7 +168,7 @@ class NvmlClockSampler:
 
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
 
-    def __init__(self, device_index: int, period_s: float = 0.002):
+    def __init__(self, device_index: int, period_s: float = 0.005):
         import threading
 
         self.period_s = period_s
