@@ -14,6 +14,7 @@ synchronisation between them, and check
 Modelled from the kernels (counter names as in csrc/kernels/device_common.cuh):
   all-gather + GEMM   ready / taken / localReady / staged   (csrc/fused/ag_gemm.cu)
   GEMM + RS           done / free, per-call local counters  (csrc/fused/gemm_rs.cu)
+  GEMM + RS on pairs  per-half arrivals, consumed counts, free (csrc/fused/gemm_rs.cu, one kernel)
   LL one-shot         per-block epochs, parity slots        (csrc/kernels/ll.cuh)
   MoE dispatch        count-matrix exchange, done counters  (csrc/fused/moe.cu)
 Stream order is modelled too: a rank's kernel for call k+1 starts only after
@@ -215,6 +216,71 @@ def run_gemm_rs(n, ctas, blocks, calls, seed):
 
 
 # ---------------------------------------------------------------------------
+# GEMM + reduce-scatter on CTA pairs, one kernel: senders push 128-row half
+# tiles and bump the owner's per-half arrival counter; the owner's epilogue
+# waits for consumed + (n - 1) arrivals, reads the slots and records the new
+# consumed count; the last CTA of a call frees the owner's slots on every
+# rank.  Calls differ in shape (halves per owner), as in the kernel, where
+# a call only touches the counters of its own tiles.
+# ---------------------------------------------------------------------------
+def run_gemm_rs_pair(n, ctas, calls, seed, relative=True, free_wait=True):
+    sim = Sim(seed)
+    rng = random.Random(seed * 7 + 1)
+    halves = [rng.choice([1, 2, 3]) for _ in range(calls)]  # per call, the same on every rank
+    arrive = defaultdict(int)    # (owner, half)
+    consumed = defaultdict(int)  # (owner, half), local to the owner
+    free = defaultdict(int)      # (at source, from owner)
+    pair_free = defaultdict(int)
+    slot = {}                    # (owner, source, half) -> call pushed there
+    unread = set()               # pushed slots the owner has not read yet
+    errors = []
+
+    def make_kernel(r):
+        def mk(k):
+            live = {"done": 0, "count": ctas}
+            H = halves[k]
+            # rank r's order: owners r+1 .. r-1, its own rows last
+            tiles = [((r + 1 + i) % n, h) for i in range(n) for h in range(H)]
+            per_cta = [tiles[j::ctas] for j in range(ctas)]
+
+            def cta(j):
+                if free_wait:
+                    yield lambda: all(free[(r, q)] >= k for q in range(n))
+                for q, h in per_cta[j]:
+                    if q != r:
+                        if (q, r, h) in unread:
+                            errors.append(f"rank {r} call {k} overwrote unread slot {(q, r, h)}")
+                        slot[(q, r, h)] = k
+                        unread.add((q, r, h))
+                        yield lambda: True  # the stores and the release are separate steps
+                        arrive[(q, h)] += 1
+                    else:
+                        target = consumed[(r, h)] + (n - 1) if relative else (k + 1) * (n - 1)
+                        yield lambda t=target, hh=h: arrive[(r, hh)] >= t
+                        for p in range(n):
+                            if p != r:
+                                if slot.get((r, p, h)) != k:
+                                    errors.append(f"owner {r} call {k} half {h} read call {slot.get((r, p, h))} of {p}")
+                                unread.discard((r, p, h))
+                        consumed[(r, h)] = target
+                pair_free[r] += 1
+                if pair_free[r] == ctas:
+                    pair_free[r] = 0
+                    for q in range(n):
+                        free[(q, r)] += 1
+                live["done"] += 1
+
+            live["procs"] = [cta(j) for j in range(ctas)]
+            return live
+        return mk
+
+    for r in range(n):
+        sim.spawn(kernel_chain(sim, calls, make_kernel(r)))
+    sim.run()
+    return errors
+
+
+# ---------------------------------------------------------------------------
 # LL one-shot all-reduce (one block; the protocol is per block)
 # ---------------------------------------------------------------------------
 def next_ll_epoch(e, wrap_to=2):
@@ -331,6 +397,35 @@ def test_ag_gemm_protocol(n, ctas):
 def test_gemm_rs_protocol(n, ctas, blocks):
     for seed in range(150):
         assert run_gemm_rs(n, ctas, blocks, calls=4, seed=seed) == []
+
+
+@pytest.mark.parametrize("n,ctas", [(2, 2), (3, 2), (4, 3), (8, 4)])
+def test_gemm_rs_pair_protocol(n, ctas):
+    for seed in range(120):
+        assert run_gemm_rs_pair(n, ctas, calls=5, seed=seed) == []
+
+
+def test_model_detects_absolute_arrival_targets():
+    """Targets counted in calls instead of relative to the consumed count
+    hang (or misread) as soon as consecutive calls have different shapes."""
+    failed = 0
+    for seed in range(60):
+        try:
+            failed += bool(run_gemm_rs_pair(3, 2, calls=5, seed=seed, relative=False))
+        except Deadlock:
+            failed += 1
+    assert failed > 0
+
+
+def test_model_detects_pair_rs_without_free_wait():
+    """Without waiting for free[q], a fast sender overwrites a slot its owner has not read."""
+    failed = 0
+    for seed in range(200):
+        try:
+            failed += bool(run_gemm_rs_pair(3, 2, calls=4, seed=seed, free_wait=False))
+        except Deadlock:
+            failed += 1
+    assert failed > 0
 
 
 @pytest.mark.parametrize("n", [2, 3, 5, 8])
