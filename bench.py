@@ -290,11 +290,21 @@ def allreduce_busbw(comm, world, measure, flush):
     import torch
     import torch.distributed as dist
 
+    from vkccl_b200.utils.timing import max_over_ranks
+
     out = {}
     for size in (1 << 20, 16 << 20, 256 << 20):
         a = torch.randn(size // 2, device="cuda").bfloat16()
         b = torch.empty_like(a)
         f = 2.0 * (world - 1) / world
+        # the result this library gives against NCCL's on the same inputs
+        # (before the timing loops, which reduce in place many times)
+        comm.all_reduce(a, b)
+        r = a.clone()
+        dist.all_reduce(r)
+        torch.cuda.synchronize()
+        rel = max_over_ranks(((b.float() - r.float()).norm() / (r.float().norm() + 1e-12)).item())
+        del r
         tv = measure(lambda: comm.all_reduce(a, b), 10, 3)
         if os.environ.get("VKCCL_BENCH_STEPS"):
             from vkccl_b200.utils.timing import time_steps
@@ -303,7 +313,8 @@ def allreduce_busbw(comm, world, measure, flush):
             print(json.dumps({"rank": dist.get_rank(), "size": size, "steps_us": [round(t, 1) for t in steps]}),
                   file=sys.stderr, flush=True)
         tn = measure(lambda: dist.all_reduce(a), 10, 3)
-        out[f"{size >> 20}MiB"] = {"vccl": round(size / (tv * 1e3) * f, 1), "nccl": round(size / (tn * 1e3) * f, 1)}
+        out[f"{size >> 20}MiB"] = {"vccl": round(size / (tv * 1e3) * f, 1), "nccl": round(size / (tn * 1e3) * f, 1),
+                                   "rel_err_vs_nccl": round(rel, 5)}
     return out
 
 
