@@ -619,14 +619,16 @@ void windowTest(vcclComm_t c, int me, int n) {
   EXPECT_OK(vcclCommWindowDeregister(c, wb));
   EXPECT_OK(vcclMemFree(a));
   EXPECT_OK(vcclMemFree(b));
-  // plain cudaMalloc memory: a point-to-point window through CUDA IPC
+  // plain cudaMalloc memory: a point-to-point window through CUDA IPC, holding
+  // the send buffer and, at the next 4 KiB boundary, the receive buffer
+  const size_t ro = (cnt * 4 + 4095) / 4096 * 4096;
+  const size_t plainBytes = 2 * ro;
   void* plain = nullptr;
-  cudaMalloc(&plain, winBytes);
+  cudaMalloc(&plain, plainBytes);
   vcclWindow_t wp = nullptr;
-  EXPECT_OK(vcclCommWindowRegister(c, plain, winBytes, &wp, 0));
+  EXPECT_OK(vcclCommWindowRegister(c, plain, plainBytes, &wp, 0));
   if (wp != nullptr) {
     char* P = static_cast<char*>(plain);
-    const size_t ro = (cnt * 4 + 4095) / 4096 * 4096;
     upload(P, vcclFloat32, cnt, 0);
     EXPECT_OK(vcclAllReduce(P, P + ro, cnt, vcclFloat32, vcclSum, c));
     checkDevice(P + ro, vcclFloat32, cnt, "allreduce cudaMalloc window", [&](size_t i) { return expect(vcclSum, n, i); });
