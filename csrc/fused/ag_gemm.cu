@@ -39,9 +39,12 @@ __device__ __forceinline__ void redAddRelease(uint32_t* p, uint32_t v, bool sys)
 __device__ __forceinline__ void fenceProxyAsync() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 __device__ __forceinline__ void copyWarpsBarrier() { asm volatile("bar.sync 2, 64;" ::: "memory"); }
 
-// Copy by the 64 copy-warp threads, 8 x 16 B in flight per thread.
+// Copy by the 64 copy-warp threads, 16 x 16 B in flight per thread: the
+// staging of the own shard and the pulls of the peers' shards are
+// latency-bound (a 4-GPU trace had the own 16 MiB shard staged only after
+// ~20 us with 8 in flight).
 __device__ __forceinline__ void groupCopy(char* dst, const char* src, size_t bytes, int tid) {
-  constexpr int U = 8;
+  constexpr int U = 16;
   const size_t n16 = bytes / 16;
   size_t i = tid;
   for (; i + (U - 1) * 64 < n16; i += U * 64) {
