@@ -65,3 +65,17 @@ $(BIN)/test_bootstrap_threads_asan: csrc/tests/test_bootstrap_threads.cc $(CTRL_
 sanitize: $(BIN)/test_bootstrap_threads_tsan $(BIN)/test_bootstrap_threads_asan
 
 .PHONY: sanitize
+
+# The reference's own build for `bench.py --impl reference` (TCP only, from an
+# unmodified copy of its source): make reference REF_SRC=<reference checkout>.
+# Output: baseline/_ref/build/libvccl.so (+ its tools and tests) and
+# baseline/_ref/vccl (its Python package); git-ignored, carried to GPU boxes.
+reference:
+	@test -n "$(REF_SRC)" || (echo "usage: make reference REF_SRC=<reference checkout>"; exit 1)
+	rm -rf _build/refsrc && mkdir -p _build/refsrc baseline/_ref
+	cp -r $(REF_SRC)/. _build/refsrc/
+	cmake -S _build/refsrc -B baseline/_ref/build -DVCCL_ENABLE_VERBS=OFF -DCMAKE_BUILD_TYPE=Release
+	cmake --build baseline/_ref/build -j8
+	rm -rf baseline/_ref/vccl && cp -r _build/refsrc/python/vccl baseline/_ref/vccl
+
+.PHONY: reference
