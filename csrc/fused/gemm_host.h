@@ -40,6 +40,11 @@ struct PairPlan {
   bool use;
   int splits;
 };
+// Pair-kernel plan with split-K (plain GEMM and SiLU*mul only) for `pairs`
+// co-resident CTA pairs: the time of ceil(units / pairs) waves of units of
+// 1 / splits of a tile, plus the fp32 partials' HBM traffic, against the
+// one-SM kernel's waves (gemm.cu).
+PairPlan planPair(int M, int N, int K, int bnOverride, int pairs);
 float* splitScratch(cudaStream_t st, size_t bytes);
 
 // Scratch for one call on `st`: the per-stream cached buffer, or a

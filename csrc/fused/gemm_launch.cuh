@@ -85,11 +85,6 @@ int pairMode();
 // shared memory and threads (0 if the device cannot run it).
 int pairMaxClusters(const void* kernel, int smemBytes, int threads);
 
-// Pair-kernel plan with split-K (plain GEMM and SiLU*mul only): the time of
-// ceil(units / pairs) waves of units of 1 / splits of a tile, plus the fp32
-// partials' HBM traffic, against the one-SM kernel's waves; see gemm.cu.
-PairPlan planPair(int M, int N, int K, int bnOverride, int pairs);
-
 // True when the pair kernel finishes the shape in no more waves x tile width
 // than the one-SM kernel's choice: it moves a third less data per FLOP, so
 // it is taken on ties.

@@ -12,6 +12,7 @@
 //  * planSplitK keeps its bounds (4+ k-blocks per split, <= 16 splits,
 //    partials <= a quarter of the weight bytes).
 #include <cstdio>
+#include <cstdlib>
 #include <set>
 #include <tuple>
 #include <vector>
@@ -187,6 +188,36 @@ void checkPlan() {
         EXPECT(p.bn == 128, "split-K tile width");
       }
 }
+// CTA-pair plans on a 148-SM device with 74 pairs: the large bench shapes run
+// on pairs without splitting K; a shape with too few pair tiles to fill the
+// device (512 x 4096 x 14336: 32 tiles) splits K in two; a shape smaller
+// than one pair tile never takes the pair kernel; VCCL_GEMM_PAIR=0 turns
+// pairs off (the plan reads the variable per call).
+void checkPairPlan() {
+  unsetenv("VCCL_GEMM_PAIR");
+  PairPlan p = planPair(8192, 28672, 4096, 0, 74);
+  EXPECT(p.use && p.splits == 1, "8192x28672x4096: use=%d splits=%d", p.use, p.splits);
+  p = planPair(8192, 4096, 14336, 0, 74);
+  EXPECT(p.use && p.splits == 1, "8192x4096x14336: use=%d splits=%d", p.use, p.splits);
+  p = planPair(512, 4096, 14336, 0, 74);
+  EXPECT(p.use && p.splits == 2, "512x4096x14336: use=%d splits=%d", p.use, p.splits);
+  p = planPair(128, 4096, 4096, 0, 74);
+  EXPECT(!p.use, "M below one pair tile");
+  p = planPair(8192, 4096, 4096, 64, 74);
+  EXPECT(!p.use, "a tile-width override keeps one-SM tiles");
+  for (int M : {256, 512, 1000, 4096, 8192})
+    for (int N : {256, 1024, 4096, 28672})
+      for (int K : {512, 4096, 14336}) {
+        p = planPair(M, N, K, 0, 74);
+        const int nk = (K + kBK - 1) / kBK;
+        EXPECT(p.splits >= 1 && p.splits <= 4 && (p.splits == 1 || nk / p.splits >= 8),
+               "pair split bounds M=%d N=%d K=%d s=%d", M, N, K, p.splits);
+      }
+  setenv("VCCL_GEMM_PAIR", "0", 1);
+  EXPECT(!planPair(8192, 28672, 4096, 0, 74).use, "VCCL_GEMM_PAIR=0");
+  unsetenv("VCCL_GEMM_PAIR");
+}
+
 // Makespan tile widths: the TP-8 gate/up shard (896 tiles at 256 = 6.05
 // waves) goes to 128; full-wave shapes stay at 256; a 512-row GEMM takes one
 // wave of 128-wide tiles instead of two of 64; one-wave decode shapes take
@@ -209,6 +240,7 @@ void checkPickWaves() {
 int main() {
   checkSplitK();
   checkPairTiles();
+  checkPairPlan();
   checkPickWaves();
   checkGrouped();
   checkStage();
