@@ -138,7 +138,12 @@ def run_vccl(args) -> int:
     srt = sorted(times)
     step_stats = {"min": round(max_over_ranks(srt[0]), 2), "median": round(max_over_ranks(srt[len(srt) // 2]), 2),
                   "max": round(max_over_ranks(srt[-1]), 2)}
-    per_step_launches = 3 if world > 1 else 2
+    # Kernels of this library per step: the all-gather + GEMM kernel and the
+    # GEMM + reduce-scatter kernel (one kernel on CTA pairs; the two-kernel
+    # form adds its sum kernel); at one rank, the two GEMMs.  The L2 flush
+    # between steps is torch's fill kernel, not counted.
+    two_kernel_rs = os.environ.get("VCCL_RS_TWO_KERNELS", "0") != "0" or os.environ.get("VCCL_RS_TMA", "0") != "0"
+    per_step_launches = 3 if world > 1 and two_kernel_rs else 2
 
     # end to end through the public API: pinned H2D input, forward, D2H output
     # (TPLlamaMLP.forward_host), the shard in 1 to 8 token groups whose copies
