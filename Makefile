@@ -21,7 +21,7 @@ HDRS    := $(wildcard include/*.h csrc/*/*.h csrc/*/*.cuh)
 
 TOOLS   := $(BIN)/vccl-bench $(BIN)/vccl-info $(BIN)/vccl-devbuf-demo $(BIN)/vccl-barrier-bench
 TESTS   := $(BIN)/test_bootstrap $(BIN)/test_collectives $(BIN)/test_control $(BIN)/test_tiling $(BIN)/test_tuning \
-           $(BIN)/test_coll_index $(BIN)/test_dmabuf
+           $(BIN)/test_coll_index $(BIN)/test_dmabuf $(BIN)/test_regcache
 
 all: $(OUT)/libvccl.so $(TOOLS) $(TESTS)
 

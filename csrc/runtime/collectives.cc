@@ -60,6 +60,10 @@ struct HostOp {
   cudaStream_t stream = nullptr;
   bool sync = true;     // host-blocking semantics
   bool staged = false;  // host pointers allowed (staged through device memory)
+  // Windows the registration cache picked for this call on every rank (null:
+  // only application windows are looked up).
+  const Window* winSend = nullptr;
+  const Window* winRecv = nullptr;
 };
 
 thread_local int tDepth = 0;
@@ -423,8 +427,8 @@ bool windowCollective(const HostOp& h, const LaunchCtx& lc, vcclResult_t* out) {
   switch (h.kind) {
     case Kind::AllReduce: {
       if (bytes <= ds.llMaxBytes) return false;
-      const Window* ws = comm->findWindow(h.send, bytes);
-      const Window* wr = comm->findWindow(h.recv, bytes);
+      const Window* ws = h.winSend ? h.winSend : comm->findWindow(h.send, bytes);
+      const Window* wr = h.winRecv ? h.winRecv : comm->findWindow(h.recv, bytes);
       if (ws == nullptr || wr == nullptr) return false;
       bindSend(ws);
       bindRecv(wr);
@@ -441,7 +445,7 @@ bool windowCollective(const HostOp& h, const LaunchCtx& lc, vcclResult_t* out) {
     }
     case Kind::AllGather: {
       if (bytes <= lc.llAgMax) return false;
-      const Window* wr = comm->findWindow(h.recv, bytes * n);
+      const Window* wr = h.winRecv ? h.winRecv : comm->findWindow(h.recv, bytes * n);
       if (wr == nullptr) return false;
       bindRecv(wr);
       w.send[me] = h.send;  // the send buffer is read locally only
@@ -452,7 +456,7 @@ bool windowCollective(const HostOp& h, const LaunchCtx& lc, vcclResult_t* out) {
     }
     case Kind::Broadcast: {
       if (bytes <= lc.llMax) return false;
-      const Window* wr = comm->findWindow(h.recv, bytes);
+      const Window* wr = h.winRecv ? h.winRecv : comm->findWindow(h.recv, bytes);
       if (wr == nullptr) return false;
       bindRecv(wr);
       w.send[me] = h.send;  // read on the root only
@@ -463,7 +467,7 @@ bool windowCollective(const HostOp& h, const LaunchCtx& lc, vcclResult_t* out) {
     }
     case Kind::ReduceScatter: {
       if (bytes <= lc.llMax) return false;
-      const Window* ws = comm->findWindow(h.send, bytes * n);
+      const Window* ws = h.winSend ? h.winSend : comm->findWindow(h.send, bytes * n);
       if (ws == nullptr) return false;
       bindSend(ws);
       w.recv[me] = h.recv;  // written locally only
@@ -474,6 +478,49 @@ bool windowCollective(const HostOp& h, const LaunchCtx& lc, vcclResult_t* out) {
     default:
       return false;
   }
+}
+
+// Registration cache (VCCL_REG_CACHE=1): windows over the buffers of a large
+// all-reduce / all-gather / reduce-scatter / broadcast on plain device
+// memory, reused across calls (runtime/regcache.h).  Whether a call consults
+// the cache depends only on its kind and size, which agree across ranks, so
+// every rank takes part in the cache's allgather for the same calls.
+// `eligible`: no buffer of this rank was a staged host range.
+vcclResult_t cacheWindowsFor(HostOp& h, bool eligible) {
+  vcclComm_t comm = h.comm;
+  const size_t n = static_cast<size_t>(comm->nranks);
+  const size_t bytes = h.count * vcclTypeSize(h.dt);
+  const void* ptrs[kRegMaxBuffers] = {nullptr, nullptr};
+  size_t sizes[kRegMaxBuffers] = {0, 0};
+  int nbuf = 1;
+  switch (h.kind) {
+    case Kind::AllReduce:
+      ptrs[0] = h.send;
+      sizes[0] = bytes;
+      if (h.recv != h.send) {
+        ptrs[1] = h.recv;
+        sizes[1] = bytes;
+        nbuf = 2;
+      }
+      break;
+    case Kind::AllGather: ptrs[0] = h.recv; sizes[0] = bytes * n; break;
+    case Kind::ReduceScatter: ptrs[0] = h.send; sizes[0] = bytes * n; break;
+    case Kind::Broadcast: ptrs[0] = h.recv; sizes[0] = bytes; break;
+    default: return vcclSuccess;
+  }
+  if (sizes[0] < comm->dev->regCacheMin) return vcclSuccess;
+  const Window* w[kRegMaxBuffers] = {nullptr, nullptr};
+  VTRY(regCacheWindows(comm, h.stream, ptrs, sizes, nbuf, eligible, w));
+  switch (h.kind) {
+    case Kind::AllReduce:
+      h.winSend = w[0];
+      h.winRecv = nbuf == 2 ? w[1] : w[0];
+      if (h.winSend == nullptr || h.winRecv == nullptr) h.winSend = h.winRecv = nullptr;
+      break;
+    case Kind::ReduceScatter: h.winSend = w[0]; break;
+    default: h.winRecv = w[0]; break;
+  }
+  return vcclSuccess;
 }
 
 // Zero-copy all-to-all(v) with the receive buffer in a registered window:
@@ -711,6 +758,7 @@ vcclResult_t launchOps(vcclComm_t comm, std::vector<HostOp>& ops, std::vector<Pe
     }
     OrderedLaunch ord(comm->dev.get(), h.stream);
     VTRY(prepareBuffers(h, st));
+    if (comm->dev->regCacheOn && comm->nranks > 1) VTRY(cacheWindowsFor(h, st.ranges.empty()));
     VTRY(launchColl(h));
     VTRY(st.finish(h.stream));
     if (h.sync) waits->push_back({comm, h.stream});

@@ -116,7 +116,7 @@ const vccl::Window* vcclComm::findWindow(const void* p, size_t bytes) {
   std::lock_guard<std::mutex> g(regMu);
   const char* q = static_cast<const char*>(p);
   for (const vccl::Window* w : windows)
-    if (q >= w->base && q + bytes <= w->base + w->bytes) return w;
+    if (!w->cached && q >= w->base && q + bytes <= w->base + w->bytes) return w;
   return nullptr;
 }
 
@@ -200,6 +200,7 @@ vcclResult_t initRank(vcclComm_t* out, int nranks, const vcclUniqueId& id, int r
       }
     }
     VTRY(vccl::deviceStateCreate(c->bootstrap.get(), device, &c->dev));
+    c->regCache.setCapacity(c->dev->regCacheEntries);
   }
   VINFO("comm ready: rank %d/%d, device %d", rank, nranks, device);
   *out = c.release();

@@ -21,6 +21,7 @@
 #include <vector>
 
 #include "control/bootstrap.h"
+#include "runtime/regcache.h"
 #include "runtime/tuning.h"
 #include "kernels/device_common.cuh"
 #include "vccl.h"
@@ -83,6 +84,9 @@ struct DeviceState {
   int nvlsPieces = 4;              // pieces of a pipelined NVLS all-reduce
   bool windowsEnabled = true;      // zero-copy kernels for buffers in registered windows (VCCL_WINDOW)
   int windowNvlsMinRanks = 3;      // window collectives go through the switch from this many ranks
+  bool regCacheOn = false;         // windows for plain device buffers on demand (VCCL_REG_CACHE)
+  size_t regCacheMin = 16u << 20;  // ... for calls whose window extent is at least this (VCCL_REG_CACHE_MIN)
+  int regCacheEntries = 16;        // ... at most this many at once (VCCL_REG_CACHE_ENTRIES)
   LaunchOrder order;
   bool orderLaunches = true;       // VCCL_LAUNCH_ORDER=0: the application keeps one stream per communicator
 };
@@ -128,9 +132,10 @@ struct Registration {
   cudaExternalMemory_t extMem = nullptr;      // external-memory import we own
 };
 
-// A registered window: user memory from vcclMemAlloc that every rank has
-// mapped (and, when the node supports NVLS, bound to a multicast object), so
-// collectives on it read and write the peers' buffers in place.
+// A registered window: user memory (vcclMemAlloc or cudaMalloc) that every
+// rank has mapped (vcclMemAlloc memory, when the node supports NVLS, also
+// bound to a multicast object), so collectives on it read and write the
+// peers' buffers in place.
 struct Window {
   char* base = nullptr;  // this rank's window
   size_t bytes = 0;
@@ -146,6 +151,7 @@ struct Window {
   size_t mcBytes = 0;
   bool mcBound = false;
   char* mc = nullptr;  // multicast address of the window, or null
+  bool cached = false;  // owned by the registration cache, not by the application
 };
 
 // The vcclMemAlloc device allocation holding [p, p + bytes): its base,
@@ -162,6 +168,20 @@ bool everyone(Bootstrap* bs, bool mine);
 // (local steps only).
 void windowReleaseMulticast(DeviceState* ds, Window* w);
 void windowRelease(DeviceState* ds, int me, Window* w);
+// Collective window registration (vcclCommWindowRegister); `cached` marks a
+// window the registration cache owns.
+vcclResult_t windowRegister(vcclComm_t comm, void* buff, size_t size, int flags, bool cached, Window** out);
+// Registration cache (VCCL_REG_CACHE=1), collective: every rank calls it for
+// the same call, with buffers of the same sizes.  Makes sure every rank holds
+// cached windows over the call's `nbuf` buffers (entries reused, registered
+// or dropped by one plan all ranks compute alike) and returns them in
+// out[i], or leaves every out[i] null on every rank when the call must stay
+// on the staged kernels.  `eligible`: this rank's buffers are device memory
+// of its own (no staged host range).
+vcclResult_t regCacheWindows(vcclComm_t comm, cudaStream_t s, const void* const* ptrs, const size_t* bytes,
+                             int nbuf, bool eligible, const Window** out);
+// Drop every cached window (collective).
+vcclResult_t regCacheFlush(vcclComm_t comm);
 
 vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<DeviceState>* out);
 // Make sure the MoE region holds at least `bytes` on every rank.  Collective
@@ -189,9 +209,14 @@ struct vcclComm {
 
   std::mutex regMu;
   std::vector<vccl::Registration*> regs;
-  std::vector<vccl::Window*> windows;  // guarded by regMu
+  std::vector<vccl::Window*> windows;  // guarded by regMu (application and cached windows)
 
-  // The window holding [p, p + bytes), or null (collective buffer lookup).
+  std::mutex regCacheMu;        // one cache step at a time
+  vccl::RegCacheBook regCache;  // guarded by regCacheMu
+
+  // The application window holding [p, p + bytes), or null (collective
+  // buffer lookup).  Cached windows are not returned: a call uses one only
+  // when the cache's plan for that call picked it on every rank.
   const vccl::Window* findWindow(const void* p, size_t bytes);
 
   int device() const { return dev ? dev->device : -1; }

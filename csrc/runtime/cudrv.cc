@@ -60,6 +60,7 @@ const DriverApi* driverApi() {
     resolve("cuMulticastUnbind", 12010, &api.mcUnbind);
     resolve("cuMulticastGetGranularity", 12010, &api.mcGranularity);
     resolve("cuTensorMapEncodeTiled", 12000, &api.tensorMapEncodeTiled);
+    resolve("cuPointerGetAttribute", 4000, &api.pointerGetAttribute);
     ok = all;
     if (!ok) VWARN("CUDA driver entry points missing; device data plane disabled");
   });

@@ -31,6 +31,7 @@ struct DriverApi {
   decltype(&::cuTensorMapEncodeTiled) tensorMapEncodeTiled;
   decltype(&::cuGetErrorString) getErrorString;
   decltype(&::cuCtxGetDevice) ctxGetDevice;
+  decltype(&::cuPointerGetAttribute) pointerGetAttribute;  // optional (registration cache)
 };
 
 // Null when no driver is present.

@@ -254,6 +254,13 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
   ds->nvlsPipeMin = envBytes("VCCL_NVLS_PIPE_MIN", 256u << 20);
   ds->nvlsPieces = static_cast<int>(envLong("VCCL_NVLS_PIECES", 4));
   ds->windowsEnabled = envLong("VCCL_WINDOW", 1) != 0;
+  // Windows on demand for plain device buffers (off unless asked for).
+  ds->regCacheOn = ds->windowsEnabled && envLong("VCCL_REG_CACHE", 0) != 0 && envLong("VCCL_MR_CACHE", 1) != 0;
+  ds->regCacheMin = envBytes("VCCL_REG_CACHE_MIN", 16u << 20);
+  // Capacity: the reference's VCCL_MR_CACHE (LRU entries, default 16) is
+  // honoured as the fallback name.
+  ds->regCacheEntries = static_cast<int>(envLong("VCCL_REG_CACHE_ENTRIES", envLong("VCCL_MR_CACHE", 16)));
+  if (ds->regCacheEntries < 2) ds->regCacheEntries = 2;
   ds->orderLaunches = envLong("VCCL_LAUNCH_ORDER", 1) != 0;
   // Per GPU, the switch moves about S each way for a window all-reduce of
   // S bytes against 2 (n-1)/n S for the point-to-point kernel.
@@ -335,7 +342,9 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
         std::to_string(ds->ll2MaxBytes) + " llag " + std::to_string(ds->llAgMaxBytes) + " nvls " +
         std::to_string(ds->nvlsMinRanks) + " " + std::to_string(ds->nvlsMinBytes) + " pipe " +
         std::to_string(ds->nvlsPipeMin) + " " + std::to_string(ds->nvlsPieces) + " win " +
-        std::to_string(ds->windowsEnabled ? 1 : 0) + " " + std::to_string(ds->windowNvlsMinRanks));
+        std::to_string(ds->windowsEnabled ? 1 : 0) + " " + std::to_string(ds->windowNvlsMinRanks) + " regcache " +
+        std::to_string(ds->regCacheOn ? 1 : 0) + " " + std::to_string(ds->regCacheMin) + " " +
+        std::to_string(ds->regCacheEntries));
     struct Sizes { uint64_t ctrl, data, fused, llBlocks, smallRows, tuning; } mine{
         ctrlBytes, dataBytes, fusedBytes, static_cast<uint64_t>(ds->llBlocks),
         static_cast<uint64_t>(static_cast<int64_t>(ds->fusedSmallRows)), tuneHash};
@@ -347,7 +356,7 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
           s.smallRows != mine.smallRows || s.tuning != mine.tuning) {
         VERR("ranks disagree on workspace sizes or algorithm settings (check VCCL_BUFFSIZE, VCCL_FUSED_BUFFSIZE, "
              "VCCL_GUARDS, VCCL_LL_BLOCKS, VCCL_NBLOCKS, VCCL_FUSED_SMALL_M, the VCCL_LL_* / VCCL_NVLS_* / "
-             "VCCL_WINDOW* thresholds and VCCL_TUNING_FILE on every rank)");
+             "VCCL_WINDOW* thresholds, VCCL_REG_CACHE* and VCCL_TUNING_FILE on every rank)");
         return vcclInvalidUsage;
       }
     }

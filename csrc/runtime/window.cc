@@ -16,6 +16,12 @@
 // enabled); such windows have no multicast binding.
 // Collectives whose buffers lie in windows then run the zero-copy kernels of
 // csrc/kernels/window.cuh.
+//
+// The registration cache (VCCL_REG_CACHE=1) registers such windows on demand
+// for plain device buffers of large collectives and keeps them: the
+// NVLink form of the reference's per-call registration with an LRU cache
+// (reference: src/core/comm.h:74-139).  Its decisions are made in
+// runtime/regcache.cc from one allgather per call.
 #include <unistd.h>
 
 #include <algorithm>
@@ -158,12 +164,7 @@ void windowRelease(DeviceState* ds, int me, Window* w) {
   }
 }
 
-}  // namespace vccl
-
-using namespace vccl;
-
-extern "C" vcclResult_t vcclCommWindowRegister(vcclComm_t comm, void* buff, size_t size, vcclWindow_t* win,
-                                               int flags) {
+vcclResult_t windowRegister(vcclComm_t comm, void* buff, size_t size, int flags, bool cached, Window** win) {
   if (comm == nullptr || buff == nullptr || size == 0 || win == nullptr) return vcclInvalidArgument;
   if (comm->aborted.load()) return vcclInvalidUsage;
   if (!comm->dev || driverApi() == nullptr) {
@@ -232,6 +233,7 @@ extern "C" vcclResult_t vcclCommWindowRegister(vcclComm_t comm, void* buff, size
   w->peerHandle.assign(n, 0);
   w->ipcBase.assign(n, nullptr);
   w->peer[me] = w->base;
+  w->cached = cached;
 
   if (mine.kind == kWinIpc) {
     bool ok = true;
@@ -259,7 +261,8 @@ extern "C" vcclResult_t vcclCommWindowRegister(vcclComm_t comm, void* buff, size
       windowRelease(ds, me, w.get());
       return res;
     }
-    VINFO("window registered: %zu bytes of cudaMalloc memory, point-to-point", size);
+    VINFO("window registered: %zu bytes of cudaMalloc memory, point-to-point%s", size,
+          cached ? " (registration cache)" : "");
     std::lock_guard<std::mutex> g(comm->regMu);
     comm->windows.push_back(w.get());
     *win = w.release();
@@ -313,9 +316,11 @@ extern "C" vcclResult_t vcclCommWindowRegister(vcclComm_t comm, void* buff, size
   return vcclSuccess;
 }
 
-extern "C" vcclResult_t vcclCommWindowDeregister(vcclComm_t comm, vcclWindow_t win) {
-  if (comm == nullptr || win == nullptr) return vcclInvalidArgument;
-  Window* w = static_cast<Window*>(win);
+namespace {
+
+// Drop one window everywhere: every rank's kernels are done with it before
+// any rank unmaps (collective).
+vcclResult_t windowDrop(vcclComm_t comm, Window* w) {
   {
     std::lock_guard<std::mutex> g(comm->regMu);
     auto it = std::find(comm->windows.begin(), comm->windows.end(), w);
@@ -325,7 +330,7 @@ extern "C" vcclResult_t vcclCommWindowDeregister(vcclComm_t comm, vcclWindow_t w
   vcclResult_t res = vcclSuccess;
   if (comm->dev) {
     cudaSetDevice(comm->dev->device);
-    cudaDeviceSynchronize();  // this rank's kernels are done with every window
+    cudaDeviceSynchronize();  // this rank's kernels are done with the window
     // ... and so are the peers' once everyone got here; an aborted
     // communicator skips the meeting (its peers may be gone).
     if (!comm->aborted.load()) res = comm->bootstrap->barrier();
@@ -333,4 +338,133 @@ extern "C" vcclResult_t vcclCommWindowDeregister(vcclComm_t comm, vcclWindow_t w
   }
   delete w;
   return res;
+}
+
+}  // namespace
+
+// The registration cache's device side.  Everything that decides is in
+// RegCacheBook (runtime/regcache.cc); this part gathers each rank's facts
+// (allocation ids from the driver, capture state, application windows),
+// runs the one allgather per call and carries out the plan with the window
+// steps above.
+vcclResult_t regCacheWindows(vcclComm_t comm, cudaStream_t s, const void* const* ptrs, const size_t* bytes,
+                             int nbuf, bool eligible, const Window** out) {
+  for (int i = 0; i < nbuf; i++) out[i] = nullptr;
+  if (nbuf < 1 || nbuf > kRegMaxBuffers) return vcclInternalError;
+  const DriverApi* d = driverApi();
+  std::lock_guard<std::mutex> cacheLock(comm->regCacheMu);
+  RegKey keys[kRegMaxBuffers];
+  bool ok = eligible && d != nullptr && d->pointerGetAttribute != nullptr && !comm->aborted.load();
+  if (ok) {
+    // Registering blocks the host and dropping synchronizes the device: not
+    // while the stream is being captured (the call then stays staged, on
+    // every rank, through the plan).
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) ok = false;
+    cudaGetLastError();
+  }
+  for (int i = 0; i < nbuf && ok; i++) {
+    keys[i].ptr = reinterpret_cast<uintptr_t>(ptrs[i]);
+    keys[i].bytes = bytes[i];
+    keys[i].userWindow = comm->findWindow(ptrs[i], bytes[i]) != nullptr;
+    if (keys[i].userWindow) continue;
+    // Only memory that CUDA IPC can export (cudaMalloc; not the stream-ordered
+    // pool, not VMM ranges, which vcclMemAlloc + vcclCommWindowRegister serve).
+    // The driver writes a boolean for the IPC attribute; a zeroed 8-byte
+    // slot reads nonzero exactly when it wrote true, whatever its width.
+    unsigned long long id = 0, ipcOk = 0;
+    const CUdeviceptr p = reinterpret_cast<CUdeviceptr>(ptrs[i]);
+    ok = d->pointerGetAttribute(&id, CU_POINTER_ATTRIBUTE_BUFFER_ID, p) == CUDA_SUCCESS &&
+         d->pointerGetAttribute(&ipcOk, CU_POINTER_ATTRIBUTE_IS_LEGACY_CUDA_IPC_CAPABLE, p) == CUDA_SUCCESS &&
+         ipcOk != 0 && id != 0;
+    keys[i].allocId = id;
+  }
+  if (ok && nbuf == 2 && keys[0].ptr < keys[1].ptr + keys[1].bytes && keys[1].ptr < keys[0].ptr + keys[0].bytes)
+    ok = false;  // overlapping send and receive ranges (in-place forms pass one buffer)
+  cudaGetLastError();
+
+  const int n = comm->nranks, me = comm->rank;
+  std::vector<RegQuery> all(n);
+  all[me] = comm->regCache.query(keys, nbuf, ok);
+  VTRY(comm->bootstrap->allGather(all.data(), sizeof(RegQuery)));
+  const RegPlan plan = comm->regCache.plan(all);
+  comm->regCache.countCall(plan);
+  if (!plan.take) return vcclSuccess;
+  for (int32_t id : plan.evict) VTRY(windowDrop(comm, static_cast<Window*>(comm->regCache.drop(id))));
+  for (int i = 0; i < nbuf; i++) {
+    if (plan.use[i] >= 0) {
+      comm->regCache.touch(plan.use[i]);
+      out[i] = static_cast<const Window*>(comm->regCache.handleOf(plan.use[i]));
+      continue;
+    }
+    if (!plan.reg[i]) continue;
+    Window* w = nullptr;
+    const vcclResult_t r = windowRegister(comm, const_cast<void*>(ptrs[i]), bytes[i], VCCL_WIN_NO_MULTICAST, true, &w);
+    if (r != vcclSuccess) {
+      // Registration fails on every rank alike (its steps agree through the
+      // bootstrap), so every rank turns the cache off here and the call, with
+      // every later one, stays on the staged kernels.
+      VWARN("registration cache: registering a %zu-byte buffer failed (%s); cache off for this communicator",
+            bytes[i], vcclGetErrorString(r));
+      comm->dev->regCacheOn = false;
+      for (int j = 0; j < nbuf; j++) out[j] = nullptr;
+      return vcclSuccess;
+    }
+    comm->regCache.add(keys[i], w);
+    out[i] = w;
+  }
+  return vcclSuccess;
+}
+
+vcclResult_t regCacheFlush(vcclComm_t comm) {
+  std::lock_guard<std::mutex> cacheLock(comm->regCacheMu);
+  vcclResult_t res = vcclSuccess;
+  for (int32_t id : comm->regCache.ids()) {
+    const vcclResult_t r = windowDrop(comm, static_cast<Window*>(comm->regCache.drop(id)));
+    if (res == vcclSuccess) res = r;
+  }
+  return res;
+}
+
+}  // namespace vccl
+
+using namespace vccl;
+
+extern "C" vcclResult_t vcclCommWindowRegister(vcclComm_t comm, void* buff, size_t size, vcclWindow_t* win,
+                                               int flags) {
+  if (win == nullptr) return vcclInvalidArgument;
+  Window* w = nullptr;
+  const vcclResult_t r = windowRegister(comm, buff, size, flags, false, &w);
+  if (r == vcclSuccess) *win = w;
+  return r;
+}
+
+extern "C" vcclResult_t vcclCommWindowDeregister(vcclComm_t comm, vcclWindow_t win) {
+  if (comm == nullptr || win == nullptr) return vcclInvalidArgument;
+  Window* w = static_cast<Window*>(win);
+  {
+    // Cached windows belong to the registration cache, not to the caller.
+    std::lock_guard<std::mutex> g(comm->regMu);
+    if (std::find(comm->windows.begin(), comm->windows.end(), w) == comm->windows.end() || w->cached)
+      return vcclInvalidArgument;
+  }
+  return windowDrop(comm, w);
+}
+
+extern "C" vcclResult_t vcclCommRegCacheFlush(vcclComm_t comm) {
+  if (comm == nullptr) return vcclInvalidArgument;
+  if (!comm->dev) return vcclSuccess;
+  return regCacheFlush(comm);
+}
+
+extern "C" vcclResult_t vcclCommRegCacheStats(vcclComm_t comm, unsigned long long* out) {
+  if (comm == nullptr || out == nullptr) return vcclInvalidArgument;
+  std::lock_guard<std::mutex> cacheLock(comm->regCacheMu);
+  const RegStats& st = comm->regCache.stats();
+  out[0] = comm->regCache.entries().size();
+  out[1] = st.calls;
+  out[2] = st.hits;
+  out[3] = st.misses;
+  out[4] = st.evictions;
+  return vcclSuccess;
 }

@@ -279,6 +279,26 @@ vcclResult_t vcclCommWindowRegister(vcclComm_t comm, void* buff, size_t size,
                                     vcclWindow_t* win, int flags);
 vcclResult_t vcclCommWindowDeregister(vcclComm_t comm, vcclWindow_t win);
 
+/* ── Registration cache (an addition: windows on demand) ──────────────────
+ * With VCCL_REG_CACHE=1 on every rank, all-reduce, all-gather,
+ * reduce-scatter and broadcast on plain cudaMalloc buffers (PyTorch
+ * tensors) of at least VCCL_REG_CACHE_MIN bytes (window extent; default
+ * 16 MiB) register their buffers as windows the first time and reuse them
+ * afterwards, so those calls run the zero-copy window kernels without
+ * vcclCommWindowRegister.  Each such call costs one small host allgather
+ * among the ranks (which decides, alike on every rank, whether every rank
+ * holds the same cached windows), registering costs a window registration,
+ * and dropping an entry (LRU beyond VCCL_REG_CACHE_ENTRIES entries, or
+ * an allocation replaced at the same address) synchronizes the device.
+ * VCCL_REG_CACHE_ENTRIES defaults to VCCL_MR_CACHE, else 16.
+ * Calls inside a stream capture stay on the staged kernels.  Peers keep the
+ * cached allocations open: drop the cache (collective) before freeing
+ * cached memory back to CUDA (torch.cuda.empty_cache()).
+ * Stats: out[0] entries, [1] calls that consulted the cache on every rank,
+ * [2] buffers reused, [3] buffers registered, [4] entries dropped. */
+vcclResult_t vcclCommRegCacheFlush(vcclComm_t comm);
+vcclResult_t vcclCommRegCacheStats(vcclComm_t comm, unsigned long long out[5]);
+
 const char* vcclGetErrorString(vcclResult_t result);
 const char* vcclGetLastError(vcclComm_t comm);
 size_t vcclTypeSize(vcclDataType_t datatype);

@@ -51,6 +51,15 @@ def test_tuning_tables():
     assert "tuning: OK" in _run("test_tuning")
 
 
+def test_registration_cache_protocol():
+    """Registration cache: simulated ranks with their own address layouts run random call sequences
+    (reuse, slices, reallocation at the same address, a rank unable to take part, application
+    windows); every rank plans alike, every cached call has one window per buffer at one offset on
+    every rank over the current allocation, entries never overlap or exceed the capacity; a skewed-
+    offset negative control (csrc/tests/test_regcache.cc)."""
+    assert "regcache: OK" in _run("test_regcache")
+
+
 def test_collective_index_arithmetic():
     """Coverage and staging bounds of the staged, pipelined-NVLS and window kernels' splits, with a
     negative control for re-split rounds (csrc/tests/test_coll_index.cc)."""

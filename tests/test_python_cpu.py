@@ -548,6 +548,9 @@ def test_window_api_without_device():
                 pass
         assert comm.WIN_NO_MULTICAST == 1
         assert comm.check_guards() is None  # no device plane, no guard regions
+        # The registration cache has nothing to hold without a device plane.
+        comm.reg_cache_flush()
+        assert comm.reg_cache_stats() == {"entries": 0, "calls": 0, "hits": 0, "misses": 0, "evictions": 0}
     finally:
         comm.destroy()
 

@@ -118,6 +118,8 @@ def _declare(h: ctypes.CDLL) -> None:
         "vcclCommRegisterDmaBuf": [P, I, c.c_uint64, Z, c.POINTER(P), c.POINTER(P)],
         "vcclCommWindowRegister": [P, P, Z, c.POINTER(P), I],
         "vcclCommWindowDeregister": [P, P],
+        "vcclCommRegCacheFlush": [P],
+        "vcclCommRegCacheStats": [P, c.POINTER(c.c_ulonglong)],
         "vcclTypeSize": [I],
         "vcclGetErrorString": [I],
         "vcclGetLastError": [P],

@@ -563,6 +563,22 @@ class Communicator:
         """Collective: undo window_register (before the memory is freed)."""
         _check(lib().vcclCommWindowDeregister(self._comm, handle), "vcclCommWindowDeregister", self._comm)
 
+    # -- registration cache (windows on demand; VCCL_REG_CACHE=1) -------------
+    def reg_cache_flush(self) -> None:
+        """Collective: drop every window the registration cache holds.  Call it
+        on every rank before cached memory goes back to CUDA (for PyTorch
+        tensors: before torch.cuda.empty_cache()); the peers keep cached
+        allocations open until then."""
+        _check(lib().vcclCommRegCacheFlush(self._comm), "vcclCommRegCacheFlush", self._comm)
+
+    def reg_cache_stats(self) -> dict:
+        """Counters of the registration cache: entries held, calls that
+        consulted it on every rank, buffers reused, buffers registered,
+        entries dropped."""
+        out = (ctypes.c_ulonglong * 5)()
+        _check(lib().vcclCommRegCacheStats(self._comm, out), "vcclCommRegCacheStats", self._comm)
+        return dict(zip(("entries", "calls", "hits", "misses", "evictions"), (int(v) for v in out)))
+
     def window(self, buf: Any, nbytes: Optional[int] = None, flags: int = 0) -> "_WindowScope":
         """`with comm.window(t): ...` registers `t` for the block (collective on
         entry and exit)."""
