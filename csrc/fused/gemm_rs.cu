@@ -460,10 +460,17 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
   const size_t slotBytes = (static_cast<size_t>(rowsPerRank) * N * 2 + 255) / 256 * 256;
   const dev::DevComm& dc = comm->dev->dc;
   // One kernel on CTA pairs (pushes + reduction in the owner's epilogue) when
-  // the pair grid covers every SM, each CTA's 128 rows have one owner and
-  // the owner's tiles fit the arrival counters.
-  if (slotBytes * n <= dc.fusedBytes / 2 && rowsPerRank % gemm::kBM == 0 && gemm::envLongGemm("VCCL_RS_TMA") == 0 &&
-      gemm::envLongGemm("VCCL_RS_TWO_KERNELS") == 0) {
+  // the pair grid covers every SM, each pair tile's 256 rows have one owner
+  // and the owner's tiles fit the arrival counters.  Whole pair tiles per
+  // shard put every rank's own rows last in each pair's tile sequence, so a
+  // pair only waits after all its pushes are out.  With half pair tiles
+  // (rowsPerRank = 128 mod 256) own rows come mid-sequence, and a pair
+  // waiting on them holds back its later pushes, which other ranks' pairs
+  // may be waiting for: at 8 ranks with 56 column tiles that closes a cycle
+  // (a model of the tile walk shows it); those shapes take the two-kernel
+  // path, whose pushes never wait.
+  if (slotBytes * n <= dc.fusedBytes / 2 && rowsPerRank % gemm::kPairBM == 0 &&
+      gemm::envLongGemm("VCCL_RS_TMA") == 0 && gemm::envLongGemm("VCCL_RS_TWO_KERNELS") == 0) {
     const int pairs = gemm::pairClustersFor<fused::EpiRsPair, fused::RsPairHooks>();
     const int tilesN = (N + gemm::kPairBN - 1) / gemm::kPairBN;
     if (2 * pairs == gemm::smCount() && pairs <= dev::kMaxFusedCtas / 2 &&
@@ -479,10 +486,10 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
       hooks.c = dc;
       const int tilesM = (M + gemm::kPairBM - 1) / gemm::kPairBM;
       hooks.pairStartTm = (((comm->rank + 1) % n) * rowsPerRank / gemm::kPairBM) % tilesM;
-      const int shardPairTiles = rowsPerRank % gemm::kPairBM == 0 ? rowsPerRank / gemm::kPairBM : 0;
+      const int shardPairTiles = rowsPerRank / gemm::kPairBM;
       hooks.pairGroupRows = 1;
       for (int gsz = 16; gsz >= 1; gsz /= 2)
-        if (shardPairTiles > 0 && shardPairTiles % gsz == 0) {
+        if (shardPairTiles % gsz == 0) {
           hooks.pairGroupRows = gsz;
           break;
         }

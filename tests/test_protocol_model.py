@@ -15,6 +15,8 @@ Modelled from the kernels (counter names as in csrc/kernels/device_common.cuh):
   all-gather + GEMM   ready / taken / localReady / staged   (csrc/fused/ag_gemm.cu)
   GEMM + RS           done / free, per-call local counters  (csrc/fused/gemm_rs.cu)
   GEMM + RS on pairs  per-half arrivals, consumed counts, free (csrc/fused/gemm_rs.cu, one kernel)
+  its tile walk       every pair's tile order and the accumulator-stage coupling of a CTA pair,
+                      run to a fixed point for cycles of waits (csrc/kernels/gemm_sm100_pair.cuh)
   LL one-shot         per-block epochs, parity slots        (csrc/kernels/ll.cuh)
   MoE dispatch        count-matrix exchange, done counters  (csrc/fused/moe.cu)
 Stream order is modelled too: a rank's kernel for call k+1 starts only after
@@ -403,6 +405,92 @@ def test_gemm_rs_protocol(n, ctas, blocks):
 def test_gemm_rs_pair_protocol(n, ctas):
     for seed in range(120):
         assert run_gemm_rs_pair(n, ctas, calls=5, seed=seed) == []
+
+
+# ---------------------------------------------------------------------------
+# One-kernel GEMM + RS: the real tile walk, checked for cyclic waits
+# ---------------------------------------------------------------------------
+def pair_tile_from(tiles_m, tiles_n, t, group_rows, start_tm, cta):
+    """csrc/kernels/gemm_sm100_pair.cuh pairTileFrom (no split-K): (row0, tn)."""
+    t %= tiles_m * tiles_n
+    group_tiles = group_rows * tiles_n
+    g = t // group_tiles
+    rows_here = min(group_rows, tiles_m - g * group_rows)
+    local = t - g * group_tiles
+    tn = local // rows_here
+    tm = (g * group_rows + local % rows_here + start_tm) % tiles_m
+    return tm * 256 + 128 * cta, tn
+
+
+def rs_pair_walk(r, n, m, tiles_n, pairs):
+    """Per pair of rank r, its pair tiles in order (pair p takes t = p, p + pairs, ...), each as the
+    two CTAs' (owner, half tile) or None past M; start and groups as vcclGemmReduceScatter sets them."""
+    rpr = m // n
+    tiles_m = (m + 255) // 256
+    start = (((r + 1) % n) * rpr // 256) % tiles_m
+    shard_tiles = rpr // 256 if rpr % 256 == 0 else 0
+    group = next((g for g in (16, 8, 4, 2, 1) if shard_tiles > 0 and shard_tiles % g == 0), 1)
+    out = []
+    for p in range(pairs):
+        seq = []
+        for t in range(p, tiles_m * tiles_n, pairs):
+            halves = []
+            for cta in (0, 1):
+                row0, tn = pair_tile_from(tiles_m, tiles_n, t, group, start, cta)
+                if row0 >= m:
+                    halves.append(None)
+                else:
+                    owner = row0 // rpr
+                    halves.append((owner, ((row0 - owner * rpr) // 128) * tiles_n + tn))
+            seq.append(halves)
+        out.append(seq)
+    return out
+
+
+def rs_pair_stuck(n, m, tiles_n, pairs):
+    """One call of the one-kernel GEMM + RS on every rank, run to a fixed point.  A CTA's epilogue
+    takes its half tiles in order; a push lands at once, an own half waits for the n - 1 arrivals;
+    the pair's MMA for tile i reuses accumulator stage i % 2, so either CTA starts tile i only
+    after both finished tile i - 2.  Returns the CTAs left waiting (a cycle of waits)."""
+    walks = [rs_pair_walk(r, n, m, tiles_n, pairs) for r in range(n)]
+    arrive = defaultdict(int)
+    pos = {(r, p, c): 0 for r in range(n) for p in range(pairs) for c in (0, 1)}
+    moved = True
+    while moved:
+        moved = False
+        for (r, p, c) in pos:
+            seq = walks[r][p]
+            while pos[(r, p, c)] < len(seq):
+                i = pos[(r, p, c)]
+                if min(pos[(r, p, 0)], pos[(r, p, 1)]) < i - 1:
+                    break
+                h = seq[i][c]
+                if h is not None:
+                    owner, half = h
+                    if owner != r:
+                        arrive[(owner, half)] += 1
+                    elif arrive[(r, half)] < n - 1:
+                        break
+                pos[(r, p, c)] = i + 1
+                moved = True
+    return [k for k, v in pos.items() if v < len(walks[k[0]][k[1]])]
+
+
+@pytest.mark.parametrize("n", [2, 3, 4, 8])
+def test_gemm_rs_pair_tile_walk(n):
+    """Shapes the one-kernel path takes (M / n a multiple of 256): no cycle of waits for any
+    column-tile count or pair-grid size (own rows end every pair's sequence)."""
+    for rpr in range(256, 2049, 256):
+        for tiles_n in (1, 3, 16, 29, 56):
+            for pairs in (74, 37, 5, 1):
+                assert rs_pair_stuck(n, rpr * n, tiles_n, pairs) == [], (rpr, tiles_n, pairs)
+
+
+def test_model_detects_rs_pair_walk_with_half_pair_tiles():
+    """Negative control: with 128-row shards (half pair tiles) own rows come mid-sequence, and at
+    8 ranks with 56 column tiles (N = 14336) the waits close a cycle; the launcher sends those
+    shapes to the two-kernel path."""
+    assert rs_pair_stuck(8, 128 * 8, 56, 74)
 
 
 def test_model_detects_absolute_arrival_targets():
