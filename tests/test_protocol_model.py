@@ -15,6 +15,7 @@ Modelled from the kernels (counter names as in csrc/kernels/device_common.cuh):
   all-gather + GEMM   ready / taken / localReady / staged   (csrc/fused/ag_gemm.cu)
   GEMM + RS           done / free, per-call local counters  (csrc/fused/gemm_rs.cu)
   GEMM + RS on pairs  per-half arrivals, consumed counts, free (csrc/fused/gemm_rs.cu, one kernel)
+  both forms mixed    the two GEMM + RS forms alternating call by call on shared counters
   its tile walk       every pair's tile order and the accumulator-stage coupling of a CTA pair,
                       run to a fixed point for cycles of waits (csrc/kernels/gemm_sm100_pair.cuh)
   LL one-shot         per-block epochs, parity slots        (csrc/kernels/ll.cuh)
@@ -405,6 +406,153 @@ def test_gemm_rs_protocol(n, ctas, blocks):
 def test_gemm_rs_pair_protocol(n, ctas):
     for seed in range(120):
         assert run_gemm_rs_pair(n, ctas, calls=5, seed=seed) == []
+
+
+# ---------------------------------------------------------------------------
+# GEMM + RS with the two forms alternating on one communicator (the launcher
+# picks the form per call from the shape, alike on every rank)
+# ---------------------------------------------------------------------------
+def run_gemm_rs_mixed(n, ctas, blocks, forms, seed, pair_counts_done=True):
+    """forms[k] is "pair" (one kernel) or "two" (push kernel + sum kernel) for call k.  Shared
+    counters as in csrc/fused/gemm_rs.cu: free[(source, owner)] (one bump per call, either form),
+    the per-CTA GEMM call count (both forms), localDone (both forms add one per CTA, so the
+    two-kernel form's "last CTA" test (k + 1) x ctas holds), done[(owner, source)] and the sum
+    kernel's call count (two-kernel form only), per-half arrivals and consumed counts (one-kernel
+    form only).  pair_counts_done=False drops the one-kernel form's localDone increment (negative
+    control)."""
+    sim = Sim(seed)
+    rng = random.Random(seed * 11 + 3)
+    halves = [rng.choice([1, 2, 3]) for _ in forms]
+    free = defaultdict(int)
+    done = defaultdict(int)
+    local_done = defaultdict(int)
+    local_free = defaultdict(int)
+    reduce_calls = defaultdict(int)
+    pair_free = defaultdict(int)
+    arrive = defaultdict(int)
+    consumed = defaultdict(int)
+    slot = {}              # (owner, source, part) -> call
+    unread = defaultdict(set)  # (owner, source) -> {(call, part)} pushed and not yet read
+    errors = []
+
+    def push(owner, src, part, k):
+        stale = [c for c, _ in unread[(owner, src)] if c < k]
+        if stale:
+            errors.append(f"source {src} call {k} overwrote owner {owner}'s unread data of call {min(stale)}")
+        slot[(owner, src, part)] = k
+        unread[(owner, src)].add((k, part))
+
+    def read(owner, src, part, k):
+        if slot.get((owner, src, part)) != k:
+            errors.append(f"owner {owner} call {k} read {part} of {src} holding call {slot.get((owner, src, part))}")
+        unread[(owner, src)].discard((k, part))
+
+    def make_call(r):
+        def mk(k):
+            live = {"done": 0, "count": 1}
+
+            def two_kernel():
+                kr = reduce_calls[r]  # the sum kernel's per-block call count
+                g = {"done": 0}
+
+                def cta(j):
+                    yield lambda: all(free[(r, q)] >= k for q in range(n))
+                    for q in range(n):
+                        push(q, r, "all", k)
+                    yield lambda: True
+                    local_done[r] += 1
+                    if local_done[r] == (k + 1) * ctas:
+                        for q in range(n):
+                            done[(q, r)] += 1
+                    g["done"] += 1
+
+                for j in range(ctas):
+                    sim.spawn(cta(j))
+                yield lambda: g["done"] == ctas
+                b = {"done": 0}
+
+                def blk(i):
+                    yield lambda: all(done[(r, p)] >= kr + 1 for p in range(n))
+                    if i == 0:
+                        for p in range(n):
+                            read(r, p, "all", k)
+                    local_free[r] += 1
+                    if local_free[r] == (kr + 1) * blocks:
+                        for q in range(n):
+                            free[(q, r)] += 1
+                    b["done"] += 1
+
+                for i in range(blocks):
+                    sim.spawn(blk(i))
+                yield lambda: b["done"] == blocks
+                reduce_calls[r] += 1
+
+            def one_kernel():
+                H = halves[k]
+                tiles = [((r + 1 + i) % n, h) for i in range(n) for h in range(H)]
+                g = {"done": 0}
+
+                def cta(j):
+                    yield lambda: all(free[(r, q)] >= k for q in range(n))
+                    for q, h in tiles[j::ctas]:
+                        if q != r:
+                            push(q, r, h, k)
+                            yield lambda: True
+                            arrive[(q, h)] += 1
+                        else:
+                            target = consumed[(r, h)] + (n - 1)
+                            yield lambda t=target, hh=h: arrive[(r, hh)] >= t
+                            for p in range(n):
+                                if p != r:
+                                    read(r, p, h, k)
+                            consumed[(r, h)] = target
+                    if pair_counts_done:
+                        local_done[r] += 1
+                    pair_free[r] += 1
+                    if pair_free[r] == ctas:
+                        pair_free[r] = 0
+                        for q in range(n):
+                            free[(q, r)] += 1
+                    g["done"] += 1
+
+                for j in range(ctas):
+                    sim.spawn(cta(j))
+                yield lambda: g["done"] == ctas
+
+            def seq():
+                yield from (one_kernel() if forms[k] == "pair" else two_kernel())
+                live["done"] += 1
+
+            live["procs"] = [seq()]
+            return live
+        return mk
+
+    for r in range(n):
+        sim.spawn(kernel_chain(sim, len(forms), make_call(r)))
+    sim.run()
+    return errors
+
+
+@pytest.mark.parametrize("n,ctas,blocks", [(2, 2, 2), (3, 2, 2), (4, 3, 2), (8, 2, 2)])
+def test_gemm_rs_forms_alternate(n, ctas, blocks):
+    """The one-kernel and two-kernel forms interleaved on one communicator (as shapes change from
+    call to call): no deadlock, no overwritten or stale reads."""
+    for seed in range(80):
+        rng = random.Random(seed)
+        forms = [rng.choice(["pair", "two"]) for _ in range(6)]
+        assert run_gemm_rs_mixed(n, ctas, blocks, forms, seed) == [], forms
+
+
+def test_model_detects_forms_without_shared_cta_count():
+    """Negative control: if the one-kernel form did not add to localDone, a later two-kernel call's
+    "last CTA" test would never fire and its sum kernel would wait forever."""
+    failed = 0
+    for seed in range(20):
+        try:
+            failed += bool(run_gemm_rs_mixed(3, 2, 2, ["pair", "two", "pair"], seed, pair_counts_done=False))
+        except Deadlock:
+            failed += 1
+    assert failed > 0
 
 
 # ---------------------------------------------------------------------------
