@@ -161,6 +161,7 @@ vcclResult_t initRank(vcclComm_t* out, int nranks, const vcclUniqueId& id, int r
   if (out == nullptr || nranks < 1 || rank < 0 || rank >= nranks) return vcclInvalidArgument;
   *out = nullptr;
   auto c = std::make_unique<vcclComm>();
+  c->regCache.setCapacity(vccl::regCacheCapacityFromEnv());
   c->rank = rank;
   c->nranks = nranks;
   if (cfg && cfg->size >= offsetof(vcclConfig_t, blocking) + sizeof(int)) c->blocking = cfg->blocking != 0;
@@ -200,7 +201,6 @@ vcclResult_t initRank(vcclComm_t* out, int nranks, const vcclUniqueId& id, int r
       }
     }
     VTRY(vccl::deviceStateCreate(c->bootstrap.get(), device, &c->dev));
-    c->regCache.setCapacity(c->dev->regCacheEntries);
   }
   VINFO("comm ready: rank %d/%d, device %d", rank, nranks, device);
   *out = c.release();

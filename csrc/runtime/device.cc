@@ -259,8 +259,7 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
   ds->regCacheMin = envBytes("VCCL_REG_CACHE_MIN", 16u << 20);
   // Capacity: the reference's VCCL_MR_CACHE (LRU entries, default 16) is
   // honoured as the fallback name.
-  ds->regCacheEntries = static_cast<int>(envLong("VCCL_REG_CACHE_ENTRIES", envLong("VCCL_MR_CACHE", 16)));
-  if (ds->regCacheEntries < 2) ds->regCacheEntries = 2;
+  ds->regCacheEntries = regCacheCapacityFromEnv();
   ds->orderLaunches = envLong("VCCL_LAUNCH_ORDER", 1) != 0;
   // Per GPU, the switch moves about S each way for a window all-reduce of
   // S bytes against 2 (n-1)/n S for the point-to-point kernel.

@@ -4,7 +4,14 @@
 
 #include <algorithm>
 
+#include "common/env.h"
+
 namespace vccl {
+
+int regCacheCapacityFromEnv() {
+  const long cap = envLong("VCCL_REG_CACHE_ENTRIES", envLong("VCCL_MR_CACHE", 16));
+  return cap < kRegMaxBuffers ? kRegMaxBuffers : cap > (1 << 20) ? (1 << 20) : static_cast<int>(cap);
+}
 
 RegQuery RegCacheBook::query(const RegKey* keys, int nbuf, bool eligible) const {
   RegQuery q;

@@ -86,6 +86,10 @@ struct RegStats {
   uint64_t evictions = 0;  // entries dropped (stale, capacity or flush)
 };
 
+// Entries the cache may hold: VCCL_REG_CACHE_ENTRIES, else the reference's
+// VCCL_MR_CACHE, else 16 (at least kRegMaxBuffers).
+int regCacheCapacityFromEnv();
+
 class RegCacheBook {
  public:
   explicit RegCacheBook(int capacity = 32) : capacity_(capacity < kRegMaxBuffers ? kRegMaxBuffers : capacity) {}

@@ -466,5 +466,6 @@ extern "C" vcclResult_t vcclCommRegCacheStats(vcclComm_t comm, unsigned long lon
   out[2] = st.hits;
   out[3] = st.misses;
   out[4] = st.evictions;
+  out[5] = static_cast<unsigned long long>(comm->regCache.capacity());
   return vcclSuccess;
 }

@@ -282,10 +282,50 @@ void directedCases() {
          (unsigned long long)sim.hits);
 }
 
+// The reference's cache scenario (capacity 4): seven distinct buffers in
+// seven calls register seven times and drop three; the four newest stay.
+// Reusing the oldest survivor makes the next registration drop the one after
+// it instead.  A flush then drops everything.
+void lruScenario() {
+  Rng rng(11);
+  Sim sim(2, 4, rng);
+  std::vector<bool> yes(2, true), no(2, false);
+  auto one = [&](int t) {
+    return std::vector<std::vector<Buf>>(2, std::vector<Buf>{{static_cast<uint64_t>(t), 0, kTensorBytes}});
+  };
+  auto cached = [&](int t) {
+    for (const RegEntry& e : sim.books[0].entries())
+      if (e.ptr == sim.mem[0].base[t]) return true;
+    return false;
+  };
+  for (int t = 0; t < 7; t++) sim.call(one(t), yes, no, "lru fill");
+  EXPECT(sim.regs == 7 && sim.books[0].stats().evictions == 3 && sim.books[0].entries().size() == 4,
+         "lru: regs %llu evictions %llu entries %zu", (unsigned long long)sim.regs,
+         (unsigned long long)sim.books[0].stats().evictions, sim.books[0].entries().size());
+  for (int t = 0; t < 3; t++) EXPECT(!cached(t), "lru: buffer %d should have been dropped", t);
+  for (int t = 3; t < 7; t++) EXPECT(cached(t), "lru: buffer %d should be cached", t);
+  sim.call(one(3), yes, no, "lru touch");  // reuse the oldest survivor
+  EXPECT(sim.hits == 1, "lru: buffer 3 was not reused");
+  sim.call(one(7), yes, no, "lru eighth");
+  EXPECT(cached(3) && !cached(4), "lru: the reused buffer must survive and buffer 4 go");
+  EXPECT(sim.books[0].entries().size() == 4, "lru: %zu entries", sim.books[0].entries().size());
+  // Flush: every rank drops every entry, in the same order.
+  const std::vector<int32_t> ids0 = sim.books[0].ids();
+  for (int r = 0; r < 2; r++) {
+    EXPECT(sim.books[r].ids() == ids0, "flush: rank %d holds other ids", r);
+    for (int32_t id : sim.books[r].ids()) {
+      delete static_cast<FakeWindow*>(sim.books[r].drop(id));
+      sim.windows[r].erase(id);
+    }
+    EXPECT(sim.books[r].entries().empty(), "flush: rank %d not empty", r);
+  }
+}
+
 }  // namespace
 
 int main() {
   directedCases();
+  lruScenario();
   int runs = 0;
   for (int nranks : {2, 3, 8})
     for (int cap : {2, 4, 32})

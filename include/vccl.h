@@ -295,9 +295,10 @@ vcclResult_t vcclCommWindowDeregister(vcclComm_t comm, vcclWindow_t win);
  * cached allocations open: drop the cache (collective) before freeing
  * cached memory back to CUDA (torch.cuda.empty_cache()).
  * Stats: out[0] entries, [1] calls that consulted the cache on every rank,
- * [2] buffers reused, [3] buffers registered, [4] entries dropped. */
+ * [2] buffers reused, [3] buffers registered, [4] entries dropped,
+ * [5] capacity. */
 vcclResult_t vcclCommRegCacheFlush(vcclComm_t comm);
-vcclResult_t vcclCommRegCacheStats(vcclComm_t comm, unsigned long long out[5]);
+vcclResult_t vcclCommRegCacheStats(vcclComm_t comm, unsigned long long out[6]);
 
 const char* vcclGetErrorString(vcclResult_t result);
 const char* vcclGetLastError(vcclComm_t comm);

@@ -550,9 +550,29 @@ def test_window_api_without_device():
         assert comm.check_guards() is None  # no device plane, no guard regions
         # The registration cache has nothing to hold without a device plane.
         comm.reg_cache_flush()
-        assert comm.reg_cache_stats() == {"entries": 0, "calls": 0, "hits": 0, "misses": 0, "evictions": 0}
+        assert comm.reg_cache_stats() == {"entries": 0, "calls": 0, "hits": 0, "misses": 0, "evictions": 0,
+                                          "capacity": 16}
     finally:
         comm.destroy()
+
+
+def test_registration_cache_capacity_from_env(monkeypatch):
+    """The cache's capacity comes from VCCL_REG_CACHE_ENTRIES, else the reference's VCCL_MR_CACHE,
+    else 16 (at least 2: a call's send and receive buffers)."""
+    _env()
+    import vkccl_b200 as v
+
+    for env, want in (({"VCCL_MR_CACHE": "4"}, 4), ({"VCCL_MR_CACHE": "4", "VCCL_REG_CACHE_ENTRIES": "7"}, 7),
+                      ({"VCCL_REG_CACHE_ENTRIES": "1"}, 2), ({}, 16)):
+        for k in ("VCCL_MR_CACHE", "VCCL_REG_CACHE_ENTRIES"):
+            monkeypatch.delenv(k, raising=False)
+        for k, val in env.items():
+            monkeypatch.setenv(k, val)
+        comm = v.Communicator(1, v.get_unique_id(), 0)
+        try:
+            assert comm.reg_cache_stats()["capacity"] == want, env
+        finally:
+            comm.destroy()
 
 
 def test_grad_buckets_single_rank_host():

@@ -574,10 +574,10 @@ class Communicator:
     def reg_cache_stats(self) -> dict:
         """Counters of the registration cache: entries held, calls that
         consulted it on every rank, buffers reused, buffers registered,
-        entries dropped."""
-        out = (ctypes.c_ulonglong * 5)()
+        entries dropped, and its capacity."""
+        out = (ctypes.c_ulonglong * 6)()
         _check(lib().vcclCommRegCacheStats(self._comm, out), "vcclCommRegCacheStats", self._comm)
-        return dict(zip(("entries", "calls", "hits", "misses", "evictions"), (int(v) for v in out)))
+        return dict(zip(("entries", "calls", "hits", "misses", "evictions", "capacity"), (int(v) for v in out)))
 
     def window(self, buf: Any, nbytes: Optional[int] = None, flags: int = 0) -> "_WindowScope":
         """`with comm.window(t): ...` registers `t` for the block (collective on
