@@ -138,6 +138,12 @@ def run_vccl(args) -> int:
     srt = sorted(times)
     step_stats = {"min": round(max_over_ranks(srt[0]), 2), "median": round(max_over_ranks(srt[len(srt) // 2]), 2),
                   "max": round(max_over_ranks(srt[-1]), 2)}
+    if world > 1:
+        # every rank's own mean: a slow rank stands out here
+        mine = torch.tensor([sum(times) / len(times)], dtype=torch.float64, device="cuda")
+        every = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        step_stats["by_rank_mean"] = [round(float(t.item()), 2) for t in every]
     # Kernels of this library per step: the all-gather + GEMM kernel and the
     # GEMM + reduce-scatter kernel (one kernel on CTA pairs; the two-kernel
     # form adds its sum kernel); at one rank, the two GEMMs.  The L2 flush
@@ -287,6 +293,9 @@ def breakdown(mlp, x, world, measure):
         "gemm_silu_local": measure(lambda: gemm_silu_mul(xfull, mlp.w_gate_up, out=h), 10, 3, True),
         "gemm_rs": measure(lambda: gemm_reduce_scatter(mlp.comm, h, mlp.w_down), 10, 3, True),
         "gemm_local": measure(lambda: gemm_bf16(h, mlp.w_down), 10, 3, True),
+        # the whole layer with the ranks aligned before every step: set against
+        # the headline (steps back to back), it shows how much rank skew costs
+        "layer_aligned": measure(lambda: mlp.forward(x), 10, 3, True),
     }
     return {k: round(v, 2) for k, v in out.items()}
 
