@@ -59,8 +59,9 @@ def time_steps(step: Callable[[], None], steps: int, flush: Optional[L2Flusher] 
     torch.cuda.synchronize()
     if not align_ranks:
         # Enough lead for the host to enqueue every step (two fused calls and a
-        # flush each, ~0.1-0.3 ms of host work) with room for a host pause.
-        gpu_lead(2.0 + 0.5 * steps)
+        # flush each, ~0.1-0.3 ms of host work) with room for host pauses and
+        # for a host slowed several-fold by other processes on its cores.
+        gpu_lead(10.0 + 1.5 * steps)
     for i in range(steps):
         if align_ranks:
             import torch.distributed as dist
