@@ -9,10 +9,19 @@
 // reduce-scatter afterwards, the GEMM epilogue stores each finished tile
 // directly into the owner's staging slot for this source rank (a plain
 // store over NVLink for remote owners), so the transfer of early tiles
-// overlaps the tensor-core work on later ones.  A short local kernel then
-// sums the n slots of the rows this rank owns.
+// overlaps the tensor-core work on later ones.  Two forms:
 //
-// Synchronisation is device-side and CUDA-graph safe and costs a constant
+//  * one kernel on CTA pairs (the default where pairs cover every SM and
+//    every shard is whole 256-row pair tiles): the owner's own tiles come
+//    last, and their epilogue adds the peers' pushed tiles to its fp32
+//    accumulator (per-half-tile arrival counters, below);
+//  * push kernel + sum kernel (one-SM tiles, half pair tiles per shard,
+//    VCCL_RS_TWO_KERNELS=1 or VCCL_RS_TMA=1): a short local kernel sums the
+//    n slots of the rows this rank owns.
+//
+// The two forms share the call and free counters and may alternate from
+// call to call.  For the two-kernel form, synchronisation is device-side
+// and CUDA-graph safe and costs a constant
 // number of system-scope operations per call: every GEMM CTA (the grid is
 // always one CTA per SM) counts itself on a local counter after its
 // stores, and the last one bumps done[me] on every rank once; the

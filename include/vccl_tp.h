@@ -45,7 +45,9 @@ vcclResult_t vcclAllReduceAddRMSNorm(const void* partial, void* residual, const 
 /* Row-parallel GEMM fused with reduce-scatter over the communicator:
  * every rank computes P = A[M,K] W[N,K]^T, rows of P are owned by rank
  * (row / (M / nranks)); out[M/nranks, N] = sum over ranks of the owned rows.
- * Tiles are pushed to their owner over NVLink from the GEMM epilogue.  Calls
+ * Tiles are pushed to their owner over NVLink from the GEMM epilogue; with
+ * M / nranks a multiple of 256 the owner's own tiles add the pushed ones in
+ * the same kernel, otherwise a second kernel sums them.  Calls
  * with at most VCCL_FUSED_SMALL_M rows (default 512) run as a (split-K)
  * GEMM into scratch followed by the LL or push reduce-scatter.  Every rank
  * calls with the same M, N, K; M % nranks == 0, N % 16 == 0, K % 8 == 0. */
