@@ -45,9 +45,27 @@ $(BIN)/test_%: csrc/tests/test_%.cc $(OUT)/libvccl.so $(HDRS)
 	$(NVCC) $(NVFLAGS) -x cu $< -o $@ -L$(OUT) -lvccl -Xlinker -rpath,'$$ORIGIN/..' $(LDFLAGS)
 
 clean:
-	rm -rf $(OUT)/obj $(OUT)/bin $(OUT)/libvccl.so
+	rm -rf $(OUT)/obj $(OUT)/bin $(OUT)/libvccl.so $(OUT)/kit $(KIT_TAR)
 
-.PHONY: all clean
+# Bring-up kit (the counterpart of the reference's kit/): the library, the
+# tools, the native collective and dmabuf tests, the headers and the
+# bring-up script in one tarball that runs on any node with a CUDA driver
+# (the CUDA runtime is linked statically; binaries find libvccl.so through
+# their $$ORIGIN/.. rpath).  `make kit` -> vkccl_b200/_native/vccl-e2e-kit-<arch>.tar.gz
+KIT     := $(OUT)/kit
+KIT_TAR := $(OUT)/vccl-e2e-kit-$(shell uname -m).tar.gz
+
+kit: $(KIT_TAR)
+
+$(KIT_TAR): $(OUT)/libvccl.so $(TOOLS) $(BIN)/test_collectives $(BIN)/test_dmabuf csrc/tools/vccl-e2e.sh
+	rm -rf $(KIT)
+	mkdir -p $(KIT)/bin $(KIT)/include
+	cp $(OUT)/libvccl.so $(KIT)/
+	cp $(TOOLS) $(BIN)/test_collectives $(BIN)/test_dmabuf csrc/tools/vccl-e2e.sh $(KIT)/bin/
+	cp include/*.h $(KIT)/include/
+	tar -C $(OUT) -czf $@ kit
+
+.PHONY: all clean kit
 
 # Host-only control plane (no CUDA) built with sanitizers for the CPU race
 # checks: `make sanitize` -> bin/test_bootstrap_threads_{tsan,asan}.

@@ -5,9 +5,16 @@
 # VCCL_COMM_ID port so a previous run's socket cannot collide with it.
 #
 #   csrc/tools/vccl-e2e.sh [max bytes] [iters]          (defaults 64M, 20)
+#
+# Inside the bring-up kit (`make kit`) the script sits next to vccl-bench and
+# uses that one; in the source tree it uses the built one.
 set -euo pipefail
-here=$(cd "$(dirname "$0")/../.." && pwd)
-bench=$here/vkccl_b200/_native/bin/vccl-bench
+self=$(cd "$(dirname "$0")" && pwd)
+if [ -x "$self/vccl-bench" ]; then
+  bench=$self/vccl-bench
+else
+  bench=$(cd "$self/../.." && pwd)/vkccl_b200/_native/bin/vccl-bench
+fi
 max=${1:-64M}
 iters=${2:-20}
 ngpu=$(nvidia-smi -L 2>/dev/null | wc -l || echo 0)

@@ -51,6 +51,32 @@ def test_tuning_tables():
     assert "tuning: OK" in _run("test_tuning")
 
 
+def test_bring_up_kit(tmp_path):
+    """`make kit` packs the library, tools, native tests, headers and the bring-up script; unpacked
+    elsewhere, the tools find the library through their rpath."""
+    import glob
+    import platform
+    import tarfile
+
+    root = os.path.dirname(BIN)
+    subprocess.run(["make", "kit"], cwd=os.path.dirname(os.path.dirname(root)), check=True,
+                   capture_output=True, timeout=600)
+    tar = os.path.join(root, f"vccl-e2e-kit-{platform.machine()}.tar.gz")
+    with tarfile.open(tar) as t:
+        names = set(t.getnames())
+        for want in ("kit/libvccl.so", "kit/bin/vccl-bench", "kit/bin/vccl-info", "kit/bin/test_collectives",
+                     "kit/bin/test_dmabuf", "kit/bin/vccl-e2e.sh", "kit/include/vccl.h"):
+            assert want in names, want
+        t.extractall(tmp_path, filter="data")
+    # the kit is a user artefact; the test leaves none behind in the tree
+    subprocess.run(["rm", "-rf", os.path.join(root, "kit"), tar], check=True)
+    p = subprocess.run([str(tmp_path / "kit" / "bin" / "vccl-bench"), "--help"], capture_output=True, text=True,
+                       timeout=60)
+    # it loaded (libvccl.so found next to bin/, else the loader exits 127) and printed its usage
+    assert p.returncode != 127 and "usage: vccl-bench" in (p.stdout + p.stderr), p.stderr
+    assert glob.glob(str(tmp_path / "kit" / "include" / "vccl*.h"))
+
+
 def test_registration_cache_protocol():
     """Registration cache: simulated ranks with their own address layouts run random call sequences
     (reuse, slices, reallocation at the same address, a rank unable to take part, application
