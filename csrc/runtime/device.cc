@@ -241,7 +241,9 @@ vcclResult_t deviceStateCreate(Bootstrap* bs, int device, std::unique_ptr<Device
   // One-hop LL sends (n-1) x 2 x payload from every rank, so its useful range
   // shrinks with the rank count.
   const size_t llDefault = n <= 2 ? (1u << 20) : n <= 4 ? (512u << 10) : (256u << 10);
-  ds->llMaxBytes = envBytes("VCCL_LL_MAX", llDefault);
+  // The reference's latency/bandwidth crossover of all-reduce
+  // (VCCL_ALLREDUCE_RD_MAX) is the fallback name of the same threshold.
+  ds->llMaxBytes = envBytes("VCCL_LL_MAX", envBytes("VCCL_ALLREDUCE_RD_MAX", llDefault));
   if (ds->llMaxBytes > dev::kLLMaxBytes) ds->llMaxBytes = dev::kLLMaxBytes;
   ds->ll2MaxBytes = envBytes("VCCL_LL2_MAX", 4u << 20);
   // Pipelined NVLS all-reduce from 256 MiB: measured on 8 B200 (bf16, bus

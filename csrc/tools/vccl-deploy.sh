@@ -4,15 +4,27 @@
 # swapping atomically so running jobs keep their mapped copy.
 #
 #   csrc/tools/vccl-deploy.sh <host> [<remote dir>]     (default /opt/vkccl_b200)
+#
+# The remote user is VCCL_SSH_USER (default root) unless <host> names one
+# (user@host); VCCL_SSH and VCCL_SCP replace the ssh and scp commands (for
+# example to add -i <key> or a jump host).  Consumers can instead point
+# VCCL_LIBRARY at any copy of the library without deploying it.
 set -euo pipefail
 host=${1:?usage: vccl-deploy.sh <host> [<remote dir>]}
 dest=${2:-/opt/vkccl_b200}
+case $host in
+  *@*) target=$host ;;
+  *) target=${VCCL_SSH_USER:-root}@$host ;;
+esac
+ssh_cmd=${VCCL_SSH:-ssh}
+scp_cmd=${VCCL_SCP:-scp}
 here=$(cd "$(dirname "$0")/../.." && pwd)
 lib=$here/vkccl_b200/_native/libvccl.so
 [ -f "$lib" ] || { echo "build first: make -j" >&2; exit 1; }
 stamp=$(date +%Y%m%d%H%M%S)
-ssh "$host" "mkdir -p '$dest/bin'"
-scp -q "$lib" "$host:$dest/libvccl.so.new.$stamp"
-scp -q "$here"/vkccl_b200/_native/bin/* "$host:$dest/bin/"
-ssh "$host" "cd '$dest' && { [ -f libvccl.so ] && cp -p libvccl.so libvccl.so.bak.$stamp || true; } && mv -f libvccl.so.new.$stamp libvccl.so"
-echo "deployed to $host:$dest (backup libvccl.so.bak.$stamp if there was one)"
+$ssh_cmd "$target" "mkdir -p '$dest/bin'"
+$scp_cmd -q "$lib" "$target:$dest/libvccl.so.new.$stamp"
+$scp_cmd -q "$here"/vkccl_b200/_native/bin/* "$target:$dest/bin/"
+$ssh_cmd "$target" "cd '$dest' && { [ -f libvccl.so ] && cp -p libvccl.so libvccl.so.bak.$stamp || true; } && mv -f libvccl.so.new.$stamp libvccl.so"
+echo "deployed to $target:$dest"
+echo "roll back: $ssh_cmd $target \"cd '$dest' && mv -f libvccl.so.bak.$stamp libvccl.so\" (if a previous library existed)"

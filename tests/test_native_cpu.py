@@ -77,6 +77,31 @@ def test_bring_up_kit(tmp_path):
     assert glob.glob(str(tmp_path / "kit" / "include" / "vccl*.h"))
 
 
+def test_deploy_script_with_fake_ssh(tmp_path):
+    """csrc/tools/vccl-deploy.sh against a stand-in ssh/scp (VCCL_SSH / VCCL_SCP, the reference's
+    override names) that act on a local directory: the library and tools land in place, the user
+    defaults to root, and a second deploy keeps the previous library as a backup."""
+    repo = os.path.dirname(os.path.dirname(os.path.dirname(BIN)))
+    log = tmp_path / "log"
+    ssh = tmp_path / "fake-ssh"
+    ssh.write_text(f'#!/bin/sh\necho "ssh $1" >> {log}\nshift\nsh -c "$1"\n')
+    scp = tmp_path / "fake-scp"
+    scp.write_text('#!/bin/sh\n[ "$1" = -q ] && shift\nn=$#\ni=0\nsrcs=""\n'
+                   'for a in "$@"; do i=$((i+1)); if [ $i -lt $n ]; then srcs="$srcs $a"; else dst=${a#*:}; fi; done\n'
+                   f'echo "scp $dst" >> {log}\ncp $srcs "$dst"\n')
+    ssh.chmod(0o755)
+    scp.chmod(0o755)
+    dest = tmp_path / "node"
+    env = dict(os.environ, VCCL_SSH=str(ssh), VCCL_SCP=str(scp))
+    script = os.path.join(repo, "csrc", "tools", "vccl-deploy.sh")
+    for _ in range(2):
+        p = subprocess.run(["bash", script, "node1", str(dest)], env=env, capture_output=True, text=True, timeout=120)
+        assert p.returncode == 0, p.stdout + p.stderr
+    assert (dest / "libvccl.so").is_file() and (dest / "bin" / "vccl-bench").is_file()
+    assert any(f.name.startswith("libvccl.so.bak.") for f in dest.iterdir())
+    assert "ssh root@node1" in log.read_text()
+
+
 def test_registration_cache_protocol():
     """Registration cache: simulated ranks with their own address layouts run random call sequences
     (reuse, slices, reallocation at the same address, a rank unable to take part, application
