@@ -103,6 +103,7 @@ def main():
     assert st["misses"] == 4 and st["entries"] == 2, st
 
     err = comm.async_error()
+    comm.reg_cache_flush()  # collective: no rank frees memory a peer still has open
     comm.destroy()
     dist.destroy_process_group()
     if err:
