@@ -347,6 +347,11 @@ vcclResult_t vcclCommGetAsyncError(vcclComm_t comm, vcclResult_t* err) {
 
 vcclResult_t vcclCommDestroy(vcclComm_t comm) {
   if (comm == nullptr) return vcclSuccess;
+  // Cached windows hold the peers' allocations open: drop them together
+  // (every rank holds the same entries) before any rank goes on to free its
+  // memory.  An aborted communicator skips the meetings; its windows are
+  // released locally below.
+  if (comm->dev && !comm->aborted.load() && !comm->regCache.entries().empty()) (void)vccl::regCacheFlush(comm);
   {
     std::lock_guard<std::mutex> g(comm->regMu);
     const vccl::DriverApi* d = vccl::driverApi();

@@ -293,7 +293,8 @@ vcclResult_t vcclCommWindowDeregister(vcclComm_t comm, vcclWindow_t win);
  * VCCL_REG_CACHE_ENTRIES defaults to VCCL_MR_CACHE, else 16.
  * Calls inside a stream capture stay on the staged kernels.  Peers keep the
  * cached allocations open: drop the cache (collective) before freeing
- * cached memory back to CUDA (torch.cuda.empty_cache()).
+ * cached memory back to CUDA (torch.cuda.empty_cache()); vcclCommDestroy
+ * drops it as well, together on every rank.
  * Stats: out[0] entries, [1] calls that consulted the cache on every rank,
  * [2] buffers reused, [3] buffers registered, [4] entries dropped,
  * [5] capacity. */
