@@ -110,7 +110,7 @@ struct AgHooks : gemm::PairNoHooks {
   }
   __device__ __forceinline__ const CUtensorMap* aMapFor(const gemm::TileInfo& ti, const CUtensorMap* mapA,
                                                         int* row) const {
-    // ownDirect needs shardRows % 128 == 0, so a CTA's rows never straddle two shards
+    // ownDirect needs shardRows % 256 == 0, so a pair tile's rows lie in one shard
     if (ownDirect != 0 && ti.row0 / shardRows == c.rank) {
       *row = ti.row0 - c.rank * shardRows;
       return &ownMap;
@@ -298,8 +298,12 @@ extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, voi
       break;
     }
   hooks.ctas = static_cast<uint32_t>(ctas);
+  // The own shard is read in place when it is whole pair tiles, so the two
+  // CTAs of a pair always read their rows the same way; a shard of half pair
+  // tiles (M / n = 128 mod 256, e.g. 1024 rows over 8 ranks) reads its staged
+  // copy like the peers' shards.
   hooks.ownDirect = 0;
-  if (usePair && gemm::envLongGemm("VCCL_AG_OWN_STAGED") == 0 && (M / n) % gemm::kBM == 0)
+  if (usePair && gemm::envLongGemm("VCCL_AG_OWN_STAGED") == 0 && (M / n) % gemm::kPairBM == 0)
     hooks.ownDirect = gemm::makeMapKMajor(&hooks.ownMap, xShard, M / n, K, gemm::kBM) ? 1 : 0;
   hooks.trace = comm->dev->fusedTrace;
   const char* xfull = dc.fused[comm->rank] + xOff;
