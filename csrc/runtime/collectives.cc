@@ -366,6 +366,40 @@ bool usesP2pKernel(Kind k) {
   return k == Kind::Send || k == Kind::Recv || k == Kind::Gather || k == Kind::Scatter || k == Kind::AllToAllv;
 }
 
+// The algorithm the latest launch on this thread chose (read back for the
+// call profile, VCCL_PROF=1).
+thread_local const char* tAlgo = nullptr;
+
+void chose(const char* op, const char* algo, int nranks, size_t bytes) {
+  tAlgo = algo;
+  noteAlgorithm(op, algo, nranks, bytes);
+}
+
+const char* opName(Kind k) {
+  switch (k) {
+    case Kind::AllReduce: return "all-reduce";
+    case Kind::Reduce: return "reduce";
+    case Kind::AllGather: return "all-gather";
+    case Kind::ReduceScatter: return "reduce-scatter";
+    case Kind::Broadcast: return "broadcast";
+    case Kind::Gather: return "gather";
+    case Kind::Scatter: return "scatter";
+    case Kind::AllToAllv: return "all-to-all(v)";
+    case Kind::Send: return "send";
+    case Kind::Recv: return "recv";
+  }
+  return "?";
+}
+
+// Bytes a call names (count x type size; all-to-all(v): this rank's sends).
+size_t callBytes(const HostOp& h) {
+  const size_t es = vcclTypeSize(h.dt);
+  if (h.kind != Kind::AllToAllv) return h.count * es;
+  size_t t = 0;
+  for (size_t c : h.sc) t += c * es;
+  return t;
+}
+
 // Launch one non-p2p collective (device pointers by now).
 const char* kindName(Kind k) {
   switch (k) {
@@ -439,7 +473,7 @@ bool windowCollective(const HostOp& h, const LaunchCtx& lc, vcclResult_t* out) {
         sw = false;
         e = launchAllReduceWindow(lc, h.dt, h.redKind, w, false);
       }
-      noteAlgorithm("all-reduce", sw ? "window NVLS" : "window two-shot", n, bytes);
+      chose("all-reduce", sw ? "window NVLS" : "window two-shot", n, bytes);
       *out = cudaToVccl(e, "window all-reduce launch");
       return true;
     }
@@ -450,7 +484,7 @@ bool windowCollective(const HostOp& h, const LaunchCtx& lc, vcclResult_t* out) {
       bindRecv(wr);
       w.send[me] = h.send;  // the send buffer is read locally only
       w.count = bytes;
-      noteAlgorithm("all-gather", w.mcRecv ? "window multimem push" : "window push", n, bytes);
+      chose("all-gather", w.mcRecv ? "window multimem push" : "window push", n, bytes);
       *out = cudaToVccl(launchAllGatherWindow(lc, w), "window all-gather launch");
       return true;
     }
@@ -461,7 +495,7 @@ bool windowCollective(const HostOp& h, const LaunchCtx& lc, vcclResult_t* out) {
       bindRecv(wr);
       w.send[me] = h.send;  // read on the root only
       w.count = bytes;
-      noteAlgorithm("broadcast", w.mcRecv ? "window multimem" : "window push", n, bytes);
+      chose("broadcast", w.mcRecv ? "window multimem" : "window push", n, bytes);
       *out = cudaToVccl(launchBroadcastWindow(lc, w, h.root), "window broadcast launch");
       return true;
     }
@@ -471,7 +505,7 @@ bool windowCollective(const HostOp& h, const LaunchCtx& lc, vcclResult_t* out) {
       if (ws == nullptr) return false;
       bindSend(ws);
       w.recv[me] = h.recv;  // written locally only
-      noteAlgorithm("reduce-scatter", switchRanks && w.mcSend ? "window NVLS" : "window pull", n, bytes);
+      chose("reduce-scatter", switchRanks && w.mcSend ? "window NVLS" : "window pull", n, bytes);
       *out = cudaToVccl(launchReduceScatterWindow(lc, h.dt, h.redKind, w, switchRanks), "window reduce-scatter launch");
       return true;
     }
@@ -558,7 +592,7 @@ vcclResult_t windowAllToAll(const HostOp& h, const Window* wr) {
     total += h.sc[q] * es;
   }
   w.count = 0;  // counts differ per rank; the table check covers them
-  noteAlgorithm("all-to-all(v)", "window push", n, total);
+  chose("all-to-all(v)", "window push", n, total);
   return cudaToVccl(launchAllToAllvWindow(launchCtx(comm, h.stream), w, t, static_cast<int>(es)),
                     "window all-to-all(v) launch");
 }
@@ -587,7 +621,7 @@ vcclResult_t launchColl(const HostOp& h) {
   switch (h.kind) {
     case Kind::AllReduce: {
       ArAlgo algo = pickAllReduce(h, h.count * es);
-      noteAlgorithm("all-reduce", algoName(algo), n, h.count * es);
+      chose("all-reduce", algoName(algo), n, h.count * es);
       cudaError_t e = launchAllReduce(lc, algo, h.dt, h.redKind, a);
       if (e == cudaErrorInvalidValue && algo != ArAlgo::TwoShot) {
         cudaGetLastError();
@@ -599,7 +633,7 @@ vcclResult_t launchColl(const HostOp& h) {
       a.root = h.root;
       return cudaToVccl(launchAllReduce(lc, ArAlgo::TwoShot, h.dt, h.redKind, a), "reduce launch");
     case Kind::ReduceScatter:
-      noteAlgorithm("reduce-scatter", h.count * es <= lc.llMax ? "LL" : "push", n, h.count * es);
+      chose("reduce-scatter", h.count * es <= lc.llMax ? "LL" : "push", n, h.count * es);
       return cudaToVccl(launchReduceScatter(lc, h.dt, h.redKind, a), "reduce-scatter launch");
     case Kind::AllGather: {
       // VCCL_ALLGATHER_ALGO forces the algorithm (read per call, as the
@@ -612,7 +646,7 @@ vcclResult_t launchColl(const HostOp& h) {
         if (f == "ll" || f == "oneshot" || f == "recdouble") agc.llAgMax = dev::kLLMaxBytes;
         else if (f == "pull" || f == "ring") agc.llAgMax = 0;
       }
-      noteAlgorithm("all-gather", h.count * es <= agc.llAgMax ? "LL" : "pull", n, h.count * es);
+      chose("all-gather", h.count * es <= agc.llAgMax ? "LL" : "pull", n, h.count * es);
       return cudaToVccl(launchAllGather(agc, h.send, h.recv, h.count * es), "all-gather launch");
     }
     case Kind::Broadcast: {
@@ -621,7 +655,7 @@ vcclResult_t launchColl(const HostOp& h) {
       if (force.empty() && !comm->dev->tuning.empty()) force = tunedAlgorithm(comm->dev->tuning, "broadcast", n, bytes);
       // The root sends S through the switch instead of (n-1) S to the peers.
       bool nv = lc.nvls && (force == "nvls" || (force.empty() && n >= 3 && bytes >= (256u << 10)));
-      noteAlgorithm("broadcast", bytes <= lc.llMax ? "LL" : nv ? "NVLS multimem" : "pull", n, bytes);
+      chose("broadcast", bytes <= lc.llMax ? "LL" : nv ? "NVLS multimem" : "pull", n, bytes);
       return cudaToVccl(launchBroadcast(lc, h.send, h.recv, bytes, h.root, nv), "broadcast launch");
     }
     default: return vcclInternalError;
@@ -672,6 +706,7 @@ vcclResult_t launchOps(vcclComm_t comm, std::vector<HostOp>& ops, std::vector<Pe
         return vcclInvalidUsage;
       }
       VTRY(runHostSingle(h));
+      comm->noteCall(opName(h.kind), "host", callBytes(h));
     }
     return vcclSuccess;
   }
@@ -686,6 +721,7 @@ vcclResult_t launchOps(vcclComm_t comm, std::vector<HostOp>& ops, std::vector<Pe
       VTRY(prepareBuffers(h, st));  // a host send buffer is staged; the receive buffer is device memory
       VTRY(windowAllToAll(h, a2aWin));
       VTRY(st.finish(h.stream));
+      comm->noteCall(opName(h.kind), "window push", callBytes(h));
       if (h.sync) waits->push_back({comm, h.stream});
       i++;
       continue;
@@ -703,6 +739,7 @@ vcclResult_t launchOps(vcclComm_t comm, std::vector<HostOp>& ops, std::vector<Pe
           VTRY(cudaToVccl(cudaMemcpyAsync(h.recv, h.send, h.count * es, cudaMemcpyDefault, h.stream), "copy"));
         }
         VTRY(st.finish(h.stream));
+        comm->noteCall(opName(h.kind), "local copy", callBytes(h));
         if (h.sync) waits->push_back({comm, h.stream});
         i++;
         continue;
@@ -745,6 +782,7 @@ vcclResult_t launchOps(vcclComm_t comm, std::vector<HostOp>& ops, std::vector<Pe
       VTRY(pb.finalize());
       VTRY(cudaToVccl(launchP2p(launchCtx(comm, s), pb.plan), "point-to-point launch"));
       VTRY(st.finish(s));
+      for (size_t k = i; k < j; k++) comm->noteCall(opName(ops[k].kind), "point-to-point kernel", callBytes(ops[k]));
       if (!others.empty()) {
         cudaEvent_t done = nullptr;
         VTRY(cudaToVccl(cudaEventCreateWithFlags(&done, cudaEventDisableTiming), "event"));
@@ -759,8 +797,11 @@ vcclResult_t launchOps(vcclComm_t comm, std::vector<HostOp>& ops, std::vector<Pe
     OrderedLaunch ord(comm->dev.get(), h.stream);
     VTRY(prepareBuffers(h, st));
     if (comm->dev->regCacheOn && comm->nranks > 1) VTRY(cacheWindowsFor(h, st.ranges.empty()));
+    tAlgo = nullptr;
     VTRY(launchColl(h));
     VTRY(st.finish(h.stream));
+    comm->noteCall(opName(h.kind), tAlgo ? tAlgo : comm->nranks == 1 ? "local copy" : "two-shot to root",
+                   callBytes(h));
     if (h.sync) waits->push_back({comm, h.stream});
     i++;
   }

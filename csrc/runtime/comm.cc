@@ -13,8 +13,11 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
+#include <string>
 #include <thread>
 
 #include "common/env.h"
@@ -112,6 +115,30 @@ bool findDeviceAllocation(const void* p, size_t bytes, void** base, size_t* allo
 }
 }  // namespace vccl
 
+void vcclComm::noteCall(const char* op, const char* algo, size_t bytes) {
+  if (!profOn) return;
+  std::lock_guard<std::mutex> g(profMu);
+  auto& e = prof[{op, algo}];
+  e.first += 1;
+  e.second += bytes;
+}
+
+namespace {
+
+std::string profText(vcclComm_t comm) {
+  std::lock_guard<std::mutex> g(comm->profMu);
+  std::string out;
+  char line[256];
+  for (const auto& kv : comm->prof) {
+    std::snprintf(line, sizeof(line), "%s\t%s\t%llu\t%llu\n", kv.first.first.c_str(), kv.first.second.c_str(),
+                  kv.second.first, kv.second.second);
+    out += line;
+  }
+  return out;
+}
+
+}  // namespace
+
 const vccl::Window* vcclComm::findWindow(const void* p, size_t bytes) {
   std::lock_guard<std::mutex> g(regMu);
   const char* q = static_cast<const char*>(p);
@@ -162,6 +189,7 @@ vcclResult_t initRank(vcclComm_t* out, int nranks, const vcclUniqueId& id, int r
   *out = nullptr;
   auto c = std::make_unique<vcclComm>();
   c->regCache.setCapacity(vccl::regCacheCapacityFromEnv());
+  c->profOn = vccl::envLong("VCCL_PROF", 0) != 0;
   c->rank = rank;
   c->nranks = nranks;
   if (cfg && cfg->size >= offsetof(vcclConfig_t, blocking) + sizeof(int)) c->blocking = cfg->blocking != 0;
@@ -347,6 +375,20 @@ vcclResult_t vcclCommGetAsyncError(vcclComm_t comm, vcclResult_t* err) {
 
 vcclResult_t vcclCommDestroy(vcclComm_t comm) {
   if (comm == nullptr) return vcclSuccess;
+  if (comm->profOn) {
+    // One line per (operation, algorithm) this rank ran.
+    std::string text = profText(comm);
+    size_t pos = 0;
+    while (pos < text.size()) {
+      const size_t end = text.find('\n', pos);
+      std::string row = text.substr(pos, end - pos);
+      pos = end + 1;
+      const size_t t1 = row.find('\t'), t2 = row.find('\t', t1 + 1), t3 = row.find('\t', t2 + 1);
+      std::fprintf(stderr, "[VCCL_PROF r%d] %s, %s: %s calls, %.3f MiB\n", comm->rank, row.substr(0, t1).c_str(),
+                   row.substr(t1 + 1, t2 - t1 - 1).c_str(), row.substr(t2 + 1, t3 - t2 - 1).c_str(),
+                   std::strtoull(row.substr(t3 + 1).c_str(), nullptr, 10) / 1048576.0);
+    }
+  }
   // Cached windows hold the peers' allocations open: drop them together
   // (every rank holds the same entries) before any rank goes on to free its
   // memory.  An aborted communicator skips the meetings; its windows are
@@ -383,6 +425,15 @@ vcclResult_t vcclCommDestroy(vcclComm_t comm) {
   }
   delete comm;
   return vcclSuccess;
+}
+
+extern "C" vcclResult_t vcclxProfSummary(vcclComm_t comm, char* buf, size_t len) {
+  if (comm == nullptr || buf == nullptr || len == 0) return vcclInvalidArgument;
+  const std::string text = profText(comm);
+  const size_t n = text.size() < len - 1 ? text.size() : len - 1;
+  memcpy(buf, text.data(), n);
+  buf[n] = '\0';
+  return text.size() < len ? vcclSuccess : vcclInvalidArgument;
 }
 
 vcclResult_t vcclCommCount(const vcclComm_t comm, int* count) {

@@ -15,6 +15,7 @@
 #include <atomic>
 #include <cstdint>
 #include <initializer_list>
+#include <map>
 #include <memory>
 #include <mutex>
 #include <string>
@@ -213,6 +214,13 @@ struct vcclComm {
 
   std::mutex regCacheMu;        // one cache step at a time
   vccl::RegCacheBook regCache;  // guarded by regCacheMu
+
+  // Call profile (VCCL_PROF=1): per (operation, algorithm), calls and bytes;
+  // printed when the communicator is destroyed (vcclxProfSummary reads it).
+  bool profOn = false;
+  std::mutex profMu;
+  std::map<std::pair<std::string, std::string>, std::pair<unsigned long long, unsigned long long>> prof;
+  void noteCall(const char* op, const char* algo, size_t bytes);
 
   // The application window holding [p, p + bytes), or null (collective
   // buffer lookup).  Cached windows are not returned: a call uses one only

@@ -35,6 +35,14 @@ vcclResult_t vcclxCheckGuards(vcclComm_t comm, unsigned long long* badBytes);
  * vcclInternalError and clears it.  For tests of that error path. */
 vcclResult_t vcclxNoAllocInjectAbort(int device);
 
+/* The call profile of a communicator created with VCCL_PROF=1: one line per
+ * (operation, algorithm) this rank ran, "op\talgorithm\tcalls\tbytes\n",
+ * bytes being count x type size summed over the calls.  The same lines are
+ * printed to stderr when the communicator is destroyed.  Empty without
+ * VCCL_PROF; vcclInvalidArgument when `len` is too small (the text is then
+ * cut off). */
+vcclResult_t vcclxProfSummary(vcclComm_t comm, char* buf, size_t len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -16,7 +16,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import free_port
+from conftest import ROOT, free_port
 
 
 def _env(port=None):
@@ -573,6 +573,48 @@ def test_registration_cache_capacity_from_env(monkeypatch):
             assert comm.reg_cache_stats()["capacity"] == want, env
         finally:
             comm.destroy()
+
+
+def test_call_profile(monkeypatch):
+    """VCCL_PROF=1: per (operation, algorithm) call counts and bytes, readable through
+    prof_summary() and printed to stderr when the communicator is destroyed."""
+    _env()
+    import subprocess
+    import sys
+    import textwrap
+
+    import vkccl_b200 as v
+
+    monkeypatch.setenv("VCCL_PROF", "1")
+    comm = v.Communicator(1, v.get_unique_id(), 0)
+    try:
+        a = np.arange(1000, dtype=np.float32)
+        b = np.zeros_like(a)
+        comm.all_reduce(a, b)
+        comm.all_reduce(a, b)
+        comm.broadcast(a, 0)
+        prof = {(e["op"], e["algo"]): (e["calls"], e["bytes"]) for e in comm.prof_summary()}
+        assert prof[("all-reduce", "host")] == (2, 8000)
+        assert prof[("broadcast", "host")] == (1, 4000)
+    finally:
+        comm.destroy()
+    monkeypatch.delenv("VCCL_PROF")
+    comm = v.Communicator(1, v.get_unique_id(), 0)
+    try:
+        comm.all_reduce(np.ones(4, dtype=np.float32), np.zeros(4, dtype=np.float32))
+        assert comm.prof_summary() == []
+    finally:
+        comm.destroy()
+    code = textwrap.dedent("""
+        import numpy as np, vkccl_b200 as v
+        c = v.Communicator(1, v.get_unique_id(), 0)
+        c.all_reduce(np.ones(256, dtype=np.float32), np.zeros(256, dtype=np.float32))
+        c.destroy()
+    """)
+    p = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120,
+                       env=dict(os.environ, VCCL_PROF="1"), cwd=ROOT)
+    assert p.returncode == 0, p.stderr
+    assert "[VCCL_PROF r0] all-reduce, host: 1 calls, 0.001 MiB" in p.stderr
 
 
 def test_grad_buckets_single_rank_host():

@@ -146,6 +146,7 @@ def _declare_extensions(h: ctypes.CDLL) -> None:
         "vcclxCheckGuards": [P, c.POINTER(c.c_ulonglong)],
         "vcclxBarrierBench": [P, I, I, I, c.POINTER(F)],
         "vcclxNoAllocInjectAbort": [I],
+        "vcclxProfSummary": [P, c.c_char_p, Z],
         "vcclGemmSiluMul": [P, P, P, I, I, I, P],
         "vcclGemmReduceScatter": [P, P, P, I, I, I, P, P],
         "vcclAllGatherGemm": [P, P, P, I, I, I, I, P, P],

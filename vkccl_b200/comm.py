@@ -563,6 +563,19 @@ class Communicator:
         """Collective: undo window_register (before the memory is freed)."""
         _check(lib().vcclCommWindowDeregister(self._comm, handle), "vcclCommWindowDeregister", self._comm)
 
+    # -- call profile (VCCL_PROF=1) ---------------------------------------------
+    def prof_summary(self) -> list:
+        """Per (operation, algorithm) this rank ran since the communicator was
+        created with VCCL_PROF=1: dicts with op, algo, calls and bytes (count x
+        type size summed).  Empty without VCCL_PROF."""
+        buf = ctypes.create_string_buffer(1 << 16)
+        _check(lib().vcclxProfSummary(self._comm, buf, len(buf)), "vcclxProfSummary", self._comm)
+        out = []
+        for line in buf.value.decode().splitlines():
+            op, algo, calls, nbytes = line.split("\t")
+            out.append({"op": op, "algo": algo, "calls": int(calls), "bytes": int(nbytes)})
+        return out
+
     # -- registration cache (windows on demand; VCCL_REG_CACHE=1) -------------
     def reg_cache_flush(self) -> None:
         """Collective: drop every window the registration cache holds.  Call it
