@@ -231,8 +231,10 @@ extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, voi
   OrderedLaunch ord(comm->dev.get(), s);
   const int bnEnv = static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN"));
   cudaError_t e;
-  if (n == 1)  // the gather is the shard itself: the plain GEMM (split-K, CTA pairs or one-SM tiles)
+  if (n == 1) {  // the gather is the shard itself: the plain GEMM (split-K, CTA pairs or one-SM tiles)
+    comm->noteCall("all-gather + gemm", "one rank: GEMM", static_cast<size_t>(M) * K * 2);
     return gemm::gemmWithScratch("vcclAllGatherGemm", xShard, W, out, M, N, K, siluMul, s);
+  }
   if (M <= comm->dev->fusedSmallRows) {
     // Few rows (decode, short prefills): the gather is a few hundred KB, so
     // an LL all-gather into local scratch followed by a (split-K) GEMM beats
@@ -255,6 +257,7 @@ extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, voi
       VERR("vcclAllGatherGemm (small): %s", cudaGetErrorString(e));
       return vcclInvalidArgument;
     }
+    comm->noteCall("all-gather + gemm", "small: LL all-gather, then GEMM", static_cast<size_t>(M) * K * 2);
     return vcclSuccess;
   }
   const dev::DevComm& dc = comm->dev->dc;
@@ -320,5 +323,9 @@ extern "C" vcclResult_t vcclAllGatherGemm(const void* xShard, const void* W, voi
     VERR("vcclAllGatherGemm launch: %s", cudaGetErrorString(e));
     return gemm::launchResult(e);
   }
+  comm->noteCall("all-gather + gemm", usePair ? (hooks.ownDirect ? "one kernel on CTA pairs, own shard in place"
+                                                                  : "one kernel on CTA pairs")
+                                              : "one kernel, one-SM tiles",
+                 static_cast<size_t>(M) * K * 2);
   return vcclSuccess;
 }

@@ -402,12 +402,15 @@ extern "C" vcclResult_t vcclAllReduceAddRMSNorm(const void* partial, void* resid
                   static_cast<char*>(out), static_cast<int>(rows), static_cast<int>(hidden), eps};
   const int n = comm->nranks;
   const size_t bytes = rows * hidden * 2;
+  const char* path = "two-shot";
   if (n == 1) {
     const int grid = static_cast<int>(rows < 1024 ? rows : 1024);
     dev::addRmsNormLocal<<<grid, dev::kNormThreads, 0, s>>>(a);
+    path = "one rank: add + RMSNorm";
   } else if (bytes <= comm->dev->llMaxBytes * 4 && bytes <= dev::kLLMaxBytes &&
              hidden / 4 / dev::kClusterCtas <= dev::kNormThreads * dev::kMaxWordsPerThread) {
     dev::arRmsNormLL<<<comm->dev->llBlocks, dev::kNormThreads, 0, s>>>(comm->dev->dc, a);
+    path = "LL, 8-CTA clusters";
   } else {
     const size_t maxRows = (rows + n - 1) / n;
     const size_t slotRows = comm->dev->dc.dataBytes / (n + 2) / (hidden * 2);
@@ -423,5 +426,6 @@ extern "C" vcclResult_t vcclAllReduceAddRMSNorm(const void* partial, void* resid
     VERR("vcclAllReduceAddRMSNorm launch: %s", cudaGetErrorString(e));
     return vcclUnhandledError;
   }
+  comm->noteCall("all-reduce + residual + RMSNorm", path, bytes);
   return vcclSuccess;
 }

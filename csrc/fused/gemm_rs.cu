@@ -432,8 +432,10 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   OrderedLaunch ord(comm->dev.get(), s);
   const int bnEnv = static_cast<int>(gemm::envLongGemm("VCCL_GEMM_BN"));
-  if (n == 1)  // nothing to scatter: the plain GEMM (split-K, CTA pairs or one-SM tiles)
+  if (n == 1) {  // nothing to scatter: the plain GEMM (split-K, CTA pairs or one-SM tiles)
+    comm->noteCall("gemm + reduce-scatter", "one rank: GEMM", static_cast<size_t>(M) * N * 2);
     return gemm::gemmWithScratch("vcclGemmReduceScatter", A, W, out, M, N, K, false, s);
+  }
   const int rowsPerRank = M / n;
   if (M <= comm->dev->fusedSmallRows && (static_cast<size_t>(rowsPerRank) * N * 2) % 8 == 0) {
     // Few rows: (split-K) GEMM into local scratch, then the LL or push
@@ -464,6 +466,7 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
       VERR("vcclGemmReduceScatter (small): %s", cudaGetErrorString(e));
       return vcclInvalidArgument;
     }
+    comm->noteCall("gemm + reduce-scatter", "small: GEMM, then reduce-scatter", static_cast<size_t>(M) * N * 2);
     return vcclSuccess;
   }
   const size_t slotBytes = (static_cast<size_t>(rowsPerRank) * N * 2 + 255) / 256 * 256;
@@ -507,6 +510,7 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
         VERR("vcclGemmReduceScatter (pairs) launch: %s", cudaGetErrorString(e));
         return gemm::launchResult(e);
       }
+      comm->noteCall("gemm + reduce-scatter", "one kernel on CTA pairs", static_cast<size_t>(M) * N * 2);
       return vcclSuccess;
     }
   }
@@ -564,5 +568,7 @@ extern "C" vcclResult_t vcclGemmReduceScatter(const void* A, const void* W, void
     VERR("vcclGemmReduceScatter reduce launch: %s", cudaGetErrorString(e));
     return vcclUnhandledError;
   }
+  comm->noteCall("gemm + reduce-scatter", tma ? "push (TMA stores) + sum kernel" : "push + sum kernel",
+                 static_cast<size_t>(M) * N * 2);
   return vcclSuccess;
 }

@@ -649,7 +649,9 @@ extern "C" vcclResult_t vcclMoeDispatchFp8(const void* x, const int* topkIds, co
   if (n == 1) {
     moe::moeLocalDispatch<<<moe::localGrid(), moe::kThreads, 0, s>>>(xb, topkIds, topkW, T, H, topk, numExperts, rx,
                                                                recvMeta, recvW, recvCount);
-    return cudaGetLastError() == cudaSuccess ? vcclSuccess : vcclUnhandledError;
+    if (cudaGetLastError() != cudaSuccess) return vcclUnhandledError;
+    comm->noteCall("moe dispatch (fp8)", "one rank: local", static_cast<size_t>(T) * H * 2);
+    return vcclSuccess;
   }
   const moe::Layout L = moe::layoutFor(capacity, H);
   VTRY(deviceStateEnsureMoe(comm->dev.get(), comm->bootstrap.get(), L.total));
@@ -664,6 +666,7 @@ extern "C" vcclResult_t vcclMoeDispatchFp8(const void* x, const int* topkIds, co
     VERR("vcclMoeDispatchFp8 launch: %s", cudaGetErrorString(e));
     return vcclUnhandledError;
   }
+  comm->noteCall("moe dispatch (fp8)", "count, push, receive", static_cast<size_t>(T) * H * 2);
   return vcclSuccess;
 }
 
@@ -694,7 +697,9 @@ extern "C" vcclResult_t vcclMoeCombine(const void* expertOut, const int* recvMet
   auto* o = static_cast<__nv_bfloat16*>(out);
   if (comm->nranks == 1) {
     moe::moeLocalCombine<<<moe::localGrid(), moe::kThreads, 0, s>>>(y, recvW, o, T, H, topk);
-    return cudaGetLastError() == cudaSuccess ? vcclSuccess : vcclUnhandledError;
+    if (cudaGetLastError() != cudaSuccess) return vcclUnhandledError;
+    comm->noteCall("moe combine", "one rank: local", static_cast<size_t>(T) * H * 2);
+    return vcclSuccess;
   }
   const moe::Layout L = moe::layoutFor(capacity, H);
   if (comm->dev->dc.moeBytes < L.total) {
@@ -709,5 +714,6 @@ extern "C" vcclResult_t vcclMoeCombine(const void* expertOut, const int* recvMet
     VERR("vcclMoeCombine launch: %s", cudaGetErrorString(e));
     return vcclUnhandledError;
   }
+  comm->noteCall("moe combine", "push, reduce", static_cast<size_t>(T) * H * 2);
   return vcclSuccess;
 }

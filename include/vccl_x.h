@@ -36,8 +36,10 @@ vcclResult_t vcclxCheckGuards(vcclComm_t comm, unsigned long long* badBytes);
 vcclResult_t vcclxNoAllocInjectAbort(int device);
 
 /* The call profile of a communicator created with VCCL_PROF=1: one line per
- * (operation, algorithm) this rank ran, "op\talgorithm\tcalls\tbytes\n",
- * bytes being count x type size summed over the calls.  The same lines are
+ * (operation, algorithm or path) this rank ran, collectives and the fused
+ * calls of vccl_tp.h alike, "op\talgorithm\tcalls\tbytes\n", bytes being
+ * count x type size for collectives and the activation bytes (M x N or
+ * M x K or T x H, bf16) for fused calls, summed over the calls.  The same lines are
  * printed to stderr when the communicator is destroyed.  Empty without
  * VCCL_PROF; vcclInvalidArgument when `len` is too small (the text is then
  * cut off). */
