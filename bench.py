@@ -76,6 +76,8 @@ def run_vccl(args) -> int:
 
     sys.path.insert(0, ROOT)
     os.environ.setdefault("VCCL_SOCKET_ADDR", "127.0.0.1")
+    # host-side call counts per kernel path (no device work): which forms ran
+    os.environ.setdefault("VCCL_PROF", "1")
     import vkccl_b200 as v
     from vkccl_b200.models.llama_mlp import MLPConfig, TPLlamaMLP
     from vkccl_b200.utils.timing import (ClockSampler, L2Flusher, NvmlClockSampler, bind_to_gpu_cpus,
@@ -188,6 +190,7 @@ def run_vccl(args) -> int:
         if world > 1:
             extras["allreduce_busbw_GBps"] = allreduce_busbw(comm, world, measure, flush)
     flops = mlp.flops(args.tokens)
+    paths = comm.prof_summary()
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -220,6 +223,8 @@ def run_vccl(args) -> int:
             "achieved_tflops": round(flops / (value * 1e-6) / 1e12, 1),
             "roofline": roofline(flops, args.tokens, world, value),
             "rel_err_vs_nccl_cublas": rel_err,
+            # rank 0's calls per (operation, kernel path) over the whole run
+            "paths": {f"{e['op']} / {e['algo']}": e["calls"] for e in paths},
             **extras,
         }
         print(json.dumps(line), flush=True)
