@@ -114,6 +114,18 @@ def main():
         ref = sum(a[rank * per:(rank + 1) * per].float() @ w.float().T for a, w in zip(As, Ws))
         close(out, ref, 2e-2, f"gemm+rs shape sequence m={m}")
 
+    # --- shards of half a pair tile (128 rows per rank) with 56 column tiles: the shape whose
+    # one-kernel tile walk could wait in a cycle at 8 ranks; it must take the two-kernel form
+    m, n_w = 128 * world, 14336
+    g.manual_seed(6000)
+    As = [torch.randn(m, 512, device="cuda", generator=g).bfloat16() for _ in range(world)]
+    Ws = [(torch.randn(n_w, 512, device="cuda", generator=g) * 0.05).bfloat16() for _ in range(world)]
+    per = m // world
+    out = gemm_reduce_scatter(comm, As[rank], Ws[rank])
+    torch.cuda.synchronize()
+    ref = sum(a[rank * per:(rank + 1) * per].float() @ w.float().T for a, w in zip(As, Ws))
+    close(out, ref, 2e-2, f"gemm+rs half pair tiles m={m} n={n_w}")
+
     err = comm.async_error()
     comm.destroy()
     if err != 0:
