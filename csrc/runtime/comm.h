@@ -86,7 +86,7 @@ struct DeviceState {
   bool windowsEnabled = true;      // zero-copy kernels for buffers in registered windows (VCCL_WINDOW)
   int windowNvlsMinRanks = 3;      // window collectives go through the switch from this many ranks
   bool regCacheOn = false;         // windows for plain device buffers on demand (VCCL_REG_CACHE)
-  size_t regCacheMin = 16u << 20;  // ... for calls whose window extent is at least this (VCCL_REG_CACHE_MIN)
+  size_t regCacheMin = 64u << 20;  // ... for calls whose window extent is at least this (VCCL_REG_CACHE_MIN)
   int regCacheEntries = 16;        // ... at most this many at once (VCCL_REG_CACHE_ENTRIES)
   LaunchOrder order;
   bool orderLaunches = true;       // VCCL_LAUNCH_ORDER=0: the application keeps one stream per communicator

@@ -283,11 +283,12 @@ vcclResult_t vcclCommWindowDeregister(vcclComm_t comm, vcclWindow_t win);
  * With VCCL_REG_CACHE=1 on every rank, all-reduce, all-gather,
  * reduce-scatter and broadcast on plain cudaMalloc buffers (PyTorch
  * tensors) of at least VCCL_REG_CACHE_MIN bytes (window extent; default
- * 16 MiB) register their buffers as windows the first time and reuse them
+ * 64 MiB) register their buffers as windows the first time and reuse them
  * afterwards, so those calls run the zero-copy window kernels without
  * vcclCommWindowRegister.  Each such call costs one small host allgather
- * among the ranks (which decides, alike on every rank, whether every rank
- * holds the same cached windows), registering costs a window registration,
+ * among the ranks (tens of microseconds over the bootstrap's TCP sockets,
+ * more with more ranks), which decides, alike on every rank, whether every rank
+ * holds the same cached windows; registering costs a window registration,
  * and dropping an entry (LRU beyond VCCL_REG_CACHE_ENTRIES entries, or
  * an allocation replaced at the same address) synchronizes the device.
  * VCCL_REG_CACHE_ENTRIES defaults to VCCL_MR_CACHE, else 16.
