@@ -14,7 +14,8 @@ on plain torch tensors in every column.
 Every number is device time from CUDA events on the launching stream,
 averaged over --iters launches captured in one CUDA graph (so host launch
 overhead is excluded for both libraries), reported as the maximum over
-ranks.  busbw factors follow the reference bench (reference:
+ranks.  --eager times the same launches without a graph (what the
+registration cache, VCCL_REG_CACHE=1, needs: captured calls stay staged).  busbw factors follow the reference bench (reference:
 bench/vccl_bench.cc:147-152): 2(n-1)/n all-reduce, (n-1)/n all-gather and
 reduce-scatter, 1 broadcast.
 """
@@ -116,6 +117,27 @@ def time_graph(fn, iters: int, warmup: int) -> float:
     return ms * 1000.0
 
 
+def time_eager(fn, iters: int, warmup: int) -> float:
+    """Mean device time per call of `iters` eager launches on the current
+    stream (CUDA events around the loop, behind a short GPU lead so host
+    launches stay ahead).  Used for paths that a graph capture would change:
+    the registration cache (VCCL_REG_CACHE=1) keeps captured calls staged."""
+    from vkccl_b200.utils.timing import gpu_lead
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    gpu_lead(5.0 + 0.2 * iters)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / iters * 1000.0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ops", default="allreduce,allgather,reducescatter,broadcast")
@@ -130,6 +152,8 @@ def main() -> int:
     ap.add_argument("--out", default="")
     ap.add_argument("--tune-out", default="", help="write a VCCL_TUNING_FILE table from the --algos sweep")
     ap.add_argument("--window", action="store_true", help="also time vccl on registered-window buffers")
+    ap.add_argument("--eager", action="store_true",
+                    help="time eager launches instead of a CUDA graph (needed to see VCCL_REG_CACHE=1)")
     a = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -186,7 +210,7 @@ def main() -> int:
                         fn = make_call("vccl", op, comm, ws, wr, world)
                     else:
                         fn = make_call(libname, op, comm, send, recv, world)
-                    us = time_graph(fn, a.iters, a.warmup)
+                    us = (time_eager if a.eager else time_graph)(fn, a.iters, a.warmup)
                     os.environ.pop("VCCL_ALLREDUCE_ALGO", None)
                     if libname == "vccl" and comm.async_error() != 0:
                         raise RuntimeError(f"vccl async error during {op} {count * es} B: {comm.last_error()}")
