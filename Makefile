@@ -47,7 +47,7 @@ $(BIN)/test_%: csrc/tests/test_%.cc $(OUT)/libvccl.so $(HDRS)
 clean:
 	rm -rf $(OUT)/obj $(OUT)/bin $(OUT)/libvccl.so $(OUT)/kit $(KIT_TAR)
 
-# Bring-up kit (the counterpart of the reference's kit/): the library, the
+# Bring-up kit (the counterpart of the reference's kit/build-kit.sh): the library, the
 # tools, the native collective and dmabuf tests, the headers and the
 # bring-up script in one tarball that runs on any node with a CUDA driver
 # (the CUDA runtime is linked statically; binaries find libvccl.so through

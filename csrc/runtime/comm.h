@@ -217,6 +217,8 @@ struct vcclComm {
 
   // Call profile (VCCL_PROF=1): per (operation, algorithm), calls and bytes;
   // printed when the communicator is destroyed (vcclxProfSummary reads it).
+  // The reference's VCCL_PROF times its verbs steps and prints them at exit
+  // (reference: src/transport/verbs.cc:57-91).
   bool profOn = false;
   std::mutex profMu;
   std::map<std::pair<std::string, std::string>, std::pair<unsigned long long, unsigned long long>> prof;

@@ -282,8 +282,9 @@ void directedCases() {
          (unsigned long long)sim.hits);
 }
 
-// The reference's cache scenario (capacity 4): seven distinct buffers in
-// seven calls register seven times and drop three; the four newest stay.
+// The reference's cache scenario (capacity 4; reference:
+// tests/test_mrcache.cc): seven distinct buffers in seven calls register
+// seven times and drop three; the four newest stay.
 // Reusing the oldest survivor makes the next registration drop the one after
 // it instead.  A flush then drops everything.
 void lruScenario() {

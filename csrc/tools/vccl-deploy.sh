@@ -1,7 +1,8 @@
 #!/usr/bin/env bash
 # SPDX-License-Identifier: Apache-2.0
 # Copy a built libvccl.so (and the tools) to a node, keeping a backup and
-# swapping atomically so running jobs keep their mapped copy.
+# swapping atomically so running jobs keep their mapped copy (the
+# reference's tools/deploy.sh does the same for its library alone).
 #
 #   csrc/tools/vccl-deploy.sh <host> [<remote dir>]     (default /opt/vkccl_b200)
 #
