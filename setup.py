@@ -7,6 +7,7 @@ import subprocess
 
 from setuptools import setup
 from setuptools.command.build_py import build_py
+from setuptools.dist import Distribution
 
 
 class BuildNative(build_py):
@@ -16,4 +17,12 @@ class BuildNative(build_py):
         super().run()
 
 
-setup(cmdclass={"build_py": BuildNative})
+class NativeDistribution(Distribution):
+    """The package ships a compiled library (libvccl.so and the tools), so
+    its wheel is tagged for the platform, not as pure Python."""
+
+    def has_ext_modules(self):
+        return True
+
+
+setup(cmdclass={"build_py": BuildNative}, distclass=NativeDistribution)
