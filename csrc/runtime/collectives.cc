@@ -698,18 +698,97 @@ struct PendingSync {
 
 // Launch a communicator's ops in order.  Streams that must be waited on for
 // blocking semantics are appended to `waits`.
-vcclResult_t launchOps(vcclComm_t comm, std::vector<HostOp>& ops, std::vector<PendingSync>* waits) {
-  if (!comm->dev) {
-    for (const HostOp& h : ops) {
-      if (comm->nranks != 1) {
-        VERR("communicator has no CUDA device; data-moving calls need one GPU per rank");
-        return vcclInvalidUsage;
+// One operation of a device-less communicator with several ranks, on the
+// host data plane (host memory only).
+vcclResult_t runHostPlane(HostPlane& hp, const HostOp& h) {
+  const size_t es = vcclTypeSize(h.dt);
+  const HostRed r{h.dt, h.redKind, h.avg, h.premul, h.scalar};
+  switch (h.kind) {
+    case Kind::AllReduce: return hp.allReduce(h.send, h.recv, h.count, r);
+    case Kind::Reduce: return hp.reduce(h.send, h.recv, h.count, r, h.root);
+    case Kind::ReduceScatter: return hp.reduceScatter(h.send, h.recv, h.count, r);
+    case Kind::AllGather: return hp.allGather(h.send, h.recv, h.count * es);
+    case Kind::Broadcast: return hp.broadcast(h.send, h.recv, h.count * es, h.root);
+    case Kind::Gather: return hp.gather(h.send, h.recv, h.count * es, h.root);
+    case Kind::Scatter: return hp.scatter(h.send, h.recv, h.count * es, h.root);
+    case Kind::AllToAllv: {
+      const size_t n = h.sc.size();
+      std::vector<size_t> sc(n), sd(n), rc(n), rd(n);
+      for (size_t p = 0; p < n; p++) {
+        sc[p] = h.sc[p] * es;
+        sd[p] = h.sd[p] * es;
+        rc[p] = h.rc[p] * es;
+        rd[p] = h.rd[p] * es;
       }
+      return hp.allToAllv(h.send, sc.data(), sd.data(), h.recv, rc.data(), rd.data());
+    }
+    default: return vcclInternalError;
+  }
+}
+
+// Device-less communicators: one rank copies locally; several ranks move
+// host memory over the host data plane (made on the first data call, which
+// every rank reaches in the same order).
+vcclResult_t launchHostOps(vcclComm_t comm, std::vector<HostOp>& ops) {
+  if (comm->nranks == 1) {
+    for (const HostOp& h : ops) {
       VTRY(runHostSingle(h));
       comm->noteCall(opName(h.kind), "host", callBytes(h));
     }
     return vcclSuccess;
   }
+  for (const HostOp& h : ops) {
+    if (!h.staged) {
+      VERR("a communicator without a device takes host buffers through the blocking calls only");
+      return vcclInvalidUsage;
+    }
+    for (const char* p : {static_cast<const char*>(h.send), static_cast<const char*>(h.recv)}) {
+      if (p != nullptr && classify(p, -1) != PtrKind::Host) {
+        VERR("a communicator without a device moves host memory only; got a device pointer");
+        return vcclInvalidArgument;
+      }
+    }
+  }
+  HostPlane* hp = nullptr;
+  {
+    std::lock_guard<std::mutex> g(comm->hostPlaneMu);
+    hp = comm->hostPlane.get();
+  }
+  if (hp == nullptr) {
+    std::unique_ptr<HostPlane> made;
+    VTRY(HostPlane::create(comm->bootstrap.get(), &made));
+    std::lock_guard<std::mutex> g(comm->hostPlaneMu);
+    comm->hostPlane = std::move(made);
+    hp = comm->hostPlane.get();
+  }
+  size_t i = 0;
+  while (i < ops.size()) {
+    const HostOp& h = ops[i];
+    if (isP2pKind(h.kind)) {
+      // A run of sends and receives progresses together (group semantics).
+      std::vector<HostXfer> xs;
+      size_t j = i;
+      for (; j < ops.size() && isP2pKind(ops[j].kind); j++) {
+        const HostOp& o = ops[j];
+        const size_t bytes = o.count * vcclTypeSize(o.dt);
+        if (o.peer == comm->rank) return vcclInvalidArgument;
+        xs.push_back({o.kind == Kind::Send, o.peer,
+                      o.kind == Kind::Send ? const_cast<char*>(o.send) : o.recv, bytes});
+        comm->noteCall(opName(o.kind), "host TCP mesh", bytes);
+      }
+      VTRY(hp->run(xs));
+      i = j;
+      continue;
+    }
+    VTRY(runHostPlane(*hp, h));
+    comm->noteCall(opName(h.kind), "host TCP mesh", callBytes(h));
+    i++;
+  }
+  return vcclSuccess;
+}
+
+vcclResult_t launchOps(vcclComm_t comm, std::vector<HostOp>& ops, std::vector<PendingSync>* waits) {
+  if (!comm->dev) return launchHostOps(comm, ops);
   cudaSetDevice(comm->dev->device);
   size_t i = 0;
   while (i < ops.size()) {

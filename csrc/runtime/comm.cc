@@ -362,6 +362,10 @@ vcclResult_t vcclCommAbort(vcclComm_t comm) {
   vccl::setThreadLastError("communicator aborted by vcclCommAbort");
   comm->noteError(vcclUnhandledError);
   if (comm->bootstrap) comm->bootstrap->abort();
+  {
+    std::lock_guard<std::mutex> g(comm->hostPlaneMu);
+    if (comm->hostPlane) comm->hostPlane->abort();
+  }
   return vcclSuccess;
 }
 

@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "control/bootstrap.h"
+#include "runtime/hostplane.h"
 #include "runtime/regcache.h"
 #include "runtime/tuning.h"
 #include "kernels/device_common.cuh"
@@ -214,6 +215,11 @@ struct vcclComm {
 
   std::mutex regCacheMu;        // one cache step at a time
   vccl::RegCacheBook regCache;  // guarded by regCacheMu
+
+  // Host data plane of a communicator without a device and with more than
+  // one rank (runtime/hostplane.h), made on its first data call.
+  std::mutex hostPlaneMu;  // guards the pointer (vcclCommAbort reads it)
+  std::unique_ptr<vccl::HostPlane> hostPlane;
 
   // Call profile (VCCL_PROF=1): per (operation, algorithm), calls and bytes;
   // printed when the communicator is destroyed (vcclxProfSummary reads it).

@@ -1,0 +1,515 @@
+// SPDX-License-Identifier: Apache-2.0
+// Host data plane over a TCP mesh (see hostplane.h).
+#include "runtime/hostplane.h"
+
+#include <arpa/inet.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <errno.h>
+#include <poll.h>
+#include <sys/socket.h>
+
+#include <algorithm>
+#include <cstring>
+#include <deque>
+
+#include "common/env.h"
+#include "common/log.h"
+#include "common/net.h"
+#include "control/bootstrap.h"
+#include "kernels/dtypes.cuh"
+
+namespace vccl {
+
+namespace {
+
+#ifndef MSG_NOSIGNAL
+#define MSG_NOSIGNAL 0
+#endif
+
+// Storage type S reduced in accumulation type A.
+template <typename S>
+struct Elem {
+  using A = S;
+  static A in(S v) { return v; }
+  static S out(A v) { return v; }
+};
+template <>
+struct Elem<__half> {
+  using A = float;
+  static A in(__half v) { return __half2float(v); }
+  static __half out(A v) { return __float2half_rn(v); }
+};
+template <>
+struct Elem<__nv_bfloat16> {
+  using A = float;
+  static A in(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __nv_bfloat16 out(A v) { return __float2bfloat16_rn(v); }
+};
+template <>
+struct Elem<__nv_fp8_e4m3> {
+  using A = float;
+  static A in(__nv_fp8_e4m3 v) { return static_cast<float>(v); }
+  static __nv_fp8_e4m3 out(A v) { return __nv_fp8_e4m3(v); }
+};
+template <>
+struct Elem<__nv_fp8_e5m2> {
+  using A = float;
+  static A in(__nv_fp8_e5m2 v) { return static_cast<float>(v); }
+  static __nv_fp8_e5m2 out(A v) { return __nv_fp8_e5m2(v); }
+};
+
+template <typename A>
+inline A combine(int kind, A a, A b) {
+  switch (kind) {
+    case dev::kProd: return a * b;
+    case dev::kMax: return a < b ? b : a;
+    case dev::kMin: return b < a ? b : a;
+    default: return a + b;
+  }
+}
+
+template <typename S>
+void reduceT(char* out, const std::vector<const char*>& src, size_t count, const HostRed& r) {
+  using E = Elem<S>;
+  using A = typename E::A;
+  const size_t n = src.size();
+  S* o = reinterpret_cast<S*>(out);
+  for (size_t i = 0; i < count; i++) {
+    // Read every contribution of element i before writing it: the output
+    // may be one of the contributions (in-place calls).
+    A acc = E::in(reinterpret_cast<const S*>(src[0])[i]);
+    for (size_t p = 1; p < n; p++) acc = combine<A>(r.kind, acc, E::in(reinterpret_cast<const S*>(src[p])[i]));
+    if (r.avg) acc = static_cast<A>(acc / static_cast<A>(n));
+    o[i] = E::out(acc);
+  }
+}
+
+template <typename S>
+void scaleT(char* out, const char* in, size_t count, double scalar) {
+  using E = Elem<S>;
+  using A = typename E::A;
+  const S* x = reinterpret_cast<const S*>(in);
+  S* o = reinterpret_cast<S*>(out);
+  for (size_t i = 0; i < count; i++) o[i] = E::out(static_cast<A>(E::in(x[i]) * static_cast<A>(scalar)));
+}
+
+template <template <typename> class F, typename... Args>
+void byType(vcclDataType_t dt, Args&&... args) {
+  switch (dt) {
+    case vcclInt8: F<int8_t>::run(args...); break;
+    case vcclUint8: F<uint8_t>::run(args...); break;
+    case vcclInt32: F<int32_t>::run(args...); break;
+    case vcclUint32: F<uint32_t>::run(args...); break;
+    case vcclInt64: F<int64_t>::run(args...); break;
+    case vcclUint64: F<uint64_t>::run(args...); break;
+    case vcclFloat16: F<__half>::run(args...); break;
+    case vcclFloat32: F<float>::run(args...); break;
+    case vcclFloat64: F<double>::run(args...); break;
+    case vcclBfloat16: F<__nv_bfloat16>::run(args...); break;
+    case vcclFloat8e4m3: F<__nv_fp8_e4m3>::run(args...); break;
+    case vcclFloat8e5m2: F<__nv_fp8_e5m2>::run(args...); break;
+    default: break;
+  }
+}
+
+template <typename S>
+struct ReduceF {
+  static void run(char* out, const std::vector<const char*>& src, size_t count, const HostRed& r) {
+    reduceT<S>(out, src, count, r);
+  }
+};
+template <typename S>
+struct ScaleF {
+  static void run(char* out, const char* in, size_t count, double scalar) { scaleT<S>(out, in, count, scalar); }
+};
+
+size_t ceilDiv(size_t a, size_t b) { return (a + b - 1) / b; }
+
+}  // namespace
+
+// True on every rank iff `mine` is true on every rank (runtime/device.cc).
+bool everyone(Bootstrap* bs, bool mine);
+
+void hostReduce(char* out, const std::vector<const char*>& src, size_t count, const HostRed& r) {
+  byType<ReduceF>(r.dt, out, src, count, r);
+}
+
+void hostScale(char* out, const char* in, size_t count, vcclDataType_t dt, double scalar) {
+  byType<ScaleF>(dt, out, in, count, scalar);
+}
+
+// ---- mesh --------------------------------------------------------------------
+
+vcclResult_t HostPlane::create(Bootstrap* bs, std::unique_ptr<HostPlane>* out) {
+  const int n = bs->nranks(), me = bs->rank();
+  std::unique_ptr<HostPlane> hp(new HostPlane(me, n));
+  hp->fd_.assign(n, -1);
+  hp->chunk_ = envBytes("VCCL_HOST_CHUNK", 8u << 20);
+  if (hp->chunk_ < 4096) hp->chunk_ = 4096;
+  hp->directMax_ = envBytes("VCCL_HOST_AR_DIRECT", 64u << 10);
+  // Every rank listens, then the ranks exchange endpoints: a rank connects to
+  // every higher rank (connections complete into the peer's backlog, so the
+  // order cannot deadlock) and accepts every lower one.
+  int lfd = -1;
+  uint16_t port = 0;
+  WireEndpoint mine{};
+  bool ok = tcpListen(0, &lfd, &port) == vcclSuccess && localEndpoint(&mine) == vcclSuccess;
+  mine.portBE = htons(port);
+  struct Entry {
+    WireEndpoint ep;
+    int32_t ok;
+  };
+  std::vector<Entry> all(n);
+  all[me] = Entry{mine, ok ? 1 : 0};
+  vcclResult_t res = bs->allGather(all.data(), sizeof(Entry));
+  if (res != vcclSuccess) {
+    closeFd(lfd);
+    return res;
+  }
+  for (const Entry& e : all) ok = ok && e.ok != 0;
+  if (!ok) {
+    closeFd(lfd);
+    VERR("host data plane: a rank could not open its listening socket");
+    return vcclSystemError;
+  }
+  for (int p = me + 1; p < n && res == vcclSuccess; p++) {
+    int fd = -1;
+    res = tcpConnect(all[p].ep, connectWindowMs(), &fd);
+    const int32_t who = me;
+    if (res == vcclSuccess) res = sendFull(fd, &who, sizeof(who));
+    hp->fd_[p] = fd;
+  }
+  for (int k = 0; k < me && res == vcclSuccess; k++) {
+    int fd = -1;
+    res = tcpAccept(lfd, nullptr, &fd);
+    int32_t who = -1;
+    if (res == vcclSuccess) res = recvFull(fd, &who, sizeof(who));
+    if (res == vcclSuccess && (who < 0 || who >= me || hp->fd_[who] >= 0)) {
+      VERR("host data plane: unexpected connection (rank %d) on rank %d", who, me);
+      res = vcclSystemError;
+    }
+    if (res == vcclSuccess) {
+      hp->fd_[who] = fd;
+    } else {
+      closeFd(fd);
+    }
+  }
+  closeFd(lfd);
+  // Every rank learns whether every mesh link came up.
+  const bool meshOk = everyone(bs, res == vcclSuccess);
+  if (!meshOk) return res != vcclSuccess ? res : vcclSystemError;
+  VINFO("host data plane: TCP mesh of %d ranks ready", n);
+  *out = std::move(hp);
+  return vcclSuccess;
+}
+
+HostPlane::~HostPlane() {
+  for (int fd : fd_) closeFd(fd);
+}
+
+void HostPlane::abort() {
+  aborted_.store(true);
+  for (int fd : fd_)
+    if (fd >= 0) shutdownFd(fd);
+}
+
+// ---- progress loop ---------------------------------------------------------
+
+vcclResult_t HostPlane::run(const std::vector<HostXfer>& xs) {
+  struct PeerQ {
+    std::deque<const HostXfer*> sends, recvs;
+    size_t soff = 0, roff = 0;
+  };
+  std::vector<PeerQ> q(n_);
+  size_t pending = 0;
+  for (const HostXfer& x : xs) {
+    if (x.peer < 0 || x.peer >= n_ || x.peer == rank_ || fd_[x.peer] < 0) {
+      VERR("host data plane: transfer with invalid peer %d", x.peer);
+      return vcclInternalError;
+    }
+    if (x.bytes == 0) continue;
+    (x.send ? q[x.peer].sends : q[x.peer].recvs).push_back(&x);
+    pending++;
+  }
+  Deadline dl;
+  std::vector<pollfd> pfd;
+  std::vector<int> who;
+  while (pending > 0) {
+    if (aborted_.load()) {
+      VERR("host data plane: communicator aborted");
+      return vcclSystemError;
+    }
+    bool moved = false;
+    for (int p = 0; p < n_; p++) {
+      PeerQ& pq = q[p];
+      // Send as much as the socket takes, then take what has arrived.
+      while (!pq.sends.empty()) {
+        const HostXfer* x = pq.sends.front();
+        const ssize_t k = ::send(fd_[p], x->buf + pq.soff, x->bytes - pq.soff, MSG_DONTWAIT | MSG_NOSIGNAL);
+        if (k > 0) {
+          moved = true;
+          pq.soff += static_cast<size_t>(k);
+          if (pq.soff == x->bytes) {
+            pq.sends.pop_front();
+            pq.soff = 0;
+            pending--;
+          }
+          continue;
+        }
+        if (k < 0 && errno == EINTR) continue;
+        if (k < 0 && (errno == EAGAIN || errno == EWOULDBLOCK)) break;
+        VERR("host data plane: send to rank %d failed: %s", p, k == 0 ? "no progress" : strerror(errno));
+        return vcclSystemError;
+      }
+      while (!pq.recvs.empty()) {
+        const HostXfer* x = pq.recvs.front();
+        const ssize_t k = ::recv(fd_[p], x->buf + pq.roff, x->bytes - pq.roff, MSG_DONTWAIT);
+        if (k > 0) {
+          moved = true;
+          pq.roff += static_cast<size_t>(k);
+          if (pq.roff == x->bytes) {
+            pq.recvs.pop_front();
+            pq.roff = 0;
+            pending--;
+          }
+          continue;
+        }
+        if (k == 0) {
+          VERR("host data plane: rank %d closed its stream", p);
+          return vcclSystemError;
+        }
+        if (errno == EINTR) continue;
+        if (errno == EAGAIN || errno == EWOULDBLOCK) break;
+        VERR("host data plane: recv from rank %d failed: %s", p, strerror(errno));
+        return vcclSystemError;
+      }
+    }
+    if (pending == 0 || moved) continue;
+    // Nothing moved: wait until some stream can.
+    pfd.clear();
+    who.clear();
+    for (int p = 0; p < n_; p++) {
+      short ev = 0;
+      if (!q[p].sends.empty()) ev |= POLLOUT;
+      if (!q[p].recvs.empty()) ev |= POLLIN;
+      if (ev) {
+        pfd.push_back(pollfd{fd_[p], ev, 0});
+        who.push_back(p);
+      }
+    }
+    const int rc = ::poll(pfd.data(), pfd.size(), dl.pollSliceMs());
+    if (rc < 0 && errno != EINTR) {
+      VERR("host data plane: poll failed: %s", strerror(errno));
+      return vcclSystemError;
+    }
+    for (size_t i = 0; rc > 0 && i < pfd.size(); i++) {
+      // A closed or failed stream with nothing left to read is an error; with
+      // data pending, the next pass reads it and then sees the close.
+      if ((pfd[i].revents & (POLLERR | POLLNVAL)) != 0) {
+        VERR("host data plane: stream to rank %d failed", who[i]);
+        return vcclSystemError;
+      }
+    }
+    if (rc == 0 && dl.expired()) {
+      VERR("host data plane: timed out after VCCL_TIMEOUT=%ds", watchdogSeconds());
+      return vcclSystemError;
+    }
+  }
+  return vcclSuccess;
+}
+
+// ---- collectives -----------------------------------------------------------
+
+vcclResult_t HostPlane::allGather(const char* send, char* recv, size_t bytes) {
+  if (bytes == 0) return vcclSuccess;
+  char* mine = recv + rank_ * bytes;
+  if (mine != send) memmove(mine, send, bytes);
+  std::vector<HostXfer> xs;
+  for (int p = 0; p < n_; p++) {
+    if (p == rank_) continue;
+    xs.push_back({true, p, mine, bytes});
+    xs.push_back({false, p, recv + p * bytes, bytes});
+  }
+  return run(xs);
+}
+
+vcclResult_t HostPlane::broadcast(const char* send, char* recv, size_t bytes, int root) {
+  if (bytes == 0) return vcclSuccess;
+  std::vector<HostXfer> xs;
+  if (rank_ == root) {
+    if (recv != send) memmove(recv, send, bytes);
+    for (int p = 0; p < n_; p++)
+      if (p != root) xs.push_back({true, p, recv, bytes});
+  } else {
+    xs.push_back({false, root, recv, bytes});
+  }
+  return run(xs);
+}
+
+vcclResult_t HostPlane::gather(const char* send, char* recv, size_t bytes, int root) {
+  if (bytes == 0) return vcclSuccess;
+  std::vector<HostXfer> xs;
+  if (rank_ == root) {
+    if (recv + root * bytes != send) memmove(recv + root * bytes, send, bytes);
+    for (int p = 0; p < n_; p++)
+      if (p != root) xs.push_back({false, p, recv + p * bytes, bytes});
+  } else {
+    xs.push_back({true, root, const_cast<char*>(send), bytes});
+  }
+  return run(xs);
+}
+
+vcclResult_t HostPlane::scatter(const char* send, char* recv, size_t bytes, int root) {
+  if (bytes == 0) return vcclSuccess;
+  std::vector<HostXfer> xs;
+  if (rank_ == root) {
+    if (recv != send + root * bytes) memmove(recv, send + root * bytes, bytes);
+    for (int p = 0; p < n_; p++)
+      if (p != root) xs.push_back({true, p, const_cast<char*>(send + p * bytes), bytes});
+  } else {
+    xs.push_back({false, root, recv, bytes});
+  }
+  return run(xs);
+}
+
+vcclResult_t HostPlane::allToAllv(const char* send, const size_t* sc, const size_t* sd, char* recv,
+                                  const size_t* rc, const size_t* rd) {
+  // A receive range that overlaps the send buffer would be overwritten
+  // before it leaves: send from a copy then.
+  size_t sEnd = 0, rEnd = 0;
+  for (int p = 0; p < n_; p++) {
+    sEnd = std::max(sEnd, sd[p] + sc[p]);
+    rEnd = std::max(rEnd, rd[p] + rc[p]);
+  }
+  std::vector<char> copy;
+  if (send < recv + rEnd && recv < send + sEnd) {
+    copy.assign(send, send + sEnd);
+    send = copy.data();
+  }
+  if (sc[rank_] > 0) memmove(recv + rd[rank_], send + sd[rank_], sc[rank_]);
+  std::vector<HostXfer> xs;
+  for (int s = 1; s < n_; s++) {
+    const int to = (rank_ + s) % n_, from = (rank_ - s + n_) % n_;
+    xs.push_back({true, to, const_cast<char*>(send + sd[to]), sc[to]});
+    xs.push_back({false, from, recv + rd[from], rc[from]});
+  }
+  return run(xs);
+}
+
+vcclResult_t HostPlane::reduceScatter(const char* send, char* recv, size_t recvCount, const HostRed& r) {
+  const size_t es = vcclTypeSize(r.dt);
+  if (recvCount == 0) return vcclSuccess;
+  const size_t cb = recvCount * es;
+  std::vector<char> scaled;
+  if (r.premul) {
+    scaled.resize(cb * n_);
+    hostScale(scaled.data(), send, recvCount * n_, r.dt, r.scalar);
+    send = scaled.data();
+  }
+  const size_t pe = std::max<size_t>(1, chunk_ / es);
+  std::vector<char> tmp(std::min(pe, recvCount) * es * n_);
+  std::vector<const char*> src(n_);
+  for (size_t off = 0; off < recvCount; off += pe) {
+    const size_t m = std::min(pe, recvCount - off);
+    std::vector<HostXfer> xs;
+    for (int p = 0; p < n_; p++) {
+      if (p == rank_) continue;
+      xs.push_back({true, p, const_cast<char*>(send + p * cb + off * es), m * es});
+      xs.push_back({false, p, tmp.data() + p * m * es, m * es});
+    }
+    VTRY(run(xs));
+    for (int p = 0; p < n_; p++) src[p] = p == rank_ ? send + rank_ * cb + off * es : tmp.data() + p * m * es;
+    hostReduce(recv + off * es, src, m, r);
+  }
+  return vcclSuccess;
+}
+
+vcclResult_t HostPlane::reduce(const char* send, char* recv, size_t count, const HostRed& r, int root) {
+  const size_t es = vcclTypeSize(r.dt);
+  if (count == 0) return vcclSuccess;
+  std::vector<char> scaled;
+  if (r.premul) {
+    scaled.resize(count * es);
+    hostScale(scaled.data(), send, count, r.dt, r.scalar);
+    send = scaled.data();
+  }
+  const size_t pe = std::max<size_t>(1, chunk_ / es);
+  if (rank_ != root) {
+    std::vector<HostXfer> xs{{true, root, const_cast<char*>(send), count * es}};
+    return run(xs);
+  }
+  std::vector<char> tmp(std::min(pe, count) * es * n_);
+  std::vector<const char*> src(n_);
+  for (size_t off = 0; off < count; off += pe) {
+    const size_t m = std::min(pe, count - off);
+    std::vector<HostXfer> xs;
+    for (int p = 0; p < n_; p++)
+      if (p != rank_) xs.push_back({false, p, tmp.data() + p * m * es, m * es});
+    VTRY(run(xs));
+    for (int p = 0; p < n_; p++) src[p] = p == rank_ ? send + off * es : tmp.data() + p * m * es;
+    hostReduce(recv + off * es, src, m, r);
+  }
+  return vcclSuccess;
+}
+
+vcclResult_t HostPlane::allReduce(const char* send, char* recv, size_t count, const HostRed& r) {
+  const size_t es = vcclTypeSize(r.dt);
+  if (count == 0) return vcclSuccess;
+  const size_t bytes = count * es;
+  std::vector<char> scaled;
+  if (r.premul) {
+    scaled.resize(bytes);
+    hostScale(scaled.data(), send, count, r.dt, r.scalar);
+    send = scaled.data();
+  }
+  std::vector<const char*> src(n_);
+  if (bytes <= directMax_ || count < static_cast<size_t>(n_)) {
+    // Small: every rank sends the whole message to every peer and reduces
+    // the n copies in rank order.
+    std::vector<char> tmp(bytes * n_);
+    std::vector<HostXfer> xs;
+    for (int p = 0; p < n_; p++) {
+      if (p == rank_) continue;
+      xs.push_back({true, p, const_cast<char*>(send), bytes});
+      xs.push_back({false, p, tmp.data() + p * bytes, bytes});
+    }
+    VTRY(run(xs));
+    for (int p = 0; p < n_; p++) src[p] = p == rank_ ? send : tmp.data() + p * bytes;
+    hostReduce(recv, src, count, r);
+    return vcclSuccess;
+  }
+  // Large: rank q owns elements [q * bc, (q + 1) * bc) (the last block may be
+  // shorter); reduce-scatter in pieces, then all-gather of the owned blocks.
+  const size_t bc = ceilDiv(count, n_);
+  auto blkOff = [&](int q) { return std::min(static_cast<size_t>(q) * bc, count); };
+  auto blkLen = [&](int q) { return std::min(static_cast<size_t>(q + 1) * bc, count) - blkOff(q); };
+  const size_t pe = std::max<size_t>(1, chunk_ / es);
+  const size_t ps = std::min(pe, bc);  // elements of one peer's piece in tmp
+  std::vector<char> tmp(ps * es * n_);
+  for (size_t off = 0; off < bc; off += pe) {
+    std::vector<HostXfer> xs;
+    auto len = [&](int q) { return blkLen(q) > off ? std::min(pe, blkLen(q) - off) : size_t{0}; };
+    const size_t mine = len(rank_);
+    for (int p = 0; p < n_; p++) {
+      if (p == rank_) continue;
+      xs.push_back({true, p, const_cast<char*>(send + (blkOff(p) + off) * es), len(p) * es});
+      xs.push_back({false, p, tmp.data() + p * ps * es, mine * es});
+    }
+    VTRY(run(xs));
+    if (mine == 0) continue;
+    for (int p = 0; p < n_; p++)
+      src[p] = p == rank_ ? send + (blkOff(rank_) + off) * es : tmp.data() + p * ps * es;
+    hostReduce(recv + (blkOff(rank_) + off) * es, src, mine, r);
+  }
+  std::vector<HostXfer> xs;
+  for (int p = 0; p < n_; p++) {
+    if (p == rank_) continue;
+    xs.push_back({true, p, recv + blkOff(rank_) * es, blkLen(rank_) * es});
+    xs.push_back({false, p, recv + blkOff(p) * es, blkLen(p) * es});
+  }
+  return run(xs);
+}
+
+}  // namespace vccl

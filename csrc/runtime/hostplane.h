@@ -1,0 +1,110 @@
+// SPDX-License-Identifier: Apache-2.0
+// Host data plane: collectives on host memory over TCP, for communicators
+// without a device (VCCL_NO_DEVICE=1, or a host with no GPU) whose ranks
+// may sit on different hosts.
+//
+// The device communicators move data with NVLink kernels and need every
+// rank on one NVSwitch domain.  The reference's only data path is the host
+// one (TCP or RoCE between hosts, reductions on the CPU; reference:
+// src/transport/tcp.cc, src/core/collectives.cc); this plane keeps that
+// capability for host tensors.  Its design is a full mesh of TCP streams
+// (one per rank pair) driven by one progress loop over all of them, and
+// every collective is a set of concurrent point-to-point transfers over the
+// mesh rather than a ring:
+//
+//  * all-gather, broadcast, gather, scatter, all-to-all(v): every rank
+//    sends its blocks to every destination at once (each stream carries
+//    exactly the bytes that must cross it);
+//  * reduce-scatter: every rank sends each owner its copy of the owner's
+//    block, and the owner reduces the n contributions in rank order;
+//  * all-reduce: reduce-scatter, then all-gather of the reduced blocks (or,
+//    below VCCL_HOST_AR_DIRECT bytes, every rank sends the whole message to
+//    every peer and reduces all n copies in rank order);
+//  * reduce: every rank sends to the root, which reduces in rank order;
+//  * a group of sends and receives runs in one progress loop.
+//
+// Every element is reduced by one rank, in rank order, with 16- and 8-bit
+// floats accumulated in fp32, so every rank ends with the same bits.
+// Large messages go in pieces (VCCL_HOST_CHUNK bytes per peer) so the
+// reduction buffers stay bounded.  Waits honour VCCL_TIMEOUT and
+// vcclCommAbort; a peer that closes its stream fails the call.
+#pragma once
+
+#include <atomic>
+#include <cstddef>
+#include <cstdint>
+#include <memory>
+#include <vector>
+
+#include "vccl.h"
+
+namespace vccl {
+
+class Bootstrap;
+
+// One transfer of a progress loop: `bytes` from `buf` to `peer` (send) or
+// from `peer` into `buf` (receive).  Transfers to (from) one peer leave
+// (arrive) in list order.
+struct HostXfer {
+  bool send;
+  int peer;
+  char* buf;
+  size_t bytes;
+};
+
+// Host-side reduction arguments of one call.
+struct HostRed {
+  vcclDataType_t dt;
+  int kind;      // sum / prod / max / min (the device RedKind values)
+  bool avg;      // divide the sum by the rank count (float types)
+  bool premul;   // every rank scales its own contribution by its `scalar` before sending
+  double scalar;
+};
+
+class HostPlane {
+ public:
+  // Collective: every rank of `bs` calls it; builds the mesh.
+  static vcclResult_t create(Bootstrap* bs, std::unique_ptr<HostPlane>* out);
+  ~HostPlane();
+
+  int rank() const { return rank_; }
+  int nranks() const { return n_; }
+
+  // Runs every transfer of `xs` to completion, all streams progressing at
+  // once.  Self transfers are not allowed (copy locally instead).
+  vcclResult_t run(const std::vector<HostXfer>& xs);
+
+  vcclResult_t allReduce(const char* send, char* recv, size_t count, const HostRed& r);
+  vcclResult_t reduceScatter(const char* send, char* recv, size_t recvCount, const HostRed& r);
+  vcclResult_t allGather(const char* send, char* recv, size_t bytes);
+  vcclResult_t broadcast(const char* send, char* recv, size_t bytes, int root);
+  vcclResult_t reduce(const char* send, char* recv, size_t count, const HostRed& r, int root);
+  vcclResult_t gather(const char* send, char* recv, size_t bytes, int root);
+  vcclResult_t scatter(const char* send, char* recv, size_t bytes, int root);
+  // Counts and displacements in bytes.
+  vcclResult_t allToAllv(const char* send, const size_t* sc, const size_t* sd, char* recv, const size_t* rc,
+                         const size_t* rd);
+
+  // Unblocks every wait (vcclCommAbort); later calls fail.
+  void abort();
+
+ private:
+  HostPlane(int rank, int n) : rank_(rank), n_(n) {}
+
+  int rank_;
+  int n_;
+  std::vector<int> fd_;  // stream to each peer ([rank_] = -1)
+  std::atomic<bool> aborted_{false};
+  size_t chunk_ = 8u << 20;      // per-peer piece of a reduction (VCCL_HOST_CHUNK)
+  size_t directMax_ = 64u << 10;  // all-reduce below this: whole message to every peer
+};
+
+// out = reduce over the contributions src[0..] in that order (count
+// elements each): fp32 accumulation for 16- and 8-bit floats, avg divides
+// by src.size() before the final rounding.  Pre-multiplication is applied
+// before the data leaves its rank (hostScale), not here.
+void hostReduce(char* out, const std::vector<const char*>& src, size_t count, const HostRed& r);
+// out = in * scalar, rounded to the element type (float types).
+void hostScale(char* out, const char* in, size_t count, vcclDataType_t dt, double scalar);
+
+}  // namespace vccl

@@ -147,9 +147,12 @@ int splitRank(int r, int n, const vcclUniqueId& id) {
     if (cnt != n - 1) return 6;
     vcclCommDestroy(s2);
   }
-  std::vector<float> x(4, 1.0f);
-  // Multi-rank data movement needs devices: must fail loudly, not hang.
-  if (vcclAllReduce(x.data(), x.data(), 4, vcclFloat32, vcclSum, c) != vcclInvalidUsage) return 7;
+  // Without a device, host buffers move over the host data plane (TCP mesh).
+  std::vector<float> x(4, 1.0f + r);
+  if (vcclAllReduce(x.data(), x.data(), 4, vcclFloat32, vcclSum, c) != vcclSuccess) return 7;
+  const float sum = n + n * (n - 1) / 2.0f;
+  for (float v : x)
+    if (v != sum) return 8;
   vcclCommDestroy(c);
   return 0;
 }

@@ -1,0 +1,306 @@
+# SPDX-License-Identifier: Apache-2.0
+"""Host data plane on the CPU: communicators without a device (VCCL_NO_DEVICE=1) and several
+ranks in separate processes move host tensors over the TCP mesh (csrc/runtime/hostplane.cc).
+
+The matrix follows the reference's collective suite (reference: tests/test_collectives.cc): every
+operation, counts 1 / 7 / 1024 / 65539 (and a large all-reduce split into pieces), sum / prod /
+max / min / avg / PreMulSum, integer and float types including bf16, fp16 and fp8, in place and
+out of place, every root; grouped send / receive rings; all-to-all(v) with uneven counts.  The
+oracle is computed on every rank from every rank's (deterministic) inputs, reducing in rank order
+with the same accumulation types, so results must match bit for bit; all-reduce outputs are also
+compared across ranks.  A rank that leaves early, and vcclCommAbort from another thread, end the
+peers' calls with an error instead of a hang.
+"""
+
+import multiprocessing as mp
+import os
+import threading
+import time
+
+import pytest
+import torch
+
+from conftest import free_port
+
+DTYPES = [torch.float32, torch.float64, torch.int32, torch.uint8, torch.int64, torch.float16, torch.bfloat16,
+          torch.float8_e4m3fn, torch.float8_e5m2]
+FLOATS = {torch.float32, torch.float64, torch.float16, torch.bfloat16, torch.float8_e4m3fn, torch.float8_e5m2}
+COUNTS = [1, 7, 1024, 65539]
+
+
+def _env(port):
+    os.environ.update(VCCL_NO_DEVICE="1", VCCL_SOCKET_ADDR="127.0.0.1", VCCL_COMM_ID=f"127.0.0.1:{port}",
+                      VCCL_DEBUG="ERROR", VCCL_TIMEOUT="30")
+
+
+def _acc(dt):
+    if dt in (torch.float16, torch.bfloat16, torch.float8_e4m3fn, torch.float8_e5m2):
+        return torch.float32
+    return dt
+
+
+def _input(rank, count, dt, seed):
+    """Small values: sums and products stay exact-ish and in range for every type."""
+    g = torch.Generator().manual_seed(seed * 131 + rank)
+    if dt in FLOATS:
+        v = torch.randint(-8, 9, (count,), generator=g).float() / 4.0
+        return v.to(dt)
+    if dt == torch.uint8:
+        return torch.randint(0, 4, (count,), generator=g).to(dt)
+    return torch.randint(-3, 4, (count,), generator=g).to(dt)
+
+
+def _oracle(xs, dt, op, n):
+    """Reduction in rank order in the accumulation type, rounded once to `dt`."""
+    acc_t = _acc(dt)
+    parts = [x.to(acc_t) for x in xs]
+    acc = parts[0].clone()
+    for p in parts[1:]:
+        if op in ("sum", "avg"):
+            acc = acc + p
+        elif op == "prod":
+            acc = acc * p
+        elif op == "max":
+            acc = torch.maximum(acc, p)
+        else:
+            acc = torch.minimum(acc, p)
+    if op == "avg":
+        acc = acc / torch.tensor(n, dtype=acc_t)
+    return acc.to(dt)
+
+
+def _same(a, b):
+    return torch.equal(a.view(torch.uint8) if a.element_size() == 1 else a, b.view(torch.uint8)
+                       if b.element_size() == 1 else b)
+
+
+def _matrix_body(rank, n, port, q):
+    try:
+        _env(port)
+        os.environ["VCCL_HOST_CHUNK"] = "4096"  # many pieces for the larger reductions
+        import vkccl_b200 as v
+
+        comm = v.Communicator(n, v.get_unique_id(), rank)
+        R = v.RedOp
+        seed = 0
+        for dt in DTYPES:
+            ops = ["sum", "prod", "max", "min"] + (["avg"] if dt in FLOATS else [])
+            if dt in (torch.float32, torch.float64, torch.float16, torch.bfloat16):
+                ops.append("premul")  # the op's scalar is given in the element type
+            for op in ops:
+                for count in COUNTS:
+                    seed += 1
+                    xs = [_input(r, count, dt, seed) for r in range(n)]
+                    scalar = 0.5 + 0.25 * rank if op == "premul" else None
+                    if op == "premul":
+                        # each rank's own scalar: build the oracle from every rank's scaled input
+                        acc_t = _acc(dt)
+                        scaled = [(x.to(acc_t) * torch.tensor(0.5 + 0.25 * r, dtype=acc_t)).to(dt)
+                                  for r, x in enumerate(xs)]
+                        want = _oracle(scaled, dt, "sum", n)
+                    else:
+                        want = _oracle(xs, dt, op, n)
+                    rop = {"sum": R.SUM, "prod": R.PROD, "max": R.MAX, "min": R.MIN, "avg": R.AVG}.get(op)
+                    handle = None
+                    if op == "premul":
+                        handle = comm.create_premul_sum(scalar, int(v.comm._NAME_TO_TYPE[str(dt).split(".")[1]]))
+                        rop = handle
+                    for inplace in (False, True):
+                        x = xs[rank].clone()
+                        if inplace:
+                            comm.all_reduce(x, op=rop)
+                            got = x
+                        else:
+                            got = torch.empty_like(x)
+                            comm.all_reduce(x, got, op=rop)
+                        assert _same(got, want), f"all_reduce {dt} {op} n={count} inplace={inplace}"
+                    if handle is not None:
+                        comm.destroy_op(handle)
+                    if count == 1024 and op in ("sum", "max"):
+                        # reduce to every root; reduce-scatter; every rank's all-reduce output agrees
+                        for root in range(n):
+                            out = torch.empty_like(xs[rank])
+                            comm.reduce(xs[rank].clone(), out, root, op=rop)
+                            if rank == root:
+                                assert _same(out, want), f"reduce {dt} {op} root={root}"
+                        per = count
+                        full = [_input(r, per * n, dt, seed + 1000) for r in range(n)]
+                        rs_want = _oracle(full, dt, op, n)[rank * per:(rank + 1) * per]
+                        rs_out = torch.empty(per, dtype=dt)
+                        comm.reduce_scatter(full[rank].clone(), rs_out, op=rop)
+                        assert _same(rs_out, rs_want), f"reduce_scatter {dt} {op}"
+                        mine = torch.empty_like(xs[rank])
+                        comm.all_reduce(xs[rank].clone(), mine, op=rop)
+                        everyone = torch.empty(count * n, dtype=dt)
+                        comm.all_gather(mine, everyone)
+                        for r in range(n):
+                            assert _same(everyone[r * count:(r + 1) * count], mine), "ranks disagree"
+        # large all-reduce: the reduce-scatter + all-gather form in many pieces
+        big = [_input(r, (1 << 20) + 3, torch.float32, 99) for r in range(n)]
+        out = torch.empty_like(big[rank])
+        comm.all_reduce(big[rank], out)
+        assert torch.equal(out, _oracle(big, torch.float32, "sum", n)), "large all_reduce"
+        # data movement: all-gather, broadcast, gather, scatter from every root
+        for count in COUNTS:
+            x = torch.arange(count, dtype=torch.int32) + 1000 * rank
+            g = torch.empty(count * n, dtype=torch.int32)
+            comm.all_gather(x, g)
+            assert torch.equal(g, torch.cat([torch.arange(count, dtype=torch.int32) + 1000 * r for r in range(n)]))
+            for root in range(n):
+                b = torch.arange(count, dtype=torch.float64) * (rank + 1)
+                comm.broadcast(b, root)
+                assert torch.equal(b, torch.arange(count, dtype=torch.float64) * (root + 1)), "broadcast"
+                gat = torch.full((count * n,), -1, dtype=torch.int32)
+                comm.gather(x, gat, root)
+                if rank == root:
+                    assert torch.equal(gat, g), "gather"
+                src = torch.arange(count * n, dtype=torch.int32) * (root + 1)
+                sc = torch.empty(count, dtype=torch.int32)
+                comm.scatter(src, sc, root)
+                assert torch.equal(sc, src[rank * count:(rank + 1) * count]), "scatter"
+        # all-to-all and all-to-all(v) with uneven counts (rank r sends r + p + 1 to p)
+        a = torch.arange(8 * n, dtype=torch.int64) + 100 * rank
+        b = torch.empty_like(a)
+        comm.all_to_all(a, b)
+        for p in range(n):
+            assert torch.equal(b[p * 8:(p + 1) * 8], torch.arange(8, dtype=torch.int64) + 8 * rank + 100 * p)
+        scn = [rank + p + 1 for p in range(n)]
+        sdp = [sum(scn[:p]) for p in range(n)]
+        rcn = [p + rank + 1 for p in range(n)]
+        rdp = [sum(rcn[:p]) for p in range(n)]
+        s = torch.arange(sum(scn), dtype=torch.int32) + 1000 * rank
+        r = torch.full((sum(rcn),), -1, dtype=torch.int32)
+        comm.all_to_all_v(s, scn, sdp, r, rcn, rdp)
+        for p in range(n):
+            # rank p sent me its block [sdp_p[rank], +scn_p[rank]) of arange + 1000 p
+            p_sc = [p + k + 1 for k in range(n)]
+            p_sd = sum(p_sc[:rank])
+            assert torch.equal(r[rdp[p]:rdp[p] + rcn[p]],
+                               torch.arange(p_sd, p_sd + p_sc[rank], dtype=torch.int32) + 1000 * p), "all_to_all_v"
+        # grouped ring: send to the next rank, receive from the previous, in one group
+        for count in (1, 4099, 300000):
+            out = torch.arange(count, dtype=torch.float32) + rank
+            inc = torch.empty(count, dtype=torch.float32)
+            with v.group():
+                comm.send(out, (rank + 1) % n)
+                comm.recv(inc, (rank - 1) % n)
+            assert torch.equal(inc, torch.arange(count, dtype=torch.float32) + (rank - 1) % n), "ring"
+        # two messages to the same peer arrive in order
+        if n >= 2 and rank < 2:
+            peer = 1 - rank
+            m1, m2 = torch.full((5,), 10 + rank), torch.full((7,), 20 + rank)
+            r1, r2 = torch.empty(5, dtype=m1.dtype), torch.empty(7, dtype=m2.dtype)
+            with v.group():
+                comm.send(m1, peer)
+                comm.send(m2, peer)
+                comm.recv(r1, peer)
+                comm.recv(r2, peer)
+            assert torch.all(r1 == 10 + peer) and torch.all(r2 == 20 + peer), "ordered p2p"
+        prof = {(e["op"], e["algo"]) for e in comm.prof_summary()}
+        assert comm.async_error() == 0
+        comm.destroy()
+        q.put((rank, "ok", sorted(prof)))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, traceback.format_exc(), None))
+
+
+def _run(body, n, timeout=600):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=body, args=(r, n, port, q)) for r in range(n)]
+    for p in ps:
+        p.start()
+    res = {}
+    try:
+        for _ in range(n):
+            r, status, extra = q.get(timeout=timeout)
+            res[r] = (status, extra)
+    finally:
+        for p in ps:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    return res
+
+
+@pytest.mark.parametrize("n", [2, 3, 4])
+def test_host_plane_matrix(n):
+    res = _run(_matrix_body, n)
+    bad = {r: s for r, (s, _) in res.items() if s != "ok"}
+    assert not bad, bad
+
+
+def _dead_peer_body(rank, n, port, q):
+    try:
+        _env(port)
+        os.environ["VCCL_TIMEOUT"] = "20"
+        import vkccl_b200 as v
+
+        comm = v.Communicator(n, v.get_unique_id(), rank)
+        x = torch.ones(1000)
+        comm.all_reduce(x)  # the mesh exists and works
+        if rank == 1:
+            os._exit(0)  # leaves between steps, with nothing in flight
+        t0 = time.time()
+        try:
+            comm.all_reduce(torch.ones(1 << 16))
+            q.put((rank, "no error", None))
+        except v.VcclError:
+            q.put((rank, "ok", round(time.time() - t0, 2)))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, traceback.format_exc(), None))
+
+
+def test_host_plane_dead_peer():
+    """A rank that exits ends its peers' next collective with an error (its streams close)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    n = 3
+    port = free_port()
+    ps = [ctx.Process(target=_dead_peer_body, args=(r, n, port, q)) for r in range(n)]
+    for p in ps:
+        p.start()
+    res = {}
+    for _ in range(n - 1):
+        r, status, extra = q.get(timeout=120)
+        res[r] = (status, extra)
+    for p in ps:
+        p.join(timeout=30)
+    assert set(res) == {0, 2} and all(s == "ok" for s, _ in res.values()), res
+    assert all(t < 15 for _, t in res.values()), res
+
+
+def _abort_body(rank, n, port, q):
+    try:
+        _env(port)
+        import vkccl_b200 as v
+
+        comm = v.Communicator(n, v.get_unique_id(), rank)
+        comm.all_reduce(torch.ones(10))
+        if rank == 0:
+            # rank 1 never joins this call; abort from another thread unblocks it
+            threading.Timer(0.5, comm.abort).start()
+            t0 = time.time()
+            try:
+                comm.all_reduce(torch.ones(1 << 16))
+                q.put((rank, "no error", None))
+            except v.VcclError:
+                q.put((rank, "ok", round(time.time() - t0, 2)))
+        else:
+            time.sleep(3)
+            q.put((rank, "ok", None))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, traceback.format_exc(), None))
+
+
+def test_host_plane_abort_unblocks():
+    res = _run(_abort_body, 2, timeout=120)
+    assert all(s == "ok" for s, _ in res.values()), res
+    assert res[0][1] < 10, res

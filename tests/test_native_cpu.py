@@ -124,9 +124,12 @@ def _run_dmabuf(args, extra_env):
 
 
 def test_dmabuf_registration_control_plane():
-    """vcclCommRegisterDmaBuf's CPU-mapping route on a control-plane-only rank: a memfd, and a real
-    dmabuf from /dev/udmabuf where the kernel has it (reference: tests/test_dmabuf.cc)."""
-    p = _run_dmabuf(["1", "memfd"], {"VCCL_NO_DEVICE": "1"})
-    assert p.returncode == 0 and "dmabuf (memfd, 1 ranks): OK" in p.stdout, p.stdout + p.stderr
-    p = _run_dmabuf(["1", "udmabuf"], {"VCCL_NO_DEVICE": "1"})
-    assert p.returncode in (0, 77), p.stdout + p.stderr
+    """vcclCommRegisterDmaBuf's CPU-mapping route on 1 to 3 device-less forked ranks: a memfd, and a
+    real dmabuf from /dev/udmabuf where the kernel has it, all-reduced and all-gathered in place
+    (reference: tests/test_dmabuf.cc)."""
+    for n in (1, 2, 3):
+        # several device-less ranks move the mappings' bytes over the host data plane
+        p = _run_dmabuf([str(n), "memfd"], {"VCCL_NO_DEVICE": "1"})
+        assert p.returncode == 0 and f"dmabuf (memfd, {n} ranks): OK" in p.stdout, p.stdout + p.stderr
+        p = _run_dmabuf([str(n), "udmabuf"], {"VCCL_NO_DEVICE": "1"})
+        assert p.returncode in (0, 77), p.stdout + p.stderr
