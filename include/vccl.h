@@ -108,9 +108,12 @@ vcclResult_t vcclGetVersion(int* version);
 vcclResult_t vcclGetUniqueId(vcclUniqueId* uniqueId);
 
 /* Collectively create a communicator.  Rank r binds to the current CUDA
- * device of the calling thread (cudaSetDevice before the call).  Without a
- * visible CUDA device the communicator is control-plane only: lifecycle,
- * split, ops and groups work; data-moving calls return vcclInvalidUsage. */
+ * device of the calling thread (cudaSetDevice before the call); every rank
+ * of a device communicator must sit in one NVSwitch domain.  Without a
+ * visible CUDA device (or with VCCL_NO_DEVICE=1) the communicator moves host
+ * buffers: the blocking collectives and send/recv run over a TCP mesh
+ * between the ranks, which may sit on different hosts, with the reductions
+ * on the CPU; the stream-ordered (*Async) calls return vcclInvalidUsage. */
 vcclResult_t vcclCommInitRank(vcclComm_t* comm, int nranks,
                               vcclUniqueId commId, int rank);
 vcclResult_t vcclCommInitRankConfig(vcclComm_t* comm, int nranks,
