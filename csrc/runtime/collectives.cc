@@ -22,6 +22,7 @@
 #include "common/log.h"
 #include "common/trace.h"
 #include "runtime/comm.h"
+#include "runtime/cudrv.h"
 #include "runtime/launch.h"
 
 namespace vccl {
@@ -742,6 +743,9 @@ vcclResult_t launchHostOps(vcclComm_t comm, std::vector<HostOp>& ops) {
       VERR("a communicator without a device takes host buffers through the blocking calls only");
       return vcclInvalidUsage;
     }
+    // Without a CUDA driver every pointer is host memory; with one (a GPU
+    // host running VCCL_NO_DEVICE=1), device pointers are refused.
+    if (driverApi() == nullptr) continue;
     for (const char* p : {static_cast<const char*>(h.send), static_cast<const char*>(h.recv)}) {
       if (p != nullptr && classify(p, -1) != PtrKind::Host) {
         VERR("a communicator without a device moves host memory only; got a device pointer");

@@ -10,7 +10,10 @@
 #include <poll.h>
 #include <sys/socket.h>
 
+#include <sched.h>
+
 #include <algorithm>
+#include <chrono>
 #include <cstring>
 #include <deque>
 
@@ -60,13 +63,30 @@ struct Elem<__nv_fp8_e5m2> {
   static __nv_fp8_e5m2 out(A v) { return __nv_fp8_e5m2(v); }
 };
 
-template <typename A>
-inline A combine(int kind, A a, A b) {
+// acc[i] = acc[i] (op) x[i] over a block, one operation per loop so the
+// compiler vectorises it.
+template <typename S, typename A>
+void foldBlock(A* acc, const S* x, size_t m, int kind) {
+  using E = Elem<S>;
   switch (kind) {
-    case dev::kProd: return a * b;
-    case dev::kMax: return a < b ? b : a;
-    case dev::kMin: return b < a ? b : a;
-    default: return a + b;
+    case dev::kProd:
+      for (size_t i = 0; i < m; i++) acc[i] = static_cast<A>(acc[i] * E::in(x[i]));
+      break;
+    case dev::kMax:
+      for (size_t i = 0; i < m; i++) {
+        const A v = E::in(x[i]);
+        acc[i] = acc[i] < v ? v : acc[i];
+      }
+      break;
+    case dev::kMin:
+      for (size_t i = 0; i < m; i++) {
+        const A v = E::in(x[i]);
+        acc[i] = v < acc[i] ? v : acc[i];
+      }
+      break;
+    default:
+      for (size_t i = 0; i < m; i++) acc[i] = static_cast<A>(acc[i] + E::in(x[i]));
+      break;
   }
 }
 
@@ -76,13 +96,19 @@ void reduceT(char* out, const std::vector<const char*>& src, size_t count, const
   using A = typename E::A;
   const size_t n = src.size();
   S* o = reinterpret_cast<S*>(out);
-  for (size_t i = 0; i < count; i++) {
-    // Read every contribution of element i before writing it: the output
-    // may be one of the contributions (in-place calls).
-    A acc = E::in(reinterpret_cast<const S*>(src[0])[i]);
-    for (size_t p = 1; p < n; p++) acc = combine<A>(r.kind, acc, E::in(reinterpret_cast<const S*>(src[p])[i]));
-    if (r.avg) acc = static_cast<A>(acc / static_cast<A>(n));
-    o[i] = E::out(acc);
+  // Block by block: every contribution of a block is read into the
+  // accumulator before the block is written (the output may be one of the
+  // contributions, in place); per element the order is rank order.
+  constexpr size_t kBlock = 2048;
+  A acc[kBlock];
+  for (size_t b = 0; b < count; b += kBlock) {
+    const size_t m = count - b < kBlock ? count - b : kBlock;
+    const S* s0 = reinterpret_cast<const S*>(src[0]) + b;
+    for (size_t i = 0; i < m; i++) acc[i] = E::in(s0[i]);
+    for (size_t p = 1; p < n; p++) foldBlock<S, A>(acc, reinterpret_cast<const S*>(src[p]) + b, m, r.kind);
+    if (r.avg)
+      for (size_t i = 0; i < m; i++) acc[i] = static_cast<A>(acc[i] / static_cast<A>(n));
+    for (size_t i = 0; i < m; i++) o[b + i] = E::out(acc[i]);
   }
 }
 
@@ -148,7 +174,8 @@ vcclResult_t HostPlane::create(Bootstrap* bs, std::unique_ptr<HostPlane>* out) {
   hp->fd_.assign(n, -1);
   hp->chunk_ = envBytes("VCCL_HOST_CHUNK", 8u << 20);
   if (hp->chunk_ < 4096) hp->chunk_ = 4096;
-  hp->directMax_ = envBytes("VCCL_HOST_AR_DIRECT", 64u << 10);
+  hp->directMax_ = envBytes("VCCL_HOST_AR_DIRECT", 32u << 10);
+  hp->spinUs_ = static_cast<int>(envLong("VCCL_HOST_SPIN_US", 50));
   // Every rank listens, then the ranks exchange endpoints: a rank connects to
   // every higher rank (connections complete into the peer's backlog, so the
   // order cannot deadlock) and accepts every lower one.
@@ -236,6 +263,8 @@ vcclResult_t HostPlane::run(const std::vector<HostXfer>& xs) {
   Deadline dl;
   std::vector<pollfd> pfd;
   std::vector<int> who;
+  const auto spin = std::chrono::microseconds(spinUs_);
+  auto idleSince = std::chrono::steady_clock::now();
   while (pending > 0) {
     if (aborted_.load()) {
       VERR("host data plane: communicator aborted");
@@ -286,8 +315,18 @@ vcclResult_t HostPlane::run(const std::vector<HostXfer>& xs) {
         return vcclSystemError;
       }
     }
-    if (pending == 0 || moved) continue;
-    // Nothing moved: wait until some stream can.
+    if (pending == 0) continue;
+    if (moved) {
+      idleSince = std::chrono::steady_clock::now();
+      continue;
+    }
+    // Nothing moved: keep trying for a short while (an answer is often
+    // microseconds away, and a sleep in poll() costs a wake-up), then wait
+    // until some stream can move.
+    if (std::chrono::steady_clock::now() - idleSince < spin) {
+      sched_yield();
+      continue;
+    }
     pfd.clear();
     who.clear();
     for (int p = 0; p < n_; p++) {

@@ -9,7 +9,10 @@
 // measured with CUDA events on the launching stream and reported as the
 // maximum over ranks, --algo forces an all-reduce algorithm, --graph times a
 // captured loop, and --window puts both buffers in registered windows
-// (vcclMemAlloc + vcclCommWindowRegister: the zero-copy kernels).
+// (vcclMemAlloc + vcclCommWindowRegister: the zero-copy kernels).  --host
+// (also taken without a GPU or with VCCL_NO_DEVICE=1) runs communicators
+// without a device on host buffers over the host data plane, timed by the
+// host clock like the reference's bench (maximum over ranks).
 // Multi-process launch: VCCL_RANK / VCCL_NRANKS and VCCL_COMM_ID or
 // VCCL_ID_FILE, as in the reference.
 #include <cuda_runtime.h>
@@ -37,6 +40,7 @@ struct Opts {
   bool check = false;
   bool graph = false;
   bool window = false;
+  bool host = false;
   vcclDataType_t dt = vcclFloat32;
   std::string algo;
 };
@@ -61,7 +65,7 @@ double busFactor(const std::string& op, int n) {
                "usage: vccl-bench [--launch N] [--op allreduce|allgather|reducescatter|broadcast|alltoall]\n"
                "                  [-b min] [-e max] [-f factor] [--iters N] [--warmup N]\n"
                "                  [--dtype f32|f16|bf16|f64] [--algo ll|twoshot|nvls|nvls_pipe] [--check]\n"
-               "                  [--graph] [--window]\n");
+               "                  [--graph] [--window] [--host]\n");
   std::exit(2);
 }
 
@@ -71,16 +75,29 @@ __global__ void fillPattern(float* p, size_t n, int rank) {
     p[i] = static_cast<float>((rank + i) % 8);
 }
 
-int checkF32(const Opts& o, vcclComm_t c, int rank, int n, float* s, float* r, size_t bytes) {
+// Copies results back for the checks (host buffers: a plain copy).
+void fetch(bool host, float* dst, const float* src, size_t cnt) {
+  if (host) {
+    std::memcpy(dst, src, cnt * 4);
+  } else {
+    cudaMemcpy(dst, src, cnt * 4, cudaMemcpyDeviceToHost);
+  }
+}
+
+int checkF32(const Opts& o, vcclComm_t c, int rank, int n, float* s, float* r, size_t bytes, bool host) {
   const size_t cnt = bytes / 4, per = cnt / n;
-  fillPattern<<<256, 256>>>(s, cnt, rank);
-  cudaDeviceSynchronize();
+  if (host) {
+    for (size_t i = 0; i < cnt; i++) s[i] = static_cast<float>((rank + i) % 8);
+  } else {
+    fillPattern<<<256, 256>>>(s, cnt, rank);
+    cudaDeviceSynchronize();
+  }
   std::vector<float> h;
   size_t bad = 0;
   if (o.op == "allreduce") {
     vcclAllReduce(s, r, cnt, vcclFloat32, vcclSum, c);
     h.resize(cnt);
-    cudaMemcpy(h.data(), r, cnt * 4, cudaMemcpyDeviceToHost);
+    fetch(host, h.data(), r, cnt);
     for (size_t i = 0; i < cnt; i++) {
       float w = 0;
       for (int p = 0; p < n; p++) w += static_cast<float>((p + i) % 8);
@@ -89,14 +106,14 @@ int checkF32(const Opts& o, vcclComm_t c, int rank, int n, float* s, float* r, s
   } else if (o.op == "allgather") {
     vcclAllGather(s, r, per, vcclFloat32, c);
     h.resize(per * n);
-    cudaMemcpy(h.data(), r, per * n * 4, cudaMemcpyDeviceToHost);
+    fetch(host, h.data(), r, per * n);
     for (int p = 0; p < n; p++)
       for (size_t i = 0; i < per; i++)
         if (h[p * per + i] != static_cast<float>((p + i) % 8)) bad++;
   } else if (o.op == "reducescatter") {
     vcclReduceScatter(s, r, per, vcclFloat32, vcclSum, c);
     h.resize(per);
-    cudaMemcpy(h.data(), r, per * 4, cudaMemcpyDeviceToHost);
+    fetch(host, h.data(), r, per);
     for (size_t i = 0; i < per; i++) {
       float w = 0;
       for (int p = 0; p < n; p++) w += static_cast<float>((p + rank * per + i) % 8);
@@ -113,13 +130,67 @@ int checkF32(const Opts& o, vcclComm_t c, int rank, int n, float* s, float* r, s
   return 0;
 }
 
+// The sweep on host buffers (communicator without a device), host clock.
+int runHostRank(const Opts& o, int rank, int n, const vcclUniqueId& id) {
+  setenv("VCCL_NO_DEVICE", "1", 1);
+  vcclComm_t c = nullptr;
+  if (vcclCommInitRank(&c, n, id, rank) != vcclSuccess) {
+    std::fprintf(stderr, "rank %d: init failed: %s\n", rank, vcclGetLastError(nullptr));
+    return 1;
+  }
+  const size_t es = vcclTypeSize(o.dt);
+  const size_t cap = o.maxBytes + 4096;
+  std::vector<float> sv(cap / 4 + 1, 0.0f), rv(cap / 4 + 1, 0.0f);
+  char* s = reinterpret_cast<char*>(sv.data());
+  char* r = reinterpret_cast<char*>(rv.data());
+  if (o.check && checkF32(o, c, rank, n, sv.data(), rv.data(), o.maxBytes, true)) return 1;
+  if (rank == 0) {
+    std::printf("# op=%s dtype_bytes=%zu nranks=%d iters=%d warmup=%d (host buffers, host data plane; "
+                "host clock, max over ranks)\n",
+                o.op.c_str(), es, n, o.iters, o.warmup);
+    std::printf("%14s %12s %12s %12s\n", "bytes", "time(us)", "algbw(GB/s)", "busbw(GB/s)");
+  }
+  for (size_t bytes = o.minBytes; bytes <= o.maxBytes;
+       bytes = std::max(bytes + 1, static_cast<size_t>(bytes * o.factor))) {
+    const size_t cnt = bytes / es, per = cnt / n;
+    if (cnt == 0) continue;
+    if ((o.op == "allgather" || o.op == "reducescatter" || o.op == "alltoall") && per == 0) continue;
+    auto once = [&]() -> vcclResult_t {
+      if (o.op == "allreduce") return vcclAllReduce(s, r, cnt, o.dt, vcclSum, c);
+      if (o.op == "allgather") return vcclAllGather(s, r, per, o.dt, c);
+      if (o.op == "reducescatter") return vcclReduceScatter(s, r, per, o.dt, vcclSum, c);
+      if (o.op == "broadcast") return vcclBroadcast(s, r, cnt, o.dt, 0, c);
+      if (o.op == "alltoall") return vcclAllToAll(s, r, per, o.dt, c);
+      return vcclInvalidArgument;
+    };
+    for (int i = 0; i < o.warmup; i++)
+      if (once() != vcclSuccess) return 1;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (int i = 0; i < o.iters; i++)
+      if (once() != vcclSuccess) return 1;
+    float us = std::chrono::duration<float, std::micro>(std::chrono::steady_clock::now() - t0).count() / o.iters;
+    if (vcclAllReduce(&us, &us, 1, vcclFloat32, vcclMax, c) != vcclSuccess) return 1;
+    if (rank == 0) {
+      const double eff = (o.op == "allgather" || o.op == "reducescatter" || o.op == "alltoall")
+                             ? static_cast<double>(per * n * es)
+                             : static_cast<double>(cnt * es);
+      const double algbw = eff / (us * 1e3);
+      std::printf("%14zu %12.2f %12.2f %12.2f\n", static_cast<size_t>(eff), us, algbw, algbw * busFactor(o.op, n));
+    }
+  }
+  vcclCommDestroy(c);
+  return 0;
+}
+
 int runRank(const Opts& o, int rank, int n, const vcclUniqueId& id) {
   setvbuf(stdout, nullptr, _IOLBF, 0);
+  const char* nd = std::getenv("VCCL_NO_DEVICE");
+  if (o.host || (nd && std::atoi(nd) != 0)) return runHostRank(o, rank, n, id);
   int ngpu = 0;
-  cudaGetDeviceCount(&ngpu);
-  if (ngpu < 1) {
-    std::fprintf(stderr, "no CUDA device\n");
-    return 1;
+  if (cudaGetDeviceCount(&ngpu) != cudaSuccess || ngpu < 1) {
+    cudaGetLastError();
+    if (rank == 0) std::printf("# no CUDA device: host buffers over the host data plane\n");
+    return runHostRank(o, rank, n, id);
   }
   cudaSetDevice(rank % ngpu);
   if (!o.algo.empty()) setenv("VCCL_ALLREDUCE_ALGO", o.algo.c_str(), 1);
@@ -145,7 +216,7 @@ int runRank(const Opts& o, int rank, int n, const vcclUniqueId& id) {
     cudaMalloc(&r, cap);
   }
   cudaMemset(s, 0, cap);
-  if (o.check && checkF32(o, c, rank, n, static_cast<float*>(s), static_cast<float*>(r), o.maxBytes)) return 1;
+  if (o.check && checkF32(o, c, rank, n, static_cast<float*>(s), static_cast<float*>(r), o.maxBytes, false)) return 1;
   cudaStream_t st;
   cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
   cudaEvent_t e0, e1;
@@ -285,6 +356,7 @@ int main(int argc, char** argv) {
     else if (a == "--check") o.check = true;
     else if (a == "--graph") o.graph = true;
     else if (a == "--window") o.window = true;
+    else if (a == "--host") o.host = true;
     else if (a == "--algo") o.algo = next();
     else if (a == "--dtype") {
       std::string d = next();
