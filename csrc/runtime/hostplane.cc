@@ -176,6 +176,8 @@ vcclResult_t HostPlane::create(Bootstrap* bs, std::unique_ptr<HostPlane>* out) {
   if (hp->chunk_ < 4096) hp->chunk_ = 4096;
   hp->directMax_ = envBytes("VCCL_HOST_AR_DIRECT", 32u << 10);
   hp->spinUs_ = static_cast<int>(envLong("VCCL_HOST_SPIN_US", 50));
+  hp->bcastDirect_ = envBytes("VCCL_HOST_BCAST_DIRECT", 16u << 10);
+  hp->bcastPiece_ = envBytes("VCCL_HOST_BCAST_PIECE", 1u << 20);
   // Every rank listens, then the ranks exchange endpoints: a rank connects to
   // every higher rank (connections complete into the peer's backlog, so the
   // order cannot deadlock) and accepts every lower one.
@@ -376,15 +378,60 @@ vcclResult_t HostPlane::allGather(const char* send, char* recv, size_t bytes) {
 
 vcclResult_t HostPlane::broadcast(const char* send, char* recv, size_t bytes, int root) {
   if (bytes == 0) return vcclSuccess;
-  std::vector<HostXfer> xs;
-  if (rank_ == root) {
-    if (recv != send) memmove(recv, send, bytes);
-    for (int p = 0; p < n_; p++)
-      if (p != root) xs.push_back({true, p, recv, bytes});
-  } else {
-    xs.push_back({false, root, recv, bytes});
+  const int m = n_ - 1;  // ranks that receive
+  if (rank_ == root && recv != send) memmove(recv, send, bytes);
+  if (bytes <= bcastDirect_ || m < 2) {
+    // Small: the root sends the whole message to every rank.
+    std::vector<HostXfer> xs;
+    if (rank_ == root) {
+      for (int p = 0; p < n_; p++)
+        if (p != root) xs.push_back({true, p, recv, bytes});
+    } else {
+      xs.push_back({false, root, recv, bytes});
+    }
+    return run(xs);
   }
-  return run(xs);
+  // Large: in pieces, the root hands receiver j the j-th block of each piece
+  // (it sends every byte once), and the receivers exchange their blocks
+  // among themselves; while they exchange one piece, the root's next piece
+  // is already on its way into their sockets.
+  const size_t piece = std::max<size_t>(bcastPiece_, 4096) * m;
+  auto block = [&](size_t off, size_t len, int j, size_t* bo, size_t* bl) {
+    const size_t b = ceilDiv(len, m);
+    const size_t lo = std::min(len, static_cast<size_t>(j) * b), hi = std::min(len, static_cast<size_t>(j + 1) * b);
+    *bo = off + lo;
+    *bl = hi - lo;
+  };
+  auto receiver = [&](int j) { return (root + 1 + j) % n_; };
+  if (rank_ == root) {
+    std::vector<HostXfer> xs;
+    for (size_t off = 0; off < bytes; off += piece) {
+      const size_t len = std::min(piece, bytes - off);
+      for (int j = 0; j < m; j++) {
+        size_t bo = 0, bl = 0;
+        block(off, len, j, &bo, &bl);
+        xs.push_back({true, receiver(j), recv + bo, bl});
+      }
+    }
+    return run(xs);
+  }
+  const int me = (rank_ - root - 1 + n_) % n_;
+  for (size_t off = 0; off < bytes; off += piece) {
+    const size_t len = std::min(piece, bytes - off);
+    size_t mo = 0, ml = 0;
+    block(off, len, me, &mo, &ml);
+    VTRY(run({{false, root, recv + mo, ml}}));
+    std::vector<HostXfer> xs;
+    for (int j = 0; j < m; j++) {
+      if (j == me) continue;
+      size_t bo = 0, bl = 0;
+      block(off, len, j, &bo, &bl);
+      xs.push_back({true, receiver(j), recv + mo, ml});
+      xs.push_back({false, receiver(j), recv + bo, bl});
+    }
+    VTRY(run(xs));
+  }
+  return vcclSuccess;
 }
 
 vcclResult_t HostPlane::gather(const char* send, char* recv, size_t bytes, int root) {

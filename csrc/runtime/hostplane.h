@@ -12,9 +12,12 @@
 // every collective is a set of concurrent point-to-point transfers over the
 // mesh rather than a ring:
 //
-//  * all-gather, broadcast, gather, scatter, all-to-all(v): every rank
-//    sends its blocks to every destination at once (each stream carries
-//    exactly the bytes that must cross it);
+//  * all-gather, gather, scatter, all-to-all(v): every rank sends its
+//    blocks to every destination at once (each stream carries exactly the
+//    bytes that must cross it);
+//  * broadcast: small messages go from the root to every rank; large ones
+//    in pieces, the root handing each receiver one block of a piece (every
+//    byte leaves the root once) and the receivers exchanging their blocks;
 //  * reduce-scatter: every rank sends each owner its copy of the owner's
 //    block, and the owner reduces the n contributions in rank order;
 //  * all-reduce: reduce-scatter, then all-gather of the reduced blocks (or,
@@ -98,6 +101,8 @@ class HostPlane {
   size_t chunk_ = 8u << 20;      // per-peer piece of a reduction (VCCL_HOST_CHUNK)
   size_t directMax_ = 32u << 10;  // all-reduce below this: whole message to every peer
   int spinUs_ = 50;               // retry without sleeping this long before poll() (VCCL_HOST_SPIN_US)
+  size_t bcastDirect_ = 16u << 10;  // broadcast up to this: root to every rank (VCCL_HOST_BCAST_DIRECT)
+  size_t bcastPiece_ = 1u << 20;    // ... above: per-receiver block of one piece (VCCL_HOST_BCAST_PIECE)
 };
 
 // out = reduce over the contributions src[0..] in that order (count

@@ -78,6 +78,7 @@ def _matrix_body(rank, n, port, q):
     try:
         _env(port)
         os.environ["VCCL_HOST_CHUNK"] = "4096"  # many pieces for the larger reductions
+        os.environ["VCCL_HOST_BCAST_PIECE"] = "8192"  # ... and broadcasts
         import vkccl_b200 as v
 
         comm = v.Communicator(n, v.get_unique_id(), rank)
