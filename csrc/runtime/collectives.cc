@@ -16,6 +16,7 @@
 #include <cstring>
 #include <functional>
 #include <map>
+#include <thread>
 #include <vector>
 
 #include "common/env.h"
@@ -1083,11 +1084,31 @@ vcclResult_t vcclGroupEnd(void) {
   // other), then wait.
   std::vector<PendingSync> waits;
   vcclResult_t first = vcclSuccess;
+  // Communicators without a device run their calls on the host, blocking
+  // until the peers take part: when one group holds several of them (ranks
+  // of one process, vcclCommInitAll), each runs on its own thread so they
+  // can meet.
+  std::vector<vcclComm_t> hostComms;
+  for (vcclComm_t c : order)
+    if (!c->dev && c->nranks > 1) hostComms.push_back(c);
+  std::vector<vcclResult_t> hostRes(hostComms.size(), vcclSuccess);
+  std::vector<std::thread> hostThreads;
+  if (hostComms.size() > 1)
+    for (size_t i = 0; i < hostComms.size(); i++)
+      hostThreads.emplace_back([&, i] { hostRes[i] = launchOps(hostComms[i], byComm[hostComms[i]], nullptr); });
   for (vcclComm_t c : order) {
+    if (hostComms.size() > 1 && !c->dev && c->nranks > 1) continue;
     vcclResult_t r = launchOps(c, byComm[c], &waits);
     if (r != vcclSuccess) {
       c->noteError(r);
       if (first == vcclSuccess) first = r;
+    }
+  }
+  for (size_t i = 0; i < hostThreads.size(); i++) {
+    hostThreads[i].join();
+    if (hostRes[i] != vcclSuccess) {
+      hostComms[i]->noteError(hostRes[i]);
+      if (first == vcclSuccess) first = hostRes[i];
     }
   }
   vcclResult_t w = waitAll(waits);

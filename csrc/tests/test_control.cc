@@ -183,8 +183,35 @@ void initAll() {
     vcclCommUserRank(c[i], &r);
     vcclCommCount(c[i], &n);
     EXPECT(r == i && n == 3, "InitAll comm %d: %d/%d", i, r, n);
-    vcclCommDestroy(c[i]);
   }
+  // One thread drives all three ranks inside a group: the host data plane
+  // runs each communicator's calls on its own thread so the ranks meet.
+  if (c[0] && c[1] && c[2]) {
+    std::vector<std::vector<double>> x(3, std::vector<double>(5000));
+    std::vector<std::vector<int32_t>> g(3, std::vector<int32_t>(3 * 7));
+    std::vector<int32_t> mine[3];
+    for (int i = 0; i < 3; i++) {
+      for (size_t k = 0; k < x[i].size(); k++) x[i][k] = i + 0.5 * k;
+      mine[i].assign(7, 100 * i);
+    }
+    vcclGroupStart();
+    for (int i = 0; i < 3; i++) {
+      vcclAllReduce(x[i].data(), x[i].data(), x[i].size(), vcclFloat64, vcclSum, c[i]);
+      vcclAllGather(mine[i].data(), g[i].data(), 7, vcclInt32, c[i]);
+    }
+    EXPECT(vcclGroupEnd() == vcclSuccess, "InitAll group of host collectives");
+    for (int i = 0; i < 3; i++) {
+      for (size_t k = 0; k < x[i].size(); k++)
+        if (x[i][k] != 3 + 1.5 * k) {
+          EXPECT(false, "InitAll all-reduce rank %d [%zu] = %g", i, k, x[i][k]);
+          break;
+        }
+      for (int p = 0; p < 3; p++)
+        EXPECT(g[i][p * 7] == 100 * p && g[i][p * 7 + 6] == 100 * p, "InitAll all-gather rank %d block %d", i, p);
+    }
+  }
+  for (int i = 0; i < 3; i++)
+    if (c[i]) vcclCommDestroy(c[i]);
 }
 
 // Failure detection on the host: a missing rank must not hang the others.
