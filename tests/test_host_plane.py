@@ -305,3 +305,47 @@ def test_host_plane_abort_unblocks():
     res = _run(_abort_body, 2, timeout=120)
     assert all(s == "ok" for s, _ in res.values()), res
     assert res[0][1] < 10, res
+
+
+def _vllm_comm_body(rank, n, port, q):
+    """The reference's end-to-end TP layer (reference: python/tests/test_e2e_tp.py:60-92) through
+    this library's VcclCommunicator on a CPU process group with CPU tensors."""
+    try:
+        _env(port)
+        import torch.distributed as dist
+
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port + 1), GLOO_SOCKET_IFNAME="lo")
+        dist.init_process_group("gloo", rank=rank, world_size=n)
+        from vkccl_b200.torch_comm import VcclCommunicator
+
+        comm = VcclCommunicator(dist.group.WORLD, device=torch.device("cpu"))
+        T, H, I = 64, 32, 48
+        g = torch.Generator().manual_seed(7)
+        x = torch.randn(T, H, generator=g)
+        wg, wu = torch.randn(I, H, generator=g) * 0.1, torch.randn(I, H, generator=g) * 0.1
+        wd = torch.randn(H, I, generator=g) * 0.1
+        shard, ish = T // n, I // n
+        xs = x[rank * shard:(rank + 1) * shard]
+        # column-parallel gate/up, row-parallel down, sequence-parallel activations
+        xf = comm.all_gather(xs, dim=0)
+        h = torch.nn.functional.silu(xf @ wg[rank * ish:(rank + 1) * ish].T) * (xf @ wu[rank * ish:(rank + 1) * ish].T)
+        y = comm.reduce_scatter(h @ wd[:, rank * ish:(rank + 1) * ish].T, dim=0)
+        ref = (torch.nn.functional.silu(x @ wg.T) * (x @ wu.T)) @ wd.T
+        torch.testing.assert_close(y, ref[rank * shard:(rank + 1) * shard], rtol=1e-4, atol=1e-5)
+        a = torch.full((5,), float(rank + 1))
+        assert torch.equal(comm.all_reduce(a.clone()), torch.full((5,), float(n * (n + 1) // 2)))
+        b = torch.arange(6, dtype=torch.float32) * (rank + 1)
+        assert torch.equal(comm.broadcast(b.clone(), src=n - 1), torch.arange(6, dtype=torch.float32) * n)
+        comm.destroy()
+        dist.destroy_process_group()
+        q.put((rank, "ok", None))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, traceback.format_exc(), None))
+
+
+@pytest.mark.parametrize("n", [2, 3])
+def test_vllm_communicator_on_host_plane(n):
+    res = _run(_vllm_comm_body, n, timeout=300)
+    assert all(s == "ok" for s, _ in res.values()), res
