@@ -212,14 +212,17 @@ vcclResult_t initRank(vcclComm_t* out, int nranks, const vcclUniqueId& id, int r
   int withDev = 0;
   for (const DeviceIdentity& d : ids) withDev += d.present ? 1 : 0;
   if (withDev != 0 && withDev != nranks) {
-    VERR("some ranks have a CUDA device and some do not; cannot form a device communicator");
+    VERR("some ranks have a CUDA device and some do not; cannot form a device communicator "
+         "(VCCL_NO_DEVICE=1 on every rank moves host buffers over TCP instead)");
     return vcclInvalidUsage;
   }
   if (withDev == nranks) {
     for (int a = 0; a < nranks; a++) {
       for (int b = a + 1; b < nranks; b++) {
         if (ids[a].host != ids[b].host) {
-          VERR("ranks %d and %d are on different hosts; device communicators need one NVLink domain", a, b);
+          VERR("ranks %d and %d are on different hosts; device communicators need one NVLink domain "
+               "(VCCL_NO_DEVICE=1 on every rank moves host buffers over TCP between hosts)",
+               a, b);
           return vcclInvalidUsage;
         }
         if (memcmp(ids[a].uuid, ids[b].uuid, 16) == 0) {
