@@ -132,7 +132,8 @@ vcclResult_t vcclCommAbort(vcclComm_t comm);
 vcclResult_t vcclCommGetAsyncError(vcclComm_t comm, vcclResult_t* asyncError);
 vcclResult_t vcclCommCount(const vcclComm_t comm, int* count);
 vcclResult_t vcclCommUserRank(const vcclComm_t comm, int* rank);
-/* CUDA device ordinal bound to this communicator (-1 when control-plane only). */
+/* CUDA device ordinal bound to this communicator (-1 for a communicator
+ * without a device, which moves host buffers; the reference always reports 0). */
 vcclResult_t vcclCommDevice(const vcclComm_t comm, int* device);
 
 /* ── Collectives (reference semantics, host-blocking) ─────────────────── */
