@@ -102,6 +102,20 @@ def test_deploy_script_with_fake_ssh(tmp_path):
     assert "ssh root@node1" in log.read_text()
 
 
+def test_bring_up_script_on_host_plane():
+    """csrc/tools/vccl-e2e.sh on a node without GPUs: vccl-bench --check for every op at 1, 2 and 4
+    ranks over the host data plane (the reference's kit/vccl-e2e.sh bring-up role)."""
+    import random
+
+    repo = os.path.dirname(os.path.dirname(os.path.dirname(BIN)))
+    env = dict(os.environ, VCCL_E2E_HOST="1", VCCL_PORT=str(20000 + random.randint(0, 20000)),
+               VCCL_DEBUG="ERROR")
+    p = subprocess.run(["bash", os.path.join(repo, "csrc", "tools", "vccl-e2e.sh"), "64K", "5"], env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert p.stdout.count("ok ") == 12, p.stdout
+
+
 def test_registration_cache_protocol():
     """Registration cache: simulated ranks with their own address layouts run random call sequences
     (reuse, slices, reallocation at the same address, a rank unable to take part, application
