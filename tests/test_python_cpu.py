@@ -3,9 +3,10 @@
 several processes, single-rank host collectives, and the host-side helpers of
 the fused ops.
 
-Multi-process cases run control-plane-only communicators (VCCL_NO_DEVICE=1)
+Multi-process cases run communicators without a device (VCCL_NO_DEVICE=1)
 over the TCP bootstrap on 127.0.0.1, as the reference's Python suites run
-their ranks as local processes (reference: python/tests/test_bindings.py).
+their ranks as local processes (reference: python/tests/test_bindings.py);
+tests/test_host_plane.py moves data between such ranks.
 """
 
 import ctypes
