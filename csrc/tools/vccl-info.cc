@@ -12,10 +12,24 @@
 #include <cstdio>
 #include <cstdlib>
 
+#include <string>
+
+#include "common/net.h"
+
 int main() {
+  // The address this host advertises for the rendezvous and for the host
+  // data plane (VCCL_SOCKET_ADDR, else VCCL_SOCKET_IFNAME, else the first
+  // non-loopback IPv4).
+  vccl::WireEndpoint ep{};
+  if (vccl::localEndpoint(&ep) == vcclSuccess) {
+    std::string addr = vccl::endpointString(ep);
+    const size_t colon = addr.rfind(':');
+    if (colon != std::string::npos) addr.resize(colon);  // no port is bound yet
+    std::printf("bootstrap / host data plane address: %s\n", addr.c_str());
+  }
   int n = 0;
   if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
-    std::printf("no CUDA devices visible\n");
+    std::printf("no CUDA devices visible: communicators move host buffers over the host data plane (TCP)\n");
     return 0;
   }
   using GetAttr = CUresult (*)(int*, CUdevice_attribute, CUdevice);
