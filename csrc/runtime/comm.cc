@@ -196,7 +196,8 @@ vcclResult_t initRank(vcclComm_t* out, int nranks, const vcclUniqueId& id, int r
   VTRY(Bootstrap::create(id, rank, nranks, &c->bootstrap));
 
   // Agree on the device data plane: either every rank has a distinct GPU on
-  // one host, or the communicator is control-plane only.
+  // one host, or the communicator has no device (host buffers, host data
+  // plane).
   const int device = callerDevice();
   std::vector<DeviceIdentity> ids(nranks);
   DeviceIdentity& mine = ids[rank];
