@@ -246,78 +246,84 @@ void HostPlane::abort() {
 
 // ---- progress loop ---------------------------------------------------------
 
-vcclResult_t HostPlane::run(const std::vector<HostXfer>& xs) {
-  struct PeerQ {
-    std::deque<const HostXfer*> sends, recvs;
-    size_t soff = 0, roff = 0;
-  };
-  std::vector<PeerQ> q(n_);
-  size_t pending = 0;
+vcclResult_t HostPlane::start(const std::vector<HostXfer>& xs, Batch* b) {
+  b->q.assign(n_, Batch::PeerQ{});
+  b->pending = 0;
   for (const HostXfer& x : xs) {
     if (x.peer < 0 || x.peer >= n_ || x.peer == rank_ || fd_[x.peer] < 0) {
       VERR("host data plane: transfer with invalid peer %d", x.peer);
       return vcclInternalError;
     }
     if (x.bytes == 0) continue;
-    (x.send ? q[x.peer].sends : q[x.peer].recvs).push_back(&x);
-    pending++;
+    (x.send ? b->q[x.peer].sends : b->q[x.peer].recvs).push_back(&x);
+    b->pending++;
   }
+  bool moved = false;
+  return b->pending ? pass(b, &moved) : vcclSuccess;
+}
+
+vcclResult_t HostPlane::pass(Batch* b, bool* moved) {
+  if (aborted_.load()) {
+    VERR("host data plane: communicator aborted");
+    return vcclSystemError;
+  }
+  for (int p = 0; p < n_ && b->pending > 0; p++) {
+    Batch::PeerQ& pq = b->q[p];
+    // Send as much as the socket takes, then take what has arrived.
+    while (!pq.sends.empty()) {
+      const HostXfer* x = pq.sends.front();
+      const ssize_t k = ::send(fd_[p], x->buf + pq.soff, x->bytes - pq.soff, MSG_DONTWAIT | MSG_NOSIGNAL);
+      if (k > 0) {
+        *moved = true;
+        pq.soff += static_cast<size_t>(k);
+        if (pq.soff == x->bytes) {
+          pq.sends.pop_front();
+          pq.soff = 0;
+          b->pending--;
+        }
+        continue;
+      }
+      if (k < 0 && errno == EINTR) continue;
+      if (k < 0 && (errno == EAGAIN || errno == EWOULDBLOCK)) break;
+      VERR("host data plane: send to rank %d failed: %s", p, k == 0 ? "no progress" : strerror(errno));
+      return vcclSystemError;
+    }
+    while (!pq.recvs.empty()) {
+      const HostXfer* x = pq.recvs.front();
+      const ssize_t k = ::recv(fd_[p], x->buf + pq.roff, x->bytes - pq.roff, MSG_DONTWAIT);
+      if (k > 0) {
+        *moved = true;
+        pq.roff += static_cast<size_t>(k);
+        if (pq.roff == x->bytes) {
+          pq.recvs.pop_front();
+          pq.roff = 0;
+          b->pending--;
+        }
+        continue;
+      }
+      if (k == 0) {
+        VERR("host data plane: rank %d closed its stream", p);
+        return vcclSystemError;
+      }
+      if (errno == EINTR) continue;
+      if (errno == EAGAIN || errno == EWOULDBLOCK) break;
+      VERR("host data plane: recv from rank %d failed: %s", p, strerror(errno));
+      return vcclSystemError;
+    }
+  }
+  return vcclSuccess;
+}
+
+vcclResult_t HostPlane::finish(Batch* b) {
   Deadline dl;
   std::vector<pollfd> pfd;
   std::vector<int> who;
   const auto spin = std::chrono::microseconds(spinUs_);
   auto idleSince = std::chrono::steady_clock::now();
-  while (pending > 0) {
-    if (aborted_.load()) {
-      VERR("host data plane: communicator aborted");
-      return vcclSystemError;
-    }
+  while (b->pending > 0) {
     bool moved = false;
-    for (int p = 0; p < n_; p++) {
-      PeerQ& pq = q[p];
-      // Send as much as the socket takes, then take what has arrived.
-      while (!pq.sends.empty()) {
-        const HostXfer* x = pq.sends.front();
-        const ssize_t k = ::send(fd_[p], x->buf + pq.soff, x->bytes - pq.soff, MSG_DONTWAIT | MSG_NOSIGNAL);
-        if (k > 0) {
-          moved = true;
-          pq.soff += static_cast<size_t>(k);
-          if (pq.soff == x->bytes) {
-            pq.sends.pop_front();
-            pq.soff = 0;
-            pending--;
-          }
-          continue;
-        }
-        if (k < 0 && errno == EINTR) continue;
-        if (k < 0 && (errno == EAGAIN || errno == EWOULDBLOCK)) break;
-        VERR("host data plane: send to rank %d failed: %s", p, k == 0 ? "no progress" : strerror(errno));
-        return vcclSystemError;
-      }
-      while (!pq.recvs.empty()) {
-        const HostXfer* x = pq.recvs.front();
-        const ssize_t k = ::recv(fd_[p], x->buf + pq.roff, x->bytes - pq.roff, MSG_DONTWAIT);
-        if (k > 0) {
-          moved = true;
-          pq.roff += static_cast<size_t>(k);
-          if (pq.roff == x->bytes) {
-            pq.recvs.pop_front();
-            pq.roff = 0;
-            pending--;
-          }
-          continue;
-        }
-        if (k == 0) {
-          VERR("host data plane: rank %d closed its stream", p);
-          return vcclSystemError;
-        }
-        if (errno == EINTR) continue;
-        if (errno == EAGAIN || errno == EWOULDBLOCK) break;
-        VERR("host data plane: recv from rank %d failed: %s", p, strerror(errno));
-        return vcclSystemError;
-      }
-    }
-    if (pending == 0) continue;
+    VTRY(pass(b, &moved));
+    if (b->pending == 0) break;
     if (moved) {
       idleSince = std::chrono::steady_clock::now();
       continue;
@@ -333,8 +339,8 @@ vcclResult_t HostPlane::run(const std::vector<HostXfer>& xs) {
     who.clear();
     for (int p = 0; p < n_; p++) {
       short ev = 0;
-      if (!q[p].sends.empty()) ev |= POLLOUT;
-      if (!q[p].recvs.empty()) ev |= POLLIN;
+      if (!b->q[p].sends.empty()) ev |= POLLOUT;
+      if (!b->q[p].recvs.empty()) ev |= POLLIN;
       if (ev) {
         pfd.push_back(pollfd{fd_[p], ev, 0});
         who.push_back(p);
@@ -357,6 +363,33 @@ vcclResult_t HostPlane::run(const std::vector<HostXfer>& xs) {
       VERR("host data plane: timed out after VCCL_TIMEOUT=%ds", watchdogSeconds());
       return vcclSystemError;
     }
+  }
+  return vcclSuccess;
+}
+
+vcclResult_t HostPlane::run(const std::vector<HostXfer>& xs) {
+  Batch b;
+  VTRY(start(xs, &b));
+  return finish(&b);
+}
+
+template <typename X, typename R>
+vcclResult_t HostPlane::pipelined(size_t pieces, X xfers, R reduce) {
+  if (pieces == 0) return vcclSuccess;
+  std::vector<HostXfer> xs[2];
+  Batch b[2];
+  xfers(size_t{0}, 0, &xs[0]);
+  VTRY(start(xs[0], &b[0]));
+  VTRY(finish(&b[0]));
+  for (size_t k = 0; k < pieces; k++) {
+    const int s = static_cast<int>(k % 2), t = 1 - s;
+    if (k + 1 < pieces) {
+      xs[t].clear();
+      xfers(k + 1, t, &xs[t]);
+      VTRY(start(xs[t], &b[t]));
+    }
+    reduce(k, s);
+    if (k + 1 < pieces) VTRY(finish(&b[t]));
   }
   return vcclSuccess;
 }
@@ -488,81 +521,85 @@ vcclResult_t HostPlane::reduceScatter(const char* send, char* recv, size_t recvC
   const size_t es = vcclTypeSize(r.dt);
   if (recvCount == 0) return vcclSuccess;
   const size_t cb = recvCount * es;
-  std::vector<char> scaled;
   if (r.premul) {
-    scaled.resize(cb * n_);
-    hostScale(scaled.data(), send, recvCount * n_, r.dt, r.scalar);
-    send = scaled.data();
+    char* scaled = scratch(2, cb * n_);
+    hostScale(scaled, send, recvCount * n_, r.dt, r.scalar);
+    send = scaled;
   }
   const size_t pe = std::max<size_t>(1, chunk_ / es);
-  std::vector<char> tmp(std::min(pe, recvCount) * es * n_);
+  const size_t ps = std::min(pe, recvCount);  // elements of one peer's piece in a buffer
+  char* tmp[2] = {scratch(0, ps * es * n_), scratch(1, ps * es * n_)};
   std::vector<const char*> src(n_);
-  for (size_t off = 0; off < recvCount; off += pe) {
-    const size_t m = std::min(pe, recvCount - off);
-    std::vector<HostXfer> xs;
-    for (int p = 0; p < n_; p++) {
-      if (p == rank_) continue;
-      xs.push_back({true, p, const_cast<char*>(send + p * cb + off * es), m * es});
-      xs.push_back({false, p, tmp.data() + p * m * es, m * es});
-    }
-    VTRY(run(xs));
-    for (int p = 0; p < n_; p++) src[p] = p == rank_ ? send + rank_ * cb + off * es : tmp.data() + p * m * es;
-    hostReduce(recv + off * es, src, m, r);
-  }
-  return vcclSuccess;
+  auto len = [&](size_t k) { return std::min(pe, recvCount - k * pe); };
+  return pipelined(
+      ceilDiv(recvCount, pe),
+      [&](size_t k, int slot, std::vector<HostXfer>* xs) {
+        const size_t off = k * pe, m = len(k);
+        for (int p = 0; p < n_; p++) {
+          if (p == rank_) continue;
+          xs->push_back({true, p, const_cast<char*>(send + p * cb + off * es), m * es});
+          xs->push_back({false, p, tmp[slot] + p * ps * es, m * es});
+        }
+      },
+      [&](size_t k, int slot) {
+        const size_t off = k * pe, m = len(k);
+        for (int p = 0; p < n_; p++) src[p] = p == rank_ ? send + rank_ * cb + off * es : tmp[slot] + p * ps * es;
+        hostReduce(recv + off * es, src, m, r);
+      });
 }
 
 vcclResult_t HostPlane::reduce(const char* send, char* recv, size_t count, const HostRed& r, int root) {
   const size_t es = vcclTypeSize(r.dt);
   if (count == 0) return vcclSuccess;
-  std::vector<char> scaled;
   if (r.premul) {
-    scaled.resize(count * es);
-    hostScale(scaled.data(), send, count, r.dt, r.scalar);
-    send = scaled.data();
+    char* scaled = scratch(2, count * es);
+    hostScale(scaled, send, count, r.dt, r.scalar);
+    send = scaled;
   }
   const size_t pe = std::max<size_t>(1, chunk_ / es);
   if (rank_ != root) {
     std::vector<HostXfer> xs{{true, root, const_cast<char*>(send), count * es}};
     return run(xs);
   }
-  std::vector<char> tmp(std::min(pe, count) * es * n_);
+  const size_t ps = std::min(pe, count);
+  char* tmp[2] = {scratch(0, ps * es * n_), scratch(1, ps * es * n_)};
   std::vector<const char*> src(n_);
-  for (size_t off = 0; off < count; off += pe) {
-    const size_t m = std::min(pe, count - off);
-    std::vector<HostXfer> xs;
-    for (int p = 0; p < n_; p++)
-      if (p != rank_) xs.push_back({false, p, tmp.data() + p * m * es, m * es});
-    VTRY(run(xs));
-    for (int p = 0; p < n_; p++) src[p] = p == rank_ ? send + off * es : tmp.data() + p * m * es;
-    hostReduce(recv + off * es, src, m, r);
-  }
-  return vcclSuccess;
+  auto len = [&](size_t k) { return std::min(pe, count - k * pe); };
+  return pipelined(
+      ceilDiv(count, pe),
+      [&](size_t k, int slot, std::vector<HostXfer>* xs) {
+        for (int p = 0; p < n_; p++)
+          if (p != rank_) xs->push_back({false, p, tmp[slot] + p * ps * es, len(k) * es});
+      },
+      [&](size_t k, int slot) {
+        const size_t off = k * pe;
+        for (int p = 0; p < n_; p++) src[p] = p == rank_ ? send + off * es : tmp[slot] + p * ps * es;
+        hostReduce(recv + off * es, src, len(k), r);
+      });
 }
 
 vcclResult_t HostPlane::allReduce(const char* send, char* recv, size_t count, const HostRed& r) {
   const size_t es = vcclTypeSize(r.dt);
   if (count == 0) return vcclSuccess;
   const size_t bytes = count * es;
-  std::vector<char> scaled;
   if (r.premul) {
-    scaled.resize(bytes);
-    hostScale(scaled.data(), send, count, r.dt, r.scalar);
-    send = scaled.data();
+    char* scaled = scratch(2, bytes);
+    hostScale(scaled, send, count, r.dt, r.scalar);
+    send = scaled;
   }
   std::vector<const char*> src(n_);
   if (bytes <= directMax_ || count < static_cast<size_t>(n_)) {
     // Small: every rank sends the whole message to every peer and reduces
     // the n copies in rank order.
-    std::vector<char> tmp(bytes * n_);
+    char* tmp = scratch(0, bytes * n_);
     std::vector<HostXfer> xs;
     for (int p = 0; p < n_; p++) {
       if (p == rank_) continue;
       xs.push_back({true, p, const_cast<char*>(send), bytes});
-      xs.push_back({false, p, tmp.data() + p * bytes, bytes});
+      xs.push_back({false, p, tmp + p * bytes, bytes});
     }
     VTRY(run(xs));
-    for (int p = 0; p < n_; p++) src[p] = p == rank_ ? send : tmp.data() + p * bytes;
+    for (int p = 0; p < n_; p++) src[p] = p == rank_ ? send : tmp + p * bytes;
     hostReduce(recv, src, count, r);
     return vcclSuccess;
   }
@@ -572,23 +609,26 @@ vcclResult_t HostPlane::allReduce(const char* send, char* recv, size_t count, co
   auto blkOff = [&](int q) { return std::min(static_cast<size_t>(q) * bc, count); };
   auto blkLen = [&](int q) { return std::min(static_cast<size_t>(q + 1) * bc, count) - blkOff(q); };
   const size_t pe = std::max<size_t>(1, chunk_ / es);
-  const size_t ps = std::min(pe, bc);  // elements of one peer's piece in tmp
-  std::vector<char> tmp(ps * es * n_);
-  for (size_t off = 0; off < bc; off += pe) {
-    std::vector<HostXfer> xs;
-    auto len = [&](int q) { return blkLen(q) > off ? std::min(pe, blkLen(q) - off) : size_t{0}; };
-    const size_t mine = len(rank_);
-    for (int p = 0; p < n_; p++) {
-      if (p == rank_) continue;
-      xs.push_back({true, p, const_cast<char*>(send + (blkOff(p) + off) * es), len(p) * es});
-      xs.push_back({false, p, tmp.data() + p * ps * es, mine * es});
-    }
-    VTRY(run(xs));
-    if (mine == 0) continue;
-    for (int p = 0; p < n_; p++)
-      src[p] = p == rank_ ? send + (blkOff(rank_) + off) * es : tmp.data() + p * ps * es;
-    hostReduce(recv + (blkOff(rank_) + off) * es, src, mine, r);
-  }
+  const size_t ps = std::min(pe, bc);  // elements of one peer's piece in a buffer
+  char* tmp[2] = {scratch(0, ps * es * n_), scratch(1, ps * es * n_)};
+  auto len = [&](int q, size_t off) { return blkLen(q) > off ? std::min(pe, blkLen(q) - off) : size_t{0}; };
+  VTRY(pipelined(
+      ceilDiv(bc, pe),
+      [&](size_t k, int slot, std::vector<HostXfer>* xs) {
+        const size_t off = k * pe, mine = len(rank_, off);
+        for (int p = 0; p < n_; p++) {
+          if (p == rank_) continue;
+          xs->push_back({true, p, const_cast<char*>(send + (blkOff(p) + off) * es), len(p, off) * es});
+          xs->push_back({false, p, tmp[slot] + p * ps * es, mine * es});
+        }
+      },
+      [&](size_t k, int slot) {
+        const size_t off = k * pe, mine = len(rank_, off);
+        if (mine == 0) return;
+        for (int p = 0; p < n_; p++)
+          src[p] = p == rank_ ? send + (blkOff(rank_) + off) * es : tmp[slot] + p * ps * es;
+        hostReduce(recv + (blkOff(rank_) + off) * es, src, mine, r);
+      }));
   std::vector<HostXfer> xs;
   for (int p = 0; p < n_; p++) {
     if (p == rank_) continue;

@@ -28,14 +28,16 @@
 //
 // Every element is reduced by one rank, in rank order, with 16- and 8-bit
 // floats accumulated in fp32, so every rank ends with the same bits.
-// Large messages go in pieces (VCCL_HOST_CHUNK bytes per peer) so the
-// reduction buffers stay bounded.  Waits honour VCCL_TIMEOUT and
+// Large messages go in pieces (VCCL_HOST_CHUNK bytes per peer): the
+// reduction buffers stay bounded, and the next piece is on the wire while the
+// current one is reduced.  Waits honour VCCL_TIMEOUT and
 // vcclCommAbort; a peer that closes its stream fails the call.
 #pragma once
 
 #include <atomic>
 #include <cstddef>
 #include <cstdint>
+#include <deque>
 #include <memory>
 #include <vector>
 
@@ -94,13 +96,41 @@ class HostPlane {
  private:
   HostPlane(int rank, int n) : rank_(rank), n_(n) {}
 
+  // Transfers in progress: run() starts a batch and finishes it; reductions
+  // in pieces start the next piece's batch (its first bytes go out, the
+  // sockets take the rest as they drain) before reducing the current piece.
+  struct Batch {
+    struct PeerQ {
+      std::deque<const HostXfer*> sends, recvs;
+      size_t soff = 0, roff = 0;
+    };
+    std::vector<PeerQ> q;
+    size_t pending = 0;
+  };
+  vcclResult_t start(const std::vector<HostXfer>& xs, Batch* b);
+  vcclResult_t finish(Batch* b);
+  // One non-blocking pass over every stream of the batch.
+  vcclResult_t pass(Batch* b, bool* moved);
+  // Pieces 0..pieces-1: xfers(k, slot, &xs) lists piece k's transfers into
+  // buffer `slot` (0 or 1), reduce(k, slot) reduces it.
+  template <typename X, typename R>
+  vcclResult_t pipelined(size_t pieces, X xfers, R reduce);
+
   int rank_;
   int n_;
   std::vector<int> fd_;  // stream to each peer ([rank_] = -1)
   std::atomic<bool> aborted_{false};
-  size_t chunk_ = 8u << 20;      // per-peer piece of a reduction (VCCL_HOST_CHUNK)
+  size_t chunk_ = 1u << 20;      // per-peer piece of a reduction (VCCL_HOST_CHUNK)
   size_t directMax_ = 32u << 10;  // all-reduce below this: whole message to every peer
   int spinUs_ = 50;               // retry without sleeping this long before poll() (VCCL_HOST_SPIN_US)
+  // Reduction buffers kept across calls (a fresh allocation per call would
+  // page-fault its way through every byte): [0] and [1] receive alternate
+  // pieces, [2] holds a pre-multiplied copy of the input.
+  std::vector<char> scratch_[3];
+  char* scratch(int i, size_t bytes) {
+    if (scratch_[i].size() < bytes) scratch_[i].resize(bytes);
+    return scratch_[i].data();
+  }
   size_t bcastDirect_ = 16u << 10;  // broadcast up to this: root to every rank (VCCL_HOST_BCAST_DIRECT)
   size_t bcastPiece_ = 1u << 20;    // ... above: per-receiver block of one piece (VCCL_HOST_BCAST_PIECE)
 };
