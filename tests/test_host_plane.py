@@ -349,3 +349,31 @@ def _vllm_comm_body(rank, n, port, q):
 def test_vllm_communicator_on_host_plane(n):
     res = _run(_vllm_comm_body, n, timeout=300)
     assert all(s == "ok" for s, _ in res.values()), res
+
+
+def _distinct_addr_body(rank, n, port, q):
+    """Every rank advertises its own address (127.0.0.1, .2, .3: distinct 'hosts' on loopback),
+    so the mesh must connect to each rank's own endpoint."""
+    try:
+        _env(port)
+        os.environ["VCCL_SOCKET_ADDR"] = f"127.0.0.{rank + 1}"
+        import vkccl_b200 as v
+
+        comm = v.Communicator(n, v.get_unique_id(), rank)
+        x = torch.full((70000,), float(rank + 1))
+        comm.all_reduce(x)
+        assert torch.all(x == n * (n + 1) / 2)
+        g = torch.empty(3 * n, dtype=torch.int64)
+        comm.all_gather(torch.full((3,), rank), g)
+        assert torch.equal(g, torch.arange(n).repeat_interleave(3))
+        comm.destroy()
+        q.put((rank, "ok", None))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, traceback.format_exc(), None))
+
+
+def test_host_plane_ranks_on_distinct_addresses():
+    res = _run(_distinct_addr_body, 3, timeout=120)
+    assert all(s == "ok" for s, _ in res.values()), res
