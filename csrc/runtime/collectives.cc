@@ -531,6 +531,10 @@ vcclResult_t cacheWindowsFor(HostOp& h, bool eligible) {
   int nbuf = 1;
   switch (h.kind) {
     case Kind::AllReduce:
+      // Where the staged NVLS all-reduce runs (NVLS, enough ranks), it moves
+      // less data per GPU than the point-to-point kernel of a cached window
+      // (cudaMalloc windows have no multicast binding): keep it.
+      if (comm->dev->nvls && comm->nranks >= comm->dev->nvlsMinRanks) return vcclSuccess;
       ptrs[0] = h.send;
       sizes[0] = bytes;
       if (h.recv != h.send) {

@@ -19,8 +19,10 @@ pytestmark = pytest.mark.gpu
 def test_registration_cache(nranks):
     if gpu_count() < nranks:
         pytest.skip(f"needs {nranks} GPUs")
+    # VCCL_NVLS_MIN_RANKS above the rank count: all-reduce consults the cache only where the
+    # staged NVLS kernel would not run
     env = dict(os.environ, VCCL_SOCKET_ADDR="127.0.0.1", VCCL_TIMEOUT="30", GLOO_SOCKET_IFNAME="lo",
-               VCCL_REG_CACHE="1", VCCL_REG_CACHE_MIN=str(1 << 20))
+               VCCL_REG_CACHE="1", VCCL_REG_CACHE_MIN=str(1 << 20), VCCL_NVLS_MIN_RANKS="8")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={nranks}",
            "--master-addr=127.0.0.1", f"--master-port={free_port()}",
            os.path.join(ROOT, "tests", "workers", "reg_cache_worker.py")]
