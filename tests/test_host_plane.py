@@ -77,6 +77,7 @@ def _same(a, b):
 def _matrix_body(rank, n, port, q):
     try:
         _env(port)
+        os.environ["VCCL_PROF"] = "1"
         os.environ["VCCL_HOST_CHUNK"] = "4096"  # many pieces for the larger reductions
         os.environ["VCCL_HOST_BCAST_PIECE"] = "8192"  # ... and broadcasts
         import vkccl_b200 as v
@@ -198,6 +199,7 @@ def _matrix_body(rank, n, port, q):
                 comm.recv(r2, peer)
             assert torch.all(r1 == 10 + peer) and torch.all(r2 == 20 + peer), "ordered p2p"
         prof = {(e["op"], e["algo"]) for e in comm.prof_summary()}
+        assert ("all-reduce", "host TCP mesh") in prof and ("send", "host TCP mesh") in prof, prof
         assert comm.async_error() == 0
         comm.destroy()
         q.put((rank, "ok", sorted(prof)))
