@@ -379,3 +379,40 @@ def _distinct_addr_body(rank, n, port, q):
 def test_host_plane_ranks_on_distinct_addresses():
     res = _run(_distinct_addr_body, 3, timeout=120)
     assert all(s == "ok" for s, _ in res.values()), res
+
+
+def _grad_buckets_body(rank, n, port, q):
+    """Data parallelism on CPU: GradBuckets averages every parameter's gradient over the ranks
+    (bucketed all-reduces on the host data plane)."""
+    try:
+        _env(port)
+        import vkccl_b200 as v
+        from vkccl_b200.parallel import GradBuckets
+
+        comm = v.Communicator(n, v.get_unique_id(), rank)
+        sizes = [1000, 3, 70000, 17]
+        params = [torch.nn.Parameter(torch.zeros(s)) for s in sizes]
+
+        def grads(r):
+            g = torch.Generator().manual_seed(500 + r)
+            return [torch.randn(s, generator=g) for s in sizes]
+
+        for p, g in zip(params, grads(rank)):
+            p.grad = g
+        gb = GradBuckets(comm, params, bucket_bytes=64 << 10)
+        gb.all_reduce()
+        mean = [sum(gs) / n for gs in zip(*[grads(r) for r in range(n)])]
+        for p, m in zip(params, mean):
+            torch.testing.assert_close(p.grad, m, rtol=1e-5, atol=1e-6)
+        gb.close()
+        comm.destroy()
+        q.put((rank, "ok", None))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, traceback.format_exc(), None))
+
+
+def test_grad_buckets_on_host_plane():
+    res = _run(_grad_buckets_body, 3, timeout=120)
+    assert all(s == "ok" for s, _ in res.values()), res
