@@ -416,3 +416,40 @@ def _grad_buckets_body(rank, n, port, q):
 def test_grad_buckets_on_host_plane():
     res = _run(_grad_buckets_body, 3, timeout=120)
     assert all(s == "ok" for s, _ in res.values()), res
+
+
+def _sequence_body(rank, n, port, q):
+    """Context / sequence parallelism on CPU ranks: the Ulysses all-to-all re-sharding round trip
+    and the ring pass (grouped send / receive) of vkccl_b200.parallel.sequence over the host
+    data plane."""
+    try:
+        _env(port)
+        import vkccl_b200 as v
+        from vkccl_b200.parallel.sequence import ring_pass, ring_schedule, ulysses_heads_to_seq, ulysses_seq_to_heads
+
+        comm = v.Communicator(n, v.get_unique_id(), rank)
+        S, H, D = 8 * n, 4 * n, 3
+        full = torch.randn(S, H, D, generator=torch.Generator().manual_seed(1))
+        s_loc, h_loc = S // n, H // n
+        heads = ulysses_seq_to_heads(comm, full[rank * s_loc:(rank + 1) * s_loc].contiguous())
+        assert torch.equal(heads, full[:, rank * h_loc:(rank + 1) * h_loc]), "seq -> heads"
+        back = ulysses_heads_to_seq(comm, heads)
+        assert torch.equal(back, full[rank * s_loc:(rank + 1) * s_loc]), "heads -> seq"
+        held = torch.full((5,), float(rank))
+        seen = [rank]
+        for _ in range(n - 1):
+            held = ring_pass(comm, held)
+            seen.append(int(held[0]))
+        assert tuple(seen) == ring_schedule(n, rank), seen
+        comm.destroy()
+        q.put((rank, "ok", None))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, traceback.format_exc(), None))
+
+
+@pytest.mark.parametrize("n", [2, 4])
+def test_sequence_parallel_on_host_plane(n):
+    res = _run(_sequence_body, n, timeout=120)
+    assert all(s == "ok" for s, _ in res.values()), res
