@@ -229,7 +229,12 @@ class Communicator:
     """One rank's handle on a communicator.
 
     ``cuda_device`` (optional) is made current before the communicator is
-    created; rank r then works on that GPU.
+    created; rank r then works on that GPU (``self.device``), and collectives
+    take CUDA tensors (stream-ordered on torch's current stream) or host
+    buffers (staged through the GPU).  Without a GPU, or with
+    ``VCCL_NO_DEVICE=1`` (``self.device == -1``), the communicator moves host
+    buffers (numpy arrays, CPU tensors, bytearrays) between its ranks over
+    TCP, which may sit on different hosts.
     """
 
     def __init__(self, nranks: int, unique_id: Optional[UniqueId], rank: int,
