@@ -6,7 +6,10 @@
 // tools/vccl_info.cc:66-114) with the B200 data plane's equivalents: which
 // devices exist, which pairs can map each other's memory over NVLink, and
 // whether NVSwitch multicast objects (NVLS) can be created.
+#include <arpa/inet.h>
 #include <cuda.h>
+#include <ifaddrs.h>
+#include <netinet/in.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -26,6 +29,20 @@ int main() {
     const size_t colon = addr.rfind(':');
     if (colon != std::string::npos) addr.resize(colon);  // no port is bound yet
     std::printf("bootstrap / host data plane address: %s\n", addr.c_str());
+  }
+  // The host's IPv4 interfaces (VCCL_SOCKET_IFNAME picks one, VCCL_SOCKET_ADDR
+  // an address), as the reference's survey lists its network devices.
+  ifaddrs* ifs = nullptr;
+  if (getifaddrs(&ifs) == 0) {
+    std::printf("IPv4 interfaces:");
+    for (ifaddrs* i = ifs; i != nullptr; i = i->ifa_next) {
+      if (i->ifa_addr == nullptr || i->ifa_addr->sa_family != AF_INET) continue;
+      char buf[INET_ADDRSTRLEN] = {0};
+      inet_ntop(AF_INET, &reinterpret_cast<sockaddr_in*>(i->ifa_addr)->sin_addr, buf, sizeof(buf));
+      std::printf(" %s=%s", i->ifa_name, buf);
+    }
+    std::printf("\n");
+    freeifaddrs(ifs);
   }
   int n = 0;
   if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {

@@ -102,6 +102,17 @@ def test_deploy_script_with_fake_ssh(tmp_path):
     assert "ssh root@node1" in log.read_text()
 
 
+def test_vccl_info_without_gpu():
+    """vccl-info on a node without GPUs: the advertised address, the IPv4 interfaces, and the note
+    that communicators use the host data plane (reference: tools/vccl_info.cc surveys the node)."""
+    p = subprocess.run([os.path.join(BIN, "vccl-info")], env=dict(os.environ, VCCL_SOCKET_ADDR="127.0.0.1"),
+                       capture_output=True, text=True, timeout=60)
+    assert p.returncode == 0, p.stderr
+    assert "bootstrap / host data plane address: 127.0.0.1" in p.stdout
+    assert "lo=127.0.0.1" in p.stdout
+    assert "host data plane" in p.stdout.splitlines()[-1] or "device(s)" in p.stdout
+
+
 def test_bring_up_script_on_host_plane():
     """csrc/tools/vccl-e2e.sh on a node without GPUs: vccl-bench --check for every op at 1, 2 and 4
     ranks over the host data plane (the reference's kit/vccl-e2e.sh bring-up role)."""
