@@ -6,6 +6,10 @@ Launch one process per GPU:
     torchrun --nproc-per-node N --master-addr 127.0.0.1 -m vkccl_b200.bench.collectives \
         --ops allreduce,allgather,reducescatter,broadcast --dtypes bf16,f32 -b 8 -e 1G
 
+--host runs the host data plane (communicators without a device, CPU
+tensors) next to torch.distributed's gloo backend, timed by the host clock;
+it needs no GPU.
+
 --window adds a "vcclwin" column: the same vccl call on buffers inside
 registered windows (vcclMemAlloc memory mapped by every rank), which runs
 the zero-copy kernels (all-reduce, all-gather, reduce-scatter, broadcast).  NCCL runs
@@ -138,6 +142,73 @@ def time_eager(fn, iters: int, warmup: int) -> float:
     return e0.elapsed_time(e1) / iters * 1000.0
 
 
+def main_host(a) -> int:
+    """--host: communicators without a device on CPU tensors (the host data plane), next to
+    torch.distributed's gloo backend on the same tensors -- the CPU baseline the reference aims
+    to beat.  Host clock over --iters calls, maximum over ranks."""
+    import time
+
+    os.environ["VCCL_NO_DEVICE"] = "1"
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    dist.init_process_group("gloo")
+    raw = torch.zeros(vc.UNIQUE_ID_BYTES, dtype=torch.uint8)
+    if rank == 0:
+        raw.copy_(torch.frombuffer(bytearray(vc.get_unique_id().to_bytes()), dtype=torch.uint8))
+    dist.broadcast(raw, 0)
+    comm = vc.Communicator(world, vc.UniqueId.from_bytes(bytes(raw.numpy())), rank)
+    lo, hi = parse_size(a.b), parse_size(a.e)
+    rows = []
+    for op in a.ops.split(","):
+        for dname in a.dtypes.split(","):
+            dt = DT[dname]
+            es = torch.tensor([], dtype=dt).element_size()
+            size = lo
+            while size <= hi:
+                count = max(1, size // es)
+                if op in ("allgather", "reducescatter"):
+                    count = max(1, count // world) * world
+                if op == "allgather":
+                    send, recv = torch.randn(count // world).to(dt), torch.empty(count, dtype=dt)
+                elif op == "reducescatter":
+                    send, recv = torch.randn(count).to(dt), torch.empty(count // world, dtype=dt)
+                else:
+                    send = torch.randn(count).to(dt)
+                    recv = send.clone() if op == "broadcast" else torch.empty_like(send)
+                row = {"op": op, "dtype": dname, "bytes": count * es, "n": world, "timing": "host clock"}
+                for libname in ("vccl", "gloo"):
+                    fn = make_call("nccl" if libname == "gloo" else "vccl", op, comm, send, recv, world)
+                    try:
+                        for _ in range(a.warmup):
+                            fn()
+                        dist.barrier()
+                        t0 = time.perf_counter()
+                        for _ in range(a.iters):
+                            fn()
+                        us = (time.perf_counter() - t0) / a.iters * 1e6
+                    except RuntimeError as exc:  # an operation the backend lacks
+                        row[libname + "_error"] = str(exc)[:80]
+                        dist.barrier()
+                        continue
+                    t = torch.tensor([us], dtype=torch.float64)
+                    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                    us = t.item()
+                    row[libname + "_us"] = round(us, 2)
+                    row[libname + "_busbw"] = round(count * es / (us * 1e3) * bus_factor(op, world), 3)
+                rows.append(row)
+                if rank == 0:
+                    print(json.dumps(row), flush=True)
+                size = int(size * a.f)
+    comm.destroy()
+    if rank == 0 and a.out:
+        with open(a.out, "w") as f:
+            for r in rows:
+                f.write(json.dumps(r) + "\n")
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ops", default="allreduce,allgather,reducescatter,broadcast")
@@ -154,7 +225,11 @@ def main() -> int:
     ap.add_argument("--window", action="store_true", help="also time vccl on registered-window buffers")
     ap.add_argument("--eager", action="store_true",
                     help="time eager launches instead of a CUDA graph (needed to see VCCL_REG_CACHE=1)")
+    ap.add_argument("--host", action="store_true",
+                    help="CPU tensors on communicators without a device, next to gloo (no GPU needed)")
     a = ap.parse_args()
+    if a.host:
+        return main_host(a)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
