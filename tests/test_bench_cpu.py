@@ -54,3 +54,19 @@ def test_roofline_helper():
     assert r["fraction_sustained"] > r["fraction"]
     assert r["nvlink_us"] > 0
     assert b.roofline(flops, 8192, 1, 500.0)["nvlink_us"] == 0
+
+
+def test_collectives_bench_host_mode():
+    """`vkccl_b200.bench.collectives --host` (CPU tensors on the host data plane next to gloo) runs
+    without a GPU and prints one JSON row per operation and size with both libraries' times."""
+    env = dict(os.environ, VCCL_SOCKET_ADDR="127.0.0.1", GLOO_SOCKET_IFNAME="lo", VCCL_DEBUG="ERROR")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={free_port()}", "-m", "vkccl_b200.bench.collectives",
+           "--host", "--ops", "allreduce,allgather,reducescatter,broadcast", "--dtypes", "f32,bf16", "-b", "4K",
+           "-e", "64K", "-f", "16", "--iters", "3", "--warmup", "1"]
+    p = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+    assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-4000:]
+    rows = [json.loads(line) for line in p.stdout.splitlines() if line.startswith("{")]
+    assert len(rows) == 4 * 2 * 2, rows
+    for r in rows:
+        assert r["vccl_us"] > 0 and ("gloo_us" in r or "gloo_error" in r), r
