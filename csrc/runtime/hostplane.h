@@ -120,7 +120,7 @@ class HostPlane {
   int n_;
   std::vector<int> fd_;  // stream to each peer ([rank_] = -1)
   std::atomic<bool> aborted_{false};
-  size_t chunk_ = 1u << 20;      // per-peer piece of a reduction (VCCL_HOST_CHUNK)
+  size_t chunk_ = 8u << 20;      // per-peer piece of a reduction (VCCL_HOST_CHUNK)
   size_t directMax_ = 32u << 10;  // all-reduce below this: whole message to every peer
   int spinUs_ = 50;               // retry without sleeping this long before poll() (VCCL_HOST_SPIN_US)
   // Reduction buffers kept across calls (a fresh allocation per call would
