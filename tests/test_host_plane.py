@@ -338,7 +338,15 @@ def _vllm_comm_body(rank, n, port, q):
         assert torch.equal(comm.all_reduce(a.clone()), torch.full((5,), float(n * (n + 1) // 2)))
         b = torch.arange(6, dtype=torch.float32) * (rank + 1)
         assert torch.equal(comm.broadcast(b.clone(), src=n - 1), torch.arange(6, dtype=torch.float32) * n)
+        # the reference's staging-buffer cache contract (reference: python/tests/test_torch_comm.py:48-55):
+        # one buffer per (role, shape, dtype), at a stable address, none added by repeated calls
+        ptr = comm._buf("ar", a.shape, a.dtype).data_ptr()
+        comm.all_reduce(a.clone())
+        comm.all_reduce(a.clone())
+        assert len(comm._buffers) == 1 and comm._buf("ar", a.shape, a.dtype).data_ptr() == ptr
+        assert comm._buf("ag_out", (n, 5), torch.bfloat16).dtype == torch.bfloat16 and len(comm._buffers) == 2
         comm.destroy()
+        assert not comm._buffers
         dist.destroy_process_group()
         q.put((rank, "ok", None))
     except Exception:  # noqa: BLE001

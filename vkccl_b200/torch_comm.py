@@ -13,7 +13,9 @@ through the library.  Differences that follow from the B200 data plane:
 * The reference's persistent registered staging buffer per (role, shape,
   dtype) existed to amortise RDMA registration; here the library's
   symmetric workspace plays that role, and outputs are fresh tensors (under
-  CUDA graph capture they come from the graph's memory pool).
+  CUDA graph capture they come from the graph's memory pool).  ``_buf``
+  keeps the reference's buffer cache for code written against it; this
+  class's own collectives do not stage through it.
 * Adds what vLLM 0.22's base class exposes beyond the reference:
   ``all_gatherv``, ``reduce_scatterv``, ``gather``, ``batch_isend_irecv``,
   ``dispatch`` / ``combine`` for expert parallelism, and the fused
@@ -114,6 +116,24 @@ class VcclCommunicator(DeviceCommunicatorBase):
         if isinstance(self.device, torch.device) and self.device.type == "cuda":
             cuda_dev = self.device.index if self.device.index is not None else torch.cuda.current_device()
         self.vccl = _c.Communicator(self.world_size, uid, self.rank_in_group, cuda_device=cuda_dev)
+        # (role, shape, dtype) -> (tensor, registration handle or None); see _buf
+        self._buffers: dict = {}
+
+    def _buf(self, role: str, shape, dtype: torch.dtype) -> torch.Tensor:
+        """The persistent buffer of one (role, shape, dtype) on this
+        communicator's device: made and registered with the communicator
+        (vcclCommRegister, a local call) on first use, the same tensor on
+        every later call, released by destroy().  The reference's
+        staging-buffer cache under the same name and contract (reference:
+        python/vccl/torch_comm.py:115-129), for callers that copy into a
+        stable buffer before a collective."""
+        key = (role, tuple(shape), dtype)
+        got = self._buffers.get(key)
+        if got is None:
+            t = torch.empty(tuple(shape), dtype=dtype, device=self.device)
+            got = (t, self.vccl.register(t) if t.numel() > 0 else None)
+            self._buffers[key] = got
+        return got[0]
 
 
     # -- collectives -------------------------------------------------------------
@@ -281,5 +301,9 @@ class VcclCommunicator(DeviceCommunicatorBase):
 
     def destroy(self) -> None:
         if getattr(self, "vccl", None) is not None:
+            for _, handle in self._buffers.values():
+                if handle is not None:
+                    self.vccl.deregister(handle)
+            self._buffers.clear()
             self.vccl.destroy()
             self.vccl = None
