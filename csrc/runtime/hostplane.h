@@ -30,15 +30,20 @@
 // floats accumulated in fp32, so every rank ends with the same bits.
 // Large messages go in pieces (VCCL_HOST_CHUNK bytes per peer): the
 // reduction buffers stay bounded, and the next piece is on the wire while the
-// current one is reduced.  Waits honour VCCL_TIMEOUT and
-// vcclCommAbort; a peer that closes its stream fails the call.
+// current one is reduced.  A batch that sends and receives many bytes hands
+// its sends to a sender thread, so the kernel's socket copies run on two
+// cores.  Waits honour VCCL_TIMEOUT and vcclCommAbort; a peer that closes
+// its stream fails the call.
 #pragma once
 
 #include <atomic>
+#include <condition_variable>
 #include <cstddef>
 #include <cstdint>
 #include <deque>
 #include <memory>
+#include <mutex>
+#include <thread>
 #include <vector>
 
 #include "vccl.h"
@@ -106,9 +111,14 @@ class HostPlane {
     };
     std::vector<PeerQ> q;
     size_t pending = 0;
+    // The sends of a large batch, handed to the sender thread (null: this
+    // thread moves them with the receives).
+    std::unique_ptr<Batch> out;
   };
   vcclResult_t start(const std::vector<HostXfer>& xs, Batch* b);
   vcclResult_t finish(Batch* b);
+  // The progress loop of one batch (this thread or the sender thread).
+  vcclResult_t drive(Batch* b);
   // One non-blocking pass over every stream of the batch.
   vcclResult_t pass(Batch* b, bool* moved);
   // Pieces 0..pieces-1: xfers(k, slot, &xs) lists piece k's transfers into
@@ -133,6 +143,22 @@ class HostPlane {
   }
   size_t bcastDirect_ = 16u << 10;  // broadcast up to this: root to every rank (VCCL_HOST_BCAST_DIRECT)
   size_t bcastPiece_ = 1u << 20;    // ... above: per-receiver block of one piece (VCCL_HOST_BCAST_PIECE)
+
+  // Sender thread: a batch that sends at least sendThreadMin_ bytes
+  // (VCCL_HOST_SEND_THREAD_MIN; 0: never) hands its sends to it, so the
+  // kernel's copies of outgoing bytes run on another core while this thread
+  // receives and reduces.  One batch at a time (finish() waits for it).
+  size_t sendThreadMin_ = 8u << 20;
+  std::thread sender_;
+  std::mutex sMu_;
+  std::condition_variable sCv_, sDoneCv_;
+  Batch* job_ = nullptr;
+  bool jobDone_ = true;
+  bool stop_ = false;
+  vcclResult_t jobRes_ = vcclSuccess;
+  void senderLoop();
+  void handOff(Batch* sends);
+  vcclResult_t waitHandOff();
 };
 
 // out = reduce over the contributions src[0..] in that order (count

@@ -236,7 +236,19 @@ def test_host_plane_matrix(n):
     assert not bad, bad
 
 
-def _dead_peer_body(rank, n, port, q):
+def _matrix_send_thread_body(rank, n, port, q):
+    os.environ["VCCL_HOST_SEND_THREAD_MIN"] = "1"  # every batch that sends and receives hands its sends off
+    _matrix_body(rank, n, port, q)
+
+
+def test_host_plane_matrix_send_thread():
+    """The same matrix with the sends of every two-way batch on the sender thread."""
+    res = _run(_matrix_send_thread_body, 3)
+    bad = {r: s for r, (s, _) in res.items() if s != "ok"}
+    assert not bad, bad
+
+
+def _dead_peer_body(rank, n, port, q, count=1 << 16):
     try:
         _env(port)
         os.environ["VCCL_TIMEOUT"] = "20"
@@ -249,7 +261,7 @@ def _dead_peer_body(rank, n, port, q):
             os._exit(0)  # leaves between steps, with nothing in flight
         t0 = time.time()
         try:
-            comm.all_reduce(torch.ones(1 << 16))
+            comm.all_reduce(torch.ones(count))
             q.put((rank, "no error", None))
         except v.VcclError:
             q.put((rank, "ok", round(time.time() - t0, 2)))
@@ -259,13 +271,20 @@ def _dead_peer_body(rank, n, port, q):
         q.put((rank, traceback.format_exc(), None))
 
 
-def test_host_plane_dead_peer():
-    """A rank that exits ends its peers' next collective with an error (its streams close)."""
+def _dead_peer_send_thread_body(rank, n, port, q):
+    os.environ["VCCL_HOST_SEND_THREAD_MIN"] = "4096"
+    _dead_peer_body(rank, n, port, q, count=1 << 22)  # 16 MiB: more than the sockets hold
+
+
+@pytest.mark.parametrize("body", [_dead_peer_body, _dead_peer_send_thread_body], ids=["one_thread", "send_thread"])
+def test_host_plane_dead_peer(body):
+    """A rank that exits ends its peers' next collective with an error (its streams close),
+    also while the sender thread is moving a large message."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     n = 3
     port = free_port()
-    ps = [ctx.Process(target=_dead_peer_body, args=(r, n, port, q)) for r in range(n)]
+    ps = [ctx.Process(target=body, args=(r, n, port, q)) for r in range(n)]
     for p in ps:
         p.start()
     res = {}
@@ -278,7 +297,7 @@ def test_host_plane_dead_peer():
     assert all(t < 15 for _, t in res.values()), res
 
 
-def _abort_body(rank, n, port, q):
+def _abort_body(rank, n, port, q, count=1 << 16):
     try:
         _env(port)
         import vkccl_b200 as v
@@ -290,7 +309,7 @@ def _abort_body(rank, n, port, q):
             threading.Timer(0.5, comm.abort).start()
             t0 = time.time()
             try:
-                comm.all_reduce(torch.ones(1 << 16))
+                comm.all_reduce(torch.ones(count))
                 q.put((rank, "no error", None))
             except v.VcclError:
                 q.put((rank, "ok", round(time.time() - t0, 2)))
@@ -303,8 +322,14 @@ def _abort_body(rank, n, port, q):
         q.put((rank, traceback.format_exc(), None))
 
 
-def test_host_plane_abort_unblocks():
-    res = _run(_abort_body, 2, timeout=120)
+def _abort_send_thread_body(rank, n, port, q):
+    os.environ["VCCL_HOST_SEND_THREAD_MIN"] = "4096"
+    _abort_body(rank, n, port, q, count=1 << 22)  # the sender thread blocks on a full socket
+
+
+@pytest.mark.parametrize("body", [_abort_body, _abort_send_thread_body], ids=["one_thread", "send_thread"])
+def test_host_plane_abort_unblocks(body):
+    res = _run(body, 2, timeout=120)
     assert all(s == "ok" for s, _ in res.values()), res
     assert res[0][1] < 10, res
 
