@@ -67,8 +67,9 @@ $(KIT_TAR): $(OUT)/libvccl.so $(TOOLS) $(BIN)/test_collectives $(BIN)/test_dmabu
 
 .PHONY: all clean kit
 
-# Host-only control plane (no CUDA) built with sanitizers for the CPU race
-# checks: `make sanitize` -> bin/test_bootstrap_threads_{tsan,asan}.
+# Host-only control plane and host data plane (no CUDA runtime) built with
+# sanitizers for the CPU race checks: `make sanitize` ->
+# bin/test_{bootstrap,hostplane}_threads_{tsan,asan}.
 CTRL_SRC := csrc/common/types.cc csrc/common/env.cc csrc/common/log.cc csrc/common/net.cc csrc/control/bootstrap.cc
 SAN_FLAGS := -std=c++17 -O1 -g -Iinclude -Icsrc -pthread
 
@@ -80,7 +81,20 @@ $(BIN)/test_bootstrap_threads_asan: csrc/tests/test_bootstrap_threads.cc $(CTRL_
 	@mkdir -p $(BIN)
 	g++ $(SAN_FLAGS) -fsanitize=address,undefined csrc/tests/test_bootstrap_threads.cc $(CTRL_SRC) -o $@
 
-sanitize: $(BIN)/test_bootstrap_threads_tsan $(BIN)/test_bootstrap_threads_asan
+# The host data plane (TCP mesh, sender thread) on top of it; its element
+# types come from the CUDA headers, which compile as host code.
+HP_SRC := csrc/runtime/hostplane.cc $(CTRL_SRC)
+
+$(BIN)/test_hostplane_threads_tsan: csrc/tests/test_hostplane_threads.cc $(HP_SRC) $(HDRS)
+	@mkdir -p $(BIN)
+	g++ $(SAN_FLAGS) -I$(CUDA_HOME)/include -fsanitize=thread csrc/tests/test_hostplane_threads.cc $(HP_SRC) -o $@
+
+$(BIN)/test_hostplane_threads_asan: csrc/tests/test_hostplane_threads.cc $(HP_SRC) $(HDRS)
+	@mkdir -p $(BIN)
+	g++ $(SAN_FLAGS) -I$(CUDA_HOME)/include -fsanitize=address,undefined csrc/tests/test_hostplane_threads.cc $(HP_SRC) -o $@
+
+sanitize: $(BIN)/test_bootstrap_threads_tsan $(BIN)/test_bootstrap_threads_asan \
+          $(BIN)/test_hostplane_threads_tsan $(BIN)/test_hostplane_threads_asan
 
 .PHONY: sanitize
 

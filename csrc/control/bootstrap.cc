@@ -214,6 +214,15 @@ vcclResult_t Bootstrap::allGather(void* buf, size_t slice) {
   return recvFull(toRoot_, b, slice * nranks_, &aborted_);
 }
 
+bool everyone(Bootstrap* bs, bool mine) {
+  std::vector<uint8_t> v(bs->nranks(), 0);
+  v[bs->rank()] = mine ? 1 : 0;
+  if (bs->allGather(v.data(), 1) != vcclSuccess) return false;
+  for (uint8_t x : v)
+    if (!x) return false;
+  return true;
+}
+
 vcclResult_t Bootstrap::barrier() {
   std::vector<uint8_t> tok(nranks_, 1);
   return allGather(tok.data(), 1);

@@ -98,4 +98,9 @@ class Bootstrap {
 
 uint64_t hostFingerprint();
 
+// Every rank reports success of a step; all ranks learn whether everyone
+// succeeded (so that optional features are enabled or skipped together).
+// False on every rank if the exchange itself fails.
+bool everyone(Bootstrap* bs, bool mine);
+
 }  // namespace vccl

@@ -165,7 +165,6 @@ bool findDeviceAllocation(const void* p, size_t bytes, void** base, size_t* allo
 struct DriverApi;
 vcclResult_t mapForDevice(const DriverApi* d, CUmemGenericAllocationHandle h, size_t bytes, size_t align,
                           int device, CUdeviceptr* va);
-bool everyone(Bootstrap* bs, bool mine);
 // Release a window's multicast binding, or that and its peer mappings
 // (local steps only).
 void windowReleaseMulticast(DeviceState* ds, Window* w);

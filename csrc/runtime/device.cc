@@ -67,16 +67,6 @@ vcclResult_t mapForDevice(const DriverApi* d, CUmemGenericAllocationHandle h, si
   return vcclSuccess;
 }
 
-// Every rank reports success of a step; all ranks learn whether everyone
-// succeeded (so that optional features are enabled or skipped together).
-bool everyone(Bootstrap* bs, bool mine) {
-  std::vector<uint8_t> v(bs->nranks(), 0);
-  v[bs->rank()] = mine ? 1 : 0;
-  if (bs->allGather(v.data(), 1) != vcclSuccess) return false;
-  for (uint8_t x : v)
-    if (!x) return false;
-  return true;
-}
 
 namespace {
 

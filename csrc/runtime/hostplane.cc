@@ -155,9 +155,6 @@ size_t ceilDiv(size_t a, size_t b) { return (a + b - 1) / b; }
 
 }  // namespace
 
-// True on every rank iff `mine` is true on every rank (runtime/device.cc).
-bool everyone(Bootstrap* bs, bool mine);
-
 void hostReduce(char* out, const std::vector<const char*>& src, size_t count, const HostRed& r) {
   byType<ReduceF>(r.dt, out, src, count, r);
 }

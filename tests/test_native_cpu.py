@@ -27,7 +27,8 @@ def test_control_plane_suite():
 
 
 def test_control_plane_under_sanitizers():
-    """Threaded bootstrap rounds, fd exchange and abort under TSan and ASan/UBSan."""
+    """Threaded bootstrap rounds, fd exchange and abort under TSan and ASan/UBSan; the host data
+    plane's collectives, its sender thread and an abort racing a waiting all-reduce likewise."""
     import shutil
 
     if shutil.which("g++") is None:
@@ -39,6 +40,9 @@ def test_control_plane_under_sanitizers():
     for name in ("test_bootstrap_threads_tsan", "test_bootstrap_threads_asan"):
         out = _run(name, timeout=300)
         assert "bootstrap-threads: OK" in out
+    for name in ("test_hostplane_threads_tsan", "test_hostplane_threads_asan"):
+        out = _run(name, timeout=300)
+        assert "hostplane-threads: OK" in out
 
 
 def test_gemm_index_arithmetic():
