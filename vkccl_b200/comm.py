@@ -65,6 +65,26 @@ _NAME_TO_TYPE = {
 }
 
 
+# torch dtype -> DataType (or None), filled on first sight of each dtype
+_TORCH_DTYPE_TYPE: dict = {}
+
+
+def _torch_type(dtype: Any) -> Optional[DataType]:
+    try:
+        return _TORCH_DTYPE_TYPE[dtype]
+    except KeyError:
+        t = _NAME_TO_TYPE.get(str(dtype).replace("torch.", ""))
+        _TORCH_DTYPE_TYPE[dtype] = t
+        return t
+
+
+def _type_size(dt: int) -> int:
+    size = TYPE_SIZE.get(dt)  # IntEnum keys: a plain int finds its member
+    if size is None:
+        raise ValueError(f"unknown vccl data type {dt}")
+    return size
+
+
 class VcclError(RuntimeError):
     def __init__(self, result: int, what: str, detail: str = ""):
         self.result = result
@@ -105,13 +125,11 @@ def buffer_info(obj: Any, writable: bool) -> _Buf:
     if callable(data_ptr):  # torch tensor
         if not obj.is_contiguous():
             raise ValueError("vccl requires a contiguous tensor; call .contiguous() first")
-        dev = obj.device
-        cuda = dev.type == "cuda"
-        if dev.type not in ("cpu", "cuda"):
-            raise ValueError(f"unsupported tensor device '{dev}'")
-        name = str(obj.dtype).replace("torch.", "")
-        return _Buf(obj.data_ptr(), obj.numel() * obj.element_size(), _NAME_TO_TYPE.get(name), cuda,
-                    dev.index if cuda else -1)
+        if obj.is_cuda:
+            return _Buf(data_ptr(), obj.nbytes, _torch_type(obj.dtype), True, obj.get_device())
+        if not obj.is_cpu:
+            raise ValueError(f"unsupported tensor device '{obj.device}'")
+        return _Buf(data_ptr(), obj.nbytes, _torch_type(obj.dtype), False, -1)
     iface = getattr(obj, "__array_interface__", None)
     if iface is not None:  # numpy
         addr, readonly = iface["data"]
@@ -274,7 +292,7 @@ class Communicator:
         if n is None:
             if b.nbytes == 0 and b.addr != 0:
                 raise ValueError("count required when passing raw addresses")
-            n = b.nbytes // TYPE_SIZE[DataType(dt)] // scale
+            n = b.nbytes // _type_size(dt) // scale
         return b, int(n), int(dt)
 
     @staticmethod
@@ -282,7 +300,7 @@ class Communicator:
         """Refuse a buffer of known size that is too small for the call (a
         kernel would otherwise write or read past its end).  Raw addresses
         and absent buffers (non-root ranks) carry no size and are not checked."""
-        need = int(elems) * TYPE_SIZE[DataType(dt)]
+        need = int(elems) * _type_size(dt)
         if b.nbytes and b.nbytes < need:
             raise ValueError(f"{what} buffer holds {b.nbytes} bytes; the call needs {need}")
 
