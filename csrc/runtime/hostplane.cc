@@ -171,7 +171,9 @@ vcclResult_t HostPlane::create(Bootstrap* bs, std::unique_ptr<HostPlane>* out) {
   hp->fd_.assign(n, -1);
   hp->chunk_ = envBytes("VCCL_HOST_CHUNK", 8u << 20);
   if (hp->chunk_ < 4096) hp->chunk_ = 4096;
-  hp->directMax_ = envBytes("VCCL_HOST_AR_DIRECT", 32u << 10);
+  // 128 KiB sent per rank: paired runs put the crossover with reduce-scatter
+  // + all-gather near 16 KiB messages at 8 ranks and 16-32 KiB at 4.
+  hp->directMax_ = envBytes("VCCL_HOST_AR_DIRECT", 128u << 10);
   hp->spinUs_ = static_cast<int>(envLong("VCCL_HOST_SPIN_US", 50));
   hp->bcastDirect_ = envBytes("VCCL_HOST_BCAST_DIRECT", 16u << 10);
   hp->bcastPiece_ = envBytes("VCCL_HOST_BCAST_PIECE", 1u << 20);
@@ -663,7 +665,7 @@ vcclResult_t HostPlane::allReduce(const char* send, char* recv, size_t count, co
     send = scaled;
   }
   std::vector<const char*> src(n_);
-  if (bytes <= directMax_ || count < static_cast<size_t>(n_)) {
+  if (bytes * static_cast<size_t>(n_ - 1) <= directMax_ || count < static_cast<size_t>(n_)) {
     // Small: every rank sends the whole message to every peer and reduces
     // the n copies in rank order.
     char* tmp = scratch(0, bytes * n_);

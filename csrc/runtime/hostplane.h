@@ -21,8 +21,9 @@
 //  * reduce-scatter: every rank sends each owner its copy of the owner's
 //    block, and the owner reduces the n contributions in rank order;
 //  * all-reduce: reduce-scatter, then all-gather of the reduced blocks (or,
-//    below VCCL_HOST_AR_DIRECT bytes, every rank sends the whole message to
-//    every peer and reduces all n copies in rank order);
+//    while (n - 1) x the message is at most VCCL_HOST_AR_DIRECT bytes, every
+//    rank sends the whole message to every peer and reduces all n copies in
+//    rank order);
 //  * reduce: every rank sends to the root, which reduces in rank order;
 //  * a group of sends and receives runs in one progress loop.
 //
@@ -131,7 +132,9 @@ class HostPlane {
   std::vector<int> fd_;  // stream to each peer ([rank_] = -1)
   std::atomic<bool> aborted_{false};
   size_t chunk_ = 8u << 20;      // per-peer piece of a reduction (VCCL_HOST_CHUNK)
-  size_t directMax_ = 32u << 10;  // all-reduce below this: whole message to every peer
+  // All-reduce whose whole message to every peer, (n - 1) x bytes, is at
+  // most this: direct exchange (VCCL_HOST_AR_DIRECT).
+  size_t directMax_ = 128u << 10;
   int spinUs_ = 50;               // retry without sleeping this long before poll() (VCCL_HOST_SPIN_US)
   // Reduction buffers kept across calls (a fresh allocation per call would
   // page-fault its way through every byte): [0] and [1] receive alternate
