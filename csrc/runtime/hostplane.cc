@@ -16,6 +16,7 @@
 #include <chrono>
 #include <cstring>
 #include <deque>
+#include <exception>
 
 #include "common/env.h"
 #include "common/log.h"
@@ -265,8 +266,19 @@ void HostPlane::senderLoop() {
   }
 }
 
+bool HostPlane::ensureSender() {
+  if (sender_.joinable()) return true;
+  try {
+    sender_ = std::thread([this] { senderLoop(); });
+    return true;
+  } catch (const std::exception& e) {
+    VWARN("host data plane: no sender thread (%s); sends stay on the calling thread", e.what());
+    sendThreadMin_ = 0;
+    return false;
+  }
+}
+
 void HostPlane::handOff(Batch* sends) {
-  if (!sender_.joinable()) sender_ = std::thread([this] { senderLoop(); });
   {
     std::lock_guard<std::mutex> g(sMu_);
     job_ = sends;
@@ -303,7 +315,7 @@ vcclResult_t HostPlane::start(const std::vector<HostXfer>& xs, Batch* b) {
   }
   // Only a batch that also receives gains: its sends and receives then
   // copy on two cores at once.
-  const bool split = sendThreadMin_ > 0 && sendBytes >= sendThreadMin_ && recvBytes > 0;
+  const bool split = sendThreadMin_ > 0 && sendBytes >= sendThreadMin_ && recvBytes > 0 && ensureSender();
   if (split) {
     b->out.reset(new Batch);
     b->out->q.assign(n_, Batch::PeerQ{});

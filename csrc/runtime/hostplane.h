@@ -160,6 +160,7 @@ class HostPlane {
   bool stop_ = false;
   vcclResult_t jobRes_ = vcclSuccess;
   void senderLoop();
+  bool ensureSender();  // starts the thread once; false (and no hand-offs) if it cannot
   void handOff(Batch* sends);
   vcclResult_t waitHandOff();
 };
