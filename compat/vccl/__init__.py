@@ -30,7 +30,27 @@ from vkccl_b200 import (  # noqa: F401
     version,
 )
 
+from vkccl_b200._lib import _declare, lib as _lib  # noqa: F401
+from vkccl_b200.comm import _NAME_TO_TYPE as _DTYPE_NAMES  # noqa: F401
+from vkccl_b200.comm import TYPE_SIZE as _TYPE_SIZE  # noqa: F401
+from vkccl_b200.comm import _check as _check_impl
+from vkccl_b200.comm import _pin_bootstrap_interface as _ensure_bootstrap_addr  # noqa: F401
 from vkccl_b200.comm import buffer_info as _buffer_info_impl
+
+# The reference's private helpers under their names (reference:
+# python/vccl/__init__.py:61-92, 121-186, 220-243), for code that reached
+# into them: the loaded library, its prototypes, the dtype tables (fp8
+# added), the result check and the bootstrap-address default.
+
+
+def _setup_prototypes(lib):
+    """Declare this library's C prototypes on a ctypes handle."""
+    _declare(lib)
+
+
+def _check(result, what):
+    """Raise VcclError for a non-success vcclResult_t."""
+    _check_impl(result, what)
 
 
 def _buffer_info(obj, writable):

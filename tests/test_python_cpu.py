@@ -254,6 +254,16 @@ def test_compat_package_names():
         for name in ("UniqueId", "DataType", "RedOp", "VcclError", "get_unique_id", "group_start", "group_end"):
             assert getattr(vccl, name) is getattr(vkccl_b200, name)
         assert vccl.UNIQUE_ID_BYTES == 128
+        # the reference's private helpers (reference: python/vccl/__init__.py:61-92, 121-243)
+        assert vccl._lib() is vkccl_b200._lib.lib()
+        assert vccl._TYPE_SIZE[vccl.DataType.BFLOAT16] == 2 and vccl._DTYPE_NAMES["half"] == vccl.DataType.FLOAT16
+        assert vccl._buffer_info(bytearray(8), True)[1] == 8
+        assert callable(vccl._ensure_bootstrap_addr) and callable(vccl._setup_prototypes)
+        try:
+            vccl._check(4, "probe")  # vcclInvalidArgument
+            raise AssertionError("no error raised")
+        except vccl.VcclError as e:
+            assert e.result == 4
         tc = importlib.import_module("vccl.torch_comm")
         assert tc.VcclCommunicator.__name__ == "VcclCommunicator"
     finally:
