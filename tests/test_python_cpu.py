@@ -266,6 +266,11 @@ def test_compat_package_names():
             assert e.result == 4
         tc = importlib.import_module("vccl.torch_comm")
         assert tc.VcclCommunicator.__name__ == "VcclCommunicator"
+        import torch
+
+        assert tc._vccl_dtype(torch.zeros(1, dtype=torch.bfloat16)) == vccl.DataType.BFLOAT16
+        assert tc._TORCH_DTYPE[torch.float32] == vccl.DataType.FLOAT32
+        assert issubclass(tc.VcclCommunicator, tc.DeviceCommunicatorBase)
     finally:
         sys.path.pop(0)
         sys.modules.pop("vccl", None)

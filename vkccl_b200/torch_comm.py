@@ -119,6 +119,11 @@ class VcclCommunicator(DeviceCommunicatorBase):
         # (role, shape, dtype) -> (tensor, registration handle or None); see _buf
         self._buffers: dict = {}
 
+    @property
+    def _comm(self):
+        """The library communicator under the reference's attribute name."""
+        return self.vccl
+
     def _buf(self, role: str, shape, dtype: torch.dtype) -> torch.Tensor:
         """The persistent buffer of one (role, shape, dtype) on this
         communicator's device: made and registered with the communicator
