@@ -44,21 +44,16 @@ __device__ __forceinline__ void mbarArriveExpectTx(uint64_t* bar, uint32_t bytes
 __device__ __forceinline__ void mbarArrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smemAddr(bar)) : "memory");
 }
-// try_wait with a suspend-time hint: a waiting thread sleeps until the phase
-// completes (it is woken then) or the hint (1 ms) runs out, so warps parked on
-// a barrier for long (the MMA and epilogue warps while the producer waits for
-// a peer's data) take no issue slots from the warps doing work (copy warps
-// pulling over NVLink, the epilogue of other tiles).  The callers loop, so
-// the hint only bounds one sleep.  This form produced every multi-GPU figure
-// up to the 4-GPU tensor-parallel layer at 538 us per step; without the hint
-// two later 4-GPU runs took 1.7-1.9 ms per step.
-constexpr uint32_t kMbarSuspendNs = 1000000u;
+// try_wait without a suspend-time hint: with a long hint (1 ms was used) a
+// waiter whose phase completes late can stay suspended for most of the hint;
+// the plain form returns within the hardware's own short limit and the
+// callers loop.
 __device__ __forceinline__ bool mbarTryWait(uint64_t* bar, uint32_t phase) {
   uint32_t ok = 0;
   asm volatile(
-      "{\n .reg .pred P;\n mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n selp.b32 %0, 1, 0, P;\n}\n"
+      "{\n .reg .pred P;\n mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n selp.b32 %0, 1, 0, P;\n}\n"
       : "=r"(ok)
-      : "r"(smemAddr(bar)), "r"(phase), "r"(kMbarSuspendNs)
+      : "r"(smemAddr(bar)), "r"(phase)
       : "memory");
   return ok != 0;
 }
@@ -228,9 +223,9 @@ __device__ __forceinline__ void mbarArriveCluster(uint32_t clusterAddr) {
 __device__ __forceinline__ bool mbarTryWaitCluster(uint64_t* bar, uint32_t phase) {
   uint32_t ok = 0;
   asm volatile(
-      "{\n .reg .pred P;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2, %3;\n selp.b32 %0, 1, 0, P;\n}\n"
+      "{\n .reg .pred P;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n selp.b32 %0, 1, 0, P;\n}\n"
       : "=r"(ok)
-      : "r"(smemAddr(bar)), "r"(phase), "r"(kMbarSuspendNs)
+      : "r"(smemAddr(bar)), "r"(phase)
       : "memory");
   return ok != 0;
 }
