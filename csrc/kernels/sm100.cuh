@@ -44,10 +44,9 @@ __device__ __forceinline__ void mbarArriveExpectTx(uint64_t* bar, uint32_t bytes
 __device__ __forceinline__ void mbarArrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smemAddr(bar)) : "memory");
 }
-// try_wait without a suspend-time hint: with a long hint (1 ms was used) a
-// waiter whose phase completes late can stay suspended for most of the hint;
-// the plain form returns within the hardware's own short limit and the
-// callers loop.
+// try_wait without a suspend-time hint: each call returns when the phase
+// completes or after the hardware's own time limit, and the callers loop
+// (the bounded waits check the abort flag and the deadline between calls).
 __device__ __forceinline__ bool mbarTryWait(uint64_t* bar, uint32_t phase) {
   uint32_t ok = 0;
   asm volatile(
