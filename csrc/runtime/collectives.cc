@@ -790,7 +790,7 @@ vcclResult_t launchHostOps(vcclComm_t comm, std::vector<HostOp>& ops) {
       continue;
     }
     VTRY(runHostPlane(*hp, h));
-    comm->noteCall(opName(h.kind), "host TCP mesh", callBytes(h));
+    comm->noteCall(opName(h.kind), hp->path(), callBytes(h));
     i++;
   }
   return vcclSuccess;

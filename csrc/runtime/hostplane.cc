@@ -486,6 +486,7 @@ vcclResult_t HostPlane::pipelined(size_t pieces, X xfers, R reduce) {
 // ---- collectives -----------------------------------------------------------
 
 vcclResult_t HostPlane::allGather(const char* send, char* recv, size_t bytes) {
+  path_ = "host TCP mesh";
   if (bytes == 0) return vcclSuccess;
   char* mine = recv + rank_ * bytes;
   if (mine != send) memmove(mine, send, bytes);
@@ -499,6 +500,7 @@ vcclResult_t HostPlane::allGather(const char* send, char* recv, size_t bytes) {
 }
 
 vcclResult_t HostPlane::broadcast(const char* send, char* recv, size_t bytes, int root) {
+  path_ = "host TCP mesh";
   if (bytes == 0) return vcclSuccess;
   const int m = n_ - 1;  // ranks that receive
   if (rank_ == root && recv != send) memmove(recv, send, bytes);
@@ -513,6 +515,7 @@ vcclResult_t HostPlane::broadcast(const char* send, char* recv, size_t bytes, in
     }
     return run(xs);
   }
+  path_ = "host TCP mesh, pieces";
   // Large: in pieces, the root hands receiver j the j-th block of each piece
   // (it sends every byte once), and the receivers exchange their blocks
   // among themselves; while they exchange one piece, the root's next piece
@@ -557,6 +560,7 @@ vcclResult_t HostPlane::broadcast(const char* send, char* recv, size_t bytes, in
 }
 
 vcclResult_t HostPlane::gather(const char* send, char* recv, size_t bytes, int root) {
+  path_ = "host TCP mesh";
   if (bytes == 0) return vcclSuccess;
   std::vector<HostXfer> xs;
   if (rank_ == root) {
@@ -570,6 +574,7 @@ vcclResult_t HostPlane::gather(const char* send, char* recv, size_t bytes, int r
 }
 
 vcclResult_t HostPlane::scatter(const char* send, char* recv, size_t bytes, int root) {
+  path_ = "host TCP mesh";
   if (bytes == 0) return vcclSuccess;
   std::vector<HostXfer> xs;
   if (rank_ == root) {
@@ -584,6 +589,7 @@ vcclResult_t HostPlane::scatter(const char* send, char* recv, size_t bytes, int 
 
 vcclResult_t HostPlane::allToAllv(const char* send, const size_t* sc, const size_t* sd, char* recv,
                                   const size_t* rc, const size_t* rd) {
+  path_ = "host TCP mesh";
   // A receive range that overlaps the send buffer would be overwritten
   // before it leaves: send from a copy then.
   size_t sEnd = 0, rEnd = 0;
@@ -607,6 +613,7 @@ vcclResult_t HostPlane::allToAllv(const char* send, const size_t* sc, const size
 }
 
 vcclResult_t HostPlane::reduceScatter(const char* send, char* recv, size_t recvCount, const HostRed& r) {
+  path_ = "host TCP mesh";
   const size_t es = vcclTypeSize(r.dt);
   if (recvCount == 0) return vcclSuccess;
   const size_t cb = recvCount * es;
@@ -638,6 +645,7 @@ vcclResult_t HostPlane::reduceScatter(const char* send, char* recv, size_t recvC
 }
 
 vcclResult_t HostPlane::reduce(const char* send, char* recv, size_t count, const HostRed& r, int root) {
+  path_ = "host TCP mesh";
   const size_t es = vcclTypeSize(r.dt);
   if (count == 0) return vcclSuccess;
   if (r.premul) {
@@ -668,6 +676,7 @@ vcclResult_t HostPlane::reduce(const char* send, char* recv, size_t count, const
 }
 
 vcclResult_t HostPlane::allReduce(const char* send, char* recv, size_t count, const HostRed& r) {
+  path_ = "host TCP mesh";
   const size_t es = vcclTypeSize(r.dt);
   if (count == 0) return vcclSuccess;
   const size_t bytes = count * es;
@@ -680,6 +689,7 @@ vcclResult_t HostPlane::allReduce(const char* send, char* recv, size_t count, co
   if (bytes * static_cast<size_t>(n_ - 1) <= directMax_ || count < static_cast<size_t>(n_)) {
     // Small: every rank sends the whole message to every peer and reduces
     // the n copies in rank order.
+    path_ = "host TCP mesh, direct";
     char* tmp = scratch(0, bytes * n_);
     std::vector<HostXfer> xs;
     for (int p = 0; p < n_; p++) {
@@ -694,6 +704,7 @@ vcclResult_t HostPlane::allReduce(const char* send, char* recv, size_t count, co
   }
   // Large: rank q owns elements [q * bc, (q + 1) * bc) (the last block may be
   // shorter); reduce-scatter in pieces, then all-gather of the owned blocks.
+  path_ = "host TCP mesh, reduce-scatter + all-gather";
   const size_t bc = ceilDiv(count, n_);
   auto blkOff = [&](int q) { return std::min(static_cast<size_t>(q) * bc, count); };
   auto blkLen = [&](int q) { return std::min(static_cast<size_t>(q + 1) * bc, count) - blkOff(q); };

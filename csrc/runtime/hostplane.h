@@ -99,6 +99,9 @@ class HostPlane {
   // Unblocks every wait (vcclCommAbort); later calls fail.
   void abort();
 
+  // How the latest collective moved its data (for the call profile).
+  const char* path() const { return path_; }
+
  private:
   HostPlane(int rank, int n) : rank_(rank), n_(n) {}
 
@@ -129,6 +132,7 @@ class HostPlane {
 
   int rank_;
   int n_;
+  const char* path_ = "host TCP mesh";
   std::vector<int> fd_;  // stream to each peer ([rank_] = -1)
   std::atomic<bool> aborted_{false};
   size_t chunk_ = 8u << 20;      // per-peer piece of a reduction (VCCL_HOST_CHUNK)

@@ -199,7 +199,10 @@ def _matrix_body(rank, n, port, q):
                 comm.recv(r2, peer)
             assert torch.all(r1 == 10 + peer) and torch.all(r2 == 20 + peer), "ordered p2p"
         prof = {(e["op"], e["algo"]) for e in comm.prof_summary()}
-        assert ("all-reduce", "host TCP mesh") in prof and ("send", "host TCP mesh") in prof, prof
+        # small all-reduces go direct, large ones as reduce-scatter + all-gather
+        assert ("all-reduce", "host TCP mesh, direct") in prof, prof
+        assert ("all-reduce", "host TCP mesh, reduce-scatter + all-gather") in prof, prof
+        assert ("send", "host TCP mesh") in prof and ("all-gather", "host TCP mesh") in prof, prof
         assert comm.async_error() == 0
         comm.destroy()
         q.put((rank, "ok", sorted(prof)))
