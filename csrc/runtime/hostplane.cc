@@ -14,6 +14,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <deque>
 #include <exception>
@@ -686,7 +687,17 @@ vcclResult_t HostPlane::allReduce(const char* send, char* recv, size_t count, co
     send = scaled;
   }
   std::vector<const char*> src(n_);
-  if (bytes * static_cast<size_t>(n_ - 1) <= directMax_ || count < static_cast<size_t>(n_)) {
+  bool direct = bytes * static_cast<size_t>(n_ - 1) <= directMax_;
+  // VCCL_ALLREDUCE_ALGO forces the path, read on every call as on the device
+  // (every rank sets it alike): ring / twoshot -> reduce-scatter + all-gather,
+  // recdouble / oneshot / ll -> direct (the reference's two families under
+  // its own names, reference: src/core/collectives.cc:525-534).
+  if (const char* f = std::getenv("VCCL_ALLREDUCE_ALGO")) {
+    if (std::strcmp(f, "ring") == 0 || std::strcmp(f, "twoshot") == 0) direct = false;
+    else if (std::strcmp(f, "recdouble") == 0 || std::strcmp(f, "oneshot") == 0 || std::strcmp(f, "ll") == 0)
+      direct = true;
+  }
+  if (direct || count < static_cast<size_t>(n_)) {
     // Small: every rank sends the whole message to every peer and reduces
     // the n copies in rank order.
     path_ = "host TCP mesh, direct";

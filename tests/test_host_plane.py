@@ -251,6 +251,40 @@ def test_host_plane_matrix_send_thread():
     assert not bad, bad
 
 
+def _forced_algo_body(rank, n, port, q):
+    """VCCL_ALLREDUCE_ALGO on the host data plane: each family forced at sizes on both sides of
+    the default threshold gives the same sums, and the call profile shows the forced path."""
+    try:
+        _env(port)
+        os.environ["VCCL_PROF"] = "1"
+        import vkccl_b200 as v
+
+        comm = v.Communicator(n, v.get_unique_id(), rank)
+        for algo, label in (("ring", "reduce-scatter + all-gather"), ("recdouble", "direct"),
+                            ("twoshot", "reduce-scatter + all-gather"), ("oneshot", "direct")):
+            os.environ["VCCL_ALLREDUCE_ALGO"] = algo
+            for count in (7 * n, 5000, 1 << 17):
+                x = torch.arange(count, dtype=torch.float32) % 17 + rank
+                y = torch.empty_like(x)
+                comm.all_reduce(x, y)
+                want = (torch.arange(count, dtype=torch.float32) % 17) * n + n * (n - 1) // 2
+                assert torch.equal(y, want), (algo, count)
+            prof = {(e["op"], e["algo"]) for e in comm.prof_summary()}
+            assert ("all-reduce", "host TCP mesh, " + label) in prof, (algo, prof)
+        del os.environ["VCCL_ALLREDUCE_ALGO"]
+        comm.destroy()
+        q.put((rank, "ok", None))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, traceback.format_exc(), None))
+
+
+def test_host_plane_forced_allreduce_algorithm():
+    res = _run(_forced_algo_body, 3, timeout=300)
+    assert all(s == "ok" for s, _ in res.values()), res
+
+
 def _dead_peer_body(rank, n, port, q, count=1 << 16):
     try:
         _env(port)
