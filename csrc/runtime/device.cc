@@ -67,7 +67,6 @@ vcclResult_t mapForDevice(const DriverApi* d, CUmemGenericAllocationHandle h, si
   return vcclSuccess;
 }
 
-
 namespace {
 
 size_t roundUp(size_t x, size_t a) { return (x + a - 1) / a * a; }
